@@ -1,0 +1,352 @@
+"""Seeded synthetic GGUF models for parity tests and benchmarks.
+
+Writes GGUF v3 files that the reference readers accept
+(model.cpp:376-448 for the CPU path, metal_model.cpp:450-562 for the
+streaming reader) and that ``CudaLLM`` / ``CudaMoeLLM`` load:
+
+* ``qwen2``: the keys model.cpp:725-776 reads, an explicit ``output.weight``
+  (both reference readers require it; a "tied" model stores a byte-identical
+  copy of ``token_embd.weight``), every tensor consumed, block-aligned rows.
+* ``qwen35moe``: the keys metal_model.cpp:573-688 reads and the tensor schema
+  of moe_model.cpp:84-247 (no MTP/NextN block).
+
+Values come from ``csrc/synth/synth.c``: a counter-based normal generator
+keyed by (config seed, tensor name), so the same seed always produces the
+same bytes.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import hashlib
+import os
+import struct
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+F32, F16, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 6, 8, 12, 13, 14
+TYPE_NAMES = {F32: "F32", F16: "F16", Q5_0: "Q5_0", Q8_0: "Q8_0",
+              Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q5_0: (32, 22), Q8_0: (32, 34),
+         Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "lib", "libsynth.so")
+_lib = None
+
+
+def row_bytes(gtype: int, cols: int) -> int:
+    block, size = BLOCK[gtype]
+    if cols % block:
+        raise ValueError(f"{TYPE_NAMES[gtype]} row of {cols} columns is not block aligned")
+    return cols // block * size
+
+
+def lib():
+    """Load (building on first use) the C helper library."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            from . import build as _build
+            _build.build_synth()
+        l = ctypes.CDLL(_LIB_PATH)
+        l.synth_fill.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong,
+                                 ctypes.c_longlong, ctypes.c_ulonglong, ctypes.c_double,
+                                 ctypes.c_double, ctypes.c_int]
+        l.synth_fill.restype = ctypes.c_int
+        l.synth_quantize.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                     ctypes.c_longlong, ctypes.c_longlong]
+        l.synth_quantize.restype = ctypes.c_int
+        l.synth_normal_f32.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_ulonglong,
+                                       ctypes.c_double, ctypes.c_double]
+        l.synth_negexp_f32.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_ulonglong,
+                                       ctypes.c_double, ctypes.c_double]
+        l.synth_uniform_ids.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_ulonglong,
+                                        ctypes.c_longlong]
+        l.synth_mix64.argtypes = [ctypes.c_ulonglong]
+        l.synth_mix64.restype = ctypes.c_ulonglong
+        _lib = l
+    return _lib
+
+
+def stream_key(seed: int, name: str) -> int:
+    """64-bit stream key for one tensor of one seeded model."""
+    h = 0xCBF29CE484222325
+    for b in name.encode():
+        h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return lib().synth_mix64((seed * 0x9E3779B97F4A7C15 ^ h) & 0xFFFFFFFFFFFFFFFF)
+
+
+def normal(n: int, key: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().synth_normal_f32(out.ctypes.data, n, key, mean, std)
+    return out
+
+
+def uniform_ids(n: int, key: int, bound: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.int32)
+    lib().synth_uniform_ids(out.ctypes.data, n, key, bound)
+    return out
+
+
+def quantize(x: np.ndarray, gtype: int) -> np.ndarray:
+    """Pack a 2-D FP32 array into native GGML rows (uint8 [rows, row_bytes])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty((rows, row_bytes(gtype, cols)), dtype=np.uint8)
+    if lib().synth_quantize(x.ctypes.data, out.ctypes.data, gtype, rows, cols) != 0:
+        raise ValueError("quantize failed")
+    return out
+
+
+def fill(gtype: int, rows: int, cols: int, key: int, mean: float, std: float) -> np.ndarray:
+    out = np.empty((rows, row_bytes(gtype, cols)), dtype=np.uint8)
+    if lib().synth_fill(out.ctypes.data, gtype, rows, cols, key, mean, std, 0) != 0:
+        raise ValueError("synth_fill failed")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# GGUF v3 writer
+# ---------------------------------------------------------------------------
+_GGUF_U32, _GGUF_I32, _GGUF_F32, _GGUF_BOOL, _GGUF_STR, _GGUF_ARR, _GGUF_U64 = 4, 5, 6, 7, 8, 9, 10
+
+
+def _gguf_str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _kv(key: str, value) -> bytes:
+    if isinstance(value, bool):
+        return _gguf_str(key) + struct.pack("<IB", _GGUF_BOOL, int(value))
+    if isinstance(value, int):
+        return _gguf_str(key) + struct.pack("<II", _GGUF_U32, value)
+    if isinstance(value, float):
+        return _gguf_str(key) + struct.pack("<If", _GGUF_F32, value)
+    if isinstance(value, str):
+        return _gguf_str(key) + struct.pack("<I", _GGUF_STR) + _gguf_str(value)
+    if isinstance(value, (list, tuple)):
+        if all(isinstance(v, str) for v in value):
+            body = b"".join(_gguf_str(v) for v in value)
+            return _gguf_str(key) + struct.pack("<IIQ", _GGUF_ARR, _GGUF_STR, len(value)) + body
+        if all(isinstance(v, bool) for v in value):
+            body = bytes(int(v) for v in value)
+            return _gguf_str(key) + struct.pack("<IIQ", _GGUF_ARR, _GGUF_BOOL, len(value)) + body
+        body = b"".join(struct.pack("<i", int(v)) for v in value)
+        return _gguf_str(key) + struct.pack("<IIQ", _GGUF_ARR, _GGUF_I32, len(value)) + body
+    raise TypeError(f"unsupported metadata value for {key}: {value!r}")
+
+
+@dataclasses.dataclass
+class TensorSpec:
+    name: str
+    gtype: int
+    dims: Tuple[int, ...]          # GGUF order: dims[0] = columns
+    producer: Callable[[], np.ndarray]
+
+    @property
+    def cols(self) -> int:
+        return self.dims[0]
+
+    @property
+    def rows(self) -> int:
+        r = 1
+        for d in self.dims[1:]:
+            r *= d
+        return r
+
+    @property
+    def nbytes(self) -> int:
+        return self.rows * row_bytes(self.gtype, self.cols)
+
+
+def write_gguf(path: str, metadata: Dict[str, object], tensors: Sequence[TensorSpec],
+               alignment: int = 32) -> str:
+    """Write a GGUF v3 file; returns the SHA-256 of its bytes."""
+    head = bytearray()
+    head += struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(metadata))
+    for k, v in metadata.items():
+        head += _kv(k, v)
+    offset = 0
+    offsets = []
+    for t in tensors:
+        offsets.append(offset)
+        head += _gguf_str(t.name) + struct.pack("<I", len(t.dims))
+        head += b"".join(struct.pack("<Q", d) for d in t.dims)
+        head += struct.pack("<IQ", t.gtype, offset)
+        offset += t.nbytes
+        offset = (offset + alignment - 1) // alignment * alignment
+    pad = (-len(head)) % alignment
+    head += b"\0" * pad
+    sha = hashlib.sha256()
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(head)
+        sha.update(head)
+        pos = 0
+        for t, off in zip(tensors, offsets):
+            if off > pos:
+                f.write(b"\0" * (off - pos))
+                sha.update(b"\0" * (off - pos))
+                pos = off
+            data = t.producer()
+            if data.nbytes != t.nbytes:
+                raise ValueError(f"{t.name}: produced {data.nbytes} bytes, expected {t.nbytes}")
+            mv = memoryview(np.ascontiguousarray(data).reshape(-1))
+            f.write(mv)
+            sha.update(mv)
+            pos += t.nbytes
+    os.replace(tmp, path)
+    return sha.hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# qwen2 models
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class Qwen2Spec:
+    name: str
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    ffn: int
+    vocab: int
+    context: int = 4096
+    rope_theta: float = 1000000.0
+    eps: float = 1e-6
+    seed: int = 1
+    # per-layer tensor types: callable(layer, tensor_name) -> ggml type
+    types: Optional[Callable[[int, str], int]] = None
+    embed_type: int = Q8_0
+    output_type: Optional[int] = None   # None = tied copy of the embedding
+    weight_std: float = 0.02
+
+
+def qwen2_q4km_types(layer: int, tensor: str) -> int:
+    """Q4_K_M-style recipe for 7B/14B shapes: Q4_K everywhere except attn_v and
+    even-layer ffn_down, which are Q6_K."""
+    if tensor == "attn_v":
+        return Q6_K
+    if tensor == "ffn_down":
+        return Q6_K if layer % 2 == 0 else Q4_K
+    return Q4_K
+
+
+def qwen2_05b_types(layer: int, tensor: str) -> int:
+    """Q4_K_M layout at hidden 896 (not a multiple of 256): 896-column tensors
+    are Q5_0 (attn_v Q8_0); ffn_down (K = 4864) alternates Q6_K / Q4_K."""
+    if tensor == "attn_v":
+        return Q8_0
+    if tensor == "ffn_down":
+        return Q6_K if layer % 2 == 0 else Q4_K
+    return Q5_0
+
+
+CONFIGS: Dict[str, Qwen2Spec] = {
+    # Qwen2.5-0.5B architecture.
+    "qwen2.5-0.5b": Qwen2Spec("qwen2.5-0.5b", hidden=896, layers=24, heads=14, kv_heads=2,
+                              ffn=4864, vocab=151936, seed=0x05B, types=qwen2_05b_types,
+                              embed_type=Q8_0, output_type=None),
+    # Qwen2.5-7B architecture.
+    "qwen2.5-7b": Qwen2Spec("qwen2.5-7b", hidden=3584, layers=28, heads=28, kv_heads=4,
+                            ffn=18944, vocab=152064, seed=0x7B, types=qwen2_q4km_types,
+                            embed_type=Q4_K, output_type=Q6_K),
+    # Qwen2.5-14B architecture.
+    "qwen2.5-14b": Qwen2Spec("qwen2.5-14b", hidden=5120, layers=48, heads=40, kv_heads=8,
+                             ffn=13824, vocab=152064, seed=0x14B, types=qwen2_q4km_types,
+                             embed_type=Q4_K, output_type=Q6_K),
+}
+
+
+def tiny_mixed_types(layer: int, tensor: str) -> int:
+    """Every format on some tensor: even layers K-quants, odd layers 32-blocks."""
+    if layer % 2 == 0:
+        return {"attn_v": Q6_K, "ffn_down": Q6_K}.get(tensor, Q4_K)
+    return {"attn_v": Q8_0, "ffn_down": Q4_K}.get(tensor, Q5_0)
+
+
+def tiny_spec(seed: int = 7, layers: int = 2, hidden: int = 256, heads: int = 4,
+              kv_heads: int = 2, ffn: int = 512, vocab: int = 1024) -> Qwen2Spec:
+    return Qwen2Spec(f"tiny-s{seed}", hidden=hidden, layers=layers, heads=heads,
+                     kv_heads=kv_heads, ffn=ffn, vocab=vocab, context=256, seed=seed,
+                     types=tiny_mixed_types, embed_type=Q8_0, output_type=Q6_K)
+
+
+def qwen2_tensors(spec: Qwen2Spec) -> List[TensorSpec]:
+    H, F, V = spec.hidden, spec.ffn, spec.vocab
+    hd = H // spec.heads
+    KV = spec.kv_heads * hd
+    std = spec.weight_std
+    out: List[TensorSpec] = []
+
+    def mat(name, gtype, rows, cols, key_name=None):
+        key = stream_key(spec.seed, key_name or name)
+        out.append(TensorSpec(name, gtype, (cols, rows),
+                              lambda g=gtype, r=rows, c=cols, k=key: fill(g, r, c, k, 0.0, std)))
+
+    def vec(name, n, mean):
+        key = stream_key(spec.seed, name)
+        out.append(TensorSpec(name, F32, (n,),
+                              lambda n=n, k=key, m=mean: normal(n, k, m, std).view(np.uint8)))
+
+    mat("token_embd.weight", spec.embed_type, V, H)
+    vec("output_norm.weight", H, 1.0)
+    if spec.output_type is None:
+        mat("output.weight", spec.embed_type, V, H, key_name="token_embd.weight")
+    else:
+        mat("output.weight", spec.output_type, V, H)
+    types = spec.types or qwen2_q4km_types
+    for l in range(spec.layers):
+        p = f"blk.{l}."
+        vec(p + "attn_norm.weight", H, 1.0)
+        mat(p + "attn_q.weight", types(l, "attn_q"), H, H)
+        vec(p + "attn_q.bias", H, 0.0)
+        mat(p + "attn_k.weight", types(l, "attn_k"), KV, H)
+        vec(p + "attn_k.bias", KV, 0.0)
+        mat(p + "attn_v.weight", types(l, "attn_v"), KV, H)
+        vec(p + "attn_v.bias", KV, 0.0)
+        mat(p + "attn_output.weight", types(l, "attn_output"), H, H)
+        vec(p + "ffn_norm.weight", H, 1.0)
+        mat(p + "ffn_gate.weight", types(l, "ffn_gate"), F, H)
+        mat(p + "ffn_up.weight", types(l, "ffn_up"), F, H)
+        mat(p + "ffn_down.weight", types(l, "ffn_down"), H, F)
+    return out
+
+
+def qwen2_metadata(spec: Qwen2Spec) -> Dict[str, object]:
+    return {
+        "general.architecture": "qwen2",
+        "general.name": spec.name,
+        "qwen2.block_count": spec.layers,
+        "qwen2.context_length": spec.context,
+        "qwen2.embedding_length": spec.hidden,
+        "qwen2.feed_forward_length": spec.ffn,
+        "qwen2.attention.head_count": spec.heads,
+        "qwen2.attention.head_count_kv": spec.kv_heads,
+        "qwen2.rope.freq_base": float(spec.rope_theta),
+        "qwen2.attention.layer_norm_rms_epsilon": float(spec.eps),
+        "tokenizer.ggml.pre": "qwen2",
+        "tokenizer.ggml.tokens_count": spec.vocab,
+        "tokenizer.ggml.eos_token_id": min(spec.vocab - 1, 151645),
+    }
+
+
+def write_qwen2(spec: Qwen2Spec, path: str) -> str:
+    return write_gguf(path, qwen2_metadata(spec), qwen2_tensors(spec))
+
+
+def prompt_ids(spec_seed: int, n: int, vocab: int) -> np.ndarray:
+    """The seeded uniform random prompt of a config."""
+    return uniform_ids(n, stream_key(spec_seed, "prompt"), vocab)
+
+
+def cached_qwen2(spec: Qwen2Spec, directory: str) -> str:
+    """Path of the model file for `spec` under `directory`, writing it once."""
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{spec.name}.gguf")
+    if not os.path.exists(path):
+        write_qwen2(spec, path)
+    return path
