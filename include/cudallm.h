@@ -1,0 +1,71 @@
+/*
+ * cudallm.h — backend C-ABI of CudaLLM (qwen2) for harnesses in other
+ * languages (Python ctypes, cgo, ...).
+ *
+ * Each call maps one-to-one onto the reference backend contract used by
+ * chat::generate (chat.cpp:832-878) and declared by CPULLM / MetalLLM
+ * (cpu_llm.h:167-194, metal_llm.h:20-51):
+ *   cudallm_create   <- CPULLM(const std::string&, std::size_t max_sequence)
+ *   cudallm_reset    <- void reset()
+ *   cudallm_prefill  <- std::int32_t prefill(const std::vector<std::int32_t>&)
+ *   cudallm_decode   <- std::int32_t decode(std::int32_t)
+ *   cudallm_position / cudallm_max_sequence / cudallm_memory_stats /
+ *   cudallm_enable_profiling / cudallm_disable_profiling <- same-named members
+ * The C++ exceptions of that contract become status codes:
+ *   std::invalid_argument -> CUDALLM_EINVAL, std::out_of_range -> CUDALLM_ERANGE,
+ *   std::length_error -> CUDALLM_ELENGTH, std::runtime_error -> CUDALLM_ERUNTIME;
+ * cudallm_last_error() returns the message of the last failure on the
+ * calling thread.
+ */
+#ifndef CUDALLM_H
+#define CUDALLM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CUDALLM_API __attribute__((visibility("default")))
+
+enum {
+    CUDALLM_OK = 0,
+    CUDALLM_EINVAL = 1,
+    CUDALLM_ERANGE = 2,
+    CUDALLM_ELENGTH = 3,
+    CUDALLM_ERUNTIME = 4
+};
+
+typedef struct cudallm_model cudallm_model;
+
+CUDALLM_API const char* cudallm_last_error(void);
+/* 128-byte NCCL unique id for a multi-GPU job (rank 0 creates, all receive). */
+CUDALLM_API int cudallm_nccl_unique_id(char out[128]);
+
+/* device < 0: current device.  world == 1: single GPU (nccl_id ignored). */
+CUDALLM_API int cudallm_create(const char* gguf_path, size_t max_sequence, int device, int rank, int world,
+                               const char* nccl_id, cudallm_model** out);
+CUDALLM_API void cudallm_destroy(cudallm_model* m);
+CUDALLM_API int cudallm_reset(cudallm_model* m);
+CUDALLM_API int cudallm_prefill(cudallm_model* m, const int32_t* ids, size_t n, int32_t* token);
+CUDALLM_API int cudallm_decode(cudallm_model* m, int32_t id, int32_t* token);
+/* Logits of the last prefill/decode, n >= vocabulary size (collective when world > 1). */
+CUDALLM_API int cudallm_last_logits(cudallm_model* m, float* out, size_t n);
+CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m);
+CUDALLM_API size_t cudallm_position(const cudallm_model* m);
+CUDALLM_API size_t cudallm_max_sequence(const cudallm_model* m);
+/* layer_count, embedding_size, feed_forward_size, attention_head_count,
+ * kv_head_count, head_size, vocabulary_size, context_length (up to n). */
+CUDALLM_API int cudallm_config(const cudallm_model* m, long long* out, int n);
+/* weight, kv_cache, recurrent_state, intermediate bytes. */
+CUDALLM_API int cudallm_memory_stats(const cudallm_model* m, uint64_t out[4]);
+CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path);
+CUDALLM_API int cudallm_disable_profiling(cudallm_model* m);
+CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDALLM_H */

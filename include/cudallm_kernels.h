@@ -1,0 +1,166 @@
+/*
+ * cudallm_kernels.h — the kernel C-ABI of the CudaLLM backend (sm_100a).
+ *
+ * Plain C: device pointers, sizes, a cudaStream_t.  Every entry point returns
+ * CL_OK (0) or a CL_ERR_* code, never throws, never allocates device memory
+ * and never synchronizes; work is enqueued on `stream`.  Kernels needing
+ * scratch take a caller-owned workspace whose size a *_workspace_bytes()
+ * query reports.
+ *
+ * Each entry replaces one operator of the reference's Metal shader library
+ * (metal_llm.metal) or CPU operator library (cpu_llm.cpp); the reference
+ * interface is cited beside each declaration.
+ */
+#ifndef CUDALLM_KERNELS_H
+#define CUDALLM_KERNELS_H
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CL_API __attribute__((visibility("default")))
+
+/* GGML tensor types (GGUF on-disk ids; metal_model.h:14-29). */
+enum {
+    CL_TYPE_F32 = 0,
+    CL_TYPE_F16 = 1,
+    CL_TYPE_Q5_0 = 6,
+    CL_TYPE_Q8_0 = 8,
+    CL_TYPE_Q4_K = 12,
+    CL_TYPE_Q5_K = 13,
+    CL_TYPE_Q6_K = 14
+};
+
+enum {
+    CL_OK = 0,
+    CL_ERR_INVALID = 1,     /* bad argument, shape or alignment */
+    CL_ERR_UNSUPPORTED = 2, /* type/shape combination not implemented */
+    CL_ERR_CUDA = 3,        /* a CUDA launch failed */
+    CL_ERR_WORKSPACE = 4    /* workspace missing or too small */
+};
+
+CL_API const char* cl_status_string(int status);
+/* 1 (default): launch with programmatic dependent launch; 0: plain launches. */
+CL_API void cl_set_pdl(int enabled);
+
+/* ---- weight layout ---------------------------------------------------- */
+/* Native GGUF bytes per row (metal_model.cpp:437-448); -1 if k is not
+ * block aligned for `type`. */
+CL_API long long cl_native_row_bytes(int type, int k);
+/* Row stride of the device layout (native bytes rounded up to 16). */
+CL_API long long cl_row_stride(int type, int k);
+/* Native rows -> device layout (per-row structure-of-arrays for Q6_K, Q8_0,
+ * Q5_0; K-quants Q4_K/Q5_K unchanged).  Replaces upload_matrix
+ * (metal_llm.mm:834-862), which kept native bytes. */
+CL_API int cl_repack_rows(int type, const void* native, void* packed, int rows, int k,
+                          cudaStream_t stream);
+
+/* ---- activation vectors (XQ) ----------------------------------------- */
+/* Bytes of the XQ encoding of a k-vector (k % 32 == 0): per 32-block scale
+ * and three int8 limbs per element, |error| < max|x_block| * 2^-22. */
+CL_API size_t cl_xq_bytes(int k);
+CL_API int cl_quantize_xq(const float* x, int k, void* xq, cudaStream_t stream);
+
+/* ---- decode GEMV (metal_gevm_*_f32, metal_llm.metal:708-781; CPU gevmtb
+ * cpu_llm.cpp:528-547) ----------------------------------------------------
+ * y[n] = W[n,k] . x (+ bias[n]) (+ residual[n]); W in the device layout. */
+CL_API int cl_gemv_xq(int type, const void* w, long long stride, int n, int k, const void* xq,
+                      const float* bias, const float* residual, float* y, cudaStream_t stream);
+
+typedef struct {
+    int type;
+    const void* w;
+    long long stride;
+    int n;
+    const float* bias;
+    const float* residual;
+    float* y;
+} cl_gemv_segment;
+
+/* Up to 4 matrices sharing one input vector (e.g. Q, K and V) in one launch. */
+CL_API int cl_gemv_xq_multi(const cl_gemv_segment* segs, int nseg, int k, const void* xq,
+                            cudaStream_t stream);
+/* y[i] = SiLU(gate_i . x) * (up_i . x): gate/up GEMV with the SwiGLU
+ * (cpu_llm.cpp:188-202, metal_swiglu_f32 metal_llm.metal:895) fused. */
+CL_API int cl_gemv_xq_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n,
+                             int k, const void* xq, float* y, cudaStream_t stream);
+/* FP32 input convenience form: quantizes x into `workspace`
+ * (>= cl_xq_bytes(k)) and runs cl_gemv_xq. */
+CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x,
+                   const float* bias, float* y, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream);
+
+/* ---- prefill GEMM (metal_gemm_*_f32, metal_llm.metal:621-704; CPU gemmtb
+ * cpu_llm.cpp:631-653) ----------------------------------------------------
+ * Y[m,n] = X[m,k] W[n,k]^T (+ bias[n]) (+ R[m,n]); X, Y, R row-major FP32. */
+CL_API int cl_gemm(int type, const void* w, long long stride, int n, int k, const float* x, int m,
+                   const float* bias, const float* residual, float* y, cudaStream_t stream);
+
+/* ---- activations ------------------------------------------------------ */
+/* Row RMSNorm (cpu_llm.cpp:143-166, metal_rmsnorm_f32 metal_llm.metal:785):
+ * sum of squares in double, y = x * (1/sqrt(mean+eps) * gamma).  Either
+ * output may be NULL; xq gets one XQ vector per row (stride cl_xq_bytes(k)). */
+CL_API int cl_rmsnorm(const float* x, const float* gamma, int rows, int k, float eps, float* y,
+                      void* xq, cudaStream_t stream);
+/* Embedding gather with dequantization (metal_embedding_*, metal_llm.metal:
+ * 1066-1162; CPU embedding cpu_llm.cpp:101-123).  Out-of-range ids produce
+ * zero rows and set *error_flag = 1 (error_flag may be NULL). */
+CL_API int cl_embed(int type, const void* table, long long stride, int vocab, int k, const int32_t* ids,
+                    int count, float* out, int* error_flag, cudaStream_t stream);
+/* NeoX RoPE from a precomputed [positions][rot/2] cos/sin table plus K/V
+ * cache append (metal_rope_heads_f32 + metal_kv_cache_write_f32,
+ * metal_llm.metal:928-990; CPU Vector::rope cpu_llm.cpp:204-235).
+ * Rows r = 0..rows-1 sit at position pos0 + r, where pos0 = *pos_dev when
+ * pos_dev != NULL, else pos_host.  q is rotated in place; k is rotated and,
+ * with v, written to cache rows.  Caches are [capacity][kv_heads*head_dim]. */
+CL_API int cl_rope_kv(float* q, const float* k, const float* v, int rows, int q_heads, int kv_heads,
+                      int head_dim, int rot_dim, const float* cos_sin, const int* pos_dev, int pos_host,
+                      float* k_cache, float* v_cache, cudaStream_t stream);
+CL_API int cl_swiglu(const float* gate, const float* up, float* out, long long n, cudaStream_t stream);
+CL_API int cl_add(const float* a, const float* b, float* out, long long n, cudaStream_t stream);
+
+/* ---- attention --------------------------------------------------------- */
+/* Decode GQA attention over the cache (metal_kv_cache_qk/softmax/av,
+ * metal_llm.metal:995-1061; CPU gevmts/softmax/gevm cpu_llm.cpp:888-903).
+ * Keys 0..len-1 with len = *len_dev (device int) so the call can be captured
+ * once in a CUDA graph; max_len bounds len.  out is [q_heads*head_dim];
+ * xq (optional) receives its XQ encoding. */
+CL_API size_t cl_attn_decode_workspace_bytes(int q_heads, int head_dim, int max_len);
+CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
+                          int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out,
+                          void* xq, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* Causal prefill attention for rows at positions pos0..pos0+rows-1 against
+ * cache rows 0..pos0+rows-1 (CPU gemmts/causal_mask/softmax/gemm,
+ * cpu_llm.cpp:816-827).  q, out: [rows][q_heads*head_dim]. */
+CL_API int cl_attn_prefill(const float* q, const float* k_cache, const float* v_cache, int pos0, int rows,
+                           int q_heads, int kv_heads, int head_dim, float* out, cudaStream_t stream);
+
+/* ---- greedy token (metal_argmax_partial/finalize_f32, metal_llm.metal:
+ * 1544-1644; CPU greedy_token cpu_llm.cpp:34-48) -------------------------
+ * *token = argmax(logits[0..n)), lowest index on ties.  Single pass: the
+ * last CTA to finish reduces the per-CTA partials and re-arms the workspace
+ * (zeroed once by the caller before first use). */
+CL_API size_t cl_argmax_workspace_bytes(int n);
+CL_API int cl_argmax(const float* logits, int n, int32_t* token, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream);
+/* Shard form for a vocabulary split across ranks: *token = local argmax +
+ * index_offset and *value = its logit (value may be NULL). */
+CL_API int cl_argmax_ex(const float* logits, int n, int index_offset, int32_t* token, float* value,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* Merge n (value, index-bits) records gathered from the shards: highest
+ * value, lowest index on ties. */
+CL_API int cl_argmax_merge(const float* records, int n, int32_t* token, cudaStream_t stream);
+
+/* counters[0..n) += delta on the device (position bookkeeping inside a
+ * captured decode graph). */
+CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDALLM_KERNELS_H */

@@ -1,0 +1,96 @@
+"""ctypes bindings of libcudallm.so (include/cudallm_kernels.h, include/cudallm.h).
+
+The library is built in-tree by ``myllm_b200.build``.  There is no fallback:
+if it is missing or cannot be loaded, importing the backend raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libcudallm.so")
+
+_lib = None
+
+c_int, c_ll, c_size, c_float, c_vp, c_char_p = (ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t,
+                                                ctypes.c_float, ctypes.c_void_p, ctypes.c_char_p)
+
+
+class GemvSegment(ctypes.Structure):
+    _fields_ = [("type", c_int), ("w", c_vp), ("stride", c_ll), ("n", c_int), ("bias", c_vp),
+                ("residual", c_vp), ("y", c_vp)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "cl_status_string": (c_char_p, [c_int]),
+    "cl_set_pdl": (None, [c_int]),
+    "cl_native_row_bytes": (c_ll, [c_int, c_int]),
+    "cl_row_stride": (c_ll, [c_int, c_int]),
+    "cl_repack_rows": (c_int, [c_int, c_vp, c_vp, c_int, c_int, c_vp]),
+    "cl_xq_bytes": (c_size, [c_int]),
+    "cl_quantize_xq": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "cl_gemv_xq": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gemv_xq_multi": (c_int, [ctypes.POINTER(GemvSegment), c_int, c_int, c_vp, c_vp]),
+    "cl_gemv_xq_swiglu": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_gemv": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_size, c_vp]),
+    "cl_gemm": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "cl_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp]),
+    "cl_embed": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
+    "cl_rope_kv": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int,
+                           c_vp, c_vp, c_vp]),
+    "cl_swiglu": (c_int, [c_vp, c_vp, c_vp, c_ll, c_vp]),
+    "cl_add": (c_int, [c_vp, c_vp, c_vp, c_ll, c_vp]),
+    "cl_attn_decode_workspace_bytes": (c_size, [c_int, c_int, c_int]),
+    "cl_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp,
+                               c_vp, c_size, c_vp]),
+    "cl_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "cl_argmax_workspace_bytes": (c_size, [c_int]),
+    "cl_argmax": (c_int, [c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
+    "cl_argmax_ex": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_size, c_vp]),
+    "cl_argmax_merge": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "cl_counter_add": (c_int, [c_vp, c_int, c_int, c_vp]),
+    # backend
+    "cudallm_last_error": (c_char_p, []),
+    "cudallm_nccl_unique_id": (c_int, [c_vp]),
+    "cudallm_create": (c_int, [c_char_p, c_size, c_int, c_int, c_int, c_vp, ctypes.POINTER(c_vp)]),
+    "cudallm_destroy": (None, [c_vp]),
+    "cudallm_reset": (c_int, [c_vp]),
+    "cudallm_prefill": (c_int, [c_vp, c_vp, c_size, ctypes.POINTER(ctypes.c_int32)]),
+    "cudallm_decode": (c_int, [c_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
+    "cudallm_last_logits": (c_int, [c_vp, c_vp, c_size]),
+    "cudallm_last_call_ms": (c_float, [c_vp]),
+    "cudallm_position": (c_size, [c_vp]),
+    "cudallm_max_sequence": (c_size, [c_vp]),
+    "cudallm_config": (c_int, [c_vp, ctypes.POINTER(c_ll), c_int]),
+    "cudallm_memory_stats": (c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "cudallm_enable_profiling": (c_int, [c_vp, c_char_p]),
+    "cudallm_disable_profiling": (c_int, [c_vp]),
+    "cudallm_device_name": (c_int, [c_vp, c_vp, c_size]),
+}
+
+
+def lib():
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m myllm_b200.build`")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def check(status: int, what: str = "") -> None:
+    if status != 0:
+        msg = lib().cl_status_string(status).decode()
+        raise KernelError(f"{what}: {msg} (status {status})")

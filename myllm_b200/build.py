@@ -99,7 +99,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError("CUDA build failed for: " + ", ".join(failed))
     tmp = out + ".tmp"
-    _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lnccl", "-lpthread"])
+    _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lnccl", "-lpthread", "-ldl", "-lrt"])
     os.replace(tmp, out)
     return out
 

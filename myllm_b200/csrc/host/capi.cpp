@@ -1,0 +1,168 @@
+// cudallm_* C-ABI over cudallm::CudaLLM (see include/cudallm.h).
+#include "cudallm.h"
+
+#include <nccl.h>
+
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "cuda_llm.h"
+
+struct cudallm_model {
+    cudallm::CudaLLM llm;
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F>
+int guard(F&& f) {
+    try {
+        f();
+        return CUDALLM_OK;
+    } catch (const std::invalid_argument& e) {
+        g_error = e.what();
+        return CUDALLM_EINVAL;
+    } catch (const std::out_of_range& e) {
+        g_error = e.what();
+        return CUDALLM_ERANGE;
+    } catch (const std::length_error& e) {
+        g_error = e.what();
+        return CUDALLM_ELENGTH;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return CUDALLM_ERUNTIME;
+    } catch (...) {
+        g_error = "unknown error";
+        return CUDALLM_ERUNTIME;
+    }
+}
+
+void need(const void* p) {
+    if (p == nullptr) throw std::invalid_argument("null handle or pointer");
+}
+
+}  // namespace
+
+extern "C" {
+
+CUDALLM_API const char* cudallm_last_error(void) { return g_error.c_str(); }
+
+CUDALLM_API int cudallm_nccl_unique_id(char out[128]) {
+    return guard([&] {
+        need(out);
+        ncclUniqueId id;
+        if (ncclGetUniqueId(&id) != ncclSuccess) throw std::runtime_error("ncclGetUniqueId failed");
+        static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+        std::memcpy(out, &id, 128);
+    });
+}
+
+CUDALLM_API int cudallm_create(const char* gguf_path, size_t max_sequence, int device, int rank, int world,
+                               const char* nccl_id, cudallm_model** out) {
+    return guard([&] {
+        need(gguf_path);
+        need(out);
+        cudallm::ParallelConfig par;
+        par.rank = rank;
+        par.world = world;
+        if (world > 1) {
+            need(nccl_id);
+            std::memcpy(par.nccl_id.data(), nccl_id, 128);
+        }
+        *out = new cudallm_model{cudallm::CudaLLM(gguf_path, max_sequence, device, par)};
+    });
+}
+
+CUDALLM_API void cudallm_destroy(cudallm_model* m) { delete m; }
+
+CUDALLM_API int cudallm_reset(cudallm_model* m) {
+    return guard([&] {
+        need(m);
+        m->llm.reset();
+    });
+}
+
+CUDALLM_API int cudallm_prefill(cudallm_model* m, const int32_t* ids, size_t n, int32_t* token) {
+    return guard([&] {
+        need(m);
+        need(token);
+        if (n > 0) need(ids);
+        *token = m->llm.prefill(std::vector<int32_t>(ids, ids + n));
+    });
+}
+
+CUDALLM_API int cudallm_decode(cudallm_model* m, int32_t id, int32_t* token) {
+    return guard([&] {
+        need(m);
+        need(token);
+        *token = m->llm.decode(id);
+    });
+}
+
+CUDALLM_API int cudallm_last_logits(cudallm_model* m, float* out, size_t n) {
+    return guard([&] {
+        need(m);
+        need(out);
+        m->llm.last_logits(out, n);
+    });
+}
+
+CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m) { return m ? m->llm.last_call_ms() : 0.0f; }
+CUDALLM_API size_t cudallm_position(const cudallm_model* m) { return m ? m->llm.position() : 0; }
+CUDALLM_API size_t cudallm_max_sequence(const cudallm_model* m) { return m ? m->llm.max_sequence() : 0; }
+
+CUDALLM_API int cudallm_config(const cudallm_model* m, long long* out, int n) {
+    return guard([&] {
+        need(m);
+        need(out);
+        const cudallm::ModelConfig& c = m->llm.config();
+        const long long v[] = {(long long)c.layer_count,          (long long)c.embedding_size,
+                               (long long)c.feed_forward_size,    (long long)c.attention_head_count,
+                               (long long)c.kv_head_count,        (long long)c.head_size,
+                               (long long)c.vocabulary_size,      (long long)c.context_length};
+        for (int i = 0; i < n && i < 8; ++i) out[i] = v[i];
+    });
+}
+
+CUDALLM_API int cudallm_memory_stats(const cudallm_model* m, uint64_t out[4]) {
+    return guard([&] {
+        need(m);
+        need(out);
+        const cudallm::MemoryStats s = m->llm.memory_stats();
+        out[0] = s.weight_bytes;
+        out[1] = s.kv_cache_bytes;
+        out[2] = s.recurrent_state_bytes;
+        out[3] = s.intermediate_bytes;
+    });
+}
+
+CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path) {
+    return guard([&] {
+        need(m);
+        need(csv_path);
+        m->llm.enable_profiling(csv_path);
+    });
+}
+
+CUDALLM_API int cudallm_disable_profiling(cudallm_model* m) {
+    return guard([&] {
+        need(m);
+        m->llm.disable_profiling();
+    });
+}
+
+CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n) {
+    return guard([&] {
+        need(m);
+        need(buf);
+        const std::string& s = m->llm.device_name();
+        if (n == 0) throw std::invalid_argument("empty name buffer");
+        std::strncpy(buf, s.c_str(), n - 1);
+        buf[n - 1] = 0;
+    });
+}
+
+}  // extern "C"

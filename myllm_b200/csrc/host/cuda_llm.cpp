@@ -1,0 +1,634 @@
+// CudaLLM: the qwen2 decode/prefill graph on one or more B200s.
+//
+// Graph order follows cpu_prefill_layer / cpu_decode_layer (cpu_llm.cpp:
+// 774-914) and encode_{prefill,decode}_layer (metal_llm.mm:2619-2904):
+//   h = embed(ids)
+//   per layer: a = rmsnorm(h); q,k,v = a W^T + b; rope(q,k); cache k,v;
+//              o = attention; h += o Wo^T; f = rmsnorm(h);
+//              h += (silu(f Wg^T) * f Wu^T) Wd^T
+//   logits = rmsnorm(h_last) Wout^T; token = argmax (lowest index on ties).
+// Decode is one CUDA graph per step (captured once, replayed); the only host
+// synchronisation is the 4-byte token read-back.
+#include "cuda_llm.h"
+
+#include <nccl.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <stdexcept>
+
+#include "device.h"
+#include "gguf.h"
+
+namespace cudallm {
+
+namespace {
+
+#define CUDALLM_NCCL(expr)                                                                    \
+    do {                                                                                      \
+        ncclResult_t r_ = (expr);                                                             \
+        if (r_ != ncclSuccess)                                                                \
+            throw std::runtime_error(std::string("NCCL error ") + ncclGetErrorString(r_) +    \
+                                     " in " #expr);                                           \
+    } while (0)
+
+ModelConfig read_qwen2_config(const GgufFile& f) {
+    ModelConfig c;
+    c.architecture = f.text("general.architecture");
+    if (c.architecture != "qwen2") {
+        throw std::runtime_error("CudaLLM supports qwen2 GGUF models, got " + c.architecture);
+    }
+    c.tensor_count = f.tensors().size();
+    c.layer_count = f.size("qwen2.block_count");
+    c.embedding_size = f.size("qwen2.embedding_length");
+    c.feed_forward_size = f.size("qwen2.feed_forward_length");
+    c.attention_head_count = f.size("qwen2.attention.head_count");
+    c.kv_head_count = f.size("qwen2.attention.head_count_kv");
+    c.context_length = f.size("qwen2.context_length");
+    c.vocabulary_size = f.array_length("tokenizer.ggml.tokens");
+    if (c.vocabulary_size == 0) c.vocabulary_size = f.size("tokenizer.ggml.tokens_count");
+    if (c.embedding_size % c.attention_head_count != 0)
+        throw std::runtime_error("embedding size must be divisible by attention head count");
+    if (c.attention_head_count % c.kv_head_count != 0)
+        throw std::runtime_error("attention head count must be divisible by KV head count");
+    c.head_size = c.embedding_size / c.attention_head_count;
+    c.rotary_dimension = c.head_size;
+    c.rope_theta = (float)f.real("qwen2.rope.freq_base", 1000000.0);
+    c.norm_epsilon = (float)f.real("qwen2.attention.layer_norm_rms_epsilon", 1e-6);
+    if (!std::isfinite(c.rope_theta) || c.rope_theta <= 0.0f)
+        throw std::runtime_error("RoPE theta must be finite and positive");
+    if (!std::isfinite(c.norm_epsilon) || c.norm_epsilon <= 0.0f)
+        throw std::runtime_error("RMSNorm epsilon must be finite and positive");
+    const uint64_t eos = f.integer("tokenizer.ggml.eos_token_id", 151645);
+    if (eos > (uint64_t)INT32_MAX) throw std::runtime_error("EOS token id does not fit in int32_t");
+    c.eos_token_id = (int32_t)eos;
+    for (const TensorInfo& t : f.tensors()) {
+        c.parameter_count += t.rows * t.cols;
+        c.stored_weight_bytes += t.bytes;
+    }
+    return c;
+}
+
+// cos/sin of NeoX RoPE for every position, computed on the host with the
+// CPU path's float expressions (cpu_llm.cpp:220-227) so that the rotation
+// inputs match it exactly.
+std::vector<float> rope_table(std::size_t positions, std::size_t rot, float theta) {
+    const std::size_t half = rot / 2;
+    std::vector<float> freq(half);
+    for (std::size_t p = 0; p < half; ++p)
+        freq[p] = std::pow(theta, -2.0f * static_cast<float>(p) / static_cast<float>(rot));
+    std::vector<float> t(positions * half * 2);
+    for (std::size_t pos = 0; pos < positions; ++pos) {
+        for (std::size_t p = 0; p < half; ++p) {
+            const float angle = static_cast<float>(pos) * freq[p];
+            t[(pos * half + p) * 2] = std::cos(angle);
+            t[(pos * half + p) * 2 + 1] = std::sin(angle);
+        }
+    }
+    return t;
+}
+
+struct Layer {
+    const float* attn_norm = nullptr;
+    DevMat q, k, v, o;
+    const float *q_b = nullptr, *k_b = nullptr, *v_b = nullptr;
+    const float* ffn_norm = nullptr;
+    DevMat gate, up, down;
+    float* k_cache = nullptr;
+    float* v_cache = nullptr;
+};
+
+// Contiguous, block-aligned share [begin, end) of `n` units for one rank.
+std::pair<std::size_t, std::size_t> split_range(std::size_t n, int world, int rank) {
+    const std::size_t base = n / world, extra = n % world;
+    const std::size_t begin = rank * base + std::min<std::size_t>(rank, extra);
+    return {begin, begin + base + ((std::size_t)rank < extra ? 1 : 0)};
+}
+
+std::size_t block_cols(int type) {
+    return (type == kQ4_K || type == kQ5_K || type == kQ6_K) ? 256 : (type == kQ5_0 || type == kQ8_0) ? 32 : 1;
+}
+
+}  // namespace
+
+struct CudaLLM::Impl {
+    ModelConfig config;
+    ParallelConfig par;
+    int device = 0;
+    std::string device_name;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+
+    // shard geometry (world == 1: everything full)
+    std::size_t H = 0, F = 0, V = 0, d = 0, hq = 0, hkv = 0;
+    std::size_t hq_l = 0, hkv_l = 0;      // local heads
+    std::size_t ffn0 = 0, F_l = 0;        // local FFN rows [ffn0, ffn0 + F_l)
+    std::size_t vocab0 = 0, V_l = 0;      // local LM-head rows
+    std::size_t o_k0 = 0, o_kl = 0;       // local o_proj input columns
+    bool gather_attn = false;             // o_proj K shard is not the local heads
+
+    std::size_t max_seq = 0;
+    std::size_t prefill_chunk = 0;
+    std::size_t position = 0;
+
+    DeviceBuffer weight_mem, state_mem, act_mem;
+    std::uint64_t weight_payload = 0, kv_bytes = 0, act_bytes = 0;
+
+    DevMat tok_embd, out_w;
+    const float* out_norm = nullptr;
+    std::vector<Layer> layers;
+    const float* rope = nullptr;
+
+    // decode activations
+    float *h = nullptr, *part = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+          *att_full = nullptr, *act = nullptr, *logits = nullptr;
+    void *xq_h = nullptr, *xq_att = nullptr, *xq_act = nullptr;
+    void *attn_ws = nullptr, *arg_ws = nullptr;
+    std::size_t attn_ws_bytes = 0, arg_ws_bytes = 0;
+    int32_t* ints = nullptr;  // [0] token in, [1] pos, [2] len, [3] token out, [4..] scratch
+    float* best = nullptr;    // TP argmax records [world][2]
+    // prefill activations
+    float *X = nullptr, *Xn = nullptr, *Q = nullptr, *K = nullptr, *Vv = nullptr, *A = nullptr,
+          *A_full = nullptr, *G = nullptr, *U = nullptr, *P = nullptr;
+    int32_t* ids_dev = nullptr;
+
+    PinnedBuffer host_io;  // [0] token in, [1] token out, [2..] ids staging
+    cudaGraphExec_t decode_exec = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.0f;
+    std::ofstream profile;
+    bool have_logits = false;
+
+    ~Impl() {
+        if (decode_exec) cudaGraphExecDestroy(decode_exec);
+        if (comm) ncclCommDestroy(comm);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    void plan_shards() {
+        const int W = par.world, R = par.rank;
+        H = config.embedding_size;
+        F = config.feed_forward_size;
+        V = config.vocabulary_size;
+        d = config.head_size;
+        hq = config.attention_head_count;
+        hkv = config.kv_head_count;
+        if (W < 1 || R < 0 || R >= W) throw std::invalid_argument("invalid parallel rank/world");
+        if (hkv % W != 0 || hq % W != 0)
+            throw std::invalid_argument("tensor-parallel world must divide the query and KV head counts");
+        hq_l = hq / W;
+        hkv_l = hkv / W;
+        ffn0 = 0;
+        F_l = F;
+        o_k0 = 0;
+        o_kl = hq * d;
+        vocab0 = 0;
+        V_l = V;
+        gather_attn = false;
+        if (W > 1) {
+            // FFN rows split on the widest block grid both formats share.
+            const std::size_t blk = 256;
+            if (F % blk) throw std::invalid_argument("FFN width must be a multiple of 256 for tensor parallelism");
+            auto fr = split_range(F / blk, W, R);
+            ffn0 = fr.first * blk;
+            F_l = (fr.second - fr.first) * blk;
+            // o_proj input columns: the local heads when block aligned,
+            // otherwise a block-aligned share of the all-gathered output.
+            const std::size_t heads_cols = hq_l * d;
+            if (heads_cols % blk == 0) {
+                o_k0 = R * heads_cols;
+                o_kl = heads_cols;
+            } else {
+                gather_attn = true;
+                auto orng = split_range(hq * d / blk, W, R);
+                o_k0 = orng.first * blk;
+                o_kl = (orng.second - orng.first) * blk;
+            }
+            auto vr = split_range(V, W, R);
+            vocab0 = vr.first;
+            V_l = vr.second - vr.first;
+        }
+    }
+
+    // Planning pass (arena base null) then the real pass with the same calls.
+    void load_weights(GgufFile& file, Arena& arena, bool real) {
+        WeightLoader wl(file, arena, stream);
+        const std::size_t kvd = hkv * d;
+        tok_embd = wl.matrix("token_embd.weight", V, H);
+        out_norm = wl.vector("output_norm.weight", H);
+        out_w = wl.matrix("output.weight", V, H, vocab0, vocab0 + V_l);
+        layers.assign(config.layer_count, Layer{});
+        for (std::size_t l = 0; l < config.layer_count; ++l) {
+            const std::string p = "blk." + std::to_string(l) + ".";
+            Layer& L = layers[l];
+            const std::size_t q0 = par.rank * hq_l * d, qn = hq_l * d;
+            const std::size_t k0 = par.rank * hkv_l * d, kn = hkv_l * d;
+            L.attn_norm = wl.vector(p + "attn_norm.weight", H);
+            L.q = wl.matrix(p + "attn_q.weight", H, H, q0, q0 + qn);
+            L.q_b = wl.vector(p + "attn_q.bias", H, q0, q0 + qn);
+            L.k = wl.matrix(p + "attn_k.weight", kvd, H, k0, k0 + kn);
+            L.k_b = wl.vector(p + "attn_k.bias", kvd, k0, k0 + kn);
+            L.v = wl.matrix(p + "attn_v.weight", kvd, H, k0, k0 + kn);
+            L.v_b = wl.vector(p + "attn_v.bias", kvd, k0, k0 + kn);
+            L.o = wl.matrix(p + "attn_output.weight", H, H, 0, H, o_k0, o_k0 + o_kl);
+            L.ffn_norm = wl.vector(p + "ffn_norm.weight", H);
+            L.gate = wl.matrix(p + "ffn_gate.weight", F, H, ffn0, ffn0 + F_l);
+            L.up = wl.matrix(p + "ffn_up.weight", F, H, ffn0, ffn0 + F_l);
+            L.down = wl.matrix(p + "ffn_down.weight", H, F, 0, H, ffn0, ffn0 + F_l);
+            if (L.gate.type != L.up.type) throw std::runtime_error("ffn_gate and ffn_up must share a type");
+        }
+        file.validate_all_loaded();
+        if (real) wl.finish();
+        weight_payload = wl.payload_bytes();
+    }
+
+    void allocate_state(Arena& a) {
+        const std::size_t kvd_l = hkv_l * d;
+        for (Layer& L : layers) {
+            L.k_cache = a.take_n<float>(max_seq * kvd_l);
+            L.v_cache = a.take_n<float>(max_seq * kvd_l);
+        }
+        rope = a.take_n<float>(max_seq * (config.rotary_dimension / 2) * 2);
+    }
+
+    void allocate_activations(Arena& a) {
+        const std::size_t qd_l = hq_l * d, kvd_l = hkv_l * d, P = prefill_chunk;
+        h = a.take_n<float>(H);
+        part = a.take_n<float>(H);
+        q = a.take_n<float>(qd_l);
+        k = a.take_n<float>(kvd_l);
+        v = a.take_n<float>(kvd_l);
+        att = a.take_n<float>(qd_l);
+        att_full = a.take_n<float>(hq * d);
+        act = a.take_n<float>(F_l);
+        logits = a.take_n<float>(V_l);
+        xq_h = a.take(cl_xq_bytes((int)H));
+        xq_att = a.take(cl_xq_bytes((int)std::max(o_kl, qd_l)));
+        xq_act = a.take(cl_xq_bytes((int)F_l));
+        attn_ws_bytes = cl_attn_decode_workspace_bytes((int)hq_l, (int)d, (int)max_seq);
+        attn_ws = a.take(attn_ws_bytes);
+        arg_ws_bytes = cl_argmax_workspace_bytes((int)V_l);
+        arg_ws = a.take(arg_ws_bytes);
+        ints = a.take_n<int32_t>(16);
+        best = a.take_n<float>(2 * (std::size_t)par.world + 2);
+        X = a.take_n<float>(P * H);
+        Xn = a.take_n<float>(P * H);
+        Q = a.take_n<float>(P * qd_l);
+        K = a.take_n<float>(P * kvd_l);
+        Vv = a.take_n<float>(P * kvd_l);
+        A = a.take_n<float>(P * qd_l);
+        A_full = a.take_n<float>(gather_attn ? P * hq * d : 1);
+        G = a.take_n<float>(P * F_l);
+        U = a.take_n<float>(P * F_l);
+        this->P = a.take_n<float>(P * H);
+        ids_dev = a.take_n<int32_t>(P);
+    }
+
+    void init(const std::string& path, std::size_t max_sequence, int dev, const ParallelConfig& parallel) {
+        par = parallel;
+        if (dev < 0) CUDALLM_CUDA(cudaGetDevice(&dev));
+        device = dev;
+        CUDALLM_CUDA(cudaSetDevice(device));
+        cudaDeviceProp prop{};
+        CUDALLM_CUDA(cudaGetDeviceProperties(&prop, device));
+        device_name = prop.name;
+        CUDALLM_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        CUDALLM_CUDA(cudaEventCreate(&ev0));
+        CUDALLM_CUDA(cudaEventCreate(&ev1));
+
+        GgufFile file(path);
+        config = read_qwen2_config(file);
+        if (max_sequence == 0) max_sequence = config.context_length;
+        if (max_sequence == 0 || max_sequence > config.context_length)
+            throw std::invalid_argument("CUDA maximum sequence must be within the model context length");
+        max_seq = max_sequence;
+        prefill_chunk = std::min<std::size_t>(max_seq, 1024);
+        // Diagnostics: a smaller prefill chunk exercises the cross-chunk KV path.
+        if (const char* e = std::getenv("CUDALLM_PREFILL_CHUNK")) {
+            const long v = std::strtol(e, nullptr, 10);
+            if (v > 0) prefill_chunk = std::min<std::size_t>(max_seq, (std::size_t)v);
+        }
+        plan_shards();
+
+        if (par.world > 1) {
+            ncclUniqueId id;
+            std::memcpy(&id, par.nccl_id.data(), sizeof(id));
+            CUDALLM_NCCL(ncclCommInitRank(&comm, par.world, id, par.rank));
+        }
+
+        Arena plan;
+        load_weights(file, plan, false);
+        weight_mem = DeviceBuffer(plan.used() + 256);
+        Arena wa;
+        wa.bind(weight_mem.get(), weight_mem.size());
+        GgufFile file2(path);
+        load_weights(file2, wa, true);
+
+        Arena sp;
+        allocate_state(sp);
+        state_mem = DeviceBuffer(sp.used() + 256);
+        Arena sa;
+        sa.bind(state_mem.get(), state_mem.size());
+        allocate_state(sa);
+        kv_bytes = (std::uint64_t)layers.size() * 2 * max_seq * hkv_l * d * sizeof(float);
+
+        Arena ap;
+        allocate_activations(ap);
+        act_mem = DeviceBuffer(ap.used() + 256);
+        Arena aa;
+        aa.bind(act_mem.get(), act_mem.size());
+        allocate_activations(aa);
+        act_bytes = ap.used();
+        CUDALLM_CUDA(cudaMemsetAsync(act_mem.get(), 0, act_mem.size(), stream));
+
+        const std::vector<float> table = rope_table(max_seq, config.rotary_dimension, config.rope_theta);
+        CUDALLM_CUDA(cudaMemcpyAsync(const_cast<float*>(rope), table.data(), table.size() * sizeof(float),
+                                     cudaMemcpyHostToDevice, stream));
+        host_io = PinnedBuffer(sizeof(int32_t) * (4 + prefill_chunk));
+        CUDALLM_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    float eps() const { return config.norm_epsilon; }
+    int32_t* host_in() const { return static_cast<int32_t*>(host_io.get()); }
+
+    void all_reduce(float* send, float* recv, std::size_t n) {
+        CUDALLM_NCCL(ncclAllReduce(send, recv, n, ncclFloat32, ncclSum, comm, stream));
+    }
+
+    // LM head + greedy token for the normalised last row already in xq_h.
+    void record_head(int32_t* token_out) {
+        cudaStream_t s = stream;
+        CUDALLM_CL(cl_gemv_xq(out_w.type, out_w.ptr, out_w.stride, (int)V_l, (int)H, xq_h, nullptr, nullptr, logits, s));
+        if (par.world == 1) {
+            CUDALLM_CL(cl_argmax(logits, (int)V_l, token_out, arg_ws, arg_ws_bytes, s));
+        } else {
+            float* rec = best + 2 * par.rank;
+            CUDALLM_CL(cl_argmax_ex(logits, (int)V_l, (int)vocab0, reinterpret_cast<int32_t*>(rec + 1), rec, arg_ws,
+                                    arg_ws_bytes, s));
+            CUDALLM_NCCL(ncclAllGather(rec, best, 2, ncclFloat32, comm, s));
+            CUDALLM_CL(cl_argmax_merge(best, par.world, token_out, s));
+        }
+    }
+
+    // One decode step: host_in[0] -> token; host_in[1] <- greedy token.
+    void record_decode() {
+        cudaStream_t s = stream;
+        const int W = par.world;
+        const float scale = 1.0f / std::sqrt(static_cast<float>(d));
+        int32_t* tok_in = ints + 0;
+        int* pos = ints + 1;
+        int* len = ints + 2;
+        CUDALLM_CUDA(cudaMemcpyAsync(tok_in, host_in(), sizeof(int32_t), cudaMemcpyHostToDevice, s));
+        CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, (int)H, tok_in, 1, h, ints + 4, s));
+        float* out = W > 1 ? part : h;
+        const float* res = par.rank == 0 ? h : nullptr;
+        for (Layer& L : layers) {
+            CUDALLM_CL(cl_rmsnorm(h, L.attn_norm, 1, (int)H, eps(), nullptr, xq_h, s));
+            const cl_gemv_segment segs[3] = {
+                {L.q.type, L.q.ptr, L.q.stride, L.q.rows, L.q_b, nullptr, q},
+                {L.k.type, L.k.ptr, L.k.stride, L.k.rows, L.k_b, nullptr, k},
+                {L.v.type, L.v.ptr, L.v.stride, L.v.rows, L.v_b, nullptr, v},
+            };
+            CUDALLM_CL(cl_gemv_xq_multi(segs, 3, (int)H, xq_h, s));
+            CUDALLM_CL(cl_rope_kv(q, k, v, 1, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, pos, 0,
+                                  L.k_cache, L.v_cache, s));
+            CUDALLM_CL(cl_attn_decode(q, L.k_cache, L.v_cache, len, (int)max_seq, (int)hq_l, (int)hkv_l, (int)d, scale,
+                                      att, gather_attn ? nullptr : xq_att, attn_ws, attn_ws_bytes, s));
+            if (gather_attn) {
+                CUDALLM_NCCL(ncclAllGather(att, att_full, hq_l * d, ncclFloat32, comm, s));
+                CUDALLM_CL(cl_quantize_xq(att_full + o_k0, (int)o_kl, xq_att, s));
+            }
+            CUDALLM_CL(cl_gemv_xq(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, xq_att, nullptr, res, out, s));
+            if (W > 1) all_reduce(part, h, H);
+            CUDALLM_CL(cl_rmsnorm(h, L.ffn_norm, 1, (int)H, eps(), nullptr, xq_h, s));
+            CUDALLM_CL(cl_gemv_xq_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, xq_h, act, s));
+            CUDALLM_CL(cl_quantize_xq(act, (int)F_l, xq_act, s));
+            CUDALLM_CL(cl_gemv_xq(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, xq_act, nullptr, res, out, s));
+            if (W > 1) all_reduce(part, h, H);
+        }
+        CUDALLM_CL(cl_rmsnorm(h, out_norm, 1, (int)H, eps(), nullptr, xq_h, s));
+        record_head(ints + 3);
+        CUDALLM_CL(cl_counter_add(pos, 2, 1, s));
+        CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    }
+
+    void build_decode_graph() {
+        cudaGraph_t graph = nullptr;
+        CUDALLM_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+        try {
+            record_decode();
+        } catch (...) {
+            cudaStreamEndCapture(stream, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            throw;
+        }
+        CUDALLM_CUDA(cudaStreamEndCapture(stream, &graph));
+        const cudaError_t e = cudaGraphInstantiate(&decode_exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CUDALLM_CUDA(e);
+    }
+
+    // Rows [0, m) of X hold the chunk at positions pos0..pos0+m-1.
+    void prefill_chunk_layers(int m, int pos0) {
+        cudaStream_t s = stream;
+        const int W = par.world;
+        float* out = W > 1 ? P : X;
+        const float* res = par.rank == 0 ? X : nullptr;
+        const std::size_t qd_l = hq_l * d;
+        for (Layer& L : layers) {
+            CUDALLM_CL(cl_rmsnorm(X, L.attn_norm, m, (int)H, eps(), Xn, nullptr, s));
+            CUDALLM_CL(cl_gemm(L.q.type, L.q.ptr, L.q.stride, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q, s));
+            CUDALLM_CL(cl_gemm(L.k.type, L.k.ptr, L.k.stride, L.k.rows, (int)H, Xn, m, L.k_b, nullptr, K, s));
+            CUDALLM_CL(cl_gemm(L.v.type, L.v.ptr, L.v.stride, L.v.rows, (int)H, Xn, m, L.v_b, nullptr, Vv, s));
+            CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
+                                  pos0, L.k_cache, L.v_cache, s));
+            CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
+            const float* o_in = A;
+            if (gather_attn) {
+                // rank-major gather [W][m][qd_l] -> rows [m][hq*d], then the
+                // contiguous o_proj column share into A.
+                CUDALLM_NCCL(ncclAllGather(A, A_full, (std::size_t)m * qd_l, ncclFloat32, comm, s));
+                for (int r = 0; r < W; ++r) {
+                    const std::size_t c0 = std::max(o_k0, r * qd_l);
+                    const std::size_t c1 = std::min(o_k0 + o_kl, (r + 1) * qd_l);
+                    if (c0 >= c1) continue;
+                    CUDALLM_CUDA(cudaMemcpy2DAsync(Xn + (c0 - o_k0), o_kl * sizeof(float),
+                                                   A_full + (std::size_t)r * m * qd_l + (c0 - r * qd_l),
+                                                   qd_l * sizeof(float), (c1 - c0) * sizeof(float), m,
+                                                   cudaMemcpyDeviceToDevice, s));
+                }
+                o_in = Xn;
+            }
+            CUDALLM_CL(cl_gemm(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, m, nullptr, res, out, s));
+            if (W > 1) all_reduce(P, X, (std::size_t)m * H);
+            CUDALLM_CL(cl_rmsnorm(X, L.ffn_norm, m, (int)H, eps(), Xn, nullptr, s));
+            CUDALLM_CL(cl_gemm(L.gate.type, L.gate.ptr, L.gate.stride, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G, s));
+            CUDALLM_CL(cl_gemm(L.up.type, L.up.ptr, L.up.stride, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U, s));
+            CUDALLM_CL(cl_swiglu(G, U, G, (long long)m * F_l, s));
+            CUDALLM_CL(cl_gemm(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, G, m, nullptr, res, out, s));
+            if (W > 1) all_reduce(P, X, (std::size_t)m * H);
+        }
+    }
+
+    void begin_timing() { CUDALLM_CUDA(cudaEventRecord(ev0, stream)); }
+
+    void end_timing(const char* phase, std::size_t tokens) {
+        CUDALLM_CUDA(cudaEventRecord(ev1, stream));
+        CUDALLM_CUDA(cudaEventSynchronize(ev1));
+        CUDALLM_CUDA(cudaEventElapsedTime(&last_ms, ev0, ev1));
+        if (profile.is_open()) {
+            profile << phase << "," << tokens << "," << position << "," << last_ms << "\n";
+            profile.flush();
+        }
+    }
+
+    int32_t prefill(const std::vector<int32_t>& ids) {
+        if (ids.empty()) throw std::invalid_argument("CUDA prefill requires at least one token");
+        if (position != 0) throw std::invalid_argument("CUDA prefill requires an empty conversation; call reset first");
+        if (ids.size() > max_seq) throw std::length_error("CUDA prefill exceeds sequence capacity");
+        for (int32_t id : ids) {
+            if (id < 0 || (std::size_t)id >= config.vocabulary_size)
+                throw std::out_of_range("CUDA prefill token id is outside the vocabulary");
+        }
+        CUDALLM_CUDA(cudaSetDevice(device));
+        begin_timing();
+        const std::size_t n = ids.size();
+        int32_t* staging = host_in() + 4;
+        std::size_t last_m = 0;
+        for (std::size_t c0 = 0; c0 < n; c0 += prefill_chunk) {
+            const std::size_t m = std::min(prefill_chunk, n - c0);
+            // the previous chunk's copy must be done before the staging is reused
+            CUDALLM_CUDA(cudaStreamSynchronize(stream));
+            std::memcpy(staging, ids.data() + c0, m * sizeof(int32_t));
+            CUDALLM_CUDA(cudaMemcpyAsync(ids_dev, staging, m * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+            CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, (int)H, ids_dev, (int)m, X,
+                                ints + 4, stream));
+            prefill_chunk_layers((int)m, (int)c0);
+            last_m = m;
+        }
+        CUDALLM_CL(cl_rmsnorm(X + (last_m - 1) * H, out_norm, 1, (int)H, eps(), nullptr, xq_h, stream));
+        record_head(ints + 3);
+        int32_t* hi = host_in();
+        hi[2] = (int32_t)n;
+        hi[3] = (int32_t)(n + 1);
+        CUDALLM_CUDA(cudaMemcpyAsync(ints + 1, hi + 2, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+        CUDALLM_CUDA(cudaMemcpyAsync(hi + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
+        end_timing("prefill", n);
+        position = n;
+        have_logits = true;
+        return hi[1];
+    }
+
+    int32_t decode(int32_t token) {
+        if (position == 0) throw std::invalid_argument("CUDA decode requires a completed prefill");
+        if (token < 0 || (std::size_t)token >= config.vocabulary_size)
+            throw std::out_of_range("CUDA decode token id is outside the vocabulary");
+        if (position >= max_seq) throw std::length_error("CUDA decode exceeds sequence capacity");
+        CUDALLM_CUDA(cudaSetDevice(device));
+        if (decode_exec == nullptr) build_decode_graph();
+        host_in()[0] = token;
+        begin_timing();
+        CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
+        end_timing("decode", 1);
+        position += 1;
+        have_logits = true;
+        return host_in()[1];
+    }
+};
+
+CudaLLM::CudaLLM(const std::string& gguf_path, std::size_t max_sequence, int device, const ParallelConfig& parallel)
+    : impl_(std::make_unique<Impl>()) {
+    impl_->init(gguf_path, max_sequence, device, parallel);
+}
+
+CudaLLM::~CudaLLM() = default;
+CudaLLM::CudaLLM(CudaLLM&&) noexcept = default;
+CudaLLM& CudaLLM::operator=(CudaLLM&&) noexcept = default;
+
+void CudaLLM::reset() {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    // Logical reset only (metal_llm.mm:3185-3187): KV rows are overwritten.
+    impl_->position = 0;
+    impl_->have_logits = false;
+}
+
+std::int32_t CudaLLM::prefill(const std::vector<std::int32_t>& token_ids) {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    return impl_->prefill(token_ids);
+}
+
+std::int32_t CudaLLM::decode(std::int32_t token_id) {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    return impl_->decode(token_id);
+}
+
+void CudaLLM::enable_profiling(const std::string& csv_path, bool) {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    impl_->profile = std::ofstream(csv_path);
+    if (!impl_->profile) throw std::runtime_error("cannot open profile CSV: " + csv_path);
+    impl_->profile << "phase,tokens,position,device_ms\n";
+}
+
+void CudaLLM::disable_profiling() {
+    if (impl_) impl_->profile.close();
+}
+
+const ModelConfig& CudaLLM::config() const {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    return impl_->config;
+}
+
+std::size_t CudaLLM::position() const noexcept { return impl_ ? impl_->position : 0; }
+std::size_t CudaLLM::max_sequence() const noexcept { return impl_ ? impl_->max_seq : 0; }
+bool CudaLLM::uses_gpu() const noexcept { return true; }
+bool CudaLLM::available() const noexcept { return impl_ != nullptr; }
+
+const std::string& CudaLLM::device_name() const {
+    if (!impl_) throw std::runtime_error("CUDA model is not initialized");
+    return impl_->device_name;
+}
+
+MemoryStats CudaLLM::memory_stats() const noexcept {
+    if (!impl_) return {};
+    MemoryStats m;
+    m.weight_bytes = impl_->weight_mem.size();
+    m.kv_cache_bytes = impl_->kv_bytes;
+    m.recurrent_state_bytes = 0;
+    m.intermediate_bytes = impl_->act_bytes;
+    m.intermediate_is_estimate = false;
+    return m;
+}
+
+void CudaLLM::last_logits(float* out, std::size_t n) const {
+    if (!impl_ || !impl_->have_logits) throw std::invalid_argument("no logits: call prefill or decode first");
+    Impl& I = *impl_;
+    if (n < I.V) throw std::invalid_argument("logits buffer is smaller than the vocabulary");
+    CUDALLM_CUDA(cudaSetDevice(I.device));
+    if (I.par.world == 1) {
+        CUDALLM_CUDA(cudaMemcpy(out, I.logits, I.V * sizeof(float), cudaMemcpyDeviceToHost));
+        return;
+    }
+    // Collective: every rank gathers the vocabulary shards (uneven shares
+    // are padded to the largest one).
+    const std::size_t chunk = (I.V + I.par.world - 1) / I.par.world;
+    DeviceBuffer send(chunk * sizeof(float)), recv(chunk * I.par.world * sizeof(float));
+    CUDALLM_CUDA(cudaMemsetAsync(send.get(), 0, send.size(), I.stream));
+    CUDALLM_CUDA(cudaMemcpyAsync(send.get(), I.logits, I.V_l * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+    CUDALLM_NCCL(ncclAllGather(send.get(), recv.get(), chunk, ncclFloat32, I.comm, I.stream));
+    std::vector<float> all(chunk * I.par.world);
+    CUDALLM_CUDA(cudaMemcpyAsync(all.data(), recv.get(), recv.size(), cudaMemcpyDeviceToHost, I.stream));
+    CUDALLM_CUDA(cudaStreamSynchronize(I.stream));
+    for (int r = 0; r < I.par.world; ++r) {
+        auto rg = split_range(I.V, I.par.world, r);
+        std::memcpy(out + rg.first, all.data() + (std::size_t)r * chunk, (rg.second - rg.first) * sizeof(float));
+    }
+}
+
+float CudaLLM::last_call_ms() const noexcept { return impl_ ? impl_->last_ms : 0.0f; }
+
+}  // namespace cudallm

@@ -1,0 +1,161 @@
+"""Torch-tensor front end of the kernel C-ABI (include/cudallm_kernels.h).
+
+PyTorch only supplies device memory and the current stream; every call lands
+in an sm_100a kernel of libcudallm.so.  Used by the GPU parity tests and the
+kernel benchmarks.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _native
+from ._native import check
+
+F32, F16, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 6, 8, 12, 13, 14
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def row_stride(gtype: int, k: int) -> int:
+    s = _native.lib().cl_row_stride(gtype, k)
+    if s < 0:
+        raise ValueError(f"type {gtype} cannot hold rows of {k} columns")
+    return int(s)
+
+
+def native_row_bytes(gtype: int, k: int) -> int:
+    return int(_native.lib().cl_native_row_bytes(gtype, k))
+
+
+def repack(gtype: int, native: np.ndarray, k: int, device="cuda") -> torch.Tensor:
+    """Native GGML rows (uint8 [rows, row_bytes]) -> device layout [rows, stride]."""
+    native = np.ascontiguousarray(native, dtype=np.uint8)
+    rows = native.shape[0]
+    src = torch.from_numpy(native).to(device)
+    dst = torch.empty((rows, row_stride(gtype, k)), dtype=torch.uint8, device=device)
+    check(_native.lib().cl_repack_rows(gtype, _p(src), _p(dst), rows, k, _stream()), "cl_repack_rows")
+    return dst
+
+
+def xq_bytes(k: int) -> int:
+    return int(_native.lib().cl_xq_bytes(k))
+
+
+def quantize_xq(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    k = x.numel()
+    if out is None:
+        out = torch.empty(xq_bytes(k), dtype=torch.uint8, device=x.device)
+    check(_native.lib().cl_quantize_xq(_p(x), k, _p(out), _stream()), "cl_quantize_xq")
+    return out
+
+
+def gemv_xq(gtype: int, w: torch.Tensor, n: int, k: int, xq: torch.Tensor, bias=None, residual=None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(n, dtype=torch.float32, device=w.device)
+    check(_native.lib().cl_gemv_xq(gtype, _p(w), w.stride(0), n, k, _p(xq), _p(bias), _p(residual), _p(out),
+                                   _stream()), "cl_gemv_xq")
+    return out
+
+
+def gemv(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None) -> torch.Tensor:
+    ws = torch.empty(xq_bytes(k), dtype=torch.uint8, device=x.device)
+    out = torch.empty(n, dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_gemv(gtype, _p(w), w.stride(0), n, k, _p(x), _p(bias), _p(out), _p(ws), ws.numel(),
+                                _stream()), "cl_gemv")
+    return out
+
+
+def gemv_multi(segments: Sequence[tuple], k: int, xq: torch.Tensor) -> None:
+    """segments: (gtype, w, n, bias, residual, out) tuples sharing x."""
+    arr = (_native.GemvSegment * len(segments))()
+    for i, (gtype, w, n, bias, res, out) in enumerate(segments):
+        arr[i] = _native.GemvSegment(gtype, w.data_ptr(), w.stride(0), n,
+                                     0 if bias is None else bias.data_ptr(),
+                                     0 if res is None else res.data_ptr(), out.data_ptr())
+    check(_native.lib().cl_gemv_xq_multi(arr, len(segments), k, _p(xq), _stream()), "cl_gemv_xq_multi")
+
+
+def gemv_swiglu(gtype: int, w_gate: torch.Tensor, w_up: torch.Tensor, n: int, k: int, xq: torch.Tensor):
+    out = torch.empty(n, dtype=torch.float32, device=w_gate.device)
+    check(_native.lib().cl_gemv_xq_swiglu(gtype, _p(w_gate), _p(w_up), w_gate.stride(0), n, k, _p(xq), _p(out),
+                                          _stream()), "cl_gemv_xq_swiglu")
+    return out
+
+
+def gemm(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None):
+    m = x.shape[0]
+    out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_gemm(gtype, _p(w), w.stride(0), n, k, _p(x), m, _p(bias), _p(residual), _p(out),
+                                _stream()), "cl_gemm")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float, want_xq: bool = False):
+    rows, k = x.shape
+    y = torch.empty_like(x)
+    xq = torch.empty(rows * xq_bytes(k), dtype=torch.uint8, device=x.device) if want_xq else None
+    check(_native.lib().cl_rmsnorm(_p(x), _p(gamma), rows, k, eps, _p(y), _p(xq), _stream()), "cl_rmsnorm")
+    return (y, xq) if want_xq else y
+
+
+def embed(gtype: int, table: torch.Tensor, vocab: int, k: int, ids: torch.Tensor):
+    out = torch.empty((ids.numel(), k), dtype=torch.float32, device=ids.device)
+    flag = torch.zeros(1, dtype=torch.int32, device=ids.device)
+    check(_native.lib().cl_embed(gtype, _p(table), table.stride(0), vocab, k, _p(ids), ids.numel(), _p(out),
+                                 _p(flag), _stream()), "cl_embed")
+    return out, flag
+
+
+def rope_kv(q, k, v, rows, hq, hkv, d, rot, table, pos: int, k_cache, v_cache, pos_dev=None):
+    check(_native.lib().cl_rope_kv(_p(q), _p(k), _p(v), rows, hq, hkv, d, rot, _p(table), _p(pos_dev), pos,
+                                   _p(k_cache), _p(v_cache), _stream()), "cl_rope_kv")
+
+
+def attn_decode(q, k_cache, v_cache, length: int, max_len: int, hq, hkv, d, scale, want_xq=False):
+    dev = q.device
+    out = torch.empty(hq * d, dtype=torch.float32, device=dev)
+    wsb = int(_native.lib().cl_attn_decode_workspace_bytes(hq, d, max_len))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    ln = torch.tensor([length], dtype=torch.int32, device=dev)
+    xq = torch.empty(xq_bytes(hq * d), dtype=torch.uint8, device=dev) if want_xq else None
+    check(_native.lib().cl_attn_decode(_p(q), _p(k_cache), _p(v_cache), _p(ln), max_len, hq, hkv, d, scale,
+                                       _p(out), _p(xq), _p(ws), wsb, _stream()), "cl_attn_decode")
+    return (out, xq) if want_xq else out
+
+
+def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d):
+    out = torch.empty((rows, hq * d), dtype=torch.float32, device=q.device)
+    check(_native.lib().cl_attn_prefill(_p(q), _p(k_cache), _p(v_cache), pos0, rows, hq, hkv, d, _p(out),
+                                        _stream()), "cl_attn_prefill")
+    return out
+
+
+def argmax_workspace(n: int, device="cuda") -> torch.Tensor:
+    """Zeroed argmax workspace (the kernel re-arms it after every call)."""
+    return torch.zeros(int(_native.lib().cl_argmax_workspace_bytes(n)), dtype=torch.uint8, device=device)
+
+
+def argmax(x: torch.Tensor, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    n = x.numel()
+    if ws is None:
+        ws = argmax_workspace(n, x.device)
+    tok = torch.empty(1, dtype=torch.int32, device=x.device)
+    check(_native.lib().cl_argmax(_p(x), n, _p(tok), _p(ws), ws.numel(), _stream()), "cl_argmax")
+    return tok
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(g)
+    check(_native.lib().cl_swiglu(_p(g), _p(u), _p(out), g.numel(), _stream()), "cl_swiglu")
+    return out

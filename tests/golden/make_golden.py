@@ -1,0 +1,124 @@
+"""Generate the golden fixtures of tests/golden from the reference itself.
+
+Runs the reference's own CPU path (CPULLM's sequence through
+oracle/ref_harness.cpp, built from the reference sources by oracle/Makefile)
+on seeded synthetic GGUF models written by myllm_b200.synth_gguf, and
+stores tokens and logits.  The GGUF SHA-256 is stored with each fixture so a
+test can tell when the generator no longer reproduces the same file.
+
+    python tests/golden/make_golden.py [--skip-05b]
+
+Fixtures:
+  tiny_s{seed}.npz   every format on some tensor (hidden 256, 2 layers),
+                     prompt 8 and 40 tokens, prefill + 4 greedy decodes, full
+                     logits from the reference.
+  blocks.npz         per format: native rows and the reference's dequantized
+                     FP32 values (known-answer vectors for the block decoders).
+  qwen2_05b.npz      BASELINE config 0 (Qwen2.5-0.5B shape): 16-token prompt,
+                     prefill + 4 decodes; tokens, top-64 logits, every 16th
+                     logit, max |logit| and the top-1/top-2 margin per step.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+from myllm_b200 import synth_gguf as sg  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def run_reference(path: str, prompt: np.ndarray, steps: int):
+    ref = oracle.ReferenceCPU(path)
+    tok, lg = ref.prefill(prompt)
+    tokens, logits = [tok], [lg]
+    for _ in range(steps):
+        tok, lg = ref.decode(tok)
+        tokens.append(tok)
+        logits.append(lg)
+    # the harness's argmax must equal CPULLM's own token sequence
+    cpu = oracle.ReferenceCPULLM(path)
+    t = [cpu.prefill(prompt)]
+    for _ in range(steps):
+        t.append(cpu.decode(t[-1]))
+    assert t == tokens, (t, tokens)
+    cpu.close()
+    return ref, np.array(tokens, dtype=np.int32), np.stack(logits)
+
+
+def tiny(seed: int, tmp: str) -> None:
+    spec = sg.tiny_spec(seed=seed)
+    path = os.path.join(tmp, f"tiny{seed}.gguf")
+    sha = sg.write_qwen2(spec, path)
+    out = {"sha256": np.array(sha), "seed": np.array(seed)}
+    for n in (8, 40):
+        prompt = sg.prompt_ids(spec.seed, n, spec.vocab)
+        ref, toks, logits = run_reference(path, prompt, 4)
+        out[f"prompt{n}"] = prompt
+        out[f"tokens{n}"] = toks
+        out[f"logits{n}"] = logits.astype(np.float32)
+        ref.close()
+    np.savez_compressed(os.path.join(HERE, f"tiny_s{seed}.npz"), **out)
+
+
+def blocks(tmp: str) -> None:
+    spec = sg.tiny_spec(seed=7)
+    path = os.path.join(tmp, "tiny7.gguf")
+    if not os.path.exists(path):
+        sg.write_qwen2(spec, path)
+    ref = oracle.ReferenceCPU(path)
+    out = {}
+    picks = {sg.Q4_K: (0, "attn_q"), sg.Q6_K: (0, "attn_v"), sg.Q5_0: (1, "attn_q"), sg.Q8_0: (1, "attn_v")}
+    for gtype, (layer, name) in picks.items():
+        vals = ref.tensor(layer, name)[:4]
+        rows, cols = 4, vals.shape[1]
+        full_rows = ref.tensor(layer, name).shape[0]
+        key = sg.stream_key(spec.seed, f"blk.{layer}.{name}.weight")
+        raw = sg.fill(gtype, full_rows, cols, key, 0.0, spec.weight_std)[:rows]
+        out[f"raw_{sg.TYPE_NAMES[gtype]}"] = raw
+        out[f"ref_{sg.TYPE_NAMES[gtype]}"] = vals
+    ref.close()
+    np.savez_compressed(os.path.join(HERE, "blocks.npz"), **out)
+
+
+def qwen2_05b(tmp: str) -> None:
+    spec = sg.CONFIGS["qwen2.5-0.5b"]
+    path = os.path.join(tmp, "q05b.gguf")
+    sha = sg.write_qwen2(spec, path)
+    prompt = sg.prompt_ids(spec.seed, 16, spec.vocab)
+    ref, toks, logits = run_reference(path, prompt, 4)
+    ref.close()
+    order = np.argsort(-logits, axis=1, kind="stable")[:, :64]
+    top_vals = np.take_along_axis(logits, order, axis=1)
+    srt = np.sort(logits, axis=1)
+    np.savez_compressed(os.path.join(HERE, "qwen2_05b.npz"), sha256=np.array(sha), prompt=prompt, tokens=toks,
+                        top_idx=order.astype(np.int32), top_val=top_vals.astype(np.float32),
+                        stride16=logits[:, ::16].astype(np.float32),
+                        maxabs=np.abs(logits).max(axis=1).astype(np.float32),
+                        margin=(srt[:, -1] - srt[:, -2]).astype(np.float32))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--skip-05b", action="store_true")
+    args = ap.parse_args()
+    if not oracle.ref_available():
+        oracle.build()
+    with tempfile.TemporaryDirectory() as tmp:
+        for seed in (7, 11):
+            tiny(seed, tmp)
+        blocks(tmp)
+        if not args.skip_05b:
+            qwen2_05b(tmp)
+
+
+if __name__ == "__main__":
+    main()

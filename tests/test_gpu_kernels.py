@@ -1,0 +1,242 @@
+"""GPU parity of the individual kernels against the oracle (CPU restatement
+of the reference arithmetic) or, for floating-point activation kernels, a
+plain FP64/FP32 restatement of the reference formula.
+
+Tolerances: GEMV/GEMM |y - y_ref| <= 2e-5 * max|y_ref| (the XQ activation
+encoding is exact to max|x_block| * 2^-22; the rest is FP32 summation order);
+activation kernels are compared at FP32 rounding level.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from myllm_b200 import kernels as K
+from myllm_b200 import synth_gguf as sg
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = [sg.Q4_K, sg.Q5_K, sg.Q6_K, sg.Q5_0, sg.Q8_0]
+# BASELINE config 1 sweep shapes (N x K); K-quants skip K = 896.
+SWEEP = [(896, 896), (4864, 896), (896, 4864), (18944, 3584), (3584, 18944), (13824, 5120)]
+
+
+def weights(gtype, n, k, seed=1):
+    return sg.fill(gtype, n, k, sg.stream_key(seed, f"w{gtype}_{n}_{k}"), 0.0, 0.02)
+
+
+def xvec(k, m=1, seed=2, std=1.0):
+    return sg.normal(m * k, sg.stream_key(seed, f"x{k}_{m}"), 0.0, std).reshape(m, k)
+
+
+def rel_err(got, ref):
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def applicable(gtype, k):
+    return k % sg.BLOCK[gtype][0] == 0
+
+
+@pytest.mark.parametrize("gtype", FORMATS)
+@pytest.mark.parametrize("n,k", SWEEP)
+def test_gemv_sweep(cuda, gtype, n, k):
+    if not applicable(gtype, k):
+        pytest.skip("K not a multiple of the block size")
+    w = weights(gtype, n, k)
+    x = xvec(k)
+    ref = oracle.gemm(gtype, w, n, k, x)[0]
+    wd = K.repack(gtype, w, k)
+    got = K.gemv(gtype, wd, n, k, torch.from_numpy(x[0]).cuda()).cpu().numpy()
+    assert rel_err(got, ref) <= 2e-5
+
+
+@pytest.mark.parametrize("gtype", FORMATS)
+def test_gemv_bias_residual_and_ragged_rows(cuda, gtype):
+    n, k = 333, 512  # n not a multiple of any CTA row tile
+    w = weights(gtype, n, k, seed=3)
+    x = xvec(k, seed=4)
+    bias = sg.normal(n, sg.stream_key(5, "b"), 0.0, 0.5)
+    res = sg.normal(n, sg.stream_key(6, "r"), 0.0, 1.0)
+    ref = oracle.gemm(gtype, w, n, k, x, bias)[0] + res
+    wd = K.repack(gtype, w, k)
+    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
+    got = K.gemv_xq(gtype, wd, n, k, xq, torch.from_numpy(bias).cuda(), torch.from_numpy(res).cuda())
+    assert rel_err(got.cpu().numpy(), ref) <= 2e-5
+
+
+def test_gemv_multi_segments_mixed_formats(cuda):
+    k = 512
+    x = xvec(k, seed=8)
+    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
+    segs, refs = [], []
+    for i, (gtype, n) in enumerate([(sg.Q4_K, 300), (sg.Q6_K, 64), (sg.Q8_0, 70), (sg.Q5_0, 33)]):
+        w = weights(gtype, n, k, seed=10 + i)
+        b = sg.normal(n, sg.stream_key(20 + i, "b"), 0.0, 0.1)
+        refs.append(oracle.gemm(gtype, w, n, k, x, b)[0])
+        out = torch.empty(n, device="cuda")
+        segs.append((gtype, K.repack(gtype, w, k), n, torch.from_numpy(b).cuda(), None, out))
+    K.gemv_multi(segs, k, xq)
+    for s, ref in zip(segs, refs):
+        assert rel_err(s[5].cpu().numpy(), ref) <= 2e-5
+
+
+@pytest.mark.parametrize("gtype", [sg.Q4_K, sg.Q5_0])
+def test_gemv_swiglu(cuda, gtype):
+    n, k = 1000, 1024
+    wg, wu = weights(gtype, n, k, seed=30), weights(gtype, n, k, seed=31)
+    x = xvec(k, seed=32)
+    g = oracle.gemm(gtype, wg, n, k, x)[0].astype(np.float64)
+    u = oracle.gemm(gtype, wu, n, k, x)[0].astype(np.float64)
+    ref = g / (1.0 + np.exp(-g)) * u
+    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
+    got = K.gemv_swiglu(gtype, K.repack(gtype, wg, k), K.repack(gtype, wu, k), n, k, xq).cpu().numpy()
+    assert rel_err(got, ref) <= 5e-5
+
+
+def test_xq_encoding_precision(cuda):
+    x = torch.from_numpy(xvec(4096, seed=40, std=3.0)[0]).cuda()
+    x[:32] = 0.0  # an all-zero block
+    xq = K.quantize_xq(x).cpu().numpy()
+    k = 4096
+    limbs = xq[: k // 16 * 48].view(np.int8).reshape(k // 16, 3, 16).astype(np.float64)
+    off = ((k // 16 * 48) + ((k // 16 * 8 + 15) // 16 * 16))
+    scale = xq[off: off + k // 32 * 4].view(np.float32).astype(np.float64)
+    t = limbs[:, 0] * 16384 + limbs[:, 1] * 128 + limbs[:, 2]
+    xr = (t.reshape(k // 32, 32) * scale[:, None]).reshape(-1)
+    xa = x.cpu().numpy().astype(np.float64)
+    bmax = np.abs(xa.reshape(-1, 32)).max(axis=1).repeat(32)
+    assert np.all(np.abs(xr - xa) <= bmax * 2.0 ** -21 + 1e-30)
+    assert np.all(xr[:32] == 0.0)
+
+
+@pytest.mark.parametrize("gtype", FORMATS)
+@pytest.mark.parametrize("m", [1, 7, 128])
+def test_gemm_small(cuda, gtype, m):
+    n, k = 384, 512
+    w = weights(gtype, n, k, seed=50)
+    x = xvec(k, m, seed=51)
+    b = sg.normal(n, sg.stream_key(52, "b"), 0.0, 0.1)
+    r = xvec(n, m, seed=53)
+    ref = oracle.gemm(gtype, w, n, k, x, b) + r
+    got = K.gemm(gtype, K.repack(gtype, w, k), n, k, torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda(),
+                 torch.from_numpy(r).cuda())
+    assert rel_err(got.cpu().numpy(), ref) <= 2e-5
+
+
+def test_rmsnorm_matches_reference_formula(cuda):
+    rows, k = 5, 3584
+    x = xvec(k, rows, seed=60)
+    g = sg.normal(k, sg.stream_key(61, "g"), 1.0, 0.02)
+    eps = 1e-6
+    # cpu_llm.cpp:156-165
+    ss = (x.astype(np.float64) ** 2).sum(axis=1)
+    inv = (np.float32(1.0) / np.sqrt((ss / k).astype(np.float32) + np.float32(eps))).astype(np.float32)
+    ref = x * (inv[:, None] * g[None, :])
+    y, xq = K.rmsnorm(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(), eps, want_xq=True)
+    np.testing.assert_array_equal(y.cpu().numpy(), ref.astype(np.float32))
+
+
+def rope_ref(vec, pos, theta, rot):
+    v = vec.copy()
+    half = rot // 2
+    for p in range(half):
+        f = np.float32(theta) ** np.float32(-2.0 * p / rot)
+        a = np.float32(pos) * np.float32(f)
+        c, s = np.float32(math.cos(a)), np.float32(math.sin(a))
+        x0, x1 = v[p], v[p + half]
+        v[p] = x0 * c - x1 * s
+        v[p + half] = x0 * s + x1 * c
+    return v
+
+
+@pytest.mark.parametrize("d,rot", [(64, 64), (128, 128), (256, 64)])
+def test_rope_kv_append(cuda, d, rot):
+    rows, hq, hkv, cap, pos0, theta = 3, 4, 2, 16, 5, 1e6
+    half = rot // 2
+    table = np.zeros((cap, half, 2), dtype=np.float32)
+    for pos in range(cap):
+        for p in range(half):
+            f = np.float32(theta) ** np.float32(-2.0 * p / rot)
+            a = np.float32(pos) * f
+            table[pos, p] = (np.cos(a), np.sin(a))
+    q = xvec(hq * d, rows, seed=70)
+    k = xvec(hkv * d, rows, seed=71)
+    v = xvec(hkv * d, rows, seed=72)
+    qt, kt, vt = (torch.from_numpy(a.copy()).cuda() for a in (q, k, v))
+    kc = torch.zeros(cap, hkv * d, device="cuda")
+    vc = torch.zeros(cap, hkv * d, device="cuda")
+    K.rope_kv(qt, kt, vt, rows, hq, hkv, d, rot, torch.from_numpy(table).cuda(), pos0, kc, vc)
+    for r in range(rows):
+        for h in range(hq):
+            want = rope_ref(q[r, h * d:(h + 1) * d], pos0 + r, theta, rot)
+            np.testing.assert_allclose(qt[r, h * d:(h + 1) * d].cpu().numpy(), want, rtol=0, atol=2e-6)
+        for h in range(hkv):
+            want = rope_ref(k[r, h * d:(h + 1) * d], pos0 + r, theta, rot)
+            np.testing.assert_allclose(kc[pos0 + r, h * d:(h + 1) * d].cpu().numpy(), want, rtol=0, atol=2e-6)
+        np.testing.assert_array_equal(vc[pos0 + r].cpu().numpy(), v[r])
+
+
+def attention_ref(q, kc, vc, hq, hkv, d, length):
+    out = np.zeros(hq * d, dtype=np.float64)
+    grp = hq // hkv
+    for h in range(hq):
+        g = h // grp
+        kk = kc[:length, g * d:(g + 1) * d].astype(np.float64)
+        s = kk @ q[h * d:(h + 1) * d].astype(np.float64) / math.sqrt(d)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        out[h * d:(h + 1) * d] = p @ vc[:length, g * d:(g + 1) * d]
+    return out
+
+
+@pytest.mark.parametrize("hq,hkv,d,length", [(14, 2, 64, 17), (28, 4, 128, 600), (16, 2, 256, 300), (5, 1, 128, 1)])
+def test_attention_decode(cuda, hq, hkv, d, length):
+    cap = 1024
+    q = xvec(hq * d, seed=80)[0]
+    kc = xvec(hkv * d, cap, seed=81)
+    vc = xvec(hkv * d, cap, seed=82)
+    ref = attention_ref(q, kc, vc, hq, hkv, d, length)
+    got = K.attn_decode(torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda(),
+                        length, cap, hq, hkv, d, 1.0 / math.sqrt(d))
+    assert rel_err(got.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("hq,hkv,d,pos0,rows", [(4, 2, 64, 0, 40), (28, 4, 128, 0, 70), (8, 8, 128, 33, 20)])
+def test_attention_prefill(cuda, hq, hkv, d, pos0, rows):
+    cap = pos0 + rows
+    q = xvec(hq * d, rows, seed=90)
+    kc = xvec(hkv * d, cap, seed=91)
+    vc = xvec(hkv * d, cap, seed=92)
+    got = K.attn_prefill(torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda(),
+                         pos0, rows, hq, hkv, d).cpu().numpy()
+    for r in range(rows):
+        ref = attention_ref(q[r], kc, vc, hq, hkv, d, pos0 + r + 1)
+        assert rel_err(got[r], ref) <= 1e-5, r
+
+
+def test_argmax_lowest_index_on_ties(cuda):
+    n = 152064
+    x = torch.from_numpy(xvec(n, seed=100)[0]).cuda()
+    ws = K.argmax_workspace(n)
+    assert int(K.argmax(x, ws)) == int(torch.argmax(x))
+    x[7] = 1e6
+    x[100000] = 1e6
+    x[150000] = 1e6
+    assert int(K.argmax(x, ws)) == 7  # workspace re-armed by the previous call
+    x.fill_(0.5)
+    assert int(K.argmax(x, ws)) == 0
+
+
+@pytest.mark.parametrize("gtype", FORMATS)
+def test_embedding_rows_are_reference_values(cuda, gtype):
+    vocab, k = 50, 512
+    w = weights(gtype, vocab, k, seed=110)
+    ref = oracle.dequant(gtype, w, vocab, k)
+    ids = torch.tensor([3, 0, 49, 3, 60, -1], dtype=torch.int32, device="cuda")
+    out, flag = K.embed(gtype, K.repack(gtype, w, k), vocab, k, ids)
+    out = out.cpu().numpy()
+    for i, t in enumerate([3, 0, 49, 3]):
+        np.testing.assert_array_equal(out[i], ref[t])
+    assert np.all(out[4:] == 0) and int(flag) == 1

@@ -1,0 +1,139 @@
+"""End-to-end parity of CudaLLM with the reference CPULLM path.
+
+Tokens must be identical at every step; logits must satisfy
+max|g - r| / max|r| <= 1e-2 (the tolerance of the north-star spec).  The
+observed error is far smaller (~1e-5), which the tighter 1e-4 check pins.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from myllm_b200 import CudaLLM, InvalidArgument, LengthError, OutOfRange
+from myllm_b200 import synth_gguf as sg
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / np.abs(b).max())
+
+
+@pytest.fixture(scope="module")
+def tiny_models(model_dir, cuda):
+    paths = {}
+    for seed in (7, 11):
+        d = np.load(os.path.join(GOLDEN, f"tiny_s{seed}.npz"))
+        path = os.path.join(model_dir, f"tiny_s{seed}.gguf")
+        sha = sg.write_qwen2(sg.tiny_spec(seed=seed), path)
+        assert sha == str(d["sha256"])
+        paths[seed] = (path, d)
+    return paths
+
+
+@pytest.mark.parametrize("seed", [7, 11])
+@pytest.mark.parametrize("n", [8, 40])
+def test_tiny_parity(tiny_models, seed, n):
+    path, d = tiny_models[seed]
+    llm = CudaLLM(path, max_sequence=64)
+    toks = [llm.prefill(d[f"prompt{n}"])]
+    logits = [llm.last_logits()]
+    for _ in range(4):
+        toks.append(llm.decode(toks[-1]))
+        logits.append(llm.last_logits())
+    assert toks == list(d[f"tokens{n}"])
+    for got, ref in zip(logits, d[f"logits{n}"]):
+        assert rel(got, ref) <= 1e-2
+        assert rel(got, ref) <= 1e-4
+    llm.close()
+
+
+def test_prefill_chunking_matches_single_pass(tiny_models, monkeypatch):
+    """A prompt split into several prefill chunks (later chunks attend to the
+    earlier ones through the KV cache) gives the one-shot result, and a
+    reset conversation reproduces it."""
+    path, d = tiny_models[7]
+    prompt = sg.prompt_ids(99, 150, 1024)
+    one = CudaLLM(path, max_sequence=200)
+    t1 = one.prefill(prompt)
+    l1 = one.last_logits()
+    d1 = one.decode(t1)
+    one.reset()
+    assert one.prefill(prompt) == t1 and np.array_equal(l1, one.last_logits())
+    one.close()
+    monkeypatch.setenv("CUDALLM_PREFILL_CHUNK", "48")
+    chunked = CudaLLM(path, max_sequence=200)
+    assert chunked.prefill(prompt) == t1
+    assert rel(chunked.last_logits(), l1) <= 1e-6
+    assert chunked.decode(t1) == d1
+    chunked.close()
+
+
+def test_protocol_errors(tiny_models):
+    path, d = tiny_models[7]
+    llm = CudaLLM(path, max_sequence=16)
+    with pytest.raises(InvalidArgument):
+        llm.decode(1)  # decode before prefill
+    with pytest.raises(InvalidArgument):
+        llm.prefill([])
+    with pytest.raises(OutOfRange):
+        llm.prefill([1, 2, 1024])
+    with pytest.raises(OutOfRange):
+        llm.prefill([-1])
+    with pytest.raises(LengthError):
+        llm.prefill(list(range(17)))
+    tok = llm.prefill(list(range(15)))
+    with pytest.raises(InvalidArgument):
+        llm.prefill([1])  # requires reset
+    with pytest.raises(OutOfRange):
+        llm.decode(5000)
+    tok = llm.decode(tok)
+    assert llm.position == 16
+    with pytest.raises(LengthError):
+        llm.decode(tok)  # capacity reached
+    llm.reset()
+    assert llm.position == 0
+    assert llm.prefill([3, 4]) >= 0
+    stats = llm.memory_stats()
+    assert stats.weight_bytes > 0 and stats.kv_cache_bytes == 2 * 2 * 16 * 2 * 64 * 4
+    assert llm.uses_gpu() and "B200" in llm.device_name()
+    llm.close()
+
+
+def test_bad_model_files(tmp_path, cuda):
+    with pytest.raises(RuntimeError):
+        CudaLLM(str(tmp_path / "missing.gguf"))
+    p = tmp_path / "trunc.gguf"
+    full = tmp_path / "full.gguf"
+    sg.write_qwen2(sg.tiny_spec(seed=7), str(full))
+    p.write_bytes(full.read_bytes()[:5000])
+    with pytest.raises(RuntimeError):
+        CudaLLM(str(p))
+    with pytest.raises(InvalidArgument):
+        CudaLLM(str(full), max_sequence=10**6)
+
+
+def test_qwen2_05b_parity(model_dir, cuda):
+    """BASELINE config 0 against the reference's tokens and logits."""
+    d = np.load(os.path.join(GOLDEN, "qwen2_05b.npz"))
+    spec = sg.CONFIGS["qwen2.5-0.5b"]
+    path = os.path.join(model_dir, "qwen2.5-0.5b.gguf")
+    if not os.path.exists(path) or os.path.getsize(path) == 0:
+        sha = sg.write_qwen2(spec, path)
+        assert sha == str(d["sha256"])
+    llm = CudaLLM(path, max_sequence=64)
+    toks = [llm.prefill(d["prompt"])]
+    logits = [llm.last_logits()]
+    for _ in range(4):
+        toks.append(llm.decode(toks[-1]))
+        logits.append(llm.last_logits())
+    assert toks == list(d["tokens"])
+    for i, lg in enumerate(logits):
+        err_top = np.abs(lg[d["top_idx"][i]] - d["top_val"][i]).max()
+        err_s = np.abs(lg[::16] - d["stride16"][i]).max()
+        assert max(err_top, err_s) / d["maxabs"][i] <= 1e-2
+        assert max(err_top, err_s) / d["maxabs"][i] <= 1e-4
+        assert abs(np.abs(lg).max() - d["maxabs"][i]) / d["maxabs"][i] <= 1e-4
+    llm.close()
