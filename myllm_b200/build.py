@@ -23,6 +23,18 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+
+
+def _nccl_dir():
+    """The NCCL that PyTorch ships, so that one libnccl.so.2 serves both."""
+    try:
+        import nvidia.nccl  # type: ignore
+        d = os.path.join(list(nvidia.nccl.__path__)[0], "lib")
+        if os.path.exists(os.path.join(d, "libnccl.so.2")):
+            return d
+    except ImportError:
+        pass
+    return None
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -99,7 +111,9 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError("CUDA build failed for: " + ", ".join(failed))
     tmp = out + ".tmp"
-    _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lnccl", "-lpthread", "-ldl", "-lrt"])
+    nd = _nccl_dir()
+    nccl = ["-L", nd, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + nd] if nd else ["-lnccl"]
+    _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, *nccl, "-lpthread", "-ldl", "-lrt"])
     os.replace(tmp, out)
     return out
 
