@@ -164,23 +164,23 @@ def time_gateup_kernel(spec, iters: int):
     base = K.repack(gtype, wn, H)
     copies = [(base.clone(), base.clone()) for _ in range(4)]
     x = torch.randn(H, device="cuda")
-    xq = K.quantize_xq(x)
+    gamma = torch.ones(H, device="cuda")
     for i in range(8):
         g, u = copies[i % 4]
-        K.gemv_swiglu(gtype, g, u, F, H, xq)
+        K.gemv_swiglu(gtype, g, u, F, H, x, gamma, 1e-6)
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for i in range(iters):
         g, u = copies[i % 4]
-        K.gemv_swiglu(gtype, g, u, F, H, xq)
+        K.gemv_swiglu(gtype, g, u, F, H, x, gamma, 1e-6)
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / iters
-    algo = 2 * F * sg.row_bytes(gtype, H) + K.xq_bytes(H) + 4 * F
+    algo = 2 * F * sg.row_bytes(gtype, H) + 2 * 4 * H + 4 * F  # weights + x, gamma + y
     del copies
-    return {"kernel": "gemv_kernel<4,true> (fused gate/up GEMV + SwiGLU)", "shape": f"2x[{F},{H}] {sg.TYPE_NAMES[gtype]}",
+    return {"kernel": "gemv_tma_kernel<8,true> (RMSNorm + gate/up GEMV + SwiGLU)", "shape": f"2x[{F},{H}] {sg.TYPE_NAMES[gtype]}",
             "bytes_per_launch": algo, "avg_launch_us": ms * 1e3, "gbs": algo / (ms * 1e-3) / 1e9}
 
 
@@ -284,7 +284,7 @@ def bench_cuda(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
-    launches_per_step = 1 + 10 * spec.layers + 4
+    launches_per_step = 1 + 7 * spec.layers + 3
     line = {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),

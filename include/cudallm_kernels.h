@@ -67,9 +67,12 @@ CL_API int cl_quantize_xq(const float* x, int k, void* xq, cudaStream_t stream);
 
 /* ---- decode GEMV (metal_gevm_*_f32, metal_llm.metal:708-781; CPU gevmtb
  * cpu_llm.cpp:528-547) ----------------------------------------------------
- * y[n] = W[n,k] . x (+ bias[n]) (+ residual[n]); W in the device layout. */
-CL_API int cl_gemv_xq(int type, const void* w, long long stride, int n, int k, const void* xq,
-                      const float* bias, const float* residual, float* y, cudaStream_t stream);
+ * y[n] = W[n,k] . x (+ bias[n]) (+ residual[n]); W in the device layout,
+ * x FP32 (16-byte aligned), k % 32 == 0 and k <= 20480.  The kernel encodes
+ * x as XQ on the fly (each CTA in registers), so no workspace is needed.
+ * y may alias residual (in-place residual add). */
+CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x,
+                   const float* bias, const float* residual, float* y, cudaStream_t stream);
 
 typedef struct {
     int type;
@@ -81,18 +84,19 @@ typedef struct {
     float* y;
 } cl_gemv_segment;
 
-/* Up to 4 matrices sharing one input vector (e.g. Q, K and V) in one launch. */
-CL_API int cl_gemv_xq_multi(const cl_gemv_segment* segs, int nseg, int k, const void* xq,
-                            cudaStream_t stream);
-/* y[i] = SiLU(gate_i . x) * (up_i . x): gate/up GEMV with the SwiGLU
- * (cpu_llm.cpp:188-202, metal_swiglu_f32 metal_llm.metal:895) fused. */
-CL_API int cl_gemv_xq_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n,
-                             int k, const void* xq, float* y, cudaStream_t stream);
-/* FP32 input convenience form: quantizes x into `workspace`
- * (>= cl_xq_bytes(k)) and runs cl_gemv_xq. */
-CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x,
-                   const float* bias, float* y, void* workspace, size_t workspace_bytes,
-                   cudaStream_t stream);
+/* Up to 4 matrices (any mix of formats) sharing one input vector, e.g. Q, K
+ * and V, in one launch.  With norm_gamma != NULL the input is first RMS-
+ * normalised (cpu_llm.cpp:143-166: double sum of squares, x*(inv*gamma)). */
+CL_API int cl_gemv_multi(const cl_gemv_segment* segs, int nseg, int k, const float* x,
+                         const float* norm_gamma, float eps, cudaStream_t stream);
+/* y[i] = SiLU(gate_i . x') * (up_i . x'), x' = optional RMSNorm of x: the
+ * gate/up GEMV with SwiGLU (cpu_llm.cpp:188-202, metal_swiglu_f32
+ * metal_llm.metal:895) fused.  gate and up share type and stride. */
+CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n, int k,
+                          const float* x, const float* norm_gamma, float eps, float* y, cudaStream_t stream);
+/* Device error word of the pipelined kernels: non-zero when a bounded wait
+ * gave up (never expected).  Synchronous; clear != 0 resets it. */
+CL_API int cl_device_error(int* code, int clear);
 
 /* ---- prefill GEMM (metal_gemm_*_f32, metal_llm.metal:621-704; CPU gemmtb
  * cpu_llm.cpp:631-653) ----------------------------------------------------

@@ -31,10 +31,10 @@ SIGNATURES = {
     "cl_repack_rows": (c_int, [c_int, c_vp, c_vp, c_int, c_int, c_vp]),
     "cl_xq_bytes": (c_size, [c_int]),
     "cl_quantize_xq": (c_int, [c_vp, c_int, c_vp, c_vp]),
-    "cl_gemv_xq": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
-    "cl_gemv_xq_multi": (c_int, [ctypes.POINTER(GemvSegment), c_int, c_int, c_vp, c_vp]),
-    "cl_gemv_xq_swiglu": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
-    "cl_gemv": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_size, c_vp]),
+    "cl_gemv": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gemv_multi": (c_int, [ctypes.POINTER(GemvSegment), c_int, c_int, c_vp, c_vp, c_float, c_vp]),
+    "cl_gemv_swiglu": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    "cl_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "cl_gemm": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
     "cl_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp]),
     "cl_embed": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),

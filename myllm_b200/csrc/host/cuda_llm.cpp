@@ -145,7 +145,6 @@ struct CudaLLM::Impl {
     // decode activations
     float *h = nullptr, *part = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
           *att_full = nullptr, *act = nullptr, *logits = nullptr;
-    void *xq_h = nullptr, *xq_att = nullptr, *xq_act = nullptr;
     void *attn_ws = nullptr, *arg_ws = nullptr;
     std::size_t attn_ws_bytes = 0, arg_ws_bytes = 0;
     int32_t* ints = nullptr;  // [0] token in, [1] pos, [2] len, [3] token out, [4..] scratch
@@ -267,9 +266,6 @@ struct CudaLLM::Impl {
         att_full = a.take_n<float>(hq * d);
         act = a.take_n<float>(F_l);
         logits = a.take_n<float>(V_l);
-        xq_h = a.take(cl_xq_bytes((int)H));
-        xq_att = a.take(cl_xq_bytes((int)std::max(o_kl, qd_l)));
-        xq_act = a.take(cl_xq_bytes((int)F_l));
         attn_ws_bytes = cl_attn_decode_workspace_bytes((int)hq_l, (int)d, (int)max_seq);
         attn_ws = a.take(attn_ws_bytes);
         arg_ws_bytes = cl_argmax_workspace_bytes((int)V_l);
@@ -360,10 +356,11 @@ struct CudaLLM::Impl {
         CUDALLM_NCCL(ncclAllReduce(send, recv, n, ncclFloat32, ncclSum, comm, stream));
     }
 
-    // LM head + greedy token for the normalised last row already in xq_h.
-    void record_head(int32_t* token_out) {
+    // Final RMSNorm + LM head + greedy token for the hidden row `hrow`.
+    void record_head(const float* hrow, int32_t* token_out) {
         cudaStream_t s = stream;
-        CUDALLM_CL(cl_gemv_xq(out_w.type, out_w.ptr, out_w.stride, (int)V_l, (int)H, xq_h, nullptr, nullptr, logits, s));
+        const cl_gemv_segment seg{out_w.type, out_w.ptr, out_w.stride, (int)V_l, nullptr, nullptr, logits};
+        CUDALLM_CL(cl_gemv_multi(&seg, 1, (int)H, hrow, out_norm, eps(), s));
         if (par.world == 1) {
             CUDALLM_CL(cl_argmax(logits, (int)V_l, token_out, arg_ws, arg_ws_bytes, s));
         } else {
@@ -388,31 +385,29 @@ struct CudaLLM::Impl {
         float* out = W > 1 ? part : h;
         const float* res = par.rank == 0 ? h : nullptr;
         for (Layer& L : layers) {
-            CUDALLM_CL(cl_rmsnorm(h, L.attn_norm, 1, (int)H, eps(), nullptr, xq_h, s));
             const cl_gemv_segment segs[3] = {
                 {L.q.type, L.q.ptr, L.q.stride, L.q.rows, L.q_b, nullptr, q},
                 {L.k.type, L.k.ptr, L.k.stride, L.k.rows, L.k_b, nullptr, k},
                 {L.v.type, L.v.ptr, L.v.stride, L.v.rows, L.v_b, nullptr, v},
             };
-            CUDALLM_CL(cl_gemv_xq_multi(segs, 3, (int)H, xq_h, s));
+            CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, h, L.attn_norm, eps(), s));
             CUDALLM_CL(cl_rope_kv(q, k, v, 1, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, pos, 0,
                                   L.k_cache, L.v_cache, s));
             CUDALLM_CL(cl_attn_decode(q, L.k_cache, L.v_cache, len, (int)max_seq, (int)hq_l, (int)hkv_l, (int)d, scale,
-                                      att, gather_attn ? nullptr : xq_att, attn_ws, attn_ws_bytes, s));
+                                      att, nullptr, attn_ws, attn_ws_bytes, s));
+            const float* o_in = att;
             if (gather_attn) {
                 CUDALLM_NCCL(ncclAllGather(att, att_full, hq_l * d, ncclFloat32, comm, s));
-                CUDALLM_CL(cl_quantize_xq(att_full + o_k0, (int)o_kl, xq_att, s));
+                o_in = att_full + o_k0;
             }
-            CUDALLM_CL(cl_gemv_xq(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, xq_att, nullptr, res, out, s));
+            CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, nullptr, res, out, s));
             if (W > 1) all_reduce(part, h, H);
-            CUDALLM_CL(cl_rmsnorm(h, L.ffn_norm, 1, (int)H, eps(), nullptr, xq_h, s));
-            CUDALLM_CL(cl_gemv_xq_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, xq_h, act, s));
-            CUDALLM_CL(cl_quantize_xq(act, (int)F_l, xq_act, s));
-            CUDALLM_CL(cl_gemv_xq(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, xq_act, nullptr, res, out, s));
+            CUDALLM_CL(cl_gemv_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, h, L.ffn_norm,
+                                      eps(), act, s));
+            CUDALLM_CL(cl_gemv(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, act, nullptr, res, out, s));
             if (W > 1) all_reduce(part, h, H);
         }
-        CUDALLM_CL(cl_rmsnorm(h, out_norm, 1, (int)H, eps(), nullptr, xq_h, s));
-        record_head(ints + 3);
+        record_head(h, ints + 3);
         CUDALLM_CL(cl_counter_add(pos, 2, 1, s));
         CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     }
@@ -511,8 +506,7 @@ struct CudaLLM::Impl {
             prefill_chunk_layers((int)m, (int)c0);
             last_m = m;
         }
-        CUDALLM_CL(cl_rmsnorm(X + (last_m - 1) * H, out_norm, 1, (int)H, eps(), nullptr, xq_h, stream));
-        record_head(ints + 3);
+        record_head(X + (last_m - 1) * H, ints + 3);
         int32_t* hi = host_in();
         hi[2] = (int32_t)n;
         hi[3] = (int32_t)(n + 1);

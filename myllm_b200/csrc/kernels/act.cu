@@ -199,14 +199,6 @@ CL_API int cl_quantize_xq(const float* x, int k, void* xq, cudaStream_t stream) 
                : CL_ERR_CUDA;
 }
 
-CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x, const float* bias,
-                   float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-    if (workspace == nullptr || workspace_bytes < cl_xq_bytes(k) || cl_xq_bytes(k) == 0) return CL_ERR_WORKSPACE;
-    int rc = cl_quantize_xq(x, k, workspace, stream);
-    if (rc != CL_OK) return rc;
-    return cl_gemv_xq(type, w, stride, n, k, workspace, bias, nullptr, y, stream);
-}
-
 CL_API int cl_rmsnorm(const float* x, const float* gamma, int rows, int k, float eps, float* y, void* xq,
                       cudaStream_t stream) {
     if (x == nullptr || gamma == nullptr || rows <= 0 || k <= 0 || !(eps > 0.0f)) return CL_ERR_INVALID;

@@ -18,14 +18,20 @@
 
 namespace cl {
 
-constexpr int kKeysPerSplit = 256;
-constexpr int kDecThreads = 256;
+constexpr int kKeysPerSplit = 64;   // decode split size (keys)
+constexpr int kDecThreads = 128;
 constexpr int kMaxGroup = 16;
 constexpr int kMaxHeadDim = 256;
 
 __host__ __device__ inline int attn_splits(int max_len) { return (max_len + kKeysPerSplit - 1) / kKeysPerSplit; }
 
-// partial record per (q head, split): [m, l, o[d]]
+// Dynamic smem: q [group][d] | tile [64][d + 4] (K, then V) | p [group][64] | stats [group][2]
+__host__ __device__ inline size_t attn_decode_smem(int group, int d) {
+    return sizeof(float) * ((size_t)group * d + (size_t)kKeysPerSplit * (d + 4) + (size_t)group * kKeysPerSplit +
+                            2 * group);
+}
+
+// partial record per (q head, split): [m, l, o[d]] with o unnormalised
 __global__ void __launch_bounds__(kDecThreads)
 attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                   const int* __restrict__ len_dev, int hq, int hkv, int d, float scale,
@@ -38,32 +44,34 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
     const int k0 = split * kKeysPerSplit;
     const int nk = min(kKeysPerSplit, L - k0);
     const int rec = d + 2;
-    if (nk <= 0) {
-        if (threadIdx.x < group) {
-            float* pr = part + ((size_t)(g * group + threadIdx.x) * splits + split) * rec;
-            pr[0] = -INFINITY;
-            pr[1] = 0.0f;
-        }
-        return;
+    if (nk <= 0) return;  // the combine kernel only reads splits below ceil(L / 64)
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;                                    // [group][d]
+    float* tile = qs + group * d;                      // [64][d + 4]
+    float* ps = tile + kKeysPerSplit * (d + 4);        // [group][64]
+    float* st = ps + group * kKeysPerSplit;            // [group][2]
+    const int kvd = hkv * d, d4 = d / 4, ld = d + 4;
+    for (int i = threadIdx.x; i < group * d4; i += kDecThreads)
+        reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q + (size_t)g * group * d)[i];
+    // K tile, coalesced float4 rows into padded smem rows
+    for (int i = threadIdx.x; i < nk * d4; i += kDecThreads) {
+        const int t = i / d4, c = i % d4;
+        *reinterpret_cast<float4*>(tile + t * ld + 4 * c) =
+            reinterpret_cast<const float4*>(kc + (size_t)(k0 + t) * kvd + (size_t)g * d)[c];
     }
-    __shared__ __align__(16) float qs[kMaxGroup * kMaxHeadDim];
-    __shared__ float sc[kMaxGroup][kKeysPerSplit];
-    __shared__ float red[kMaxGroup][2];
-    for (int i = threadIdx.x; i < group * d; i += kDecThreads) qs[i] = q[(size_t)g * group * d + i];
     __syncthreads();
-    const int kvd = hkv * d;
-    // scores: thread t -> key k0 + t
-    for (int t = threadIdx.x; t < nk; t += kDecThreads) {
-        const float4* kr = reinterpret_cast<const float4*>(kc + (size_t)(k0 + t) * kvd + (size_t)g * d);
+    // scores: thread t -> key t, all heads of the group (q reads broadcast)
+    if (threadIdx.x < nk) {
+        const int t = threadIdx.x;
         float acc[kMaxGroup];
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-        for (int i = 0; i < d / 4; ++i) {
-            const float4 kv = kr[i];
+        for (int c = 0; c < d4; ++c) {
+            const float4 kv = *reinterpret_cast<const float4*>(tile + t * ld + 4 * c);
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h) {
                 if (h < group) {
-                    const float4 qv = reinterpret_cast<const float4*>(qs + h * d)[i];
+                    const float4 qv = reinterpret_cast<const float4*>(qs + h * d)[c];
                     acc[h] += kv.x * qv.x;
                     acc[h] += kv.y * qv.y;
                     acc[h] += kv.z * qv.z;
@@ -73,39 +81,43 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         }
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h)
-            if (h < group) sc[h][t] = acc[h] * scale;
+            if (h < group) ps[h * kKeysPerSplit + t] = acc[h] * scale;
     }
     __syncthreads();
-    // per-head max and exp-sum: warp w handles heads w, w+8, ...
+    // V tile into the same buffer; per-head max/exp-sum meanwhile
+    for (int i = threadIdx.x; i < nk * d4; i += kDecThreads) {
+        const int t = i / d4, c = i % d4;
+        *reinterpret_cast<float4*>(tile + t * ld + 4 * c) =
+            reinterpret_cast<const float4*>(vc + (size_t)(k0 + t) * kvd + (size_t)g * d)[c];
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int h = warp; h < group; h += kDecThreads / 32) {
         float m = -INFINITY;
-        for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[h][t]);
+        for (int t = lane; t < nk; t += 32) m = fmaxf(m, ps[h * kKeysPerSplit + t]);
         m = warp_max(m);
         float l = 0.0f;
         for (int t = lane; t < nk; t += 32) {
-            const float e = expf(sc[h][t] - m);
-            sc[h][t] = e;
+            const float e = expf(ps[h * kKeysPerSplit + t] - m);
+            ps[h * kKeysPerSplit + t] = e;
             l += e;
         }
         l = warp_sum(l);
         if (lane == 0) {
-            red[h][0] = m;
-            red[h][1] = l;
+            st[2 * h] = m;
+            st[2 * h + 1] = l;
         }
     }
     __syncthreads();
-    // p . V: thread -> output dim
+    // p . V: thread -> output dims
     for (int dim = threadIdx.x; dim < d; dim += kDecThreads) {
         float acc[kMaxGroup];
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-        const float* vr = vc + (size_t)k0 * kvd + (size_t)g * d + dim;
         for (int t = 0; t < nk; ++t) {
-            const float vv = vr[(size_t)t * kvd];
+            const float vv = tile[t * ld + dim];
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h)
-                if (h < group) acc[h] += sc[h][t] * vv;
+                if (h < group) acc[h] += ps[h * kKeysPerSplit + t] * vv;
         }
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
@@ -113,8 +125,8 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
                 float* pr = part + ((size_t)(g * group + h) * splits + split) * rec;
                 pr[2 + dim] = acc[h];
                 if (dim == 0) {
-                    pr[0] = red[h][0];
-                    pr[1] = red[h][1];
+                    pr[0] = st[2 * h];
+                    pr[1] = st[2 * h + 1];
                 }
             }
         }
@@ -267,7 +279,15 @@ CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_c
         return CL_ERR_WORKSPACE;
     const int splits = attn_splits(max_len);
     float* part = static_cast<float*>(workspace);
-    if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), 0, stream, q, k_cache, v_cache,
+    const size_t smem = attn_decode_smem(q_heads / kv_heads, head_dim);
+    static int configured_for = 0;
+    if ((int)smem > configured_for) {
+        if (cudaFuncSetAttribute(attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return CL_ERR_CUDA;
+        configured_for = (int)smem;
+    }
+    if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), smem, stream, q, k_cache, v_cache,
                    len_dev, q_heads, kv_heads, head_dim, scale, part) != cudaSuccess)
         return CL_ERR_CUDA;
     const int threads = head_dim < 1024 ? head_dim : 1024;

@@ -3,434 +3,576 @@
 // Reference: metal_gevm_{q4_k,q6_k,q5_0,q8_0,q5_k}_f32 (metal_llm.metal:708-781)
 // and the CPU oracle gevmt/gevmtb over GgufDequantizer rows
 // (cpu_llm.cpp:512-547, model.cpp:581-683).  Same products, different order:
-// a lane owns a 32-element "unit" of a row, the block bytes are read with
-// coalesced 128-bit loads, the quantized integers are dotted with the XQ
-// limbs of x by dp4a (exact), and the per-sub-block scales are applied in
-// FP32 afterwards (the factored form d*sc*sum(x*q) - dmin*m*sum(x) that the
-// Metal kernels also use, metal_llm.metal:392-393).
+// the quantized integers are dotted with the XQ limbs of x by dp4a (exact)
+// and the per-sub-block scales are applied in FP32 afterwards (the factored
+// form d*sc*sum(x*q) - dmin*m*sum(x) that the Metal kernels also use,
+// metal_llm.metal:392-393).
+//
+// Kernel shape (B200): persistent CTAs, one producer warp + NC consumer
+// warps.  The producer streams tiles of RT consecutive weight rows (one
+// contiguous byte range) into an NS-stage shared-memory ring with
+// cp.async.bulk, completion tracked by mbarriers, so ~100-200 KB per SM is
+// in flight without tying up registers.  Consumer thread t owns the 32-column
+// "unit" t of x for the CTA's lifetime (its XQ limbs stay in registers), dots
+// it with unit t of every staged row, and the per-row partials are reduced
+// across the CTA.  Weights are immutable, so the producer starts streaming
+// before the programmatic-dependent-launch wait; consumers wait before
+// reading x.
 //
 // Device weight layout (cl_repack_rows): each row padded to a multiple of 16
-// bytes; Q4_K and Q5_K keep their native blocks (already 16-byte aligned),
-// Q6_K/Q8_0/Q5_0 rows are re-ordered structure-of-arrays inside the row so
-// that every vector load is aligned.  The byte count per row is unchanged
-// apart from the <16-byte pad.
+// bytes; Q4_K and Q5_K keep their native blocks, Q6_K/Q8_0/Q5_0 rows are
+// re-ordered structure-of-arrays inside the row so vector loads are aligned:
 //   Q6_K row: [nb x (ql128 qh64 sc16)] [nb x f16 d]
 //   Q8_0 row: [nb x qs32] [nb x f16 d]
 //   Q5_0 row: [nb x qs16] [nb x u32 qh] [nb x f16 d]
 #include "common.cuh"
 #include "launch.cuh"
 
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
+
 namespace cl {
 
-// x data of one lane unit: two 16-element chunks.
+// Device-side error word: set when a bounded wait gives up (never expected).
+__device__ int g_gemv_error = 0;
+
+// x data of one consumer thread: the unit's two 16-element chunks.
 struct XUnit {
     int4 l[2][3];
     int2 s[2];
-    float sc[2];
-    float xsum[2];
+    float xs;    // scale * 2^-14 of the unit's 32-block
+    float xsum;  // sum of the unit's (encoded) x values
 };
 
-CL_DEVINL void load_xunit(const XQView& x, int c0, int c1, XUnit& u) {
-    const int cs[2] = {c0, c1};
+CL_DEVINL void load_xunit(const XQView& x, int u, XUnit& r) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int c = cs[h];
-        u.l[h][0] = __ldg(x.limbs + 3 * c + 0);
-        u.l[h][1] = __ldg(x.limbs + 3 * c + 1);
-        u.l[h][2] = __ldg(x.limbs + 3 * c + 2);
-        u.s[h] = __ldg(x.lsum + c);
-        u.sc[h] = __ldg(x.scale + (c >> 1));
-        u.xsum[h] = fmaf((float)u.s[h].x, 16384.0f, (float)u.s[h].y) * u.sc[h];
+    for (int c = 0; c < 2; ++c) {
+        const int ch = 2 * u + c;
+        r.l[c][0] = x.limbs[3 * ch + 0];
+        r.l[c][1] = x.limbs[3 * ch + 1];
+        r.l[c][2] = x.limbs[3 * ch + 2];
+        r.s[c] = x.lsum[ch];
     }
+    r.xs = x.scale[u];
+    r.xsum = fmaf((float)(r.s[0].x + r.s[1].x), 16384.0f, (float)(r.s[0].y + r.s[1].y)) * r.xs;
 }
 
-// Integer dot of 16 unsigned weight bytes with one chunk's limbs; `offset`
-// is subtracted from every weight (q - offset) exactly via the limb sums.
-CL_DEVINL float chunk_dot_u(const uint32_t w[4], const int4 (&l)[3], int2 s, float sc, int offset) {
-    int s0 = dp4a_us(w[0], l[0].x, 0);
-    s0 = dp4a_us(w[1], l[0].y, s0);
-    s0 = dp4a_us(w[2], l[0].z, s0);
-    s0 = dp4a_us(w[3], l[0].w, s0);
-    int s1 = dp4a_us(w[0], l[1].x, 0);
-    s1 = dp4a_us(w[1], l[1].y, s1);
-    s1 = dp4a_us(w[2], l[1].z, s1);
-    s1 = dp4a_us(w[3], l[1].w, s1);
-    int s2 = dp4a_us(w[0], l[2].x, 0);
-    s2 = dp4a_us(w[1], l[2].y, s2);
-    s2 = dp4a_us(w[2], l[2].z, s2);
-    s2 = dp4a_us(w[3], l[2].w, s2);
-    int s12 = s1 * 128 + s2;
-    if (offset) {
-        s0 -= offset * s.x;
-        s12 -= offset * s.y;
-    }
-    return fmaf((float)s0, 16384.0f, (float)s12) * sc;
+struct Sums {
+    int s0, s1, s2;
+};
+
+CL_DEVINL void acc_u(Sums& a, uint32_t w, int4 const (&l)[3], int i) {
+    const int l0 = i == 0 ? l[0].x : i == 1 ? l[0].y : i == 2 ? l[0].z : l[0].w;
+    const int l1 = i == 0 ? l[1].x : i == 1 ? l[1].y : i == 2 ? l[1].z : l[1].w;
+    const int l2 = i == 0 ? l[2].x : i == 1 ? l[2].y : i == 2 ? l[2].z : l[2].w;
+    a.s0 = dp4a_us(w, l0, a.s0);
+    a.s1 = dp4a_us(w, l1, a.s1);
+    a.s2 = dp4a_us(w, l2, a.s2);
 }
 
-CL_DEVINL float chunk_dot_s(const uint32_t w[4], const int4 (&l)[3], float sc) {
-    int s0 = dp4a_ss((int)w[0], l[0].x, 0);
-    s0 = dp4a_ss((int)w[1], l[0].y, s0);
-    s0 = dp4a_ss((int)w[2], l[0].z, s0);
-    s0 = dp4a_ss((int)w[3], l[0].w, s0);
-    int s1 = dp4a_ss((int)w[0], l[1].x, 0);
-    s1 = dp4a_ss((int)w[1], l[1].y, s1);
-    s1 = dp4a_ss((int)w[2], l[1].z, s1);
-    s1 = dp4a_ss((int)w[3], l[1].w, s1);
-    int s2 = dp4a_ss((int)w[0], l[2].x, 0);
-    s2 = dp4a_ss((int)w[1], l[2].y, s2);
-    s2 = dp4a_ss((int)w[2], l[2].z, s2);
-    s2 = dp4a_ss((int)w[3], l[2].w, s2);
-    return fmaf((float)s0, 16384.0f, (float)(s1 * 128 + s2)) * sc;
+CL_DEVINL void acc_s(Sums& a, uint32_t w, int4 const (&l)[3], int i) {
+    const int l0 = i == 0 ? l[0].x : i == 1 ? l[0].y : i == 2 ? l[0].z : l[0].w;
+    const int l1 = i == 0 ? l[1].x : i == 1 ? l[1].y : i == 2 ? l[1].z : l[1].w;
+    const int l2 = i == 0 ? l[2].x : i == 1 ? l[2].y : i == 2 ? l[2].z : l[2].w;
+    a.s0 = dp4a_ss((int)w, l0, a.s0);
+    a.s1 = dp4a_ss((int)w, l1, a.s1);
+    a.s2 = dp4a_ss((int)w, l2, a.s2);
+}
+
+// (sum of q * x) / scale; `off` subtracted from every q exactly.
+CL_DEVINL float sums_value(const Sums& a, int l0sum, int l12sum, int off) {
+    const int s0 = a.s0 - off * l0sum;
+    const int s12 = a.s1 * 128 + a.s2 - off * l12sum;
+    return fmaf((float)s0, 16384.0f, (float)s12);
 }
 
 CL_DEVINL uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
 // 6-bit scale/min of K-quant sub-block i from the 12 scale bytes
-// (get_scale_min_k4, model.cpp:524-537), with s0..s2 = bytes 0-3, 4-7, 8-11.
+// (get_scale_min_k4, model.cpp:524-537); s0..s2 = bytes 0-3, 4-7, 8-11.
 CL_DEVINL void kscale(uint32_t s0, uint32_t s1, uint32_t s2, int i, float& sc, float& m) {
     const int lo = i & 3;
     const uint32_t a = byte_of(s0, lo), b = byte_of(s1, lo), c = byte_of(s2, lo);
-    uint32_t vs, vm;
-    if (i < 4) {
-        vs = a & 63u;
-        vm = b & 63u;
-    } else {
-        vs = (c & 0x0fu) | ((a >> 6) << 4);
-        vm = (c >> 4) | ((b >> 6) << 4);
-    }
+    const uint32_t vs = i < 4 ? (a & 63u) : ((c & 0x0fu) | ((a >> 6) << 4));
+    const uint32_t vm = i < 4 ? (b & 63u) : ((c >> 4) | ((b >> 6) << 4));
     sc = (float)vs;
     m = (float)vm;
 }
 
-// ---- per-format lane-unit kernels --------------------------------------
-// chunks(): the two XQ chunk indices a unit reads; dot(): the unit's
-// contribution for one row (row points at the row start, nb = blocks/row).
-struct FQ4K {
-    static constexpr int kType = CL_TYPE_Q4_K;
-    CL_DEVINL static void chunks(int u, int& c0, int& c1) {
-        const int b = u >> 3, j = u & 7;
-        c0 = 16 * b + 4 * (j >> 1) + (j & 1);
-        c1 = c0 + 2;
-    }
+CL_DEVINL uint4 lds4(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+CL_DEVINL uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
+
+// ---- per-format unit dots.  Unit u = elements [32u, 32u + 32) of a row held
+// in shared memory; nb = blocks per row.
+template <int T>
+struct Fmt;
+
+template <>
+struct Fmt<CL_TYPE_Q4_K> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const int b = u >> 3, j = u & 7, g = j >> 1;
+        const int b = u >> 3, i = u & 7, g = i >> 1, sh = 4 * (i & 1);
         const uint8_t* blk = row + b * 144;
-        const uint4 hdr = ldg_nc_v4(blk);
-        const uint4 q = ldg_nc_v4(blk + 16 + 16 * j);
+        const uint4 hdr = lds4(blk);
+        const uint4 q0 = lds4(blk + 16 + 32 * g), q1 = lds4(blk + 32 + 32 * g);
+        Sums a{0, 0, 0};
+        acc_u(a, (q0.x >> sh) & 0x0f0f0f0fu, x.l[0], 0);
+        acc_u(a, (q0.y >> sh) & 0x0f0f0f0fu, x.l[0], 1);
+        acc_u(a, (q0.z >> sh) & 0x0f0f0f0fu, x.l[0], 2);
+        acc_u(a, (q0.w >> sh) & 0x0f0f0f0fu, x.l[0], 3);
+        acc_u(a, (q1.x >> sh) & 0x0f0f0f0fu, x.l[1], 0);
+        acc_u(a, (q1.y >> sh) & 0x0f0f0f0fu, x.l[1], 1);
+        acc_u(a, (q1.z >> sh) & 0x0f0f0f0fu, x.l[1], 2);
+        acc_u(a, (q1.w >> sh) & 0x0f0f0f0fu, x.l[1], 3);
+        float sc, m;
+        kscale(hdr.y, hdr.z, hdr.w, i, sc, m);
         const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-        float sc0, m0, sc1, m1;
-        kscale(hdr.y, hdr.z, hdr.w, 2 * g, sc0, m0);
-        kscale(hdr.y, hdr.z, hdr.w, 2 * g + 1, sc1, m1);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = qw[i] & 0x0f0f0f0fu;
-            hi[i] = (qw[i] >> 4) & 0x0f0f0f0fu;
-        }
-        const float dl = chunk_dot_u(lo, x.l[0], x.s[0], x.sc[0], 0);
-        const float dh = chunk_dot_u(hi, x.l[1], x.s[1], x.sc[1], 0);
-        return (d * sc0) * dl - (dmin * m0) * x.xsum[0] + (d * sc1) * dh - (dmin * m1) * x.xsum[1];
+        return (d * sc) * (sums_value(a, 0, 0, 0) * x.xs) - (dmin * m) * x.xsum;
     }
 };
 
-struct FQ5K {
-    static constexpr int kType = CL_TYPE_Q5_K;
-    CL_DEVINL static void chunks(int u, int& c0, int& c1) { FQ4K::chunks(u, c0, c1); }
+template <>
+struct Fmt<CL_TYPE_Q5_K> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const int b = u >> 3, j = u & 7, g = j >> 1;
+        const int b = u >> 3, i = u & 7, g = i >> 1, sh = 4 * (i & 1);
         const uint8_t* blk = row + b * 176;
-        const uint4 hdr = ldg_nc_v4(blk);
-        const uint4 h = ldg_nc_v4(blk + 16 + 16 * (j & 1));
-        const uint4 q = ldg_nc_v4(blk + 48 + 16 * j);
+        const uint4 hdr = lds4(blk);
+        const uint4 h0 = lds4(blk + 16), h1 = lds4(blk + 32);
+        const uint4 q0 = lds4(blk + 48 + 32 * g), q1 = lds4(blk + 64 + 32 * g);
+#define Q5K_W(q, h) ((((q) >> sh) & 0x0f0f0f0fu) | ((((h) >> i) & 0x01010101u) << 4))
+        Sums a{0, 0, 0};
+        acc_u(a, Q5K_W(q0.x, h0.x), x.l[0], 0);
+        acc_u(a, Q5K_W(q0.y, h0.y), x.l[0], 1);
+        acc_u(a, Q5K_W(q0.z, h0.z), x.l[0], 2);
+        acc_u(a, Q5K_W(q0.w, h0.w), x.l[0], 3);
+        acc_u(a, Q5K_W(q1.x, h1.x), x.l[1], 0);
+        acc_u(a, Q5K_W(q1.y, h1.y), x.l[1], 1);
+        acc_u(a, Q5K_W(q1.z, h1.z), x.l[1], 2);
+        acc_u(a, Q5K_W(q1.w, h1.w), x.l[1], 3);
+#undef Q5K_W
+        float sc, m;
+        kscale(hdr.y, hdr.z, hdr.w, i, sc, m);
         const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-        float sc0, m0, sc1, m1;
-        kscale(hdr.y, hdr.z, hdr.w, 2 * g, sc0, m0);
-        kscale(hdr.y, hdr.z, hdr.w, 2 * g + 1, sc1, m1);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-        const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = (qw[i] & 0x0f0f0f0fu) | (((hw[i] >> (2 * g)) & 0x01010101u) << 4);
-            hi[i] = ((qw[i] >> 4) & 0x0f0f0f0fu) | (((hw[i] >> (2 * g + 1)) & 0x01010101u) << 4);
-        }
-        const float dl = chunk_dot_u(lo, x.l[0], x.s[0], x.sc[0], 0);
-        const float dh = chunk_dot_u(hi, x.l[1], x.s[1], x.sc[1], 0);
-        return (d * sc0) * dl - (dmin * m0) * x.xsum[0] + (d * sc1) * dh - (dmin * m1) * x.xsum[1];
+        return (d * sc) * (sums_value(a, 0, 0, 0) * x.xs) - (dmin * m) * x.xsum;
     }
 };
 
-struct FQ6K {
-    static constexpr int kType = CL_TYPE_Q6_K;
-    CL_DEVINL static void chunks(int u, int& c0, int& c1) {
-        const int b = u >> 3, j = u & 7, h = j >> 2, a = j & 3;
-        c0 = 16 * b + 8 * h + 2 * (a >> 1) + (a & 1);
-        c1 = c0 + 4;
-    }
+template <>
+struct Fmt<CL_TYPE_Q6_K> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const int b = u >> 3, j = u & 7, h = j >> 2, a = j & 3;
+        const int b = u >> 3, j = u & 7, h = j >> 2, q = j & 3;
         const uint8_t* blk = row + b * 208;
-        const uint4 ql = ldg_nc_v4(blk + 64 * h + 16 * a);
-        const uint4 qh = ldg_nc_v4(blk + 128 + 32 * h + 16 * (a & 1));
-        const uint4 sv = ldg_nc_v4(blk + 192);
-        const float d = half_bits_to_float(ldg_nc_u16(row + (size_t)nb * 208 + 2 * b));
-        const int sl = 2 * (a >> 1), sh = 4 + sl;
-        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
-        const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = (lw[i] & 0x0f0f0f0fu) | (((hw[i] >> sl) & 0x03030303u) << 4);
-            hi[i] = ((lw[i] >> 4) & 0x0f0f0f0fu) | (((hw[i] >> sh) & 0x03030303u) << 4);
-        }
-        const int il = 8 * h + 2 * (a >> 1) + (a & 1);
-        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-        const float scl = (float)(int8_t)byte_of(sw[il >> 2], il & 3);
-        const float sch = (float)(int8_t)byte_of(sw[(il + 4) >> 2], (il + 4) & 3);
-        const float dl = chunk_dot_u(lo, x.l[0], x.s[0], x.sc[0], 32);
-        const float dh = chunk_dot_u(hi, x.l[1], x.s[1], x.sc[1], 32);
-        return d * (scl * dl + sch * dh);
+        const uint4 l0 = lds4(blk + 64 * h + 32 * (q & 1)), l1 = lds4(blk + 64 * h + 32 * (q & 1) + 16);
+        const uint4 h0 = lds4(blk + 128 + 32 * h), h1 = lds4(blk + 144 + 32 * h);
+        const int nsh = 4 * (q >> 1), qsh = 2 * q;
+#define Q6K_W(l, hh) ((((l) >> nsh) & 0x0f0f0f0fu) | ((((hh) >> qsh) & 0x03030303u) << 4))
+        Sums a0{0, 0, 0}, a1{0, 0, 0};
+        acc_u(a0, Q6K_W(l0.x, h0.x), x.l[0], 0);
+        acc_u(a0, Q6K_W(l0.y, h0.y), x.l[0], 1);
+        acc_u(a0, Q6K_W(l0.z, h0.z), x.l[0], 2);
+        acc_u(a0, Q6K_W(l0.w, h0.w), x.l[0], 3);
+        acc_u(a1, Q6K_W(l1.x, h1.x), x.l[1], 0);
+        acc_u(a1, Q6K_W(l1.y, h1.y), x.l[1], 1);
+        acc_u(a1, Q6K_W(l1.z, h1.z), x.l[1], 2);
+        acc_u(a1, Q6K_W(l1.w, h1.w), x.l[1], 3);
+#undef Q6K_W
+        const uint32_t s16 = lds_u16(blk + 192 + 2 * j);
+        const float sc0 = (float)(int8_t)(s16 & 0xffu), sc1 = (float)(int8_t)(s16 >> 8);
+        const float d = half_bits_to_float(lds_u16(row + (size_t)nb * 208 + 2 * b));
+        const float v0 = sums_value(a0, x.s[0].x, x.s[0].y, 32);
+        const float v1 = sums_value(a1, x.s[1].x, x.s[1].y, 32);
+        return d * (sc0 * v0 + sc1 * v1) * x.xs;
     }
 };
 
-struct FQ8_0 {
-    static constexpr int kType = CL_TYPE_Q8_0;
-    CL_DEVINL static void chunks(int u, int& c0, int& c1) {
-        c0 = 2 * u;
-        c1 = 2 * u + 1;
-    }
+template <>
+struct Fmt<CL_TYPE_Q8_0> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const uint4 q0 = ldg_nc_v4(row + 32 * u);
-        const uint4 q1 = ldg_nc_v4(row + 32 * u + 16);
-        const float d = half_bits_to_float(ldg_nc_u16(row + (size_t)nb * 32 + 2 * u));
-        const uint32_t a[4] = {q0.x, q0.y, q0.z, q0.w};
-        const uint32_t c[4] = {q1.x, q1.y, q1.z, q1.w};
-        return d * (chunk_dot_s(a, x.l[0], x.sc[0]) + chunk_dot_s(c, x.l[1], x.sc[1]));
+        const uint4 q0 = lds4(row + 32 * u), q1 = lds4(row + 32 * u + 16);
+        Sums a{0, 0, 0};
+        acc_s(a, q0.x, x.l[0], 0);
+        acc_s(a, q0.y, x.l[0], 1);
+        acc_s(a, q0.z, x.l[0], 2);
+        acc_s(a, q0.w, x.l[0], 3);
+        acc_s(a, q1.x, x.l[1], 0);
+        acc_s(a, q1.y, x.l[1], 1);
+        acc_s(a, q1.z, x.l[1], 2);
+        acc_s(a, q1.w, x.l[1], 3);
+        const float d = half_bits_to_float(lds_u16(row + (size_t)nb * 32 + 2 * u));
+        return d * (sums_value(a, 0, 0, 0) * x.xs);
     }
 };
 
-struct FQ5_0 {
-    static constexpr int kType = CL_TYPE_Q5_0;
-    CL_DEVINL static void chunks(int u, int& c0, int& c1) {
-        c0 = 2 * u;
-        c1 = 2 * u + 1;
-    }
+template <>
+struct Fmt<CL_TYPE_Q5_0> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const uint4 q = ldg_nc_v4(row + 16 * u);
-        const uint32_t qh = ldg_nc_u32(row + (size_t)nb * 16 + 4 * u);
-        const float d = half_bits_to_float(ldg_nc_u16(row + (size_t)nb * 20 + 2 * u));
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = (qw[i] & 0x0f0f0f0fu) | ((((qh >> (4 * i)) & 0xfu) * 0x02040810u) & 0x10101010u);
-            hi[i] = ((qw[i] >> 4) & 0x0f0f0f0fu) |
-                    ((((qh >> (16 + 4 * i)) & 0xfu) * 0x02040810u) & 0x10101010u);
-        }
-        return d * (chunk_dot_u(lo, x.l[0], x.s[0], x.sc[0], 16) +
-                    chunk_dot_u(hi, x.l[1], x.s[1], x.sc[1], 16));
+        const uint4 q = lds4(row + 16 * u);
+        const uint32_t qh = *reinterpret_cast<const uint32_t*>(row + (size_t)nb * 16 + 4 * u);
+        const float d = half_bits_to_float(lds_u16(row + (size_t)nb * 20 + 2 * u));
+#define Q50_LO(w, i) (((w) & 0x0f0f0f0fu) | ((((qh >> (4 * (i))) & 0xfu) * 0x02040810u) & 0x10101010u))
+#define Q50_HI(w, i) ((((w) >> 4) & 0x0f0f0f0fu) | ((((qh >> (16 + 4 * (i))) & 0xfu) * 0x02040810u) & 0x10101010u))
+        Sums a{0, 0, 0};
+        acc_u(a, Q50_LO(q.x, 0), x.l[0], 0);
+        acc_u(a, Q50_LO(q.y, 1), x.l[0], 1);
+        acc_u(a, Q50_LO(q.z, 2), x.l[0], 2);
+        acc_u(a, Q50_LO(q.w, 3), x.l[0], 3);
+        acc_u(a, Q50_HI(q.x, 0), x.l[1], 0);
+        acc_u(a, Q50_HI(q.y, 1), x.l[1], 1);
+        acc_u(a, Q50_HI(q.z, 2), x.l[1], 2);
+        acc_u(a, Q50_HI(q.w, 3), x.l[1], 3);
+#undef Q50_LO
+#undef Q50_HI
+        return d * (sums_value(a, x.s[0].x + x.s[1].x, x.s[0].y + x.s[1].y, 16) * x.xs);
     }
 };
 
-// ---- kernel ---------------------------------------------------------------
-constexpr int kGemvThreads = 256;
-constexpr int kGemvWarps = kGemvThreads / 32;
+CL_DEVINL float unit_dot(int type, const uint8_t* row, int u, int nb, const XUnit& x) {
+    switch (type) {
+    case CL_TYPE_Q4_K: return Fmt<CL_TYPE_Q4_K>::dot(row, u, nb, x);
+    case CL_TYPE_Q5_K: return Fmt<CL_TYPE_Q5_K>::dot(row, u, nb, x);
+    case CL_TYPE_Q6_K: return Fmt<CL_TYPE_Q6_K>::dot(row, u, nb, x);
+    case CL_TYPE_Q8_0: return Fmt<CL_TYPE_Q8_0>::dot(row, u, nb, x);
+    case CL_TYPE_Q5_0: return Fmt<CL_TYPE_Q5_0>::dot(row, u, nb, x);
+    default: return 0.0f;
+    }
+}
+
+// ---- input preparation ---------------------------------------------------------
+// Each consumer thread turns x[32u, 32u + 32) (optionally RMS-normalised) into
+// its XQ unit in registers, with the expressions of xq_store_block_warp.
+CL_DEVINL void encode_unit(const float (&v)[32], XUnit& r) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    const float sc = amax / 127.0f;
+    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    uint32_t w0[8], w1[8], w2[8];
+    int t0[2] = {0, 0}, t12[2] = {0, 0};
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const float r0 = v[e] * inv;
+        const float l0 = fminf(fmaxf(rintf(r0), -127.0f), 127.0f);
+        const float r1 = (r0 - l0) * 128.0f;
+        const float l1 = fminf(fmaxf(rintf(r1), -64.0f), 64.0f);
+        const float r2 = (r1 - l1) * 128.0f;
+        const float l2 = fminf(fmaxf(rintf(r2), -64.0f), 64.0f);
+        const int i0 = (int)l0, i1 = (int)l1, i2 = (int)l2;
+        const int sh = 8 * (e & 3);
+        if ((e & 3) == 0) {
+            w0[e >> 2] = 0u;
+            w1[e >> 2] = 0u;
+            w2[e >> 2] = 0u;
+        }
+        w0[e >> 2] |= ((uint32_t)i0 & 0xffu) << sh;
+        w1[e >> 2] |= ((uint32_t)i1 & 0xffu) << sh;
+        w2[e >> 2] |= ((uint32_t)i2 & 0xffu) << sh;
+        t0[e >> 4] += i0;
+        t12[e >> 4] += i1 * 128 + i2;
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        r.l[c][0] = make_int4((int)w0[4 * c], (int)w0[4 * c + 1], (int)w0[4 * c + 2], (int)w0[4 * c + 3]);
+        r.l[c][1] = make_int4((int)w1[4 * c], (int)w1[4 * c + 1], (int)w1[4 * c + 2], (int)w1[4 * c + 3]);
+        r.l[c][2] = make_int4((int)w2[4 * c], (int)w2[4 * c + 1], (int)w2[4 * c + 2], (int)w2[4 * c + 3]);
+        r.s[c] = make_int2(t0[c], t12[c]);
+    }
+    r.xs = sc * (1.0f / 16384.0f);
+    r.xsum = fmaf((float)(t0[0] + t0[1]), 16384.0f, (float)(t12[0] + t12[1])) * r.xs;
+}
+
+// ---- kernel -------------------------------------------------------------------
 constexpr int kMaxSegs = 4;
+constexpr int kMaxConsumerWarps = 20;  // k <= 20480
+constexpr int kMaxThreads = (kMaxConsumerWarps + 1) * 32;
 
 struct GemvSeg {
     const uint8_t* w;
+    const uint8_t* w_up;  // SwiGLU: up rows (same type/stride as w)
     long long stride;
     const float* bias;
     const float* residual;
     float* y;
     int type;
-    int n;
-    int cta_begin;  // first CTA of this segment
+    int n;           // output rows
+    int tile_begin;  // first tile index of this segment
 };
 
 struct GemvParams {
     GemvSeg seg[kMaxSegs];
-    const void* xq;
+    const float* x;
+    const float* gamma;  // RMSNorm weight applied to x first (cpu_llm.cpp:143-166), or null
+    float eps;
     int nseg;
     int k;
-    int wpr;      // warps per row group (K split), divides kGemvWarps
-    int swiglu;   // 1: seg[0] = gate, seg[1] = up, out = silu(g) * u into seg[0].y
-    const uint8_t* w_up;
+    int units;        // k / 32
+    int tiles;        // total tiles over all segments
+    int stages;       // ring depth
+    int stage_bytes;  // bytes of one stage (RT rows x max stride x matrices)
+    int consumers;    // consumer threads (multiple of 32)
 };
 
-template <int R, class F, bool SWIGLU>
-CL_DEVINL void gemv_body(const GemvParams& p, const GemvSeg& s, int cta_in_seg) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wpr = p.wpr;
-    const int groups = kGemvWarps / wpr;
-    const int rg = warp / wpr, wk = warp % wpr;
-    constexpr int OUT = SWIGLU ? R / 2 : R;  // output rows per warp group
-    const int out_per_cta = OUT * groups;
-    const int out0 = cta_in_seg * out_per_cta + rg * OUT;
-    const int k = p.k;
-    const int units = k / 32;
-    const int nb = F::kType == CL_TYPE_Q8_0 || F::kType == CL_TYPE_Q5_0 ? k / 32 : k / 256;
+struct TileInfo {
+    int seg, row0, rows;
+};
 
-    const uint8_t* rows[R];
+CL_DEVINL TileInfo tile_info(const GemvParams& p, int t, int rt) {
+    int s = 0;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-        int o = SWIGLU ? out0 + r / 2 : out0 + r;
-        o = o < s.n ? o : s.n - 1;
-        const uint8_t* base = SWIGLU && (r & 1) ? p.w_up : s.w;
-        rows[r] = base + (size_t)o * s.stride;
+    for (int i = 1; i < kMaxSegs; ++i)
+        if (i < p.nseg && t >= p.seg[i].tile_begin) s = i;
+    const int row0 = (t - p.seg[s].tile_begin) * rt;
+    return TileInfo{s, row0, min(rt, p.seg[s].n - row0)};
+}
+
+// Dynamic shared memory: [full|empty mbarriers][abort flag][double norm partials]
+// [float row partials, double buffered][NS stages, 128-byte aligned]
+__host__ __device__ inline int smem_red_offset(int stages) { return 16 * stages + 16 + 32 * 8; }
+__host__ __device__ inline int smem_stage_offset(int stages, int nmat, int rt) {
+    return (smem_red_offset(stages) + 2 * 32 * nmat * rt * 4 + 127) & ~127;
+}
+
+template <int RT, bool SWIGLU>
+__global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams p) {
+    constexpr int NMAT = SWIGLU ? 2 : 1;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + p.stages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * p.stages);
+    double* dred = reinterpret_cast<double*>(smem + 16 * p.stages + 16);
+    float* red = reinterpret_cast<float*>(smem + smem_red_offset(p.stages));
+    uint8_t* stage_base = smem + smem_stage_offset(p.stages, NMAT, RT);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nconsumer = p.consumers;
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    grid_launch_dependents();
+
+    if (tid >= nconsumer) {
+        // ---- producer: stream weight tiles (immutable: no dependency wait) ----
+        if (tid == nconsumer) {
+            for (int i = 0, t = blockIdx.x; t < p.tiles; ++i, t += gridDim.x) {
+                const int s = i % p.stages;
+                const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                    atomicExch(&g_gemv_error, 1);
+                    *abort_flag = 1;
+                    break;
+                }
+                const TileInfo ti = tile_info(p, t, RT);
+                const GemvSeg& g = p.seg[ti.seg];
+                const uint32_t bytes = (uint32_t)(ti.rows * g.stride);
+                uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+                mbar_arrive_expect_tx(&full[s], bytes * NMAT);
+                bulk_g2s(dst, g.w + (size_t)ti.row0 * g.stride, bytes, &full[s]);
+                if (SWIGLU)
+                    bulk_g2s(dst + (size_t)RT * g.stride, g.w_up + (size_t)ti.row0 * g.stride, bytes, &full[s]);
+            }
+        }
+        return;
     }
 
-    // Warm L2 with this CTA's weight rows while the previous kernel drains.
-    if (threadIdx.x == 0) {
-        const int first = cta_in_seg * out_per_cta;
-        const int last = min(first + out_per_cta, s.n);
-        if (last > first) {
-            const size_t bytes = (size_t)(last - first) * s.stride;
-            for (int m = 0; m < (SWIGLU ? 2 : 1); ++m) {
-                const uint8_t* b = (m ? p.w_up : s.w) + (size_t)first * s.stride;
-                for (size_t off = 0; off < bytes; off += 65536) {
-                    prefetch_l2(b + off, (uint32_t)min((size_t)65536, bytes - off));
-                }
+    // ---- consumers: build this thread's x unit (after the dependency wait) ----
+    grid_wait();
+    const int u = tid;
+    const bool active = u < p.units;
+    const int nwarps = nconsumer >> 5;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 f = active ? reinterpret_cast<const float4*>(p.x + 32 * u)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * q] = f.x;
+        v[4 * q + 1] = f.y;
+        v[4 * q + 2] = f.z;
+        v[4 * q + 3] = f.w;
+    }
+    if (p.gamma) {
+        // cpu_llm.cpp:156-165: sum of squares in double, mean -> float,
+        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every CTA
+        // reduces in the same order, so all CTAs see the same inv.
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ss += (double)v[e] * (double)v[e];
+        ss = warp_sum_d(ss);
+        if (lane == 0) dred[warp] = ss;
+        named_barrier(1, nconsumer);
+        double tot = 0.0;
+        for (int w = 0; w < nwarps; ++w) tot += dred[w];
+        const float inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
+        if (active) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 gm = reinterpret_cast<const float4*>(p.gamma + 32 * u)[q];
+                v[4 * q] = __fmul_rn(v[4 * q], __fmul_rn(inv, gm.x));
+                v[4 * q + 1] = __fmul_rn(v[4 * q + 1], __fmul_rn(inv, gm.y));
+                v[4 * q + 2] = __fmul_rn(v[4 * q + 2], __fmul_rn(inv, gm.z));
+                v[4 * q + 3] = __fmul_rn(v[4 * q + 3], __fmul_rn(inv, gm.w));
             }
         }
     }
-    grid_launch_dependents();
-    grid_wait();
+    XUnit xu;
+    encode_unit(v, xu);
 
-    const XQView xv = xq_view(p.xq, k);
-    float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-
-#pragma unroll 2
-    for (int u = lane + 32 * wk; u < units; u += 32 * wpr) {
-        int c0, c1;
-        F::chunks(u, c0, c1);
-        XUnit xu;
-        load_xunit(xv, c0, c1, xu);
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] += F::dot(rows[r], u, nb, xu);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
-
-    __shared__ float red[kGemvWarps][R];
-    if (wpr > 1) {
-        if (lane == 0) {
-#pragma unroll
-            for (int r = 0; r < R; ++r) red[warp][r] = acc[r];
+    for (int i = 0, t = blockIdx.x; t < p.tiles; ++i, t += gridDim.x) {
+        const int s = i % p.stages;
+        const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+        const TileInfo ti = tile_info(p, t, RT);
+        const GemvSeg& g = p.seg[ti.seg];
+        const int nb = (g.type == CL_TYPE_Q8_0 || g.type == CL_TYPE_Q5_0) ? p.units : p.units / 8;
+        const bool ok = mbar_wait(&full[s], ph);
+        if (!ok) {
+            atomicExch(&g_gemv_error, 2);
+            *abort_flag = 1;
         }
-        __syncthreads();
-        if (wk != 0) return;
+        const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
+        float acc[NMAT * RT];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            float t = 0.0f;
-            for (int w = 0; w < wpr; ++w) t += red[rg * wpr + w][r];
-            acc[r] = t;
+        for (int r = 0; r < NMAT * RT; ++r) {
+            acc[r] = 0.0f;
+            if (ok && active && (r % RT) < ti.rows) acc[r] = unit_dot(g.type, st + (size_t)r * g.stride, u, nb, xu);
         }
-    }
-    if (lane != 0) return;
+        float* rb = red + (i & 1) * 32 * NMAT * RT;
 #pragma unroll
-    for (int r = 0; r < OUT; ++r) {
-        const int o = out0 + r;
-        if (o >= s.n) break;
-        float v;
-        if (SWIGLU) {
-            // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
-            const float g = acc[2 * r], up = acc[2 * r + 1];
-            const float sig = g >= 0.0f ? 1.0f / (1.0f + expf(-g)) : expf(g) / (1.0f + expf(g));
-            v = g * sig * up;
-        } else {
-            v = acc[r];
-            if (s.bias) v += s.bias[o];
-            if (s.residual) v = s.residual[o] + v;
+        for (int r = 0; r < NMAT * RT; ++r) {
+            const float w = warp_sum(acc[r]);
+            if (lane == 0) rb[warp * NMAT * RT + r] = w;
         }
-        s.y[o] = v;
+        named_barrier(1, nconsumer);
+        if (tid == 0) mbar_arrive(&empty[s]);  // every consumer is done with stage s
+        if (*abort_flag) break;
+        if (tid < ti.rows) {
+            float y = 0.0f, up = 0.0f;
+            for (int w = 0; w < nwarps; ++w) {
+                y += rb[w * NMAT * RT + tid];
+                if (SWIGLU) up += rb[w * NMAT * RT + RT + tid];
+            }
+            const int o = ti.row0 + tid;
+            if (SWIGLU) {
+                // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
+                const float sig = y >= 0.0f ? 1.0f / (1.0f + expf(-y)) : expf(y) / (1.0f + expf(y));
+                y = __fmul_rn(__fmul_rn(y, sig), up);
+            } else {
+                if (g.bias) y += g.bias[o];
+                if (g.residual) y = g.residual[o] + y;
+            }
+            g.y[o] = y;
+        }
     }
 }
 
-template <int R, bool SWIGLU>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
-    int si = 0;
-#pragma unroll
-    for (int i = 1; i < kMaxSegs; ++i) {
-        if (i < p.nseg && (int)blockIdx.x >= p.seg[i].cta_begin) si = i;
-    }
-    const GemvSeg& s = p.seg[si];
-    const int cta = blockIdx.x - s.cta_begin;
-    switch (s.type) {
-    case CL_TYPE_Q4_K: gemv_body<R, FQ4K, SWIGLU>(p, s, cta); break;
-    case CL_TYPE_Q5_K: gemv_body<R, FQ5K, SWIGLU>(p, s, cta); break;
-    case CL_TYPE_Q6_K: gemv_body<R, FQ6K, SWIGLU>(p, s, cta); break;
-    case CL_TYPE_Q8_0: gemv_body<R, FQ8_0, SWIGLU>(p, s, cta); break;
-    case CL_TYPE_Q5_0: gemv_body<R, FQ5_0, SWIGLU>(p, s, cta); break;
-    default: break;
-    }
-}
-
-constexpr int kRows = 4;
-
+// ---- host launcher -----------------------------------------------------------
 bool gemv_type_ok(int t) {
-    return t == CL_TYPE_Q4_K || t == CL_TYPE_Q5_K || t == CL_TYPE_Q6_K || t == CL_TYPE_Q8_0 ||
-           t == CL_TYPE_Q5_0;
+    return t == CL_TYPE_Q4_K || t == CL_TYPE_Q5_K || t == CL_TYPE_Q6_K || t == CL_TYPE_Q8_0 || t == CL_TYPE_Q5_0;
 }
 
-// K-split heuristic: enough CTAs to fill 148 SMs a few times over, but every
-// warp keeps at least ~one unit per lane.
-int choose_wpr(long long total_out, int out_per_warp, int k) {
-    const int units = k / 32;
-    int wpr = 1;
-    while (wpr < kGemvWarps) {
-        const long long ctas = (total_out + (long long)out_per_warp * (kGemvWarps / wpr) - 1) /
-                               ((long long)out_per_warp * (kGemvWarps / wpr));
-        if (ctas >= 4 * 148) break;
-        if (units / (2 * wpr) < 32) break;
-        wpr *= 2;
+constexpr int kStageTarget = 40 * 1024;
+constexpr int kSmemBudget = 190 * 1024;
+
+template <int RT, bool SW>
+cudaError_t launch_rt(GemvParams& p, int threads, cudaStream_t stream) {
+    constexpr int NMAT = SW ? 2 : 1;
+    auto kern = gemv_tma_kernel<RT, SW>;
+    const int smem = smem_stage_offset(p.stages, NMAT, RT) + p.stages * p.stage_bytes;
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> occ_cache;  // (threads, smem) -> CTAs per SM
+    static int sm_count = 0;
+    static bool attr_set = false;
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attr_set) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+            attr_set = true;
+        }
+        auto it = occ_cache.find({threads, smem});
+        if (it == occ_cache.end()) {
+            cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+            if (e != cudaSuccess) return e;
+            occ_cache[{threads, smem}] = occ;
+        } else {
+            occ = it->second;
+        }
     }
-    return wpr;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    const int grid = std::min(p.tiles, occ * sm_count);
+    return launch_pdl(kern, dim3(grid), dim3(threads), smem, stream, p);
 }
 
-int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const void* xq, int swiglu,
+int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
                 const void* w_up, cudaStream_t stream) {
-    if (nseg < 1 || nseg > kMaxSegs || k <= 0 || k % 32 != 0 || xq == nullptr) return CL_ERR_INVALID;
+    const bool sw = w_up != nullptr;
+    if (nseg < 1 || nseg > kMaxSegs || (sw && nseg != 1) || k <= 0 || k % 32 != 0 || x == nullptr ||
+        reinterpret_cast<uintptr_t>(x) % 16 != 0 || (gamma && (reinterpret_cast<uintptr_t>(gamma) % 16 != 0 || !(eps > 0.0f))))
+        return CL_ERR_INVALID;
+    const int units = k / 32;
+    if (units > kMaxConsumerWarps * 32) return CL_ERR_UNSUPPORTED;
     GemvParams p{};
-    long long total = 0;
+    long long smax = 0;
     for (int i = 0; i < nseg; ++i) {
-        if (!gemv_type_ok(segs[i].type) || segs[i].w == nullptr || segs[i].y == nullptr ||
-            segs[i].n <= 0)
+        const cl_gemv_segment& s = segs[i];
+        if (!gemv_type_ok(s.type) || s.w == nullptr || s.y == nullptr || s.n <= 0) return CL_ERR_INVALID;
+        if (cl_native_row_bytes(s.type, k) < 0) return CL_ERR_INVALID;
+        if (s.stride < cl_row_stride(s.type, k) || s.stride % 16 != 0 || reinterpret_cast<uintptr_t>(s.w) % 16 != 0)
             return CL_ERR_INVALID;
-        if ((segs[i].type == CL_TYPE_Q4_K || segs[i].type == CL_TYPE_Q5_K ||
-             segs[i].type == CL_TYPE_Q6_K) && k % 256 != 0)
-            return CL_ERR_INVALID;
-        if (segs[i].stride < cl_row_stride(segs[i].type, k) || segs[i].stride % 16 != 0 ||
-            reinterpret_cast<uintptr_t>(segs[i].w) % 16 != 0)
-            return CL_ERR_INVALID;
-        total += segs[i].n;
+        if (sw && reinterpret_cast<uintptr_t>(w_up) % 16 != 0) return CL_ERR_INVALID;
+        smax = std::max(smax, s.stride);
     }
-    const int out_per_warp = swiglu ? kRows / 2 : kRows;
-    p.wpr = choose_wpr(total, out_per_warp, k);
-    const int out_per_cta = out_per_warp * (kGemvWarps / p.wpr);
-    int ctas = 0;
+    const int nmat = sw ? 2 : 1;
+    int rt = sw ? 8 : 16;  // SwiGLU keeps 2 x RT partial sums per thread
+    while (rt > 1 && (long long)rt * smax * nmat > kStageTarget) rt /= 2;
+    if ((long long)smax * nmat > kSmemBudget / 2) return CL_ERR_UNSUPPORTED;
+    p.stage_bytes = (int)((long long)rt * smax * nmat);
+    p.stages = std::max(2, std::min(8, kSmemBudget / p.stage_bytes));
+    int tiles = 0;
     for (int i = 0; i < nseg; ++i) {
-        GemvSeg& s = p.seg[i];
-        s.w = static_cast<const uint8_t*>(segs[i].w);
-        s.stride = segs[i].stride;
-        s.bias = segs[i].bias;
-        s.residual = segs[i].residual;
-        s.y = segs[i].y;
-        s.type = segs[i].type;
-        s.n = segs[i].n;
-        s.cta_begin = ctas;
-        ctas += (segs[i].n + out_per_cta - 1) / out_per_cta;
+        GemvSeg& g = p.seg[i];
+        g.w = static_cast<const uint8_t*>(segs[i].w);
+        g.w_up = static_cast<const uint8_t*>(w_up);
+        g.stride = segs[i].stride;
+        g.bias = segs[i].bias;
+        g.residual = segs[i].residual;
+        g.y = segs[i].y;
+        g.type = segs[i].type;
+        g.n = segs[i].n;
+        g.tile_begin = tiles;
+        tiles += (segs[i].n + rt - 1) / rt;
     }
+    p.x = x;
+    p.gamma = gamma;
+    p.eps = eps;
     p.nseg = nseg;
     p.k = k;
-    p.xq = xq;
-    p.swiglu = swiglu;
-    p.w_up = static_cast<const uint8_t*>(w_up);
-    cudaError_t e = swiglu ? launch_pdl(gemv_kernel<kRows, true>, dim3(ctas), dim3(kGemvThreads), 0, stream, p)
-                           : launch_pdl(gemv_kernel<kRows, false>, dim3(ctas), dim3(kGemvThreads), 0, stream, p);
+    p.units = units;
+    p.tiles = tiles;
+    p.consumers = ((units + 31) / 32) * 32;
+    const int threads = p.consumers + 32;
+    cudaError_t e;
+#define CL_GEMV_CASE(R)                                                              \
+    case R:                                                                          \
+        e = sw ? launch_rt<R, true>(p, threads, stream) : launch_rt<R, false>(p, threads, stream); \
+        break;
+    switch (rt) {
+        CL_GEMV_CASE(1)
+        CL_GEMV_CASE(2)
+        CL_GEMV_CASE(4)
+        CL_GEMV_CASE(8)
+        CL_GEMV_CASE(16)
+    default: return CL_ERR_INVALID;
+    }
+#undef CL_GEMV_CASE
     return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
 }
 
@@ -438,22 +580,33 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const void* xq, in
 
 extern "C" {
 
-CL_API int cl_gemv_xq_multi(const cl_gemv_segment* segs, int nseg, int k, const void* xq,
-                            cudaStream_t stream) {
-    return cl::launch_gemv(segs, nseg, k, xq, 0, nullptr, stream);
-}
-
-CL_API int cl_gemv_xq(int type, const void* w, long long stride, int n, int k, const void* xq,
-                      const float* bias, const float* residual, float* y, cudaStream_t stream) {
+CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x, const float* bias,
+                   const float* residual, float* y, cudaStream_t stream) {
     cl_gemv_segment s{type, w, stride, n, bias, residual, y};
-    return cl::launch_gemv(&s, 1, k, xq, 0, nullptr, stream);
+    return cl::launch_gemv(&s, 1, k, x, nullptr, 0.0f, nullptr, stream);
 }
 
-CL_API int cl_gemv_xq_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n,
-                             int k, const void* xq, float* y, cudaStream_t stream) {
-    if (w_up == nullptr || reinterpret_cast<uintptr_t>(w_up) % 16 != 0) return CL_ERR_INVALID;
+CL_API int cl_gemv_multi(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* norm_gamma,
+                         float eps, cudaStream_t stream) {
+    if (segs == nullptr) return CL_ERR_INVALID;
+    return cl::launch_gemv(segs, nseg, k, x, norm_gamma, eps, nullptr, stream);
+}
+
+CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n, int k,
+                          const float* x, const float* norm_gamma, float eps, float* y, cudaStream_t stream) {
+    if (w_up == nullptr) return CL_ERR_INVALID;
     cl_gemv_segment s{type, w_gate, stride, n, nullptr, nullptr, y};
-    return cl::launch_gemv(&s, 1, k, xq, 1, w_up, stream);
+    return cl::launch_gemv(&s, 1, k, x, norm_gamma, eps, w_up, stream);
+}
+
+CL_API int cl_device_error(int* code, int clear) {
+    if (code == nullptr) return CL_ERR_INVALID;
+    if (cudaMemcpyFromSymbol(code, cl::g_gemv_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    if (clear) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(cl::g_gemv_error, &zero, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    }
+    return CL_OK;
 }
 
 }  // extern "C"

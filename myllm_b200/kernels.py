@@ -59,38 +59,38 @@ def quantize_xq(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     return out
 
 
-def gemv_xq(gtype: int, w: torch.Tensor, n: int, k: int, xq: torch.Tensor, bias=None, residual=None,
-            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def gemv(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None,
+         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = W x (+ bias) (+ residual) with the TMA-staged decode GEMV."""
     if out is None:
         out = torch.empty(n, dtype=torch.float32, device=w.device)
-    check(_native.lib().cl_gemv_xq(gtype, _p(w), w.stride(0), n, k, _p(xq), _p(bias), _p(residual), _p(out),
-                                   _stream()), "cl_gemv_xq")
-    return out
-
-
-def gemv(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None) -> torch.Tensor:
-    ws = torch.empty(xq_bytes(k), dtype=torch.uint8, device=x.device)
-    out = torch.empty(n, dtype=torch.float32, device=x.device)
-    check(_native.lib().cl_gemv(gtype, _p(w), w.stride(0), n, k, _p(x), _p(bias), _p(out), _p(ws), ws.numel(),
+    check(_native.lib().cl_gemv(gtype, _p(w), w.stride(0), n, k, _p(x), _p(bias), _p(residual), _p(out),
                                 _stream()), "cl_gemv")
     return out
 
 
-def gemv_multi(segments: Sequence[tuple], k: int, xq: torch.Tensor) -> None:
-    """segments: (gtype, w, n, bias, residual, out) tuples sharing x."""
+def gemv_multi(segments: Sequence[tuple], k: int, x: torch.Tensor, gamma=None, eps: float = 1e-6) -> None:
+    """segments: (gtype, w, n, bias, residual, out) tuples sharing x (RMS-normalised by gamma if given)."""
     arr = (_native.GemvSegment * len(segments))()
     for i, (gtype, w, n, bias, res, out) in enumerate(segments):
         arr[i] = _native.GemvSegment(gtype, w.data_ptr(), w.stride(0), n,
                                      0 if bias is None else bias.data_ptr(),
                                      0 if res is None else res.data_ptr(), out.data_ptr())
-    check(_native.lib().cl_gemv_xq_multi(arr, len(segments), k, _p(xq), _stream()), "cl_gemv_xq_multi")
+    check(_native.lib().cl_gemv_multi(arr, len(segments), k, _p(x), _p(gamma), eps, _stream()), "cl_gemv_multi")
 
 
-def gemv_swiglu(gtype: int, w_gate: torch.Tensor, w_up: torch.Tensor, n: int, k: int, xq: torch.Tensor):
+def gemv_swiglu(gtype: int, w_gate: torch.Tensor, w_up: torch.Tensor, n: int, k: int, x: torch.Tensor,
+                gamma=None, eps: float = 1e-6):
     out = torch.empty(n, dtype=torch.float32, device=w_gate.device)
-    check(_native.lib().cl_gemv_xq_swiglu(gtype, _p(w_gate), _p(w_up), w_gate.stride(0), n, k, _p(xq), _p(out),
-                                          _stream()), "cl_gemv_xq_swiglu")
+    check(_native.lib().cl_gemv_swiglu(gtype, _p(w_gate), _p(w_up), w_gate.stride(0), n, k, _p(x), _p(gamma), eps,
+                                       _p(out), _stream()), "cl_gemv_swiglu")
     return out
+
+
+def device_error(clear: bool = True) -> int:
+    code = ctypes.c_int(0)
+    check(_native.lib().cl_device_error(ctypes.byref(code), 1 if clear else 0), "cl_device_error")
+    return code.value
 
 
 def gemm(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None):

@@ -61,15 +61,18 @@ def test_gemv_bias_residual_and_ragged_rows(cuda, gtype):
     res = sg.normal(n, sg.stream_key(6, "r"), 0.0, 1.0)
     ref = oracle.gemm(gtype, w, n, k, x, bias)[0] + res
     wd = K.repack(gtype, w, k)
-    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
-    got = K.gemv_xq(gtype, wd, n, k, xq, torch.from_numpy(bias).cuda(), torch.from_numpy(res).cuda())
+    got = K.gemv(gtype, wd, n, k, torch.from_numpy(x[0]).cuda(), torch.from_numpy(bias).cuda(),
+                 torch.from_numpy(res).cuda())
     assert rel_err(got.cpu().numpy(), ref) <= 2e-5
+    # in place: y aliases the residual
+    r = torch.from_numpy(res).cuda()
+    K.gemv(gtype, wd, n, k, torch.from_numpy(x[0]).cuda(), torch.from_numpy(bias).cuda(), r, out=r)
+    assert rel_err(r.cpu().numpy(), ref) <= 2e-5
 
 
 def test_gemv_multi_segments_mixed_formats(cuda):
     k = 512
     x = xvec(k, seed=8)
-    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
     segs, refs = [], []
     for i, (gtype, n) in enumerate([(sg.Q4_K, 300), (sg.Q6_K, 64), (sg.Q8_0, 70), (sg.Q5_0, 33)]):
         w = weights(gtype, n, k, seed=10 + i)
@@ -77,7 +80,7 @@ def test_gemv_multi_segments_mixed_formats(cuda):
         refs.append(oracle.gemm(gtype, w, n, k, x, b)[0])
         out = torch.empty(n, device="cuda")
         segs.append((gtype, K.repack(gtype, w, k), n, torch.from_numpy(b).cuda(), None, out))
-    K.gemv_multi(segs, k, xq)
+    K.gemv_multi(segs, k, torch.from_numpy(x[0]).cuda())
     for s, ref in zip(segs, refs):
         assert rel_err(s[5].cpu().numpy(), ref) <= 2e-5
 
@@ -90,9 +93,45 @@ def test_gemv_swiglu(cuda, gtype):
     g = oracle.gemm(gtype, wg, n, k, x)[0].astype(np.float64)
     u = oracle.gemm(gtype, wu, n, k, x)[0].astype(np.float64)
     ref = g / (1.0 + np.exp(-g)) * u
-    xq = K.quantize_xq(torch.from_numpy(x[0]).cuda())
-    got = K.gemv_swiglu(gtype, K.repack(gtype, wg, k), K.repack(gtype, wu, k), n, k, xq).cpu().numpy()
+    got = K.gemv_swiglu(gtype, K.repack(gtype, wg, k), K.repack(gtype, wu, k), n, k,
+                        torch.from_numpy(x[0]).cuda()).cpu().numpy()
     assert rel_err(got, ref) <= 5e-5
+
+
+def rmsnorm_ref(x, g, eps):
+    """cpu_llm.cpp:156-165 in numpy: double sum of squares, float mean/inv."""
+    ss = (x.astype(np.float64) ** 2).sum(axis=-1)
+    inv = (np.float32(1.0) / np.sqrt((ss / x.shape[-1]).astype(np.float32) + np.float32(eps))).astype(np.float32)
+    return (x * (inv[..., None] * g)).astype(np.float32)
+
+
+@pytest.mark.parametrize("k", [896, 3584, 18944])
+def test_gemv_fused_rmsnorm(cuda, k):
+    gtype = sg.Q8_0 if k == 896 else sg.Q4_K
+    n = 700
+    w = weights(gtype, n, k, seed=33)
+    x = xvec(k, seed=34, std=3.0)
+    g = sg.normal(k, sg.stream_key(35, "g"), 1.0, 0.02)
+    ref = oracle.gemm(gtype, w, n, k, rmsnorm_ref(x, g, 1e-6))[0]
+    out = torch.empty(n, device="cuda")
+    K.gemv_multi([(gtype, K.repack(gtype, w, k), n, None, None, out)], k, torch.from_numpy(x[0]).cuda(),
+                 torch.from_numpy(g).cuda(), 1e-6)
+    assert rel_err(out.cpu().numpy(), ref) <= 2e-5
+    gate = K.gemv_swiglu(gtype, K.repack(gtype, w, k), K.repack(gtype, w, k), n, k, torch.from_numpy(x[0]).cuda(),
+                         torch.from_numpy(g).cuda(), 1e-6).cpu().numpy().astype(np.float64)
+    r = ref.astype(np.float64)
+    assert rel_err(gate, r / (1.0 + np.exp(-r)) * r) <= 5e-5
+
+
+def test_gemv_rejects_unsupported_width(cuda):
+    w = torch.zeros((4, K.row_stride(sg.Q4_K, 20736)), dtype=torch.uint8, device="cuda")
+    from myllm_b200._native import KernelError
+    with pytest.raises(KernelError):
+        K.gemv(sg.Q4_K, w, 4, 20736, torch.zeros(20736, device="cuda"))
+
+
+def test_no_device_error_recorded(cuda):
+    assert K.device_error() == 0
 
 
 def test_xq_encoding_precision(cuda):
