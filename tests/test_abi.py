@@ -26,7 +26,7 @@ def declared_symbols():
 
 def test_headers_declare_entry_points():
     names = declared_symbols()
-    assert "cl_gemv_xq" in names and "cudallm_prefill" in names
+    assert "cl_gemv_multi" in names and "cudallm_prefill" in names
     assert len(names) >= 40
 
 
@@ -63,6 +63,6 @@ def test_xq_bytes():
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
     lib = _native.lib()
-    assert lib.cl_gemv_xq(99, None, 0, 1, 256, None, None, None, None, None) == 1
+    assert lib.cl_gemv(99, None, 0, 1, 256, None, None, None, None, None) == 1
     assert lib.cl_argmax(None, 10, None, None, 0, None) == 1
     assert lib.cl_status_string(4) == b"workspace missing or too small"
