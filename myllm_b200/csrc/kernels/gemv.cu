@@ -227,17 +227,6 @@ struct Fmt<CL_TYPE_Q5_0> {
     }
 };
 
-CL_DEVINL float unit_dot(int type, const uint8_t* row, int u, int nb, const XUnit& x) {
-    switch (type) {
-    case CL_TYPE_Q4_K: return Fmt<CL_TYPE_Q4_K>::dot(row, u, nb, x);
-    case CL_TYPE_Q5_K: return Fmt<CL_TYPE_Q5_K>::dot(row, u, nb, x);
-    case CL_TYPE_Q6_K: return Fmt<CL_TYPE_Q6_K>::dot(row, u, nb, x);
-    case CL_TYPE_Q8_0: return Fmt<CL_TYPE_Q8_0>::dot(row, u, nb, x);
-    case CL_TYPE_Q5_0: return Fmt<CL_TYPE_Q5_0>::dot(row, u, nb, x);
-    default: return 0.0f;
-    }
-}
-
 // ---- input preparation ---------------------------------------------------------
 // Each consumer thread turns x[32u, 32u + 32) (optionally RMS-normalised) into
 // its XQ unit in registers, with the expressions of xq_store_block_warp.
@@ -308,8 +297,9 @@ struct GemvParams {
     int units;        // k / 32
     int tiles;        // total tiles over all segments
     int stages;       // ring depth
-    int stage_bytes;  // bytes of one stage (RT rows x max stride x matrices)
-    int consumers;    // consumer threads (multiple of 32)
+    int stage_bytes;  // bytes of one stage (RT rows x stride x matrices)
+    int groups;       // consumer groups; each holds all of x and takes RPG rows of a tile
+    int group_warps;  // warps per group (ceil(units / 32))
 };
 
 struct TileInfo {
@@ -328,24 +318,28 @@ CL_DEVINL TileInfo tile_info(const GemvParams& p, int t, int rt) {
 // Dynamic shared memory: [full|empty mbarriers][abort flag][double norm partials]
 // [float row partials, double buffered][NS stages, 128-byte aligned]
 __host__ __device__ inline int smem_red_offset(int stages) { return 16 * stages + 16 + 32 * 8; }
-__host__ __device__ inline int smem_stage_offset(int stages, int nmat, int rt) {
-    return (smem_red_offset(stages) + 2 * 32 * nmat * rt * 4 + 127) & ~127;
+__host__ __device__ inline int smem_stage_offset(int stages, int vals_per_warp) {
+    return (smem_red_offset(stages) + 2 * 32 * vals_per_warp * 4 + 127) & ~127;
 }
 
-template <int RT, bool SWIGLU>
+// Tile = groups x RPG consecutive rows; group g owns rows [g*RPG, g*RPG + RPG).
+template <int F, int RPG, bool SWIGLU>
 __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams p) {
     constexpr int NMAT = SWIGLU ? 2 : 1;
+    constexpr int VPW = NMAT * RPG;  // partial sums per warp per tile
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + p.stages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * p.stages);
     double* dred = reinterpret_cast<double*>(smem + 16 * p.stages + 16);
     float* red = reinterpret_cast<float*>(smem + smem_red_offset(p.stages));
-    uint8_t* stage_base = smem + smem_stage_offset(p.stages, NMAT, RT);
+    uint8_t* stage_base = smem + smem_stage_offset(p.stages, VPW);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int nconsumer = p.consumers;
+    const int gthreads = p.group_warps * 32;
+    const int nconsumer = p.groups * gthreads;
+    const int RT = p.groups * RPG;
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
@@ -383,9 +377,9 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
 
     // ---- consumers: build this thread's x unit (after the dependency wait) ----
     grid_wait();
-    const int u = tid;
+    const int grp = tid / gthreads;
+    const int u = tid - grp * gthreads;
     const bool active = u < p.units;
-    const int nwarps = nconsumer >> 5;
     float v[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -397,8 +391,8 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     }
     if (p.gamma) {
         // cpu_llm.cpp:156-165: sum of squares in double, mean -> float,
-        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every CTA
-        // reduces in the same order, so all CTAs see the same inv.
+        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every group of
+        // every CTA reduces in the same order, so all see the same inv.
         double ss = 0.0;
 #pragma unroll
         for (int e = 0; e < 32; ++e) ss += (double)v[e] * (double)v[e];
@@ -406,7 +400,7 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
         if (lane == 0) dred[warp] = ss;
         named_barrier(1, nconsumer);
         double tot = 0.0;
-        for (int w = 0; w < nwarps; ++w) tot += dred[w];
+        for (int w = 0; w < p.group_warps; ++w) tot += dred[grp * p.group_warps + w];
         const float inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
         if (active) {
 #pragma unroll
@@ -421,39 +415,47 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     }
     XUnit xu;
     encode_unit(v, xu);
+    const int nb = (F == CL_TYPE_Q8_0 || F == CL_TYPE_Q5_0) ? p.units : p.units / 8;
 
     for (int i = 0, t = blockIdx.x; t < p.tiles; ++i, t += gridDim.x) {
         const int s = i % p.stages;
         const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
         const TileInfo ti = tile_info(p, t, RT);
         const GemvSeg& g = p.seg[ti.seg];
-        const int nb = (g.type == CL_TYPE_Q8_0 || g.type == CL_TYPE_Q5_0) ? p.units : p.units / 8;
         const bool ok = mbar_wait(&full[s], ph);
         if (!ok) {
             atomicExch(&g_gemv_error, 2);
             *abort_flag = 1;
         }
-        const uint8_t* st = stage_base + (size_t)s * p.stage_bytes;
-        float acc[NMAT * RT];
+        const uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)grp * RPG * g.stride;
+        const int myrows = ti.rows - grp * RPG;  // rows of this tile owned by the group (may be <= 0)
+        float acc[VPW];
 #pragma unroll
-        for (int r = 0; r < NMAT * RT; ++r) {
-            acc[r] = 0.0f;
-            if (ok && active && (r % RT) < ti.rows) acc[r] = unit_dot(g.type, st + (size_t)r * g.stride, u, nb, xu);
+        for (int m = 0; m < NMAT; ++m) {
+#pragma unroll
+            for (int j = 0; j < RPG; ++j) {
+                float a = 0.0f;
+                if (ok && active && j < myrows)
+                    a = Fmt<F>::dot(st + (size_t)m * RT * g.stride + (size_t)j * g.stride, u, nb, xu);
+                acc[m * RPG + j] = a;
+            }
         }
-        float* rb = red + (i & 1) * 32 * NMAT * RT;
+        float* rb = red + (i & 1) * 32 * VPW;
 #pragma unroll
-        for (int r = 0; r < NMAT * RT; ++r) {
+        for (int r = 0; r < VPW; ++r) {
             const float w = warp_sum(acc[r]);
-            if (lane == 0) rb[warp * NMAT * RT + r] = w;
+            if (lane == 0) rb[warp * VPW + r] = w;
         }
         named_barrier(1, nconsumer);
         if (tid == 0) mbar_arrive(&empty[s]);  // every consumer is done with stage s
         if (*abort_flag) break;
         if (tid < ti.rows) {
+            const int og = tid / RPG, j = tid % RPG;
             float y = 0.0f, up = 0.0f;
-            for (int w = 0; w < nwarps; ++w) {
-                y += rb[w * NMAT * RT + tid];
-                if (SWIGLU) up += rb[w * NMAT * RT + RT + tid];
+            for (int w = 0; w < p.group_warps; ++w) {
+                const float* pw = rb + (og * p.group_warps + w) * VPW;
+                y += pw[j];
+                if (SWIGLU) up += pw[RPG + j];
             }
             const int o = ti.row0 + tid;
             if (SWIGLU) {
@@ -476,12 +478,14 @@ bool gemv_type_ok(int t) {
 
 constexpr int kStageTarget = 40 * 1024;
 constexpr int kSmemBudget = 190 * 1024;
+constexpr int kTargetWarps = 16;  // consumer warps per CTA to aim for
 
-template <int RT, bool SW>
-cudaError_t launch_rt(GemvParams& p, int threads, cudaStream_t stream) {
+template <int F, int RPG, bool SW>
+cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     constexpr int NMAT = SW ? 2 : 1;
-    auto kern = gemv_tma_kernel<RT, SW>;
-    const int smem = smem_stage_offset(p.stages, NMAT, RT) + p.stages * p.stage_bytes;
+    auto kern = gemv_tma_kernel<F, RPG, SW>;
+    const int threads = p.groups * p.group_warps * 32 + 32;
+    const int smem = smem_stage_offset(p.stages, NMAT * RPG) + p.stages * p.stage_bytes;
     static std::mutex mu;
     static std::map<std::pair<int, int>, int> occ_cache;  // (threads, smem) -> CTAs per SM
     static int sm_count = 0;
@@ -511,31 +515,47 @@ cudaError_t launch_rt(GemvParams& p, int threads, cudaStream_t stream) {
     return launch_pdl(kern, dim3(grid), dim3(threads), smem, stream, p);
 }
 
-int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
-                const void* w_up, cudaStream_t stream) {
-    const bool sw = w_up != nullptr;
-    if (nseg < 1 || nseg > kMaxSegs || (sw && nseg != 1) || k <= 0 || k % 32 != 0 || x == nullptr ||
-        reinterpret_cast<uintptr_t>(x) % 16 != 0 || (gamma && (reinterpret_cast<uintptr_t>(gamma) % 16 != 0 || !(eps > 0.0f))))
-        return CL_ERR_INVALID;
-    const int units = k / 32;
-    if (units > kMaxConsumerWarps * 32) return CL_ERR_UNSUPPORTED;
-    GemvParams p{};
-    long long smax = 0;
-    for (int i = 0; i < nseg; ++i) {
-        const cl_gemv_segment& s = segs[i];
-        if (!gemv_type_ok(s.type) || s.w == nullptr || s.y == nullptr || s.n <= 0) return CL_ERR_INVALID;
-        if (cl_native_row_bytes(s.type, k) < 0) return CL_ERR_INVALID;
-        if (s.stride < cl_row_stride(s.type, k) || s.stride % 16 != 0 || reinterpret_cast<uintptr_t>(s.w) % 16 != 0)
-            return CL_ERR_INVALID;
-        if (sw && reinterpret_cast<uintptr_t>(w_up) % 16 != 0) return CL_ERR_INVALID;
-        smax = std::max(smax, s.stride);
+template <int F, bool SW>
+cudaError_t launch_fmt(const GemvParams& p, int rpg, cudaStream_t stream) {
+    switch (rpg) {
+    case 1: return launch_cfg<F, 1, SW>(p, stream);
+    case 2: return launch_cfg<F, 2, SW>(p, stream);
+    default: return launch_cfg<F, 4, SW>(p, stream);
     }
+}
+
+template <bool SW>
+cudaError_t launch_type(int type, const GemvParams& p, int rpg, cudaStream_t stream) {
+    switch (type) {
+    case CL_TYPE_Q4_K: return launch_fmt<CL_TYPE_Q4_K, SW>(p, rpg, stream);
+    case CL_TYPE_Q5_K: return launch_fmt<CL_TYPE_Q5_K, SW>(p, rpg, stream);
+    case CL_TYPE_Q6_K: return launch_fmt<CL_TYPE_Q6_K, SW>(p, rpg, stream);
+    case CL_TYPE_Q8_0: return launch_fmt<CL_TYPE_Q8_0, SW>(p, rpg, stream);
+    case CL_TYPE_Q5_0: return launch_fmt<CL_TYPE_Q5_0, SW>(p, rpg, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// One launch over segments that share a type.
+int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
+                     const void* w_up, cudaStream_t stream) {
+    const bool sw = w_up != nullptr;
     const int nmat = sw ? 2 : 1;
-    int rt = sw ? 8 : 16;  // SwiGLU keeps 2 x RT partial sums per thread
-    while (rt > 1 && (long long)rt * smax * nmat > kStageTarget) rt /= 2;
-    if ((long long)smax * nmat > kSmemBudget / 2) return CL_ERR_UNSUPPORTED;
-    p.stage_bytes = (int)((long long)rt * smax * nmat);
-    p.stages = std::max(2, std::min(8, kSmemBudget / p.stage_bytes));
+    GemvParams p{};
+    p.units = k / 32;
+    p.group_warps = (p.units + 31) / 32;
+    long long smax = 0;
+    for (int i = 0; i < nseg; ++i) smax = std::max(smax, segs[i].stride);
+    int groups = std::max(1, std::min(8, kTargetWarps / p.group_warps));
+    while (groups > 1 && groups * p.group_warps > kMaxConsumerWarps) --groups;
+    int rpg = 4;
+    while (rpg > 1 && (long long)groups * rpg * smax * nmat > kStageTarget) rpg /= 2;
+    while (groups > 1 && (long long)groups * rpg * smax * nmat > kStageTarget) --groups;
+    if ((long long)groups * rpg * smax * nmat > kSmemBudget / 2) return CL_ERR_UNSUPPORTED;
+    p.groups = groups;
+    p.stage_bytes = (int)((long long)groups * rpg * smax * nmat);
+    p.stages = std::max(2, std::min(6, kSmemBudget / p.stage_bytes));
+    const int rt = groups * rpg;
     int tiles = 0;
     for (int i = 0; i < nseg; ++i) {
         GemvSeg& g = p.seg[i];
@@ -555,25 +575,37 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, co
     p.eps = eps;
     p.nseg = nseg;
     p.k = k;
-    p.units = units;
     p.tiles = tiles;
-    p.consumers = ((units + 31) / 32) * 32;
-    const int threads = p.consumers + 32;
-    cudaError_t e;
-#define CL_GEMV_CASE(R)                                                              \
-    case R:                                                                          \
-        e = sw ? launch_rt<R, true>(p, threads, stream) : launch_rt<R, false>(p, threads, stream); \
-        break;
-    switch (rt) {
-        CL_GEMV_CASE(1)
-        CL_GEMV_CASE(2)
-        CL_GEMV_CASE(4)
-        CL_GEMV_CASE(8)
-        CL_GEMV_CASE(16)
-    default: return CL_ERR_INVALID;
-    }
-#undef CL_GEMV_CASE
+    const cudaError_t e = sw ? launch_type<true>(segs[0].type, p, rpg, stream)
+                             : launch_type<false>(segs[0].type, p, rpg, stream);
     return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+}
+
+int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
+                const void* w_up, cudaStream_t stream) {
+    const bool sw = w_up != nullptr;
+    if (nseg < 1 || nseg > kMaxSegs || (sw && nseg != 1) || k <= 0 || k % 32 != 0 || x == nullptr ||
+        reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
+        (gamma && (reinterpret_cast<uintptr_t>(gamma) % 16 != 0 || !(eps > 0.0f))))
+        return CL_ERR_INVALID;
+    if (k / 32 > kMaxConsumerWarps * 32) return CL_ERR_UNSUPPORTED;
+    for (int i = 0; i < nseg; ++i) {
+        const cl_gemv_segment& s = segs[i];
+        if (!gemv_type_ok(s.type) || s.w == nullptr || s.y == nullptr || s.n <= 0) return CL_ERR_INVALID;
+        if (cl_native_row_bytes(s.type, k) < 0) return CL_ERR_INVALID;
+        if (s.stride < cl_row_stride(s.type, k) || s.stride % 16 != 0 || reinterpret_cast<uintptr_t>(s.w) % 16 != 0)
+            return CL_ERR_INVALID;
+    }
+    if (sw && reinterpret_cast<uintptr_t>(w_up) % 16 != 0) return CL_ERR_INVALID;
+    // Consecutive segments of one type share a launch.
+    for (int i = 0; i < nseg;) {
+        int j = i + 1;
+        while (j < nseg && segs[j].type == segs[i].type) ++j;
+        const int rc = launch_same_type(segs + i, j - i, k, x, gamma, eps, w_up, stream);
+        if (rc != CL_OK) return rc;
+        i = j;
+    }
+    return CL_OK;
 }
 
 }  // namespace cl
