@@ -22,11 +22,24 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, uint8_t
         uint8_t* d = dst + r * dst_rb;
         switch (type) {
         case CL_TYPE_Q4_K:
-            for (int i = 0; i < 144; ++i) d[b * 144 + i] = s[b * 144 + i];
+        case CL_TYPE_Q5_K: {
+            const int bs = type == CL_TYPE_Q4_K ? 144 : 176;
+            const uint8_t* sb = s + b * bs;
+            uint8_t* db = d + b * bs;
+            for (int i = 0; i < 4; ++i) db[i] = sb[i];
+            for (int i = 16; i < bs; ++i) db[i] = sb[i];
+            uint8_t slots[12] = {0};
+            for (int i = 0; i < 8; ++i) {
+                int sc, m;
+                kscale_native(sb + 4, i, sc, m);
+                const uint32_t v = (uint32_t)sc | ((uint32_t)m << 6);
+                const int bit = 12 * i;
+                slots[bit >> 3] |= (uint8_t)((v << (bit & 7)) & 0xffu);
+                slots[(bit >> 3) + 1] |= (uint8_t)((v << (bit & 7)) >> 8);
+            }
+            for (int i = 0; i < 12; ++i) db[4 + i] = slots[i];
             break;
-        case CL_TYPE_Q5_K:
-            for (int i = 0; i < 176; ++i) d[b * 176 + i] = s[b * 176 + i];
-            break;
+        }
         case CL_TYPE_Q6_K:
             for (int i = 0; i < 208; ++i) d[b * 208 + i] = s[b * 210 + i];
             d[nb * 208 + 2 * b] = s[b * 210 + 208];

@@ -8,7 +8,8 @@
 
 namespace cl {
 
-CL_DEVINL void kscale_bytes(const uint8_t* s, int i, int& sc, int& m) {
+// Native 6-bit scale/min of sub-block i (get_scale_min_k4, model.cpp:524-537).
+__host__ __device__ inline void kscale_native(const uint8_t* s, int i, int& sc, int& m) {
     if (i < 4) {
         sc = s[i] & 63;
         m = s[i + 4] & 63;
@@ -16,6 +17,16 @@ CL_DEVINL void kscale_bytes(const uint8_t* s, int i, int& sc, int& m) {
         sc = (s[i + 4] & 0x0f) | ((s[i - 4] >> 6) << 4);
         m = (s[i + 4] >> 4) | ((s[i] >> 6) << 4);
     }
+}
+
+// Device-layout K-quant header (cl_repack_rows): bytes 4..15 hold eight
+// 12-bit slots, slot i = sc_i | m_i << 6 at bit 12 i (little endian).  Same
+// 16 bytes as the native header, re-arranged so one funnel shift finds a slot.
+CL_DEVINL void kscale_slot(const uint8_t* s, int i, int& sc, int& m) {
+    const int bit = 12 * i, byte = bit >> 3, sh = bit & 7;
+    const uint32_t v = ((uint32_t)s[byte] | ((uint32_t)s[byte + 1] << 8)) >> sh;
+    sc = (int)(v & 63u);
+    m = (int)((v >> 6) & 63u);
 }
 
 CL_DEVINL float load_half(const uint8_t* p) {
@@ -49,7 +60,7 @@ CL_DEVINL float dequant_at(int type, const uint8_t* row, int k, int c) {
         const int e = c & 255, g = e >> 6, hi = (e >> 5) & 1, l = e & 31;
         const float d = load_half(blk), dmin = load_half(blk + 2);
         int sc, m;
-        kscale_bytes(blk + 4, 2 * g + hi, sc, m);
+        kscale_slot(blk + 4, 2 * g + hi, sc, m);
         const uint8_t byte = blk[(k5 ? 48 : 16) + g * 32 + l];
         int q = hi ? (byte >> 4) : (byte & 0x0f);
         if (k5 && (blk[16 + l] & (1u << (2 * g + hi)))) q += 16;

@@ -90,17 +90,6 @@ CL_DEVINL float sums_value(const Sums& a, int l0sum, int l12sum, int off) {
 
 CL_DEVINL uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
-// 6-bit scale/min of K-quant sub-block i from the 12 scale bytes
-// (get_scale_min_k4, model.cpp:524-537); s0..s2 = bytes 0-3, 4-7, 8-11.
-CL_DEVINL void kscale(uint32_t s0, uint32_t s1, uint32_t s2, int i, float& sc, float& m) {
-    const int lo = i & 3;
-    const uint32_t a = byte_of(s0, lo), b = byte_of(s1, lo), c = byte_of(s2, lo);
-    const uint32_t vs = i < 4 ? (a & 63u) : ((c & 0x0fu) | ((a >> 6) << 4));
-    const uint32_t vm = i < 4 ? (b & 63u) : ((c >> 4) | ((b >> 6) << 4));
-    sc = (float)vs;
-    m = (float)vm;
-}
-
 CL_DEVINL uint4 lds4(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 CL_DEVINL uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
 
@@ -109,26 +98,41 @@ CL_DEVINL uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const un
 template <int T>
 struct Fmt;
 
+// Scale/min slot i of a device-layout K-quant header (see dequant.cuh):
+// eight 12-bit slots sc | m << 6 in header words 1..3.
+CL_DEVINL void kslot(const uint4& hdr, int i, float& sc, float& m) {
+    const int bit = 12 * i, wi = bit >> 5, off = bit & 31;
+    const uint32_t lo = wi == 0 ? hdr.y : (wi == 1 ? hdr.z : hdr.w);
+    const uint32_t hw = wi == 0 ? hdr.z : hdr.w;
+    const uint32_t v = __funnelshift_r(lo, hw, off);
+    sc = (float)(v & 63u);
+    m = (float)((v >> 6) & 63u);
+}
+
 template <>
 struct Fmt<CL_TYPE_Q4_K> {
     CL_DEVINL static float dot(const uint8_t* row, int u, int nb, const XUnit& x) {
-        const int b = u >> 3, i = u & 7, g = i >> 1, sh = 4 * (i & 1);
+        const int b = u >> 3, i = u & 7, g = i >> 1;
+        const bool hi = (i & 1) != 0;
         const uint8_t* blk = row + b * 144;
         const uint4 hdr = lds4(blk);
         const uint4 q0 = lds4(blk + 16 + 32 * g), q1 = lds4(blk + 32 + 32 * g);
+        // high nibbles stay in place (16 q): one AND per word, 1/16 folded below
+        const uint32_t mk = hi ? 0xf0f0f0f0u : 0x0f0f0f0fu;
         Sums a{0, 0, 0};
-        acc_u(a, (q0.x >> sh) & 0x0f0f0f0fu, x.l[0], 0);
-        acc_u(a, (q0.y >> sh) & 0x0f0f0f0fu, x.l[0], 1);
-        acc_u(a, (q0.z >> sh) & 0x0f0f0f0fu, x.l[0], 2);
-        acc_u(a, (q0.w >> sh) & 0x0f0f0f0fu, x.l[0], 3);
-        acc_u(a, (q1.x >> sh) & 0x0f0f0f0fu, x.l[1], 0);
-        acc_u(a, (q1.y >> sh) & 0x0f0f0f0fu, x.l[1], 1);
-        acc_u(a, (q1.z >> sh) & 0x0f0f0f0fu, x.l[1], 2);
-        acc_u(a, (q1.w >> sh) & 0x0f0f0f0fu, x.l[1], 3);
+        acc_u(a, q0.x & mk, x.l[0], 0);
+        acc_u(a, q0.y & mk, x.l[0], 1);
+        acc_u(a, q0.z & mk, x.l[0], 2);
+        acc_u(a, q0.w & mk, x.l[0], 3);
+        acc_u(a, q1.x & mk, x.l[1], 0);
+        acc_u(a, q1.y & mk, x.l[1], 1);
+        acc_u(a, q1.z & mk, x.l[1], 2);
+        acc_u(a, q1.w & mk, x.l[1], 3);
         float sc, m;
-        kscale(hdr.y, hdr.z, hdr.w, i, sc, m);
+        kslot(hdr, i, sc, m);
         const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-        return (d * sc) * (sums_value(a, 0, 0, 0) * x.xs) - (dmin * m) * x.xsum;
+        const float xs = hi ? x.xs * 0.0625f : x.xs;
+        return (d * sc) * (sums_value(a, 0, 0, 0) * xs) - (dmin * m) * x.xsum;
     }
 };
 
@@ -152,7 +156,7 @@ struct Fmt<CL_TYPE_Q5_K> {
         acc_u(a, Q5K_W(q1.w, h1.w), x.l[1], 3);
 #undef Q5K_W
         float sc, m;
-        kscale(hdr.y, hdr.z, hdr.w, i, sc, m);
+        kslot(hdr, i, sc, m);
         const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
         return (d * sc) * (sums_value(a, 0, 0, 0) * x.xs) - (dmin * m) * x.xsum;
     }
@@ -227,6 +231,43 @@ struct Fmt<CL_TYPE_Q5_0> {
     }
 };
 
+// ---- warp reduction of N partial sums at once -------------------------------
+// Butterfly that halves the vector each step: N values cost ~N + 5 shuffles
+// instead of 5 N.  Afterwards every lane holds the full sum of value
+// index red_index<N>(lane).
+template <int N>
+CL_DEVINL float warp_sum_many(float (&v)[N], int lane) {
+    static_assert(N == 1 || N == 2 || N == 4 || N == 8, "N must be 1, 2, 4 or 8");
+    float w[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) w[j] = v[j];
+    int n = N, bit = 16;
+#pragma unroll
+    for (int step = 0; step < 3; ++step) {
+        if (n > 1) {
+            const bool upper = (lane & bit) != 0;
+#pragma unroll
+            for (int j = 0; j < N / 2; ++j) {
+                if (j < n / 2) {
+                    const float keep = upper ? w[j + n / 2] : w[j];
+                    const float send = upper ? w[j] : w[j + n / 2];
+                    w[j] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+                }
+            }
+            n /= 2;
+            bit >>= 1;
+        }
+    }
+    float r = w[0];
+    for (; bit > 0; bit >>= 1) r += __shfl_xor_sync(0xffffffffu, r, bit);
+    return r;
+}
+
+template <int N>
+CL_DEVINL int red_index(int lane) {
+    return N == 1 ? 0 : N == 2 ? (lane >> 4) & 1 : N == 4 ? (lane >> 3) & 3 : (lane >> 2) & 7;
+}
+
 // ---- input preparation ---------------------------------------------------------
 // Each consumer thread turns x[32u, 32u + 32) (optionally RMS-normalised) into
 // its XQ unit in registers, with the expressions of xq_store_block_warp.
@@ -272,8 +313,9 @@ CL_DEVINL void encode_unit(const float (&v)[32], XUnit& r) {
 
 // ---- kernel -------------------------------------------------------------------
 constexpr int kMaxSegs = 4;
-constexpr int kMaxConsumerWarps = 20;  // k <= 20480
+constexpr int kMaxConsumerWarps = 31;  // k <= 31744
 constexpr int kMaxThreads = (kMaxConsumerWarps + 1) * 32;
+constexpr int kMaxGroups = 15;         // named barriers 1..15
 
 struct GemvSeg {
     const uint8_t* w;
@@ -295,10 +337,10 @@ struct GemvParams {
     int nseg;
     int k;
     int units;        // k / 32
-    int tiles;        // total tiles over all segments
-    int stages;       // ring depth
-    int stage_bytes;  // bytes of one stage (RT rows x stride x matrices)
-    int groups;       // consumer groups; each holds all of x and takes RPG rows of a tile
+    int tiles;        // total tiles (RPG rows each) over all segments
+    int stages;       // ring depth per group
+    int stage_bytes;  // bytes of one stage (RPG rows x stride x matrices)
+    int groups;       // consumer groups; each holds all of x and runs its own ring
     int group_warps;  // warps per group (ceil(units / 32))
 };
 
@@ -315,36 +357,36 @@ CL_DEVINL TileInfo tile_info(const GemvParams& p, int t, int rt) {
     return TileInfo{s, row0, min(rt, p.seg[s].n - row0)};
 }
 
-// Dynamic shared memory: [full|empty mbarriers][abort flag][double norm partials]
-// [float row partials, double buffered][NS stages, 128-byte aligned]
-__host__ __device__ inline int smem_red_offset(int stages) { return 16 * stages + 16 + 32 * 8; }
-__host__ __device__ inline int smem_stage_offset(int stages, int vals_per_warp) {
-    return (smem_red_offset(stages) + 2 * 32 * vals_per_warp * 4 + 127) & ~127;
+// Dynamic shared memory:
+//   [full|empty mbarriers: groups x stages x 2 x 8 B][abort flag 16 B]
+//   [double norm partials: 32 x 8 B][float row partials: 32 warps x 2 x VPW]
+//   [stages: groups x stages x stage_bytes, 128-byte aligned]
+__host__ __device__ inline int smem_red_offset(int groups, int stages) { return 16 * groups * stages + 16 + 32 * 8; }
+__host__ __device__ inline int smem_stage_offset(int groups, int stages, int vpw) {
+    return (smem_red_offset(groups, stages) + 32 * 2 * vpw * 4 + 127) & ~127;
 }
 
-// Tile = groups x RPG consecutive rows; group g owns rows [g*RPG, g*RPG + RPG).
+// Group g of CTA c processes tiles c*G + g, c*G + g + gridDim.x*G, ...; a
+// tile is RPG consecutive rows (and the same rows of `up` for SwiGLU).
 template <int F, int RPG, bool SWIGLU>
 __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams p) {
     constexpr int NMAT = SWIGLU ? 2 : 1;
     constexpr int VPW = NMAT * RPG;  // partial sums per warp per tile
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + p.stages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * p.stages);
-    double* dred = reinterpret_cast<double*>(smem + 16 * p.stages + 16);
-    float* red = reinterpret_cast<float*>(smem + smem_red_offset(p.stages));
-    uint8_t* stage_base = smem + smem_stage_offset(p.stages, VPW);
+    const int G = p.groups, NS = p.stages;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // [G][NS][2]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * G * NS);
+    double* dred = reinterpret_cast<double*>(smem + 16 * G * NS + 16);
+    float* red = reinterpret_cast<float*>(smem + smem_red_offset(G, NS));
+    uint8_t* stage_base = smem + smem_stage_offset(G, NS, VPW);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int gthreads = p.group_warps * 32;
-    const int nconsumer = p.groups * gthreads;
-    const int RT = p.groups * RPG;
+    const int nconsumer = G * gthreads;
+    const int tile_stride = gridDim.x * G;
     if (tid == 0) {
-        for (int s = 0; s < p.stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
+        for (int i = 0; i < 2 * G * NS; ++i) mbar_init(&bars[i], 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -352,24 +394,33 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     grid_launch_dependents();
 
     if (tid >= nconsumer) {
-        // ---- producer: stream weight tiles (immutable: no dependency wait) ----
-        if (tid == nconsumer) {
-            for (int i = 0, t = blockIdx.x; t < p.tiles; ++i, t += gridDim.x) {
-                const int s = i % p.stages;
-                const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+        // ---- producer warp: lane g feeds group g (weights are immutable, so
+        // streaming starts before the dependency wait) ----
+        const int g = tid - nconsumer;
+        if (g < G) {
+            uint64_t* full = bars + 2 * g * NS;
+            uint64_t* empty = full + NS;
+            uint8_t* ring = stage_base + (size_t)g * NS * p.stage_bytes;
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x * G + g; t < p.tiles; t += tile_stride) {
                 if (!mbar_wait(&empty[s], ph ^ 1u)) {
                     atomicExch(&g_gemv_error, 1);
                     *abort_flag = 1;
                     break;
                 }
-                const TileInfo ti = tile_info(p, t, RT);
-                const GemvSeg& g = p.seg[ti.seg];
-                const uint32_t bytes = (uint32_t)(ti.rows * g.stride);
-                uint8_t* dst = stage_base + (size_t)s * p.stage_bytes;
+                const TileInfo ti = tile_info(p, t, RPG);
+                const GemvSeg& sg = p.seg[ti.seg];
+                const uint32_t bytes = (uint32_t)(ti.rows * sg.stride);
+                uint8_t* dst = ring + (size_t)s * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[s], bytes * NMAT);
-                bulk_g2s(dst, g.w + (size_t)ti.row0 * g.stride, bytes, &full[s]);
+                bulk_g2s(dst, sg.w + (size_t)ti.row0 * sg.stride, bytes, &full[s]);
                 if (SWIGLU)
-                    bulk_g2s(dst + (size_t)RT * g.stride, g.w_up + (size_t)ti.row0 * g.stride, bytes, &full[s]);
+                    bulk_g2s(dst + (size_t)RPG * sg.stride, sg.w_up + (size_t)ti.row0 * sg.stride, bytes, &full[s]);
+                if (++s == NS) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
         }
         return;
@@ -378,8 +429,10 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     // ---- consumers: build this thread's x unit (after the dependency wait) ----
     grid_wait();
     const int grp = tid / gthreads;
-    const int u = tid - grp * gthreads;
+    const int gt = tid - grp * gthreads;  // thread within the group = unit index
+    const int u = gt;
     const bool active = u < p.units;
+    const uint32_t gbar = 1 + grp;  // named barrier of the group
     float v[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -398,7 +451,7 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
         for (int e = 0; e < 32; ++e) ss += (double)v[e] * (double)v[e];
         ss = warp_sum_d(ss);
         if (lane == 0) dred[warp] = ss;
-        named_barrier(1, nconsumer);
+        named_barrier(gbar, gthreads);
         double tot = 0.0;
         for (int w = 0; w < p.group_warps; ++w) tot += dred[grp * p.group_warps + w];
         const float inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
@@ -416,57 +469,60 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     XUnit xu;
     encode_unit(v, xu);
     const int nb = (F == CL_TYPE_Q8_0 || F == CL_TYPE_Q5_0) ? p.units : p.units / 8;
-
-    for (int i = 0, t = blockIdx.x; t < p.tiles; ++i, t += gridDim.x) {
-        const int s = i % p.stages;
-        const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
-        const TileInfo ti = tile_info(p, t, RT);
-        const GemvSeg& g = p.seg[ti.seg];
+    uint64_t* full = bars + 2 * grp * NS;
+    uint64_t* empty = full + NS;
+    const uint8_t* ring = stage_base + (size_t)grp * NS * p.stage_bytes;
+    int s = 0, it = 0;
+    uint32_t ph = 0;
+    for (int t = blockIdx.x * G + grp; t < p.tiles; t += tile_stride, ++it) {
+        const TileInfo ti = tile_info(p, t, RPG);
+        const GemvSeg& sg = p.seg[ti.seg];
         const bool ok = mbar_wait(&full[s], ph);
         if (!ok) {
             atomicExch(&g_gemv_error, 2);
             *abort_flag = 1;
         }
-        const uint8_t* st = stage_base + (size_t)s * p.stage_bytes + (size_t)grp * RPG * g.stride;
-        const int myrows = ti.rows - grp * RPG;  // rows of this tile owned by the group (may be <= 0)
+        const uint8_t* st = ring + (size_t)s * p.stage_bytes;
         float acc[VPW];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
 #pragma unroll
             for (int j = 0; j < RPG; ++j) {
                 float a = 0.0f;
-                if (ok && active && j < myrows)
-                    a = Fmt<F>::dot(st + (size_t)m * RT * g.stride + (size_t)j * g.stride, u, nb, xu);
+                if (ok && active && j < ti.rows)
+                    a = Fmt<F>::dot(st + (size_t)(m * RPG + j) * sg.stride, u, nb, xu);
                 acc[m * RPG + j] = a;
             }
         }
-        float* rb = red + (i & 1) * 32 * VPW;
-#pragma unroll
-        for (int r = 0; r < VPW; ++r) {
-            const float w = warp_sum(acc[r]);
-            if (lane == 0) rb[warp * VPW + r] = w;
+        float* rb = red + (warp * 2 + (it & 1)) * VPW;
+        {
+            const float w = warp_sum_many<VPW>(acc, lane);
+            if ((lane & (32 / VPW - 1)) == 0) rb[red_index<VPW>(lane)] = w;
         }
-        named_barrier(1, nconsumer);
-        if (tid == 0) mbar_arrive(&empty[s]);  // every consumer is done with stage s
+        named_barrier(gbar, gthreads);
+        if (gt == 0) mbar_arrive(&empty[s]);  // the whole group is done with stage s
         if (*abort_flag) break;
-        if (tid < ti.rows) {
-            const int og = tid / RPG, j = tid % RPG;
+        if (gt < ti.rows) {
             float y = 0.0f, up = 0.0f;
             for (int w = 0; w < p.group_warps; ++w) {
-                const float* pw = rb + (og * p.group_warps + w) * VPW;
-                y += pw[j];
-                if (SWIGLU) up += pw[RPG + j];
+                const float* pw = red + ((grp * p.group_warps + w) * 2 + (it & 1)) * VPW;
+                y += pw[gt];
+                if (SWIGLU) up += pw[RPG + gt];
             }
-            const int o = ti.row0 + tid;
+            const int o = ti.row0 + gt;
             if (SWIGLU) {
                 // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
                 const float sig = y >= 0.0f ? 1.0f / (1.0f + expf(-y)) : expf(y) / (1.0f + expf(y));
                 y = __fmul_rn(__fmul_rn(y, sig), up);
             } else {
-                if (g.bias) y += g.bias[o];
-                if (g.residual) y = g.residual[o] + y;
+                if (sg.bias) y += sg.bias[o];
+                if (sg.residual) y = sg.residual[o] + y;
             }
-            g.y[o] = y;
+            sg.y[o] = y;
+        }
+        if (++s == NS) {
+            s = 0;
+            ph ^= 1u;
         }
     }
 }
@@ -478,14 +534,14 @@ bool gemv_type_ok(int t) {
 
 constexpr int kStageTarget = 40 * 1024;
 constexpr int kSmemBudget = 190 * 1024;
-constexpr int kTargetWarps = 16;  // consumer warps per CTA to aim for
+constexpr int kTargetWarps = 28;  // consumer warps per CTA to aim for
 
 template <int F, int RPG, bool SW>
 cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     constexpr int NMAT = SW ? 2 : 1;
     auto kern = gemv_tma_kernel<F, RPG, SW>;
     const int threads = p.groups * p.group_warps * 32 + 32;
-    const int smem = smem_stage_offset(p.stages, NMAT * RPG) + p.stages * p.stage_bytes;
+    const int smem = smem_stage_offset(p.groups, p.stages, NMAT * RPG) + p.groups * p.stages * p.stage_bytes;
     static std::mutex mu;
     static std::map<std::pair<int, int>, int> occ_cache;  // (threads, smem) -> CTAs per SM
     static int sm_count = 0;
@@ -511,7 +567,7 @@ cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
         }
     }
     if (occ < 1) return cudaErrorInvalidConfiguration;
-    const int grid = std::min(p.tiles, occ * sm_count);
+    const int grid = std::min((p.tiles + p.groups - 1) / p.groups, occ * sm_count);
     return launch_pdl(kern, dim3(grid), dim3(threads), smem, stream, p);
 }
 
@@ -546,16 +602,18 @@ int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* 
     p.group_warps = (p.units + 31) / 32;
     long long smax = 0;
     for (int i = 0; i < nseg; ++i) smax = std::max(smax, segs[i].stride);
-    int groups = std::max(1, std::min(8, kTargetWarps / p.group_warps));
+    int groups = std::max(1, std::min(kMaxGroups, kTargetWarps / p.group_warps));
     while (groups > 1 && groups * p.group_warps > kMaxConsumerWarps) --groups;
+    // Per-group stage: up to 4 rows, sized so that >= 3 stages per group fit.
+    const long long target = std::min<long long>(48 * 1024, kSmemBudget / (3LL * groups));
     int rpg = 4;
-    while (rpg > 1 && (long long)groups * rpg * smax * nmat > kStageTarget) rpg /= 2;
-    while (groups > 1 && (long long)groups * rpg * smax * nmat > kStageTarget) --groups;
-    if ((long long)groups * rpg * smax * nmat > kSmemBudget / 2) return CL_ERR_UNSUPPORTED;
+    while (rpg > 1 && (long long)rpg * smax * nmat > target) rpg /= 2;
+    while (groups > 1 && (long long)groups * 2 * rpg * smax * nmat > kSmemBudget) --groups;
+    if ((long long)groups * 2 * rpg * smax * nmat > kSmemBudget) return CL_ERR_UNSUPPORTED;
     p.groups = groups;
-    p.stage_bytes = (int)((long long)groups * rpg * smax * nmat);
-    p.stages = std::max(2, std::min(6, kSmemBudget / p.stage_bytes));
-    const int rt = groups * rpg;
+    p.stage_bytes = (int)((long long)rpg * smax * nmat);
+    p.stages = std::max(2, std::min(6, kSmemBudget / (groups * p.stage_bytes)));
+    const int rt = rpg;
     int tiles = 0;
     for (int i = 0; i < nseg; ++i) {
         GemvSeg& g = p.seg[i];
