@@ -124,10 +124,10 @@ def test_gemv_fused_rmsnorm(cuda, k):
 
 
 def test_gemv_rejects_unsupported_width(cuda):
-    w = torch.zeros((4, K.row_stride(sg.Q4_K, 20736)), dtype=torch.uint8, device="cuda")
+    w = torch.zeros((4, K.row_stride(sg.Q4_K, 32768)), dtype=torch.uint8, device="cuda")
     from myllm_b200._native import KernelError
     with pytest.raises(KernelError):
-        K.gemv(sg.Q4_K, w, 4, 20736, torch.zeros(20736, device="cuda"))
+        K.gemv(sg.Q4_K, w, 4, 32768, torch.zeros(32768, device="cuda"))
 
 
 def test_no_device_error_recorded(cuda):
