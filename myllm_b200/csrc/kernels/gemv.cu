@@ -318,9 +318,14 @@ CL_DEVINL TileInfo tile_info(const GemvParams& p, int t, int rt) {
 //   [full|empty mbarriers: groups x stages x 2 x 8 B][abort flag 16 B]
 //   [double norm partials: 32 x 8 B][float row partials: 32 warps x 2 x VPW]
 //   [stages: groups x stages x stage_bytes, 128-byte aligned]
-__host__ __device__ inline int smem_red_offset(int groups, int stages) { return 16 * groups * stages + 16 + 32 * 8; }
+// tickets: groups x stages ints after the norm partials; partial sums:
+// [group][stage][warp in group][VPW] floats.
+__host__ __device__ inline int smem_ticket_offset(int groups, int stages) { return 16 * groups * stages + 16 + 32 * 8; }
+__host__ __device__ inline int smem_red_offset(int groups, int stages) {
+    return (smem_ticket_offset(groups, stages) + 4 * groups * stages + 15) & ~15;
+}
 __host__ __device__ inline int smem_xq_offset(int groups, int stages, int vpw) {
-    return (smem_red_offset(groups, stages) + 32 * 2 * vpw * 4 + 127) & ~127;
+    return (smem_red_offset(groups, stages) + 4 * kMaxConsumerWarps * stages * vpw + 127) & ~127;
 }
 __host__ __device__ inline int smem_stage_offset(int groups, int stages, int vpw, int k) {
     return (smem_xq_offset(groups, stages, vpw) + (int)xq_total_bytes(k) + 127) & ~127;
@@ -337,6 +342,7 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // [G][NS][2]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * G * NS);
     double* dred = reinterpret_cast<double*>(smem + 16 * G * NS + 16);
+    int* tickets = reinterpret_cast<int*>(smem + smem_ticket_offset(G, NS));
     float* red = reinterpret_cast<float*>(smem + smem_red_offset(G, NS));
     void* xq_smem = smem + smem_xq_offset(G, NS, VPW);
     uint8_t* stage_base = smem + smem_stage_offset(G, NS, VPW, p.k);
@@ -347,7 +353,14 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     const int nconsumer = G * gthreads;
     const int tile_stride = gridDim.x * G;
     if (tid == 0) {
-        for (int i = 0; i < 2 * G * NS; ++i) mbar_init(&bars[i], 1);
+        // full: one producer arrival (+ tx bytes); empty: one per warp of the group
+        for (int g = 0; g < G; ++g) {
+            for (int s = 0; s < NS; ++s) {
+                mbar_init(&bars[2 * g * NS + s], 1);
+                mbar_init(&bars[2 * g * NS + NS + s], p.group_warps);
+            }
+        }
+        for (int i = 0; i < G * NS; ++i) tickets[i] = 0;
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -394,7 +407,6 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     const int gt = tid - grp * gthreads;  // thread within the group = unit index
     const int u = gt;
     const bool active = u < p.units;
-    const uint32_t gbar = 1 + grp;  // named barrier of the group
     const int cwarps = nconsumer >> 5;
     float inv = 1.0f;
     if (p.gamma) {
@@ -450,32 +462,45 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
                 acc[m * RPG + j] = a;
             }
         }
-        float* rb = red + (warp * 2 + (it & 1)) * VPW;
+        // publish this warp's partials; the last warp of the group to finish
+        // the tile reduces them and writes the outputs (no group barrier)
+        const int gw = warp - grp * p.group_warps;
+        float* rb = red + ((size_t)(grp * NS + s) * kMaxConsumerWarps) * VPW;
         {
             const float w = warp_sum_many<VPW>(acc, lane);
-            if ((lane & (32 / VPW - 1)) == 0) rb[red_index<VPW>(lane)] = w;
+            if ((lane & (32 / VPW - 1)) == 0) rb[gw * VPW + red_index<VPW>(lane)] = w;
         }
-        named_barrier(gbar, gthreads);
-        if (gt == 0) mbar_arrive(&empty[s]);  // the whole group is done with stage s
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&tickets[grp * NS + s], 1) == p.group_warps - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            if (lane < ti.rows && !*abort_flag) {
+                float y = 0.0f, up = 0.0f;
+                for (int w = 0; w < p.group_warps; ++w) {
+                    y += rb[w * VPW + lane];
+                    if (SWIGLU) up += rb[w * VPW + RPG + lane];
+                }
+                const int o = ti.row0 + lane;
+                if (SWIGLU) {
+                    // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
+                    const float sig = y >= 0.0f ? 1.0f / (1.0f + expf(-y)) : expf(y) / (1.0f + expf(y));
+                    y = __fmul_rn(__fmul_rn(y, sig), up);
+                } else {
+                    if (sg.bias) y += sg.bias[o];
+                    if (sg.residual) y = sg.residual[o] + y;
+                }
+                sg.y[o] = y;
+            }
+            if (lane == 0) tickets[grp * NS + s] = 0;
+            __syncwarp();
+        }
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
         if (*abort_flag) break;
-        if (gt < ti.rows) {
-            float y = 0.0f, up = 0.0f;
-            for (int w = 0; w < p.group_warps; ++w) {
-                const float* pw = red + ((grp * p.group_warps + w) * 2 + (it & 1)) * VPW;
-                y += pw[gt];
-                if (SWIGLU) up += pw[RPG + gt];
-            }
-            const int o = ti.row0 + gt;
-            if (SWIGLU) {
-                // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
-                const float sig = y >= 0.0f ? 1.0f / (1.0f + expf(-y)) : expf(y) / (1.0f + expf(y));
-                y = __fmul_rn(__fmul_rn(y, sig), up);
-            } else {
-                if (sg.bias) y += sg.bias[o];
-                if (sg.residual) y = sg.residual[o] + y;
-            }
-            sg.y[o] = y;
-        }
         if (++s == NS) {
             s = 0;
             ph ^= 1u;
