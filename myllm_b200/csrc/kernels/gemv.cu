@@ -268,6 +268,49 @@ CL_DEVINL int red_index(int lane) {
     return N == 1 ? 0 : N == 2 ? (lane >> 4) & 1 : N == 4 ? (lane >> 3) & 3 : (lane >> 2) & 7;
 }
 
+// ---- input preparation ---------------------------------------------------------
+// Each consumer thread turns x[32u, 32u + 32) (optionally RMS-normalised) into
+// its XQ unit in registers, with the expressions of xq_store_block_warp.
+CL_DEVINL void encode_unit(const float (&v)[32], XUnit& r) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    const float sc = amax / 127.0f;
+    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    uint32_t w0[8], w1[8], w2[8];
+    int t0[2] = {0, 0}, t12[2] = {0, 0};
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const float r0 = v[e] * inv;
+        const float l0 = fminf(fmaxf(rintf(r0), -127.0f), 127.0f);
+        const float r1 = (r0 - l0) * 128.0f;
+        const float l1 = fminf(fmaxf(rintf(r1), -64.0f), 64.0f);
+        const float r2 = (r1 - l1) * 128.0f;
+        const float l2 = fminf(fmaxf(rintf(r2), -64.0f), 64.0f);
+        const int i0 = (int)l0, i1 = (int)l1, i2 = (int)l2;
+        const int sh = 8 * (e & 3);
+        if ((e & 3) == 0) {
+            w0[e >> 2] = 0u;
+            w1[e >> 2] = 0u;
+            w2[e >> 2] = 0u;
+        }
+        w0[e >> 2] |= ((uint32_t)i0 & 0xffu) << sh;
+        w1[e >> 2] |= ((uint32_t)i1 & 0xffu) << sh;
+        w2[e >> 2] |= ((uint32_t)i2 & 0xffu) << sh;
+        t0[e >> 4] += i0;
+        t12[e >> 4] += i1 * 128 + i2;
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        r.l[c][0] = make_int4((int)w0[4 * c], (int)w0[4 * c + 1], (int)w0[4 * c + 2], (int)w0[4 * c + 3]);
+        r.l[c][1] = make_int4((int)w1[4 * c], (int)w1[4 * c + 1], (int)w1[4 * c + 2], (int)w1[4 * c + 3]);
+        r.l[c][2] = make_int4((int)w2[4 * c], (int)w2[4 * c + 1], (int)w2[4 * c + 2], (int)w2[4 * c + 3]);
+        r.s[c] = make_int2(t0[c], t12[c]);
+    }
+    r.xs = sc * (1.0f / 16384.0f);
+    r.xsum = fmaf((float)(t0[0] + t0[1]), 16384.0f, (float)(t12[0] + t12[1])) * r.xs;
+}
+
 // ---- kernel -------------------------------------------------------------------
 constexpr int kMaxSegs = 4;
 constexpr int kMaxConsumerWarps = 23;  // k <= 23552
@@ -324,11 +367,12 @@ __host__ __device__ inline int smem_ticket_offset(int groups, int stages) { retu
 __host__ __device__ inline int smem_red_offset(int groups, int stages) {
     return (smem_ticket_offset(groups, stages) + 4 * groups * stages + 15) & ~15;
 }
-__host__ __device__ inline int smem_xq_offset(int groups, int stages, int vpw) {
-    return (smem_red_offset(groups, stages) + 4 * kMaxConsumerWarps * stages * vpw + 127) & ~127;
+__host__ __device__ inline int smem_xq_offset(int groups, int stages, int vpw, int gwarps) {
+    return (smem_red_offset(groups, stages) + 4 * groups * stages * gwarps * vpw + 127) & ~127;
 }
-__host__ __device__ inline int smem_stage_offset(int groups, int stages, int vpw, int k) {
-    return (smem_xq_offset(groups, stages, vpw) + (int)xq_total_bytes(k) + 127) & ~127;
+__host__ __device__ inline int xpub_bytes(int groups, int k) { return groups > 1 ? (k / 32) * 128 : 0; }
+__host__ __device__ inline int smem_stage_offset(int groups, int stages, int vpw, int gwarps, int k) {
+    return (smem_xq_offset(groups, stages, vpw, gwarps) + xpub_bytes(groups, k) + 127) & ~127;
 }
 
 // Group g of CTA c processes tiles c*G + g, c*G + g + gridDim.x*G, ...; a
@@ -344,8 +388,8 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
     double* dred = reinterpret_cast<double*>(smem + 16 * G * NS + 16);
     int* tickets = reinterpret_cast<int*>(smem + smem_ticket_offset(G, NS));
     float* red = reinterpret_cast<float*>(smem + smem_red_offset(G, NS));
-    void* xq_smem = smem + smem_xq_offset(G, NS, VPW);
-    uint8_t* stage_base = smem + smem_stage_offset(G, NS, VPW, p.k);
+    void* xq_smem = smem + smem_xq_offset(G, NS, VPW, p.group_warps);
+    uint8_t* stage_base = smem + smem_stage_offset(G, NS, VPW, p.group_warps, p.k);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -400,42 +444,79 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
         return;
     }
 
-    // ---- consumers: encode x once per CTA into shared memory (a warp per
-    // 32-element block), then each thread takes its unit into registers ----
+    // ---- consumers: group 0 turns x into XQ units (one 32-column unit per
+    // thread, in registers) and, when there are more groups, publishes them
+    // in shared memory for the others ----
     grid_wait();
     const int grp = tid / gthreads;
     const int gt = tid - grp * gthreads;  // thread within the group = unit index
     const int u = gt;
     const bool active = u < p.units;
-    const int cwarps = nconsumer >> 5;
-    float inv = 1.0f;
-    if (p.gamma) {
-        // cpu_llm.cpp:156-165: sum of squares in double, mean -> float,
-        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every CTA
-        // reduces in the same order, so all CTAs see the same inv.
-        double ss = 0.0;
-        for (int b = warp; b < p.units; b += cwarps) {
-            const double xv = (double)p.x[32 * b + lane];
-            ss += xv * xv;
-        }
-        ss = warp_sum_d(ss);
-        if (lane == 0) dred[warp] = ss;
-        named_barrier(1, nconsumer);
-        double tot = 0.0;
-        for (int w = 0; w < cwarps; ++w) tot += dred[w];
-        inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
-    }
-    {
-        const XQMut xm = xq_mut(xq_smem, p.k);
-        for (int b = warp; b < p.units; b += cwarps) {
-            float xv = p.x[32 * b + lane];
-            if (p.gamma) xv = __fmul_rn(xv, __fmul_rn(inv, p.gamma[32 * b + lane]));
-            xq_store_block_warp(xm, b, xv);
-        }
-    }
-    named_barrier(1, nconsumer);
     XUnit xu{};
-    if (active) load_xunit(xq_view(xq_smem, p.k), u, xu);
+    uint4* xpub = reinterpret_cast<uint4*>(xq_smem);  // [units][8] uint4
+    if (grp == 0) {
+        float v[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 f =
+                active ? reinterpret_cast<const float4*>(p.x + 32 * u)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * q] = f.x;
+            v[4 * q + 1] = f.y;
+            v[4 * q + 2] = f.z;
+            v[4 * q + 3] = f.w;
+        }
+        if (p.gamma) {
+            // cpu_llm.cpp:156-165: sum of squares in double, mean -> float,
+            // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every
+            // CTA reduces in the same order, so all CTAs see the same inv.
+            double ss = 0.0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ss += (double)v[e] * (double)v[e];
+            ss = warp_sum_d(ss);
+            if (lane == 0) dred[warp] = ss;
+            named_barrier(1, gthreads);
+            double tot = 0.0;
+            for (int w = 0; w < p.group_warps; ++w) tot += dred[w];
+            const float inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
+            if (active) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 gm = reinterpret_cast<const float4*>(p.gamma + 32 * u)[q];
+                    v[4 * q] = __fmul_rn(v[4 * q], __fmul_rn(inv, gm.x));
+                    v[4 * q + 1] = __fmul_rn(v[4 * q + 1], __fmul_rn(inv, gm.y));
+                    v[4 * q + 2] = __fmul_rn(v[4 * q + 2], __fmul_rn(inv, gm.z));
+                    v[4 * q + 3] = __fmul_rn(v[4 * q + 3], __fmul_rn(inv, gm.w));
+                }
+            }
+        }
+        encode_unit(v, xu);
+        if (G > 1 && active) {
+            uint4* o = xpub + 8 * u;
+            o[0] = make_uint4(xu.l[0][0].x, xu.l[0][0].y, xu.l[0][0].z, xu.l[0][0].w);
+            o[1] = make_uint4(xu.l[0][1].x, xu.l[0][1].y, xu.l[0][1].z, xu.l[0][1].w);
+            o[2] = make_uint4(xu.l[0][2].x, xu.l[0][2].y, xu.l[0][2].z, xu.l[0][2].w);
+            o[3] = make_uint4(xu.l[1][0].x, xu.l[1][0].y, xu.l[1][0].z, xu.l[1][0].w);
+            o[4] = make_uint4(xu.l[1][1].x, xu.l[1][1].y, xu.l[1][1].z, xu.l[1][1].w);
+            o[5] = make_uint4(xu.l[1][2].x, xu.l[1][2].y, xu.l[1][2].z, xu.l[1][2].w);
+            o[6] = make_uint4(xu.s[0].x, xu.s[0].y, xu.s[1].x, xu.s[1].y);
+            o[7] = make_uint4(__float_as_uint(xu.xs), __float_as_uint(xu.xsum), 0u, 0u);
+        }
+    }
+    if (G > 1) {
+        named_barrier(1, nconsumer);
+        if (grp > 0 && active) {
+            const uint4* o = xpub + 8 * u;
+            uint4 t;
+            t = o[0]; xu.l[0][0] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[1]; xu.l[0][1] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[2]; xu.l[0][2] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[3]; xu.l[1][0] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[4]; xu.l[1][1] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[5]; xu.l[1][2] = make_int4(t.x, t.y, t.z, t.w);
+            t = o[6]; xu.s[0] = make_int2(t.x, t.y); xu.s[1] = make_int2(t.z, t.w);
+            t = o[7]; xu.xs = __uint_as_float(t.x); xu.xsum = __uint_as_float(t.y);
+        }
+    }
     const int nb = (F == CL_TYPE_Q8_0 || F == CL_TYPE_Q5_0) ? p.units : p.units / 8;
     uint64_t* full = bars + 2 * grp * NS;
     uint64_t* empty = full + NS;
@@ -465,7 +546,7 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
         // publish this warp's partials; the last warp of the group to finish
         // the tile reduces them and writes the outputs (no group barrier)
         const int gw = warp - grp * p.group_warps;
-        float* rb = red + ((size_t)(grp * NS + s) * kMaxConsumerWarps) * VPW;
+        float* rb = red + ((size_t)(grp * NS + s) * p.group_warps) * VPW;
         {
             const float w = warp_sum_many<VPW>(acc, lane);
             if ((lane & (32 / VPW - 1)) == 0) rb[gw * VPW + red_index<VPW>(lane)] = w;
@@ -522,7 +603,8 @@ cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     constexpr int NMAT = SW ? 2 : 1;
     auto kern = gemv_tma_kernel<F, RPG, SW>;
     const int threads = p.groups * p.group_warps * 32 + 32;
-    const int smem = smem_stage_offset(p.groups, p.stages, NMAT * RPG, p.k) + p.groups * p.stages * p.stage_bytes;
+    const int smem = smem_stage_offset(p.groups, p.stages, NMAT * RPG, p.group_warps, p.k) +
+                     p.groups * p.stages * p.stage_bytes;
     static std::mutex mu;
     static std::map<std::pair<int, int>, int> occ_cache;  // (threads, smem) -> CTAs per SM
     static int sm_count = 0;
@@ -587,7 +669,7 @@ int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* 
     while (groups > 1 && groups * p.group_warps > kMaxConsumerWarps) --groups;
     // Per-group stage: up to 4 rows, sized so that >= 3 stages per group fit
     // next to the CTA's XQ copy of x.
-    const int budget = kSmemBudget - (int)xq_total_bytes(k);
+    const int budget = kSmemBudget - xpub_bytes(groups, k);
     const long long target = std::min<long long>(48 * 1024, budget / (3LL * groups));
     int rpg = 4;
     while (rpg > 1 && (long long)rpg * smax * nmat > target) rpg /= 2;
