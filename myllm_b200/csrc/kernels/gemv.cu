@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
             for (int e = 0; e < 32; ++e) ss += (double)v[e] * (double)v[e];
             ss = warp_sum_d(ss);
             if (lane == 0) dred[warp] = ss;
-            named_barrier(1, gthreads);
+            named_barrier(2, gthreads);  // group 0 only (barrier 1 is the all-consumer one)
             double tot = 0.0;
             for (int w = 0; w < p.group_warps; ++w) tot += dred[w];
             const float inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
