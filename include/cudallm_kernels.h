@@ -40,7 +40,8 @@ enum {
     CL_ERR_INVALID = 1,     /* bad argument, shape or alignment */
     CL_ERR_UNSUPPORTED = 2, /* type/shape combination not implemented */
     CL_ERR_CUDA = 3,        /* a CUDA launch failed */
-    CL_ERR_WORKSPACE = 4    /* workspace missing or too small */
+    CL_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+    CL_ERR_LIMIT = 5        /* request exceeds a fixed built-in scratch size */
 };
 
 CL_API const char* cl_status_string(int status);
@@ -137,6 +138,21 @@ CL_API size_t cl_attn_decode_workspace_bytes(int q_heads, int head_dim, int max_
 CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
                           int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out,
                           void* xq, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* cl_attn_decode without a workspace argument, for callers that cannot
+ * allocate device memory (no counterpart in the reference: MetalLLM and
+ * CPULLM allocate their scratch themselves).  The split partials live in a
+ * fixed 2 MiB array compiled into the library (held by every GPU that loads
+ * it until exit); requests needing more than
+ * cl_attn_decode_noalloc_limit_bytes() (q_heads * ceil(max_len / 64) *
+ * (head_dim + 2) * 4 bytes) return CL_ERR_LIMIT.  The first call on a device
+ * looks up the array's device address with that device current; make that
+ * first call before any stream capture.  All calls on a device share the
+ * array, so calls that overlap on the GPU (e.g. on concurrent streams) race;
+ * serialise them.  Allocates nothing (no cudaMalloc/cudaFree). */
+CL_API size_t cl_attn_decode_noalloc_limit_bytes(void);
+CL_API int cl_attn_decode_noalloc(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
+                                  int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out,
+                                  cudaStream_t stream);
 /* Causal prefill attention for rows at positions pos0..pos0+rows-1 against
  * cache rows 0..pos0+rows-1 (CPU gemmts/causal_mask/softmax/gemm,
  * cpu_llm.cpp:816-827).  q, out: [rows][q_heads*head_dim]. */

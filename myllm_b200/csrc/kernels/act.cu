@@ -162,6 +162,7 @@ CL_API const char* cl_status_string(int status) {
     case CL_ERR_UNSUPPORTED: return "unsupported type or shape";
     case CL_ERR_CUDA: return "CUDA launch failed";
     case CL_ERR_WORKSPACE: return "workspace missing or too small";
+    case CL_ERR_LIMIT: return "request exceeds the fixed no-allocation scratch size";
     default: return "unknown status";
     }
 }

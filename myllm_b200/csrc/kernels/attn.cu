@@ -16,6 +16,8 @@
 #include "common.cuh"
 #include "launch.cuh"
 
+#include <mutex>
+
 namespace cl {
 
 constexpr int kKeysPerSplit = 64;   // decode split size (keys)
@@ -322,3 +324,62 @@ CL_API int cl_attn_prefill(const float* q, const float* k_cache, const float* v_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode attention without a caller workspace.
+//
+// Some callers cannot allocate device memory at the moment they run decode
+// attention: host code inside a CUDA stream capture in a mode where
+// cudaMalloc is refused, runtimes that hand out a fixed device-memory budget
+// at start-up and forbid later allocations, latency-critical loops where the
+// implicit device synchronisation of cudaMalloc/cudaFree is unacceptable, and
+// foreign-language bindings that have no way to own or free CUDA buffers.
+// This variant keeps the per-split softmax partials in a fixed array that
+// is part of the library image instead: every GPU that loads the library
+// holds kAttnNoAllocScratchBytes for it until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kAttnNoAllocScratchBytes = 2u << 20;  // 2 MiB per GPU
+constexpr int kMaxDevicesTracked = 64;
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kAttnNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevicesTracked] = {};
+
+// Device address of the array on the current device.  The symbol name is a
+// host-side stand-in, so the address is looked up once per device (with
+// that device current) and cached; the lookup itself allocates nothing.
+int noalloc_scratch(void** ptr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CL_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevicesTracked) return CL_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_attn_noalloc_scratch) != cudaSuccess || p == nullptr) return CL_ERR_CUDA;
+        g_noalloc_ptr[dev] = p;
+    }
+    *ptr = g_noalloc_ptr[dev];
+    return CL_OK;
+}
+
+}  // namespace
+
+extern "C" CL_API size_t cl_attn_decode_noalloc_limit_bytes(void) { return kAttnNoAllocScratchBytes; }
+
+extern "C" CL_API int cl_attn_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,
+                                             const int* len_dev, int max_len, int q_heads, int kv_heads,
+                                             int head_dim, float scale, float* out, cudaStream_t stream) {
+    const size_t need = cl_attn_decode_workspace_bytes(q_heads, head_dim, max_len);
+    if (need == 0) return CL_ERR_INVALID;
+    if (need > kAttnNoAllocScratchBytes) return CL_ERR_LIMIT;
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != CL_OK) return rc;
+    // Nothing in the array has to start at zero: the split kernel writes
+    // every partial that the combine kernel reads in the same call.
+    return cl_attn_decode(q, k_cache, v_cache, len_dev, max_len, q_heads, kv_heads, head_dim, scale, out, nullptr,
+                          scratch, kAttnNoAllocScratchBytes, stream);
+}
