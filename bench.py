@@ -284,7 +284,11 @@ def bench_cuda(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
-    launches_per_step = 1 + 7 * spec.layers + 3
+    # embed; per layer: QKV GEMV (one launch per run of equal formats), rope,
+    # attention split + combine, o, gate/up, down; final head GEMV, argmax, counter
+    qkv = sum(1 + (spec.types(l, "attn_k") != spec.types(l, "attn_q")) +
+              (spec.types(l, "attn_v") != spec.types(l, "attn_k")) for l in range(spec.layers))
+    launches_per_step = 1 + qkv + 6 * spec.layers + 3
     line = {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),
