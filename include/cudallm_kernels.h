@@ -96,14 +96,30 @@ CL_API int cl_gemv_multi(const cl_gemv_segment* segs, int nseg, int k, const flo
 CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n, int k,
                           const float* x, const float* norm_gamma, float eps, float* y, cudaStream_t stream);
 /* Device error word of the pipelined kernels: non-zero when a bounded wait
- * gave up (never expected).  Synchronous; clear != 0 resets it. */
+ * gave up (never expected): 1-3 from the GEMV, 16 + 1..3 from the
+ * tensor-core GEMM.  Synchronous; clear != 0 resets it. */
 CL_API int cl_device_error(int* code, int clear);
 
 /* ---- prefill GEMM (metal_gemm_*_f32, metal_llm.metal:621-704; CPU gemmtb
  * cpu_llm.cpp:631-653) ----------------------------------------------------
- * Y[m,n] = X[m,k] W[n,k]^T (+ bias[n]) (+ R[m,n]); X, Y, R row-major FP32. */
+ * Y[m,n] = X[m,k] W[n,k]^T (+ bias[n]) (+ R[m,n]); X, Y, R row-major FP32.
+ * R may alias Y.  The reference computes in FP32; cl_gemm keeps FP32-grade
+ * results: tensor cores with split-TF32 operands (CL_GEMM_TF32X3) when
+ * k % 32 == 0 and X, W, stride are 16-byte aligned, else the FP32 CUDA-core
+ * kernel. */
 CL_API int cl_gemm(int type, const void* w, long long stride, int n, int k, const float* x, int m,
                    const float* bias, const float* residual, float* y, cudaStream_t stream);
+enum {
+    CL_GEMM_TF32X3 = 0, /* operands split hi + lo TF32, 3 MMAs: FP32-grade (k % 32 == 0) */
+    CL_GEMM_F16 = 1     /* operands rounded to FP16, 1 MMA: 11-bit significands (k % 64 == 0) */
+};
+/* The tcgen05 path with an explicit precision; CL_ERR_UNSUPPORTED for shapes
+ * it does not take. */
+CL_API int cl_gemm_tc(int type, const void* w, long long stride, int n, int k, const float* x, int m,
+                      const float* bias, const float* residual, float* y, int precision, cudaStream_t stream);
+/* The FP32 CUDA-core path (exact reference weights, FMA accumulation). */
+CL_API int cl_gemm_simt(int type, const void* w, long long stride, int n, int k, const float* x, int m,
+                        const float* bias, const float* residual, float* y, cudaStream_t stream);
 
 /* ---- activations ------------------------------------------------------ */
 /* Row RMSNorm (cpu_llm.cpp:143-166, metal_rmsnorm_f32 metal_llm.metal:785):

@@ -36,6 +36,8 @@ SIGNATURES = {
     "cl_gemv_swiglu": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
     "cl_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "cl_gemm": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gemm_simt": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gemm_tc": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_vp]),
     "cl_rmsnorm": (c_int, [c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp]),
     "cl_embed": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
     "cl_rope_kv": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int,

@@ -309,6 +309,18 @@ struct CudaLLM::Impl {
             const long v = std::strtol(e, nullptr, 10);
             if (v > 0) prefill_chunk = std::min<std::size_t>(max_seq, (std::size_t)v);
         }
+        // Prefill GEMM precision: "tf32x3" (default, FP32-grade, as the
+        // reference's FP32 GEMM), "f16" (one FP16 tensor-core pass) or "simt"
+        // (FP32 CUDA cores).
+        if (const char* e = std::getenv("CUDALLM_PREFILL_GEMM")) {
+            const std::string v(e);
+            if (v == "f16")
+                gemm_path = GemmPath::F16;
+            else if (v == "simt")
+                gemm_path = GemmPath::Simt;
+            else if (v != "tf32x3" && !v.empty())
+                throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be tf32x3, f16 or simt");
+        }
         plan_shards();
 
         if (par.world > 1) {
@@ -428,6 +440,28 @@ struct CudaLLM::Impl {
         CUDALLM_CUDA(e);
     }
 
+    enum class GemmPath { Auto, F16, Simt };
+    GemmPath gemm_path = GemmPath::Auto;
+
+    // Y[m, W.rows] = X[m, k] W^T (+ bias) (+ residual) on the selected path.
+    void gemm(const DevMat& Wm, int n, int k, const float* x, int m, const float* bias, const float* res, float* y) {
+        switch (gemm_path) {
+        case GemmPath::F16: {
+            const int rc = cl_gemm_tc(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, CL_GEMM_F16, stream);
+            if (rc != CL_ERR_UNSUPPORTED) {
+                CUDALLM_CL(rc);
+                return;
+            }
+            break;  // shapes the FP16 path does not take use the default path
+        }
+        case GemmPath::Simt:
+            CUDALLM_CL(cl_gemm_simt(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, stream));
+            return;
+        case GemmPath::Auto: break;
+        }
+        CUDALLM_CL(cl_gemm(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, stream));
+    }
+
     // Rows [0, m) of X hold the chunk at positions pos0..pos0+m-1.
     void prefill_chunk_layers(int m, int pos0) {
         cudaStream_t s = stream;
@@ -437,9 +471,9 @@ struct CudaLLM::Impl {
         const std::size_t qd_l = hq_l * d;
         for (Layer& L : layers) {
             CUDALLM_CL(cl_rmsnorm(X, L.attn_norm, m, (int)H, eps(), Xn, nullptr, s));
-            CUDALLM_CL(cl_gemm(L.q.type, L.q.ptr, L.q.stride, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q, s));
-            CUDALLM_CL(cl_gemm(L.k.type, L.k.ptr, L.k.stride, L.k.rows, (int)H, Xn, m, L.k_b, nullptr, K, s));
-            CUDALLM_CL(cl_gemm(L.v.type, L.v.ptr, L.v.stride, L.v.rows, (int)H, Xn, m, L.v_b, nullptr, Vv, s));
+            gemm(L.q, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q);
+            gemm(L.k, L.k.rows, (int)H, Xn, m, L.k_b, nullptr, K);
+            gemm(L.v, L.v.rows, (int)H, Xn, m, L.v_b, nullptr, Vv);
             CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
                                   pos0, L.k_cache, L.v_cache, s));
             CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
@@ -459,13 +493,13 @@ struct CudaLLM::Impl {
                 }
                 o_in = Xn;
             }
-            CUDALLM_CL(cl_gemm(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, m, nullptr, res, out, s));
+            gemm(L.o, (int)H, (int)o_kl, o_in, m, nullptr, res, out);
             if (W > 1) all_reduce(P, X, (std::size_t)m * H);
             CUDALLM_CL(cl_rmsnorm(X, L.ffn_norm, m, (int)H, eps(), Xn, nullptr, s));
-            CUDALLM_CL(cl_gemm(L.gate.type, L.gate.ptr, L.gate.stride, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G, s));
-            CUDALLM_CL(cl_gemm(L.up.type, L.up.ptr, L.up.stride, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U, s));
+            gemm(L.gate, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G);
+            gemm(L.up, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U);
             CUDALLM_CL(cl_swiglu(G, U, G, (long long)m * F_l, s));
-            CUDALLM_CL(cl_gemm(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, G, m, nullptr, res, out, s));
+            gemm(L.down, (int)H, (int)F_l, G, m, nullptr, res, out);
             if (W > 1) all_reduce(P, X, (std::size_t)m * H);
         }
     }

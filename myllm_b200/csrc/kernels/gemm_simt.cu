@@ -4,8 +4,8 @@
 // 621-704) and the CPU gemmtb/gemmt loops (cpu_llm.cpp:591-653).  Weight
 // tiles are dequantized into shared memory with the CPU decoder's exact FP32
 // element values, then multiplied in FP32 in k order, so the result differs
-// from the CPU only by FMA rounding.  Used for small token counts and for
-// shapes the tensor-core path does not take.
+// from the CPU only by FMA rounding.  cl_gemm uses it for shapes the
+// tensor-core path (gemm_tc.cu) does not take; cl_gemm_simt calls it directly.
 #include "common.cuh"
 #include "dequant.cuh"
 #include "launch.cuh"
@@ -17,7 +17,7 @@ constexpr int kBM = 64, kBN = 64, kBK = 32, kSimtThreads = 256;
 __global__ void __launch_bounds__(kSimtThreads)
 gemm_simt_kernel(int type, const uint8_t* __restrict__ w, long long stride, int n, int k,
                  const float* __restrict__ x, int m, const float* __restrict__ bias,
-                 const float* __restrict__ res, float* __restrict__ y) {
+                 const float* res, float* y) {
     grid_launch_dependents();
     grid_wait();
     __shared__ float Xs[kBK][kBM + 4];
@@ -79,10 +79,31 @@ int launch_gemm_simt(int type, const void* w, long long stride, int n, int k, co
 
 }  // namespace cl
 
+namespace cl {
+bool gemm_tc_supported(int type, int n, int k, int m, int precision);
+int launch_gemm_tc(int type, const void* w, long long stride, int n, int k, const float* x, int m, const float* bias,
+                   const float* residual, float* y, int precision, cudaStream_t stream);
+}  // namespace cl
+
+namespace {
+bool gemm_args_ok(int type, const void* w, long long stride, int n, int k, const float* x, int m, float* y) {
+    return w != nullptr && x != nullptr && y != nullptr && n > 0 && k > 0 && m > 0 &&
+           cl_native_row_bytes(type, k) >= 0 && stride >= cl_row_stride(type, k);
+}
+}  // namespace
+
+extern "C" CL_API int cl_gemm_simt(int type, const void* w, long long stride, int n, int k, const float* x, int m,
+                                   const float* bias, const float* residual, float* y, cudaStream_t stream) {
+    if (!gemm_args_ok(type, w, stride, n, k, x, m, y)) return CL_ERR_INVALID;
+    return cl::launch_gemm_simt(type, w, stride, n, k, x, m, bias, residual, y, stream);
+}
+
 extern "C" CL_API int cl_gemm(int type, const void* w, long long stride, int n, int k, const float* x, int m,
                               const float* bias, const float* residual, float* y, cudaStream_t stream) {
-    if (w == nullptr || x == nullptr || y == nullptr || n <= 0 || k <= 0 || m <= 0 ||
-        cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k))
-        return CL_ERR_INVALID;
+    if (!gemm_args_ok(type, w, stride, n, k, x, m, y)) return CL_ERR_INVALID;
+    const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+                         stride % 16 == 0;
+    if (aligned && cl::gemm_tc_supported(type, n, k, m, CL_GEMM_TF32X3))
+        return cl::launch_gemm_tc(type, w, stride, n, k, x, m, bias, residual, y, CL_GEMM_TF32X3, stream);
     return cl::launch_gemm_simt(type, w, stride, n, k, x, m, bias, residual, y, stream);
 }

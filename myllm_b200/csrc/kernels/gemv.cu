@@ -732,6 +732,10 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, co
 
 }  // namespace cl
 
+namespace cl {
+int gemm_tc_device_error(int* code, bool clear);  // gemm_tc.cu
+}  // namespace cl
+
 extern "C" {
 
 CL_API int cl_gemv(int type, const void* w, long long stride, int n, int k, const float* x, const float* bias,
@@ -755,7 +759,11 @@ CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long l
 
 CL_API int cl_device_error(int* code, int clear) {
     if (code == nullptr) return CL_ERR_INVALID;
-    if (cudaMemcpyFromSymbol(code, cl::g_gemv_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    int gemv = 0, gemm = 0;
+    if (cudaMemcpyFromSymbol(&gemv, cl::g_gemv_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    if (cl::gemm_tc_device_error(&gemm, clear != 0) != CL_OK) return CL_ERR_CUDA;
+    // GEMV codes are 1-3; tensor-core GEMM codes are reported as 16 + code.
+    *code = gemv != 0 ? gemv : (gemm != 0 ? 16 + gemm : 0);
     if (clear) {
         const int zero = 0;
         if (cudaMemcpyToSymbol(cl::g_gemv_error, &zero, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;

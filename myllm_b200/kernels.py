@@ -93,11 +93,24 @@ def device_error(clear: bool = True) -> int:
     return code.value
 
 
-def gemm(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None):
+GEMM_TF32X3, GEMM_F16 = 0, 1
+
+
+def gemm(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None, path="auto",
+         out=None):
+    """Y = X W^T (+bias) (+residual).  path: "auto" (cl_gemm), "simt", "tf32x3" or "f16"."""
     m = x.shape[0]
-    out = torch.empty((m, n), dtype=torch.float32, device=x.device)
-    check(_native.lib().cl_gemm(gtype, _p(w), w.stride(0), n, k, _p(x), m, _p(bias), _p(residual), _p(out),
-                                _stream()), "cl_gemm")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    lib = _native.lib()
+    args = (gtype, _p(w), w.stride(0), n, k, _p(x), m, _p(bias), _p(residual), _p(out))
+    if path == "auto":
+        check(lib.cl_gemm(*args, _stream()), "cl_gemm")
+    elif path == "simt":
+        check(lib.cl_gemm_simt(*args, _stream()), "cl_gemm_simt")
+    else:
+        prec = {"tf32x3": GEMM_TF32X3, "f16": GEMM_F16}[path]
+        check(lib.cl_gemm_tc(*args, prec, _stream()), "cl_gemm_tc")
     return out
 
 

@@ -50,6 +50,28 @@ def test_tiny_parity(tiny_models, seed, n):
     llm.close()
 
 
+@pytest.mark.parametrize("path_name", ["simt", "f16"])
+def test_prefill_gemm_paths(tiny_models, monkeypatch, path_name):
+    """The other prefill GEMM paths: the FP32 CUDA-core kernel keeps the
+    1e-4 bar; the single-pass FP16 tensor-core path keeps the spec's 1e-2."""
+    path, d = tiny_models[11]
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", path_name)
+    llm = CudaLLM(path, max_sequence=64)
+    tok = llm.prefill(d["prompt40"])
+    err = rel(llm.last_logits(), d["logits40"][0])
+    assert err <= (1e-4 if path_name == "simt" else 1e-2)
+    if path_name == "simt":
+        assert tok == d["tokens40"][0]
+    llm.close()
+
+
+def test_prefill_gemm_path_rejects_unknown(tiny_models, monkeypatch):
+    path, _ = tiny_models[7]
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", "int4")
+    with pytest.raises(InvalidArgument):
+        CudaLLM(path, max_sequence=16)
+
+
 def test_prefill_chunking_matches_single_pass(tiny_models, monkeypatch):
     """A prompt split into several prefill chunks (later chunks attend to the
     earlier ones through the KV cache) gives the one-shot result, and a
