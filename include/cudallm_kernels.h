@@ -195,6 +195,58 @@ CL_API int cl_argmax_merge(const float* records, int n, int32_t* token, cudaStre
  * captured decode graph). */
 CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
 
+/* ---- qwen35moe ---------------------------------------------------------- */
+/* y[n] = W[n,k] x for an FP32 row-major W (the router, DeltaNet alpha/beta
+ * and shared-expert gate products, encode_product on F32 tensors,
+ * moe_llm.mm:2642-2690, 2476-2490, 2820-2824); k % 4 == 0. */
+CL_API int cl_gemv_f32(const float* w, int n, int k, const float* x, float* y, cudaStream_t stream);
+/* Router: softmax over n_experts logits, top-k by strict '>' (lower expert
+ * id first on ties), the k probabilities renormalised to sum 1
+ * (metal_softmax_f32 + metal_topk_f32 + metal_topk_renorm_f32,
+ * metal_llm.metal:826-890, 1424-1474).  ids / weights: device [k], k <= 8. */
+CL_API int cl_moe_route(const float* logits, int n_experts, int k, int32_t* ids, float* weights,
+                        cudaStream_t stream);
+/* Routed expert product (metal_expert_gemm_{q4_k,q6_k}_f32, metal_llm.metal:
+ * 1476-1524): for route r < routes, expert e = ids[r] (device),
+ * y[r][i] = W_e[i] . x_r with x_r = x + r * x_stride (x_stride 0: one shared
+ * input).  w holds this rank's experts e % world == rank as consecutive
+ * [n, k] blocks (local index e / world); routes of other ranks are skipped.
+ * With w_up != NULL the SwiGLU silu(W_e[i] . x) * (U_e[i] . x) is stored. */
+CL_API int cl_moe_expert_gemv(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                              const float* x, int x_stride, const int32_t* ids, int routes, int rank, int world,
+                              float* y, cudaStream_t stream);
+/* out = residual + (sum_r weights[r] y[r] + sigmoid(*shared_logit) shared_y)
+ * over this rank's routes (metal_expert_weighted_reduce_f32 + row scale +
+ * residual, moe_llm.mm:2786-2843); residual and the shared pair may be NULL.
+ * out may alias residual. */
+CL_API int cl_moe_combine(const float* y, const int32_t* ids, const float* weights, int routes, int n, int rank,
+                          int world, const float* shared_y, const float* shared_logit, const float* residual,
+                          float* out, cudaStream_t stream);
+/* Gated DeltaNet, one token (moe_llm.mm:2436-2640): causal depthwise conv of
+ * qkv [(2 key_heads + value_heads) * head_dim] over the conv_kernel - 1
+ * history rows (hist, updated) with conv_w [channels][conv_kernel], SiLU,
+ * L2 norm of each q / k head (metal_llm.metal:1288-1420) -> act; and
+ * decay = exp(softplus(alpha + dt_bias) * a), beta = sigmoid(beta_raw). */
+CL_API int cl_gdn_prep(const float* qkv, const float* alpha, const float* beta_raw, const float* conv_w, float* hist,
+                       const float* dt_bias, const float* a, int key_heads, int value_heads, int head_dim,
+                       int conv_kernel, float eps, float* act, float* decay, float* beta, cudaStream_t stream);
+/* The delta-rule step per value head h (key head h % key_heads) on
+ * state [value_heads][head_dim][head_dim] (metal_gdn_recurrence_f32,
+ * metal_llm.metal:1366-1420), then RMSNorm(o; gamma) * silu(z); head_dim <= 128. */
+CL_API int cl_gdn_step(const float* act, const float* decay, const float* beta, const float* z, const float* gamma,
+                       float* state, int key_heads, int value_heads, int head_dim, float eps, float* out,
+                       cudaStream_t stream);
+/* Gated attention prologue (moe_llm.mm:2238-2363): split the packed
+ * [query, gate] heads of mixed, RMSNorm q and k per head, NeoX RoPE on the
+ * first rot_dim dims from cos_sin [positions][rot_dim/2][2] at *pos_dev, and
+ * append k / v to the caches at *pos_dev. */
+CL_API int cl_attn_gate_prep(const float* mixed, const float* k_raw, const float* v_raw, const float* q_norm,
+                             const float* k_norm, int q_heads, int kv_heads, int head_dim, int rot_dim,
+                             const float* cos_sin, const int* pos_dev, float eps, float* q_out, float* gate_out,
+                             float* k_cache, float* v_cache, cudaStream_t stream);
+/* out = a * sigmoid(g) (the attention output gate, moe_llm.mm:2420-2429). */
+CL_API int cl_mul_sigmoid(const float* a, const float* g, float* out, int n, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

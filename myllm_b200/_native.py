@@ -55,6 +55,17 @@ SIGNATURES = {
     "cl_argmax_ex": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_size, c_vp]),
     "cl_argmax_merge": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "cl_counter_add": (c_int, [c_vp, c_int, c_int, c_vp]),
+    "cl_gemv_f32": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_moe_route": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_moe_expert_gemv": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_int, c_int, c_int,
+                                   c_vp, c_vp]),
+    "cl_moe_combine": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gdn_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp,
+                            c_vp, c_vp, c_vp]),
+    "cl_gdn_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_vp, c_vp]),
+    "cl_attn_gate_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,
+                                  c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "cl_mul_sigmoid": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp]),
     # backend
     "cudallm_last_error": (c_char_p, []),
     "cudallm_nccl_unique_id": (c_int, [c_vp]),

@@ -172,3 +172,69 @@ def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(g)
     check(_native.lib().cl_swiglu(_p(g), _p(u), _p(out), g.numel(), _stream()), "cl_swiglu")
     return out
+
+
+# ---- qwen35moe -----------------------------------------------------------------
+def gemv_f32(w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    n, k = w.shape
+    y = torch.empty(n, dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_gemv_f32(_p(w), n, k, _p(x), _p(y), _stream()), "cl_gemv_f32")
+    return y
+
+
+def moe_route(logits: torch.Tensor, k: int):
+    ids = torch.empty(k, dtype=torch.int32, device=logits.device)
+    wts = torch.empty(k, dtype=torch.float32, device=logits.device)
+    check(_native.lib().cl_moe_route(_p(logits), logits.numel(), k, _p(ids), _p(wts), _stream()), "cl_moe_route")
+    return ids, wts
+
+
+def moe_expert_gemv(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, ids: torch.Tensor,
+                    x_stride: int = 0, w_up=None, rank: int = 0, world: int = 1, out=None):
+    routes = ids.numel()
+    y = out if out is not None else torch.zeros((routes, n), dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_moe_expert_gemv(gtype, _p(w), _p(w_up), w.stride(0), n, k, _p(x), x_stride, _p(ids),
+                                           routes, rank, world, _p(y), _stream()), "cl_moe_expert_gemv")
+    return y
+
+
+def moe_combine(y: torch.Tensor, ids, wts, shared_y=None, shared_logit=None, residual=None, rank=0, world=1):
+    routes, n = y.shape
+    out = torch.empty(n, dtype=torch.float32, device=y.device)
+    check(_native.lib().cl_moe_combine(_p(y), _p(ids), _p(wts), routes, n, rank, world, _p(shared_y),
+                                       _p(shared_logit), _p(residual), _p(out), _stream()), "cl_moe_combine")
+    return out
+
+
+def gdn_prep(qkv, alpha, beta_raw, conv_w, hist, dt_bias, a, key_heads, value_heads, head_dim, eps):
+    kc = conv_w.shape[1]
+    act = torch.empty_like(qkv)
+    decay = torch.empty(value_heads, dtype=torch.float32, device=qkv.device)
+    beta = torch.empty_like(decay)
+    check(_native.lib().cl_gdn_prep(_p(qkv), _p(alpha), _p(beta_raw), _p(conv_w), _p(hist), _p(dt_bias), _p(a),
+                                    key_heads, value_heads, head_dim, kc, eps, _p(act), _p(decay), _p(beta),
+                                    _stream()), "cl_gdn_prep")
+    return act, decay, beta
+
+
+def gdn_step(act, decay, beta, z, gamma, state, key_heads, value_heads, head_dim, eps):
+    out = torch.empty(value_heads * head_dim, dtype=torch.float32, device=act.device)
+    check(_native.lib().cl_gdn_step(_p(act), _p(decay), _p(beta), _p(z), _p(gamma), _p(state), key_heads,
+                                    value_heads, head_dim, eps, _p(out), _stream()), "cl_gdn_step")
+    return out
+
+
+def attn_gate_prep(mixed, k_raw, v_raw, q_norm, k_norm, hq, hkv, d, rot, cos_sin, pos: int, eps, k_cache, v_cache):
+    q = torch.empty(hq * d, dtype=torch.float32, device=mixed.device)
+    gate = torch.empty_like(q)
+    pos_dev = torch.tensor([pos], dtype=torch.int32, device=mixed.device)
+    check(_native.lib().cl_attn_gate_prep(_p(mixed), _p(k_raw), _p(v_raw), _p(q_norm), _p(k_norm), hq, hkv, d, rot,
+                                          _p(cos_sin), _p(pos_dev), eps, _p(q), _p(gate), _p(k_cache), _p(v_cache),
+                                          _stream()), "cl_attn_gate_prep")
+    return q, gate
+
+
+def mul_sigmoid(a, g):
+    out = torch.empty_like(a)
+    check(_native.lib().cl_mul_sigmoid(_p(a), _p(g), _p(out), a.numel(), _stream()), "cl_mul_sigmoid")
+    return out

@@ -350,3 +350,181 @@ def cached_qwen2(spec: Qwen2Spec, directory: str) -> str:
     if not os.path.exists(path):
         write_qwen2(spec, path)
     return path
+
+
+# ---------------------------------------------------------------------------
+# qwen35moe models (moe_model.cpp:84-247, metal_model.cpp:573-688)
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class MoeSpec:
+    name: str
+    hidden: int
+    layers: int
+    experts: int
+    experts_used: int
+    expert_ffn: int
+    shared_ffn: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    rot_dim: int
+    ssm_state: int        # DeltaNet head size
+    ssm_groups: int       # DeltaNet key heads
+    ssm_rank: int         # DeltaNet value heads
+    vocab: int
+    conv_kernel: int = 4
+    attn_interval: int = 4
+    context: int = 4096
+    rope_theta: float = 10000000.0
+    eps: float = 1e-6
+    seed: int = 1
+    weight_std: float = 0.02
+
+    @property
+    def ssm_inner(self) -> int:
+        return self.ssm_rank * self.ssm_state
+
+    @property
+    def qkv_width(self) -> int:
+        return 2 * self.ssm_groups * self.ssm_state + self.ssm_inner
+
+    def is_attention(self, layer: int) -> bool:
+        return (layer + 1) % self.attn_interval == 0
+
+
+def moe_a3b_types(layer: int, tensor: str) -> int:
+    """The real Qwen3.6-35B-A3B Q4_K_M recipe (per-tensor types listed in the
+    reference's compatibility notes), alternating where the real file mixes
+    two types over the layers."""
+    odd = layer % 2 == 1
+    return {
+        "attn_qkv": Q6_K, "attn_gate": Q4_K, "ssm_out": Q8_0 if odd else Q4_K,
+        "attn_q": Q6_K if odd else Q4_K, "attn_k": Q8_0, "attn_v": Q8_0, "attn_output": Q5_K,
+        "ffn_gate_exps": Q4_K, "ffn_up_exps": Q4_K, "ffn_down_exps": Q6_K if odd else Q4_K,
+        "ffn_gate_shexp": Q8_0 if odd else Q6_K, "ffn_up_shexp": Q8_0 if odd else Q6_K,
+        "ffn_down_shexp": Q8_0 if odd else Q6_K,
+    }[tensor]
+
+
+MOE_CONFIGS: Dict[str, MoeSpec] = {
+    # BASELINE config 4: Qwen3.6-35B-A3B architecture.
+    "qwen3.6-35b-a3b": MoeSpec("qwen3.6-35b-a3b", hidden=2048, layers=40, experts=256, experts_used=8,
+                               expert_ffn=512, shared_ffn=512, heads=16, kv_heads=2, head_dim=256,
+                               rot_dim=64, ssm_state=128, ssm_groups=16, ssm_rank=32, vocab=248320,
+                               seed=0x35A3B),
+}
+
+
+def tiny_moe_spec(seed: int = 5, layers: int = 8, experts: int = 16, used: int = 4) -> MoeSpec:
+    """Every qwen35moe operator at small sizes (K-quant rows stay 256-aligned)."""
+    return MoeSpec(f"tiny-moe-s{seed}", hidden=256, layers=layers, experts=experts, experts_used=used,
+                   expert_ffn=256, shared_ffn=256, heads=4, kv_heads=2, head_dim=64, rot_dim=32,
+                   ssm_state=64, ssm_groups=2, ssm_rank=4, vocab=1024, context=512, seed=seed)
+
+
+def moe_tensors(spec: MoeSpec) -> List[TensorSpec]:
+    H, V, E = spec.hidden, spec.vocab, spec.experts
+    std = spec.weight_std
+    out: List[TensorSpec] = []
+
+    def mat(name, gtype, rows, cols, s=std, depth=None):
+        key = stream_key(spec.seed, name)
+        dims = (cols, rows) if depth is None else (cols, rows, depth)
+        total_rows = rows * (depth or 1)
+        out.append(TensorSpec(name, gtype, dims,
+                              lambda g=gtype, r=total_rows, c=cols, k=key, s=s: fill(g, r, c, k, 0.0, s)))
+
+    def f32mat(name, rows, cols, s):
+        key = stream_key(spec.seed, name)
+        out.append(TensorSpec(name, F32, (cols, rows),
+                              lambda n=rows * cols, k=key, s=s: normal(n, k, 0.0, s).view(np.uint8)))
+
+    def vec(name, n, mean, s=std, transform=None):
+        key = stream_key(spec.seed, name)
+
+        def make(n=n, k=key, m=mean, s=s, tr=transform):
+            v = normal(n, k, m, s)
+            return (tr(v) if tr else v).astype(np.float32).view(np.uint8)
+        out.append(TensorSpec(name, F32, (n,), make))
+
+    router_std = 1.0 / float(np.sqrt(H))  # router logits ~ N(0, 1) after the norm
+    mat("token_embd.weight", Q4_K, V, H)
+    vec("output_norm.weight", H, 1.0)
+    mat("output.weight", Q6_K, V, H)
+    for l in range(spec.layers):
+        p = f"blk.{l}."
+        t = lambda name, l=l: moe_a3b_types(l, name)
+        vec(p + "attn_norm.weight", H, 1.0)
+        vec(p + "post_attention_norm.weight", H, 1.0)
+        if spec.is_attention(l):
+            qw = spec.heads * spec.head_dim
+            kvw = spec.kv_heads * spec.head_dim
+            mat(p + "attn_q.weight", t("attn_q"), 2 * qw, H)
+            mat(p + "attn_k.weight", t("attn_k"), kvw, H)
+            mat(p + "attn_v.weight", t("attn_v"), kvw, H)
+            vec(p + "attn_q_norm.weight", spec.head_dim, 1.0)
+            vec(p + "attn_k_norm.weight", spec.head_dim, 1.0)
+            mat(p + "attn_output.weight", t("attn_output"), H, qw)
+        else:
+            mat(p + "attn_qkv.weight", t("attn_qkv"), spec.qkv_width, H)
+            mat(p + "attn_gate.weight", t("attn_gate"), spec.ssm_inner, H)
+            f32mat(p + "ssm_alpha.weight", spec.ssm_rank, H, std)
+            f32mat(p + "ssm_beta.weight", spec.ssm_rank, H, std)
+            f32mat(p + "ssm_conv1d.weight", spec.qkv_width, spec.conv_kernel, 0.5)
+            vec(p + "ssm_dt.bias", spec.ssm_rank, 0.0, 0.1)
+            # real files store A = -exp(A_log): negative, so the decay stays below 1
+            vec(p + "ssm_a", spec.ssm_rank, 0.0, 0.5, transform=lambda v: -np.exp(v))
+            vec(p + "ssm_norm.weight", spec.ssm_state, 1.0)
+            mat(p + "ssm_out.weight", t("ssm_out"), H, spec.ssm_inner)
+        f32mat(p + "ffn_gate_inp.weight", E, H, router_std)
+        mat(p + "ffn_gate_exps.weight", t("ffn_gate_exps"), spec.expert_ffn, H, depth=E)
+        mat(p + "ffn_up_exps.weight", t("ffn_up_exps"), spec.expert_ffn, H, depth=E)
+        mat(p + "ffn_down_exps.weight", t("ffn_down_exps"), H, spec.expert_ffn, depth=E)
+        vec(p + "ffn_gate_inp_shexp.weight", H, 0.0, router_std)
+        mat(p + "ffn_gate_shexp.weight", t("ffn_gate_shexp"), spec.shared_ffn, H)
+        mat(p + "ffn_up_shexp.weight", t("ffn_up_shexp"), spec.shared_ffn, H)
+        mat(p + "ffn_down_shexp.weight", t("ffn_down_shexp"), H, spec.shared_ffn)
+    return out
+
+
+def moe_metadata(spec: MoeSpec) -> Dict[str, object]:
+    a = "qwen35moe."
+    return {
+        "general.architecture": "qwen35moe",
+        "general.name": spec.name,
+        a + "block_count": spec.layers,
+        a + "context_length": spec.context,
+        a + "embedding_length": spec.hidden,
+        a + "attention.head_count": spec.heads,
+        a + "attention.head_count_kv": spec.kv_heads,
+        a + "attention.key_length": spec.head_dim,
+        a + "attention.value_length": spec.head_dim,
+        a + "rope.dimension_count": spec.rot_dim,
+        a + "rope.freq_base": float(spec.rope_theta),
+        a + "attention.layer_norm_rms_epsilon": float(spec.eps),
+        a + "expert_count": spec.experts,
+        a + "expert_used_count": spec.experts_used,
+        a + "expert_feed_forward_length": spec.expert_ffn,
+        a + "expert_shared_feed_forward_length": spec.shared_ffn,
+        a + "full_attention_interval": spec.attn_interval,
+        a + "ssm.conv_kernel": spec.conv_kernel,
+        a + "ssm.state_size": spec.ssm_state,
+        a + "ssm.group_count": spec.ssm_groups,
+        a + "ssm.time_step_rank": spec.ssm_rank,
+        a + "ssm.inner_size": spec.ssm_inner,
+        "tokenizer.ggml.pre": "qwen35",
+        "tokenizer.ggml.tokens_count": spec.vocab,
+        "tokenizer.ggml.eos_token_id": spec.vocab - 1,
+    }
+
+
+def write_moe(spec: MoeSpec, path: str) -> str:
+    return write_gguf(path, moe_metadata(spec), moe_tensors(spec))
+
+
+def cached_moe(spec: MoeSpec, directory: str) -> str:
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{spec.name}.gguf")
+    if not os.path.exists(path):
+        write_moe(spec, path)
+    return path
