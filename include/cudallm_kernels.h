@@ -244,6 +244,8 @@ CL_API int cl_attn_gate_prep(const float* mixed, const float* k_raw, const float
                              const float* k_norm, int q_heads, int kv_heads, int head_dim, int rot_dim,
                              const float* cos_sin, const int* pos_dev, float eps, float* q_out, float* gate_out,
                              float* k_cache, float* v_cache, cudaStream_t stream);
+/* *out = ids[*index_dev] (the next prompt token inside a captured prefill step). */
+CL_API int cl_select_token(const int32_t* ids, const int* index_dev, int32_t* out, cudaStream_t stream);
 /* out = a * sigmoid(g) (the attention output gate, moe_llm.mm:2420-2429). */
 CL_API int cl_mul_sigmoid(const float* a, const float* g, float* out, int n, cudaStream_t stream);
 

@@ -66,6 +66,7 @@ SIGNATURES = {
     "cl_attn_gate_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,
                                   c_vp, c_vp, c_vp, c_vp, c_vp]),
     "cl_mul_sigmoid": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp]),
+    "cl_select_token": (c_int, [c_vp, c_vp, c_vp, c_vp]),
     # backend
     "cudallm_last_error": (c_char_p, []),
     "cudallm_nccl_unique_id": (c_int, [c_vp]),

@@ -1,4 +1,5 @@
-// cudallm_* C-ABI over cudallm::CudaLLM (see include/cudallm.h).
+// cudallm_* C-ABI over cudallm::CudaLLM (qwen2) and cudallm::CudaMoeLLM
+// (qwen35moe), chosen by the GGUF's general.architecture (see include/cudallm.h).
 #include "cudallm.h"
 
 #include <nccl.h>
@@ -8,9 +9,24 @@
 #include <string>
 
 #include "cuda_llm.h"
+#include "cuda_moe_llm.h"
+
+#include <memory>
 
 struct cudallm_model {
-    cudallm::CudaLLM llm;
+    std::unique_ptr<cudallm::CudaLLM> dense;
+    std::unique_ptr<cudallm::CudaMoeLLM> moe;
+
+    template <typename F>
+    auto with(F&& f) -> decltype(f(*dense)) {
+        if (moe) return f(*moe);
+        return f(*dense);
+    }
+    template <typename F>
+    auto with(F&& f) const -> decltype(f(*dense)) {
+        if (moe) return f(static_cast<const cudallm::CudaMoeLLM&>(*moe));
+        return f(static_cast<const cudallm::CudaLLM&>(*dense));
+    }
 };
 
 namespace {
@@ -72,7 +88,17 @@ CUDALLM_API int cudallm_create(const char* gguf_path, size_t max_sequence, int d
             need(nccl_id);
             std::memcpy(par.nccl_id.data(), nccl_id, 128);
         }
-        *out = new cudallm_model{cudallm::CudaLLM(gguf_path, max_sequence, device, par)};
+        auto* m = new cudallm_model{};
+        try {
+            if (cudallm::gguf_architecture(gguf_path) == "qwen35moe")
+                m->moe = std::make_unique<cudallm::CudaMoeLLM>(gguf_path, max_sequence, device, par);
+            else
+                m->dense = std::make_unique<cudallm::CudaLLM>(gguf_path, max_sequence, device, par);
+        } catch (...) {
+            delete m;
+            throw;
+        }
+        *out = m;
     });
 }
 
@@ -81,7 +107,7 @@ CUDALLM_API void cudallm_destroy(cudallm_model* m) { delete m; }
 CUDALLM_API int cudallm_reset(cudallm_model* m) {
     return guard([&] {
         need(m);
-        m->llm.reset();
+        m->with([](auto& b) { b.reset(); });
     });
 }
 
@@ -90,7 +116,7 @@ CUDALLM_API int cudallm_prefill(cudallm_model* m, const int32_t* ids, size_t n, 
         need(m);
         need(token);
         if (n > 0) need(ids);
-        *token = m->llm.prefill(std::vector<int32_t>(ids, ids + n));
+        *token = m->with([&](auto& b) { return b.prefill(std::vector<int32_t>(ids, ids + n)); });
     });
 }
 
@@ -98,7 +124,7 @@ CUDALLM_API int cudallm_decode(cudallm_model* m, int32_t id, int32_t* token) {
     return guard([&] {
         need(m);
         need(token);
-        *token = m->llm.decode(id);
+        *token = m->with([&](auto& b) { return b.decode(id); });
     });
 }
 
@@ -106,19 +132,25 @@ CUDALLM_API int cudallm_last_logits(cudallm_model* m, float* out, size_t n) {
     return guard([&] {
         need(m);
         need(out);
-        m->llm.last_logits(out, n);
+        m->with([&](auto& b) { b.last_logits(out, n); });
     });
 }
 
-CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m) { return m ? m->llm.last_call_ms() : 0.0f; }
-CUDALLM_API size_t cudallm_position(const cudallm_model* m) { return m ? m->llm.position() : 0; }
-CUDALLM_API size_t cudallm_max_sequence(const cudallm_model* m) { return m ? m->llm.max_sequence() : 0; }
+CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m) {
+    return m ? m->with([](const auto& b) { return b.last_call_ms(); }) : 0.0f;
+}
+CUDALLM_API size_t cudallm_position(const cudallm_model* m) {
+    return m ? m->with([](const auto& b) { return b.position(); }) : 0;
+}
+CUDALLM_API size_t cudallm_max_sequence(const cudallm_model* m) {
+    return m ? m->with([](const auto& b) { return b.max_sequence(); }) : 0;
+}
 
 CUDALLM_API int cudallm_config(const cudallm_model* m, long long* out, int n) {
     return guard([&] {
         need(m);
         need(out);
-        const cudallm::ModelConfig& c = m->llm.config();
+        const cudallm::ModelConfig& c = m->with([](const auto& b) -> const cudallm::ModelConfig& { return b.config(); });
         const long long v[] = {(long long)c.layer_count,          (long long)c.embedding_size,
                                (long long)c.feed_forward_size,    (long long)c.attention_head_count,
                                (long long)c.kv_head_count,        (long long)c.head_size,
@@ -131,7 +163,7 @@ CUDALLM_API int cudallm_memory_stats(const cudallm_model* m, uint64_t out[4]) {
     return guard([&] {
         need(m);
         need(out);
-        const cudallm::MemoryStats s = m->llm.memory_stats();
+        const cudallm::MemoryStats s = m->with([](const auto& b) { return b.memory_stats(); });
         out[0] = s.weight_bytes;
         out[1] = s.kv_cache_bytes;
         out[2] = s.recurrent_state_bytes;
@@ -143,14 +175,14 @@ CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path)
     return guard([&] {
         need(m);
         need(csv_path);
-        m->llm.enable_profiling(csv_path);
+        m->with([&](auto& b) { b.enable_profiling(csv_path); });
     });
 }
 
 CUDALLM_API int cudallm_disable_profiling(cudallm_model* m) {
     return guard([&] {
         need(m);
-        m->llm.disable_profiling();
+        m->with([](auto& b) { b.disable_profiling(); });
     });
 }
 
@@ -158,7 +190,7 @@ CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n)
     return guard([&] {
         need(m);
         need(buf);
-        const std::string& s = m->llm.device_name();
+        const std::string& s = m->with([](const auto& b) -> const std::string& { return b.device_name(); });
         if (n == 0) throw std::invalid_argument("empty name buffer");
         std::strncpy(buf, s.c_str(), n - 1);
         buf[n - 1] = 0;

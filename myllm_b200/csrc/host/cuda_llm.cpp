@@ -234,11 +234,22 @@ struct CudaLLM::Impl {
             L.k_b = wl.vector(p + "attn_k.bias", kvd, k0, k0 + kn);
             L.v = wl.matrix(p + "attn_v.weight", kvd, H, k0, k0 + kn);
             L.v_b = wl.vector(p + "attn_v.bias", kvd, k0, k0 + kn);
-            L.o = wl.matrix(p + "attn_output.weight", H, H, 0, H, o_k0, o_k0 + o_kl);
+            // a rank whose share of a row-split matrix is empty (fewer blocks
+            // than ranks) loads nothing and contributes zeros to the all-reduce
+            if (o_kl > 0)
+                L.o = wl.matrix(p + "attn_output.weight", H, H, 0, H, o_k0, o_k0 + o_kl);
+            else
+                file.mark_loaded(p + "attn_output.weight");
             L.ffn_norm = wl.vector(p + "ffn_norm.weight", H);
-            L.gate = wl.matrix(p + "ffn_gate.weight", F, H, ffn0, ffn0 + F_l);
-            L.up = wl.matrix(p + "ffn_up.weight", F, H, ffn0, ffn0 + F_l);
-            L.down = wl.matrix(p + "ffn_down.weight", H, F, 0, H, ffn0, ffn0 + F_l);
+            if (F_l > 0) {
+                L.gate = wl.matrix(p + "ffn_gate.weight", F, H, ffn0, ffn0 + F_l);
+                L.up = wl.matrix(p + "ffn_up.weight", F, H, ffn0, ffn0 + F_l);
+                L.down = wl.matrix(p + "ffn_down.weight", H, F, 0, H, ffn0, ffn0 + F_l);
+            } else {
+                file.mark_loaded(p + "ffn_gate.weight");
+                file.mark_loaded(p + "ffn_up.weight");
+                file.mark_loaded(p + "ffn_down.weight");
+            }
             if (L.gate.type != L.up.type) throw std::runtime_error("ffn_gate and ffn_up must share a type");
         }
         file.validate_all_loaded();
@@ -412,8 +423,16 @@ struct CudaLLM::Impl {
                 CUDALLM_NCCL(ncclAllGather(att, att_full, hq_l * d, ncclFloat32, comm, s));
                 o_in = att_full + o_k0;
             }
-            CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, nullptr, res, out, s));
+            if (o_kl > 0)
+                CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, nullptr, res, out, s));
+            else
+                CUDALLM_CUDA(cudaMemsetAsync(out, 0, H * sizeof(float), s));
             if (W > 1) all_reduce(part, h, H);
+            if (F_l == 0) {
+                CUDALLM_CUDA(cudaMemsetAsync(out, 0, H * sizeof(float), s));
+                if (W > 1) all_reduce(part, h, H);
+                continue;
+            }
             CUDALLM_CL(cl_gemv_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, h, L.ffn_norm,
                                       eps(), act, s));
             CUDALLM_CL(cl_gemv(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, act, nullptr, res, out, s));
@@ -493,9 +512,17 @@ struct CudaLLM::Impl {
                 }
                 o_in = Xn;
             }
-            gemm(L.o, (int)H, (int)o_kl, o_in, m, nullptr, res, out);
+            if (o_kl > 0)
+                gemm(L.o, (int)H, (int)o_kl, o_in, m, nullptr, res, out);
+            else
+                CUDALLM_CUDA(cudaMemsetAsync(out, 0, (std::size_t)m * H * sizeof(float), s));
             if (W > 1) all_reduce(P, X, (std::size_t)m * H);
             CUDALLM_CL(cl_rmsnorm(X, L.ffn_norm, m, (int)H, eps(), Xn, nullptr, s));
+            if (F_l == 0) {
+                CUDALLM_CUDA(cudaMemsetAsync(out, 0, (std::size_t)m * H * sizeof(float), s));
+                if (W > 1) all_reduce(P, X, (std::size_t)m * H);
+                continue;
+            }
             gemm(L.gate, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G);
             gemm(L.up, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U);
             CUDALLM_CL(cl_swiglu(G, U, G, (long long)m * F_l, s));

@@ -1,5 +1,7 @@
 #include "device.h"
 
+#include <set>
+
 #include <algorithm>
 #include <cstring>
 
@@ -123,13 +125,14 @@ DevMat WeightLoader::stacked(const std::vector<Part>& parts) {
     m.type = (int)first.type;
     m.cols = (int)parts[0].cols;
     std::size_t total_rows = 0;
+    std::set<std::string> names;  // several row ranges of one tensor (experts) are one load
     for (const Part& p : parts) {
         const TensorInfo& t = file_.require(p.name, p.rows, p.cols);
         if ((int)t.type != m.type || (int)p.cols != m.cols)
             throw std::runtime_error("stacked tensors differ in type or width: " + p.name);
         if (p.row_end > p.rows || p.row_begin > p.row_end) throw std::invalid_argument("bad row range for " + p.name);
         total_rows += p.row_end - p.row_begin;
-        file_.mark_loaded(p.name);
+        if (names.insert(p.name).second) file_.mark_loaded(p.name);
     }
     const long long stride = cl_row_stride(m.type, m.cols);
     if (stride < 0) throw std::runtime_error(std::string("unsupported matrix type ") + ggml_type_name(m.type));

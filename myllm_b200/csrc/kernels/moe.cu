@@ -519,3 +519,19 @@ CL_API int cl_mul_sigmoid(const float* a, const float* g, float* out, int n, cud
 }
 
 }  // extern "C"
+
+namespace cl {
+namespace moe {
+__global__ void select_token_kernel(const int32_t* __restrict__ ids, const int* __restrict__ index,
+                                    int32_t* __restrict__ out) {
+    grid_launch_dependents();
+    grid_wait();
+    out[0] = ids[*index];
+}
+}  // namespace moe
+}  // namespace cl
+
+extern "C" CL_API int cl_select_token(const int32_t* ids, const int* index_dev, int32_t* out, cudaStream_t stream) {
+    if (ids == nullptr || index_dev == nullptr || out == nullptr) return CL_ERR_INVALID;
+    return cl::moe::status(cl::launch_pdl(cl::moe::select_token_kernel, dim3(1), dim3(1), 0, stream, ids, index_dev, out));
+}

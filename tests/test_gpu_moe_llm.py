@@ -1,0 +1,116 @@
+"""qwen35moe end to end: CudaMoeLLM (through the same C-ABI / Python binding
+as CudaLLM) against the FP64 oracle (oracle/moe_fp64.py) on seeded tiny
+models.  The reference has no CPU qwen35moe path; the oracle restates its
+formulas (moe_llm.mm, metal_llm.metal) in float64.
+
+Tokens must be identical at every step; logits within 1e-2 max-abs relative
+(the north-star tolerance); the observed error is pinned tighter.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from myllm_b200 import CudaLLM, InvalidArgument, LengthError, OutOfRange
+from myllm_b200 import synth_gguf as sg
+from oracle.moe_fp64 import MoeFP64
+from ranks import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / np.abs(b).max())
+
+
+@pytest.fixture(scope="module")
+def tiny_moe(model_dir, cuda):
+    out = {}
+    for seed in (5, 9):
+        spec = sg.tiny_moe_spec(seed=seed)
+        out[seed] = (spec, sg.cached_moe(spec, model_dir))
+    return out
+
+
+@pytest.mark.parametrize("seed", [5, 9])
+def test_moe_parity_with_fp64_oracle(tiny_moe, seed):
+    spec, path = tiny_moe[seed]
+    prompt = sg.prompt_ids(spec.seed, 12, spec.vocab)
+    ref = MoeFP64(path, max_sequence=64)
+    llm = CudaLLM(path, max_sequence=64)
+    assert llm.config().layer_count == spec.layers
+    rt, rl = ref.prefill(prompt)
+    gt = llm.prefill(prompt)
+    steps = [(gt, rt, llm.last_logits(), rl)]
+    for _ in range(6):
+        rt2, rl2 = ref.decode(rt)
+        gt = llm.decode(gt)
+        rt = rt2
+        steps.append((gt, rt, llm.last_logits(), rl2))
+    for i, (g, r, gl, refl) in enumerate(steps):
+        assert g == r, f"step {i}: token {g} != {r} (oracle margin {ref.margin(refl):.4g})"
+        err = rel(gl, refl)
+        assert err <= 1e-2, f"step {i}"
+        assert err <= 1e-3, f"step {i}: {err:.3g}"
+    llm.close()
+
+
+def test_moe_reset_reproduces_and_state_is_cleared(tiny_moe):
+    spec, path = tiny_moe[5]
+    prompt = sg.prompt_ids(spec.seed, 10, spec.vocab)
+    llm = CudaLLM(path, max_sequence=32)
+    t1 = llm.prefill(prompt)
+    l1 = llm.last_logits()
+    d1 = llm.decode(t1)
+    llm.reset()
+    assert llm.position == 0
+    # the DeltaNet state and conv history are zeroed by reset: same result
+    assert llm.prefill(prompt) == t1
+    assert np.array_equal(llm.last_logits(), l1)
+    assert llm.decode(t1) == d1
+    m = llm.memory_stats()
+    assert m.recurrent_state_bytes > 0 and m.kv_cache_bytes > 0 and m.weight_bytes > 0
+    llm.close()
+
+
+def test_moe_protocol_errors(tiny_moe):
+    spec, path = tiny_moe[5]
+    llm = CudaLLM(path, max_sequence=8)
+    with pytest.raises(InvalidArgument):
+        llm.decode(1)
+    with pytest.raises(InvalidArgument):
+        llm.prefill([])
+    with pytest.raises(OutOfRange):
+        llm.prefill([spec.vocab])
+    with pytest.raises(LengthError):
+        llm.prefill(list(range(9)))
+    t = llm.prefill([1, 2, 3])
+    with pytest.raises(InvalidArgument):
+        llm.prefill([1])  # prefill without reset
+    for _ in range(5):
+        t = llm.decode(t)
+    with pytest.raises(LengthError):
+        llm.decode(t)
+    llm.close()
+
+
+@pytest.mark.skipif("torch.cuda.device_count() < 2")
+def test_moe_expert_parallel_two_gpus(tiny_moe):
+    """Expert parallel over 2 GPUs (expert e on rank e % 2, one all-reduce
+    per layer) gives the single-GPU result and the oracle's tokens."""
+    spec, path = tiny_moe[9]
+    prompt = sg.prompt_ids(spec.seed, 8, spec.vocab)
+    ref = MoeFP64(path, max_sequence=64)
+    rt, rl = ref.prefill(prompt)
+    rtoks, rlogits = [rt], [rl]
+    for _ in range(4):
+        rt, rl = ref.decode(rt)
+        rtoks.append(rt)
+        rlogits.append(rl)
+    got = run_ranks(2, path, prompt, 4)
+    for r in (0, 1):
+        toks, logits = got[r]
+        assert toks == rtoks, r
+        for i in range(len(toks)):
+            assert rel(logits[i], rlogits[i]) <= 1e-3, (r, i)
