@@ -149,7 +149,9 @@ CL_API int cl_add(const float* a, const float* b, float* out, long long n, cudaS
  * metal_llm.metal:995-1061; CPU gevmts/softmax/gevm cpu_llm.cpp:888-903).
  * Keys 0..len-1 with len = *len_dev (device int) so the call can be captured
  * once in a CUDA graph; max_len bounds len.  out is [q_heads*head_dim];
- * xq (optional) receives its XQ encoding. */
+ * xq (optional) receives its XQ encoding.  Two launches: key splits per KV
+ * head (the split length derived from *len_dev on the device), then a merge
+ * per query head; concurrent calls must not share a workspace. */
 CL_API size_t cl_attn_decode_workspace_bytes(int q_heads, int head_dim, int max_len);
 CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
                           int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out,

@@ -1,10 +1,10 @@
 // GQA attention over the FP32 KV cache.
 //
 // Decode: flash-decoding.  CTA (kv head, key split) scores the group's query
-// heads against <= kKeysPerSplit keys, keeps an unnormalised softmax partial
-// (max, sum, sum p*V) in the workspace; a combine kernel merges the splits,
-// normalises and emits the head outputs (and their XQ encoding for the
-// o_proj GEMV).  Reference: metal_kv_cache_qk/softmax/av (metal_llm.metal:
+// heads against its share of the live keys, keeps an unnormalised softmax
+// partial (max, sum, sum p*V) in the workspace; a combine kernel (CTA per
+// query head) merges the splits, normalises and emits the head outputs (and
+// optionally their XQ encoding).  Reference: metal_kv_cache_qk/softmax/av (metal_llm.metal:
 // 995-1061, 826-890) and cpu_decode_layer's gevmts/softmax/gevm
 // (cpu_llm.cpp:888-903): score = (q.k) * (1/sqrt(d)), head h uses KV head
 // h / (q_heads / kv_heads).
@@ -20,144 +20,214 @@
 
 namespace cl {
 
-constexpr int kKeysPerSplit = 64;   // decode split size (keys)
-constexpr int kDecThreads = 128;
+constexpr int kDecThreads = 256;
+constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kMaxGroup = 16;
 constexpr int kMaxHeadDim = 256;
+constexpr int kTileKeys = 64;         // keys staged per tile
+constexpr int kMaxSplits = 32;        // key splits per KV head
 
-__host__ __device__ inline int attn_splits(int max_len) { return (max_len + kKeysPerSplit - 1) / kKeysPerSplit; }
-
-// Dynamic smem: q [group][d] | tile [64][d + 4] (K, then V) | p [group][64] | stats [group][2]
-__host__ __device__ inline size_t attn_decode_smem(int group, int d) {
-    return sizeof(float) * ((size_t)group * d + (size_t)kKeysPerSplit * (d + 4) + (size_t)group * kKeysPerSplit +
-                            2 * group);
+// Splits for a KV capacity: 32 (to cover the GPU) unless fewer than 16 keys
+// each would remain.  The keys of a split are walked in 64-key tiles.
+__host__ __device__ inline int attn_splits(int max_len) {
+    return max(1, min(kMaxSplits, (max_len + 15) / 16));
 }
 
-// partial record per (q head, split): [m, l, o[d]] with o unnormalised
+CL_DEVINL void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+CL_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CL_DEVINL void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Butterfly sum of 8 values per lane: afterwards lane l holds the full sum
+// of value (l >> 2) & 7.
+CL_DEVINL float warp_sum8(float (&v)[8], int lane) {
+#pragma unroll
+    for (int step = 0, n = 8, bit = 16; step < 3; ++step, n >>= 1, bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j < n / 2) {
+                const float keep = upper ? v[j + n / 2] : v[j];
+                const float send = upper ? v[j] : v[j + n / 2];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+            }
+        }
+    }
+    float r = v[0];
+    r += __shfl_xor_sync(0xffffffffu, r, 2);
+    r += __shfl_xor_sync(0xffffffffu, r, 1);
+    return r;
+}
+
+// Dynamic smem: q [G][d] | K tile [64][d + 4] | V tile [64][d] | p [G][64] |
+//               PV partials [parts - 1][G][d] | running (m, l) [G][2] | rescale [G]
+__host__ __device__ inline size_t attn_decode_smem(int group, int d) {
+    const int parts = max(1, kDecThreads / d);
+    return sizeof(float) * ((size_t)group * d + (size_t)kTileKeys * (d + 4) + (size_t)kTileKeys * d +
+                            (size_t)group * kTileKeys + (size_t)(parts - 1) * group * d + 3 * group);
+}
+
+// One CTA per (KV head, key split).  The split length comes from the live
+// length (*len_dev), so a graph captured once spreads every step's keys over
+// all CTAs.  K and V tiles are staged with asynchronous copies (a tile's
+// loads all in flight at once; K rows padded by 16 bytes so that threads on
+// different keys hit different banks).  Scores: one thread per (key, head)
+// dot product; the per-head softmax statistics by one thread per head; an
+// online softmax carries (m, l, o) across tiles.  Each CTA leaves an
+// unnormalised partial [m, l, o[d]] per query head in the workspace.
 __global__ void __launch_bounds__(kDecThreads)
 attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                  const int* __restrict__ len_dev, int hq, int hkv, int d, float scale,
-                  float* __restrict__ part) {
+                  const int* __restrict__ len_dev, int hq, int hkv, int d, float scale, float* __restrict__ part) {
     grid_launch_dependents();
     grid_wait();
-    const int g = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
-    const int group = hq / hkv;
+    const int g = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+    const int G = hq / hkv;
     const int L = *len_dev;
-    const int k0 = split * kKeysPerSplit;
-    const int nk = min(kKeysPerSplit, L - k0);
-    const int rec = d + 2;
-    if (nk <= 0) return;  // the combine kernel only reads splits below ceil(L / 64)
+    const int S = (L + nsplit - 1) / nsplit;
+    const int k0 = split * S;
+    const int nk_all = max(0, min(S, L - k0));
+    const int rec = d + 2, kvd = hkv * d, d4 = d / 4, kld = d + 4;
+    const int tid = threadIdx.x;
     extern __shared__ __align__(16) float sm[];
-    float* qs = sm;                                    // [group][d]
-    float* tile = qs + group * d;                      // [64][d + 4]
-    float* ps = tile + kKeysPerSplit * (d + 4);        // [group][64]
-    float* st = ps + group * kKeysPerSplit;            // [group][2]
-    const int kvd = hkv * d, d4 = d / 4, ld = d + 4;
-    for (int i = threadIdx.x; i < group * d4; i += kDecThreads)
-        reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q + (size_t)g * group * d)[i];
-    // K tile, coalesced float4 rows into padded smem rows
-    for (int i = threadIdx.x; i < nk * d4; i += kDecThreads) {
-        const int t = i / d4, c = i % d4;
-        *reinterpret_cast<float4*>(tile + t * ld + 4 * c) =
-            reinterpret_cast<const float4*>(kc + (size_t)(k0 + t) * kvd + (size_t)g * d)[c];
+    const int parts = max(1, kDecThreads / d);
+    float* qs = sm;                        // [G][d]
+    float* ks = qs + G * d;                // [64][d + 4]
+    float* vs = ks + kTileKeys * kld;      // [64][d]
+    float* ps = vs + kTileKeys * d;        // [G][64]
+    float* pv = ps + G * kTileKeys;        // [parts - 1][G][d]
+    float* run = pv + (parts - 1) * G * d; // [G][2] running max / sum
+    float* fac = run + 2 * G;              // [G] rescale of the running (l, o)
+
+    const int dim = tid % d, pt = tid / d;
+    const bool active = pt < parts;  // d not dividing the CTA leaves a few threads idle
+    float acc[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+    if (tid < G) {
+        run[2 * tid] = -INFINITY;
+        run[2 * tid + 1] = 0.0f;
     }
-    __syncthreads();
-    // scores: thread t -> key t, all heads of the group (q reads broadcast)
-    if (threadIdx.x < nk) {
-        const int t = threadIdx.x;
-        float acc[kMaxGroup];
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-        for (int c = 0; c < d4; ++c) {
-            const float4 kv = *reinterpret_cast<const float4*>(tile + t * ld + 4 * c);
-#pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) {
-                if (h < group) {
-                    const float4 qv = reinterpret_cast<const float4*>(qs + h * d)[c];
-                    acc[h] += kv.x * qv.x;
-                    acc[h] += kv.y * qv.y;
-                    acc[h] += kv.z * qv.z;
-                    acc[h] += kv.w * qv.w;
-                }
+    for (int i = tid; i < G * d4; i += kDecThreads) cp_async16(qs + 4 * i, q + (size_t)g * G * d + 4 * i);
+    cp_async_commit();
+    for (int t0 = 0; t0 < nk_all; t0 += kTileKeys) {
+        const int nk = min(kTileKeys, nk_all - t0);
+        const size_t base = (size_t)(k0 + t0) * kvd + (size_t)g * d;
+        for (int i = tid; i < nk * d4; i += kDecThreads) {
+            const int t = i / d4, c = i - t * d4;
+            cp_async16(ks + t * kld + 4 * c, kc + base + (size_t)t * kvd + 4 * c);
+        }
+        cp_async_commit();
+        for (int i = tid; i < nk * d4; i += kDecThreads) {
+            const int t = i / d4, c = i - t * d4;
+            cp_async16(vs + t * d + 4 * c, vc + base + (size_t)t * kvd + 4 * c);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();  // q and K
+        __syncthreads();
+        // scores: thread per (key, head)
+        for (int pidx = tid; pidx < nk * G; pidx += kDecThreads) {
+            const int t = pidx / G, h = pidx - t * G;
+            const float4* kr = reinterpret_cast<const float4*>(ks + t * kld);
+            const float4* qr = reinterpret_cast<const float4*>(qs + h * d);
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 8
+            for (int c = 0; c < d4; ++c) {
+                const float4 kv = kr[c], qv = qr[c];
+                a0 += kv.x * qv.x;
+                a1 += kv.y * qv.y;
+                a2 += kv.z * qv.z;
+                a3 += kv.w * qv.w;
             }
+            ps[h * kTileKeys + t] = ((a0 + a1) + (a2 + a3)) * scale;
         }
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h)
-            if (h < group) ps[h * kKeysPerSplit + t] = acc[h] * scale;
-    }
-    __syncthreads();
-    // V tile into the same buffer; per-head max/exp-sum meanwhile
-    for (int i = threadIdx.x; i < nk * d4; i += kDecThreads) {
-        const int t = i / d4, c = i % d4;
-        *reinterpret_cast<float4*>(tile + t * ld + 4 * c) =
-            reinterpret_cast<const float4*>(vc + (size_t)(k0 + t) * kvd + (size_t)g * d)[c];
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int h = warp; h < group; h += kDecThreads / 32) {
-        float m = -INFINITY;
-        for (int t = lane; t < nk; t += 32) m = fmaxf(m, ps[h * kKeysPerSplit + t]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int t = lane; t < nk; t += 32) {
-            const float e = expf(ps[h * kKeysPerSplit + t] - m);
-            ps[h * kKeysPerSplit + t] = e;
-            l += e;
+        __syncthreads();
+        // online softmax statistics: one thread per head
+        if (tid < G) {
+            const int h = tid;
+            float m = -INFINITY;
+            for (int t = 0; t < nk; ++t) m = fmaxf(m, ps[h * kTileKeys + t]);
+            const float mo = run[2 * h], mn = fmaxf(mo, m);
+            float l = 0.0f;
+            for (int t = 0; t < nk; ++t) {
+                const float e = expf(ps[h * kTileKeys + t] - mn);
+                ps[h * kTileKeys + t] = e;
+                l += e;
+            }
+            const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+            fac[h] = f;
+            run[2 * h] = mn;
+            run[2 * h + 1] = run[2 * h + 1] * f + l;
         }
-        l = warp_sum(l);
-        if (lane == 0) {
-            st[2 * h] = m;
-            st[2 * h + 1] = l;
-        }
-    }
-    __syncthreads();
-    // p . V: thread -> output dims
-    for (int dim = threadIdx.x; dim < d; dim += kDecThreads) {
-        float acc[kMaxGroup];
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-        for (int t = 0; t < nk; ++t) {
-            const float vv = tile[t * ld + dim];
+        cp_async_wait<0>();  // V
+        __syncthreads();
+        if (active) {
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h)
-                if (h < group) acc[h] += ps[h * kKeysPerSplit + t] * vv;
+                if (h < G) acc[h] *= fac[h];
+            for (int t = pt; t < nk; t += parts) {
+                const float vv = vs[t * d + dim];
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h)
+                    if (h < G) acc[h] += ps[h * kTileKeys + t] * vv;
+            }
         }
+        __syncthreads();  // the tile buffers are refilled next
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // this split's partials: [m, l, o[d]] per head (m = -inf, l = 0, o = 0 when empty)
+    if (active && pt > 0) {
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) pv[((pt - 1) * G + h) * d + dim] = acc[h];
+    }
+    __syncthreads();
+    if (active && pt == 0) {
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
-            if (h < group) {
-                float* pr = part + ((size_t)(g * group + h) * splits + split) * rec;
-                pr[2 + dim] = acc[h];
+            if (h < G) {
+                float o = acc[h];
+                for (int r = 1; r < parts; ++r) o += pv[((r - 1) * G + h) * d + dim];
+                float* pr = part + ((size_t)(g * G + h) * nsplit + split) * rec;
+                pr[2 + dim] = o;
                 if (dim == 0) {
-                    pr[0] = st[2 * h];
-                    pr[1] = st[2 * h + 1];
+                    pr[0] = run[2 * h];
+                    pr[1] = run[2 * h + 1];
                 }
             }
         }
     }
 }
 
-__global__ void attn_decode_combine(const float* __restrict__ part, const int* __restrict__ len_dev, int splits,
-                                    int d, float* __restrict__ out, void* xq, int xq_k) {
+// Merge the splits of one query head: CTA per head, thread per dimension.
+// The split weights exp(m_s - m) / l come from one warp; the partial loads
+// are independent and unrolled, so they are all in flight together.
+__global__ void __launch_bounds__(kMaxHeadDim)
+attn_decode_combine(const float* __restrict__ part, int nsplit, int d, float* __restrict__ out, void* xq,
+                    int xq_k) {
     grid_launch_dependents();
     grid_wait();
-    const int h = blockIdx.x;
-    const int L = *len_dev;
-    const int used = min(splits, attn_splits(L));
-    const int rec = d + 2;
-    const float* pr = part + (size_t)h * splits * rec;
-    float m = -INFINITY;
-    for (int s = 0; s < used; ++s) m = fmaxf(m, pr[(size_t)s * rec]);
-    float l = 0.0f;
-    for (int s = 0; s < used; ++s) l += pr[(size_t)s * rec + 1] * expf(pr[(size_t)s * rec] - m);
-    const float inv = 1.0f / l;
-    XQMut q{};
-    if (xq) q = xq_mut(xq, xq_k);
-    for (int dim = threadIdx.x; dim < d; dim += blockDim.x) {
-        float o = 0.0f;
-        for (int s = 0; s < used; ++s) o += pr[(size_t)s * rec + 2 + dim] * expf(pr[(size_t)s * rec] - m);
-        o *= inv;
-        out[(size_t)h * d + dim] = o;
-        if (xq) xq_store_block_warp(q, (h * d + dim) / 32, o);
+    __shared__ float wsm[kMaxSplits];
+    const int h = blockIdx.x, tid = threadIdx.x, rec = d + 2;
+    const float* pr = part + (size_t)h * nsplit * rec;
+    if (tid < 32) {
+        const float ms = tid < nsplit ? pr[(size_t)tid * rec] : -INFINITY;
+        const float ls = tid < nsplit ? pr[(size_t)tid * rec + 1] : 0.0f;
+        const float m = warp_max(ms);
+        const float e = ls > 0.0f ? expf(ms - m) : 0.0f;
+        const float l = warp_sum(ls * e);
+        wsm[tid] = e / l;
     }
+    __syncthreads();
+    float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxSplits; ++s2)
+        if (s2 < nsplit) o4[s2 & 3] += pr[(size_t)s2 * rec + 2 + tid] * wsm[s2];
+    const float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    out[(size_t)h * d + tid] = o;
+    if (xq) xq_store_block_warp(xq_mut(xq, xq_k), (h * d + tid) / 32, o);
 }
 
 // ---- prefill -------------------------------------------------------------------
@@ -282,19 +352,22 @@ CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_c
     const int splits = attn_splits(max_len);
     float* part = static_cast<float*>(workspace);
     const size_t smem = attn_decode_smem(q_heads / kv_heads, head_dim);
-    static int configured_for = 0;
-    if ((int)smem > configured_for) {
-        if (cudaFuncSetAttribute(attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return CL_ERR_CUDA;
-        configured_for = (int)smem;
+    static std::mutex mu;
+    static int configured_for = 48 * 1024;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if ((int)smem > configured_for) {
+            if (cudaFuncSetAttribute(attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess)
+                return CL_ERR_CUDA;
+            configured_for = (int)smem;
+        }
     }
     if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), smem, stream, q, k_cache, v_cache,
                    len_dev, q_heads, kv_heads, head_dim, scale, part) != cudaSuccess)
         return CL_ERR_CUDA;
-    const int threads = head_dim < 1024 ? head_dim : 1024;
-    return launch_pdl(attn_decode_combine, dim3(q_heads), dim3(threads), 0, stream, part, len_dev, splits, head_dim,
-                      out, xq, q_heads * head_dim) == cudaSuccess
+    return launch_pdl(attn_decode_combine, dim3(q_heads), dim3(head_dim), 0, stream, part, splits, head_dim, out, xq,
+                      q_heads * head_dim) == cudaSuccess
                ? CL_OK
                : CL_ERR_CUDA;
 }

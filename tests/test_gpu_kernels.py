@@ -230,9 +230,11 @@ def attention_ref(q, kc, vc, hq, hkv, d, length):
     return out
 
 
-@pytest.mark.parametrize("hq,hkv,d,length", [(14, 2, 64, 17), (28, 4, 128, 600), (16, 2, 256, 300), (5, 1, 128, 1)])
-def test_attention_decode(cuda, hq, hkv, d, length):
-    cap = 1024
+@pytest.mark.parametrize("hq,hkv,d,length,cap", [(14, 2, 64, 17, 1024), (28, 4, 128, 600, 1024),
+                                                 (16, 2, 256, 300, 1024), (5, 1, 128, 1, 1024),
+                                                 (32, 2, 96, 77, 100), (28, 4, 128, 4096, 4096),
+                                                 (40, 8, 128, 5, 4096), (16, 2, 256, 2500, 4096)])
+def test_attention_decode(cuda, hq, hkv, d, length, cap):
     q = xvec(hq * d, seed=80)[0]
     kc = xvec(hkv * d, cap, seed=81)
     vc = xvec(hkv * d, cap, seed=82)
@@ -240,6 +242,29 @@ def test_attention_decode(cuda, hq, hkv, d, length):
     got = K.attn_decode(torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda(),
                         length, cap, hq, hkv, d, 1.0 / math.sqrt(d))
     assert rel_err(got.cpu().numpy(), ref) <= 1e-5
+
+
+def test_attention_decode_reuses_workspace(cuda):
+    """One workspace across calls of different lengths (as in a captured
+    decode graph replayed at growing positions)."""
+    import ctypes
+    from myllm_b200 import _native
+    lib = _native.lib()
+    hq, hkv, d, cap = 28, 4, 128, 2048
+    q = xvec(hq * d, seed=85)[0]
+    kc = xvec(hkv * d, cap, seed=86)
+    vc = xvec(hkv * d, cap, seed=87)
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, kc, vc))
+    wsb = int(lib.cl_attn_decode_workspace_bytes(hq, d, cap))
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    out = torch.empty(hq * d, device="cuda")
+    for length in (2048, 3, 555, 1, 1200):
+        ln = torch.tensor([length], dtype=torch.int32, device="cuda")
+        rc = lib.cl_attn_decode(K._p(qd), K._p(kd), K._p(vd), K._p(ln), cap, hq, hkv, d,
+                                ctypes.c_float(1.0 / math.sqrt(d)), K._p(out), None, K._p(ws), wsb, K._stream())
+        assert rc == 0
+        ref = attention_ref(q, kc, vc, hq, hkv, d, length)
+        assert rel_err(out.cpu().numpy(), ref) <= 1e-5, length
 
 
 @pytest.mark.parametrize("hq,hkv,d,pos0,rows", [(4, 2, 64, 0, 40), (28, 4, 128, 0, 70), (8, 8, 128, 33, 20)])
