@@ -129,6 +129,29 @@ def profile_traffic(kernel: str):
 
 
 # ---------------------------------------------------------------------------
+FUSED_PAIRS = {(12, 14), (6, 8)}  # GGML ids: (Q4_K, Q6_K), (Q5_0, Q8_0)
+
+
+def gemv_launches(types) -> int:
+    """Launches cl_gemv_multi makes for consecutive segments of these types:
+    runs of one format, or of a fused pair of formats, share a launch."""
+    n, i = 0, 0
+    while i < len(types):
+        j, other = i + 1, None
+        while j < len(types):
+            t = types[j]
+            if t == types[i] or t == other:
+                j += 1
+            elif other is None and (min(t, types[i]), max(t, types[i])) in FUSED_PAIRS:
+                other = t
+                j += 1
+            else:
+                break
+        n += 1
+        i = j
+    return n
+
+
 def decode_bytes_per_token(spec, position: int) -> int:
     """Algorithmic HBM bytes of one decode token at `position`: every weight
     matrix once (native GGML bytes), one embedding row, the norms and biases,
@@ -284,10 +307,10 @@ def bench_cuda(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
-    # embed; per layer: QKV GEMV (one launch per run of equal formats), rope,
-    # attention split + combine, o, gate/up, down; final head GEMV, argmax, counter
-    qkv = sum(1 + (spec.types(l, "attn_k") != spec.types(l, "attn_q")) +
-              (spec.types(l, "attn_v") != spec.types(l, "attn_k")) for l in range(spec.layers))
+    # embed; per layer: QKV GEMV (one launch per run of one format or of a
+    # fused format pair), rope, attention split + combine, o, gate/up, down;
+    # final head GEMV, argmax, counter
+    qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")]) for l in range(spec.layers))
     launches_per_step = 1 + qkv + 6 * spec.layers + 3
     line = {
         "metric": "batch-1 greedy decode tokens/s",

@@ -105,7 +105,13 @@ __host__ __device__ inline int smem_stage_offset(int groups, int stages, int vpw
 
 // Group g of CTA c processes tiles c*G + g, c*G + g + gridDim.x*G, ...; a
 // tile is RPG consecutive rows (and the same rows of `up` for SwiGLU).
-template <int F, int RPG, bool SWIGLU>
+__host__ __device__ constexpr int nb_of(int type, int units) {
+    return (type == CL_TYPE_Q8_0 || type == CL_TYPE_Q5_0) ? units : units / 8;
+}
+
+// F2 != F: a fused pair of formats (chosen per tile), e.g. Q4_K q/k with
+// Q6_K v in one launch.
+template <int F, int RPG, bool SWIGLU, int F2 = F>
 __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams p) {
     constexpr int NMAT = SWIGLU ? 2 : 1;
     constexpr int VPW = NMAT * RPG;  // partial sums per warp per tile
@@ -245,7 +251,6 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
             t = o[7]; xu.xs = __uint_as_float(t.x); xu.xsum = __uint_as_float(t.y);
         }
     }
-    const int nb = (F == CL_TYPE_Q8_0 || F == CL_TYPE_Q5_0) ? p.units : p.units / 8;
     uint64_t* full = bars + 2 * grp * NS;
     uint64_t* empty = full + NS;
     const uint8_t* ring = stage_base + (size_t)grp * NS * p.stage_bytes;
@@ -267,7 +272,11 @@ __global__ void __launch_bounds__(kMaxThreads) gemv_tma_kernel(const GemvParams 
             for (int j = 0; j < RPG; ++j) {
                 float a = 0.0f;
                 if (ok && active && j < ti.rows)
-                    a = Fmt<F>::template dot<SmemLd>(st + (size_t)(m * RPG + j) * sg.stride, u, nb, xu);
+                {
+                    const uint8_t* rw = st + (size_t)(m * RPG + j) * sg.stride;
+                    a = (F == F2 || sg.type == F) ? Fmt<F>::template dot<SmemLd>(rw, u, nb_of(F, p.units), xu)
+                                                  : Fmt<F2>::template dot<SmemLd>(rw, u, nb_of(F2, p.units), xu);
+                }
                 acc[m * RPG + j] = a;
             }
         }
@@ -326,10 +335,10 @@ constexpr int kStageTarget = 40 * 1024;
 constexpr int kSmemBudget = 190 * 1024;
 constexpr int kTargetWarps = 16;  // consumer warps per CTA to aim for
 
-template <int F, int RPG, bool SW>
+template <int F, int RPG, bool SW, int F2 = F>
 cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     constexpr int NMAT = SW ? 2 : 1;
-    auto kern = gemv_tma_kernel<F, RPG, SW>;
+    auto kern = gemv_tma_kernel<F, RPG, SW, F2>;
     const int threads = p.groups * p.group_warps * 32 + 32;
     const int smem = smem_stage_offset(p.groups, p.stages, NMAT * RPG, p.group_warps, p.k) +
                      p.groups * p.stages * p.stage_bytes;
@@ -362,13 +371,25 @@ cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     return launch_pdl(kern, dim3(grid), dim3(threads), smem, stream, p);
 }
 
-template <int F, bool SW>
+template <int F, bool SW, int F2 = F>
 cudaError_t launch_fmt(const GemvParams& p, int rpg, cudaStream_t stream) {
     switch (rpg) {
-    case 1: return launch_cfg<F, 1, SW>(p, stream);
-    case 2: return launch_cfg<F, 2, SW>(p, stream);
-    default: return launch_cfg<F, 4, SW>(p, stream);
+    case 1: return launch_cfg<F, 1, SW, F2>(p, stream);
+    case 2: return launch_cfg<F, 2, SW, F2>(p, stream);
+    default: return launch_cfg<F, 4, SW, F2>(p, stream);
     }
+}
+
+// Format pairs with a fused instance (the Q4_K_M attention projections: Q4_K
+// q/k with Q6_K v; small models' Q5_0 with Q8_0).
+bool pair_supported(int a, int b) {
+    return (a == CL_TYPE_Q4_K && b == CL_TYPE_Q6_K) || (a == CL_TYPE_Q5_0 && b == CL_TYPE_Q8_0);
+}
+
+cudaError_t launch_pair(int a, int b, const GemvParams& p, int rpg, cudaStream_t stream) {
+    if (a == CL_TYPE_Q4_K && b == CL_TYPE_Q6_K) return launch_fmt<CL_TYPE_Q4_K, false, CL_TYPE_Q6_K>(p, rpg, stream);
+    if (a == CL_TYPE_Q5_0 && b == CL_TYPE_Q8_0) return launch_fmt<CL_TYPE_Q5_0, false, CL_TYPE_Q8_0>(p, rpg, stream);
+    return cudaErrorInvalidValue;
 }
 
 template <bool SW>
@@ -426,8 +447,12 @@ int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* 
     p.nseg = nseg;
     p.k = k;
     p.tiles = tiles;
+    int ta = segs[0].type, tb = segs[0].type;
+    for (int i = 1; i < nseg; ++i)
+        if (segs[i].type != ta) tb = segs[i].type;
+    if (ta > tb) std::swap(ta, tb);
     const cudaError_t e = sw ? launch_type<true>(segs[0].type, p, rpg, stream)
-                             : launch_type<false>(segs[0].type, p, rpg, stream);
+                             : (ta == tb ? launch_type<false>(ta, p, rpg, stream) : launch_pair(ta, tb, p, rpg, stream));
     return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
 }
 
@@ -447,10 +472,22 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, co
             return CL_ERR_INVALID;
     }
     if (sw && reinterpret_cast<uintptr_t>(w_up) % 16 != 0) return CL_ERR_INVALID;
-    // Consecutive segments of one type share a launch.
+    // Consecutive segments of one type, or of a fused pair of types, share a launch.
     for (int i = 0; i < nseg;) {
-        int j = i + 1;
-        while (j < nseg && segs[j].type == segs[i].type) ++j;
+        int j = i + 1, other = -1;
+        while (j < nseg) {
+            const int t = segs[j].type;
+            if (t == segs[i].type || t == other) {
+                ++j;
+                continue;
+            }
+            if (other < 0 && !sw && pair_supported(std::min(t, segs[i].type), std::max(t, segs[i].type))) {
+                other = t;
+                ++j;
+                continue;
+            }
+            break;
+        }
         const int rc = launch_same_type(segs + i, j - i, k, x, gamma, eps, w_up, stream);
         if (rc != CL_OK) return rc;
         i = j;
