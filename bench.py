@@ -203,7 +203,9 @@ def time_gateup_kernel(spec, iters: int):
     ms = e0.elapsed_time(e1) / iters
     algo = 2 * F * sg.row_bytes(gtype, H) + 2 * 4 * H + 4 * F  # weights + x, gamma + y
     del copies
-    return {"kernel": "gemv_tma_kernel<8,true> (RMSNorm + gate/up GEMV + SwiGLU)", "shape": f"2x[{F},{H}] {sg.TYPE_NAMES[gtype]}",
+    name = ("gemv_mma_kernel<Q4_K,swiglu> (RMSNorm + gate/up GEMV on mma.sync + SwiGLU)" if gtype == sg.Q4_K
+            else "gemv_tma_kernel<swiglu> (RMSNorm + gate/up GEMV + SwiGLU)")
+    return {"kernel": name, "shape": f"2x[{F},{H}] {sg.TYPE_NAMES[gtype]}",
             "bytes_per_launch": algo, "avg_launch_us": ms * 1e3, "gbs": algo / (ms * 1e-3) / 1e9}
 
 
@@ -323,7 +325,7 @@ def bench_cuda(args):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "q4_k_m weights x fp32 activations (int8x3 limbs, fp32 accumulate)",
+        "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
         "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
         "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
                    "layers": spec.layers, "hidden": spec.hidden, "ffn": spec.ffn, "vocab": spec.vocab,

@@ -405,8 +405,22 @@ cudaError_t launch_type(int type, const GemvParams& p, int rpg, cudaStream_t str
 }
 
 // One launch over segments that share a type.
+int launch_gemv_mma(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
+                    const void* w_up, cudaStream_t stream);  // gemv_mma.cu
+int gemv_mma_device_error(int* code, bool clear);            // gemv_mma.cu
+
 int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
                      const void* w_up, cudaStream_t stream) {
+    // Segments of one K-quant type go to the tensor-core GEMV (gemv_mma.cu)
+    // when it takes the shape; fused format pairs and the other types run here.
+    {
+        bool one_type = true;
+        for (int i = 1; i < nseg; ++i) one_type = one_type && segs[i].type == segs[0].type;
+        if (one_type) {
+            const int rc = launch_gemv_mma(segs, nseg, k, x, gamma, eps, w_up, stream);
+            if (rc != CL_ERR_UNSUPPORTED) return rc;
+        }
+    }
     const bool sw = w_up != nullptr;
     const int nmat = sw ? 2 : 1;
     GemvParams p{};
@@ -524,11 +538,13 @@ CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long l
 
 CL_API int cl_device_error(int* code, int clear) {
     if (code == nullptr) return CL_ERR_INVALID;
-    int gemv = 0, gemm = 0;
+    int gemv = 0, gemm = 0, mma = 0;
     if (cudaMemcpyFromSymbol(&gemv, cl::g_gemv_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    if (cl::gemv_mma_device_error(&mma, clear != 0) != CL_OK) return CL_ERR_CUDA;
     if (cl::gemm_tc_device_error(&gemm, clear != 0) != CL_OK) return CL_ERR_CUDA;
-    // GEMV codes are 1-3; tensor-core GEMM codes are reported as 16 + code.
-    *code = gemv != 0 ? gemv : (gemm != 0 ? 16 + gemm : 0);
+    // GEMV codes are 1-5 (4-5: tensor-core GEMV); tensor-core GEMM codes are
+    // reported as 16 + code.
+    *code = gemv != 0 ? gemv : (mma != 0 ? mma : (gemm != 0 ? 16 + gemm : 0));
     if (clear) {
         const int zero = 0;
         if (cudaMemcpyToSymbol(cl::g_gemv_error, &zero, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;

@@ -1,0 +1,624 @@
+// Decode GEMV over native K-quant blocks with the integer dot products on the
+// tensor cores: y[n] = W[n, k] . x (+ bias) (+ residual), optionally with the
+// input RMS-normalised first and a fused SwiGLU over (gate, up) row pairs.
+//
+// Reference: metal_gevm_q4_k_f32 / metal_gevm_q6_k_f32 (metal_llm.metal:708-781)
+// and the CPU oracle gevmt over GgufDequantizer rows (cpu_llm.cpp:512-547,
+// model.cpp:581-683).  Same products, different order: the factored form
+// d*sc*sum(q*x) - dmin*m*sum(x) (metal_llm.metal:392-393), with sum(q*x)
+// exact in integers and only the per-super-block sums scaled in FP32.
+//
+// Why the tensor cores at batch 1 (measured on B200): the per-row dp4a form
+// needs ~24 dp4a + masks + scale decode per row and 32 columns, i.e. more
+// issue slots per HBM byte than a B200 SM has at 6.5 TB/s.  Here one
+// mma.sync.m16n8k32 (u8 weights x s8 activations, s32 accumulate) replaces
+// 16 rows x 32 columns x 4 limbs of dp4a work.
+//
+// Activation encoding (XQ4, built in shared memory by every CTA): per
+// 256-element block b a scale s_b = max|x| / 127 and four signed 8-bit limbs
+//     x = s_b * (l0 + l1 / 2^7 + l2 / 2^14 + l3 / 2^21),
+// absolute error below max|x_b| * 2^-29.  Limbs are the MMA's N columns.
+//
+// Q4_K MMA layout.  A 64-element group of a super-block is 32 bytes whose low
+// nibbles are unit 2gi (32 elements) and high nibbles unit 2gi + 1.  One MMA
+// takes 16 bytes of the group for 16 rows: K slots 0-15 = the bytes' low
+// nibbles, K slots 16-31 = their high nibbles, kept in place (16 q) so one
+// AND extracts each.  B columns 0-3 = limbs of the low unit (zero on slots
+// 16-31), columns 4-7 = limbs of the high unit (zero on slots 0-15).  Two
+// MMAs (bytes 8t..8t+3 and 8t+4..8t+7 of lane quad t) chain into one
+// accumulator, so lane (g, t) ends a group holding, for rows g and g+8, the
+// sums of one unit (low if t < 2) for limbs 2(t&1), 2(t&1)+1; it scales them
+// by that unit's 6-bit sc with integer multiply-adds over the super-block
+// (|acc| < 2^28) and converts to FP32 once per super-block.
+//
+// Kernel shape: persistent CTAs, one producer warp + 16 consumer warps.  The
+// producer streams 16-row tiles (a K-chunk of each row per stage) into a
+// shared-memory ring with cp.async.bulk (mbarrier completion, bounded waits);
+// consumer warps take the stage's super-blocks round-robin, and the warps'
+// partial rows are summed in shared memory at the end of each tile.  Weights
+// are immutable, so the producer starts before the programmatic-dependent-
+// launch wait; consumers wait before reading x.
+#include "common.cuh"
+#include "launch.cuh"
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+namespace cl {
+
+// Device-side error word: 4 = producer wait gave up, 5 = consumer wait gave up
+// (never expected; reported through cl_device_error).
+__device__ int g_gemv_mma_error = 0;
+
+namespace gmma {
+
+constexpr int kRows = 16;   // rows per tile (M of the MMA)
+constexpr int kWarps = 16;  // consumer warps per CTA
+constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kMaxSegs = 4;
+constexpr int kZeroBytes = 1024;
+constexpr int kMaxBlocksPerWarp = 6;  // x blocks a consumer warp holds: k <= 16 * 6 * 256
+
+struct Seg {
+    const uint8_t* w;
+    const uint8_t* w_up;  // SwiGLU: up rows (same type/stride as w)
+    long long stride;
+    const float* bias;
+    const float* residual;
+    float* y;
+    int type;
+    int n;
+    int tile_begin;
+};
+
+// Stage geometry of one weight format in this launch.
+struct Geo {
+    int bb;      // bytes of one super-block in the device layout
+    int c;       // super-blocks per chunk (one stage holds one chunk of 16 rows)
+    int chunks;  // chunks per row
+    int rs;      // shared-memory row stride of a stage
+    int db;      // Q6_K: bytes of the row's scale array copied with every chunk
+};
+
+struct Params {
+    Seg seg[kMaxSegs];
+    Geo geo[2];  // [0]: format F, [1]: format F2
+    const float* x;
+    const float* gamma;  // RMSNorm weight applied to x first (cpu_llm.cpp:143-166), or null
+    float eps;
+    int nseg, k, nb, tiles, stages, stage_bytes;
+    int off_xs, off_xsum, off_xq, off_stage;  // shared-memory offsets
+};
+
+// Fixed part of the shared-memory layout: barriers (16 B per stage), abort
+// flag, RMSNorm partials, tile tickets and partial rows for R = NS + 1 tiles
+// in flight (a warp runs at most NS stages, hence NS tiles, ahead of the
+// slowest), and a zero block.
+__host__ __device__ constexpr int off_abort(int ns) { return 16 * ns; }
+__host__ __device__ constexpr int off_segs(int ns) { return 16 * ns + 16; }
+__host__ __device__ constexpr int off_dred(int ns) { return 16 * ns + 16 + kMaxSegs * (int)sizeof(Seg); }
+__host__ __device__ constexpr int off_ticket(int ns) { return off_dred(ns) + 256; }
+__host__ __device__ constexpr int off_red(int ns) { return (off_ticket(ns) + 4 * (ns + 1) + 15) & ~15; }
+__host__ __device__ constexpr int red_floats(int nmat) { return kWarps * kRows * nmat; }
+__host__ __device__ constexpr int off_zero(int ns, int nmat) { return off_red(ns) + 4 * (ns + 1) * red_floats(nmat); }
+__host__ __device__ constexpr int fixed_bytes(int ns, int nmat) { return off_zero(ns, nmat) + kZeroBytes; }
+
+struct TileInfo {
+    int seg, row0, rows;
+};
+
+// The segment table is copied to shared memory once per CTA: reading the
+// kernel-parameter copy with a runtime index costs an indexed constant-cache
+// load per field, which showed up as long-latency stalls in the stage loops.
+CL_DEVINL TileInfo tile_of(const Seg* segs, int nseg, int t) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxSegs; ++i)
+        if (i < nseg && t >= segs[i].tile_begin) s = i;
+    const int row0 = (t - segs[s].tile_begin) * kRows;
+    return TileInfo{s, row0, min(kRows, segs[s].n - row0)};
+}
+
+// m16n8k32 u8 x s8 -> s32: D = A B + C.
+CL_DEVINL void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                        uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+CL_DEVINL void mma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                          uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Per-lane constants of the Q4_K consumer.
+struct Q4Lane {
+    uint32_t sh;     // 12 * h: header shift that puts unit (2gi + h)'s slot at a fixed bit
+    float lw0, lw1;  // weights of the lane's two limb columns (1/16 for high-nibble units)
+    int pp;          // row of the min term: g (0) or g + 8 (1)
+};
+
+// Slot field of unit 2gi + h after the per-lane shift: sc at bit 32 + 24 gi,
+// m at bit 38 + 24 gi of the 128-bit header (w1..w3 = header words 1..3).
+template <int GI>
+CL_DEVINL int q4_sc(uint32_t w1, uint32_t w2, uint32_t w3) {
+    if (GI == 0) return (int)(w1 & 63u);
+    if (GI == 1) return (int)(__funnelshift_r(w1, w2, 24) & 63u);
+    if (GI == 2) return (int)((w2 >> 16) & 63u);
+    return (int)((w3 >> 8) & 63u);
+}
+template <int GI>
+CL_DEVINL float q4_m(uint32_t w1, uint32_t w2, uint32_t w3) {
+    if (GI == 0) return (float)((w1 >> 6) & 63u);
+    if (GI == 1) return (float)(__funnelshift_r(w1, w2, 30) & 63u);
+    if (GI == 2) return (float)((w2 >> 22) & 63u);
+    return (float)((w3 >> 14) & 63u);
+}
+
+// One Q4_K super-block of 16 rows.  bg/b8: the rows' block in shared memory;
+// bx0/bx1: the lane's B words for the four groups (low-unit and high-unit
+// columns, zero where the lane's column is the other unit); xsum4: sums of x
+// over the lane's four units; xs: the block's x scale.
+CL_DEVINL void q4k_sb(const uint8_t* bg, const uint8_t* b8, const uint2 (&bx0)[4], const uint2 (&bx1)[4],
+                      const float4& xsum4, float xs, int t, const Q4Lane& L, float& yg, float& y8, float& ym) {
+    const uint4 hg = *reinterpret_cast<const uint4*>(bg);
+    const uint4 h8 = *reinterpret_cast<const uint4*>(b8);
+    const uint32_t g1 = __funnelshift_r(hg.y, hg.z, L.sh), g2 = __funnelshift_r(hg.z, hg.w, L.sh), g3 = hg.w >> L.sh;
+    const uint32_t e1 = __funnelshift_r(h8.y, h8.z, L.sh), e2 = __funnelshift_r(h8.z, h8.w, L.sh), e3 = h8.w >> L.sh;
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+        const uint2 wg = *reinterpret_cast<const uint2*>(bg + 16 + 32 * gi + 8 * t);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(b8 + 16 + 32 * gi + 8 * t);
+        int c[4];
+        mma_u8s8_z(c, wg.x & 0x0f0f0f0fu, w8.x & 0x0f0f0f0fu, wg.x & 0xf0f0f0f0u, w8.x & 0xf0f0f0f0u, bx0[gi].x,
+                   bx1[gi].x);
+        mma_u8s8(c, wg.y & 0x0f0f0f0fu, w8.y & 0x0f0f0f0fu, wg.y & 0xf0f0f0f0u, w8.y & 0xf0f0f0f0u, bx0[gi].y,
+                 bx1[gi].y);
+        int sg, s8;
+        switch (gi) {
+            case 0: sg = q4_sc<0>(g1, g2, g3); s8 = q4_sc<0>(e1, e2, e3); break;
+            case 1: sg = q4_sc<1>(g1, g2, g3); s8 = q4_sc<1>(e1, e2, e3); break;
+            case 2: sg = q4_sc<2>(g1, g2, g3); s8 = q4_sc<2>(e1, e2, e3); break;
+            default: sg = q4_sc<3>(g1, g2, g3); s8 = q4_sc<3>(e1, e2, e3); break;
+        }
+        a0 += c[0] * sg;
+        a1 += c[1] * sg;
+        a2 += c[2] * s8;
+        a3 += c[3] * s8;
+    }
+    // min term of the lane's (row, unit kind): dmin * sum_u m_u * sum(x_u)
+    const uint32_t m1 = L.pp ? e1 : g1, m2 = L.pp ? e2 : g2, m3 = L.pp ? e3 : g3;
+    const float msum = fmaf(q4_m<0>(m1, m2, m3), xsum4.x,
+                            fmaf(q4_m<1>(m1, m2, m3), xsum4.y,
+                                 fmaf(q4_m<2>(m1, m2, m3), xsum4.z, q4_m<3>(m1, m2, m3) * xsum4.w)));
+    const float dmin = half_bits_to_float((L.pp ? h8.x : hg.x) >> 16);
+    ym = fmaf(-dmin, msum, ym);
+    const float vg = fmaf((float)a0, L.lw0, (float)a1 * L.lw1) * xs;
+    const float v8 = fmaf((float)a2, L.lw0, (float)a3 * L.lw1) * xs;
+    yg = fmaf(half_bits_to_float(hg.x), vg, yg);
+    y8 = fmaf(half_bits_to_float(h8.x), v8, y8);
+}
+
+// Encode one 256-element block (lane holds elements 8 lane .. 8 lane + 7)
+// into XQ4: xq[unit][limb][32] bytes, xs = s, xsum[h][gi] = sum of the
+// encoded x over unit 2 gi + h.
+CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* xs, float* xsum) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = warp_max(amax);
+    const float s = amax / 127.0f;
+    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    uint32_t w[4][2] = {};
+    int t0 = 0, t123 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float r0 = v[i] * inv;
+        const float l0 = fminf(fmaxf(rintf(r0), -127.0f), 127.0f);
+        const float r1 = (r0 - l0) * 128.0f;
+        const float l1 = fminf(fmaxf(rintf(r1), -64.0f), 64.0f);
+        const float r2 = (r1 - l1) * 128.0f;
+        const float l2 = fminf(fmaxf(rintf(r2), -64.0f), 64.0f);
+        const float r3 = (r2 - l2) * 128.0f;
+        const float l3 = fminf(fmaxf(rintf(r3), -64.0f), 64.0f);
+        const int i0 = (int)l0, i1 = (int)l1, i2 = (int)l2, i3 = (int)l3;
+        const int sh = 8 * (i & 3);
+        w[0][i >> 2] |= ((uint32_t)i0 & 0xffu) << sh;
+        w[1][i >> 2] |= ((uint32_t)i1 & 0xffu) << sh;
+        w[2][i >> 2] |= ((uint32_t)i2 & 0xffu) << sh;
+        w[3][i >> 2] |= ((uint32_t)i3 & 0xffu) << sh;
+        t0 += i0;
+        t123 += i1 * 16384 + i2 * 128 + i3;
+    }
+    const int unit = lane >> 2, e0 = (lane & 3) * 8;
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+        *reinterpret_cast<uint2*>(xq + unit * 128 + l * 32 + e0) = make_uint2(w[l][0], w[l][1]);
+    t0 += __shfl_xor_sync(0xffffffffu, t0, 1);
+    t123 += __shfl_xor_sync(0xffffffffu, t123, 1);
+    t0 += __shfl_xor_sync(0xffffffffu, t0, 2);
+    t123 += __shfl_xor_sync(0xffffffffu, t123, 2);
+    if ((lane & 3) == 0) {
+        // sum of x over the unit = s * 2^-21 * (2^21 sum l0 + sum(l1 2^14 + l2 2^7 + l3))
+        const int gi = unit >> 1, h = unit & 1;
+        xsum[h * 4 + gi] = fmaf((float)t0, 2097152.0f, (float)t123) * (s * (1.0f / 2097152.0f));
+    }
+    if (lane == 0) *xs = s;
+}
+
+template <int F, bool SW, int F2>
+__global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
+    constexpr int NMAT = SW ? 2 : 1;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int NS = p.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + NS;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + off_abort(NS));
+    Seg* segs = reinterpret_cast<Seg*>(smem + off_segs(NS));
+    double* dred = reinterpret_cast<double*>(smem + off_dred(NS));
+    int* tickets = reinterpret_cast<int*>(smem + off_ticket(NS));  // [NS + 1]
+    float* red = reinterpret_cast<float*>(smem + off_red(NS));      // [NS + 1][kWarps][NMAT * 16]
+    uint8_t* zero = smem + off_zero(NS, NMAT);
+    float* xs = reinterpret_cast<float*>(smem + p.off_xs);
+    float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // [nb][2][4]
+    uint8_t* xq = smem + p.off_xq;                              // [nb][8 units][4 limbs][32]
+    uint8_t* stages = smem + p.off_stage;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        for (int r = 0; r <= NS; ++r) tickets[r] = 0;
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (tid < kZeroBytes / 16) reinterpret_cast<uint4*>(zero)[tid] = make_uint4(0u, 0u, 0u, 0u);
+    if (tid < p.nseg) segs[tid] = p.seg[tid];
+    __syncthreads();
+    grid_launch_dependents();
+
+    if (warp == kWarps) {
+        // ---- producer: lane r (< 16 NMAT) copies row r of the tile's chunk ----
+        int s = 0;
+        uint32_t ph = 0;
+        for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+            const TileInfo ti = tile_of(segs, p.nseg, tile);
+            const Seg& sg = segs[ti.seg];
+            const Geo& ge = p.geo[(F == F2 || sg.type == F) ? 0 : 1];
+            for (int ch = 0; ch < ge.chunks; ++ch) {
+                // the whole warp waits: a wait by one elected lane while the
+                // others sit in __syncwarp() measured 2.5x slower hand-offs
+                int ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1u);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok && lane == 0) {
+                    if (!*abort_flag) {
+                        atomicExch(&g_gemv_mma_error, 4);
+                        *abort_flag = 1;
+                    }
+                }
+                if (ok) {
+                    const int sb0 = ch * ge.c, nsb = min(ge.c, p.nb - sb0);
+                    const uint32_t rb = (uint32_t)(nsb * ge.bb);
+                    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(NMAT * ti.rows) * (rb + ge.db));
+                    __syncwarp();
+                    if (lane < NMAT * kRows) {
+                        const int m = lane / kRows, r = lane % kRows;
+                        if (r < ti.rows) {
+                            const uint8_t* src = (m ? sg.w_up : sg.w) + (size_t)(ti.row0 + r) * sg.stride;
+                            uint8_t* dst = stages + (size_t)s * p.stage_bytes + (size_t)(m * kRows + r) * ge.rs;
+                            bulk_g2s(dst, src + (size_t)sb0 * ge.bb, rb, &full[s]);
+                            if (ge.db) bulk_g2s(dst + ge.c * ge.bb, src + (size_t)p.nb * ge.bb, ge.db, &full[s]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (++s == NS) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+        return;
+    }
+
+    // ---- consumers: x -> XQ4 in shared memory (RMS-normalised first if asked).
+    // Warp w takes blocks w, w + 16, ...; all of its x loads are issued at
+    // once and held in registers for both passes (one dependent load per
+    // block measured ~1 us each at K = 18944). ----
+    grid_wait();
+    const int nb = p.nb;
+    float xv[kMaxBlocksPerWarp][8];
+#pragma unroll
+    for (int i = 0; i < kMaxBlocksPerWarp; ++i) {
+        const int b = warp + i * kWarps;
+        if (b < nb) {
+            const float4* px = reinterpret_cast<const float4*>(p.x + b * 256 + lane * 8);
+            const float4 u0 = px[0], u1 = px[1];
+            xv[i][0] = u0.x; xv[i][1] = u0.y; xv[i][2] = u0.z; xv[i][3] = u0.w;
+            xv[i][4] = u1.x; xv[i][5] = u1.y; xv[i][6] = u1.z; xv[i][7] = u1.w;
+        }
+    }
+    float inv = 1.0f;
+    if (p.gamma) {
+        // cpu_llm.cpp:156-165: sum of squares in double, mean -> float,
+        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).  Every CTA
+        // reduces in the same order, so all CTAs see the same inv.
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < kMaxBlocksPerWarp; ++i)
+            if (warp + i * kWarps < nb) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += (double)xv[i][e] * (double)xv[i][e];
+            }
+        ss = warp_sum_d(ss);
+        if (lane == 0) dred[warp] = ss;
+        named_barrier(1, kWarps * 32);
+        double tot = 0.0;
+        for (int w = 0; w < kWarps; ++w) tot += dred[w];
+        inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxBlocksPerWarp; ++i) {
+        const int b = warp + i * kWarps;
+        if (b < nb) {
+            if (p.gamma) {
+                const float4* pg = reinterpret_cast<const float4*>(p.gamma + b * 256 + lane * 8);
+                const float4 q0 = pg[0], q1 = pg[1];
+                const float gm[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[i][e] = __fmul_rn(xv[i][e], __fmul_rn(inv, gm[e]));
+            }
+            encode_block(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8);
+        }
+    }
+    named_barrier(1, kWarps * 32);
+
+    // ---- main loop ----
+    const int g = lane >> 2, t = lane & 3, h = t >> 1;
+    Q4Lane L;
+    L.sh = 12u * (uint32_t)h;
+    L.lw0 = ((t & 1) ? (1.0f / 16384.0f) : 1.0f) * (h ? (1.0f / 16.0f) : 1.0f);
+    L.lw1 = L.lw0 * (1.0f / 128.0f);
+    L.pp = t & 1;
+    // B words: columns 0-3 (g < 4) read the low unit, columns 4-7 the high
+    // unit; the other half reads the zero block.
+    const uint8_t* xb0 = g < 4 ? xq + g * 32 + 8 * t : zero;
+    const uint8_t* xb1 = g >= 4 ? xq + 128 + (g - 4) * 32 + 8 * t : zero;
+    const int xinc0 = g < 4 ? 1024 : 0, xinc1 = g >= 4 ? 1024 : 0;
+
+    int s = 0, base = 0, slot = 0;
+    uint32_t ph = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+        const TileInfo ti = tile_of(segs, p.nseg, tile);
+        const Seg& sg = segs[ti.seg];
+        const Geo& ge = p.geo[(F == F2 || sg.type == F) ? 0 : 1];
+        float yg = 0.f, y8 = 0.f, ym = 0.f, ug = 0.f, u8 = 0.f, um = 0.f;
+        for (int ch = 0; ch < ge.chunks; ++ch) {
+            const int sb0 = ch * ge.c, nsb = min(ge.c, nb - sb0);
+            int ok = !*abort_flag && mbar_wait(&full[s], ph);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok && lane == 0) {
+                if (!*abort_flag) {
+                    atomicExch(&g_gemv_mma_error, 5);
+                    *abort_flag = 1;
+                }
+            }
+            if (ok) {
+                const uint8_t* st = stages + (size_t)s * p.stage_bytes;
+                int j = warp - base;
+                if (j < 0) j += kWarps;
+                for (; j < nsb; j += kWarps) {
+                    const int sb = sb0 + j;
+                    uint2 bx0[4], bx1[4];
+                    const uint8_t* p0 = xb0 + sb * xinc0;
+                    const uint8_t* p1 = xb1 + sb * xinc1;
+#pragma unroll
+                    for (int gi = 0; gi < 4; ++gi) {
+                        bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
+                        bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
+                    }
+                    const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
+                    const float xsb = xs[sb];
+                    const uint8_t* rg = st + (size_t)g * ge.rs + j * ge.bb;
+                    const uint8_t* r8 = rg + 8 * ge.rs;
+                    q4k_sb(rg, r8, bx0, bx1, xsum4, xsb, t, L, yg, y8, ym);
+                    if (SW) q4k_sb(rg + kRows * ge.rs, r8 + kRows * ge.rs, bx0, bx1, xsum4, xsb, t, L, ug, u8, um);
+                }
+            }
+            base += nsb;
+            base %= kWarps;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == NS) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        // ---- end of tile: quad sums, then warp 0 adds the warps' rows ----
+        if (L.pp) y8 += ym; else yg += ym;
+        yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+        yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+        y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+        y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+        if (SW) {
+            if (L.pp) u8 += um; else ug += um;
+            ug += __shfl_xor_sync(0xffffffffu, ug, 1);
+            ug += __shfl_xor_sync(0xffffffffu, ug, 2);
+            u8 += __shfl_xor_sync(0xffffffffu, u8, 1);
+            u8 += __shfl_xor_sync(0xffffffffu, u8, 2);
+        }
+        // publish this warp's rows; the last warp to finish the tile sums
+        // all warps' rows in warp order and writes the outputs
+        float* rb = red + (size_t)slot * red_floats(NMAT);
+        if (t == 0) {
+            rb[warp * kRows * NMAT + g] = yg;
+            rb[warp * kRows * NMAT + g + 8] = y8;
+            if (SW) {
+                rb[warp * kRows * NMAT + kRows + g] = ug;
+                rb[warp * kRows * NMAT + kRows + g + 8] = u8;
+            }
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&tickets[slot], 1) == kWarps - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            if (lane < ti.rows && !*abort_flag) {
+                float y = 0.0f, up = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) {
+                    y += rb[w * kRows * NMAT + lane];
+                    if (SW) up += rb[w * kRows * NMAT + kRows + lane];
+                }
+                const int o = ti.row0 + lane;
+                if (SW) {
+                    // Branch-stable SiLU(g) * u (cpu_llm.cpp:188-202).
+                    const float sig = y >= 0.0f ? 1.0f / (1.0f + expf(-y)) : expf(y) / (1.0f + expf(y));
+                    y = __fmul_rn(__fmul_rn(y, sig), up);
+                } else {
+                    if (sg.bias) y += sg.bias[o];
+                    if (sg.residual) y = sg.residual[o] + y;
+                }
+                sg.y[o] = y;
+            }
+            if (lane == 0) tickets[slot] = 0;
+            __syncwarp();
+        }
+        if (++slot > NS) slot = 0;
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+
+constexpr int kSmemMax = 227 * 1024;
+// Measured on B200: large stages (whole 16-row tiles where they fit) stream
+// far better than chunked rows; per-stage hand-off costs dominate below ~32 KB.
+constexpr int kStageTarget = 72 * 1024;
+
+bool type_ok(int t) { return t == CL_TYPE_Q4_K; }
+
+int block_bytes(int type) { return type == CL_TYPE_Q4_K ? 144 : 208; }
+
+// Row stride in a stage: conflict-free fragment reads need stride / 32 odd
+// (Q4_K: 8-byte reads by 4 lanes per row, 4 rows per half-warp phase).
+int stage_row_stride(int type, int bytes) {
+    int rs = (bytes + 15) & ~15;
+    if (type == CL_TYPE_Q4_K)
+        while (rs % 64 != 32) rs += 16;
+    return rs;
+}
+
+Geo make_geo(int type, int nb, int nmat) {
+    Geo g{};
+    g.bb = block_bytes(type);
+    g.db = 0;
+    int c = std::max(1, std::min(nb, kStageTarget / (nmat * kRows * g.bb)));
+    g.chunks = (nb + c - 1) / c;
+    g.c = (nb + g.chunks - 1) / g.chunks;
+    g.rs = stage_row_stride(type, g.c * g.bb + g.db);
+    return g;
+}
+
+template <int F, bool SW, int F2>
+cudaError_t launch_cfg(const Params& p, int smem, cudaStream_t stream) {
+    auto kern = gemv_mma_kernel<F, SW, F2>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    static int sm_count = 0;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    const int grid = std::min(p.tiles, sm_count);
+    return launch_pdl(kern, dim3(grid), dim3(kThreads), (size_t)smem, stream, p);
+}
+
+}  // namespace gmma
+
+// Launch over 1-4 segments of one K-quant type sharing x (optionally
+// RMS-normalised by gamma; SwiGLU over (w, w_up) when w_up is given).
+// Returns CL_ERR_UNSUPPORTED for shapes this kernel does not take.
+int launch_gemv_mma(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
+                    const void* w_up, cudaStream_t stream) {
+    using namespace gmma;
+    const bool sw = w_up != nullptr;
+    const int nmat = sw ? 2 : 1;
+    if (nseg < 1 || nseg > kMaxSegs || k <= 0 || k % 256 != 0 || k / 256 > kWarps * kMaxBlocksPerWarp)
+        return CL_ERR_UNSUPPORTED;
+    const int type = segs[0].type;
+    for (int i = 0; i < nseg; ++i)
+        if (segs[i].type != type || !type_ok(type)) return CL_ERR_UNSUPPORTED;
+    Params p{};
+    p.nb = k / 256;
+    p.k = k;
+    p.geo[0] = p.geo[1] = make_geo(type, p.nb, nmat);
+    int tiles = 0;
+    for (int i = 0; i < nseg; ++i) {
+        Seg& s = p.seg[i];
+        s.w = static_cast<const uint8_t*>(segs[i].w);
+        s.w_up = static_cast<const uint8_t*>(w_up);
+        s.stride = segs[i].stride;
+        s.bias = segs[i].bias;
+        s.residual = segs[i].residual;
+        s.y = segs[i].y;
+        s.type = segs[i].type;
+        s.n = segs[i].n;
+        s.tile_begin = tiles;
+        tiles += (segs[i].n + kRows - 1) / kRows;
+    }
+    p.nseg = nseg;
+    p.tiles = tiles;
+    p.x = x;
+    p.gamma = gamma;
+    p.eps = eps;
+    p.stage_bytes = nmat * kRows * p.geo[0].rs;
+    // layout: fixed | xs | xsum | xq | stages; the stage count fills the rest
+    auto layout = [&](int ns) {
+        int off = fixed_bytes(ns, nmat);
+        p.off_xs = off;
+        off += (4 * p.nb + 15) & ~15;
+        p.off_xsum = off;
+        off += 32 * p.nb;
+        p.off_xq = (off + 127) & ~127;
+        off = p.off_xq + 1024 * p.nb;
+        p.off_stage = (off + 127) & ~127;
+        return p.off_stage + ns * p.stage_bytes;
+    };
+    int ns = 8;
+    while (ns > 2 && layout(ns) > kSmemMax) --ns;
+    const int smem = layout(ns);
+    if (smem > kSmemMax) return CL_ERR_UNSUPPORTED;
+    p.stages = ns;
+    cudaError_t e;
+    if (sw)
+        e = launch_cfg<CL_TYPE_Q4_K, true, CL_TYPE_Q4_K>(p, smem, stream);
+    else
+        e = launch_cfg<CL_TYPE_Q4_K, false, CL_TYPE_Q4_K>(p, smem, stream);
+    return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+}
+
+int gemv_mma_device_error(int* code, bool clear) {
+    if (cudaMemcpyFromSymbol(code, g_gemv_mma_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    if (clear) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_gemv_mma_error, &zero, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
+    }
+    return CL_OK;
+}
+
+}  // namespace cl
