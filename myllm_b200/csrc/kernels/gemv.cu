@@ -411,15 +411,12 @@ int gemv_mma_device_error(int* code, bool clear);            // gemv_mma.cu
 
 int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* x, const float* gamma, float eps,
                      const void* w_up, cudaStream_t stream) {
-    // Segments of one K-quant type go to the tensor-core GEMV (gemv_mma.cu)
-    // when it takes the shape; fused format pairs and the other types run here.
+    // Q4_K / Q6_K segments (one type, or the Q4_K + Q6_K pair) go to the
+    // tensor-core GEMV (gemv_mma.cu) when it takes the shape; the other types
+    // and shapes run here.
     {
-        bool one_type = true;
-        for (int i = 1; i < nseg; ++i) one_type = one_type && segs[i].type == segs[0].type;
-        if (one_type) {
-            const int rc = launch_gemv_mma(segs, nseg, k, x, gamma, eps, w_up, stream);
-            if (rc != CL_ERR_UNSUPPORTED) return rc;
-        }
+        const int rc = launch_gemv_mma(segs, nseg, k, x, gamma, eps, w_up, stream);
+        if (rc != CL_ERR_UNSUPPORTED) return rc;
     }
     const bool sw = w_up != nullptr;
     const int nmat = sw ? 2 : 1;

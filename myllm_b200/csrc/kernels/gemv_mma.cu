@@ -31,6 +31,16 @@
 // by that unit's 6-bit sc with integer multiply-adds over the super-block
 // (|acc| < 2^28) and converts to FP32 once per super-block.
 //
+// Q6_K MMA layout.  A super-block half (128 elements) holds ql[64] (low 4
+// bits), qh[32] (2 high bits) and 8 int8 scales, one per 16 elements; the
+// low nibble of ql byte l + 32j is element l + 32j and the high nibble element
+// l + 32j + 64 (j = 0, 1).  One MMA takes 16 such bytes (l = 16s .. 16s+15)
+// for 16 rows: K slots 0-15 = q of element l + 32j (B columns 0-3, limbs of
+// that 16-element sub-block), slots 16-31 = q of element l + 32j + 64
+// (columns 4-7), each q = nibble | 2 bits << 4 in [0, 63] as u8; the -32
+// offset is folded in as -32 * sum(limb) per sub-block, precomputed with x.
+// Every lane then holds one sub-block and scales by its int8 sc.
+//
 // Kernel shape: persistent CTAs, one producer warp + 16 consumer warps.  The
 // producer streams 16-row tiles (a K-chunk of each row per stage) into a
 // shared-memory ring with cp.async.bulk (mbarrier completion, bounded waits);
@@ -88,7 +98,7 @@ struct Params {
     const float* gamma;  // RMSNorm weight applied to x first (cpu_llm.cpp:143-166), or null
     float eps;
     int nseg, k, nb, tiles, stages, stage_bytes;
-    int off_xs, off_xsum, off_xq, off_stage;  // shared-memory offsets
+    int off_xs, off_xsum, off_xn, off_xq, off_stage;  // shared-memory offsets
 };
 
 // Fixed part of the shared-memory layout: barriers (16 B per stage), abort
@@ -205,10 +215,57 @@ CL_DEVINL void q4k_sb(const uint8_t* bg, const uint8_t* b8, const uint2 (&bx0)[4
     y8 = fmaf(half_bits_to_float(h8.x), v8, y8);
 }
 
+// One Q6_K super-block of 16 rows (device layout: [ql 128][qh 64][sc 16] per
+// block, the row's f16 d array copied after the chunk).  bx0/bx1: the lane's
+// B words for the 8 MMAs (m = 4 hh + 2 j + s); xn: -32 * sum of the lane's two
+// limbs over each of its sub-blocks; dg/d8: the rows' d.
+CL_DEVINL void q6k_sb(const uint8_t* bg, const uint8_t* b8, const uint32_t (&bx0)[8], const uint32_t (&bx1)[8],
+                      const int2 (&xn)[8], float xs, int t, float dg, float d8, const Q4Lane& L, float& yg,
+                      float& y8) {
+    const int h = t >> 1;
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const uint32_t qg = *reinterpret_cast<const uint32_t*>(bg + 128 + 32 * hh + 16 * s + 4 * t);
+            const uint32_t q8 = *reinterpret_cast<const uint32_t*>(b8 + 128 + 32 * hh + 16 * s + 4 * t);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int m = 4 * hh + 2 * j + s;
+                const uint32_t lg = *reinterpret_cast<const uint32_t*>(bg + 64 * hh + 32 * j + 16 * s + 4 * t);
+                const uint32_t l8 = *reinterpret_cast<const uint32_t*>(b8 + 64 * hh + 32 * j + 16 * s + 4 * t);
+                // high bits of quarter j at bits 4-5 (low-nibble elements) and of quarter j+2
+                const uint32_t hag = (j ? (qg << 2) : (qg << 4)) & 0x30303030u;
+                const uint32_t ha8 = (j ? (q8 << 2) : (q8 << 4)) & 0x30303030u;
+                const uint32_t hbg = (j ? (qg >> 2) : qg) & 0x30303030u;
+                const uint32_t hb8 = (j ? (q8 >> 2) : q8) & 0x30303030u;
+                int c[4];
+                mma_u8s8_z(c, (lg & 0x0f0f0f0fu) | hag, (l8 & 0x0f0f0f0fu) | ha8, ((lg >> 4) & 0x0f0f0f0fu) | hbg,
+                           ((l8 >> 4) & 0x0f0f0f0fu) | hb8, bx0[m], bx1[m]);
+                // the lane's sub-block: quarter j (t < 2) or j + 2, elements 16 s ..
+                const int sci = 192 + 8 * hh + s + 2 * j + 4 * h;
+                const int sg = (int)*reinterpret_cast<const int8_t*>(bg + sci);
+                const int s8 = (int)*reinterpret_cast<const int8_t*>(b8 + sci);
+                a0 += (c[0] + xn[m].x) * sg;
+                a1 += (c[1] + xn[m].y) * sg;
+                a2 += (c[2] + xn[m].x) * s8;
+                a3 += (c[3] + xn[m].y) * s8;
+            }
+        }
+    }
+    const float vg = fmaf((float)a0, L.lw0, (float)a1 * L.lw1) * xs;
+    const float v8 = fmaf((float)a2, L.lw0, (float)a3 * L.lw1) * xs;
+    yg = fmaf(dg, vg, yg);
+    y8 = fmaf(d8, v8, y8);
+}
+
 // Encode one 256-element block (lane holds elements 8 lane .. 8 lane + 7)
-// into XQ4: xq[unit][limb][32] bytes, xs = s, xsum[h][gi] = sum of the
-// encoded x over unit 2 gi + h.
-CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* xs, float* xsum) {
+// into XQ4: xq[unit][limb][32] bytes, xs = s; for Q4_K xsum[h][gi] = sum of
+// the encoded x over unit 2 gi + h; for Q6_K xn[sub-block][limb] =
+// -32 * sum of the limb over the 16-element sub-block (sub-block = lane / 2).
+template <bool XSUM, bool XN>
+CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* xs, float* xsum, int* xn) {
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -217,6 +274,7 @@ CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* x
     const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
     uint32_t w[4][2] = {};
     int t0 = 0, t123 = 0;
+    int ls[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float r0 = v[i] * inv;
@@ -235,16 +293,28 @@ CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* x
         w[3][i >> 2] |= ((uint32_t)i3 & 0xffu) << sh;
         t0 += i0;
         t123 += i1 * 16384 + i2 * 128 + i3;
+        ls[0] += i0;
+        ls[1] += i1;
+        ls[2] += i2;
+        ls[3] += i3;
+    }
+    if (XN) {
+#pragma unroll
+        for (int l = 0; l < 4; ++l) ls[l] += __shfl_xor_sync(0xffffffffu, ls[l], 1);
+        if ((lane & 1) == 0)
+            *reinterpret_cast<int4*>(xn + (lane >> 1) * 4) = make_int4(-32 * ls[0], -32 * ls[1], -32 * ls[2], -32 * ls[3]);
     }
     const int unit = lane >> 2, e0 = (lane & 3) * 8;
 #pragma unroll
     for (int l = 0; l < 4; ++l)
         *reinterpret_cast<uint2*>(xq + unit * 128 + l * 32 + e0) = make_uint2(w[l][0], w[l][1]);
-    t0 += __shfl_xor_sync(0xffffffffu, t0, 1);
-    t123 += __shfl_xor_sync(0xffffffffu, t123, 1);
-    t0 += __shfl_xor_sync(0xffffffffu, t0, 2);
-    t123 += __shfl_xor_sync(0xffffffffu, t123, 2);
-    if ((lane & 3) == 0) {
+    if (XSUM) {
+        t0 += __shfl_xor_sync(0xffffffffu, t0, 1);
+        t123 += __shfl_xor_sync(0xffffffffu, t123, 1);
+        t0 += __shfl_xor_sync(0xffffffffu, t0, 2);
+        t123 += __shfl_xor_sync(0xffffffffu, t123, 2);
+    }
+    if (XSUM && (lane & 3) == 0) {
         // sum of x over the unit = s * 2^-21 * (2^21 sum l0 + sum(l1 2^14 + l2 2^7 + l3))
         const int gi = unit >> 1, h = unit & 1;
         xsum[h * 4 + gi] = fmaf((float)t0, 2097152.0f, (float)t123) * (s * (1.0f / 2097152.0f));
@@ -255,6 +325,8 @@ CL_DEVINL void encode_block(const float (&v)[8], int lane, uint8_t* xq, float* x
 template <int F, bool SW, int F2>
 __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
     constexpr int NMAT = SW ? 2 : 1;
+    constexpr bool HAS_Q4 = F == CL_TYPE_Q4_K || F2 == CL_TYPE_Q4_K;
+    constexpr bool HAS_Q6 = F == CL_TYPE_Q6_K || F2 == CL_TYPE_Q6_K;
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -266,7 +338,8 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
     float* red = reinterpret_cast<float*>(smem + off_red(NS));      // [NS + 1][kWarps][NMAT * 16]
     uint8_t* zero = smem + off_zero(NS, NMAT);
     float* xs = reinterpret_cast<float*>(smem + p.off_xs);
-    float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // [nb][2][4]
+    float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);  // Q4_K: [nb][2][4]
+    int* xn = reinterpret_cast<int*>(smem + p.off_xn);             // Q6_K: [nb][16][4]
     uint8_t* xq = smem + p.off_xq;                              // [nb][8 units][4 limbs][32]
     uint8_t* stages = smem + p.off_stage;
 
@@ -376,7 +449,7 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) xv[i][e] = __fmul_rn(xv[i][e], __fmul_rn(inv, gm[e]));
             }
-            encode_block(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8);
+            encode_block<HAS_Q4, HAS_Q6>(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8, xn + b * 64);
         }
     }
     named_barrier(1, kWarps * 32);
@@ -393,6 +466,12 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
     const uint8_t* xb0 = g < 4 ? xq + g * 32 + 8 * t : zero;
     const uint8_t* xb1 = g >= 4 ? xq + 128 + (g - 4) * 32 + 8 * t : zero;
     const int xinc0 = g < 4 ? 1024 : 0, xinc1 = g >= 4 ? 1024 : 0;
+    // Q6_K: columns 0-3 read unit 4 hh + j, columns 4-7 unit 4 hh + j + 2
+    const uint8_t* xb0q6 = g < 4 ? xq + g * 32 + 4 * t : zero;
+    const uint8_t* xb1q6 = g >= 4 ? xq + 256 + (g - 4) * 32 + 4 * t : zero;
+    Q4Lane L6 = L;  // Q6_K: no 1/16 factor on the high half
+    L6.lw0 = (t & 1) ? (1.0f / 16384.0f) : 1.0f;
+    L6.lw1 = L6.lw0 * (1.0f / 128.0f);
 
     int s = 0, base = 0, slot = 0;
     uint32_t ph = 0;
@@ -415,22 +494,51 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
                 const uint8_t* st = stages + (size_t)s * p.stage_bytes;
                 int j = warp - base;
                 if (j < 0) j += kWarps;
+                const bool q4 = F == F2 ? F == CL_TYPE_Q4_K : sg.type == CL_TYPE_Q4_K;
                 for (; j < nsb; j += kWarps) {
                     const int sb = sb0 + j;
-                    uint2 bx0[4], bx1[4];
-                    const uint8_t* p0 = xb0 + sb * xinc0;
-                    const uint8_t* p1 = xb1 + sb * xinc1;
-#pragma unroll
-                    for (int gi = 0; gi < 4; ++gi) {
-                        bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
-                        bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
-                    }
-                    const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
                     const float xsb = xs[sb];
                     const uint8_t* rg = st + (size_t)g * ge.rs + j * ge.bb;
                     const uint8_t* r8 = rg + 8 * ge.rs;
-                    q4k_sb(rg, r8, bx0, bx1, xsum4, xsb, t, L, yg, y8, ym);
-                    if (SW) q4k_sb(rg + kRows * ge.rs, r8 + kRows * ge.rs, bx0, bx1, xsum4, xsb, t, L, ug, u8, um);
+                    if (HAS_Q4 && q4) {
+                        uint2 bx0[4], bx1[4];
+                        const uint8_t* p0 = xb0 + sb * xinc0;
+                        const uint8_t* p1 = xb1 + sb * xinc1;
+#pragma unroll
+                        for (int gi = 0; gi < 4; ++gi) {
+                            bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
+                            bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
+                        }
+                        const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
+                        q4k_sb(rg, r8, bx0, bx1, xsum4, xsb, t, L, yg, y8, ym);
+                        if (SW)
+                            q4k_sb(rg + kRows * ge.rs, r8 + kRows * ge.rs, bx0, bx1, xsum4, xsb, t, L, ug, u8, um);
+                    } else if (HAS_Q6) {
+                        // B words: MMA m = 4 hh + 2 j + s reads 4 bytes at 16 s + 4 t of unit
+                        // 4 hh + j (columns 0-3) or 4 hh + j + 2 (columns 4-7), limb g & 3
+                        uint32_t bx0[8], bx1[8];
+                        int2 xnl[8];
+                        const uint8_t* p0 = xb0q6 + sb * xinc0;
+                        const uint8_t* p1 = xb1q6 + sb * xinc1;
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) {
+                            const int hh = m >> 2, jj = (m >> 1) & 1, ss = m & 1;
+                            bx0[m] = *reinterpret_cast<const uint32_t*>(p0 + 512 * hh + 128 * jj + 16 * ss);
+                            bx1[m] = *reinterpret_cast<const uint32_t*>(p1 + 512 * hh + 128 * jj + 16 * ss);
+                            // the lane's sub-block (quarter jj + 2h, half ss) and limb pair
+                            const int sbi = 8 * hh + 2 * (jj + 2 * h) + ss;
+                            xnl[m] = *reinterpret_cast<const int2*>(xn + sb * 64 + sbi * 4 + 2 * (t & 1));
+                        }
+                        const uint8_t* dcol = st + (size_t)ge.c * ge.bb + 2 * sb;
+                        const float dg = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dcol + (size_t)g * ge.rs));
+                        const float d8 = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dcol + (size_t)(g + 8) * ge.rs));
+                        q6k_sb(rg, r8, bx0, bx1, xnl, xsb, t, dg, d8, L6, yg, y8);
+                        if (SW) {
+                            const float ug0 = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dcol + (size_t)(kRows + g) * ge.rs));
+                            const float u80 = half_bits_to_float(*reinterpret_cast<const unsigned short*>(dcol + (size_t)(kRows + g + 8) * ge.rs));
+                            q6k_sb(rg + kRows * ge.rs, r8 + kRows * ge.rs, bx0, bx1, xnl, xsb, t, ug0, u80, L6, ug, u8);
+                        }
+                    }
                 }
             }
             base += nsb;
@@ -507,27 +615,36 @@ constexpr int kSmemMax = 227 * 1024;
 // far better than chunked rows; per-stage hand-off costs dominate below ~32 KB.
 constexpr int kStageTarget = 72 * 1024;
 
-bool type_ok(int t) { return t == CL_TYPE_Q4_K; }
+bool type_ok(int t) { return t == CL_TYPE_Q4_K || t == CL_TYPE_Q6_K; }
 
 int block_bytes(int type) { return type == CL_TYPE_Q4_K ? 144 : 208; }
 
-// Row stride in a stage: conflict-free fragment reads need stride / 32 odd
-// (Q4_K: 8-byte reads by 4 lanes per row, 4 rows per half-warp phase).
+// Row stride in a stage for conflict-free fragment reads: Q4_K reads 8 bytes
+// per lane (4 lanes per row, 4 rows per half-warp phase) -> stride / 32 odd;
+// Q6_K reads 4 bytes per lane (4 lanes per row, 8 rows per access) ->
+// stride / 16 odd.
 int stage_row_stride(int type, int bytes) {
     int rs = (bytes + 15) & ~15;
     if (type == CL_TYPE_Q4_K)
         while (rs % 64 != 32) rs += 16;
+    else
+        while (rs % 32 != 16) rs += 16;
     return rs;
 }
 
-Geo make_geo(int type, int nb, int nmat) {
+// Stage geometry: whole rows per stage when 16 of them fit the target, else
+// the fewest equal chunks that do.  `limit` caps the stage bytes.
+Geo make_geo(int type, int nb, int nmat, int limit) {
     Geo g{};
     g.bb = block_bytes(type);
-    g.db = 0;
-    int c = std::max(1, std::min(nb, kStageTarget / (nmat * kRows * g.bb)));
-    g.chunks = (nb + c - 1) / c;
-    g.c = (nb + g.chunks - 1) / g.chunks;
-    g.rs = stage_row_stride(type, g.c * g.bb + g.db);
+    g.db = type == CL_TYPE_Q6_K ? ((2 * nb + 15) & ~15) : 0;
+    g.chunks = 1;
+    for (;;) {
+        g.c = (nb + g.chunks - 1) / g.chunks;
+        g.rs = stage_row_stride(type, g.c * g.bb + g.db);
+        if (nmat * kRows * g.rs <= limit || g.c == 1) break;
+        ++g.chunks;
+    }
     return g;
 }
 
@@ -560,13 +677,18 @@ int launch_gemv_mma(const cl_gemv_segment* segs, int nseg, int k, const float* x
     const int nmat = sw ? 2 : 1;
     if (nseg < 1 || nseg > kMaxSegs || k <= 0 || k % 256 != 0 || k / 256 > kWarps * kMaxBlocksPerWarp)
         return CL_ERR_UNSUPPORTED;
-    const int type = segs[0].type;
-    for (int i = 0; i < nseg; ++i)
-        if (segs[i].type != type || !type_ok(type)) return CL_ERR_UNSUPPORTED;
+    // one type, or the fused pair Q4_K + Q6_K (the Q4_K_M attention projections)
+    int ta = segs[0].type, tb = segs[0].type;
+    for (int i = 0; i < nseg; ++i) {
+        if (!type_ok(segs[i].type)) return CL_ERR_UNSUPPORTED;
+        if (segs[i].type != ta) tb = segs[i].type;
+    }
+    if (sw && ta != tb) return CL_ERR_UNSUPPORTED;
+    const bool has4 = ta == CL_TYPE_Q4_K || tb == CL_TYPE_Q4_K;
+    const bool has6 = ta == CL_TYPE_Q6_K || tb == CL_TYPE_Q6_K;
     Params p{};
     p.nb = k / 256;
     p.k = k;
-    p.geo[0] = p.geo[1] = make_geo(type, p.nb, nmat);
     int tiles = 0;
     for (int i = 0; i < nseg; ++i) {
         Seg& s = p.seg[i];
@@ -586,29 +708,40 @@ int launch_gemv_mma(const cl_gemv_segment* segs, int nseg, int k, const float* x
     p.x = x;
     p.gamma = gamma;
     p.eps = eps;
-    p.stage_bytes = nmat * kRows * p.geo[0].rs;
-    // layout: fixed | xs | xsum | xq | stages; the stage count fills the rest
+    // layout: fixed | xs | xsum (Q4_K) | xn (Q6_K) | xq | stages
     auto layout = [&](int ns) {
         int off = fixed_bytes(ns, nmat);
         p.off_xs = off;
         off += (4 * p.nb + 15) & ~15;
         p.off_xsum = off;
-        off += 32 * p.nb;
+        off += has4 ? 32 * p.nb : 0;
+        p.off_xn = off;
+        off += has6 ? 256 * p.nb : 0;
         p.off_xq = (off + 127) & ~127;
         off = p.off_xq + 1024 * p.nb;
         p.off_stage = (off + 127) & ~127;
         return p.off_stage + ns * p.stage_bytes;
     };
+    // Stages as large as possible (whole tiles), at least two of them.
+    const int room = kSmemMax - layout(0);
+    const int limit = std::min(kStageTarget, room / 2);
+    p.geo[0] = make_geo(has4 ? CL_TYPE_Q4_K : CL_TYPE_Q6_K, p.nb, nmat, limit);
+    p.geo[1] = make_geo(has6 ? CL_TYPE_Q6_K : CL_TYPE_Q4_K, p.nb, nmat, limit);
+    p.stage_bytes = nmat * kRows * std::max(p.geo[0].rs, p.geo[1].rs);
     int ns = 8;
     while (ns > 2 && layout(ns) > kSmemMax) --ns;
     const int smem = layout(ns);
     if (smem > kSmemMax) return CL_ERR_UNSUPPORTED;
     p.stages = ns;
     cudaError_t e;
-    if (sw)
-        e = launch_cfg<CL_TYPE_Q4_K, true, CL_TYPE_Q4_K>(p, smem, stream);
+    if (has4 && has6)
+        e = launch_cfg<CL_TYPE_Q4_K, false, CL_TYPE_Q6_K>(p, smem, stream);
+    else if (has4)
+        e = sw ? launch_cfg<CL_TYPE_Q4_K, true, CL_TYPE_Q4_K>(p, smem, stream)
+               : launch_cfg<CL_TYPE_Q4_K, false, CL_TYPE_Q4_K>(p, smem, stream);
     else
-        e = launch_cfg<CL_TYPE_Q4_K, false, CL_TYPE_Q4_K>(p, smem, stream);
+        e = sw ? launch_cfg<CL_TYPE_Q6_K, true, CL_TYPE_Q6_K>(p, smem, stream)
+               : launch_cfg<CL_TYPE_Q6_K, false, CL_TYPE_Q6_K>(p, smem, stream);
     return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
 }
 
