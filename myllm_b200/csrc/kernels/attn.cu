@@ -74,7 +74,7 @@ __host__ __device__ inline size_t attn_decode_smem(int group, int d) {
 // all CTAs.  K and V tiles are staged with asynchronous copies (a tile's
 // loads all in flight at once; K rows padded by 16 bytes so that threads on
 // different keys hit different banks).  Scores: one thread per (key, head)
-// dot product; the per-head softmax statistics by one thread per head; an
+// dot product; the per-head softmax statistics by one warp per head; an
 // online softmax carries (m, l, o) across tiles.  Each CTA leaves an
 // unnormalised partial [m, l, o[d]] per query head in the workspace.
 __global__ void __launch_bounds__(kDecThreads)
@@ -143,22 +143,26 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
             ps[h * kTileKeys + t] = ((a0 + a1) + (a2 + a3)) * scale;
         }
         __syncthreads();
-        // online softmax statistics: one thread per head
-        if (tid < G) {
-            const int h = tid;
-            float m = -INFINITY;
-            for (int t = 0; t < nk; ++t) m = fmaxf(m, ps[h * kTileKeys + t]);
-            const float mo = run[2 * h], mn = fmaxf(mo, m);
-            float l = 0.0f;
-            for (int t = 0; t < nk; ++t) {
-                const float e = expf(ps[h * kTileKeys + t] - mn);
-                ps[h * kTileKeys + t] = e;
-                l += e;
+        // online softmax statistics: one warp per head, lanes over the keys
+        {
+            const int warp = tid >> 5, lane = tid & 31;
+            for (int h = warp; h < G; h += kDecWarps) {
+                float* ph = ps + h * kTileKeys;
+                const float s0 = lane < nk ? ph[lane] : -INFINITY;
+                const float s1 = lane + 32 < nk ? ph[lane + 32] : -INFINITY;
+                const float mo = run[2 * h], mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+                const float e0 = lane < nk ? expf(s0 - mn) : 0.0f;
+                const float e1 = lane + 32 < nk ? expf(s1 - mn) : 0.0f;
+                if (lane < nk) ph[lane] = e0;
+                if (lane + 32 < nk) ph[lane + 32] = e1;
+                const float l = warp_sum(e0 + e1);
+                if (lane == 0) {
+                    const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                    fac[h] = f;
+                    run[2 * h] = mn;
+                    run[2 * h + 1] = run[2 * h + 1] * f + l;
+                }
             }
-            const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
-            fac[h] = f;
-            run[2 * h] = mn;
-            run[2 * h + 1] = run[2 * h + 1] * f + l;
         }
         cp_async_wait<0>();  // V
         __syncthreads();
