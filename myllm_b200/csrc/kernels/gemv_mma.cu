@@ -359,44 +359,53 @@ __global__ void __launch_bounds__(kThreads) gemv_mma_kernel(const Params p) {
     grid_launch_dependents();
 
     if (warp == kWarps) {
-        // ---- producer: lane r (< 16 NMAT) copies row r of the tile's chunk ----
+        // ---- producer: lane r (< 16 NMAT) copies row r of the tile's chunk.
+        // Each stage's sources, sizes and byte count are computed before the
+        // wait for its slot, so the copies issue as soon as the slot frees. ----
         int s = 0;
         uint32_t ph = 0;
-        for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+        int tile = blockIdx.x, ch = 0;
+        while (tile < p.tiles) {
             const TileInfo ti = tile_of(segs, p.nseg, tile);
             const Seg& sg = segs[ti.seg];
             const Geo& ge = p.geo[(F == F2 || sg.type == F) ? 0 : 1];
-            for (int ch = 0; ch < ge.chunks; ++ch) {
-                // the whole warp waits: a wait by one elected lane while the
-                // others sit in __syncwarp() measured 2.5x slower hand-offs
-                int ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1u);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok && lane == 0) {
-                    if (!*abort_flag) {
-                        atomicExch(&g_gemv_mma_error, 4);
-                        *abort_flag = 1;
-                    }
+            const int sb0 = ch * ge.c, nsb = min(ge.c, p.nb - sb0);
+            const uint32_t rb = (uint32_t)(nsb * ge.bb);
+            const uint32_t tx = (uint32_t)(NMAT * ti.rows) * (rb + ge.db);
+            const int m = lane / kRows, r = lane % kRows;
+            const bool copies = lane < NMAT * kRows && r < ti.rows;
+            const uint8_t* src = (m ? sg.w_up : sg.w) + (size_t)(ti.row0 + r) * sg.stride;
+            const int dst_off = (m * kRows + r) * ge.rs;
+            const int db = ge.db, dpos = ge.c * ge.bb;
+            const uint8_t* dsrc = src + (size_t)p.nb * ge.bb;
+            src += (size_t)sb0 * ge.bb;
+            if (++ch == ge.chunks) {
+                ch = 0;
+                tile += gridDim.x;
+            }
+            // the whole warp waits: a wait by one elected lane while the
+            // others sit in __syncwarp() measured 2.5x slower hand-offs
+            int ok = !*abort_flag && mbar_wait(&empty[s], ph ^ 1u);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok && lane == 0) {
+                if (!*abort_flag) {
+                    atomicExch(&g_gemv_mma_error, 4);
+                    *abort_flag = 1;
                 }
-                if (ok) {
-                    const int sb0 = ch * ge.c, nsb = min(ge.c, p.nb - sb0);
-                    const uint32_t rb = (uint32_t)(nsb * ge.bb);
-                    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(NMAT * ti.rows) * (rb + ge.db));
-                    __syncwarp();
-                    if (lane < NMAT * kRows) {
-                        const int m = lane / kRows, r = lane % kRows;
-                        if (r < ti.rows) {
-                            const uint8_t* src = (m ? sg.w_up : sg.w) + (size_t)(ti.row0 + r) * sg.stride;
-                            uint8_t* dst = stages + (size_t)s * p.stage_bytes + (size_t)(m * kRows + r) * ge.rs;
-                            bulk_g2s(dst, src + (size_t)sb0 * ge.bb, rb, &full[s]);
-                            if (ge.db) bulk_g2s(dst + ge.c * ge.bb, src + (size_t)p.nb * ge.bb, ge.db, &full[s]);
-                        }
-                    }
-                }
+            }
+            if (ok) {
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], tx);
                 __syncwarp();
-                if (++s == NS) {
-                    s = 0;
-                    ph ^= 1u;
+                if (copies) {
+                    uint8_t* dst = stages + (size_t)s * p.stage_bytes + dst_off;
+                    bulk_g2s(dst, src, rb, &full[s]);
+                    if (db) bulk_g2s(dst + dpos, dsrc, db, &full[s]);
                 }
+            }
+            __syncwarp();
+            if (++s == NS) {
+                s = 0;
+                ph ^= 1u;
             }
         }
         return;
