@@ -418,6 +418,7 @@ int launch_same_type(const cl_gemv_segment* segs, int nseg, int k, const float* 
         const int rc = launch_gemv_mma(segs, nseg, k, x, gamma, eps, w_up, stream);
         if (rc != CL_ERR_UNSUPPORTED) return rc;
     }
+    if (k / 32 > kMaxConsumerWarps * 32) return CL_ERR_UNSUPPORTED;
     const bool sw = w_up != nullptr;
     const int nmat = sw ? 2 : 1;
     GemvParams p{};
@@ -474,7 +475,6 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, co
         reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
         (gamma && (reinterpret_cast<uintptr_t>(gamma) % 16 != 0 || !(eps > 0.0f))))
         return CL_ERR_INVALID;
-    if (k / 32 > kMaxConsumerWarps * 32) return CL_ERR_UNSUPPORTED;
     for (int i = 0; i < nseg; ++i) {
         const cl_gemv_segment& s = segs[i];
         if (!gemv_type_ok(s.type) || s.w == nullptr || s.y == nullptr || s.n <= 0) return CL_ERR_INVALID;
