@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--model", default=None, help="synthetic config name (default by --gpus)")
     ap.add_argument("--kernel-iters", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 kernel sweep (N = 1 only)")
     return ap.parse_args()
 
 
@@ -209,6 +210,71 @@ def time_gateup_kernel(spec, iters: int):
             "bytes_per_launch": algo, "avg_launch_us": ms * 1e3, "gbs": algo / (ms * 1e-3) / 1e9}
 
 
+# GEMV shapes (N x K) per format, GEMM at M in {128, 512, 2048}
+SWEEP_SHAPES = [(896, 896), (4864, 896), (896, 4864), (18944, 3584), (3584, 18944), (13824, 5120)]
+
+
+def graph_time_us(fn, iters: int) -> float:
+    """Average device time of fn(i) over `iters` calls captured in one CUDA
+    graph (replayed after a warm-up), so the host call cost is not timed."""
+    import torch
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3
+
+
+def kernel_sweep(peak_gbs: float, seed: int):
+    """Config 1: decode GEMV GB/s over the sweep shapes and formats (weights
+    rotate over copies whose total exceeds the 126 MB L2 where memory allows;
+    `l2_resident` marks the small shapes whose copies fit in L2), and the
+    prefill GEMM at M = 128 / 512 / 2048 on the 18944 x 3584 Q4_K weights."""
+    import math
+    import torch
+    from myllm_b200 import kernels as K
+    from myllm_b200 import synth_gguf as sg
+    gemv = []
+    for gtype in (sg.Q4_K, sg.Q6_K, sg.Q5_0, sg.Q8_0):
+        for n, k in SWEEP_SHAPES:
+            if k % sg.BLOCK[gtype][0]:
+                continue  # K-quants need K % 256 == 0 (n/a at K = 896)
+            w = K.repack(gtype, sg.fill(gtype, n, k, sg.stream_key(seed, f"sweep{gtype}_{n}_{k}"), 0.0, 0.02), k)
+            nbytes = n * sg.row_bytes(gtype, k) + 4 * k + 4 * n
+            copies = max(2, min(64, math.ceil(300e6 / nbytes)))
+            ws = [w] + [w.clone() for _ in range(copies - 1)]
+            x = torch.randn(k, device="cuda")
+            y = torch.empty(n, device="cuda")
+            us = graph_time_us(lambda i: K.gemv(gtype, ws[i % copies], n, k, x, out=y), 40)
+            gemv.append({"type": sg.TYPE_NAMES[gtype], "n": n, "k": k, "us": round(us, 2),
+                         "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak_gbs, 3),
+                         "l2_resident": copies * nbytes < 126e6})
+            del ws, w
+    gemm = []
+    n, k = 18944, 3584
+    w = K.repack(sg.Q4_K, sg.fill(sg.Q4_K, n, k, sg.stream_key(seed, "sweep_gemm"), 0.0, 0.02), k)
+    for m in (128, 512, 2048):
+        x = torch.randn(m, k, device="cuda")
+        out = torch.empty(m * n, device="cuda")
+        us = graph_time_us(lambda i: K.gemm(sg.Q4_K, w, n, k, x, path="tf32x3", out=out), 10)
+        gemm.append({"type": "Q4_K", "n": n, "k": k, "m": m, "us": round(us, 1),
+                     "tflops": round(2 * m * n * k / us / 1e6, 1)})
+    return {"gemv": gemv, "gemm_tf32x3": gemm,
+            "note": "GEMV frac of the measured HBM copy peak; GEMM TFLOP/s of useful work (2 M N K), "
+                    "the split-TF32 mode issues three tensor-core products per useful one"}
+
+
 def run_cpu_baseline(path: str, timeout: int = 900):
     cmd = [sys.executable, "-m", "oracle.cpu_baseline", "--model", path, "--prompt", "4", "--decode", "2"]
     try:
@@ -297,6 +363,7 @@ def bench_cuda(args):
 
     peak, peak_kind = measured_peaks()
     kern = time_gateup_kernel(spec, args.kernel_iters)
+    sweep = kernel_sweep(peak, spec.seed) if world == 1 and not args.no_sweep else None
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -344,6 +411,7 @@ def bench_cuda(args):
                      "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
                      "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
         "cpu_baseline": cpu,
+        "kernel_sweep": sweep,
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }
