@@ -377,10 +377,10 @@ def bench_cuda(args):
     if world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
     # embed; per layer: QKV GEMV (one launch per run of one format or of a
-    # fused format pair), rope, attention split + combine, o, gate/up, down;
-    # final head GEMV, argmax, counter
+    # fused format pair), attention split (with RoPE and the KV append) +
+    # combine, o, gate/up, down; final head GEMV, argmax, counter
     qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")]) for l in range(spec.layers))
-    launches_per_step = 1 + qkv + 6 * spec.layers + 3
+    launches_per_step = 1 + qkv + 5 * spec.layers + 3
     line = {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),

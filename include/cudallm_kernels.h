@@ -156,6 +156,18 @@ CL_API size_t cl_attn_decode_workspace_bytes(int q_heads, int head_dim, int max_
 CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
                           int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out,
                           void* xq, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* cl_attn_decode with the NeoX RoPE of the current position and the KV
+ * append fused in (replaces cl_rope_kv + cl_attn_decode for one decode row;
+ * cpu_llm.cpp:204-235 rotation, cpu_llm.cpp:885-886 append): q holds the
+ * unrotated query [q_heads*head_dim] (left unchanged), k_new / v_new the new
+ * key / value [kv_heads*head_dim]; the position is *pos_dev (device int) and
+ * the live length *pos_dev + 1; cos_sin is the [capacity][rot_dim/2][2]
+ * table.  Writes the rotated key and the value to cache row *pos_dev.
+ * Results equal the two separate calls exactly. */
+CL_API int cl_attn_decode_rope(const float* q, const float* k_new, const float* v_new, const float* cos_sin,
+                               const int* pos_dev, int rot_dim, float* k_cache, float* v_cache, int max_len,
+                               int q_heads, int kv_heads, int head_dim, float scale, float* out, void* xq,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream);
 /* cl_attn_decode without a workspace argument, for callers that cannot
  * allocate device memory (no counterpart in the reference: MetalLLM and
  * CPULLM allocate their scratch themselves).  The split partials live in a

@@ -47,6 +47,8 @@ SIGNATURES = {
     "cl_attn_decode_workspace_bytes": (c_size, [c_int, c_int, c_int]),
     "cl_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp,
                                c_vp, c_size, c_vp]),
+    "cl_attn_decode_rope": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                                    c_float, c_vp, c_vp, c_vp, c_size, c_vp]),
     "cl_attn_decode_noalloc_limit_bytes": (c_size, []),
     "cl_attn_decode_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp]),
     "cl_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),

@@ -414,10 +414,10 @@ struct CudaLLM::Impl {
                 {L.v.type, L.v.ptr, L.v.stride, L.v.rows, L.v_b, nullptr, v},
             };
             CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, h, L.attn_norm, eps(), s));
-            CUDALLM_CL(cl_rope_kv(q, k, v, 1, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, pos, 0,
-                                  L.k_cache, L.v_cache, s));
-            CUDALLM_CL(cl_attn_decode(q, L.k_cache, L.v_cache, len, (int)max_seq, (int)hq_l, (int)hkv_l, (int)d, scale,
-                                      att, nullptr, attn_ws, attn_ws_bytes, s));
+            // RoPE of q/k at *pos, the KV append and attention over keys 0..*pos in one launch pair
+            CUDALLM_CL(cl_attn_decode_rope(q, k, v, rope, pos, (int)config.rotary_dimension, L.k_cache, L.v_cache,
+                                           (int)max_seq, (int)hq_l, (int)hkv_l, (int)d, scale, att, nullptr, attn_ws,
+                                           attn_ws_bytes, s));
             const float* o_in = att;
             if (gather_attn) {
                 CUDALLM_NCCL(ncclAllGather(att, att_full, hq_l * d, ncclFloat32, comm, s));

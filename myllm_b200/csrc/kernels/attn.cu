@@ -77,14 +77,33 @@ __host__ __device__ inline size_t attn_decode_smem(int group, int d) {
 // dot product; the per-head softmax statistics by one warp per head; an
 // online softmax carries (m, l, o) across tiles.  Each CTA leaves an
 // unnormalised partial [m, l, o[d]] per query head in the workspace.
+// Optional fused RoPE + KV append (Rope.cs != null): q holds the unrotated
+// query; the CTA rotates its heads in shared memory.  The key and value of
+// the current position (Rope.pos_dev; live length = pos + 1) come from
+// Rope.k / Rope.v: the CTA whose keys include that position rotates the key,
+// writes both rows to the caches and uses them in place of the tile rows it
+// loaded.  Same expressions as rope_kv_kernel, so the results are identical
+// to RoPE + KV append + attention as separate launches.
+struct AttnRope {
+    const float* cs;  // [capacity][rot/2][cos, sin], or null
+    const float* k;   // [kv_heads * d] new key (unrotated)
+    const float* v;   // [kv_heads * d] new value
+    const int* pos_dev;
+    float* kc;        // caches, written at row pos
+    float* vc;
+    int rot;
+};
+
 __global__ void __launch_bounds__(kDecThreads)
 attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                  const int* __restrict__ len_dev, int hq, int hkv, int d, float scale, float* __restrict__ part) {
+                  const int* __restrict__ len_dev, int hq, int hkv, int d, float scale, float* __restrict__ part,
+                  const AttnRope rope) {
     grid_launch_dependents();
     grid_wait();
     const int g = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
     const int G = hq / hkv;
-    const int L = *len_dev;
+    const int pos = rope.cs ? *rope.pos_dev : -1;
+    const int L = rope.cs ? pos + 1 : *len_dev;
     const int S = (L + nsplit - 1) / nsplit;
     const int k0 = split * S;
     const int nk_all = max(0, min(S, L - k0));
@@ -126,6 +145,50 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         cp_async_commit();
         cp_async_wait<1>();  // q and K
         __syncthreads();
+        if (rope.cs) {
+            const int half = rope.rot / 2;
+            const float* csp = rope.cs + (size_t)pos * half * 2;
+            if (t0 == 0) {
+                // rotate this CTA's query heads (NeoX split halves)
+                for (int i = tid; i < G * half; i += kDecThreads) {
+                    const int h = i / half, pp = i - h * half;
+                    float* qh = qs + h * d;
+                    const float c = csp[2 * pp], sn = csp[2 * pp + 1];
+                    const float a = qh[pp], b = qh[pp + half];
+                    qh[pp] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+                    qh[pp + half] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+                }
+            }
+            const int r = pos - (k0 + t0);
+            if (r >= 0 && r < nk) {
+                // the current position's key: rotate, cache it, use it in the tile
+                const float* kn = rope.k + (size_t)g * d;
+                float* kw = rope.kc + (size_t)pos * kvd + (size_t)g * d;
+                for (int pp = tid; pp < d / 2; pp += kDecThreads) {
+                    int i0, i1;
+                    if (pp < half) {
+                        i0 = pp;
+                        i1 = pp + half;
+                    } else {
+                        i0 = rope.rot + 2 * (pp - half);
+                        i1 = i0 + 1;
+                    }
+                    float a = kn[i0], b = kn[i1];
+                    if (pp < half) {
+                        const float c = csp[2 * pp], sn = csp[2 * pp + 1];
+                        const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+                        const float rb = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+                        a = ra;
+                        b = rb;
+                    }
+                    kw[i0] = a;
+                    kw[i1] = b;
+                    ks[r * kld + i0] = a;
+                    ks[r * kld + i1] = b;
+                }
+            }
+            __syncthreads();
+        }
         // scores: thread per (key, head)
         for (int pidx = tid; pidx < nk * G; pidx += kDecThreads) {
             const int t = pidx / G, h = pidx - t * G;
@@ -165,6 +228,17 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
             }
         }
         cp_async_wait<0>();  // V
+        if (rope.cs) {
+            const int r = pos - (k0 + t0);
+            if (r >= 0 && r < nk) {
+                const float* vn = rope.v + (size_t)g * d;
+                float* vw = rope.vc + (size_t)pos * kvd + (size_t)g * d;
+                for (int c = tid; c < d; c += kDecThreads) {
+                    vw[c] = vn[c];
+                    vs[r * d + c] = vn[c];
+                }
+            }
+        }
         __syncthreads();
         if (active) {
 #pragma unroll
@@ -344,10 +418,10 @@ CL_API size_t cl_attn_decode_workspace_bytes(int q_heads, int head_dim, int max_
     return (size_t)q_heads * attn_splits(max_len) * (head_dim + 2) * sizeof(float);
 }
 
-CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
-                          int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out, void* xq,
-                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-    if (q == nullptr || k_cache == nullptr || v_cache == nullptr || len_dev == nullptr || out == nullptr ||
+static int attn_decode_launch(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
+                              int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out, void* xq,
+                              void* workspace, size_t workspace_bytes, const AttnRope& rope, cudaStream_t stream) {
+    if (q == nullptr || k_cache == nullptr || v_cache == nullptr || (len_dev == nullptr && !rope.cs) || out == nullptr ||
         max_len <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || q_heads / kv_heads > kMaxGroup ||
         head_dim <= 0 || head_dim % 32 || head_dim > kMaxHeadDim)
         return CL_ERR_INVALID;
@@ -368,12 +442,32 @@ CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_c
         }
     }
     if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), smem, stream, q, k_cache, v_cache,
-                   len_dev, q_heads, kv_heads, head_dim, scale, part) != cudaSuccess)
+                   len_dev, q_heads, kv_heads, head_dim, scale, part, rope) != cudaSuccess)
         return CL_ERR_CUDA;
     return launch_pdl(attn_decode_combine, dim3(q_heads), dim3(head_dim), 0, stream, part, splits, head_dim, out, xq,
                       q_heads * head_dim) == cudaSuccess
                ? CL_OK
                : CL_ERR_CUDA;
+}
+
+CL_API int cl_attn_decode(const float* q, const float* k_cache, const float* v_cache, const int* len_dev,
+                          int max_len, int q_heads, int kv_heads, int head_dim, float scale, float* out, void* xq,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    const AttnRope none{};
+    return attn_decode_launch(q, k_cache, v_cache, len_dev, max_len, q_heads, kv_heads, head_dim, scale, out, xq,
+                              workspace, workspace_bytes, none, stream);
+}
+
+CL_API int cl_attn_decode_rope(const float* q, const float* k_new, const float* v_new, const float* cos_sin,
+                               const int* pos_dev, int rot_dim, float* k_cache, float* v_cache, int max_len,
+                               int q_heads, int kv_heads, int head_dim, float scale, float* out, void* xq,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (k_new == nullptr || v_new == nullptr || cos_sin == nullptr || pos_dev == nullptr || rot_dim <= 0 ||
+        rot_dim > head_dim || rot_dim % 2)
+        return CL_ERR_INVALID;
+    const AttnRope rope{cos_sin, k_new, v_new, pos_dev, k_cache, v_cache, rot_dim};
+    return attn_decode_launch(q, k_cache, v_cache, nullptr, max_len, q_heads, kv_heads, head_dim, scale, out, xq,
+                              workspace, workspace_bytes, rope, stream);
 }
 
 static size_t prefill_smem(int d) {

@@ -147,6 +147,20 @@ def attn_decode(q, k_cache, v_cache, length: int, max_len: int, hq, hkv, d, scal
     return (out, xq) if want_xq else out
 
 
+def attn_decode_rope(q, k_new, v_new, cos_sin, pos: int, rot: int, k_cache, v_cache, max_len: int, hq, hkv, d,
+                     scale):
+    """RoPE at `pos` + KV append + decode attention over keys 0..pos in one call."""
+    dev = q.device
+    out = torch.empty(hq * d, dtype=torch.float32, device=dev)
+    wsb = int(_native.lib().cl_attn_decode_workspace_bytes(hq, d, max_len))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    pd = torch.tensor([pos], dtype=torch.int32, device=dev)
+    check(_native.lib().cl_attn_decode_rope(_p(q), _p(k_new), _p(v_new), _p(cos_sin), _p(pd), rot, _p(k_cache),
+                                            _p(v_cache), max_len, hq, hkv, d, scale, _p(out), None, _p(ws), wsb,
+                                            _stream()), "cl_attn_decode_rope")
+    return out
+
+
 def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d):
     out = torch.empty((rows, hq * d), dtype=torch.float32, device=q.device)
     check(_native.lib().cl_attn_prefill(_p(q), _p(k_cache), _p(v_cache), pos0, rows, hq, hkv, d, _p(out),

@@ -304,3 +304,30 @@ def test_embedding_rows_are_reference_values(cuda, gtype):
     for i, t in enumerate([3, 0, 49, 3]):
         np.testing.assert_array_equal(out[i], ref[t])
     assert np.all(out[4:] == 0) and int(flag) == 1
+
+
+@pytest.mark.parametrize("hq,hkv,d,rot,pos,cap", [(28, 4, 128, 128, 549, 4096), (28, 4, 128, 128, 0, 4096),
+                                                  (14, 2, 64, 64, 63, 512), (8, 2, 64, 32, 200, 256),
+                                                  (28, 4, 128, 128, 2047, 2048)])
+def test_attention_decode_with_fused_rope_matches_separate_calls(cuda, hq, hkv, d, rot, pos, cap):
+    """cl_attn_decode_rope = cl_rope_kv (one row) + cl_attn_decode, exactly:
+    same outputs bit for bit and the same cache row written."""
+    g = torch.Generator(device="cpu").manual_seed(pos + d)
+    q = torch.randn(hq * d, generator=g).cuda()
+    kn = torch.randn(hkv * d, generator=g).cuda()
+    vn = torch.randn(hkv * d, generator=g).cuda()
+    kc = torch.randn(cap, hkv * d, generator=g).cuda()
+    vc = torch.randn(cap, hkv * d, generator=g).cuda()
+    ang = torch.arange(cap, dtype=torch.float64)[:, None] * 1e6 ** (-2.0 * torch.arange(rot // 2, dtype=torch.float64) / rot)
+    table = torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).float().cuda()  # [cap][rot/2][2]
+    scale = 1.0 / math.sqrt(d)
+    # separate: RoPE + append, then attention
+    q1, kc1, vc1 = q.clone(), kc.clone(), vc.clone()
+    K.rope_kv(q1, kn, vn, 1, hq, hkv, d, rot, table, pos, kc1, vc1)
+    want = K.attn_decode(q1, kc1, vc1, pos + 1, cap, hq, hkv, d, scale)
+    # fused
+    kc2, vc2 = kc.clone(), vc.clone()
+    got = K.attn_decode_rope(q, kn, vn, table, pos, rot, kc2, vc2, cap, hq, hkv, d, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
