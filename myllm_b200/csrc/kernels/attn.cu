@@ -96,14 +96,18 @@ struct AttnRope {
 
 __global__ void __launch_bounds__(kDecThreads)
 attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                  const int* __restrict__ len_dev, int hq, int hkv, int d, float scale, float* __restrict__ part,
-                  const AttnRope rope) {
+                  const int* __restrict__ len_dev, int cap, int hq, int hkv, int d, float scale,
+                  float* __restrict__ part, const AttnRope rope) {
     grid_launch_dependents();
     grid_wait();
     const int g = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
     const int G = hq / hkv;
-    const int pos = rope.cs ? *rope.pos_dev : -1;
-    const int L = rope.cs ? pos + 1 : *len_dev;
+    // The live length comes from device memory: clamp it to the cache
+    // capacity so that a bad value can never read (or, with the fused
+    // append, write) outside the caches; a position beyond them is skipped.
+    const int pos_raw = rope.cs ? *rope.pos_dev : -1;
+    const int pos = pos_raw < cap ? pos_raw : -1;
+    const int L = max(0, min(cap, rope.cs ? pos_raw + 1 : *len_dev));
     const int S = (L + nsplit - 1) / nsplit;
     const int k0 = split * S;
     const int nk_all = max(0, min(S, L - k0));
@@ -147,8 +151,8 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         __syncthreads();
         if (rope.cs) {
             const int half = rope.rot / 2;
-            const float* csp = rope.cs + (size_t)pos * half * 2;
-            if (t0 == 0) {
+            const float* csp = rope.cs + (size_t)max(pos_raw < cap ? pos_raw : 0, 0) * half * 2;
+            if (t0 == 0 && pos_raw >= 0 && pos_raw < cap) {
                 // rotate this CTA's query heads (NeoX split halves)
                 for (int i = tid; i < G * half; i += kDecThreads) {
                     const int h = i / half, pp = i - h * half;
@@ -160,7 +164,7 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
                 }
             }
             const int r = pos - (k0 + t0);
-            if (r >= 0 && r < nk) {
+            if (pos >= 0 && r >= 0 && r < nk) {
                 // the current position's key: rotate, cache it, use it in the tile
                 const float* kn = rope.k + (size_t)g * d;
                 float* kw = rope.kc + (size_t)pos * kvd + (size_t)g * d;
@@ -230,7 +234,7 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         cp_async_wait<0>();  // V
         if (rope.cs) {
             const int r = pos - (k0 + t0);
-            if (r >= 0 && r < nk) {
+            if (pos >= 0 && r >= 0 && r < nk) {
                 const float* vn = rope.v + (size_t)g * d;
                 float* vw = rope.vc + (size_t)pos * kvd + (size_t)g * d;
                 for (int c = tid; c < d; c += kDecThreads) {
@@ -442,7 +446,7 @@ static int attn_decode_launch(const float* q, const float* k_cache, const float*
         }
     }
     if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), smem, stream, q, k_cache, v_cache,
-                   len_dev, q_heads, kv_heads, head_dim, scale, part, rope) != cudaSuccess)
+                   len_dev, max_len, q_heads, kv_heads, head_dim, scale, part, rope) != cudaSuccess)
         return CL_ERR_CUDA;
     return launch_pdl(attn_decode_combine, dim3(q_heads), dim3(head_dim), 0, stream, part, splits, head_dim, out, xq,
                       q_heads * head_dim) == cudaSuccess

@@ -331,3 +331,18 @@ def test_attention_decode_with_fused_rope_matches_separate_calls(cuda, hq, hkv, 
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+
+
+def test_attention_decode_clamps_length_to_capacity(cuda):
+    """A device-side length beyond the cache capacity is clamped to it (the
+    kernel never reads outside the caches): same result as length = capacity."""
+    hq, hkv, d, cap = 8, 2, 64, 96
+    g = torch.Generator(device="cpu").manual_seed(5)
+    q = torch.randn(hq * d, generator=g).cuda()
+    kc = torch.randn(cap, hkv * d, generator=g).cuda()
+    vc = torch.randn(cap, hkv * d, generator=g).cuda()
+    scale = 1.0 / math.sqrt(d)
+    want = K.attn_decode(q, kc, vc, cap, cap, hq, hkv, d, scale)
+    got = K.attn_decode(q, kc, vc, cap + 100, cap, hq, hkv, d, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
