@@ -61,11 +61,11 @@ CL_DEVINL float warp_sum8(float (&v)[8], int lane) {
     return r;
 }
 
-// Dynamic smem: q [G][d] | K tile [64][d + 4] | V tile [64][d] | p [G][64] |
+// Dynamic smem: q [G][d + 4] | K tile [64][d + 4] | V tile [64][d] | p [G][64] |
 //               PV partials [parts - 1][G][d] | running (m, l) [G][2] | rescale [G]
 __host__ __device__ inline size_t attn_decode_smem(int group, int d) {
     const int parts = max(1, kDecThreads / d);
-    return sizeof(float) * ((size_t)group * d + (size_t)kTileKeys * (d + 4) + (size_t)kTileKeys * d +
+    return sizeof(float) * ((size_t)group * (d + 4) + (size_t)kTileKeys * (d + 4) + (size_t)kTileKeys * d +
                             (size_t)group * kTileKeys + (size_t)(parts - 1) * group * d + 3 * group);
 }
 
@@ -115,8 +115,9 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
     const int tid = threadIdx.x;
     extern __shared__ __align__(16) float sm[];
     const int parts = max(1, kDecThreads / d);
-    float* qs = sm;                        // [G][d]
-    float* ks = qs + G * d;                // [64][d + 4]
+    float* qs = sm;                        // [G][d + 4]: rows padded like K (query heads on
+                                           // different banks in the score loop)
+    float* ks = qs + G * kld;              // [64][d + 4]
     float* vs = ks + kTileKeys * kld;      // [64][d]
     float* ps = vs + kTileKeys * d;        // [G][64]
     float* pv = ps + G * kTileKeys;        // [parts - 1][G][d]
@@ -132,7 +133,10 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         run[2 * tid] = -INFINITY;
         run[2 * tid + 1] = 0.0f;
     }
-    for (int i = tid; i < G * d4; i += kDecThreads) cp_async16(qs + 4 * i, q + (size_t)g * G * d + 4 * i);
+    for (int i = tid; i < G * d4; i += kDecThreads) {
+        const int h = i / d4, c = i - h * d4;
+        cp_async16(qs + h * kld + 4 * c, q + (size_t)g * G * d + 4 * i);
+    }
     cp_async_commit();
     for (int t0 = 0; t0 < nk_all; t0 += kTileKeys) {
         const int nk = min(kTileKeys, nk_all - t0);
@@ -156,7 +160,7 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
                 // rotate this CTA's query heads (NeoX split halves)
                 for (int i = tid; i < G * half; i += kDecThreads) {
                     const int h = i / half, pp = i - h * half;
-                    float* qh = qs + h * d;
+                    float* qh = qs + h * kld;
                     const float c = csp[2 * pp], sn = csp[2 * pp + 1];
                     const float a = qh[pp], b = qh[pp + half];
                     qh[pp] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
@@ -197,7 +201,7 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
         for (int pidx = tid; pidx < nk * G; pidx += kDecThreads) {
             const int t = pidx / G, h = pidx - t * G;
             const float4* kr = reinterpret_cast<const float4*>(ks + t * kld);
-            const float4* qr = reinterpret_cast<const float4*>(qs + h * d);
+            const float4* qr = reinterpret_cast<const float4*>(qs + h * kld);
             float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
 #pragma unroll 8
             for (int c = 0; c < d4; ++c) {
