@@ -9,10 +9,11 @@
 // exact in integers and only the per-super-block sums scaled in FP32.
 //
 // Why the tensor cores at batch 1 (measured on B200): the per-row dp4a form
-// needs ~24 dp4a + masks + scale decode per row and 32 columns, i.e. more
-// issue slots per HBM byte than a B200 SM has at 6.5 TB/s.  Here one
-// mma.sync.m16n8k32 (u8 weights x s8 activations, s32 accumulate) replaces
-// 16 rows x 32 columns x 4 limbs of dp4a work.
+// needs ~24 dp4a + masks + scale decode per row and 32 columns, close to the
+// issue slots a B200 SM has per HBM byte at 6.5 TB/s (it measured 0.38 of the
+// HBM roofline).  Here one mma.sync.m16n8k32 (u8 weights x s8 activations,
+// s32 accumulate) replaces 16 rows x 32 columns x 4 limbs of dp4a work: a
+// 16-row Q4_K super-block costs 133 warp instructions.
 //
 // Activation encoding (XQ4, built in shared memory by every CTA): per
 // 256-element block b a scale s_b = max|x| / 127 and four signed 8-bit limbs
@@ -42,17 +43,17 @@
 // Every lane then holds one sub-block and scales by its int8 sc.
 //
 // Kernel shape: persistent CTAs, one producer warp + 16 consumer warps.  The
-// producer streams 16-row tiles (a K-chunk of each row per stage) into a
-// shared-memory ring with cp.async.bulk (mbarrier completion, bounded waits);
-// consumer warps take the stage's super-blocks round-robin, and the warps'
-// partial rows are summed in shared memory at the end of each tile.  Weights
-// are immutable, so the producer starts before the programmatic-dependent-
-// launch wait; consumers wait before reading x.
+// producer streams 16-row tiles (whole rows per stage where they fit, else an
+// equal K-chunk of each row) into a shared-memory ring with cp.async.bulk
+// (mbarrier completion, bounded waits, every wait taken by the whole warp);
+// consumer warps take the stage's super-blocks round-robin, and the last warp
+// to finish a tile (a shared-memory ticket) sums the warps' partial rows in
+// warp order.  Weights are immutable, so the producer starts before the
+// programmatic-dependent-launch wait; consumers wait before reading x.
 #include "common.cuh"
 #include "launch.cuh"
 
 #include <algorithm>
-#include <map>
 #include <mutex>
 
 namespace cl {
@@ -146,7 +147,8 @@ CL_DEVINL void mma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
-// Per-lane constants of the Q4_K consumer.
+// Per-lane constants of a consumer lane (Q4_K; the Q6_K copy has no 1/16
+// factor in lw0/lw1).
 struct Q4Lane {
     uint32_t sh;     // 12 * h: header shift that puts unit (2gi + h)'s slot at a fixed bit
     float lw0, lw1;  // weights of the lane's two limb columns (1/16 for high-nibble units)
