@@ -6,7 +6,7 @@ on seeded synthetic GGUF models written by myllm_b200.synth_gguf, and
 stores tokens and logits.  The GGUF SHA-256 is stored with each fixture so a
 test can tell when the generator no longer reproduces the same file.
 
-    python tests/golden/make_golden.py [--skip-05b]
+    python tests/golden/make_golden.py [--skip-05b] [--only-7b]
 
 Fixtures:
   tiny_s{seed}.npz   every format on some tensor (hidden 256, 2 layers),
@@ -17,6 +17,11 @@ Fixtures:
   qwen2_05b.npz      BASELINE config 0 (Qwen2.5-0.5B shape): 16-token prompt,
                      prefill + 4 decodes; tokens, top-64 logits, every 16th
                      logit, max |logit| and the top-1/top-2 margin per step.
+  qwen2_7b.npz       BASELINE config 2 (Qwen2.5-7B shape, the bench workload's
+                     model): 8-token prompt, prefill + 2 decodes, the same
+                     summary as qwen2_05b.  The reference holds ~35 GB of FP32
+                     weights, so the harness and the CPULLM cross-check run
+                     one after the other (--only-7b makes just this one).
 """
 from __future__ import annotations
 
@@ -52,6 +57,44 @@ def run_reference(path: str, prompt: np.ndarray, steps: int):
     assert t == tokens, (t, tokens)
     cpu.close()
     return ref, np.array(tokens, dtype=np.int32), np.stack(logits)
+
+
+def run_reference_sequential(path: str, prompt: np.ndarray, steps: int):
+    """run_reference for models whose FP32 weights fit in host memory only
+    once: the harness is closed before CPULLM cross-checks its tokens."""
+    ref = oracle.ReferenceCPU(path)
+    tok, lg = ref.prefill(prompt)
+    tokens, logits = [tok], [lg]
+    for _ in range(steps):
+        tok, lg = ref.decode(tok)
+        tokens.append(tok)
+        logits.append(lg)
+    ref.close()
+    cpu = oracle.ReferenceCPULLM(path)
+    t = [cpu.prefill(prompt)]
+    for _ in range(steps):
+        t.append(cpu.decode(t[-1]))
+    cpu.close()
+    assert t == tokens, (t, tokens)
+    return np.array(tokens, dtype=np.int32), np.stack(logits)
+
+
+def summary(logits: np.ndarray) -> dict:
+    order = np.argsort(-logits, axis=1, kind="stable")[:, :64]
+    srt = np.sort(logits, axis=1)
+    return dict(top_idx=order.astype(np.int32), top_val=np.take_along_axis(logits, order, axis=1).astype(np.float32),
+                stride16=logits[:, ::16].astype(np.float32), maxabs=np.abs(logits).max(axis=1).astype(np.float32),
+                margin=(srt[:, -1] - srt[:, -2]).astype(np.float32))
+
+
+def qwen2_7b(tmp: str) -> None:
+    spec = sg.CONFIGS["qwen2.5-7b"]
+    path = os.path.join(tmp, "q7b.gguf")
+    sha = sg.write_qwen2(spec, path)
+    prompt = sg.prompt_ids(spec.seed, 8, spec.vocab)
+    toks, logits = run_reference_sequential(path, prompt, 2)
+    np.savez_compressed(os.path.join(HERE, "qwen2_7b.npz"), sha256=np.array(sha), prompt=prompt, tokens=toks,
+                        **summary(logits))
 
 
 def tiny(seed: int, tmp: str) -> None:
@@ -109,9 +152,14 @@ def qwen2_05b(tmp: str) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-05b", action="store_true")
+    ap.add_argument("--only-7b", action="store_true")
     args = ap.parse_args()
     if not oracle.ref_available():
         oracle.build()
+    if args.only_7b:
+        with tempfile.TemporaryDirectory(dir=os.environ.get("MYLLM_GOLDEN_TMP")) as tmp:
+            qwen2_7b(tmp)
+        return
     with tempfile.TemporaryDirectory() as tmp:
         for seed in (7, 11):
             tiny(seed, tmp)
