@@ -81,6 +81,33 @@ struct ParallelConfig {
     std::array<char, 128> nccl_id{};
 };
 
+// One rank's tensor-parallel share of a qwen2 model: the split CudaLLM loads
+// and computes with (world == 1: everything on the one rank).
+//  * query and KV heads: an even split (world must divide both counts);
+//  * gate / up rows and ffn_down input columns: contiguous shares of the
+//    256-column block grid, the lower ranks taking the extra blocks;
+//  * o_proj input columns: this rank's heads when their columns start and end
+//    on the o_proj block grid (o_block: the widest column block among the
+//    layers' attn_output types), otherwise a contiguous share of that grid over
+//    the all-gathered attention output (gather_attn);
+//  * LM-head rows: contiguous shares of the vocabulary, uneven by one row.
+// Rank 0 always holds a non-empty share of every split, so it can add the
+// residual; a later rank's share may be empty (fewer blocks than ranks).
+struct TensorParallelShard {
+    std::size_t q_head0 = 0, q_heads = 0;
+    std::size_t kv_head0 = 0, kv_heads = 0;
+    std::size_t ffn0 = 0, ffn_rows = 0;
+    std::size_t o_col0 = 0, o_cols = 0;
+    bool gather_attn = false;
+    std::size_t vocab0 = 0, vocab_rows = 0;
+};
+
+// Throws std::invalid_argument for a rank / world or a shape the split does
+// not take.  Host only: needs no GPU.
+TensorParallelShard plan_tensor_parallel(std::size_t feed_forward, std::size_t vocabulary, std::size_t heads,
+                                         std::size_t kv_heads, std::size_t head_size, std::size_t o_block, int world,
+                                         int rank);
+
 class CudaLLM {
 public:
     // device < 0 uses the current CUDA device.

@@ -25,6 +25,14 @@ struct ExpertCacheStats {
     std::uint64_t requests() const noexcept { return hits + misses; }
 };
 
+// Expert-parallel placement: routed expert e lives on rank e % world, stacked
+// in expert order (local index e / world); layer l's shared expert runs on
+// rank l % world.  The device kernels (cl_moe_expert_gemv, cl_moe_combine)
+// apply the same rule to the expert ids they read.
+inline int ep_expert_rank(std::size_t expert, int world) noexcept { return (int)(expert % (std::size_t)world); }
+inline std::size_t ep_local_index(std::size_t expert, int world) noexcept { return expert / (std::size_t)world; }
+inline int ep_shared_rank(std::size_t layer, int world) noexcept { return (int)(layer % (std::size_t)world); }
+
 class CudaMoeLLM {
 public:
     // parallel.world > 1: expert parallel — expert e lives on rank

@@ -64,6 +64,31 @@ CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path)
 CUDALLM_API int cudallm_disable_profiling(cudallm_model* m);
 CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n);
 
+/* Multi-GPU placement, host only (no GPU needed): the shards cudallm_create
+ * loads on each rank.  No counterpart in the reference, which runs on one GPU;
+ * these make the split inspectable by harnesses and CPU tests.
+ *
+ * Tensor parallel (qwen2): rank `rank` of `world` holds query heads
+ * [q_head0, q_head0 + q_heads) and KV heads [kv_head0, kv_head0 + kv_heads)
+ * (Q/K/V rows of those heads), gate/up rows and ffn_down input columns
+ * [ffn0, ffn0 + ffn_rows), o_proj input columns [o_col0, o_col0 + o_cols) (of
+ * the all-gathered attention output when gather_attn), and LM-head rows
+ * [vocab0, vocab0 + vocab_rows).  o_block: the widest column block of the
+ * layers' attn_output types (256 for K-quants, 32 for Q5_0 / Q8_0, 1 for F32). */
+typedef struct cudallm_tp_shard {
+    uint64_t q_head0, q_heads, kv_head0, kv_heads;
+    uint64_t ffn0, ffn_rows, o_col0, o_cols, vocab0, vocab_rows;
+    int32_t gather_attn;
+} cudallm_tp_shard;
+CUDALLM_API int cudallm_tp_plan(uint64_t feed_forward, uint64_t vocabulary, uint64_t heads, uint64_t kv_heads,
+                                uint64_t head_size, uint64_t o_block, int world, int rank, cudallm_tp_shard* out);
+/* Expert parallel (qwen35moe): expert_rank[e] / expert_local[e] = the rank
+ * holding routed expert e and its index in that rank's stacked expert
+ * tensors, for e < experts; shared_rank[l] = the rank running layer l's
+ * shared expert, for l < layers.  Any output may be NULL. */
+CUDALLM_API int cudallm_ep_plan(uint64_t experts, uint64_t layers, int world, int32_t* expert_rank,
+                                int32_t* expert_local, int32_t* shared_rank);
+
 #ifdef __cplusplus
 }
 #endif

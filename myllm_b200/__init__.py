@@ -6,7 +6,7 @@
 Python mirror of that interface.
 """
 from .llm import (BackendError, CudaLLM, InvalidArgument, LengthError, MemoryStats, ModelConfig, OutOfRange,
-                  nccl_unique_id)
+                  TensorParallelShard, ep_plan, nccl_unique_id, tp_plan)
 
 __all__ = ["CudaLLM", "InvalidArgument", "OutOfRange", "LengthError", "BackendError", "MemoryStats",
-           "ModelConfig", "nccl_unique_id"]
+           "ModelConfig", "nccl_unique_id", "TensorParallelShard", "tp_plan", "ep_plan"]

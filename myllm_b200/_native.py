@@ -17,6 +17,13 @@ c_int, c_ll, c_size, c_float, c_vp, c_char_p = (ctypes.c_int, ctypes.c_longlong,
                                                 ctypes.c_float, ctypes.c_void_p, ctypes.c_char_p)
 
 
+class TpShard(ctypes.Structure):
+    """cudallm_tp_shard (include/cudallm.h)."""
+    _fields_ = [(n, ctypes.c_uint64) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "ffn0", "ffn_rows",
+                                               "o_col0", "o_cols", "vocab0", "vocab_rows")] + [
+        ("gather_attn", ctypes.c_int32)]
+
+
 class GemvSegment(ctypes.Structure):
     _fields_ = [("type", c_int), ("w", c_vp), ("stride", c_ll), ("n", c_int), ("bias", c_vp),
                 ("residual", c_vp), ("y", c_vp)]
@@ -86,6 +93,8 @@ SIGNATURES = {
     "cudallm_enable_profiling": (c_int, [c_vp, c_char_p]),
     "cudallm_disable_profiling": (c_int, [c_vp]),
     "cudallm_device_name": (c_int, [c_vp, c_vp, c_size]),
+    "cudallm_tp_plan": (c_int, [ctypes.c_uint64] * 6 + [c_int, c_int, c_vp]),
+    "cudallm_ep_plan": (c_int, [ctypes.c_uint64, ctypes.c_uint64, c_int, c_vp, c_vp, c_vp]),
 }
 
 

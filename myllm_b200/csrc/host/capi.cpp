@@ -197,4 +197,27 @@ CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n)
     });
 }
 
+CUDALLM_API int cudallm_tp_plan(uint64_t feed_forward, uint64_t vocabulary, uint64_t heads, uint64_t kv_heads,
+                                uint64_t head_size, uint64_t o_block, int world, int rank, cudallm_tp_shard* out) {
+    return guard([&] {
+        need(out);
+        const cudallm::TensorParallelShard s =
+            cudallm::plan_tensor_parallel(feed_forward, vocabulary, heads, kv_heads, head_size, o_block, world, rank);
+        *out = cudallm_tp_shard{s.q_head0, s.q_heads, s.kv_head0, s.kv_heads, s.ffn0,   s.ffn_rows,
+                                s.o_col0,  s.o_cols,  s.vocab0,   s.vocab_rows, s.gather_attn ? 1 : 0};
+    });
+}
+
+CUDALLM_API int cudallm_ep_plan(uint64_t experts, uint64_t layers, int world, int32_t* expert_rank,
+                                int32_t* expert_local, int32_t* shared_rank) {
+    return guard([&] {
+        if (world < 1) throw std::invalid_argument("invalid parallel world");
+        for (uint64_t e = 0; e < experts; ++e) {
+            if (expert_rank) expert_rank[e] = cudallm::ep_expert_rank(e, world);
+            if (expert_local) expert_local[e] = (int32_t)cudallm::ep_local_index(e, world);
+        }
+        for (uint64_t l = 0; l < layers && shared_rank; ++l) shared_rank[l] = cudallm::ep_shared_rank(l, world);
+    });
+}
+
 }  // extern "C"

@@ -114,6 +114,46 @@ std::size_t block_cols(int type) {
 
 }  // namespace
 
+TensorParallelShard plan_tensor_parallel(std::size_t F, std::size_t V, std::size_t hq, std::size_t hkv, std::size_t d,
+                                         std::size_t o_block, int W, int R) {
+    if (W < 1 || R < 0 || R >= W) throw std::invalid_argument("invalid parallel rank/world");
+    if (hq == 0 || hkv == 0 || hkv % W != 0 || hq % W != 0)
+        throw std::invalid_argument("tensor-parallel world must divide the query and KV head counts");
+    if (o_block == 0 || (hq * d) % o_block != 0)
+        throw std::invalid_argument("attention output width is not a multiple of the o_proj block");
+    TensorParallelShard s;
+    s.q_heads = hq / W;
+    s.q_head0 = R * s.q_heads;
+    s.kv_heads = hkv / W;
+    s.kv_head0 = R * s.kv_heads;
+    s.ffn_rows = F;
+    s.o_cols = hq * d;
+    s.vocab_rows = V;
+    if (W == 1) return s;
+    // FFN rows split on the widest block grid both formats share.
+    const std::size_t blk = 256;
+    if (F % blk) throw std::invalid_argument("FFN width must be a multiple of 256 for tensor parallelism");
+    auto fr = split_range(F / blk, W, R);
+    s.ffn0 = fr.first * blk;
+    s.ffn_rows = (fr.second - fr.first) * blk;
+    // o_proj input columns: the local heads when they are block aligned,
+    // otherwise a block-aligned share of the all-gathered output.
+    const std::size_t heads_cols = s.q_heads * d;
+    if (heads_cols % o_block == 0) {
+        s.o_col0 = R * heads_cols;
+        s.o_cols = heads_cols;
+    } else {
+        s.gather_attn = true;
+        auto orng = split_range(hq * d / o_block, W, R);
+        s.o_col0 = orng.first * o_block;
+        s.o_cols = (orng.second - orng.first) * o_block;
+    }
+    auto vr = split_range(V, W, R);
+    s.vocab0 = vr.first;
+    s.vocab_rows = vr.second - vr.first;
+    return s;
+}
+
 struct CudaLLM::Impl {
     ModelConfig config;
     ParallelConfig par;
@@ -169,49 +209,24 @@ struct CudaLLM::Impl {
         if (stream) cudaStreamDestroy(stream);
     }
 
-    void plan_shards() {
-        const int W = par.world, R = par.rank;
+    // o_block: the widest column block among the layers' attn_output types.
+    void plan_shards(std::size_t o_block) {
         H = config.embedding_size;
         F = config.feed_forward_size;
         V = config.vocabulary_size;
         d = config.head_size;
         hq = config.attention_head_count;
         hkv = config.kv_head_count;
-        if (W < 1 || R < 0 || R >= W) throw std::invalid_argument("invalid parallel rank/world");
-        if (hkv % W != 0 || hq % W != 0)
-            throw std::invalid_argument("tensor-parallel world must divide the query and KV head counts");
-        hq_l = hq / W;
-        hkv_l = hkv / W;
-        ffn0 = 0;
-        F_l = F;
-        o_k0 = 0;
-        o_kl = hq * d;
-        vocab0 = 0;
-        V_l = V;
-        gather_attn = false;
-        if (W > 1) {
-            // FFN rows split on the widest block grid both formats share.
-            const std::size_t blk = 256;
-            if (F % blk) throw std::invalid_argument("FFN width must be a multiple of 256 for tensor parallelism");
-            auto fr = split_range(F / blk, W, R);
-            ffn0 = fr.first * blk;
-            F_l = (fr.second - fr.first) * blk;
-            // o_proj input columns: the local heads when block aligned,
-            // otherwise a block-aligned share of the all-gathered output.
-            const std::size_t heads_cols = hq_l * d;
-            if (heads_cols % blk == 0) {
-                o_k0 = R * heads_cols;
-                o_kl = heads_cols;
-            } else {
-                gather_attn = true;
-                auto orng = split_range(hq * d / blk, W, R);
-                o_k0 = orng.first * blk;
-                o_kl = (orng.second - orng.first) * blk;
-            }
-            auto vr = split_range(V, W, R);
-            vocab0 = vr.first;
-            V_l = vr.second - vr.first;
-        }
+        const TensorParallelShard sh = plan_tensor_parallel(F, V, hq, hkv, d, o_block, par.world, par.rank);
+        hq_l = sh.q_heads;
+        hkv_l = sh.kv_heads;
+        ffn0 = sh.ffn0;
+        F_l = sh.ffn_rows;
+        o_k0 = sh.o_col0;
+        o_kl = sh.o_cols;
+        gather_attn = sh.gather_attn;
+        vocab0 = sh.vocab0;
+        V_l = sh.vocab_rows;
     }
 
     // Planning pass (arena base null) then the real pass with the same calls.
@@ -332,7 +347,12 @@ struct CudaLLM::Impl {
             else if (v != "tf32x3" && !v.empty())
                 throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be tf32x3, f16 or simt");
         }
-        plan_shards();
+        std::size_t o_block = 1;
+        for (std::size_t l = 0; l < config.layer_count; ++l) {
+            const std::string name = "blk." + std::to_string(l) + ".attn_output.weight";
+            if (file.has_tensor(name)) o_block = std::max(o_block, block_cols((int)file.require(name).type));
+        }
+        plan_shards(o_block);
 
         if (par.world > 1) {
             ncclUniqueId id;

@@ -235,7 +235,8 @@ struct CudaMoeLLM::Impl {
             }
             L.router = wl.matrix_f32(p + "ffn_gate_inp.weight", E, H);
             std::vector<WeightLoader::Part> g, u, dn;
-            for (std::size_t e = (std::size_t)R; e < E; e += (std::size_t)W) {
+            for (std::size_t e = 0; e < E; ++e) {
+                if (ep_expert_rank(e, W) != R) continue;
                 g.push_back({p + "ffn_gate_exps.weight", E * FF, H, e * FF, (e + 1) * FF});
                 u.push_back({p + "ffn_up_exps.weight", E * FF, H, e * FF, (e + 1) * FF});
                 dn.push_back({p + "ffn_down_exps.weight", E * H, FF, e * H, (e + 1) * H});
@@ -350,7 +351,7 @@ struct CudaMoeLLM::Impl {
         kc = config.ssm_conv_kernel;
         qkvw = 2 * sg * sd + config.ssm_inner_size;
         E_l = 0;
-        for (std::size_t e = (std::size_t)par.rank; e < E; e += (std::size_t)par.world) ++E_l;
+        for (std::size_t e = 0; e < E; ++e) E_l += ep_expert_rank(e, par.world) == par.rank;
         if (sd > 128) throw std::runtime_error("DeltaNet state size above 128 is not supported");
         if (d > 256 || d % 32) throw std::runtime_error("attention head size must be a multiple of 32 up to 256");
 
@@ -451,7 +452,7 @@ struct CudaMoeLLM::Impl {
                 CUDALLM_CL(cl_moe_expert_gemv(L.down_e.type, L.down_e.ptr, nullptr, L.down_e.stride, (int)H, (int)FF,
                                               ea, (int)FF, ids, (int)Kr, R, W, ey, s));
             }
-            const bool shared_here = (int)(l % (std::size_t)W) == R;
+            const bool shared_here = ep_shared_rank(l, W) == R;
             if (shared_here) {
                 CUDALLM_CL(cl_gemv_f32(L.shared_router, 1, (int)H, xn, sh_logit, s));
                 CUDALLM_CL(cl_gemv_swiglu(L.sh_gate.type, L.sh_gate.ptr, L.sh_up.ptr, L.sh_gate.stride, (int)SFF,

@@ -83,6 +83,43 @@ def nccl_unique_id() -> bytes:
     return buf.raw
 
 
+@dataclass
+class TensorParallelShard:
+    """One rank's share of a tensor-parallel qwen2 model (``cudallm_tp_plan``):
+    half-open ranges of query / KV heads, FFN rows (= ffn_down input columns),
+    o_proj input columns (of the all-gathered attention output when
+    ``gather_attn``) and LM-head rows."""
+    q_heads: range
+    kv_heads: range
+    ffn_rows: range
+    o_cols: range
+    vocab_rows: range
+    gather_attn: bool
+
+
+def tp_plan(feed_forward: int, vocabulary: int, heads: int, kv_heads: int, head_size: int, o_block: int,
+            world: int, rank: int) -> TensorParallelShard:
+    """The shard ``CudaLLM(..., rank=rank, world=world)`` loads (no GPU needed).
+    ``o_block`` is the widest column block of the layers' attn_output types."""
+    s = _native.TpShard()
+    _check(_native.lib().cudallm_tp_plan(feed_forward, vocabulary, heads, kv_heads, head_size, o_block, world, rank,
+                                         ctypes.byref(s)))
+    r = lambda a, n: range(a, a + n)  # noqa: E731
+    return TensorParallelShard(r(s.q_head0, s.q_heads), r(s.kv_head0, s.kv_heads), r(s.ffn0, s.ffn_rows),
+                               r(s.o_col0, s.o_cols), r(s.vocab0, s.vocab_rows), bool(s.gather_attn))
+
+
+def ep_plan(experts: int, layers: int, world: int):
+    """Expert-parallel placement (``cudallm_ep_plan``): arrays (rank of each
+    routed expert, its index in that rank's stacked expert tensors, rank of
+    each layer's shared expert)."""
+    er = np.empty(experts, dtype=np.int32)
+    el = np.empty(experts, dtype=np.int32)
+    sr = np.empty(layers, dtype=np.int32)
+    _check(_native.lib().cudallm_ep_plan(experts, layers, world, er.ctypes.data, el.ctypes.data, sr.ctypes.data))
+    return er, el, sr
+
+
 class CudaLLM:
     """qwen2 GGUF model on one GPU, or tensor-parallel over ``world`` GPUs."""
 
