@@ -11,7 +11,9 @@ Weights are seeded synthetic values (no public checkpoint is involved).  A
 step is one greedy decode token; `value` is decode tokens/s of the whole job
 from device time (CUDA events, max over ranks); `e2e` is the same metric from
 the public CudaLLM.decode() call, host to host.  The 4.4 GB (7B) weight set is
-far larger than the 126 MB L2, so no flush is needed between steps.
+far larger than the 126 MB L2, so no flush is needed between steps.  The
+N = 1 line also carries `scaling_base`: the N > 1 workload (14B) on one GPU,
+the same-model denominator for the scaling series.
 """
 from __future__ import annotations
 
@@ -42,6 +44,8 @@ def parse():
     ap.add_argument("--kernel-iters", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 kernel sweep (N = 1 only)")
+    ap.add_argument("--no-scaling-base", action="store_true",
+                    help="skip the single-GPU run of the N > 1 workload (N = 1 only)")
     return ap.parse_args()
 
 
@@ -307,6 +311,39 @@ def ensure_model(name, rank, world, dist):
     return spec, path
 
 
+def scaling_base(args, device: int):
+    """The N > 1 workload (the 14B shape, tensor-parallel there) on this one
+    GPU, timed like the main run (CUDA events per decode call, summed over the
+    steps): the same-model N = 1 point of the scaling series, since the N = 1
+    headline is the 7B shape, whose 4 KV heads do not split 8 ways."""
+    from myllm_b200 import CudaLLM
+    from myllm_b200 import synth_gguf as sg
+    name = model_name(args, 2)
+    try:
+        spec, path = ensure_model(name, 0, 1, None)
+        llm = CudaLLM(path, max_sequence=args.max_sequence, device=device)
+        prompt = sg.prompt_ids(spec.seed, args.prompt, spec.vocab)
+        llm.prefill(prompt)
+        llm.reset()
+        tok = llm.prefill(prompt)
+        prefill_ms = llm.last_call_ms()
+        for _ in range(args.warmup):
+            tok = llm.decode(tok)
+        dev_ms = 0.0
+        for _ in range(args.steps):
+            tok = llm.decode(tok)
+            dev_ms += llm.last_call_ms()
+        llm.close()
+    except Exception as e:  # reported in the line; the headline numbers stand
+        return {"workload": name, "unavailable": f"{type(e).__name__}: {e}"}
+    mid = args.prompt + args.warmup + args.steps // 2
+    ms_step = dev_ms / args.steps
+    return {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
+            "parallelism": "single GPU", "value": args.steps / (dev_ms / 1e3), "unit": "tokens/s",
+            "ms_per_step": ms_step, "prefill_tokens_per_s": args.prompt / (prefill_ms / 1e3),
+            "decode_hbm_gbs": decode_bytes_per_token(spec, mid) / (ms_step * 1e-3) / 1e9}
+
+
 def bench_cuda(args):
     import torch
     import torch.distributed as dist
@@ -376,6 +413,7 @@ def bench_cuda(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
+    base = scaling_base(args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     # embed; per layer: QKV GEMV (one launch per run of one format or of a
     # fused format pair), attention split (with RoPE and the KV append) +
     # combine, o, gate/up, down; final head GEMV, argmax, counter
@@ -412,6 +450,7 @@ def bench_cuda(args):
                      "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
         "cpu_baseline": cpu,
         "kernel_sweep": sweep,
+        "scaling_base": base,
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }

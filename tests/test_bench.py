@@ -47,3 +47,54 @@ def test_sweep_shapes_are_the_config1_shapes():
     assert (18944, 3584) in bench.SWEEP_SHAPES and (3584, 18944) in bench.SWEEP_SHAPES
     # K-quants skip K = 896 (not a multiple of their 256-element blocks)
     assert 896 % sg.BLOCK[sg.Q4_K][0] != 0
+
+
+class _FakeLLM:
+    """Stands in for CudaLLM: every call 'takes' 2 ms of device time."""
+
+    def __init__(self, path, max_sequence=0, device=0):
+        self.calls = 0
+
+    def prefill(self, ids):
+        return 1
+
+    def reset(self):
+        pass
+
+    def decode(self, tok):
+        self.calls += 1
+        return tok
+
+    def last_call_ms(self):
+        return 2.0
+
+    def close(self):
+        pass
+
+
+def _args(**kw):
+    import argparse
+    base = dict(gpus=1, steps=8, warmup=3, prompt=16, max_sequence=64, model=None, no_scaling_base=False)
+    base.update(kw)
+    return argparse.Namespace(**base)
+
+
+def test_scaling_base_times_the_multi_gpu_workload_on_one_gpu(monkeypatch):
+    import myllm_b200
+    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
+    out = bench.scaling_base(_args(), 0)
+    assert out["workload"].startswith("qwen2.5-14b") and out["parallelism"] == "single GPU"
+    assert out["value"] == 8 / (8 * 2.0 / 1e3) and out["ms_per_step"] == 2.0
+    assert out["prefill_tokens_per_s"] == 16 / 2e-3
+
+
+def test_scaling_base_failure_is_reported_not_raised(monkeypatch):
+    import myllm_b200
+
+    def boom(*a, **k):
+        raise RuntimeError("no device")
+    monkeypatch.setattr(myllm_b200, "CudaLLM", boom)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
+    out = bench.scaling_base(_args(), 0)
+    assert out["unavailable"] == "RuntimeError: no device"
