@@ -7,6 +7,8 @@ prefill tok/s, GEMV HBM GB/s against the measured HBM peak).
 Workload: N = 1 runs BASELINE config 2 (Qwen2.5-7B architecture, Q4_K_M
 layout, 512-token prompt, greedy decode against a 4096-slot KV cache); N > 1
 runs config 3 (Qwen2.5-14B architecture) tensor-parallel over the N ranks.
+`--model qwen3.6-35b-a3b --prompt 64 --steps 64 --max-sequence 1024` runs
+config 4 (qwen35moe), expert-parallel over the N ranks.
 Weights are seeded synthetic values (no public checkpoint is involved).  A
 step is one greedy decode token; `value` is decode tokens/s of the whole job
 from device time (CUDA events, max over ranks); `e2e` is the same metric from
@@ -178,6 +180,96 @@ def decode_bytes_per_token(spec, position: int) -> int:
     return total
 
 
+def moe_decode_bytes(spec, position: int):
+    """Algorithmic HBM bytes of one qwen35moe decode token at `position`, as
+    (replicated, expert): `replicated` is read by every expert-parallel rank
+    (embedding row, attention / DeltaNet weights, the F32 router, norms, the
+    LM head, the KV rows 0..position of the attention layers, each DeltaNet
+    state and convolution history read and written once); `expert` is the
+    top-k routed experts' gate/up/down rows plus the shared expert, spread
+    over the ranks."""
+    from myllm_b200 import synth_gguf as sg
+    t = sg.moe_a3b_types
+    H, E, FF, SFF = spec.hidden, spec.experts, spec.expert_ffn, spec.shared_ffn
+    qw, kvw = spec.heads * spec.head_dim, spec.kv_heads * spec.head_dim
+    rep = sg.row_bytes(sg.Q4_K, H) + spec.vocab * sg.row_bytes(sg.Q6_K, H) + 4 * H
+    exp = 0
+    for l in range(spec.layers):
+        rep += 4 * 2 * H + E * H * 4                          # norms + F32 router
+        if spec.is_attention(l):
+            rep += 2 * qw * sg.row_bytes(t(l, "attn_q"), H) + kvw * sg.row_bytes(t(l, "attn_k"), H)
+            rep += kvw * sg.row_bytes(t(l, "attn_v"), H) + H * sg.row_bytes(t(l, "attn_output"), qw)
+            rep += 4 * 2 * spec.head_dim + 2 * (position + 1) * kvw * 4
+        else:
+            rep += spec.qkv_width * sg.row_bytes(t(l, "attn_qkv"), H)
+            rep += spec.ssm_inner * sg.row_bytes(t(l, "attn_gate"), H)
+            rep += 2 * spec.ssm_rank * H * 4 + spec.qkv_width * spec.conv_kernel * 4
+            rep += 4 * (2 * spec.ssm_rank + spec.ssm_state)
+            rep += H * sg.row_bytes(t(l, "ssm_out"), spec.ssm_inner)
+            rep += 2 * 4 * spec.ssm_rank * spec.ssm_state * spec.ssm_state  # state read + write
+            rep += 2 * 4 * (spec.conv_kernel - 1) * spec.qkv_width          # conv history
+        exp += spec.experts_used * (FF * sg.row_bytes(t(l, "ffn_gate_exps"), H)
+                                    + FF * sg.row_bytes(t(l, "ffn_up_exps"), H)
+                                    + H * sg.row_bytes(t(l, "ffn_down_exps"), FF))
+        exp += 4 * H + SFF * sg.row_bytes(t(l, "ffn_gate_shexp"), H) + SFF * sg.row_bytes(t(l, "ffn_up_shexp"), H)
+        exp += H * sg.row_bytes(t(l, "ffn_down_shexp"), SFF)
+    return rep, exp
+
+
+def moe_launches_per_step(spec, world: int, rank: int) -> int:
+    """Kernels one qwen35moe decode step launches on `rank` (NCCL's own
+    kernels not counted): the graph recorded by CudaMoeLLM's decode."""
+    from myllm_b200 import synth_gguf as sg
+    t = sg.moe_a3b_types
+    n = 1                                                       # embed
+    for l in range(spec.layers):
+        n += 1                                                  # attn_norm
+        if spec.is_attention(l):
+            # q/gate + k + v GEMV, gate prep, attention split + combine, gate, o_proj
+            n += gemv_launches([t(l, "attn_q"), t(l, "attn_k"), t(l, "attn_v")]) + 1 + 2 + 1 + 1
+        else:
+            # qkv + z GEMV, alpha, beta, prep, recurrence step, out GEMV
+            n += gemv_launches([t(l, "attn_qkv"), t(l, "attn_gate")]) + 2 + 1 + 1 + 1
+        n += 1 + 1 + 1                                          # post norm, router, top-k
+        if any(e % world == rank for e in range(spec.experts)):
+            n += 2                                              # routed gate/up, down
+        if l % world == rank:
+            n += 3                                              # shared router, gate/up, down
+        n += 1 if world == 1 else 2                             # combine (+ residual add)
+    return n + 3                                                # head GEMV, argmax, counter
+
+
+def time_head_kernel(spec, iters: int):
+    """Device time of the LM-head GEMV (RMSNorm fused; the largest single
+    weight read of a qwen35moe token) timed alone with CUDA events on the
+    launching stream; two weight copies alternate (2 x 417 MB > 126 MB L2)."""
+    import torch
+    from myllm_b200 import kernels as K
+    from myllm_b200 import synth_gguf as sg
+    H, V, gtype = spec.hidden, spec.vocab, sg.Q6_K
+    w = K.repack(gtype, sg.fill(gtype, V, H, sg.stream_key(spec.seed, "bench_head"), 0.0, 0.02), H)
+    ws = [w, w.clone()]
+    x = torch.randn(H, device="cuda")
+    gamma = torch.ones(H, device="cuda")
+    y = torch.empty(V, device="cuda")
+    for i in range(4):
+        K.gemv_multi([(gtype, ws[i % 2], V, None, None, y)], H, x, gamma, 1e-6)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(iters):
+        K.gemv_multi([(gtype, ws[i % 2], V, None, None, y)], H, x, gamma, 1e-6)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    algo = V * sg.row_bytes(gtype, H) + 2 * 4 * H + 4 * V
+    del ws, w
+    return {"kernel": "gemv_mma_kernel<Q6_K> (RMSNorm + LM-head GEMV on mma.sync)",
+            "shape": f"[{V},{H}] Q6_K", "bytes_per_launch": algo, "avg_launch_us": ms * 1e3,
+            "gbs": algo / (ms * 1e-3) / 1e9}
+
+
 def time_gateup_kernel(spec, iters: int):
     """Device time of the dominant decode kernel (fused gate/up GEMV with
     SwiGLU over the FFN rows) on the model's shapes and formats, timed alone
@@ -300,12 +392,21 @@ def dist_setup(args):
     return world, rank, local
 
 
-def ensure_model(name, rank, world, dist):
+def model_spec(name):
+    """(spec, writer) of a synthetic qwen2 or qwen35moe config."""
     from myllm_b200 import synth_gguf as sg
-    spec = sg.CONFIGS[name]
+    if name in sg.MOE_CONFIGS:
+        return sg.MOE_CONFIGS[name], sg.cached_moe
+    if name in sg.CONFIGS:
+        return sg.CONFIGS[name], sg.cached_qwen2
+    raise SystemExit(f"unknown model {name!r}: one of {sorted(sg.CONFIGS) + sorted(sg.MOE_CONFIGS)}")
+
+
+def ensure_model(name, rank, world, dist):
+    spec, writer = model_spec(name)
     path = os.path.join(MODEL_DIR, f"{spec.name}.gguf")
     if rank == 0 and not os.path.exists(path):
-        sg.cached_qwen2(spec, MODEL_DIR)
+        writer(spec, MODEL_DIR)
     if world > 1:
         dist.barrier()
     return spec, path
@@ -398,9 +499,10 @@ def bench_cuda(args):
     dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms = [float(v) for v in vals.cpu()]
     llm.close()
 
+    moe = isinstance(spec, sg.MoeSpec)
     peak, peak_kind = measured_peaks()
-    kern = time_gateup_kernel(spec, args.kernel_iters)
-    sweep = kernel_sweep(peak, spec.seed) if world == 1 and not args.no_sweep else None
+    kern = time_head_kernel(spec, args.kernel_iters) if moe else time_gateup_kernel(spec, args.kernel_iters)
+    sweep = kernel_sweep(peak, spec.seed) if world == 1 and not args.no_sweep and not moe else None
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -408,17 +510,28 @@ def bench_cuda(args):
             dist.destroy_process_group()
         return
     mid = args.prompt + args.warmup + args.steps // 2
-    tok_bytes = decode_bytes_per_token(spec, mid) / world
+    if moe:
+        rep, exp = moe_decode_bytes(spec, mid)
+        tok_bytes = rep + exp / world
+    else:
+        tok_bytes = decode_bytes_per_token(spec, mid) / world
     ms_step = dev_ms / args.steps
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if moe:
+        cpu = {"value": None, "unavailable": "the reference has no CPU qwen35moe path (its parity oracle is the "
+                                             "FP64 restatement, not a timed baseline)"}
+    elif world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path)
     base = scaling_base(args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     # embed; per layer: QKV GEMV (one launch per run of one format or of a
     # fused format pair), attention split (with RoPE and the KV append) +
     # combine, o, gate/up, down; final head GEMV, argmax, counter
-    qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")]) for l in range(spec.layers))
-    launches_per_step = 1 + qkv + 5 * spec.layers + 3
+    if moe:
+        launches_per_step = moe_launches_per_step(spec, world, rank)
+    else:
+        qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")])
+                  for l in range(spec.layers))
+        launches_per_step = 1 + qkv + 5 * spec.layers + 3
     line = {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),
@@ -433,8 +546,9 @@ def bench_cuda(args):
         "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
         "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
         "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
-                   "layers": spec.layers, "hidden": spec.hidden, "ffn": spec.ffn, "vocab": spec.vocab,
-                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "layers": spec.layers, "hidden": spec.hidden,
+                   "ffn": spec.expert_ffn if moe else spec.ffn, "vocab": spec.vocab,
+                   "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
                    "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"},
         "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
@@ -444,7 +558,7 @@ def bench_cuda(args):
                        "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
                        "peak_kind": peak_kind},
         "roofline": {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": kern["gbs"] / peak, "traffic": profile_traffic("gemv_gateup"),
+                     "frac": kern["gbs"] / peak, "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
                      "kernel": kern["kernel"], "shape": kern["shape"],
                      "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
                      "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
@@ -465,10 +579,11 @@ def bench_reference(args):
         return
     name = model_name(args, world)
     from myllm_b200 import synth_gguf as sg
-    spec = sg.CONFIGS[name]
-    path = os.path.join(MODEL_DIR, f"{spec.name}.gguf")
-    if not os.path.exists(path):
-        sg.cached_qwen2(spec, MODEL_DIR)
+    if name in sg.MOE_CONFIGS:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's qwen35moe path is Metal-only "
+                                                             "(no CPU implementation to run here)"}))
+        return
+    spec, path = ensure_model(name, 0, 1, None)
     from oracle import cpu_baseline
     steps = min(args.steps, 4)
     warm = min(args.warmup, 1)

@@ -98,3 +98,33 @@ def test_scaling_base_failure_is_reported_not_raised(monkeypatch):
     monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
     out = bench.scaling_base(_args(), 0)
     assert out["unavailable"] == "RuntimeError: no device"
+
+
+def test_moe_bytes_per_token():
+    spec = sg.MOE_CONFIGS["qwen3.6-35b-a3b"]
+    rep, exp = bench.moe_decode_bytes(spec, 0)
+    # the active weights of one token: about 2.2 GB for the real file, plus the
+    # F32 routers (84 MB) and the DeltaNet state read + write (126 MB) counted here
+    assert 2.2e9 < rep + exp < 2.5e9
+    # one more position reads one more K and V row in each attention layer
+    attn = sum(spec.is_attention(l) for l in range(spec.layers))
+    rep1, exp1 = bench.moe_decode_bytes(spec, 1)
+    assert rep1 - rep == attn * 2 * spec.kv_heads * spec.head_dim * 4 and exp1 == exp
+    # routed experts scale with the number used per token
+    half = sg.MoeSpec(**{**spec.__dict__, "experts_used": spec.experts_used // 2})
+    shared = exp - 2 * (exp - bench.moe_decode_bytes(half, 0)[1])
+    assert 0 < shared < exp / 4
+
+
+def test_moe_launch_count_per_rank():
+    spec = sg.tiny_moe_spec(layers=8, experts=16)
+    attn = sum(spec.is_attention(l) for l in range(spec.layers))
+    # one GPU: attention layers 6 + the q/k/v GEMV launches, DeltaNet 7, MoE 9
+    qkv = [bench.gemv_launches([sg.moe_a3b_types(l, t) for t in ("attn_q", "attn_k", "attn_v")])
+           for l in range(spec.layers) if spec.is_attention(l)]
+    assert bench.moe_launches_per_step(spec, 1, 0) == 1 + sum(6 + q for q in qkv) + 7 * (8 - attn) + 9 * 8 + 3
+    # two ranks: the shared expert on every other layer, plus the residual add
+    assert bench.moe_launches_per_step(spec, 2, 0) == bench.moe_launches_per_step(spec, 1, 0) - 3 * 4 + 8
+    # more ranks than experts: a rank without experts skips the routed GEMVs
+    assert bench.moe_launches_per_step(sg.tiny_moe_spec(experts=2, used=2), 4, 3) < \
+        bench.moe_launches_per_step(sg.tiny_moe_spec(experts=2, used=2), 4, 1)
