@@ -445,6 +445,43 @@ def scaling_base(args, device: int):
             "decode_hbm_gbs": decode_bytes_per_token(spec, mid) / (ms_step * 1e-3) / 1e9}
 
 
+def time_allreduce(n_floats: int, iters: int, dist) -> float:
+    """Device time (µs, max over ranks) of one NCCL all-reduce (sum) of
+    n_floats FP32 values: torch.distributed's NCCL group, the calls enqueued
+    back to back from the host and bracketed by CUDA events on the current
+    stream. Every rank makes the same calls."""
+    import torch
+    x = torch.ones(n_floats, device="cuda")
+    for _ in range(5):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    works = [dist.all_reduce(x, async_op=True) for _ in range(iters)]
+    for w in works:
+        w.wait()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def tp_collectives_per_token(spec, world: int) -> dict:
+    """Collectives of one tensor-parallel decode token: an all-reduce after
+    o_proj and after ffn_down in every layer, an all-gather of the attention
+    output before o_proj when the shard plan says so, and the LM head's
+    (value, index) all-gather."""
+    from myllm_b200 import synth_gguf as sg
+    from myllm_b200 import tp_plan
+    d = spec.hidden // spec.heads
+    o_block = max(sg.BLOCK[spec.types(l, "attn_output")][0] for l in range(spec.layers))
+    gather = tp_plan(spec.ffn, spec.vocab, spec.heads, spec.kv_heads, d, o_block, world, 0).gather_attn
+    return {"all_reduce": 2 * spec.layers, "all_gather": (spec.layers if gather else 0) + 1,
+            "all_reduce_bytes": 4 * spec.hidden}
+
+
 def bench_cuda(args):
     import torch
     import torch.distributed as dist
@@ -498,6 +535,18 @@ def bench_cuda(args):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms = [float(v) for v in vals.cpu()]
     llm.close()
+    collectives = None
+    if world > 1:
+        if isinstance(spec, sg.MoeSpec):  # one all-reduce of the MoE output per layer
+            collectives = {"all_reduce": spec.layers, "all_gather": 0, "all_reduce_bytes": 4 * spec.hidden}
+        else:
+            collectives = tp_collectives_per_token(spec, world)
+        us = time_allreduce(spec.hidden, 200, dist)
+        ms_all_reduce = us * collectives["all_reduce"] / 1e3
+        collectives.update({"all_reduce_us": us, "all_reduce_ms_per_token": ms_all_reduce,
+                            "share_of_step": ms_all_reduce / (dev_ms / args.steps),
+                            "note": "torch.distributed NCCL all-reduce of the same size, host-launched back to "
+                                    "back; the model's own calls run inside its decode CUDA graph"})
 
     moe = isinstance(spec, sg.MoeSpec)
     peak, peak_kind = measured_peaks()
@@ -565,6 +614,7 @@ def bench_cuda(args):
         "cpu_baseline": cpu,
         "kernel_sweep": sweep,
         "scaling_base": base,
+        "collectives": collectives,
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
     }

@@ -128,3 +128,12 @@ def test_moe_launch_count_per_rank():
     # more ranks than experts: a rank without experts skips the routed GEMVs
     assert bench.moe_launches_per_step(sg.tiny_moe_spec(experts=2, used=2), 4, 3) < \
         bench.moe_launches_per_step(sg.tiny_moe_spec(experts=2, used=2), 4, 1)
+
+
+def test_tp_collectives_per_token():
+    spec = sg.CONFIGS["qwen2.5-14b"]
+    # two all-reduces per layer; the attention output is all-gathered only at
+    # 8 ranks (5 heads x 128 columns are off the 256-column o_proj grid)
+    for world, gathers in ((2, 1), (4, 1), (8, spec.layers + 1)):
+        c = bench.tp_collectives_per_token(spec, world)
+        assert c == {"all_reduce": 2 * spec.layers, "all_gather": gathers, "all_reduce_bytes": 4 * 5120}
