@@ -209,6 +209,30 @@ CL_API int cl_argmax_merge(const float* records, int n, int32_t* token, cudaStre
  * captured decode graph). */
 CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
 
+/* ---- tensor-parallel exchange over peer memory --------------------------- */
+/* One-shot all-reduce (sum) of a decode-size FP32 vector across up to 8 ranks
+ * of one node, through exchange buffers that every rank maps from every
+ * other (CUDA IPC over NVLink / NVSwitch).  It replaces the NCCL all-reduce
+ * after the row-split o_proj and ffn_down products of a tensor-parallel
+ * decode token; the reference has no multi-GPU path (its layer computes the
+ * unsplit products, cpu_llm.cpp:774-914).
+ *
+ * Each rank allocates one buffer of cl_peer_exchange_bytes(max_n) bytes with
+ * cudaMalloc (256-byte aligned), zeroes its header once with
+ * cl_peer_exchange_init before any rank's first call, and shares it by IPC
+ * handle.  buffers[r] = rank r's buffer as mapped in this process
+ * (buffers[rank] = its own).  Every rank makes the same calls in the same
+ * order.  n % 4 == 0, n <= max_n (the max_n the buffers were sized for), in
+ * and out 16-byte aligned and not overlapping.  out receives the sum in rank
+ * order 0..world-1, bit-identical on every rank.  A rank that waits more than
+ * 20 s for the others sets the buffer's status word
+ * (cl_peer_exchange_status: a device address; 0 = ok) and returns. */
+CL_API size_t cl_peer_exchange_bytes(int max_n);
+CL_API int cl_peer_exchange_init(void* buffer, int max_n, cudaStream_t stream);
+CL_API const int* cl_peer_exchange_status(const void* buffer);
+CL_API int cl_peer_allreduce(const float* in, float* out, int n, int max_n, int rank, int world,
+                             void* const* buffers, cudaStream_t stream);
+
 /* ---- qwen35moe ---------------------------------------------------------- */
 /* y[n] = W[n,k] x for an FP32 row-major W (the router, DeltaNet alpha/beta
  * and shared-expert gate products, encode_product on F32 tensors,

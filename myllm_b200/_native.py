@@ -76,6 +76,10 @@ SIGNATURES = {
                                   c_vp, c_vp, c_vp, c_vp, c_vp]),
     "cl_mul_sigmoid": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp]),
     "cl_select_token": (c_int, [c_vp, c_vp, c_vp, c_vp]),
+    "cl_peer_exchange_bytes": (c_size, [c_int]),
+    "cl_peer_exchange_init": (c_int, [c_vp, c_int, c_vp]),
+    "cl_peer_exchange_status": (c_vp, [c_vp]),
+    "cl_peer_allreduce": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     # backend
     "cudallm_last_error": (c_char_p, []),
     "cudallm_nccl_unique_id": (c_int, [c_vp]),

@@ -194,7 +194,13 @@ struct CudaLLM::Impl {
           *A_full = nullptr, *G = nullptr, *U = nullptr, *P = nullptr;
     int32_t* ids_dev = nullptr;
 
-    PinnedBuffer host_io;  // [0] token in, [1] token out, [2..] ids staging
+    PinnedBuffer host_io;  // [0] token in, [1] token out, [2] exchange status, [4..] ids staging
+
+    // Decode all-reduce through peer memory (CUDALLM_ALLREDUCE=p2p): this
+    // rank's exchange buffer and every rank's buffer as mapped here.
+    DeviceBuffer peer_buf;
+    std::vector<void*> peer_bufs;
+    bool peer_allreduce = false;
     cudaGraphExec_t decode_exec = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
@@ -202,6 +208,8 @@ struct CudaLLM::Impl {
     bool have_logits = false;
 
     ~Impl() {
+        for (std::size_t r = 0; r < peer_bufs.size(); ++r)
+            if ((int)r != par.rank && peer_bufs[r]) cudaIpcCloseMemHandle(peer_bufs[r]);
         if (decode_exec) cudaGraphExecDestroy(decode_exec);
         if (comm) ncclCommDestroy(comm);
         if (ev0) cudaEventDestroy(ev0);
@@ -358,6 +366,14 @@ struct CudaLLM::Impl {
             ncclUniqueId id;
             std::memcpy(&id, par.nccl_id.data(), sizeof(id));
             CUDALLM_NCCL(ncclCommInitRank(&comm, par.world, id, par.rank));
+            // decode all-reduce: "nccl" (default) or "p2p" (cl_peer_allreduce)
+            if (const char* e = std::getenv("CUDALLM_ALLREDUCE")) {
+                const std::string v(e);
+                if (v == "p2p")
+                    setup_peer_exchange();
+                else if (v != "nccl" && !v.empty())
+                    throw std::invalid_argument("CUDALLM_ALLREDUCE must be nccl or p2p");
+            }
         }
 
         Arena plan;
@@ -397,6 +413,43 @@ struct CudaLLM::Impl {
 
     void all_reduce(float* send, float* recv, std::size_t n) {
         CUDALLM_NCCL(ncclAllReduce(send, recv, n, ncclFloat32, ncclSum, comm, stream));
+    }
+
+    // The [hidden] all-reduces of a decode step.
+    void decode_all_reduce(float* send, float* recv) {
+        if (peer_allreduce)
+            CUDALLM_CL(cl_peer_allreduce(send, recv, (int)H, (int)H, par.rank, par.world, peer_bufs.data(), stream));
+        else
+            all_reduce(send, recv, H);
+    }
+
+    // Exchange buffers for decode_all_reduce: allocate and zero this rank's,
+    // all-gather the IPC handles over NCCL, map the others.  The all-gather
+    // also orders every rank's zeroing before any rank's first call.
+    void setup_peer_exchange() {
+        const int W = par.world, R = par.rank;
+        if (H % 4 != 0) throw std::invalid_argument("peer all-reduce needs a hidden size that is a multiple of 4");
+        peer_buf = DeviceBuffer(cl_peer_exchange_bytes((int)H));
+        CUDALLM_CL(cl_peer_exchange_init(peer_buf.get(), (int)H, stream));
+        cudaIpcMemHandle_t mine;
+        CUDALLM_CUDA(cudaIpcGetMemHandle(&mine, peer_buf.get()));
+        const std::size_t hb = sizeof(cudaIpcMemHandle_t);
+        DeviceBuffer handles(hb * W);
+        char* hd = static_cast<char*>(handles.get());
+        CUDALLM_CUDA(cudaMemcpyAsync(hd + R * hb, &mine, hb, cudaMemcpyHostToDevice, stream));
+        CUDALLM_NCCL(ncclAllGather(hd + R * hb, hd, hb, ncclChar, comm, stream));
+        std::vector<cudaIpcMemHandle_t> all(W);
+        CUDALLM_CUDA(cudaMemcpyAsync(all.data(), hd, hb * W, cudaMemcpyDeviceToHost, stream));
+        CUDALLM_CUDA(cudaStreamSynchronize(stream));
+        peer_bufs.assign(W, nullptr);
+        peer_bufs[R] = peer_buf.get();
+        for (int r = 0; r < W; ++r) {
+            if (r == R) continue;
+            void* p = nullptr;
+            CUDALLM_CUDA(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+            peer_bufs[r] = p;
+        }
+        peer_allreduce = true;
     }
 
     // Final RMSNorm + LM head + greedy token for the hidden row `hrow`.
@@ -447,20 +500,23 @@ struct CudaLLM::Impl {
                 CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, nullptr, res, out, s));
             else
                 CUDALLM_CUDA(cudaMemsetAsync(out, 0, H * sizeof(float), s));
-            if (W > 1) all_reduce(part, h, H);
+            if (W > 1) decode_all_reduce(part, h);
             if (F_l == 0) {
                 CUDALLM_CUDA(cudaMemsetAsync(out, 0, H * sizeof(float), s));
-                if (W > 1) all_reduce(part, h, H);
+                if (W > 1) decode_all_reduce(part, h);
                 continue;
             }
             CUDALLM_CL(cl_gemv_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, h, L.ffn_norm,
                                       eps(), act, s));
             CUDALLM_CL(cl_gemv(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, act, nullptr, res, out, s));
-            if (W > 1) all_reduce(part, h, H);
+            if (W > 1) decode_all_reduce(part, h);
         }
         record_head(h, ints + 3);
         CUDALLM_CL(cl_counter_add(pos, 2, 1, s));
         CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+        if (peer_allreduce)
+            CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 2, cl_peer_exchange_status(peer_buf.get()), sizeof(int32_t),
+                                         cudaMemcpyDeviceToHost, s));
     }
 
     void build_decode_graph() {
@@ -610,6 +666,8 @@ struct CudaLLM::Impl {
         begin_timing();
         CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
         end_timing("decode", 1);
+        if (peer_allreduce && host_in()[2] != 0)
+            throw std::runtime_error("peer all-reduce: a rank did not reach the decode step within the wait limit");
         position += 1;
         have_logits = true;
         return host_in()[1];

@@ -66,3 +66,32 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.cl_gemv(99, None, 0, 1, 256, None, None, None, None, None) == 1
     assert lib.cl_argmax(None, 10, None, None, 0, None) == 1
     assert lib.cl_status_string(4) == b"workspace missing or too small"
+
+
+def test_peer_exchange_layout_and_argument_checks():
+    """The tensor-parallel exchange buffer: a 256-byte header and two
+    parities of 8 rank slots, each rounded up to 64 floats; bad arguments are
+    rejected before anything touches a GPU."""
+    import ctypes
+    lib = _native.lib()
+    assert lib.cl_peer_exchange_bytes(0) == 0
+    assert lib.cl_peer_exchange_bytes(5120) == 256 + 2 * 8 * 5120 * 4
+    assert lib.cl_peer_exchange_bytes(100) == 256 + 2 * 8 * 128 * 4
+    assert lib.cl_peer_exchange_init(None, 5120, None) == 1
+    assert lib.cl_peer_exchange_init(4096 + 16, 5120, None) == 1  # not 256-byte aligned
+    assert lib.cl_peer_exchange_status(None) is None
+    assert lib.cl_peer_exchange_status(4096) == 4096 + 96  # after epoch[8] and flag[2][8]
+    bufs = (ctypes.c_void_p * 8)(*[4096 * (i + 1) for i in range(8)])
+    a, b = 1 << 20, 2 << 20
+    ok = dict(inp=a, out=b, n=5120, max_n=5120, rank=0, world=2)
+
+    def call(**kw):
+        p = {**ok, **kw}
+        return lib.cl_peer_allreduce(p["inp"], p["out"], p["n"], p["max_n"], p["rank"], p["world"], bufs, None)
+    assert call(n=5122) == 1                     # n % 4
+    assert call(n=6000) == 1                     # n > max_n
+    assert call(world=9) == 1 and call(world=0) == 1
+    assert call(rank=2) == 1
+    assert call(out=a + 64) == 1                 # overlapping in / out
+    assert call(inp=a + 4) == 1                  # unaligned
+    assert lib.cl_peer_allreduce(a, b, 5120, 5120, 0, 2, None, None) == 1
