@@ -64,6 +64,14 @@ CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path)
 CUDALLM_API int cudallm_disable_profiling(cudallm_model* m);
 CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n);
 
+/* Host only (no GPU needed): parse a GGUF file's header, metadata and tensor
+ * table without reading tensor data, the first step of cudallm_create.
+ * Writes general.architecture (NUL-terminated, cut to n - 1 bytes) and the
+ * tensor count (either may be NULL).  A malformed or truncated file returns
+ * CUDALLM_ERUNTIME with the reader's message, as the reference's readers
+ * throw std::runtime_error (model.cpp:376-448, metal_model.cpp:450-562). */
+CUDALLM_API int cudallm_gguf_inspect(const char* gguf_path, char* arch, size_t n, uint64_t* tensor_count);
+
 /* Multi-GPU placement, host only (no GPU needed): the shards cudallm_create
  * loads on each rank.  No counterpart in the reference, which runs on one GPU;
  * these make the split inspectable by harnesses and CPU tests.

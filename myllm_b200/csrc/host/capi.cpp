@@ -10,6 +10,7 @@
 
 #include "cuda_llm.h"
 #include "cuda_moe_llm.h"
+#include "gguf.h"
 
 #include <memory>
 
@@ -194,6 +195,20 @@ CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n)
         if (n == 0) throw std::invalid_argument("empty name buffer");
         std::strncpy(buf, s.c_str(), n - 1);
         buf[n - 1] = 0;
+    });
+}
+
+CUDALLM_API int cudallm_gguf_inspect(const char* gguf_path, char* arch, size_t n, uint64_t* tensor_count) {
+    return guard([&] {
+        need(gguf_path);
+        const cudallm::GgufFile f(gguf_path);
+        if (arch) {
+            if (n == 0) throw std::invalid_argument("empty architecture buffer");
+            const std::string a = f.text("general.architecture");
+            std::strncpy(arch, a.c_str(), n - 1);
+            arch[n - 1] = 0;
+        }
+        if (tensor_count) *tensor_count = f.tensors().size();
     });
 }
 

@@ -82,7 +82,11 @@ private:
     std::size_t pos_ = 0;
 };
 
-void skip_value(Cursor& c, uint32_t type) {
+// Arrays of arrays are legal GGUF, but no file this reader serves nests
+// them; the limit keeps a crafted chain from exhausting the stack.
+constexpr int kMaxArrayDepth = 8;
+
+void skip_value(Cursor& c, uint32_t type, int depth = 0) {
     switch (type) {
     case kU8: case kI8: case kBool: c.skip(1); break;
     case kU16: case kI16: c.skip(2); break;
@@ -90,9 +94,10 @@ void skip_value(Cursor& c, uint32_t type) {
     case kU64: case kI64: case kF64: c.skip(8); break;
     case kString: c.skip((std::size_t)c.get<uint64_t>()); break;
     case kArray: {
+        if (depth >= kMaxArrayDepth) throw std::runtime_error("GGUF metadata arrays nested too deeply");
         const uint32_t et = c.get<uint32_t>();
         const uint64_t n = c.get<uint64_t>();
-        for (uint64_t i = 0; i < n; ++i) skip_value(c, et);
+        for (uint64_t i = 0; i < n; ++i) skip_value(c, et, depth + 1);
         break;
     }
     default: throw std::runtime_error("unsupported GGUF metadata type " + std::to_string(type));
@@ -156,6 +161,12 @@ GgufFile::GgufFile(const std::string& path) : path_(path) {
         if (version != 2 && version != 3) throw std::runtime_error("unsupported GGUF version");
         const uint64_t n_tensors = c.get<uint64_t>();
         const uint64_t n_kv = c.get<uint64_t>();
+        // every metadata entry takes at least 12 bytes (key length, type) and
+        // every tensor descriptor at least 32 (name length, rank, one
+        // dimension, type, offset): counts beyond that are corrupt, and must
+        // not reach an allocation
+        if (n_kv > file_size_ / 12 || n_tensors > file_size_ / 32)
+            throw std::runtime_error("invalid GGUF header counts");
         for (uint64_t i = 0; i < n_kv; ++i) {
             const std::string key = c.str();
             const uint32_t type = c.get<uint32_t>();
