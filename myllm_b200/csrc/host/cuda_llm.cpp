@@ -22,6 +22,7 @@
 
 #include "device.h"
 #include "gguf.h"
+#include "profile.h"
 
 namespace cudallm {
 
@@ -204,7 +205,8 @@ struct CudaLLM::Impl {
     cudaGraphExec_t decode_exec = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
-    std::ofstream profile;
+    std::unique_ptr<ProfileCsv> profile;
+    std::chrono::steady_clock::time_point call_start;
     bool have_logits = false;
 
     ~Impl() {
@@ -607,15 +609,49 @@ struct CudaLLM::Impl {
         }
     }
 
-    void begin_timing() { CUDALLM_CUDA(cudaEventRecord(ev0, stream)); }
+    void begin_timing() {
+        call_start = std::chrono::steady_clock::now();
+        CUDALLM_CUDA(cudaEventRecord(ev0, stream));
+    }
+
+    // Logical, shape-derived FLOPs and bytes of a call on this rank: prefill
+    // of n tokens (n > 0) or one decode step (n == 0) at the current position.
+    ProfileMetrics call_metrics(std::size_t n) const {
+        std::uint64_t elems = 0;
+        for (const Layer& L : layers)
+            for (const DevMat* m : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+                elems += (std::uint64_t)m->rows * (std::uint64_t)m->cols;
+        const std::uint64_t head = (std::uint64_t)out_w.rows * (std::uint64_t)out_w.cols;
+        const std::uint64_t kv_row = 2 * hkv_l * d * sizeof(float) * layers.size();  // K and V, all layers
+        const std::uint64_t embed_row = V ? tok_embd.payload / V : 0;
+        const std::uint64_t weights = weight_payload - tok_embd.payload;
+        const std::uint64_t attn = 4 * d * hq_l * layers.size();  // QK and AV per (query, key)
+        ProfileMetrics m;
+        if (n > 0) {  // causal: query i reads keys 0..i
+            const std::uint64_t pairs = (std::uint64_t)n * (n + 1) / 2;
+            m.flops = 2 * n * elems + 2 * head + attn * pairs;
+            m.read_bytes = weights + n * embed_row + kv_row * pairs;
+            m.write_bytes = kv_row * n + 4 * (std::uint64_t)V_l;
+        } else {  // the new key at `position` and keys 0..position
+            const std::uint64_t keys = position + 1;
+            m.flops = 2 * (elems + head) + attn * keys;
+            m.read_bytes = weights + embed_row + kv_row * keys;
+            m.write_bytes = kv_row + 4 * (std::uint64_t)V_l;
+        }
+        return m;
+    }
 
     void end_timing(const char* phase, std::size_t tokens) {
         CUDALLM_CUDA(cudaEventRecord(ev1, stream));
         CUDALLM_CUDA(cudaEventSynchronize(ev1));
         CUDALLM_CUDA(cudaEventElapsedTime(&last_ms, ev0, ev1));
-        if (profile.is_open()) {
-            profile << phase << "," << tokens << "," << position << "," << last_ms << "\n";
-            profile.flush();
+        if (profile) {
+            const bool pre = std::strcmp(phase, "prefill") == 0;
+            const auto ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() -
+                                                                                 call_start);
+            // stage names of the reference's resident GPU path (metal_llm.mm:3219-3221, 3319-3321)
+            profile->forward(pre ? "prefill.gpu_resident" : "decode.gpu_resident", pre ? tokens : position + 1,
+                             (std::uint64_t)ns.count(), call_metrics(pre ? tokens : 0));
         }
     }
 
@@ -702,13 +738,12 @@ std::int32_t CudaLLM::decode(std::int32_t token_id) {
 
 void CudaLLM::enable_profiling(const std::string& csv_path, bool) {
     if (!impl_) throw std::runtime_error("CUDA model is not initialized");
-    impl_->profile = std::ofstream(csv_path);
-    if (!impl_->profile) throw std::runtime_error("cannot open profile CSV: " + csv_path);
-    impl_->profile << "phase,tokens,position,device_ms\n";
+    impl_->profile.reset();  // a previous file gets its summary rows first
+    impl_->profile = std::make_unique<ProfileCsv>(csv_path);
 }
 
 void CudaLLM::disable_profiling() {
-    if (impl_) impl_->profile.close();
+    if (impl_) impl_->profile.reset();
 }
 
 const ModelConfig& CudaLLM::config() const {

@@ -23,12 +23,14 @@
 #include <nccl.h>
 
 #include <cmath>
+#include <chrono>
 #include <cstring>
 #include <fstream>
 #include <stdexcept>
 
 #include "device.h"
 #include "gguf.h"
+#include "profile.h"
 
 namespace cudallm {
 
@@ -185,7 +187,8 @@ struct CudaMoeLLM::Impl {
     cudaGraphExec_t decode_exec = nullptr, prefill_exec = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
-    std::ofstream profile;
+    std::unique_ptr<ProfileCsv> profile;
+    std::chrono::steady_clock::time_point call_start;
     bool have_logits = false;
     std::uint64_t routed = 0;
 
@@ -512,15 +515,79 @@ struct CudaMoeLLM::Impl {
         return exec;
     }
 
-    void begin_timing() { CUDALLM_CUDA(cudaEventRecord(ev0, stream)); }
+    void begin_timing() {
+        call_start = std::chrono::steady_clock::now();
+        CUDALLM_CUDA(cudaEventRecord(ev0, stream));
+    }
+
+    // Logical, shape-derived FLOPs and bytes of one token through every layer
+    // on this rank with `keys` attention keys (routed experts: the expected
+    // share Kr * E_l / E of the routes; the shared expert where it runs).
+    ProfileMetrics token_metrics(std::size_t keys) const {
+        auto el = [](const DevMat& m) { return (std::uint64_t)m.rows * (std::uint64_t)m.cols; };
+        ProfileMetrics t;
+        const double routes = E ? (double)Kr * (double)E_l / (double)E : 0.0;
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            const MoeLayer& L = layers[l];
+            std::uint64_t e = 0, b = 0;
+            if (L.attention) {
+                for (const DevMat* m : {&L.q_gate, &L.k, &L.v, &L.o}) e += el(*m), b += m->payload;
+                t.flops += 4 * d * hq * keys;
+                b += 2 * keys * hkv * d * sizeof(float);
+                t.write_bytes += 2 * hkv * d * sizeof(float);
+            } else {
+                for (const DevMat* m : {&L.qkv, &L.z, &L.out}) e += el(*m), b += m->payload;
+                e += 2 * sr * H;                             // alpha, beta (F32)
+                b += (2 * sr * H + qkvw * kc) * sizeof(float);
+                const std::uint64_t state = sr * sd * sd * sizeof(float), hist = (kc - 1) * qkvw * sizeof(float);
+                t.flops += 8 * sr * sd * sd;                 // decay, prediction, update, output
+                b += state + hist;
+                t.write_bytes += state + hist;
+            }
+            e += E * H;  // router (F32)
+            b += E * H * sizeof(float);
+            if (E_l > 0) {
+                e += (std::uint64_t)(routes * (double)(el(L.gate_e) + el(L.up_e) + el(L.down_e)) / (double)E_l);
+                b += (std::uint64_t)(routes * (double)(L.gate_e.payload + L.up_e.payload + L.down_e.payload) /
+                                     (double)E_l);
+            }
+            if (ep_shared_rank(l, par.world) == par.rank)
+                for (const DevMat* m : {&L.sh_gate, &L.sh_up, &L.sh_down}) e += el(*m), b += m->payload;
+            t.flops += 2 * e;
+            t.read_bytes += b;
+        }
+        t.read_bytes += V ? tok_embd.payload / V : 0;  // one embedding row
+        return t;
+    }
+
+    // prefill of n tokens (n > 0; positions 0..n-1, then the LM head once) or
+    // one decode step at the current position (n == 0)
+    ProfileMetrics call_metrics(std::size_t n) const {
+        ProfileMetrics m;
+        const std::size_t first = n > 0 ? 0 : position, count = n > 0 ? n : 1;
+        for (std::size_t i = first; i < first + count; ++i) {
+            const ProfileMetrics t = token_metrics(i + 1);
+            m.flops += t.flops;
+            m.read_bytes += t.read_bytes;
+            m.write_bytes += t.write_bytes;
+        }
+        m.flops += 2 * (std::uint64_t)out_w.rows * (std::uint64_t)out_w.cols;
+        m.read_bytes += out_w.payload;
+        m.write_bytes += 4 * (std::uint64_t)V;
+        return m;
+    }
 
     void end_timing(const char* phase, std::size_t tokens) {
         CUDALLM_CUDA(cudaEventRecord(ev1, stream));
         CUDALLM_CUDA(cudaEventSynchronize(ev1));
         CUDALLM_CUDA(cudaEventElapsedTime(&last_ms, ev0, ev1));
-        if (profile.is_open()) {
-            profile << phase << "," << tokens << "," << position << "," << last_ms << "\n";
-            profile.flush();
+        if (profile) {
+            const bool pre = std::strcmp(phase, "prefill") == 0;
+            const auto ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() -
+                                                                                 call_start);
+            // stage names of the reference's MoE GPU path (moe_llm.mm:3086, 3136)
+            profile->forward(pre ? "prefill.gpu_moe" : "decode.gpu_moe", pre ? tokens : position + 1,
+                             (std::uint64_t)ns.count(), call_metrics(pre ? tokens : 0));
         }
     }
 
@@ -607,13 +674,12 @@ std::int32_t CudaMoeLLM::decode(std::int32_t token_id) {
 
 void CudaMoeLLM::enable_profiling(const std::string& csv_path, bool) {
     if (!impl_) throw std::runtime_error("CUDA model is not initialized");
-    impl_->profile = std::ofstream(csv_path);
-    if (!impl_->profile) throw std::runtime_error("cannot open profile CSV: " + csv_path);
-    impl_->profile << "phase,tokens,position,device_ms\n";
+    impl_->profile.reset();  // a previous file gets its summary rows first
+    impl_->profile = std::make_unique<ProfileCsv>(csv_path);
 }
 
 void CudaMoeLLM::disable_profiling() {
-    if (impl_) impl_->profile.close();
+    if (impl_) impl_->profile.reset();
 }
 
 const ModelConfig& CudaMoeLLM::config() const {

@@ -184,3 +184,28 @@ def test_qwen2_7b_parity(model_dir, cuda):
         assert max(err_top, err_s) / d["maxabs"][i] <= 1e-2
         assert max(err_top, err_s) / d["maxabs"][i] <= 1e-4
     llm.close()
+
+
+def test_profile_csv(tiny_models, tmp_path):
+    """enable_profiling writes the reference Profiler's CSV format: one
+    forward_total and one forward_stage row per call (stage names of the
+    reference's resident GPU path), global rows when profiling stops."""
+    import csv
+    path, d = tiny_models[7]
+    llm = CudaLLM(path, max_sequence=64)
+    out = str(tmp_path / "profile.csv")
+    llm.enable_profiling(out)
+    tok = llm.prefill(d["prompt8"])
+    for _ in range(2):
+        tok = llm.decode(tok)
+    llm.disable_profiling()
+    llm.close()
+    with open(out, newline="") as f:
+        rows = list(csv.DictReader(f))
+    stages = [(r["record_type"], r["stage"], r["sequence_tokens"]) for r in rows]
+    assert stages[:6] == [("forward_total", "forward.total", "8"), ("forward_stage", "prefill.gpu_resident", "8"),
+                          ("forward_total", "forward.total", "9"), ("forward_stage", "decode.gpu_resident", "9"),
+                          ("forward_total", "forward.total", "10"), ("forward_stage", "decode.gpu_resident", "10")]
+    assert sorted(r["stage"] for r in rows[6:]) == ["decode.gpu_resident", "forward.total", "prefill.gpu_resident"]
+    for r in rows:
+        assert int(r["flops"]) > 0 and int(r["read_bytes"]) > 0 and float(r["time_ms"]) > 0

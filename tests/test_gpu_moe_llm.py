@@ -114,3 +114,25 @@ def test_moe_expert_parallel_two_gpus(tiny_moe):
         assert toks == rtoks, r
         for i in range(len(toks)):
             assert rel(logits[i], rlogits[i]) <= 1e-3, (r, i)
+
+
+def test_moe_profile_csv(tiny_moe, tmp_path):
+    """The qwen35moe backend's profile CSV: the reference Profiler's format
+    with the stage names of the reference's MoE GPU path."""
+    import csv
+    spec, path = tiny_moe[5]
+    llm = CudaLLM(path, max_sequence=64)
+    out = str(tmp_path / "profile.csv")
+    llm.enable_profiling(out)
+    tok = llm.prefill(sg.prompt_ids(spec.seed, 12, spec.vocab))
+    llm.decode(tok)
+    llm.disable_profiling()
+    llm.close()
+    with open(out, newline="") as f:
+        rows = list(csv.DictReader(f))
+    assert [(r["stage"], r["sequence_tokens"]) for r in rows if r["record_type"] == "forward_stage"] == \
+        [("prefill.gpu_moe", "12"), ("decode.gpu_moe", "13")]
+    assert sorted(r["stage"] for r in rows if r["record_type"] == "global") == \
+        ["decode.gpu_moe", "forward.total", "prefill.gpu_moe"]
+    for r in rows:
+        assert int(r["flops"]) > 0 and int(r["read_bytes"]) > 0 and float(r["time_ms"]) > 0
