@@ -371,8 +371,39 @@ def kernel_sweep(peak_gbs: float, seed: int):
                     "the split-TF32 mode issues three tensor-core products per useful one"}
 
 
-def run_cpu_baseline(path: str, timeout: int = 900):
-    cmd = [sys.executable, "-m", "oracle.cpu_baseline", "--model", path, "--prompt", "4", "--decode", "2"]
+def reference_host_bytes(spec) -> int:
+    """Host memory the reference CPULLM holds for a qwen2 model: every tensor
+    dequantized to FP32 plus the file image it reads whole (model.cpp:392)."""
+    from myllm_b200 import synth_gguf as sg
+    tensors = sg.qwen2_tensors(spec)
+    return sum(4 * t.rows * t.cols + t.nbytes for t in tensors)
+
+
+def mem_available():
+    """MemAvailable of this host in bytes, or None where /proc/meminfo is absent."""
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return None
+
+
+def run_cpu_baseline(path: str, spec=None, prompt: int = 4, decode: int = 2, warmup: int = 0,
+                     timeout: int = 900):
+    """The reference CPULLM sample in a child process (oracle.cpu_baseline),
+    so that running out of host memory or time gives an `unavailable` record
+    instead of ending the bench."""
+    if spec is not None:
+        need, avail = reference_host_bytes(spec), mem_available()
+        if avail is not None and need > 0.9 * avail:
+            return {"value": None, "unavailable": f"the reference CPULLM holds FP32 weights and the file image: "
+                                                  f"~{need / 1e9:.0f} GB of host memory, {avail / 1e9:.0f} GB "
+                                                  f"available here"}
+    cmd = [sys.executable, "-m", "oracle.cpu_baseline", "--model", path, "--prompt", str(prompt),
+           "--decode", str(decode), "--warmup", str(warmup)]
     try:
         res = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=timeout)
     except subprocess.TimeoutExpired:
@@ -380,7 +411,9 @@ def run_cpu_baseline(path: str, timeout: int = 900):
     for line in res.stdout.splitlines()[::-1]:
         if line.startswith("{"):
             return json.loads(line)
-    return {"value": None, "unavailable": (res.stderr or res.stdout).strip().splitlines()[-1:] or "no output"}
+    tail = (res.stderr or res.stdout).strip().splitlines()[-1:]
+    return {"value": None, "unavailable": f"reference CPU sample exited with code {res.returncode}"
+                                          + (f": {tail[0]}" if tail else "")}
 
 
 def dist_setup(args):
@@ -570,7 +603,7 @@ def bench_cuda(args):
         cpu = {"value": None, "unavailable": "the reference has no CPU qwen35moe path (its parity oracle is the "
                                              "FP64 restatement, not a timed baseline)"}
     elif world == 1 and not args.no_cpu_baseline:
-        cpu = run_cpu_baseline(path)
+        cpu = run_cpu_baseline(path, spec)
     base = scaling_base(args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     # embed; per layer: QKV GEMV (one launch per run of one format or of a
     # fused format pair), attention split (with RoPE and the KV append) +
@@ -634,10 +667,9 @@ def bench_reference(args):
                                                              "(no CPU implementation to run here)"}))
         return
     spec, path = ensure_model(name, 0, 1, None)
-    from oracle import cpu_baseline
     steps = min(args.steps, 4)
     warm = min(args.warmup, 1)
-    res = cpu_baseline.measure(path, prompt=4, decode=steps, warmup=warm)
+    res = run_cpu_baseline(path, spec, prompt=4, decode=steps, warmup=warm, timeout=1800)
     if res.get("value") is None:
         print(json.dumps({"impl": "reference", "unavailable": res.get("unavailable", "reference CPU path failed")}))
         return

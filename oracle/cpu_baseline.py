@@ -4,7 +4,7 @@ sample of the benchmark workload: a short prefill and a few greedy decode
 steps, each timed with a monotonic clock around the call as chat.cpp:852-871
 does.  CPULLM is single-threaded, so one host core is used.
 
-    python -m oracle.cpu_baseline --model M.gguf --prompt 4 --decode 2
+    python -m oracle.cpu_baseline --model M.gguf --prompt 4 --decode 2 [--warmup 1]
 """
 from __future__ import annotations
 
@@ -45,8 +45,9 @@ def main():
     ap.add_argument("--model", required=True)
     ap.add_argument("--prompt", type=int, default=4)
     ap.add_argument("--decode", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=0)
     a = ap.parse_args()
-    print(json.dumps(measure(a.model, a.prompt, a.decode)))
+    print(json.dumps(measure(a.model, a.prompt, a.decode, a.warmup)))
 
 
 if __name__ == "__main__":

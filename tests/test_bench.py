@@ -137,3 +137,18 @@ def test_tp_collectives_per_token():
     for world, gathers in ((2, 1), (4, 1), (8, spec.layers + 1)):
         c = bench.tp_collectives_per_token(spec, world)
         assert c == {"all_reduce": 2 * spec.layers, "all_gather": gathers, "all_reduce_bytes": 4 * 5120}
+
+
+def test_reference_memory_guard(monkeypatch):
+    # CPULLM holds FP32 weights plus the file: ~35 GB (7B), ~68 GB (14B)
+    assert 34e9 < bench.reference_host_bytes(sg.CONFIGS["qwen2.5-7b"]) < 36e9
+    assert 67e9 < bench.reference_host_bytes(sg.CONFIGS["qwen2.5-14b"]) < 69e9
+    monkeypatch.setattr(bench, "mem_available", lambda: 16e9)
+    out = bench.run_cpu_baseline("unused.gguf", sg.CONFIGS["qwen2.5-14b"])
+    assert out["value"] is None and "~68 GB of host memory, 16 GB available" in out["unavailable"]
+
+
+def test_reference_sample_failure_is_reported(tmp_path):
+    # a child that fails (here: no such model) gives an `unavailable` record
+    out = bench.run_cpu_baseline(str(tmp_path / "absent.gguf"), timeout=300)
+    assert out["value"] is None and out["unavailable"]
