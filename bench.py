@@ -425,6 +425,18 @@ def dist_setup(args):
     return world, rank, local
 
 
+# The reference's own published decode rates for a workload this bench runs:
+# Qwen2.5-14B Q4_K_M batch-1 greedy decode on its Metal backend (Apple M4),
+# after its packed-byte Q4_K optimisation (METAL_14B_PROFILE.md:128-132).
+# No number is published for the other shapes.
+PUBLISHED_DECODE_TOK_S = {"qwen2.5-14b": 5.777}
+
+
+def vs_published(name, value):
+    ref = PUBLISHED_DECODE_TOK_S.get(name)
+    return value / ref if ref and value else None
+
+
 def model_spec(name):
     """(spec, writer) of a synthetic qwen2 or qwen35moe config."""
     from myllm_b200 import synth_gguf as sg
@@ -474,6 +486,7 @@ def scaling_base(args, device: int):
     ms_step = dev_ms / args.steps
     return {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
             "parallelism": "single GPU", "value": args.steps / (dev_ms / 1e3), "unit": "tokens/s",
+            "vs_baseline": vs_published(name, args.steps / (dev_ms / 1e3)),
             "ms_per_step": ms_step, "prefill_tokens_per_s": args.prompt / (prefill_ms / 1e3),
             "decode_hbm_gbs": decode_bytes_per_token(spec, mid) / (ms_step * 1e-3) / 1e9}
 
@@ -624,7 +637,7 @@ def bench_cuda(args):
         "ms_per_step": ms_step,
         "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": None,
+        "vs_baseline": vs_published(name, args.steps / (dev_ms / 1e3)),
         "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
         "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
         "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
@@ -684,7 +697,7 @@ def bench_reference(args):
         "ms_per_step": 1e3 / res["value"],
         "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": None,
+        "vs_baseline": vs_published(name, res["value"]),
         "dtype": "fp32 (reference dequantizes to FP32 at load)",
         "data": "synthetic (same seeded GGUF as the cuda arm)",
         "config": {"workload": f"{name} Q4_K_M, reference CPULLM, prompt 4 + {steps} decode tokens (bounded sample)",

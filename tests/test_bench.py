@@ -152,3 +152,9 @@ def test_reference_sample_failure_is_reported(tmp_path):
     # a child that fails (here: no such model) gives an `unavailable` record
     out = bench.run_cpu_baseline(str(tmp_path / "absent.gguf"), timeout=300)
     assert out["value"] is None and out["unavailable"]
+
+
+def test_vs_baseline_only_where_the_reference_publishes():
+    # 14B decode: the reference's Metal figure (5.777 tok/s); nothing for 7B
+    assert bench.vs_published("qwen2.5-14b", 57.77) == pytest.approx(10.0)
+    assert bench.vs_published("qwen2.5-7b", 466.0) is None
