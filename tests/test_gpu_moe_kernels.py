@@ -98,8 +98,10 @@ def test_moe_experts_end_to_end(cuda, gtype, world, rank):
     assert rel_err(out.cpu().numpy(), ref) <= 2e-5
 
 
-def test_gdn_prep_and_step(cuda):
-    G, R, D, KC, eps = 2, 4, 64, 4, 1e-6
+# small heads, then config 4's widths (16 key / 32 value heads, 128 x 128 state)
+@pytest.mark.parametrize("G,R,D", [(2, 4, 64), (16, 32, 128)])
+def test_gdn_prep_and_step(cuda, G, R, D):
+    KC, eps = 4, 1e-6
     W = (2 * G + R) * D
     qkv, alpha, beta_raw = rnd(W, 20), rnd(R, 21), rnd(R, 22)
     conv_w = rnd(0, 23, 0.5, (W, KC))
@@ -136,8 +138,10 @@ def test_gdn_prep_and_step(cuda):
     assert rel_err(state_d.cpu().numpy(), S) <= 2e-5
 
 
-def test_attn_gate_prep(cuda):
-    hq, hkv, d, rot, eps, pos, cap = 4, 2, 64, 32, 1e-6, 5, 8
+# small heads, then config 4's gated attention (16 / 2 heads of 256, RoPE on 64)
+@pytest.mark.parametrize("hq,hkv,d,rot", [(4, 2, 64, 32), (16, 2, 256, 64)])
+def test_attn_gate_prep(cuda, hq, hkv, d, rot):
+    eps, pos, cap = 1e-6, 5, 8
     mixed, kr, vr = rnd(2 * hq * d, 30), rnd(hkv * d, 31), rnd(hkv * d, 32)
     qn, kn = 1.0 + rnd(d, 33, 0.02), 1.0 + rnd(d, 34, 0.02)
     theta = 1e7
