@@ -30,3 +30,20 @@ def test_tensor_parallel_two_gpus_matches_reference(model_dir, cuda, n):
         assert toks == list(d[f"tokens{n}"]), r
         for i, ref in enumerate(d[f"logits{n}"]):
             assert rel(logits[i], ref) <= 1e-4, (r, i)
+
+
+def test_tensor_parallel_peer_allreduce(model_dir, cuda, monkeypatch):
+    """The decode all-reduces through cl_peer_allreduce (exchange buffers
+    mapped by CUDA IPC, rank-order sum) instead of NCCL: the same tokens and
+    logits as the reference, and bit-identical logits on both ranks."""
+    monkeypatch.setenv("CUDALLM_ALLREDUCE", "p2p")  # inherited by the spawned ranks
+    d = np.load(os.path.join(GOLDEN, "tiny_s7.npz"))
+    path = os.path.join(model_dir, "tiny_s7.gguf")
+    assert sg.write_qwen2(sg.tiny_spec(seed=7), path) == str(d["sha256"])
+    got = run_ranks(2, path, d["prompt8"], 4)
+    for r in (0, 1):
+        toks, logits = got[r]
+        assert toks == list(d["tokens8"]), r
+        for i, ref in enumerate(d["logits8"]):
+            assert rel(logits[i], ref) <= 1e-4, (r, i)
+    assert np.array_equal(got[0][1], got[1][1])
