@@ -415,6 +415,16 @@ MOE_CONFIGS: Dict[str, MoeSpec] = {
 }
 
 
+def a3b_width_spec(layers: int = 4, vocab: int = 4096, seed: int = 0xA3B4) -> MoeSpec:
+    """BASELINE config 4's layer widths (hidden 2048, 256 experts top-8 of
+    FFN 512 plus a shared expert, 16 / 2 attention heads of 256 with RoPE on
+    64, DeltaNet 16 key / 32 value heads of 128) in fewer layers and a
+    smaller vocabulary, so that an FP64 restatement runs it on a CPU: every
+    full-width operator of the model, at a fraction of its bytes."""
+    return dataclasses.replace(MOE_CONFIGS["qwen3.6-35b-a3b"], name=f"a3b-width-{layers}l", layers=layers,
+                               vocab=vocab, context=1024, seed=seed)
+
+
 def tiny_moe_spec(seed: int = 5, layers: int = 8, experts: int = 16, used: int = 4) -> MoeSpec:
     """Every qwen35moe operator at small sizes (K-quant rows stay 256-aligned)."""
     return MoeSpec(f"tiny-moe-s{seed}", hidden=256, layers=layers, experts=experts, experts_used=used,

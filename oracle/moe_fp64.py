@@ -99,6 +99,19 @@ class MoeFP64:
     def vec(self, name: str) -> np.ndarray:
         return self.w(name).reshape(-1)
 
+    def expert(self, name: str, e: int) -> np.ndarray:
+        """Expert e's rows of a stacked [experts * rows, cols] tensor, in
+        float64.  Dequantized on use and not cached: a token touches K of the
+        E experts, and a whole stack in float64 is gigabytes at full width.
+        GGML blocks lie within a row, so these rows equal the same rows of
+        the whole tensor's dequantization."""
+        gtype, rows, cols, data = self._r.rows(name)
+        per = rows // self.E
+        part = data[e * per:(e + 1) * per]
+        if gtype == 0:
+            return part.view(np.float32).reshape(per, cols).astype(np.float64)
+        return dequant(gtype, part, per, cols).astype(np.float64)
+
     def is_attention(self, l: int) -> bool:
         return (l + 1) % self.interval == 0
 
@@ -191,13 +204,11 @@ class MoeFP64:
     def _moe(self, l, x):
         p = f"blk.{l}."
         ids, wts = self.route(l, x)
-        ff = self.w(p + "ffn_gate_exps.weight").shape[0] // self.E
-        G, U, D = self.w(p + "ffn_gate_exps.weight"), self.w(p + "ffn_up_exps.weight"), self.w(p + "ffn_down_exps.weight")
         acc = np.zeros(self.H)
         for e, wt in zip(ids, wts):
-            g = G[e * ff:(e + 1) * ff] @ x
-            u = U[e * ff:(e + 1) * ff] @ x
-            acc += wt * (D[e * self.H:(e + 1) * self.H] @ (_silu(g) * u))
+            g = self.expert(p + "ffn_gate_exps.weight", e) @ x
+            u = self.expert(p + "ffn_up_exps.weight", e) @ x
+            acc += wt * (self.expert(p + "ffn_down_exps.weight", e) @ (_silu(g) * u))
         sgate = _sigmoid(self.vec(p + "ffn_gate_inp_shexp.weight") @ x)
         sa = _silu(self.w(p + "ffn_gate_shexp.weight") @ x) * (self.w(p + "ffn_up_shexp.weight") @ x)
         return acc + (self.w(p + "ffn_down_shexp.weight") @ sa) * sgate

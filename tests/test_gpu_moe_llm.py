@@ -136,3 +136,38 @@ def test_moe_profile_csv(tiny_moe, tmp_path):
         ["decode.gpu_moe", "forward.total", "prefill.gpu_moe"]
     for r in rows:
         assert int(r["flops"]) > 0 and int(r["read_bytes"]) > 0 and float(r["time_ms"]) > 0
+
+
+def test_moe_config4_widths_against_fp64_fixture(model_dir, cuda):
+    """Every config-4 width end to end: 256 experts top-8 of FFN 512 plus the
+    shared expert, gated attention of 16 / 2 heads of 256 with RoPE on 64,
+    DeltaNet of 16 key / 32 value heads of 128, hidden 2048, Q5_K o_proj.
+    4 layers and a 4096-word vocabulary keep the FP64 restatement's fixture
+    (tests/golden/make_moe_golden.py) affordable.
+
+    The decode steps are teacher-forced with the fixture's tokens, so that a
+    near-tie cannot make the rest diverge.  Logits must be within the spec's
+    1e-2 at every step.  The greedy token must be equal wherever the top-1 /
+    top-2 margin exceeds twice the step's observed error; a smaller margin
+    is tie-ambiguous, is reported, and does not count as a match."""
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "moe_a3b_width.npz"))
+    spec = sg.a3b_width_spec()
+    path = os.path.join(model_dir, f"{spec.name}.gguf")
+    # written afresh: the hash pins the generator the fixture was made with
+    assert sg.write_moe(spec, path) == str(d["sha256"])
+    llm = CudaLLM(path, max_sequence=64)
+    got = [(llm.prefill(d["prompt"]), llm.last_logits())]
+    for i in range(1, len(d["tokens"])):
+        got.append((llm.decode(int(d["tokens"][i - 1])), llm.last_logits()))
+    llm.close()
+    checked, ambiguous = 0, []
+    for i, (tok, logits) in enumerate(got):
+        ref = d["logits"][i]
+        err = rel(logits, ref)
+        assert err <= 1e-2, f"step {i}: {err:.3g}"
+        if d["margin"][i] / np.abs(ref).max() > 2 * err:
+            assert tok == int(d["tokens"][i]), f"step {i}"
+            checked += 1
+        else:
+            ambiguous.append(i)
+    assert checked >= len(got) - 1, f"tie-ambiguous steps {ambiguous}"
