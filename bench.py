@@ -533,6 +533,69 @@ def tp_collectives_per_token(spec, world: int) -> dict:
             "all_reduce_bytes": 4 * spec.hidden}
 
 
+def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms, kern, peak, peak_kind,
+              sweep, cpu, base, collectives, clk) -> dict:
+    """The bench's JSON line from the measured numbers (device ms summed over
+    the timed decode steps, host ms around them, the prefill's device and host
+    ms, the roofline kernel's timing, the peak) and the reports gathered
+    beside them."""
+    from myllm_b200 import synth_gguf as sg
+    moe = isinstance(spec, sg.MoeSpec)
+    mid = args.prompt + args.warmup + args.steps // 2
+    if moe:
+        rep, exp = moe_decode_bytes(spec, mid)
+        tok_bytes = rep + exp / world
+    else:
+        tok_bytes = decode_bytes_per_token(spec, mid) / world
+    ms_step = dev_ms / args.steps
+    # embed; per layer: QKV GEMV (one launch per run of one format or of a
+    # fused format pair), attention split (with RoPE and the KV append) +
+    # combine, o, gate/up, down; final head GEMV, argmax, counter
+    if moe:
+        launches_per_step = moe_launches_per_step(spec, world, rank)
+    else:
+        qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")])
+                  for l in range(spec.layers))
+        launches_per_step = 1 + qkv + 5 * spec.layers + 3
+    return {
+        "metric": "batch-1 greedy decode tokens/s",
+        "value": args.steps / (dev_ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": vs_published(name, args.steps / (dev_ms / 1e3)),
+        "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
+        "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
+        "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
+                   "layers": spec.layers, "hidden": spec.hidden,
+                   "ffn": spec.expert_ffn if moe else spec.ffn, "vocab": spec.vocab,
+                   "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
+                   "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"},
+        "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "prefill": {"value": args.prompt / (prefill_ms / 1e3), "unit": "tokens/s", "tokens": args.prompt,
+                    "e2e_tokens_per_s": args.prompt / (prefill_e2e_ms / 1e3)},
+        "decode_hbm": {"bytes_per_token_per_gpu": tok_bytes, "achieved_gbs": tok_bytes / (ms_step * 1e-3) / 1e9,
+                       "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
+                       "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": kern["gbs"] / peak, "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
+                     "kernel": kern["kernel"], "shape": kern["shape"],
+                     "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
+                     "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
+        "cpu_baseline": cpu,
+        "kernel_sweep": sweep,
+        "scaling_base": base,
+        "collectives": collectives,
+        "clocks": clk,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+
+
 def bench_cuda(args):
     import torch
     import torch.distributed as dist
@@ -609,13 +672,6 @@ def bench_cuda(args):
         if world > 1:
             dist.destroy_process_group()
         return
-    mid = args.prompt + args.warmup + args.steps // 2
-    if moe:
-        rep, exp = moe_decode_bytes(spec, mid)
-        tok_bytes = rep + exp / world
-    else:
-        tok_bytes = decode_bytes_per_token(spec, mid) / world
-    ms_step = dev_ms / args.steps
     cpu = None
     if moe:
         cpu = {"value": None, "unavailable": "the reference has no CPU qwen35moe path (its parity oracle is the "
@@ -623,52 +679,9 @@ def bench_cuda(args):
     elif world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path, spec)
     base = scaling_base(args, local) if world == 1 and not args.no_scaling_base and not args.model else None
-    # embed; per layer: QKV GEMV (one launch per run of one format or of a
-    # fused format pair), attention split (with RoPE and the KV append) +
-    # combine, o, gate/up, down; final head GEMV, argmax, counter
-    if moe:
-        launches_per_step = moe_launches_per_step(spec, world, rank)
-    else:
-        qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")])
-                  for l in range(spec.layers))
-        launches_per_step = 1 + qkv + 5 * spec.layers + 3
-    line = {
-        "metric": "batch-1 greedy decode tokens/s",
-        "value": args.steps / (dev_ms / 1e3),
-        "unit": "tokens/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms_step,
-        "higher_is_better": True,
-        "scaling": "strong",
-        "vs_baseline": vs_published(name, args.steps / (dev_ms / 1e3)),
-        "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
-        "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
-        "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
-                   "layers": spec.layers, "hidden": spec.hidden,
-                   "ffn": spec.expert_ffn if moe else spec.ffn, "vocab": spec.vocab,
-                   "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
-                   "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"},
-        "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
-                "d2h_bytes_per_step": 4},
-        "prefill": {"value": args.prompt / (prefill_ms / 1e3), "unit": "tokens/s", "tokens": args.prompt,
-                    "e2e_tokens_per_s": args.prompt / (prefill_e2e_ms / 1e3)},
-        "decode_hbm": {"bytes_per_token_per_gpu": tok_bytes, "achieved_gbs": tok_bytes / (ms_step * 1e-3) / 1e9,
-                       "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
-                       "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": kern["gbs"] / peak, "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
-                     "kernel": kern["kernel"], "shape": kern["shape"],
-                     "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
-                     "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
-        "cpu_baseline": cpu,
-        "kernel_sweep": sweep,
-        "scaling_base": base,
-        "collectives": collectives,
-        "clocks": clk,
-        "gpu_launches": launches_per_step * args.steps,
-    }
+    line = make_line(name, spec, args, world, rank, dev_ms=dev_ms, e2e_ms=e2e_ms, prefill_ms=prefill_ms,
+                     prefill_e2e_ms=prefill_e2e_ms, kern=kern, peak=peak, peak_kind=peak_kind, sweep=sweep, cpu=cpu,
+                     base=base, collectives=collectives, clk=clk)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -158,3 +158,34 @@ def test_vs_baseline_only_where_the_reference_publishes():
     # 14B decode: the reference's Metal figure (5.777 tok/s); nothing for 7B
     assert bench.vs_published("qwen2.5-14b", 57.77) == pytest.approx(10.0)
     assert bench.vs_published("qwen2.5-7b", 466.0) is None
+
+
+REQUIRED = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+            "vs_baseline", "dtype", "data", "config", "e2e", "roofline", "cpu_baseline", "clocks", "gpu_launches"}
+
+
+@pytest.mark.parametrize("name,world", [("qwen2.5-7b", 1), ("qwen2.5-14b", 8), ("qwen3.6-35b-a3b", 2)])
+def test_json_line_contract(name, world):
+    """Every key the driver reads, for the headline, a tensor-parallel and an
+    expert-parallel line, built from made-up measurements."""
+    import json
+    spec, _ = bench.model_spec(name)
+    args = _args(steps=128, warmup=4, prompt=512, max_sequence=4096, kernel_iters=40)
+    kern = {"kernel": "k", "shape": "s", "bytes_per_launch": 1e8, "avg_launch_us": 20.0, "gbs": 5000.0}
+    clk = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    line = bench.make_line(name, spec, args, world, 0, dev_ms=256.0, e2e_ms=260.0, prefill_ms=100.0,
+                           prefill_e2e_ms=110.0, kern=kern, peak=6545.0, peak_kind="measured", sweep=None,
+                           cpu=None, base=None, collectives=None, clk=clk)
+    assert REQUIRED <= set(line)
+    json.loads(json.dumps(line))
+    assert line["value"] == pytest.approx(500.0) and line["ms_per_step"] == pytest.approx(2.0)
+    assert line["n_gpus"] == world and line["higher_is_better"] is True and line["scaling"] == "strong"
+    assert set(line["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
+    assert line["e2e"]["value"] == pytest.approx(128 / 0.26)
+    assert set(line["roofline"]) >= {"bound", "achieved", "peak", "unit", "frac", "traffic"}
+    assert line["roofline"]["frac"] == pytest.approx(5000 / 6545)
+    assert "workload" in line["config"] and name in line["config"]["workload"]
+    assert line["config"]["parallelism"] == ("single GPU" if world == 1 else
+                                             ("ep" if "a3b" in name else "tp") + str(world))
+    assert isinstance(line["gpu_launches"], int) and line["gpu_launches"] > 128
+    assert (line["vs_baseline"] is None) == (name != "qwen2.5-14b")
