@@ -95,3 +95,43 @@ def test_peer_exchange_layout_and_argument_checks():
     assert call(out=a + 64) == 1                 # overlapping in / out
     assert call(inp=a + 4) == 1                  # unaligned
     assert lib.cl_peer_allreduce(a, b, 5120, 5120, 0, 2, None, None) == 1
+
+
+# pointers the header documents as optional: a NULL there is a valid call
+OPTIONAL_POINTERS = {("cl_argmax_ex", 4),   # value
+                     ("cl_rmsnorm", 5), ("cl_rmsnorm", 6),  # y or xq may be omitted
+                     ("cl_rope_kv", 9)}     # device position (host pos0 used instead)
+
+
+def _is_ptr(a):
+    import ctypes
+    return a in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(a, type) and issubclass(a, ctypes._Pointer))
+
+
+def test_null_pointers_are_rejected_before_any_launch():
+    """Every kernel entry point returns an error status for a NULL required
+    pointer instead of launching: on a GPU such a launch would read or write
+    address 0.  Without a GPU, a call that got as far as a launch returns
+    CL_ERR_CUDA (3); a checked argument returns CL_ERR_INVALID (1) or the
+    workspace error (4).  The no-allocation attention variant resolves its
+    scratch array before delegating to cl_attn_decode's checks, so without a
+    device it stops earlier and is left out here."""
+    import ctypes
+    lib = _native.lib()
+    fake = 1 << 20
+    unchecked = []
+    for name, (rt, args) in sorted(_native.SIGNATURES.items()):
+        if not name.startswith("cl_") or rt is not ctypes.c_int or name in ("cl_device_error",
+                                                                             "cl_attn_decode_noalloc"):
+            continue
+        base = [(ctypes.cast(fake, a) if isinstance(a, type) and issubclass(a, ctypes._Pointer) else fake)
+                if _is_ptr(a) else (1.0 if a is ctypes.c_float else 64) for a in args]
+        for i, a in enumerate(args[:-1]):  # the last argument is the stream: NULL is the default stream
+            if not _is_ptr(a) or (name, i) in OPTIONAL_POINTERS:
+                continue
+            v = list(base)
+            v[i] = None
+            rc = getattr(lib, name)(*v)
+            if rc not in (1, 4):
+                unchecked.append((name, i, rc))
+    assert not unchecked, unchecked
