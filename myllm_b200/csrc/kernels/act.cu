@@ -229,6 +229,8 @@ CL_API int cl_embed(int type, const void* table, long long stride, int vocab, in
     if (table == nullptr || ids == nullptr || out == nullptr || count <= 0 || k <= 0 || vocab <= 0 ||
         cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k))
         return CL_ERR_INVALID;
+    // quantized rows are read byte by byte; F32 rows as floats
+    if (type == CL_TYPE_F32 && (reinterpret_cast<uintptr_t>(table) % 4 || stride % 4)) return CL_ERR_INVALID;
     const long long total = (long long)count * k;
     const int grid = (int)min((total + 255) / 256, 4096LL);
     return launch_pdl(embed_kernel, dim3(grid), dim3(256), 0, stream, type,

@@ -433,6 +433,11 @@ static int attn_decode_launch(const float* q, const float* k_cache, const float*
         max_len <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || q_heads / kv_heads > kMaxGroup ||
         head_dim <= 0 || head_dim % 32 || head_dim > kMaxHeadDim)
         return CL_ERR_INVALID;
+    // q and the K / V rows are staged with 16-byte cp.async copies, and xq is
+    // a set of 16-byte-aligned planes: other alignments would fault
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+         reinterpret_cast<uintptr_t>(xq)) & 15u)
+        return CL_ERR_INVALID;
     if (workspace == nullptr || workspace_bytes < cl_attn_decode_workspace_bytes(q_heads, head_dim, max_len))
         return CL_ERR_WORKSPACE;
     const int splits = attn_splits(max_len);

@@ -87,8 +87,10 @@ int launch_gemm_tc(int type, const void* w, long long stride, int n, int k, cons
 
 namespace {
 bool gemm_args_ok(int type, const void* w, long long stride, int n, int k, const float* x, int m, float* y) {
+    // quantized rows are read byte by byte; F32 rows as floats
     return w != nullptr && x != nullptr && y != nullptr && n > 0 && k > 0 && m > 0 &&
-           cl_native_row_bytes(type, k) >= 0 && stride >= cl_row_stride(type, k);
+           cl_native_row_bytes(type, k) >= 0 && stride >= cl_row_stride(type, k) &&
+           (type != CL_TYPE_F32 || (reinterpret_cast<uintptr_t>(w) % 4 == 0 && stride % 4 == 0));
 }
 }  // namespace
 

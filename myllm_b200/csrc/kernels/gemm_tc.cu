@@ -612,6 +612,8 @@ extern "C" CL_API int cl_gemm_tc(int type, const void* w, long long stride, int 
     if (w == nullptr || x == nullptr || y == nullptr || n <= 0 || k <= 0 || m <= 0 ||
         cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k))
         return CL_ERR_INVALID;
+    // weight rows and activation rows are read with 16-byte vector loads
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) % 16 || stride % 16) return CL_ERR_INVALID;
     if (!cl::gemm_tc_supported(type, n, k, m, precision)) return CL_ERR_UNSUPPORTED;
     return cl::launch_gemm_tc(type, w, stride, n, k, x, m, bias, residual, y, precision, stream);
 }

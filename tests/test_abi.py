@@ -135,3 +135,44 @@ def test_null_pointers_are_rejected_before_any_launch():
             if rc not in (1, 4):
                 unchecked.append((name, i, rc))
     assert not unchecked, unchecked
+
+
+def test_misaligned_pointers_are_rejected_where_kernels_use_wide_loads():
+    """Pointers that a kernel reads with 16-byte vector loads, bulk copies or
+    cp.async must be 16-byte aligned (F32 weight rows read as floats: 4), or
+    the call returns CL_ERR_INVALID instead of faulting on the GPU; the same
+    call with aligned pointers gets past the checks (CL_ERR_CUDA: no GPU)."""
+    import ctypes
+    lib = _native.lib()
+    F, M = 1 << 20, (1 << 20) + 4
+    q4 = sg.Q4_K
+    st = lib.cl_row_stride(q4, 256)
+    ws = lib.cl_attn_decode_workspace_bytes(4, 64, 128)
+    cases = {
+        "cl_gemv": (lambda w=F, x=F: lib.cl_gemv(q4, w, st, 16, 256, x, None, None, F, None), ("w", "x")),
+        "cl_gemv_swiglu": (lambda w=F, x=F: lib.cl_gemv_swiglu(q4, w, F, st, 16, 256, x, None, 1e-6, F, None),
+                           ("w", "x")),
+        "cl_gemm_tc": (lambda w=F, x=F: lib.cl_gemm_tc(q4, w, st, 128, 256, x, 128, None, None, F, 0, None),
+                       ("w", "x")),
+        "cl_attn_decode": (lambda q=F, kc=F, vc=F, xq=None: lib.cl_attn_decode(q, kc, vc, F, 128, 4, 2, 64, 0.1, F,
+                                                                               xq, F, ws, None),
+                           ("q", "kc", "vc", "xq")),
+        "cl_attn_decode_rope": (lambda q=F, kc=F, vc=F: lib.cl_attn_decode_rope(q, F, F, F, F, 64, kc, vc, 128, 4, 2,
+                                                                                64, 0.1, F, None, F, ws, None),
+                                ("q", "kc", "vc")),
+        "cl_moe_expert_gemv": (lambda w=F, x=F: lib.cl_moe_expert_gemv(q4, w, F, st, 16, 256, x, 0, F, 2, 0, 1, F,
+                                                                       None), ("w", "x")),
+        "cl_gemv_f32": (lambda w=F, x=F: lib.cl_gemv_f32(w, 16, 256, x, F, None), ("w", "x")),
+        "cl_peer_allreduce": (lambda inp=F, out=2 * F: lib.cl_peer_allreduce(
+            inp, out, 256, 256, 0, 1, (ctypes.c_void_p * 1)(4 * F), None), ("inp", "out")),
+    }
+    for name, (call, ptrs) in cases.items():
+        assert call() == 3, name  # aligned: reaches the launch
+        for p in ptrs:
+            assert call(**{p: M}) == 1, (name, p)
+    # F32 rows are read as floats: 4-byte alignment; quantized rows byte by byte
+    f32 = sg.F32
+    st32 = lib.cl_row_stride(f32, 256)
+    assert lib.cl_embed(f32, F + 2, st32, 8, 256, F, 1, F, F, None) == 1
+    assert lib.cl_embed(q4, F + 2, st, 8, 256, F, 1, F, F, None) == 3
+    assert lib.cl_gemm_simt(f32, F + 2, st32, 16, 256, F, 4, None, None, F, None) == 1
