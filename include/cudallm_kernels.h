@@ -249,7 +249,11 @@ CL_API int cl_moe_route(const float* logits, int n_experts, int k, int32_t* ids,
  * y[r][i] = W_e[i] . x_r with x_r = x + r * x_stride (x_stride 0: one shared
  * input).  w holds this rank's experts e % world == rank as consecutive
  * [n, k] blocks (local index e / world); routes of other ranks are skipped.
- * With w_up != NULL the SwiGLU silu(W_e[i] . x) * (U_e[i] . x) is stored. */
+ * With w_up != NULL the SwiGLU silu(W_e[i] . x) * (U_e[i] . x) is stored.
+ * Precondition: every ids[r] lies in [0, experts) for the expert count the
+ * stacked w was built for, as cl_moe_route produces them.  The ids are read
+ * on the device, where the kernel has no expert count to check them
+ * against, so another value would index outside w. */
 CL_API int cl_moe_expert_gemv(int type, const void* w, const void* w_up, long long stride, int n, int k,
                               const float* x, int x_stride, const int32_t* ids, int routes, int rank, int world,
                               float* y, cudaStream_t stream);
