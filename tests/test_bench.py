@@ -189,3 +189,40 @@ def test_json_line_contract(name, world):
                                              ("ep" if "a3b" in name else "tp") + str(world))
     assert isinstance(line["gpu_launches"], int) and line["gpu_launches"] > 128
     assert (line["vs_baseline"] is None) == (name != "qwen2.5-14b")
+
+
+def test_moe_kernel_timing_code_runs(monkeypatch):
+    """The config-4 kernel timings of the sweep, dry-run on the CPU: tensors
+    on the host, the library and the graph timer replaced by stand-ins that
+    check every call's argument count against the C signatures."""
+    import numpy as np
+    import torch
+    from myllm_b200 import _native
+    from myllm_b200 import kernels as K
+
+    calls = {}
+
+    class FakeLib:
+        def __getattr__(self, name):
+            res, args = _native.SIGNATURES[name]
+
+            def f(*a):
+                assert len(a) == len(args), name
+                calls[name] = calls.get(name, 0) + 1
+                return 0 if res is not None else None
+            return f
+
+    for fn in ("randn", "zeros", "ones", "empty", "rand", "arange", "tensor"):
+        real = getattr(torch, fn)
+        monkeypatch.setattr(torch, fn, lambda *a, _f=real, **k: _f(*a, **{x: v for x, v in k.items() if x != "device"}))
+    monkeypatch.setattr(_native, "lib", lambda: FakeLib())
+    monkeypatch.setattr(K, "repack", lambda gtype, w, k: torch.from_numpy(w))
+    monkeypatch.setattr(K, "_p", lambda t: None if t is None else 1 << 20)
+    monkeypatch.setattr(K, "_stream", lambda: None)
+    monkeypatch.setattr(sg, "fill", lambda *a, **k: np.zeros((1, 16), dtype=np.uint8))
+    monkeypatch.setattr(bench, "graph_time_us", lambda fn, iters: [fn(i) for i in range(iters)] and 5.0)
+    out = bench.moe_kernel_times(6545.0, 1)
+    assert set(out) == {"router_gemv_f32", "route_topk", "expert_gate_up_swiglu", "expert_down", "gdn_prep",
+                        "gdn_step", "attn_gate_prep", "attn_decode_512_keys"}
+    assert all("error" not in v for v in out.values()), out
+    assert calls["cl_moe_expert_gemv"] > 0 and calls["cl_gdn_step"] > 0 and calls["cl_attn_decode"] > 0
