@@ -341,7 +341,7 @@ def kernel_sweep(peak_gbs: float, seed: int):
     import torch
     from myllm_b200 import kernels as K
     from myllm_b200 import synth_gguf as sg
-    gemv = []
+    gemv, gemm = [], []
     for gtype in (sg.Q4_K, sg.Q6_K, sg.Q5_0, sg.Q8_0):
         for n, k in SWEEP_SHAPES:
             if k % sg.BLOCK[gtype][0]:

@@ -52,7 +52,7 @@ def test_sweep_shapes_are_the_config1_shapes():
 class _FakeLLM:
     """Stands in for CudaLLM: every call 'takes' 2 ms of device time."""
 
-    def __init__(self, path, max_sequence=0, device=0):
+    def __init__(self, path, max_sequence=0, device=0, rank=0, world=1, nccl_id=None):
         self.calls = 0
 
     def prefill(self, ids):
@@ -191,10 +191,10 @@ def test_json_line_contract(name, world):
     assert (line["vs_baseline"] is None) == (name != "qwen2.5-14b")
 
 
-def test_moe_kernel_timing_code_runs(monkeypatch):
-    """The config-4 kernel timings of the sweep, dry-run on the CPU: tensors
-    on the host, the library and the graph timer replaced by stand-ins that
-    check every call's argument count against the C signatures."""
+def _dry_run(monkeypatch):
+    """CPU stand-ins for the GPU side of the bench's sweep code: tensors on
+    the host, a library that checks each call's argument count against the C
+    signatures, a graph timer that just calls the launches."""
     import numpy as np
     import torch
     from myllm_b200 import _native
@@ -221,8 +221,128 @@ def test_moe_kernel_timing_code_runs(monkeypatch):
     monkeypatch.setattr(K, "_stream", lambda: None)
     monkeypatch.setattr(sg, "fill", lambda *a, **k: np.zeros((1, 16), dtype=np.uint8))
     monkeypatch.setattr(bench, "graph_time_us", lambda fn, iters: [fn(i) for i in range(iters)] and 5.0)
+    return calls
+
+
+def test_sweep_code_runs(monkeypatch):
+    """Config 1's sweep, dry-run: every GEMV entry and the prefill GEMM at
+    three batch sizes for every format and shape, without errors."""
+    calls = _dry_run(monkeypatch)
+    monkeypatch.setattr(bench, "SWEEP_SHAPES", [(896, 896), (256, 512)])
+    out = bench.kernel_sweep(6545.0, 1)
+    # K-quants skip K = 896: 2 formats x 1 shape + 2 formats x 2 shapes
+    assert len(out["gemv"]) == 6 and len(out["gemm"]) == 18
+    assert all("error" not in e for e in out["gemm"]), out["gemm"]
+    assert calls["cl_gemv"] > 0 and calls["cl_gemm"] > 0
+
+
+def test_moe_kernel_timing_code_runs(monkeypatch):
+    """The config-4 kernel timings of the sweep, dry-run on the CPU."""
+    calls = _dry_run(monkeypatch)
     out = bench.moe_kernel_times(6545.0, 1)
     assert set(out) == {"router_gemv_f32", "route_topk", "expert_gate_up_swiglu", "expert_down", "gdn_prep",
                         "gdn_step", "attn_gate_prep", "attn_decode_512_keys"}
     assert all("error" not in v for v in out.values()), out
     assert calls["cl_moe_expert_gemv"] > 0 and calls["cl_gdn_step"] > 0 and calls["cl_attn_decode"] > 0
+
+
+def test_default_run_prints_a_complete_line(monkeypatch, capsys):
+    """The N = 1 default run end to end on the CPU: a stand-in model and CUDA
+    timer, the sweep and kernel timings dry-run, the reference sample and
+    the 14B point stubbed; one JSON line with every key of the contract."""
+    import json
+    import sys
+    import torch
+    import myllm_b200
+    _dry_run(monkeypatch)
+    monkeypatch.setattr(bench, "SWEEP_SHAPES", [(256, 512)])
+
+    class Event:
+        def __init__(self, enable_timing=False):
+            pass
+
+        def record(self, stream=None):
+            pass
+
+        def elapsed_time(self, other):
+            return 1.0
+
+    class Clocks:
+        def __init__(self, gpu):
+            pass
+
+        def start(self):
+            pass
+
+        def stop(self):
+            return {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+
+    monkeypatch.setattr(torch.cuda, "Event", Event)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
+    monkeypatch.setattr(torch.cuda, "set_device", lambda *a: None)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a: None)
+    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
+    monkeypatch.setattr(bench, "ClockSampler", Clocks)
+    monkeypatch.setattr(bench, "run_cpu_baseline", lambda *a, **k: {"value": 0.2, "unit": "tokens/s", "cores": 1,
+                                                                     "kind": "reference", "sample": "stub"})
+    monkeypatch.setattr(bench, "scaling_base", lambda args, dev: {"workload": "qwen2.5-14b", "value": 1.0})
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--steps", "8", "--warmup", "3"])
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    bench.main()
+    lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert REQUIRED <= set(line) and line["n_gpus"] == 1 and line["steps"] == 8
+    assert line["value"] == pytest.approx(8 / (8 * 2.0 / 1e3)) and line["cpu_baseline"]["value"] == 0.2
+    assert "moe_kernels" in line["kernel_sweep"] and line["scaling_base"]["value"] == 1.0
+    assert line["roofline"]["achieved"] > 0
+
+
+def test_tensor_parallel_run_prints_a_complete_line(monkeypatch, capsys):
+    """Rank 0 of a 2-rank run (the 14B shape, tensor-parallel) on the CPU:
+    torch.distributed replaced by stand-ins; the line carries the contract
+    keys and the collectives report."""
+    import json
+    import sys
+    import torch
+    import torch.distributed as dist
+    import myllm_b200
+    _dry_run(monkeypatch)
+
+    class Event:
+        def __init__(self, enable_timing=False):
+            pass
+
+        def record(self, stream=None):
+            pass
+
+        def elapsed_time(self, other):
+            return 1.0
+
+    class Work:
+        def wait(self):
+            pass
+
+    monkeypatch.setattr(torch.cuda, "Event", Event)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
+    monkeypatch.setattr(torch.cuda, "set_device", lambda *a: None)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a: None)
+    for fn in ("init_process_group", "barrier", "broadcast_object_list", "destroy_process_group"):
+        monkeypatch.setattr(dist, fn, lambda *a, **k: None)
+    monkeypatch.setattr(dist, "all_reduce", lambda t, op=None, async_op=False: Work() if async_op else None)
+    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
+    monkeypatch.setattr(bench, "ClockSampler", lambda gpu: type("C", (), {
+        "start": lambda self: None, "stop": lambda self: {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}})())
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", "2", "--steps", "8", "--warmup", "3"])
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("LOCAL_RANK", "0")
+    bench.main()
+    lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert REQUIRED <= set(line) and line["n_gpus"] == 2 and line["config"]["parallelism"] == "tp2"
+    assert line["collectives"]["all_reduce"] == 2 * sg.CONFIGS["qwen2.5-14b"].layers
+    assert line["collectives"]["all_reduce_us"] > 0 and line["vs_baseline"] is not None
