@@ -633,6 +633,17 @@ def tp_collectives_per_token(spec, world: int) -> dict:
             "all_reduce_bytes": 4 * spec.hidden}
 
 
+def workload_config(name, spec, args, world) -> dict:
+    """The `config` of both arms' lines: the workload of this run."""
+    from myllm_b200 import synth_gguf as sg
+    moe = isinstance(spec, sg.MoeSpec)
+    return {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
+            "layers": spec.layers, "hidden": spec.hidden, "ffn": spec.expert_ffn if moe else spec.ffn,
+            "vocab": spec.vocab,
+            "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
+            "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"}
+
+
 def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms, kern, peak, peak_kind,
               sweep, cpu, base, collectives, clk) -> dict:
     """The bench's JSON line from the measured numbers (device ms summed over
@@ -670,11 +681,7 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         "vs_baseline": vs_published(name, args.steps / (dev_ms / 1e3)),
         "dtype": "q4_k_m weights x fp32 activations (int8 limbs, exact integer dots, fp32 scaling)",
         "data": "synthetic (seeded N(0,0.02) weights quantized to GGML blocks; uniform random prompt ids)",
-        "config": {"workload": f"{name} Q4_K_M, prompt {args.prompt}, greedy decode, KV capacity {args.max_sequence}",
-                   "layers": spec.layers, "hidden": spec.hidden,
-                   "ffn": spec.expert_ffn if moe else spec.ffn, "vocab": spec.vocab,
-                   "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
-                   "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"},
+        "config": workload_config(name, spec, args, world),
         "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "prefill": {"value": args.prompt / (prefill_ms / 1e3), "unit": "tokens/s", "tokens": args.prompt,
@@ -823,10 +830,11 @@ def bench_reference(args):
         "vs_baseline": vs_published(name, res["value"]),
         "dtype": "fp32 (reference dequantizes to FP32 at load)",
         "data": "synthetic (same seeded GGUF as the cuda arm)",
-        "config": {"workload": f"{name} Q4_K_M, reference CPULLM, prompt 4 + {steps} decode tokens (bounded sample)",
-                   "parallelism": "1 host thread (CPULLM has no threading)"},
+        "config": workload_config(name, spec, args, world),
         "prefill": {"value": res["prefill_tokens_per_s"], "unit": "tokens/s", "tokens": 4},
-        "cpu_baseline": res,
+        "cpu_baseline": dict(res, sample=f"{res.get('sample', '')}; a bounded sample of the workload in `config` "
+                                         f"(prompt 4 + {steps} decode tokens), 1 host thread (CPULLM has no "
+                                         f"threading)"),
         "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -346,3 +346,42 @@ def test_tensor_parallel_run_prints_a_complete_line(monkeypatch, capsys):
     assert REQUIRED <= set(line) and line["n_gpus"] == 2 and line["config"]["parallelism"] == "tp2"
     assert line["collectives"]["all_reduce"] == 2 * sg.CONFIGS["qwen2.5-14b"].layers
     assert line["collectives"]["all_reduce_us"] > 0 and line["vs_baseline"] is not None
+
+
+@pytest.mark.parametrize("gpus,model,expect", [(1, None, "qwen2.5-7b"), (2, None, "qwen2.5-14b"),
+                                               (1, "qwen3.6-35b-a3b", None)])
+def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect):
+    """`--impl reference`: the CPULLM sample (stubbed) on the cuda arm's
+    workload, with the contract keys; rank 0 only; the MoE model reports the
+    reference's missing CPU path."""
+    import json
+    import sys
+    seen = {}
+
+    def sample(path, spec=None, **k):
+        seen["spec"] = spec.name
+        return {"value": 0.25, "unit": "tokens/s", "cores": 1, "kind": "reference", "sample": "stub",
+                "prefill_tokens_per_s": 1.0}
+    monkeypatch.setattr(bench, "run_cpu_baseline", sample)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (bench.model_spec(name)[0], "unused"))
+    argv = ["bench.py", "--impl", "reference", "--gpus", str(gpus)] + (["--model", model] if model else [])
+    monkeypatch.setattr(sys, "argv", argv)
+    monkeypatch.setenv("WORLD_SIZE", str(gpus))
+    monkeypatch.setenv("RANK", "0")
+    bench.main()
+    line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
+    assert line["impl"] == "reference"
+    if expect is None:
+        assert "unavailable" in line
+        return
+    assert seen["spec"] == expect
+    assert REQUIRED - {"clocks", "gpu_launches", "roofline"} <= set(line) and line["value"] == 0.25
+    # the cuda arm's config, so that the driver pairs the two lines
+    spec = bench.model_spec(expect)[0]
+    assert line["config"] == bench.workload_config(expect, spec, bench.parse(), gpus)
+    assert line["cpu_baseline"]["kind"] == "reference" and "bounded sample" in line["cpu_baseline"]["sample"]
+    assert line["e2e"] == {"value": 0.25, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # other ranks print nothing
+    monkeypatch.setenv("RANK", "1")
+    bench.main()
+    assert not capsys.readouterr().out.strip() or gpus == 1
