@@ -385,3 +385,51 @@ def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect)
     monkeypatch.setenv("RANK", "1")
     bench.main()
     assert not capsys.readouterr().out.strip() or gpus == 1
+
+
+@pytest.mark.parametrize("gpus", [1, 2])
+def test_moe_mode_prints_a_complete_line(monkeypatch, capsys, gpus):
+    """`--model qwen3.6-35b-a3b`: the expert-parallel workload's line (LM-head
+    roofline kernel, replicated + expert bytes, no timed CPU reference)."""
+    import json
+    import sys
+    import torch
+    import torch.distributed as dist
+    import myllm_b200
+    _dry_run(monkeypatch)
+
+    class Event:
+        def __init__(self, enable_timing=False):
+            pass
+
+        def record(self, stream=None):
+            pass
+
+        def elapsed_time(self, other):
+            return 1.0
+
+    class Work:
+        def wait(self):
+            pass
+
+    monkeypatch.setattr(torch.cuda, "Event", Event)
+    for fn in ("synchronize", "set_device", "current_stream"):
+        monkeypatch.setattr(torch.cuda, fn, lambda *a: None)
+    for fn in ("init_process_group", "barrier", "broadcast_object_list", "destroy_process_group"):
+        monkeypatch.setattr(dist, fn, lambda *a, **k: None)
+    monkeypatch.setattr(dist, "all_reduce", lambda t, op=None, async_op=False: Work() if async_op else None)
+    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (bench.model_spec(name)[0], "unused"))
+    monkeypatch.setattr(bench, "ClockSampler", lambda gpu: type("C", (), {
+        "start": lambda self: None, "stop": lambda self: {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}})())
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", str(gpus), "--model", "qwen3.6-35b-a3b", "--prompt", "64",
+                                      "--steps", "8", "--warmup", "3", "--max-sequence", "1024"])
+    monkeypatch.setenv("WORLD_SIZE", str(gpus))
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("LOCAL_RANK", "0")
+    bench.main()
+    line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
+    assert REQUIRED <= set(line)
+    assert line["config"]["parallelism"] == ("single GPU" if gpus == 1 else "ep2")
+    assert line["roofline"]["shape"].endswith("Q6_K") and line["cpu_baseline"]["value"] is None
+    assert (line["collectives"] is None) == (gpus == 1) and line["kernel_sweep"] is None
