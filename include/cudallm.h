@@ -63,6 +63,14 @@ CUDALLM_API int cudallm_memory_stats(const cudallm_model* m, uint64_t out[4]);
 CUDALLM_API int cudallm_enable_profiling(cudallm_model* m, const char* csv_path);
 CUDALLM_API int cudallm_disable_profiling(cudallm_model* m);
 CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n);
+/* available() of the reference GPU backends (metal_llm.h:46, moe_llm.h:55):
+ * 1 for a created model, 0 for NULL. */
+CUDALLM_API int cudallm_available(const cudallm_model* m);
+/* The qwen35moe expert cache (moe_llm.h:9-17, 49-50): out[0] = experts
+ * resident per layer on this rank (all of them: every expert stays in HBM),
+ * out[1] = hits (routed expert uses so far), out[2] = misses (always 0).
+ * A qwen2 model reports zeros. */
+CUDALLM_API int cudallm_expert_cache(const cudallm_model* m, uint64_t out[3]);
 
 /* Host only (no GPU needed): parse a GGUF file's header, metadata and tensor
  * table without reading tensor data, the first step of cudallm_create.

@@ -97,6 +97,8 @@ SIGNATURES = {
     "cudallm_enable_profiling": (c_int, [c_vp, c_char_p]),
     "cudallm_disable_profiling": (c_int, [c_vp]),
     "cudallm_device_name": (c_int, [c_vp, c_vp, c_size]),
+    "cudallm_available": (c_int, [c_vp]),
+    "cudallm_expert_cache": (c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
     "cudallm_gguf_inspect": (c_int, [c_char_p, c_vp, c_size, c_vp]),
     "cudallm_tp_plan": (c_int, [ctypes.c_uint64] * 6 + [c_int, c_int, c_vp]),
     "cudallm_ep_plan": (c_int, [ctypes.c_uint64, ctypes.c_uint64, c_int, c_vp, c_vp, c_vp]),

@@ -198,6 +198,24 @@ CUDALLM_API int cudallm_device_name(const cudallm_model* m, char* buf, size_t n)
     });
 }
 
+CUDALLM_API int cudallm_available(const cudallm_model* m) {
+    return m && m->with([](const auto& b) { return b.available(); }) ? 1 : 0;
+}
+
+CUDALLM_API int cudallm_expert_cache(const cudallm_model* m, uint64_t out[3]) {
+    return guard([&] {
+        need(m);
+        need(out);
+        out[0] = out[1] = out[2] = 0;
+        if (m->moe) {
+            const cudallm::ExpertCacheStats st = m->moe->expert_cache_stats();
+            out[0] = m->moe->expert_cache_count();
+            out[1] = st.hits;
+            out[2] = st.misses;
+        }
+    });
+}
+
 CUDALLM_API int cudallm_gguf_inspect(const char* gguf_path, char* arch, size_t n, uint64_t* tensor_count) {
     return guard([&] {
         need(gguf_path);

@@ -66,6 +66,16 @@ class MemoryStats:
 
 
 @dataclass
+class ExpertCacheStats:
+    """ExpertCacheStats of the reference's MoeLLM (moe_llm.h:9-17)."""
+    hits: int
+    misses: int
+
+    def requests(self) -> int:
+        return self.hits + self.misses
+
+
+@dataclass
 class ModelConfig:
     layer_count: int
     embedding_size: int
@@ -196,6 +206,22 @@ class CudaLLM:
 
     def uses_gpu(self) -> bool:
         return True
+
+    def available(self) -> bool:
+        return bool(_native.lib().cudallm_available(self._h))
+
+    def _expert_cache(self):
+        out = (ctypes.c_uint64 * 3)()
+        _check(_native.lib().cudallm_expert_cache(self._h, out))
+        return [int(v) for v in out]
+
+    def expert_cache_count(self) -> int:
+        """qwen35moe: experts resident per layer on this rank (all of them); 0 for qwen2."""
+        return self._expert_cache()[0]
+
+    def expert_cache_stats(self) -> ExpertCacheStats:
+        _, hits, misses = self._expert_cache()
+        return ExpertCacheStats(hits, misses)
 
     def memory_stats(self) -> MemoryStats:
         out = (ctypes.c_uint64 * 4)()

@@ -176,3 +176,11 @@ def test_misaligned_pointers_are_rejected_where_kernels_use_wide_loads():
     assert lib.cl_embed(f32, F + 2, st32, 8, 256, F, 1, F, F, None) == 1
     assert lib.cl_embed(q4, F + 2, st, 8, 256, F, 1, F, F, None) == 3
     assert lib.cl_gemm_simt(f32, F + 2, st32, 16, 256, F, 4, None, None, F, None) == 1
+
+
+def test_backend_queries_without_a_model():
+    import ctypes
+    lib = _native.lib()
+    assert lib.cudallm_available(None) == 0
+    out = (ctypes.c_uint64 * 3)()
+    assert lib.cudallm_expert_cache(None, out) == 1  # CUDALLM_EINVAL

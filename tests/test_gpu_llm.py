@@ -209,3 +209,11 @@ def test_profile_csv(tiny_models, tmp_path):
     assert sorted(r["stage"] for r in rows[6:]) == ["decode.gpu_resident", "forward.total", "prefill.gpu_resident"]
     for r in rows:
         assert int(r["flops"]) > 0 and int(r["read_bytes"]) > 0 and float(r["time_ms"]) > 0
+
+
+def test_backend_queries(tiny_models):
+    path, _ = tiny_models[7]
+    llm = CudaLLM(path, max_sequence=64)
+    assert llm.available() and llm.uses_gpu() and llm.device_name()
+    assert llm.expert_cache_count() == 0 and llm.expert_cache_stats().requests() == 0
+    llm.close()

@@ -171,3 +171,17 @@ def test_moe_config4_widths_against_fp64_fixture(model_dir, cuda):
         else:
             ambiguous.append(i)
     assert checked >= len(got) - 1, f"tie-ambiguous steps {ambiguous}"
+
+
+def test_moe_backend_queries(tiny_moe):
+    """available() and MoeLLM's expert cache (moe_llm.h:49-50): every expert
+    is resident, so every routed use is a hit and none is a miss."""
+    spec, path = tiny_moe[5]
+    llm = CudaLLM(path, max_sequence=64)
+    assert llm.available() and llm.uses_gpu()
+    assert llm.expert_cache_count() == spec.experts
+    tok = llm.prefill(sg.prompt_ids(spec.seed, 12, spec.vocab))
+    llm.decode(tok)
+    st = llm.expert_cache_stats()
+    assert st.misses == 0 and st.hits == 13 * spec.layers * spec.experts_used == st.requests()
+    llm.close()
