@@ -210,6 +210,9 @@ struct CudaLLM::Impl {
     bool have_logits = false;
 
     ~Impl() {
+        // the mappings belong to this model's device, which another model of
+        // the same process may not have left current
+        if (!peer_bufs.empty()) cudaSetDevice(device);
         for (std::size_t r = 0; r < peer_bufs.size(); ++r)
             if ((int)r != par.rank && peer_bufs[r]) cudaIpcCloseMemHandle(peer_bufs[r]);
         if (decode_exec) cudaGraphExecDestroy(decode_exec);
