@@ -668,6 +668,8 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         qkv = sum(gemv_launches([spec.types(l, t) for t in ("attn_q", "attn_k", "attn_v")])
                   for l in range(spec.layers))
         launches_per_step = 1 + qkv + 5 * spec.layers + 3
+        if world > 1 and os.environ.get("CUDALLM_ALLREDUCE") == "p2p":
+            launches_per_step += 2 * spec.layers  # the decode all-reduces are this library's kernel then
     return {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),

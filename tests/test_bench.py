@@ -433,3 +433,16 @@ def test_moe_mode_prints_a_complete_line(monkeypatch, capsys, gpus):
     assert line["config"]["parallelism"] == ("single GPU" if gpus == 1 else "ep2")
     assert line["roofline"]["shape"].endswith("Q6_K") and line["cpu_baseline"]["value"] is None
     assert (line["collectives"] is None) == (gpus == 1) and line["kernel_sweep"] is None
+
+
+def test_launch_count_includes_the_peer_allreduce(monkeypatch):
+    spec = sg.CONFIGS["qwen2.5-14b"]
+    kw = dict(dev_ms=256.0, e2e_ms=260.0, prefill_ms=100.0, prefill_e2e_ms=110.0,
+              kern={"kernel": "k", "shape": "s", "bytes_per_launch": 1, "avg_launch_us": 1.0, "gbs": 1.0},
+              peak=6545.0, peak_kind="measured", sweep=None, cpu=None, base=None, collectives=None, clk={})
+    args = _args(steps=10, warmup=3, prompt=512, max_sequence=4096)
+    monkeypatch.delenv("CUDALLM_ALLREDUCE", raising=False)
+    nccl = bench.make_line("qwen2.5-14b", spec, args, 2, 0, **kw)["gpu_launches"]
+    monkeypatch.setenv("CUDALLM_ALLREDUCE", "p2p")
+    p2p = bench.make_line("qwen2.5-14b", spec, args, 2, 0, **kw)["gpu_launches"]
+    assert p2p - nccl == 2 * spec.layers * 10
