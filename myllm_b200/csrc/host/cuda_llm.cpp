@@ -667,6 +667,7 @@ struct CudaLLM::Impl {
                 throw std::out_of_range("CUDA prefill token id is outside the vocabulary");
         }
         CUDALLM_CUDA(cudaSetDevice(device));
+        const TraceRange trace("prefill.gpu_resident");
         begin_timing();
         const std::size_t n = ids.size();
         int32_t* staging = host_in() + 4;
@@ -702,6 +703,7 @@ struct CudaLLM::Impl {
         CUDALLM_CUDA(cudaSetDevice(device));
         if (decode_exec == nullptr) build_decode_graph();
         host_in()[0] = token;
+        const TraceRange trace("decode.gpu_resident");
         begin_timing();
         CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
         end_timing("decode", 1);

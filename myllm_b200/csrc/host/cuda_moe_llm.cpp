@@ -613,6 +613,7 @@ struct CudaMoeLLM::Impl {
             if (id < 0 || (std::size_t)id >= V) throw std::out_of_range("CUDA prefill token id is outside the vocabulary");
         CUDALLM_CUDA(cudaSetDevice(device));
         if (prefill_exec == nullptr) prefill_exec = capture([&] { record_prefill_step(); });
+        const TraceRange trace("prefill.gpu_moe");
         begin_timing();
         int32_t* hi = host_in();
         std::memcpy(hi + 4, tokens.data(), tokens.size() * sizeof(int32_t));
@@ -637,6 +638,7 @@ struct CudaMoeLLM::Impl {
         CUDALLM_CUDA(cudaSetDevice(device));
         if (decode_exec == nullptr) decode_exec = capture([&] { record_decode(); });
         host_in()[0] = token;
+        const TraceRange trace("decode.gpu_moe");
         begin_timing();
         CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
         end_timing("decode", 1);

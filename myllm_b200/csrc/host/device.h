@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstddef>
 #include <cstdint>
@@ -46,6 +47,18 @@ public:
 private:
     void* ptr_ = nullptr;
     std::size_t bytes_ = 0;
+};
+
+// An NVTX range around one backend call (closed on every exit path), named
+// like the reference profiler's stage for it, so that timelines taken with
+// NVIDIA's tools show each prefill / decode.  Without a tool attached the
+// calls return at once.
+class TraceRange {
+public:
+    explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+    ~TraceRange() { nvtxRangePop(); }
+    TraceRange(const TraceRange&) = delete;
+    TraceRange& operator=(const TraceRange&) = delete;
 };
 
 class PinnedBuffer {
