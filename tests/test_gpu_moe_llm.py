@@ -10,7 +10,7 @@ import os
 
 import numpy as np
 import pytest
-import torch
+import torch  # noqa: F401  (a skipif condition below is evaluated in this namespace)
 
 from myllm_b200 import CudaLLM, InvalidArgument, LengthError, OutOfRange
 from myllm_b200 import synth_gguf as sg

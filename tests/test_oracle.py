@@ -1,6 +1,5 @@
 """CPU tests: the oracle is pinned to the reference, the generator is stable."""
 import os
-import tempfile
 
 import numpy as np
 import pytest
