@@ -295,7 +295,7 @@ struct CudaLLM::Impl {
     }
 
     void allocate_activations(Arena& a) {
-        const std::size_t qd_l = hq_l * d, kvd_l = hkv_l * d, P = prefill_chunk;
+        const std::size_t qd_l = hq_l * d, kvd_l = hkv_l * d, chunk = prefill_chunk;
         h = a.take_n<float>(H);
         part = a.take_n<float>(H);
         q = a.take_n<float>(qd_l);
@@ -311,17 +311,17 @@ struct CudaLLM::Impl {
         arg_ws = a.take(arg_ws_bytes);
         ints = a.take_n<int32_t>(16);
         best = a.take_n<float>(2 * (std::size_t)par.world + 2);
-        X = a.take_n<float>(P * H);
-        Xn = a.take_n<float>(P * H);
-        Q = a.take_n<float>(P * qd_l);
-        K = a.take_n<float>(P * kvd_l);
-        Vv = a.take_n<float>(P * kvd_l);
-        A = a.take_n<float>(P * qd_l);
-        A_full = a.take_n<float>(gather_attn ? P * hq * d : 1);
-        G = a.take_n<float>(P * F_l);
-        U = a.take_n<float>(P * F_l);
-        this->P = a.take_n<float>(P * H);
-        ids_dev = a.take_n<int32_t>(P);
+        X = a.take_n<float>(chunk * H);
+        Xn = a.take_n<float>(chunk * H);
+        Q = a.take_n<float>(chunk * qd_l);
+        K = a.take_n<float>(chunk * kvd_l);
+        Vv = a.take_n<float>(chunk * kvd_l);
+        A = a.take_n<float>(chunk * qd_l);
+        A_full = a.take_n<float>(gather_attn ? chunk * hq * d : 1);
+        G = a.take_n<float>(chunk * F_l);
+        U = a.take_n<float>(chunk * F_l);
+        P = a.take_n<float>(chunk * H);
+        ids_dev = a.take_n<int32_t>(chunk);
     }
 
     void init(const std::string& path, std::size_t max_sequence, int dev, const ParallelConfig& parallel) {
@@ -345,19 +345,19 @@ struct CudaLLM::Impl {
         prefill_chunk = std::min<std::size_t>(max_seq, 1024);
         // Diagnostics: a smaller prefill chunk exercises the cross-chunk KV path.
         if (const char* e = std::getenv("CUDALLM_PREFILL_CHUNK")) {
-            const long v = std::strtol(e, nullptr, 10);
-            if (v > 0) prefill_chunk = std::min<std::size_t>(max_seq, (std::size_t)v);
+            const long val = std::strtol(e, nullptr, 10);
+            if (val > 0) prefill_chunk = std::min<std::size_t>(max_seq, (std::size_t)val);
         }
         // Prefill GEMM precision: "tf32x3" (default, FP32-grade, as the
         // reference's FP32 GEMM), "f16" (one FP16 tensor-core pass) or "simt"
         // (FP32 CUDA cores).
         if (const char* e = std::getenv("CUDALLM_PREFILL_GEMM")) {
-            const std::string v(e);
-            if (v == "f16")
+            const std::string val(e);
+            if (val == "f16")
                 gemm_path = GemmPath::F16;
-            else if (v == "simt")
+            else if (val == "simt")
                 gemm_path = GemmPath::Simt;
-            else if (v != "tf32x3" && !v.empty())
+            else if (val != "tf32x3" && !val.empty())
                 throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be tf32x3, f16 or simt");
         }
         std::size_t o_block = 1;
@@ -373,10 +373,10 @@ struct CudaLLM::Impl {
             CUDALLM_NCCL(ncclCommInitRank(&comm, par.world, id, par.rank));
             // decode all-reduce: "nccl" (default) or "p2p" (cl_peer_allreduce)
             if (const char* e = std::getenv("CUDALLM_ALLREDUCE")) {
-                const std::string v(e);
-                if (v == "p2p")
+                const std::string val(e);
+                if (val == "p2p")
                     setup_peer_exchange();
-                else if (v != "nccl" && !v.empty())
+                else if (val != "nccl" && !val.empty())
                     throw std::invalid_argument("CUDALLM_ALLREDUCE must be nccl or p2p");
             }
         }
@@ -480,7 +480,6 @@ struct CudaLLM::Impl {
         const float scale = 1.0f / std::sqrt(static_cast<float>(d));
         int32_t* tok_in = ints + 0;
         int* pos = ints + 1;
-        int* len = ints + 2;
         CUDALLM_CUDA(cudaMemcpyAsync(tok_in, host_in(), sizeof(int32_t), cudaMemcpyHostToDevice, s));
         CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, (int)H, tok_in, 1, h, ints + 4, s));
         float* out = W > 1 ? part : h;
@@ -543,11 +542,11 @@ struct CudaLLM::Impl {
     enum class GemmPath { Auto, F16, Simt };
     GemmPath gemm_path = GemmPath::Auto;
 
-    // Y[m, W.rows] = X[m, k] W^T (+ bias) (+ residual) on the selected path.
-    void gemm(const DevMat& Wm, int n, int k, const float* x, int m, const float* bias, const float* res, float* y) {
+    // Y[m, W.rows] = X[m, kdim] W^T (+ bias) (+ residual) on the selected path.
+    void gemm(const DevMat& Wm, int n, int kdim, const float* x, int m, const float* bias, const float* res, float* y) {
         switch (gemm_path) {
         case GemmPath::F16: {
-            const int rc = cl_gemm_tc(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, CL_GEMM_F16, stream);
+            const int rc = cl_gemm_tc(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, CL_GEMM_F16, stream);
             if (rc != CL_ERR_UNSUPPORTED) {
                 CUDALLM_CL(rc);
                 return;
@@ -555,11 +554,11 @@ struct CudaLLM::Impl {
             break;  // shapes the FP16 path does not take use the default path
         }
         case GemmPath::Simt:
-            CUDALLM_CL(cl_gemm_simt(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, stream));
+            CUDALLM_CL(cl_gemm_simt(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, stream));
             return;
         case GemmPath::Auto: break;
         }
-        CUDALLM_CL(cl_gemm(Wm.type, Wm.ptr, Wm.stride, n, k, x, m, bias, res, y, stream));
+        CUDALLM_CL(cl_gemm(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, stream));
     }
 
     // Rows [0, m) of X hold the chunk at positions pos0..pos0+m-1.
