@@ -331,7 +331,6 @@ bool gemv_type_ok(int t) {
     return t == CL_TYPE_Q4_K || t == CL_TYPE_Q5_K || t == CL_TYPE_Q6_K || t == CL_TYPE_Q8_0 || t == CL_TYPE_Q5_0;
 }
 
-constexpr int kStageTarget = 40 * 1024;
 constexpr int kSmemBudget = 190 * 1024;
 constexpr int kTargetWarps = 16;  // consumer warps per CTA to aim for
 
