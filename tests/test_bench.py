@@ -246,49 +246,71 @@ def test_moe_kernel_timing_code_runs(monkeypatch):
     assert calls["cl_moe_expert_gemv"] > 0 and calls["cl_gdn_step"] > 0 and calls["cl_attn_decode"] > 0
 
 
+class _Event:
+    """CUDA event stand-in: every interval is 1 ms."""
+
+    def __init__(self, enable_timing=False):
+        pass
+
+    def record(self, stream=None):
+        pass
+
+    def elapsed_time(self, other):
+        return 1.0
+
+
+class _Work:
+    def wait(self):
+        pass
+
+
+class _Clocks:
+    def __init__(self, gpu):
+        pass
+
+    def start(self):
+        pass
+
+    def stop(self):
+        return {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+
+
+def _fake_run(monkeypatch, argv, env):
+    """Everything a whole bench run touches, replaced for the CPU: the sweep
+    stand-ins of _dry_run, CUDA events and device calls, torch.distributed,
+    the model, the model file and the clock sampler; argv and the launcher's
+    environment as given."""
+    import sys
+    import torch
+    import torch.distributed as dist
+    import myllm_b200
+    _dry_run(monkeypatch)
+    monkeypatch.setattr(torch.cuda, "Event", _Event)
+    for fn in ("synchronize", "set_device", "current_stream"):
+        monkeypatch.setattr(torch.cuda, fn, lambda *a: None)
+    for fn in ("init_process_group", "barrier", "broadcast_object_list", "destroy_process_group"):
+        monkeypatch.setattr(dist, fn, lambda *a, **k: None)
+    monkeypatch.setattr(dist, "all_reduce", lambda t, op=None, async_op=False: _Work() if async_op else None)
+    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
+    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (bench.model_spec(name)[0], "unused"))
+    monkeypatch.setattr(bench, "ClockSampler", _Clocks)
+    monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
+    for k in ("WORLD_SIZE", "RANK", "LOCAL_RANK"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+
+
 def test_default_run_prints_a_complete_line(monkeypatch, capsys):
     """The N = 1 default run end to end on the CPU: a stand-in model and CUDA
     timer, the sweep and kernel timings dry-run, the reference sample and
     the 14B point stubbed; one JSON line with every key of the contract."""
     import json
-    import sys
-    import torch
-    import myllm_b200
-    _dry_run(monkeypatch)
+    _fake_run(monkeypatch, ["--steps", "8", "--warmup", "3"], {})
     monkeypatch.setattr(bench, "SWEEP_SHAPES", [(256, 512)])
-
-    class Event:
-        def __init__(self, enable_timing=False):
-            pass
-
-        def record(self, stream=None):
-            pass
-
-        def elapsed_time(self, other):
-            return 1.0
-
-    class Clocks:
-        def __init__(self, gpu):
-            pass
-
-        def start(self):
-            pass
-
-        def stop(self):
-            return {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
-
-    monkeypatch.setattr(torch.cuda, "Event", Event)
-    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
-    monkeypatch.setattr(torch.cuda, "set_device", lambda *a: None)
-    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a: None)
-    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
-    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
-    monkeypatch.setattr(bench, "ClockSampler", Clocks)
     monkeypatch.setattr(bench, "run_cpu_baseline", lambda *a, **k: {"value": 0.2, "unit": "tokens/s", "cores": 1,
                                                                      "kind": "reference", "sample": "stub"})
     monkeypatch.setattr(bench, "scaling_base", lambda args, dev: {"workload": "qwen2.5-14b", "value": 1.0})
-    monkeypatch.setattr(sys, "argv", ["bench.py", "--steps", "8", "--warmup", "3"])
-    monkeypatch.delenv("WORLD_SIZE", raising=False)
     bench.main()
     lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -304,41 +326,8 @@ def test_tensor_parallel_run_prints_a_complete_line(monkeypatch, capsys):
     torch.distributed replaced by stand-ins; the line carries the contract
     keys and the collectives report."""
     import json
-    import sys
-    import torch
-    import torch.distributed as dist
-    import myllm_b200
-    _dry_run(monkeypatch)
-
-    class Event:
-        def __init__(self, enable_timing=False):
-            pass
-
-        def record(self, stream=None):
-            pass
-
-        def elapsed_time(self, other):
-            return 1.0
-
-    class Work:
-        def wait(self):
-            pass
-
-    monkeypatch.setattr(torch.cuda, "Event", Event)
-    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
-    monkeypatch.setattr(torch.cuda, "set_device", lambda *a: None)
-    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a: None)
-    for fn in ("init_process_group", "barrier", "broadcast_object_list", "destroy_process_group"):
-        monkeypatch.setattr(dist, fn, lambda *a, **k: None)
-    monkeypatch.setattr(dist, "all_reduce", lambda t, op=None, async_op=False: Work() if async_op else None)
-    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
-    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (sg.CONFIGS[name], "unused"))
-    monkeypatch.setattr(bench, "ClockSampler", lambda gpu: type("C", (), {
-        "start": lambda self: None, "stop": lambda self: {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}})())
-    monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", "2", "--steps", "8", "--warmup", "3"])
-    monkeypatch.setenv("WORLD_SIZE", "2")
-    monkeypatch.setenv("RANK", "0")
-    monkeypatch.setenv("LOCAL_RANK", "0")
+    _fake_run(monkeypatch, ["--gpus", "2", "--steps", "8", "--warmup", "3"],
+              {"WORLD_SIZE": "2", "RANK": "0", "LOCAL_RANK": "0"})
     bench.main()
     lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -392,41 +381,9 @@ def test_moe_mode_prints_a_complete_line(monkeypatch, capsys, gpus):
     """`--model qwen3.6-35b-a3b`: the expert-parallel workload's line (LM-head
     roofline kernel, replicated + expert bytes, no timed CPU reference)."""
     import json
-    import sys
-    import torch
-    import torch.distributed as dist
-    import myllm_b200
-    _dry_run(monkeypatch)
-
-    class Event:
-        def __init__(self, enable_timing=False):
-            pass
-
-        def record(self, stream=None):
-            pass
-
-        def elapsed_time(self, other):
-            return 1.0
-
-    class Work:
-        def wait(self):
-            pass
-
-    monkeypatch.setattr(torch.cuda, "Event", Event)
-    for fn in ("synchronize", "set_device", "current_stream"):
-        monkeypatch.setattr(torch.cuda, fn, lambda *a: None)
-    for fn in ("init_process_group", "barrier", "broadcast_object_list", "destroy_process_group"):
-        monkeypatch.setattr(dist, fn, lambda *a, **k: None)
-    monkeypatch.setattr(dist, "all_reduce", lambda t, op=None, async_op=False: Work() if async_op else None)
-    monkeypatch.setattr(myllm_b200, "CudaLLM", _FakeLLM)
-    monkeypatch.setattr(bench, "ensure_model", lambda name, r, w, d: (bench.model_spec(name)[0], "unused"))
-    monkeypatch.setattr(bench, "ClockSampler", lambda gpu: type("C", (), {
-        "start": lambda self: None, "stop": lambda self: {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}})())
-    monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", str(gpus), "--model", "qwen3.6-35b-a3b", "--prompt", "64",
-                                      "--steps", "8", "--warmup", "3", "--max-sequence", "1024"])
-    monkeypatch.setenv("WORLD_SIZE", str(gpus))
-    monkeypatch.setenv("RANK", "0")
-    monkeypatch.setenv("LOCAL_RANK", "0")
+    _fake_run(monkeypatch, ["--gpus", str(gpus), "--model", "qwen3.6-35b-a3b", "--prompt", "64", "--steps", "8",
+                            "--warmup", "3", "--max-sequence", "1024"],
+              {"WORLD_SIZE": str(gpus), "RANK": "0", "LOCAL_RANK": "0"})
     bench.main()
     line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
     assert REQUIRED <= set(line)
