@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-1 kernel sweep (N = 1 only)")
     ap.add_argument("--no-scaling-base", action="store_true",
                     help="skip the single-GPU run of the N > 1 workload (N = 1 only)")
+    ap.add_argument("--allreduce", choices=["nccl", "p2p"], default=None,
+                    help="tensor-parallel decode all-reduce: NCCL (default) or the peer-memory kernel")
     return ap.parse_args()
 
 
@@ -641,6 +643,7 @@ def workload_config(name, spec, args, world) -> dict:
             "layers": spec.layers, "hidden": spec.hidden, "ffn": spec.expert_ffn if moe else spec.ffn,
             "vocab": spec.vocab,
             "parallelism": (f"ep{world}" if moe else f"tp{world}") if world > 1 else "single GPU",
+            **({"decode_allreduce": os.environ.get("CUDALLM_ALLREDUCE") or "nccl"} if world > 1 and not moe else {}),
             "l2": "no flush: weights (GB) exceed the 126 MB L2 every step"}
 
 
@@ -708,6 +711,8 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
 def bench_cuda(args):
     import torch
     import torch.distributed as dist
+    if args.allreduce:
+        os.environ["CUDALLM_ALLREDUCE"] = args.allreduce  # read when the model is created
     world, rank, local = dist_setup(args)
     torch.cuda.set_device(local)
     if world > 1:

@@ -335,6 +335,19 @@ def test_tensor_parallel_run_prints_a_complete_line(monkeypatch, capsys):
     assert REQUIRED <= set(line) and line["n_gpus"] == 2 and line["config"]["parallelism"] == "tp2"
     assert line["collectives"]["all_reduce"] == 2 * sg.CONFIGS["qwen2.5-14b"].layers
     assert line["collectives"]["all_reduce_us"] > 0 and line["vs_baseline"] is not None
+    assert line["config"]["decode_allreduce"] == "nccl"
+
+
+def test_peer_allreduce_switch(monkeypatch, capsys):
+    import json
+    import os
+    # registered with monkeypatch, so the value the bench sets is undone afterwards
+    monkeypatch.setenv("CUDALLM_ALLREDUCE", "")
+    _fake_run(monkeypatch, ["--gpus", "2", "--steps", "8", "--warmup", "3", "--allreduce", "p2p"],
+              {"WORLD_SIZE": "2", "RANK": "0", "LOCAL_RANK": "0"})
+    bench.main()
+    line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
+    assert os.environ["CUDALLM_ALLREDUCE"] == "p2p" and line["config"]["decode_allreduce"] == "p2p"
 
 
 @pytest.mark.parametrize("gpus,model,expect", [(1, None, "qwen2.5-7b"), (2, None, "qwen2.5-14b"),
