@@ -2,6 +2,7 @@
 and its pure host queries agree with the GGUF block sizes."""
 import os
 import re
+import shutil
 
 import pytest
 
@@ -184,3 +185,18 @@ def test_backend_queries_without_a_model():
     assert lib.cudallm_available(None) == 0
     out = (ctypes.c_uint64 * 3)()
     assert lib.cudallm_expert_cache(None, out) == 1  # CUDALLM_EINVAL
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None or shutil.which("g++") is None, reason="needs gcc and g++")
+@pytest.mark.parametrize("header,lang", [("cudallm.h", "c"), ("cudallm_kernels.h", "c"),
+                                         ("cuda_llm.h", "c++"), ("cuda_moe_llm.h", "c++")])
+def test_headers_stand_alone(tmp_path, header, lang):
+    """The C-ABI headers compile as plain C11 (cgo, ctypes-generated stubs and
+    other C hosts include them); the C++ API headers as C++17, each on its own."""
+    import subprocess
+    src = tmp_path / ("h.c" if lang == "c" else "h.cpp")
+    src.write_text(f'#include "{header}"\nint main(void) {{ return 0; }}\n')
+    cmd = (["gcc", "-std=c11"] if lang == "c" else ["g++", "-std=c++17"]) + [
+        "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", INCLUDE, "-I", "/usr/local/cuda/include", str(src)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
