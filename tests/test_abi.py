@@ -200,3 +200,26 @@ def test_headers_stand_alone(tmp_path, header, lang):
         "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", INCLUDE, "-I", "/usr/local/cuda/include", str(src)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_a_c_host_links_and_calls_the_backend_abi(tmp_path):
+    """C linkage of the backend ABI: a C program built against include/ and
+    linked to libcudallm.so reads a model's header and the shard plans."""
+    import subprocess
+    root = os.path.dirname(INCLUDE)
+    exe = str(tmp_path / "c_abi_check")
+    libdir = os.path.dirname(_native.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", INCLUDE,
+                        os.path.join(root, "tests", "sanitize", "c_abi_check.c"), "-L", libdir, "-lcudallm",
+                        "-Wl,-rpath," + libdir, "-o", exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    model = str(tmp_path / "tiny.gguf")
+    sg.write_qwen2(sg.tiny_spec(seed=7), model)
+    r = subprocess.run([exe, model], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    arch, tensors, q0, vrows, gather, er13, sr3 = r.stdout.split()
+    assert arch == "qwen2" and int(tensors) == len(sg.qwen2_tensors(sg.tiny_spec(seed=7)))
+    # 14B at 8 ranks, rank 7: heads 35..39, the last 19008 vocabulary rows, gathered attention
+    assert (int(q0), int(vrows), int(gather)) == (35, 19008, 1)
+    assert (int(er13), int(sr3)) == (13 % 4, 3 % 4)
