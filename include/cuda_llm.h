@@ -20,6 +20,14 @@
 #include <string>
 #include <vector>
 
+// The C++ API is exported from libcudallm.so (which builds everything else
+// with hidden visibility), so C++ hosts can link against it.
+#if defined(__GNUC__)
+#define CUDALLM_CXX_API __attribute__((visibility("default")))
+#else
+#define CUDALLM_CXX_API
+#endif
+
 namespace cudallm {
 
 // Byte accounting returned by every backend (memory_stats.h:11-36 layout).
@@ -104,11 +112,12 @@ struct TensorParallelShard {
 
 // Throws std::invalid_argument for a rank / world or a shape the split does
 // not take.  Host only: needs no GPU.
-TensorParallelShard plan_tensor_parallel(std::size_t feed_forward, std::size_t vocabulary, std::size_t heads,
-                                         std::size_t kv_heads, std::size_t head_size, std::size_t o_block, int world,
-                                         int rank);
+CUDALLM_CXX_API TensorParallelShard plan_tensor_parallel(std::size_t feed_forward, std::size_t vocabulary,
+                                                         std::size_t heads, std::size_t kv_heads,
+                                                         std::size_t head_size, std::size_t o_block, int world,
+                                                         int rank);
 
-class CudaLLM {
+class CUDALLM_CXX_API CudaLLM {
 public:
     // device < 0 uses the current CUDA device.
     explicit CudaLLM(const std::string& gguf_path, std::size_t max_sequence = 0, int device = -1,

@@ -33,7 +33,7 @@ inline int ep_expert_rank(std::size_t expert, int world) noexcept { return (int)
 inline std::size_t ep_local_index(std::size_t expert, int world) noexcept { return expert / (std::size_t)world; }
 inline int ep_shared_rank(std::size_t layer, int world) noexcept { return (int)(layer % (std::size_t)world); }
 
-class CudaMoeLLM {
+class CUDALLM_CXX_API CudaMoeLLM {
 public:
     // parallel.world > 1: expert parallel — expert e lives on rank
     // e % world; attention, DeltaNet and the LM head are replicated.
@@ -72,6 +72,6 @@ private:
 };
 
 // "qwen2", "qwen35moe", ...: the general.architecture of a GGUF file.
-std::string gguf_architecture(const std::string& gguf_path);
+CUDALLM_CXX_API std::string gguf_architecture(const std::string& gguf_path);
 
 }  // namespace cudallm

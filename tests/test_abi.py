@@ -223,3 +223,27 @@ def test_a_c_host_links_and_calls_the_backend_abi(tmp_path):
     # 14B at 8 ranks, rank 7: heads 35..39, the last 19008 vocabulary rows, gathered attention
     assert (int(q0), int(vrows), int(gather)) == (35, 19008, 1)
     assert (int(er13), int(sr3)) == (13 % 4, 3 % 4)
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_a_cxx_host_links_the_cxx_api(tmp_path):
+    """The C++ API (cuda_llm.h, cuda_moe_llm.h) is exported from the shared
+    library: a C++17 program links it, plans shards, reads a model's
+    architecture, and gets std::runtime_error (not a crash) when it builds a
+    model on a host without a GPU."""
+    import subprocess
+    import torch
+    root = os.path.dirname(INCLUDE)
+    exe = str(tmp_path / "cxx_api_check")
+    libdir = os.path.dirname(_native.LIB_PATH)
+    r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-I", INCLUDE,
+                        os.path.join(root, "tests", "sanitize", "cxx_api_check.cpp"), "-L", libdir, "-lcudallm",
+                        "-Wl,-rpath," + libdir, "-o", exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    model = str(tmp_path / "tiny.gguf")
+    sg.write_qwen2(sg.tiny_spec(seed=7), model)
+    r = subprocess.run([exe, model], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    arch, q0, gather, outcome = r.stdout.split()
+    assert (arch, q0, gather) == ("qwen2", "35", "1")
+    assert outcome == ("constructed" if torch.cuda.is_available() else "runtime_error")
