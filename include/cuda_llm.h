@@ -47,6 +47,20 @@ struct MemoryStats {
         }
         return t;
     }
+
+    // Converts to any stats struct with these five fields, such as the
+    // reference's MemoryStats, so that callers written against it (a generic
+    // generate<Backend> storing backend.memory_stats()) compile unchanged.
+    template <typename Stats>
+    operator Stats() const {
+        Stats s{};
+        s.weight_bytes = weight_bytes;
+        s.kv_cache_bytes = kv_cache_bytes;
+        s.recurrent_state_bytes = recurrent_state_bytes;
+        s.intermediate_bytes = intermediate_bytes;
+        s.intermediate_is_estimate = intermediate_is_estimate;
+        return s;
+    }
 };
 
 // Model hyper-parameters read from GGUF metadata (model.h:14-35 fields that
@@ -79,6 +93,12 @@ struct ModelConfig {
     std::size_t ssm_group_count = 0;
     std::size_t ssm_time_step_rank = 0;
     std::size_t ssm_inner_size = 0;
+    // tokenizer tables, for callers that build their tokenizer from the
+    // backend's config (model.h:30-32): tokenizer.ggml.tokens / .merges /
+    // .pre; empty when the file carries only a token count
+    std::vector<std::string> vocabulary;
+    std::vector<std::string> merges;
+    std::string tokenizer_pre;
 };
 
 // Rank layout for multi-GPU runs.  nccl_id is the 128-byte ncclUniqueId that

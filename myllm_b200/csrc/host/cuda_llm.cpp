@@ -51,6 +51,9 @@ ModelConfig read_qwen2_config(const GgufFile& f) {
     c.context_length = f.size("qwen2.context_length");
     c.vocabulary_size = f.array_length("tokenizer.ggml.tokens");
     if (c.vocabulary_size == 0) c.vocabulary_size = f.size("tokenizer.ggml.tokens_count");
+    c.vocabulary = f.strings("tokenizer.ggml.tokens");
+    c.merges = f.strings("tokenizer.ggml.merges");
+    c.tokenizer_pre = f.text("tokenizer.ggml.pre");
     if (c.embedding_size % c.attention_head_count != 0)
         throw std::runtime_error("embedding size must be divisible by attention head count");
     if (c.attention_head_count % c.kv_head_count != 0)

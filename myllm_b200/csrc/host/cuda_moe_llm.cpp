@@ -72,6 +72,9 @@ ModelConfig read_moe_config(const GgufFile& f) {
     c.ssm_inner_size = f.size(a + "ssm.inner_size");
     c.vocabulary_size = f.array_length("tokenizer.ggml.tokens");
     if (c.vocabulary_size == 0) c.vocabulary_size = f.size("tokenizer.ggml.tokens_count");
+    c.vocabulary = f.strings("tokenizer.ggml.tokens");
+    c.merges = f.strings("tokenizer.ggml.merges");
+    c.tokenizer_pre = f.text("tokenizer.ggml.pre");
     c.head_size = f.size(a + "attention.key_length");
     if (f.size(a + "attention.value_length") != c.head_size)
         throw std::runtime_error("qwen35moe key/value head dimensions differ");

@@ -187,7 +187,15 @@ GgufFile::GgufFile(const std::string& path) : path_(path) {
                 const uint32_t et = c.get<uint32_t>();
                 const uint64_t n = c.get<uint64_t>();
                 arrays_[key] = (std::size_t)n;
-                for (uint64_t j = 0; j < n; ++j) skip_value(c, et);
+                if (et == kString) {
+                    // every string takes at least its 8-byte length
+                    if (n > (file_size_ - c.position()) / 8) throw std::runtime_error("truncated GGUF file");
+                    std::vector<std::string>& v = string_arrays_[key];
+                    v.reserve((std::size_t)n);
+                    for (uint64_t j = 0; j < n; ++j) v.push_back(c.str());
+                } else {
+                    for (uint64_t j = 0; j < n; ++j) skip_value(c, et);
+                }
                 break;
             }
             default: throw std::runtime_error("unsupported GGUF metadata type " + std::to_string(type));
@@ -275,6 +283,12 @@ double GgufFile::real(const std::string& key, double fallback) const {
 std::string GgufFile::text(const std::string& key, const std::string& fallback) const {
     const auto it = texts_.find(key);
     return it == texts_.end() ? fallback : it->second;
+}
+
+const std::vector<std::string>& GgufFile::strings(const std::string& key) const {
+    static const std::vector<std::string> none;
+    const auto it = string_arrays_.find(key);
+    return it == string_arrays_.end() ? none : it->second;
 }
 
 std::size_t GgufFile::array_length(const std::string& key) const {

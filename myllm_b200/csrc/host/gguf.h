@@ -69,6 +69,9 @@ public:
     double real(const std::string& key, double fallback) const;
     std::string text(const std::string& key, const std::string& fallback = {}) const;
     std::size_t array_length(const std::string& key) const;  // 0 if absent
+    // The elements of a string array (tokenizer vocabulary, merges); empty if
+    // the key is absent or not an array of strings.
+    const std::vector<std::string>& strings(const std::string& key) const;
 
     // pread bytes [offset, offset + bytes) of a tensor's payload.
     void read(const TensorInfo& t, std::size_t offset, void* dst, std::size_t bytes) const;
@@ -87,6 +90,7 @@ private:
     std::unordered_map<std::string, double> reals_;
     std::unordered_map<std::string, std::string> texts_;
     std::unordered_map<std::string, std::size_t> arrays_;
+    std::unordered_map<std::string, std::vector<std::string>> string_arrays_;
     std::vector<TensorInfo> tensors_;
     std::unordered_map<std::string, std::size_t> index_;
     std::unordered_set<std::string> loaded_;

@@ -247,3 +247,16 @@ def test_a_cxx_host_links_the_cxx_api(tmp_path):
     arch, q0, gather, outcome = r.stdout.split()
     assert (arch, q0, gather) == ("qwen2", "35", "1")
     assert outcome == ("constructed" if torch.cuda.is_available() else "runtime_error")
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_generic_backend_host_compiles():
+    """A generic host of the reference's backend contract (generate<Backend>
+    style: capacity checks, stop token, tokenizer tables, stats in the
+    caller's own struct) compiles for both CUDA backends."""
+    import subprocess
+    root = os.path.dirname(INCLUDE)
+    r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", INCLUDE,
+                        os.path.join(root, "tests", "sanitize", "generic_backend_check.cpp")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

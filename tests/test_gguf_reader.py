@@ -16,6 +16,7 @@ import struct
 import subprocess
 import sys
 
+import numpy as np
 import pytest
 
 from myllm_b200 import _native
@@ -118,7 +119,8 @@ CORRUPT = {
     "nested arrays": (raw_gguf([sg._gguf_str("k") + struct.pack("<I", 9) + struct.pack("<IQ", 9, 1) * 100 +
                                 struct.pack("<IQ", 0, 0)]), "nested too deeply"),
     "array of huge strings": (raw_gguf([sg._gguf_str("k") + struct.pack("<IIQ", 9, 8, 3) + struct.pack("<Q", 1 << 60)]),
-                              "truncated GGUF file"),
+                              "invalid GGUF string length"),
+    "string array count": (raw_gguf([sg._gguf_str("k") + struct.pack("<IIQ", 9, 8, 1 << 40)]), "truncated GGUF file"),
     "tensor rank": (raw_gguf([ARCH], [tensor_info("t", [], sg.F32)]), "invalid tensor rank"),
     "tensor type": (raw_gguf([ARCH], [tensor_info("t", [32], 99)]), "unsupported GGUF tensor type"),
     "block alignment": (raw_gguf([ARCH], [tensor_info("t", [100], sg.Q4_K)]), "not block aligned"),
@@ -205,3 +207,35 @@ def test_reader_under_address_and_undefined_behavior_sanitizers(models, tmp_path
         r.stderr[-3000:]
     accepted, rejected = map(int, r.stdout.split())
     assert accepted >= 2 and accepted + rejected == len(corpus)
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_tokenizer_tables_are_read(tmp_path):
+    """tokenizer.ggml.tokens / .merges / .pre, which a caller building its
+    tokenizer from the backend's config needs (model.h:30-32), read back
+    entry for entry through the product's reader (under ASan / UBSan), and
+    cuts inside the tables are errors, not crashes."""
+    tokens = [f"tok{i}" for i in range(997)] + ["<|im_end|>", "Ġthe", "中文"]
+    merges = [f"a{i} b{i}" for i in range(499)] + ["Ġ t"]
+    meta = {"general.architecture": "qwen2", "tokenizer.ggml.pre": "qwen2",
+            "tokenizer.ggml.tokens": tokens, "tokenizer.ggml.merges": merges}
+    t = sg.TensorSpec("t", sg.F32, (4,), lambda: np.zeros(4, dtype=np.float32).view(np.uint8))
+    path = str(tmp_path / "vocab.gguf")
+    sg.write_gguf(path, meta, [t])
+    exe = str(tmp_path / "strings")
+    build = subprocess.run(["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined",
+                            "-fno-sanitize-recover=all", "-I", os.path.join(ROOT, "myllm_b200", "csrc", "host"),
+                            os.path.join(ROOT, "tests", "sanitize", "gguf_strings_check.cpp"),
+                            os.path.join(ROOT, "myllm_b200", "csrc", "host", "gguf.cpp"), "-o", exe],
+                           capture_output=True, text=True, timeout=300)
+    assert build.returncode == 0, build.stderr[-2000:]
+    r = subprocess.run([exe, path], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.splitlines() == ["1000", "500", "tok0", "中文", "a0 b0", "Ġ t", "qwen2"]
+    data = open(path, "rb").read()
+    for cut in range(24, header_length(data), 97):
+        p = str(tmp_path / f"cut{cut}.gguf")
+        with open(p, "wb") as f:
+            f.write(data[:cut])
+        r = subprocess.run([exe, p], capture_output=True, text=True, timeout=60)
+        assert r.returncode == 0 and r.stdout.startswith("error: "), (cut, r.stdout, r.stderr[-500:])
