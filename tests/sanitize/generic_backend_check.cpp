@@ -1,5 +1,5 @@
 // The members a generic host of the reference's backend contract uses
-// (a generate<Backend> loop and its helpers: capacity and protocol checks,
+// (a generate<Backend> loop and its helpers: profiling switches, capacity and protocol checks,
 // stop tokens from config().eos_token_id, a tokenizer built from
 // config().vocabulary / merges / tokenizer_pre, stats kept in the caller's own
 // memory-stats struct), instantiated for both CUDA backends.  Compile-only:
@@ -30,11 +30,14 @@ std::size_t drive(Backend& backend, std::vector<std::int32_t> ids) {
     std::size_t tables = config.vocabulary.size() + config.merges.size() + config.tokenizer_pre.size();
     std::vector<std::int32_t> stop{config.eos_token_id};
     const bool gpu = backend.uses_gpu();
+    backend.enable_profiling("profile.csv");          // the CLI's call for a non-Metal backend
+    backend.enable_profiling("profile.csv", false);   // and the two-argument form
     backend.reset();
     std::int32_t next = backend.prefill(ids);
     next = backend.decode(next);
     CallerMemoryStats memory;
     memory = backend.memory_stats();
+    backend.disable_profiling();
     return tables + stop.size() + (std::size_t)next + (std::size_t)memory.weight_bytes + (gpu ? 1 : 0) +
            backend.position() + config.embedding_size;
 }
