@@ -211,7 +211,7 @@ def test_a_c_host_links_and_calls_the_backend_abi(tmp_path):
     exe = str(tmp_path / "c_abi_check")
     libdir = os.path.dirname(_native.LIB_PATH)
     r = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", INCLUDE,
-                        os.path.join(root, "tests", "sanitize", "c_abi_check.c"), "-L", libdir, "-lcudallm",
+                        os.path.join(root, "tests", "native", "c_abi_check.c"), "-L", libdir, "-lcudallm",
                         "-Wl,-rpath," + libdir, "-o", exe], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     model = str(tmp_path / "tiny.gguf")
@@ -237,7 +237,7 @@ def test_a_cxx_host_links_the_cxx_api(tmp_path):
     exe = str(tmp_path / "cxx_api_check")
     libdir = os.path.dirname(_native.LIB_PATH)
     r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-I", INCLUDE,
-                        os.path.join(root, "tests", "sanitize", "cxx_api_check.cpp"), "-L", libdir, "-lcudallm",
+                        os.path.join(root, "tests", "native", "cxx_api_check.cpp"), "-L", libdir, "-lcudallm",
                         "-Wl,-rpath," + libdir, "-o", exe], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     model = str(tmp_path / "tiny.gguf")
@@ -257,6 +257,6 @@ def test_generic_backend_host_compiles():
     import subprocess
     root = os.path.dirname(INCLUDE)
     r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I", INCLUDE,
-                        os.path.join(root, "tests", "sanitize", "generic_backend_check.cpp")],
+                        os.path.join(root, "tests", "native", "generic_backend_check.cpp")],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr

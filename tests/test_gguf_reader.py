@@ -183,7 +183,7 @@ def test_reader_under_address_and_undefined_behavior_sanitizers(models, tmp_path
     exe = str(tmp_path / "gguf_check")
     build = subprocess.run(["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined",
                             "-fno-sanitize-recover=all", "-I", os.path.join(ROOT, "myllm_b200", "csrc", "host"),
-                            os.path.join(ROOT, "tests", "sanitize", "gguf_check.cpp"),
+                            os.path.join(ROOT, "tests", "native", "gguf_check.cpp"),
                             os.path.join(ROOT, "myllm_b200", "csrc", "host", "gguf.cpp"), "-o", exe],
                            capture_output=True, text=True, timeout=300)
     assert build.returncode == 0, build.stderr[-2000:]
@@ -225,7 +225,7 @@ def test_tokenizer_tables_are_read(tmp_path):
     exe = str(tmp_path / "strings")
     build = subprocess.run(["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined",
                             "-fno-sanitize-recover=all", "-I", os.path.join(ROOT, "myllm_b200", "csrc", "host"),
-                            os.path.join(ROOT, "tests", "sanitize", "gguf_strings_check.cpp"),
+                            os.path.join(ROOT, "tests", "native", "gguf_strings_check.cpp"),
                             os.path.join(ROOT, "myllm_b200", "csrc", "host", "gguf.cpp"), "-o", exe],
                            capture_output=True, text=True, timeout=300)
     assert build.returncode == 0, build.stderr[-2000:]

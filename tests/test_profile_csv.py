@@ -38,7 +38,7 @@ def compile_and_run(sources, include, out_csv, tmp_path, name):
 @pytest.fixture(scope="module")
 def ours(tmp_path_factory):
     t = tmp_path_factory.mktemp("profile")
-    return compile_and_run([os.path.join(ROOT, "tests", "sanitize", "profile_check.cpp"),
+    return compile_and_run([os.path.join(ROOT, "tests", "native", "profile_check.cpp"),
                             os.path.join(HOST, "profile.cpp")], HOST, str(t / "ours.csv"), t, "ours")
 
 
@@ -68,7 +68,7 @@ def test_rows_and_derived_columns(ours):
                     reason="reference sources not present")
 def test_matches_the_reference_profiler(ours, tmp_path):
     ref_dir = oracle.REFERENCE_SOURCES
-    ref = compile_and_run([os.path.join(ROOT, "tests", "sanitize", "ref_profile_check.cpp"),
+    ref = compile_and_run([os.path.join(ROOT, "tests", "native", "ref_profile_check.cpp"),
                            os.path.join(ref_dir, "profiler.cpp")], ref_dir, str(tmp_path / "ref.csv"), tmp_path, "ref")
     assert ref[0] == ours[0]  # the header
     assert len(ref) == len(ours)
