@@ -695,10 +695,12 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
                        "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
                        "peak_kind": peak_kind},
         "roofline": {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": kern["gbs"] / peak, "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
+                     "frac": kern["gbs"] / peak if kern["gbs"] else None,
+                     "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
                      "kernel": kern["kernel"], "shape": kern["shape"],
                      "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
-                     "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)"},
+                     "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)",
+                     **({"error": kern["error"]} if "error" in kern else {})},
         "cpu_baseline": cpu,
         "kernel_sweep": sweep,
         "scaling_base": base,
@@ -778,12 +780,22 @@ def bench_cuda(args):
 
     moe = isinstance(spec, sg.MoeSpec)
     peak, peak_kind = measured_peaks()
-    kern = time_head_kernel(spec, args.kernel_iters) if moe else time_gateup_kernel(spec, args.kernel_iters)
-    sweep = kernel_sweep(peak, spec.seed) if world == 1 and not args.no_sweep and not moe else None
-    if sweep is not None:
+    # the reports below are each guarded: a failure is recorded in its own
+    # field, and the headline numbers already measured still print
+    try:
+        kern = time_head_kernel(spec, args.kernel_iters) if moe else time_gateup_kernel(spec, args.kernel_iters)
+    except Exception as e:
+        kern = {"kernel": None, "shape": None, "bytes_per_launch": None, "avg_launch_us": None, "gbs": None,
+                "error": f"{type(e).__name__}: {e}"}
+    sweep = None
+    if world == 1 and not args.no_sweep and not moe:
+        try:
+            sweep = kernel_sweep(peak, spec.seed)
+        except Exception as e:
+            sweep = {"error": f"{type(e).__name__}: {e}"}
         try:
             sweep["moe_kernels"] = moe_kernel_times(peak, spec.seed)
-        except Exception as e:  # recorded; the headline numbers stand
+        except Exception as e:
             sweep["moe_kernels"] = {"error": f"{type(e).__name__}: {e}"}
     if world > 1:
         dist.barrier()

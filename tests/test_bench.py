@@ -416,3 +416,22 @@ def test_launch_count_includes_the_peer_allreduce(monkeypatch):
     monkeypatch.setenv("CUDALLM_ALLREDUCE", "p2p")
     p2p = bench.make_line("qwen2.5-14b", spec, args, 2, 0, **kw)["gpu_launches"]
     assert p2p - nccl == 2 * spec.layers * 10
+
+
+def test_a_failing_report_does_not_lose_the_line(monkeypatch, capsys):
+    """The roofline kernel timing and the sweep raising: the line still
+    prints, with each failure recorded in its own field."""
+    import json
+
+    def boom(*a, **k):
+        raise RuntimeError("planted")
+    _fake_run(monkeypatch, ["--steps", "8", "--warmup", "3"], {})
+    monkeypatch.setattr(bench, "time_gateup_kernel", boom)
+    monkeypatch.setattr(bench, "kernel_sweep", boom)
+    monkeypatch.setattr(bench, "run_cpu_baseline", lambda *a, **k: {"value": 0.2})
+    monkeypatch.setattr(bench, "scaling_base", lambda args, dev: None)
+    bench.main()
+    line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
+    assert REQUIRED <= set(line) and line["value"] > 0
+    assert line["roofline"]["error"] == "RuntimeError: planted" and line["roofline"]["frac"] is None
+    assert line["kernel_sweep"]["error"] == "RuntimeError: planted" and "moe_kernels" in line["kernel_sweep"]
