@@ -9,7 +9,10 @@
 // Multi-GPU: one process per GPU.  With world > 1 the dense Qwen2 model is
 // tensor-parallel (column-split QKV / gate / up, row-split o_proj / down,
 // NCCL all-reduce after each row split); every rank calls the same methods
-// with the same arguments and receives the same token.
+// with the same arguments and receives the same token.  A process drives one
+// device: the kernels' shared-memory limits are raised once per process, so
+// models on two devices of one process are not supported (the second
+// device's large-shared-memory launches would return an error status).
 #pragma once
 
 #include <array>
