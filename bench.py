@@ -40,8 +40,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--prompt", type=int, default=512)
-    ap.add_argument("--max-sequence", type=int, default=4096)
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="prompt tokens (default: the BASELINE config's: 512 for the 7B shape, 1024 for the "
+                         "14B shape, 64 for qwen3.6-35b-a3b)")
+    ap.add_argument("--max-sequence", type=int, default=None,
+                    help="KV capacity (default: 4096, or 1024 for qwen3.6-35b-a3b)")
     ap.add_argument("--model", default=None, help="synthetic config name (default by --gpus)")
     ap.add_argument("--kernel-iters", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -50,13 +53,31 @@ def parse():
                     help="skip the single-GPU run of the N > 1 workload (N = 1 only)")
     ap.add_argument("--allreduce", choices=["nccl", "p2p"], default=None,
                     help="tensor-parallel decode all-reduce: NCCL (default) or the peer-memory kernel")
-    return ap.parse_args()
+    ap.add_argument("--no-parity", action="store_true",
+                    help="N > 1: skip the check of the sharded run's tokens and logits against one GPU")
+    args = ap.parse_args()
+    return args
+
+
+# Prompt length and KV capacity of each BASELINE config (configs 2, 3, 4).
+CONFIG_RUN = {"qwen2.5-7b": (512, 4096), "qwen2.5-14b": (1024, 4096), "qwen3.6-35b-a3b": (64, 1024)}
 
 
 def model_name(args, world):
     if args.model:
         return args.model
     return "qwen2.5-7b" if world == 1 else "qwen2.5-14b"
+
+
+def for_model(args, name):
+    """A copy of args with prompt / max_sequence resolved for model `name`:
+    the flags where given, else the BASELINE config's values."""
+    import copy
+    prompt, cap = CONFIG_RUN.get(name, (512, 4096))
+    out = copy.copy(args)
+    out.prompt = args.prompt if args.prompt is not None else prompt
+    out.max_sequence = args.max_sequence if args.max_sequence is not None else cap
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -572,6 +593,7 @@ def scaling_base(args, device: int):
     from myllm_b200 import CudaLLM
     from myllm_b200 import synth_gguf as sg
     name = model_name(args, 2)
+    args = for_model(args, name)
     try:
         spec, path = ensure_model(name, 0, 1, None)
         llm = CudaLLM(path, max_sequence=args.max_sequence, device=device)
@@ -710,6 +732,33 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
     }
 
 
+def sharded_parity(path, args, device, prompt, run_tokens, last_logits) -> dict:
+    """Tokens and last logits of a sharded (tensor- or expert-parallel) run
+    against the same GGUF and prompt on this one GPU, unsharded: the greedy
+    token of the prefill and of every decode step (warm-up and timed) must be
+    identical, and the last step's logits within 1e-4 of the one-GPU run's
+    (max-abs relative), the level every parity test holds.  The one-GPU
+    model is itself pinned to the reference CPULLM by the golden tests."""
+    import numpy as np
+    from myllm_b200 import CudaLLM
+    one = CudaLLM(path, max_sequence=args.max_sequence, device=device)
+    try:
+        toks = [one.prefill(prompt)]
+        for t in run_tokens[:-1]:
+            toks.append(one.decode(t))  # teacher-forced on the sharded run's own tokens
+        ref = one.last_logits()
+    finally:
+        one.close()
+    same = [int(a) == int(b) for a, b in zip(toks, run_tokens)]
+    err = float(np.abs(last_logits - ref).max() / np.abs(ref).max())
+    ok = all(same) and err <= 1e-4
+    return {"status": "ok" if ok else "mismatch",
+            "against": "the same GGUF and prompt unsharded on one GPU (CudaLLM, pinned to CPULLM by the goldens)",
+            "steps_compared": len(same), "tokens_identical": all(same),
+            "first_mismatch": None if all(same) else same.index(False),
+            "last_logits_rel_err": err, "tolerance": 1e-4}
+
+
 def bench_cuda(args):
     import torch
     import torch.distributed as dist
@@ -724,6 +773,7 @@ def bench_cuda(args):
     from myllm_b200 import CudaLLM, nccl_unique_id
     from myllm_b200 import synth_gguf as sg
     name = model_name(args, world)
+    raw_args, args = args, for_model(args, name)
     spec, path = ensure_model(name, rank, world, dist)
     nid = None
     if world > 1:
@@ -742,9 +792,11 @@ def bench_cuda(args):
     tok = llm.prefill(prompt)
     prefill_e2e = time.perf_counter() - t0
     prefill_ms = llm.last_call_ms()
+    run_tokens = [tok]
 
     for _ in range(args.warmup):
         tok = llm.decode(tok)
+        run_tokens.append(tok)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -755,16 +807,27 @@ def bench_cuda(args):
     for _ in range(args.steps):
         tok = llm.decode(tok)
         dev_ms += llm.last_call_ms()
+        run_tokens.append(tok)
     e2e_s = time.perf_counter() - t0
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
+    # the last step's full logits (a collective for a sharded model)
+    last_logits = llm.last_logits() if world > 1 and not args.no_parity else None
     vals = torch.tensor([dev_ms, e2e_s * 1e3, prefill_ms, prefill_e2e * 1e3], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms = [float(v) for v in vals.cpu()]
     llm.close()
+    parity = None
+    if world > 1 and not args.no_parity:
+        if rank == 0:
+            try:
+                parity = sharded_parity(path, args, local, prompt, run_tokens, last_logits)
+            except Exception as e:  # reported in the line; the measured numbers stand
+                parity = {"status": "error", "error": f"{type(e).__name__}: {e}"}
+        dist.barrier()
     collectives = None
     if world > 1:
         if isinstance(spec, sg.MoeSpec):  # one all-reduce of the MoE output per layer
@@ -809,10 +872,12 @@ def bench_cuda(args):
                                              "FP64 restatement, not a timed baseline)"}
     elif world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(path, spec)
-    base = scaling_base(args, local) if world == 1 and not args.no_scaling_base and not args.model else None
+    base = scaling_base(raw_args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     line = make_line(name, spec, args, world, rank, dev_ms=dev_ms, e2e_ms=e2e_ms, prefill_ms=prefill_ms,
                      prefill_e2e_ms=prefill_e2e_ms, kern=kern, peak=peak, peak_kind=peak_kind, sweep=sweep, cpu=cpu,
                      base=base, collectives=collectives, clk=clk)
+    if parity is not None:
+        line["parity"] = parity
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -823,6 +888,7 @@ def bench_reference(args):
     if rank != 0:
         return
     name = model_name(args, world)
+    args = for_model(args, name)
     from myllm_b200 import synth_gguf as sg
     if name in sg.MOE_CONFIGS:
         print(json.dumps({"impl": "reference", "unavailable": "the reference's qwen35moe path is Metal-only "

@@ -9,10 +9,10 @@
 // Multi-GPU: one process per GPU.  With world > 1 the dense Qwen2 model is
 // tensor-parallel (column-split QKV / gate / up, row-split o_proj / down,
 // NCCL all-reduce after each row split); every rank calls the same methods
-// with the same arguments and receives the same token.  A process drives one
-// device: the kernels' shared-memory limits are raised once per process, so
-// models on two devices of one process are not supported (the second
-// device's large-shared-memory launches would return an error status).
+// with the same arguments and receives the same token.  One process may also
+// hold models on several devices (each model's calls run with its device
+// current): the kernels' shared-memory limits and SM counts are set up per
+// device, the first time a launch runs on it.
 #pragma once
 
 #include <array>

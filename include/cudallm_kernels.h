@@ -173,8 +173,9 @@ CL_API int cl_attn_decode_rope(const float* q, const float* k_new, const float* 
  * CPULLM allocate their scratch themselves).  The split partials live in a
  * fixed 2 MiB array compiled into the library (held by every GPU that loads
  * it until exit); requests needing more than
- * cl_attn_decode_noalloc_limit_bytes() (q_heads * ceil(max_len / 64) *
- * (head_dim + 2) * 4 bytes) return CL_ERR_LIMIT.  The first call on a device
+ * cl_attn_decode_noalloc_limit_bytes() return CL_ERR_LIMIT.  A request needs
+ * cl_attn_decode_workspace_bytes(q_heads, head_dim, max_len) =
+ * q_heads * min(32, ceil(max_len / 16)) * (head_dim + 2) * 4 bytes.  The first call on a device
  * looks up the array's device address with that device current; make that
  * first call before any stream capture.  All calls on a device share the
  * array, so calls that overlap on the GPU (e.g. on concurrent streams) race;
@@ -224,14 +225,20 @@ CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
  * (buffers[rank] = its own).  Every rank makes the same calls in the same
  * order.  n % 4 == 0, n <= max_n (the max_n the buffers were sized for), in
  * and out 16-byte aligned and not overlapping.  out receives the sum in rank
- * order 0..world-1, bit-identical on every rank.  A rank that waits more than
- * 20 s for the others sets the buffer's status word
- * (cl_peer_exchange_status: a device address; 0 = ok) and returns. */
+ * order 0..world-1, bit-identical on every rank.  A rank that waits longer
+ * than the wait limit (20 s unless cl_peer_set_wait_limit_ns changed it) for
+ * the others sets the buffer's status word (cl_peer_exchange_status: a
+ * device address; 0 = ok), skips the sum and returns; re-initialise every
+ * rank's buffer (cl_peer_exchange_init) before the ranks exchange again.
+ * cl_peer_set_wait_limit_ns sets the limit for later launches of this
+ * process (1 ms .. 120 s, else CL_ERR_INVALID); it has no counterpart in
+ * the reference. */
 CL_API size_t cl_peer_exchange_bytes(int max_n);
 CL_API int cl_peer_exchange_init(void* buffer, int max_n, cudaStream_t stream);
 CL_API const int* cl_peer_exchange_status(const void* buffer);
 CL_API int cl_peer_allreduce(const float* in, float* out, int n, int max_n, int rank, int world,
                              void* const* buffers, cudaStream_t stream);
+CL_API int cl_peer_set_wait_limit_ns(unsigned long long ns);
 
 /* ---- qwen35moe ---------------------------------------------------------- */
 /* y[n] = W[n,k] x for an FP32 row-major W (the router, DeltaNet alpha/beta

@@ -80,6 +80,7 @@ SIGNATURES = {
     "cl_peer_exchange_init": (c_int, [c_vp, c_int, c_vp]),
     "cl_peer_exchange_status": (c_vp, [c_vp]),
     "cl_peer_allreduce": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "cl_peer_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
     # backend
     "cudallm_last_error": (c_char_p, []),
     "cudallm_nccl_unique_id": (c_int, [c_vp]),

@@ -443,17 +443,8 @@ static int attn_decode_launch(const float* q, const float* k_cache, const float*
     const int splits = attn_splits(max_len);
     float* part = static_cast<float*>(workspace);
     const size_t smem = attn_decode_smem(q_heads / kv_heads, head_dim);
-    static std::mutex mu;
-    static int configured_for = 48 * 1024;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if ((int)smem > configured_for) {
-            if (cudaFuncSetAttribute(attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                cudaSuccess)
-                return CL_ERR_CUDA;
-            configured_for = (int)smem;
-        }
-    }
+    static SmemLimit limit;
+    if (smem > 48 * 1024 && limit.ensure(attn_decode_split, (int)smem) != cudaSuccess) return CL_ERR_CUDA;
     if (launch_pdl(attn_decode_split, dim3(kv_heads, splits), dim3(kDecThreads), smem, stream, q, k_cache, v_cache,
                    len_dev, max_len, q_heads, kv_heads, head_dim, scale, part, rope) != cudaSuccess)
         return CL_ERR_CUDA;
@@ -494,13 +485,8 @@ CL_API int cl_attn_prefill(const float* q, const float* k_cache, const float* v_
         head_dim > kMaxHeadDim)
         return CL_ERR_INVALID;
     const size_t smem = prefill_smem(head_dim);
-    static int configured_for = 0;
-    if ((int)smem > configured_for) {
-        if (cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return CL_ERR_CUDA;
-        configured_for = (int)smem;
-    }
+    static SmemLimit limit;
+    if (limit.ensure(attn_prefill_kernel, (int)smem) != cudaSuccess) return CL_ERR_CUDA;
     return launch_pdl(attn_prefill_kernel, dim3(q_heads, (rows + kQT - 1) / kQT), dim3(kPreThreads), smem, stream,
                       q, k_cache, v_cache, pos0, rows, q_heads, kv_heads, head_dim, out) == cudaSuccess
                ? CL_OK

@@ -569,9 +569,8 @@ template <int T, bool X3>
 int launch_tc_fmt(const void* w, long long stride, int n, int k, const float* x, int m, const float* bias,
                   const float* residual, float* y, cudaStream_t stream) {
     using P = tc::Mode<X3>;
-    static const cudaError_t configured = cudaFuncSetAttribute(
-        tc::gemm_tc_kernel<T, X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P::kSmem);
-    if (configured != cudaSuccess) return CL_ERR_CUDA;
+    static SmemLimit limit;
+    if (limit.ensure(tc::gemm_tc_kernel<T, X3>, (int)P::kSmem) != cudaSuccess) return CL_ERR_CUDA;
     const dim3 grid((m + tc::BM - 1) / tc::BM, (n + tc::BN - 1) / tc::BN);
     return launch_pdl(tc::gemm_tc_kernel<T, X3>, grid, dim3(tc::kThreads), P::kSmem, stream,
                       static_cast<const uint8_t*>(w), stride, n, k, x, m, bias, residual, y) == cudaSuccess

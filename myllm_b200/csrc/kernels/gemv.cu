@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 namespace cl {
@@ -341,26 +342,21 @@ cudaError_t launch_cfg(const GemvParams& p, cudaStream_t stream) {
     const int threads = p.groups * p.group_warps * 32 + 32;
     const int smem = smem_stage_offset(p.groups, p.stages, NMAT * RPG, p.group_warps, p.k) +
                      p.groups * p.stages * p.stage_bytes;
+    static SmemLimit limit;
     static std::mutex mu;
-    static std::map<std::pair<int, int>, int> occ_cache;  // (threads, smem) -> CTAs per SM
-    static int sm_count = 0;
-    static bool attr_set = false;
+    static std::map<std::tuple<int, int, int>, int> occ_cache;  // (device, threads, smem) -> CTAs per SM
+    cudaError_t e = limit.ensure(kern, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    int sm_count = 0, dev = 0;
+    if ((e = device_sm_count(&sm_count)) != cudaSuccess || (e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     int occ = 0;
     {
         std::lock_guard<std::mutex> lock(mu);
-        if (!attr_set) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-            if (e != cudaSuccess) return e;
-            int dev = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-            attr_set = true;
-        }
-        auto it = occ_cache.find({threads, smem});
+        auto it = occ_cache.find({dev, threads, smem});
         if (it == occ_cache.end()) {
-            cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
             if (e != cudaSuccess) return e;
-            occ_cache[{threads, smem}] = occ;
+            occ_cache[{dev, threads, smem}] = occ;
         } else {
             occ = it->second;
         }

@@ -54,7 +54,6 @@
 #include "launch.cuh"
 
 #include <algorithm>
-#include <mutex>
 
 namespace cl {
 
@@ -662,16 +661,11 @@ Geo make_geo(int type, int nb, int nmat, int limit) {
 template <int F, bool SW, int F2>
 cudaError_t launch_cfg(const Params& p, int smem, cudaStream_t stream) {
     auto kern = gemv_mma_kernel<F, SW, F2>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    static int sm_count = 0;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    });
-    if (attr_err != cudaSuccess) return attr_err;
+    static SmemLimit limit;
+    cudaError_t e = limit.ensure(kern, kSmemMax);
+    if (e != cudaSuccess) return e;
+    int sm_count = 0;
+    if ((e = device_sm_count(&sm_count)) != cudaSuccess) return e;
     const int grid = std::min(p.tiles, sm_count);
     return launch_pdl(kern, dim3(grid), dim3(kThreads), (size_t)smem, stream, p);
 }

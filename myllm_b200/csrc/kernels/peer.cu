@@ -36,8 +36,13 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kThreads = 512;
 // A peer may start the same decode step seconds later (host jitter, a
-// profiler); only a rank that never arrives should trip this.
-constexpr unsigned long long kWaitLimitNs = 20ull * 1000 * 1000 * 1000;
+// profiler); only a rank that never arrives should trip this.  Process-wide,
+// read at each launch; cl_peer_set_wait_limit_ns changes it (tests shorten it
+// to make the wait run out quickly).
+constexpr unsigned long long kDefaultWaitLimitNs = 20ull * 1000 * 1000 * 1000;
+constexpr unsigned long long kMinWaitLimitNs = 1000ull * 1000;                // 1 ms
+constexpr unsigned long long kMaxWaitLimitNs = 120ull * 1000 * 1000 * 1000;  // 2 min
+unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 struct PeerHeader {
     uint32_t epoch[kMaxRanks];
@@ -71,7 +76,7 @@ CL_DEVINL unsigned long long global_ns() {
 
 __global__ void __launch_bounds__(kThreads)
     peer_allreduce_kernel(const float* __restrict__ in, float* __restrict__ out, int n, int rank, int world,
-                          size_t slot, const __grid_constant__ PeerBuffers peers) {
+                          size_t slot, unsigned long long wait_limit_ns, const __grid_constant__ PeerBuffers peers) {
     const int b = blockIdx.x;
     PeerHeader* mine = reinterpret_cast<PeerHeader*>(peers.buf[rank]);
     __shared__ uint32_t s_epoch;
@@ -103,7 +108,7 @@ __global__ void __launch_bounds__(kThreads)
         const uint32_t* f = &mine->flag[par][threadIdx.x];
         const unsigned long long t0 = global_ns();
         while ((int)(ld_acquire_sys(f) - e) < 0) {
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > wait_limit_ns) {
                 atomicOr(&mine->status, 1u);
                 s_fail = 1;
                 break;
@@ -173,9 +178,15 @@ CL_API int cl_peer_allreduce(const float* in, float* out, int n, int max_n, int 
         peers.buf[r] = static_cast<char*>(buffers[r]);
     }
     return launch_pdl(peer_allreduce_kernel, dim3(world), dim3(kThreads), 0, stream, in, out, n, rank, world,
-                      slot_floats(max_n), peers) == cudaSuccess
+                      slot_floats(max_n), g_wait_limit_ns, peers) == cudaSuccess
                ? CL_OK
                : CL_ERR_CUDA;
+}
+
+CL_API int cl_peer_set_wait_limit_ns(unsigned long long ns) {
+    if (ns < kMinWaitLimitNs || ns > kMaxWaitLimitNs) return CL_ERR_INVALID;
+    g_wait_limit_ns = ns;
+    return CL_OK;
 }
 
 }  // extern "C"

@@ -26,7 +26,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_LIB = os.path.join(HERE, "lib", "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_cpu.so")
-REFERENCE_SOURCES = "/root/reference"
+# The reference checkout (tianjin95/MyLLM sources) to compile the reference
+# checker from: MYLLM_REFERENCE_DIR.  Unset, only an already built
+# _ref/libref_cpu.so is used.
+REFERENCE_SOURCES = os.environ.get("MYLLM_REFERENCE_DIR", "")
 
 _port = None
 _ref = None
@@ -36,7 +39,7 @@ def build(reference: Optional[str] = None) -> None:
     """Build the port and, when the reference sources exist, the reference."""
     subprocess.run(["make", "-C", HERE, "port"], check=True, capture_output=True)
     ref = reference or REFERENCE_SOURCES
-    if os.path.isdir(ref):
+    if ref and os.path.isdir(ref):
         subprocess.run(["make", "-C", HERE, "ref", f"REF={ref}"], check=True,
                        capture_output=True)
 

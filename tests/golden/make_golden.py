@@ -22,6 +22,13 @@ Fixtures:
                      summary as qwen2_05b.  The reference holds ~35 GB of FP32
                      weights, so the harness and the CPULLM cross-check run
                      one after the other (--only-7b makes just this one).
+  qwen2_7b_long.npz  BASELINE config 2 at its full length: the bench's
+                     512-token prompt, prefill + 128 greedy decodes, the same
+                     summary (--only-7b-long).  The harness's fixture is
+                     written as soon as it finishes (cpullm_checked = 0), then
+                     rewritten with cpullm_checked = 1 once CPULLM itself has
+                     produced the same tokens (about 40 minutes of one core
+                     for each of the two runs).
 """
 from __future__ import annotations
 
@@ -97,6 +104,36 @@ def qwen2_7b(tmp: str) -> None:
                         **summary(logits))
 
 
+def qwen2_7b_long(tmp: str, prompt_len: int = 512, steps: int = 128) -> None:
+    """The bench workload end to end: the same prompt bench.py prefills
+    (prompt_ids(seed, 512)), then `steps` greedy decodes."""
+    spec = sg.CONFIGS["qwen2.5-7b"]
+    path = os.path.join(tmp, "q7b.gguf")
+    sha = sg.write_qwen2(spec, path)
+    prompt = sg.prompt_ids(spec.seed, prompt_len, spec.vocab)
+    out = os.path.join(HERE, "qwen2_7b_long.npz")
+    ref = oracle.ReferenceCPU(path)
+    tok, lg = ref.prefill(prompt)
+    tokens, logits = [tok], [lg]
+    for _ in range(steps):
+        tok, lg = ref.decode(tok)
+        tokens.append(tok)
+        logits.append(lg)
+    ref.close()
+    toks = np.array(tokens, dtype=np.int32)
+    summ = summary(np.stack(logits))
+    np.savez_compressed(out, sha256=np.array(sha), prompt=prompt, tokens=toks, cpullm_checked=np.array(0),
+                        **summ)
+    cpu = oracle.ReferenceCPULLM(path)
+    t = [cpu.prefill(prompt)]
+    for _ in range(steps):
+        t.append(cpu.decode(t[-1]))
+    cpu.close()
+    assert t == tokens, (t, tokens)
+    np.savez_compressed(out, sha256=np.array(sha), prompt=prompt, tokens=toks, cpullm_checked=np.array(1),
+                        **summ)
+
+
 def tiny(seed: int, tmp: str) -> None:
     spec = sg.tiny_spec(seed=seed)
     path = os.path.join(tmp, f"tiny{seed}.gguf")
@@ -153,9 +190,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-05b", action="store_true")
     ap.add_argument("--only-7b", action="store_true")
+    ap.add_argument("--only-7b-long", action="store_true")
     args = ap.parse_args()
     if not oracle.ref_available():
         oracle.build()
+    if args.only_7b_long:
+        with tempfile.TemporaryDirectory(dir=os.environ.get("MYLLM_GOLDEN_TMP")) as tmp:
+            qwen2_7b_long(tmp)
+        return
     if args.only_7b:
         with tempfile.TemporaryDirectory(dir=os.environ.get("MYLLM_GOLDEN_TMP")) as tmp:
             qwen2_7b(tmp)

@@ -69,6 +69,15 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.cl_status_string(4) == b"workspace missing or too small"
 
 
+def test_peer_wait_limit_bounds():
+    """The peer exchange's wait limit is settable within 1 ms .. 2 min."""
+    from myllm_b200 import _native
+    lib = _native.lib()
+    assert lib.cl_peer_set_wait_limit_ns(10) == 1            # below 1 ms
+    assert lib.cl_peer_set_wait_limit_ns(10 ** 12) == 1      # above 2 min
+    assert lib.cl_peer_set_wait_limit_ns(20 * 10 ** 9) == 0  # the default
+
+
 def test_peer_exchange_layout_and_argument_checks():
     """The tensor-parallel exchange buffer: a 256-byte header and two
     parities of 8 rank slots, each rounded up to 64 floats; bad arguments are

@@ -68,6 +68,10 @@ class _FakeLLM:
     def last_call_ms(self):
         return 2.0
 
+    def last_logits(self):
+        import numpy as np
+        return np.linspace(-1.0, 1.0, 64, dtype=np.float32)
+
     def close(self):
         pass
 
@@ -336,6 +340,25 @@ def test_tensor_parallel_run_prints_a_complete_line(monkeypatch, capsys):
     assert line["collectives"]["all_reduce"] == 2 * sg.CONFIGS["qwen2.5-14b"].layers
     assert line["collectives"]["all_reduce_us"] > 0 and line["vs_baseline"] is not None
     assert line["config"]["decode_allreduce"] == "nccl"
+    # config 3's prompt, and the sharded run checked against one GPU
+    assert "prompt 1024" in line["config"]["workload"]
+    assert line["parity"]["status"] == "ok" and line["parity"]["steps_compared"] == 1 + 3 + 8
+
+
+def test_sharded_parity_reports_a_mismatch(monkeypatch):
+    """A one-GPU run that disagrees at the third token is reported, not hidden."""
+    import argparse
+    import myllm_b200
+
+    class Diverging(_FakeLLM):
+        def decode(self, tok):
+            self.calls += 1
+            return tok + 1 if self.calls == 2 else tok
+
+    monkeypatch.setattr(myllm_b200, "CudaLLM", Diverging)
+    out = bench.sharded_parity("unused", argparse.Namespace(max_sequence=64), 0, [1, 2], [1, 1, 1, 1],
+                               _FakeLLM("x").last_logits())
+    assert out["status"] == "mismatch" and out["first_mismatch"] == 2 and not out["tokens_identical"]
 
 
 def test_peer_allreduce_switch(monkeypatch, capsys):
@@ -380,7 +403,7 @@ def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect)
     assert REQUIRED - {"clocks", "gpu_launches", "roofline"} <= set(line) and line["value"] == 0.25
     # the cuda arm's config, so that the driver pairs the two lines
     spec = bench.model_spec(expect)[0]
-    assert line["config"] == bench.workload_config(expect, spec, bench.parse(), gpus)
+    assert line["config"] == bench.workload_config(expect, spec, bench.for_model(bench.parse(), expect), gpus)
     assert line["cpu_baseline"]["kind"] == "reference" and "bounded sample" in line["cpu_baseline"]["sample"]
     assert line["e2e"] == {"value": 0.25, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     # other ranks print nothing

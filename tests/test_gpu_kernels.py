@@ -280,6 +280,43 @@ def test_attention_prefill(cuda, hq, hkv, d, pos0, rows):
         assert rel_err(got[r], ref) <= 1e-5, r
 
 
+def causal_attention_ref(q, kc, vc, hq, hkv, d, pos0, rows):
+    """float64 causal GQA attention of query rows at positions pos0.. against
+    cache rows 0..pos0+rows-1 (cpu_llm.cpp:816-827), all rows at once."""
+    out = np.zeros((rows, hq * d), dtype=np.float64)
+    grp = hq // hkv
+    n = pos0 + rows
+    mask = np.arange(n)[None, :] > (pos0 + np.arange(rows))[:, None]
+    for h in range(hq):
+        g = h // grp
+        qq = q[:, h * d:(h + 1) * d].astype(np.float64)
+        kk = kc[:n, g * d:(g + 1) * d].astype(np.float64)
+        s = qq @ kk.T / math.sqrt(d)
+        s[mask] = -np.inf
+        p = np.exp(s - s.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, h * d:(h + 1) * d] = p @ vc[:n, g * d:(g + 1) * d].astype(np.float64)
+    return out
+
+
+@pytest.mark.parametrize("hq,hkv,d,pos0,rows", [
+    (28, 4, 128, 0, 512),    # BASELINE config 2 (7B shape): the bench's 512-token prompt
+    (40, 8, 128, 0, 1024),   # BASELINE config 3 (14B shape): the 1024-token prompt
+    (28, 4, 128, 512, 256),  # a later chunk of a chunked prefill
+])
+def test_attention_prefill_long(cuda, hq, hkv, d, pos0, rows):
+    """Causal prefill attention at the prompt lengths the benchmarks prefill."""
+    cap = pos0 + rows
+    q = xvec(hq * d, rows, seed=93)
+    kc = xvec(hkv * d, cap, seed=94)
+    vc = xvec(hkv * d, cap, seed=95)
+    got = K.attn_prefill(torch.from_numpy(q).cuda(), torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda(),
+                         pos0, rows, hq, hkv, d).cpu().numpy()
+    ref = causal_attention_ref(q, kc, vc, hq, hkv, d, pos0, rows)
+    err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    assert err.max() <= 1e-5, (int(err.argmax()), float(err.max()))
+
+
 def test_argmax_lowest_index_on_ties(cuda):
     n = 152064
     x = torch.from_numpy(xvec(n, seed=100)[0]).cuda()

@@ -64,7 +64,7 @@ def test_rows_and_derived_columns(ours):
         assert float(r["arithmetic_intensity"]) == pytest.approx(int(r["flops"]) / (read + write), abs=1e-3)
 
 
-@pytest.mark.skipif(not os.path.exists(os.path.join(oracle.REFERENCE_SOURCES, "profiler.cpp")),
+@pytest.mark.skipif(not oracle.REFERENCE_SOURCES or not os.path.exists(os.path.join(oracle.REFERENCE_SOURCES, "profiler.cpp")),
                     reason="reference sources not present")
 def test_matches_the_reference_profiler(ours, tmp_path):
     ref_dir = oracle.REFERENCE_SOURCES

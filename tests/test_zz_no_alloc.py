@@ -5,8 +5,10 @@ when they run decode attention (for example inside a stream capture that
 refuses cudaMalloc, or under a fixed device-memory budget): its scratch is a
 fixed array inside the library instead of a caller workspace.  This test
 checks that it returns what the workspace entry point (cl_attn_decode)
-returns, on two calls in a row with different inputs, and that a request
-larger than the fixed array is refused with CL_ERR_LIMIT.  It is collected
+returns, on two calls in a row with different inputs, that both agree with
+a float64 restatement of the attention formula (score = q.k / sqrt(d),
+softmax over the live keys, weighted sum of V; cpu_llm.cpp:888-903), and
+that a request larger than the fixed array is refused with CL_ERR_LIMIT.  It is collected
 last, and it works both alone in a fresh process (the first call performs
 the per-device set-up) and after the other tests.
 """
@@ -40,6 +42,20 @@ def _inputs(seed, hq, hkv, d, cap):
     return q, kc, vc
 
 
+def _attention_f64(q, kc, vc, hq, hkv, d, length):
+    """float64 GQA decode attention over cache rows 0..length-1."""
+    out = np.zeros(hq * d, dtype=np.float64)
+    grp = hq // hkv
+    for h in range(hq):
+        g = h // grp
+        kk = kc[:length, g * d:(g + 1) * d].astype(np.float64)
+        s = kk @ q[h * d:(h + 1) * d].astype(np.float64) / math.sqrt(d)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        out[h * d:(h + 1) * d] = p @ vc[:length, g * d:(g + 1) * d].astype(np.float64)
+    return out
+
+
 def test_noalloc_attention_matches_workspace_entry_point(cuda):
     lib = _native.lib()
     hq, hkv, d, cap = 28, 4, 128, 4096
@@ -61,14 +77,23 @@ def test_noalloc_attention_matches_workspace_entry_point(cuda):
         w, g = want.cpu().numpy(), got.cpu().numpy()
         # same kernels on the same inputs: within the attention tests' 1e-5
         assert np.abs(g - w).max() <= 1e-5 * np.abs(w).max(), f"call {call}"
+        # and both against float64, at the attention tests' 1e-5
+        ref = _attention_f64(q.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy(), hq, hkv, d, length)
+        assert np.abs(g - ref).max() <= 1e-5 * np.abs(ref).max(), f"call {call}"
 
 
 def test_noalloc_attention_refuses_requests_beyond_the_fixed_scratch(cuda):
     lib = _native.lib()
     limit = int(lib.cl_attn_decode_noalloc_limit_bytes())
-    hq, d = 64, 256
-    max_len = 64 * (limit // (hq * (d + 2) * 4) + 1)  # one split more than fits
-    assert int(lib.cl_attn_decode_workspace_bytes(hq, d, max_len)) > limit
+    # A long context uses the full split count, so the need grows with the
+    # query heads: take the fewest heads (a multiple of the 8 KV heads) whose
+    # need, as the library computes it, exceeds the fixed array.
+    d, max_len = 256, 4096
+    hq = 8
+    while int(lib.cl_attn_decode_workspace_bytes(hq, d, max_len)) <= limit:
+        hq += 8
+    assert hq // 8 <= 16, "the refused request must be valid in every other respect"
+    assert int(lib.cl_attn_decode_workspace_bytes(hq - 8, d, max_len)) <= limit
     dummy = torch.zeros(16, device="cuda")
     ln = torch.ones(1, dtype=torch.int32, device="cuda")
     rc = lib.cl_attn_decode_noalloc(_p(dummy), _p(dummy), _p(dummy), _p(ln), max_len, hq, 8, d, 1.0, _p(dummy),
