@@ -670,7 +670,7 @@ def workload_config(name, spec, args, world) -> dict:
 
 
 def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, prefill_e2e_ms, kern, peak, peak_kind,
-              sweep, cpu, base, collectives, clk) -> dict:
+              sweep, cpu, base, collectives, clk, fused_ms=0.0) -> dict:
     """The bench's JSON line from the measured numbers (device ms summed over
     the timed decode steps, host ms around them, the prefill's device and host
     ms, the roofline kernel's timing, the peak) and the reports gathered
@@ -695,6 +695,26 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         launches_per_step = 1 + qkv + 5 * spec.layers + 3
         if world > 1 and os.environ.get("CUDALLM_ALLREDUCE") == "p2p":
             launches_per_step += 2 * spec.layers  # the decode all-reduces are this library's kernel then
+    if fused_ms > 0:
+        launches_per_step = 1  # the whole step is one cooperative launch
+    roofline = {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": kern["gbs"] / peak if kern["gbs"] else None,
+                "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
+                "kernel": kern["kernel"], "shape": kern["shape"],
+                "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
+                "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)",
+                **({"error": kern["error"]} if "error" in kern else {})}
+    if fused_ms > 0:
+        # the step kernel is the whole decode: its algorithmic bytes are the
+        # token's, its duration the CUDA events around it in every timed step
+        k_us = fused_ms / args.steps * 1e3
+        ach = tok_bytes / (k_us * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                    "traffic": profile_traffic(f"decode_fused_{name}"),
+                    "kernel": "decode_fused_kernel (one decode step: every layer, LM head and argmax in one "
+                              "cooperative launch)",
+                    "shape": f"{name}, position {mid}", "bytes_per_launch": tok_bytes, "avg_launch_us": k_us,
+                    "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)", "per_operator_gemv": kern}
     return {
         "metric": "batch-1 greedy decode tokens/s",
         "value": args.steps / (dev_ms / 1e3),
@@ -716,13 +736,7 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         "decode_hbm": {"bytes_per_token_per_gpu": tok_bytes, "achieved_gbs": tok_bytes / (ms_step * 1e-3) / 1e9,
                        "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
                        "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": kern["gbs"] / peak if kern["gbs"] else None,
-                     "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
-                     "kernel": kern["kernel"], "shape": kern["shape"],
-                     "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
-                     "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)",
-                     **({"error": kern["error"]} if "error" in kern else {})},
+        "roofline": roofline,
         "cpu_baseline": cpu,
         "kernel_sweep": sweep,
         "scaling_base": base,
@@ -803,10 +817,12 @@ def bench_cuda(args):
     clocks = ClockSampler(local)
     clocks.start()
     dev_ms = 0.0
+    fused_ms = 0.0  # the one-launch step kernel alone (0 on the per-operator graph)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         tok = llm.decode(tok)
         dev_ms += llm.last_call_ms()
+        fused_ms += llm.last_kernel_ms()
         run_tokens.append(tok)
     e2e_s = time.perf_counter() - t0
     torch.cuda.synchronize()
@@ -875,7 +891,7 @@ def bench_cuda(args):
     base = scaling_base(raw_args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     line = make_line(name, spec, args, world, rank, dev_ms=dev_ms, e2e_ms=e2e_ms, prefill_ms=prefill_ms,
                      prefill_e2e_ms=prefill_e2e_ms, kern=kern, peak=peak, peak_kind=peak_kind, sweep=sweep, cpu=cpu,
-                     base=base, collectives=collectives, clk=clk)
+                     base=base, collectives=collectives, clk=clk, fused_ms=fused_ms)
     if parity is not None:
         line["parity"] = parity
     print(json.dumps(line), flush=True)

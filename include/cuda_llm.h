@@ -172,6 +172,10 @@ public:
     void last_logits(float* out, std::size_t n) const;
     // Device time of the most recent prefill / decode call, milliseconds.
     float last_call_ms() const noexcept;
+    // Device time of the most recent decode's one-launch step kernel alone
+    // (without the token copies around it), milliseconds; 0 when the decode
+    // ran as the per-operator graph.
+    float last_kernel_ms() const noexcept;
 
 private:
     struct Impl;

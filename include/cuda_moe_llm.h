@@ -65,6 +65,7 @@ public:
 
     void last_logits(float* out, std::size_t n) const;
     float last_call_ms() const noexcept;
+    float last_kernel_ms() const noexcept;  // 0: the MoE decode has no one-launch step
 
 private:
     struct Impl;

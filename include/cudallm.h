@@ -53,6 +53,9 @@ CUDALLM_API int cudallm_decode(cudallm_model* m, int32_t id, int32_t* token);
 /* Logits of the last prefill/decode, n >= vocabulary size (collective when world > 1). */
 CUDALLM_API int cudallm_last_logits(cudallm_model* m, float* out, size_t n);
 CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m);
+/* Device time of the last decode's one-launch step kernel alone (qwen2 on one
+ * GPU), milliseconds; 0 when the decode ran as a graph of per-operator kernels. */
+CUDALLM_API float cudallm_last_kernel_ms(const cudallm_model* m);
 CUDALLM_API size_t cudallm_position(const cudallm_model* m);
 CUDALLM_API size_t cudallm_max_sequence(const cudallm_model* m);
 /* layer_count, embedding_size, feed_forward_size, attention_head_count,

@@ -97,7 +97,8 @@ CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long l
                           const float* x, const float* norm_gamma, float eps, float* y, cudaStream_t stream);
 /* Device error word of the pipelined kernels: non-zero when a bounded wait
  * gave up (never expected): 1-3 from the GEMV, 16 + 1..3 from the
- * tensor-core GEMM.  Synchronous; clear != 0 resets it. */
+ * tensor-core GEMM, 32 + 1..3 from the 16-bit GEMM.  Synchronous;
+ * clear != 0 resets it. */
 CL_API int cl_device_error(int* code, int clear);
 
 /* ---- prefill GEMM (metal_gemm_*_f32, metal_llm.metal:621-704; CPU gemmtb
@@ -111,7 +112,8 @@ CL_API int cl_gemm(int type, const void* w, long long stride, int n, int k, cons
                    const float* bias, const float* residual, float* y, cudaStream_t stream);
 enum {
     CL_GEMM_TF32X3 = 0, /* operands split hi + lo TF32, 3 MMAs: FP32-grade (k % 32 == 0) */
-    CL_GEMM_F16 = 1     /* operands rounded to FP16, 1 MMA: 11-bit significands (k % 64 == 0) */
+    CL_GEMM_F16 = 1,    /* operands rounded to FP16, 1 MMA: 11-bit significands (k % 64 == 0) */
+    CL_GEMM_BF16 = 2    /* operands rounded to BF16 (cl_gemm16 path only): 8-bit significands */
 };
 /* The tcgen05 path with an explicit precision; CL_ERR_UNSUPPORTED for shapes
  * it does not take. */
@@ -120,6 +122,33 @@ CL_API int cl_gemm_tc(int type, const void* w, long long stride, int n, int k, c
 /* The FP32 CUDA-core path (exact reference weights, FMA accumulation). */
 CL_API int cl_gemm_simt(int type, const void* w, long long stride, int n, int k, const float* x, int m,
                         const float* bias, const float* residual, float* y, cudaStream_t stream);
+
+/* The 16-bit tensor-core prefill path (same product as metal_gemm_*_f32 /
+ * gemmtb, operands rounded once to FP16 or BF16, FP32 accumulation):
+ *   cl_dequant16  W rows (device layout) -> row-major [n][k] 16-bit, each
+ *                 element the CPU decoder's FP32 value rounded once
+ *                 (format CL_GEMM_F16 or CL_GEMM_BF16; k % 32 == 0);
+ *   cl_convert16  count FP32 values -> 16-bit (count % 4 == 0);
+ *   cl_gemm16_run Y = X16[m][k] W16[n][k]^T on tcgen05 (k % 64 == 0; TMA
+ *                 tensor loads, 128 x 256 or 128 x 128 tiles, optional K
+ *                 split summed in split order).  The n output columns are
+ *                 split into nout (1-3) consecutive ranges, each written to
+ *                 its own row-major buffer with its own bias / residual (a
+ *                 fused Q/K/V or gate/up product).  A K split needs
+ *                 cl_gemm16_workspace_bytes(m, n, k) of workspace; with less
+ *                 (or none) the product runs unsplit. */
+typedef struct cl_gemm_out {
+    float* y;              /* [m][ld], columns col0 .. col0 + cols - 1 of the product */
+    const float* bias;     /* [cols] or NULL */
+    const float* residual; /* [m][ld] or NULL (may alias y) */
+    int col0, cols, ld;
+} cl_gemm_out;
+CL_API int cl_dequant16(int type, const void* w, long long stride, int n, int k, void* out, int format,
+                        cudaStream_t stream);
+CL_API int cl_convert16(const float* x, long long count, void* out, int format, cudaStream_t stream);
+CL_API size_t cl_gemm16_workspace_bytes(int m, int n, int k);
+CL_API int cl_gemm16_run(const void* w16, int n, int k, const void* x16, int m, const cl_gemm_out* outs, int nout,
+                         int format, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* ---- activations ------------------------------------------------------ */
 /* Row RMSNorm (cpu_llm.cpp:143-166, metal_rmsnorm_f32 metal_llm.metal:785):
@@ -209,6 +238,60 @@ CL_API int cl_argmax_merge(const float* records, int n, int32_t* token, cudaStre
 /* counters[0..n) += delta on the device (position bookkeeping inside a
  * captured decode graph). */
 CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
+
+/* ---- one decode step of a qwen2 model in one launch ------------------------
+ * The whole batch-1 decode step of cpu_decode_layer x n_layers + the head
+ * (cpu_llm.cpp:843-914, 1051-1070; Metal encode_decode_layer,
+ * metal_llm.mm:2758-2904): embedding row of ints[0], per layer RMSNorm ->
+ * Q/K/V (+bias) -> NeoX RoPE -> KV append at ints[1] -> GQA attention over
+ * keys 0..ints[1] -> o_proj + residual -> RMSNorm -> gate/up -> SwiGLU ->
+ * down + residual, then RMSNorm -> LM head -> greedy token (lowest index on
+ * ties) into ints[3]; ints[1] advances by one.  The same products and
+ * expressions as the per-operator entry points (the GEMVs' exact integer
+ * dots, the RMSNorm sum in double), in one persistent cooperative launch
+ * with one CTA per SM: every warp streams its share of each weight matrix
+ * through its own shared-memory ring and keeps loading the next matrix while
+ * the grid waits at the barrier between two products.
+ *
+ * Supported: every layer matrix Q4_K or Q6_K (gate and up one type), hidden,
+ * ffn % 256 == 0, output rows % 16 == 0, head_dim 128 with RoPE over the
+ * whole head, q_heads / kv_heads <= 8, kv_heads <= 32, ffn and hidden <=
+ * 20480; else CL_ERR_UNSUPPORTED (use the per-operator path).
+ * `layers` is a device array of n_layers entries; `host_layers` the same
+ * table in host memory (checked here).  Weights are in the device layout
+ * (cl_repack_rows).  The workspace (cl_qwen2_decode_workspace_bytes, for
+ * the current device) must be zeroed once by cl_qwen2_decode_init; every
+ * step leaves it re-armed.  If a grid barrier wait runs out (2 s) the step
+ * stops, and cl_qwen2_decode_status reports it (a device int: 0 = ok,
+ * else 1 + the phase); re-run cl_qwen2_decode_init before the next step. */
+typedef struct cl_qwen2_layer {
+    const void *q, *k, *v, *o, *gate, *up, *down;
+    const float *q_bias, *k_bias, *v_bias, *attn_norm, *ffn_norm;
+    float *k_cache, *v_cache; /* [capacity][kv_heads * head_dim], K after RoPE */
+    int q_type, k_type, v_type, o_type, gate_type, down_type;
+    int reserved[2];
+} cl_qwen2_layer;
+
+typedef struct cl_qwen2_decode {
+    const cl_qwen2_layer* layers; /* device array [n_layers] */
+    int n_layers, hidden, ffn, vocab, q_heads, kv_heads, head_dim, capacity;
+    float eps, scale;             /* RMSNorm epsilon; attention scale 1/sqrt(head_dim) */
+    const void* embd;             /* token_embd rows (device layout) */
+    long long embd_stride;
+    int embd_type, out_type;
+    const void* out_w;            /* output.weight rows */
+    const float* out_norm;
+    const float* rope;            /* [capacity][head_dim / 2][cos, sin] */
+    int* ints;                    /* [0] token in, [1] position, [3] token out */
+    float *h, *q, *k, *v, *att, *act, *logits; /* [hidden], [q_heads*d], [kv*d] x2, [q_heads*d], [ffn], [vocab] */
+} cl_qwen2_decode;
+
+CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_layer* host_layers);
+CL_API size_t cl_qwen2_decode_workspace_bytes(const cl_qwen2_decode* m);
+CL_API int cl_qwen2_decode_init(void* workspace, size_t workspace_bytes, cudaStream_t stream);
+CL_API int cl_qwen2_decode_step(const cl_qwen2_decode* m, const cl_qwen2_layer* host_layers, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+CL_API const int* cl_qwen2_decode_status(const void* workspace);
 
 /* ---- tensor-parallel exchange over peer memory --------------------------- */
 /* One-shot all-reduce (sum) of a decode-size FP32 vector across up to 8 ranks

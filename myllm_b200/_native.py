@@ -81,6 +81,15 @@ SIGNATURES = {
     "cl_peer_exchange_status": (c_vp, [c_vp]),
     "cl_peer_allreduce": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     "cl_peer_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
+    "cl_dequant16": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
+    "cl_convert16": (c_int, [c_vp, c_ll, c_vp, c_int, c_vp]),
+    "cl_gemm16_workspace_bytes": (c_size, [c_int, c_int, c_int]),
+    "cl_gemm16_run": (c_int, [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_int, c_int, c_vp, c_size, c_vp]),
+    "cl_qwen2_decode_supported": (c_int, [c_vp, c_vp]),
+    "cl_qwen2_decode_workspace_bytes": (c_size, [c_vp]),
+    "cl_qwen2_decode_init": (c_int, [c_vp, c_size, c_vp]),
+    "cl_qwen2_decode_step": (c_int, [c_vp, c_vp, c_vp, c_size, c_vp]),
+    "cl_qwen2_decode_status": (c_vp, [c_vp]),
     # backend
     "cudallm_last_error": (c_char_p, []),
     "cudallm_nccl_unique_id": (c_int, [c_vp]),
@@ -91,6 +100,7 @@ SIGNATURES = {
     "cudallm_decode": (c_int, [c_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
     "cudallm_last_logits": (c_int, [c_vp, c_vp, c_size]),
     "cudallm_last_call_ms": (c_float, [c_vp]),
+    "cudallm_last_kernel_ms": (c_float, [c_vp]),
     "cudallm_position": (c_size, [c_vp]),
     "cudallm_max_sequence": (c_size, [c_vp]),
     "cudallm_config": (c_int, [c_vp, ctypes.POINTER(c_ll), c_int]),
@@ -104,6 +114,29 @@ SIGNATURES = {
     "cudallm_tp_plan": (c_int, [ctypes.c_uint64] * 6 + [c_int, c_int, c_vp]),
     "cudallm_ep_plan": (c_int, [ctypes.c_uint64, ctypes.c_uint64, c_int, c_vp, c_vp, c_vp]),
 }
+
+
+class GemmOut(ctypes.Structure):
+    """cl_gemm_out of cudallm_kernels.h: one column range of a cl_gemm16_run product."""
+    _fields_ = [("y", c_vp), ("bias", c_vp), ("residual", c_vp), ("col0", c_int), ("cols", c_int), ("ld", c_int)]
+
+
+class Qwen2Layer(ctypes.Structure):
+    """cl_qwen2_layer of cudallm_kernels.h: one layer of the one-launch decode step."""
+    _fields_ = ([(n, c_vp) for n in ("q", "k", "v", "o", "gate", "up", "down", "q_bias", "k_bias", "v_bias",
+                                    "attn_norm", "ffn_norm", "k_cache", "v_cache")] +
+                [(n, c_int) for n in ("q_type", "k_type", "v_type", "o_type", "gate_type", "down_type")] +
+                [("reserved", c_int * 2)])
+
+
+class Qwen2Decode(ctypes.Structure):
+    """cl_qwen2_decode of cudallm_kernels.h: the model of the one-launch decode step."""
+    _fields_ = ([("layers", c_vp)] +
+                [(n, c_int) for n in ("n_layers", "hidden", "ffn", "vocab", "q_heads", "kv_heads", "head_dim",
+                                      "capacity")] +
+                [("eps", c_float), ("scale", c_float), ("embd", c_vp), ("embd_stride", c_ll), ("embd_type", c_int),
+                 ("out_type", c_int), ("out_w", c_vp), ("out_norm", c_vp), ("rope", c_vp), ("ints", c_vp)] +
+                [(n, c_vp) for n in ("h", "q", "k", "v", "att", "act", "logits")])
 
 
 def lib():

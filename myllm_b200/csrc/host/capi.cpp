@@ -140,6 +140,9 @@ CUDALLM_API int cudallm_last_logits(cudallm_model* m, float* out, size_t n) {
 CUDALLM_API float cudallm_last_call_ms(const cudallm_model* m) {
     return m ? m->with([](const auto& b) { return b.last_call_ms(); }) : 0.0f;
 }
+CUDALLM_API float cudallm_last_kernel_ms(const cudallm_model* m) {
+    return m ? m->with([](const auto& b) { return b.last_kernel_ms(); }) : 0.0f;
+}
 CUDALLM_API size_t cudallm_position(const cudallm_model* m) {
     return m ? m->with([](const auto& b) { return b.position(); }) : 0;
 }

@@ -103,6 +103,8 @@ struct Layer {
     DevMat gate, up, down;
     float* k_cache = nullptr;
     float* v_cache = nullptr;
+    // 16-bit prefill copies (row-major [rows][cols]): Q|K|V rows, o, gate|up rows, down
+    void *qkv16 = nullptr, *o16 = nullptr, *gu16 = nullptr, *down16 = nullptr;
 };
 
 // Contiguous, block-aligned share [begin, end) of `n` units for one rank.
@@ -206,8 +208,19 @@ struct CudaLLM::Impl {
     std::vector<void*> peer_bufs;
     bool peer_allreduce = false;
     cudaGraphExec_t decode_exec = nullptr;
+    // One-GPU decode as one persistent launch (cl_qwen2_decode_step) where
+    // the model's shapes and types allow it; CUDALLM_DECODE=graph selects the
+    // per-operator graph instead.
+    bool fused = false;
+    bool fused_eager = false;  // the step is launched directly when graph capture refuses it
+    cl_qwen2_decode fused_desc{};
+    std::vector<cl_qwen2_layer> fused_layers;
+    cl_qwen2_layer* fused_layers_dev = nullptr;
+    void* fused_ws = nullptr;
+    std::size_t fused_ws_bytes = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    float last_ms = 0.0f;
+    cudaEvent_t kev0 = nullptr, kev1 = nullptr;  // around the fused step kernel
+    float last_ms = 0.0f, last_kernel_ms = 0.0f;
     std::unique_ptr<ProfileCsv> profile;
     std::chrono::steady_clock::time_point call_start;
     bool have_logits = false;
@@ -222,6 +235,8 @@ struct CudaLLM::Impl {
         if (comm) ncclCommDestroy(comm);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
+        if (kev0) cudaEventDestroy(kev0);
+        if (kev1) cudaEventDestroy(kev1);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -325,6 +340,153 @@ struct CudaLLM::Impl {
         U = a.take_n<float>(chunk * F_l);
         P = a.take_n<float>(chunk * H);
         ids_dev = a.take_n<int32_t>(chunk);
+        if (par.world == 1) {
+            fill_fused_desc();
+            fused_layers_dev = a.take_n<cl_qwen2_layer>(layers.size());
+            fused_ws_bytes = cl_qwen2_decode_workspace_bytes(&fused_desc);
+            fused_ws = fused_ws_bytes ? a.take(fused_ws_bytes) : nullptr;
+        }
+    }
+
+    // The fused step's description of this model (pointers valid once the
+    // arenas are bound).
+    void fill_fused_desc() {
+        cl_qwen2_decode& m = fused_desc;
+        m = cl_qwen2_decode{};
+        m.layers = fused_layers_dev;
+        m.n_layers = (int)layers.size();
+        m.hidden = (int)H;
+        m.ffn = (int)F;
+        m.vocab = (int)V;
+        m.q_heads = (int)hq;
+        m.kv_heads = (int)hkv;
+        m.head_dim = (int)d;
+        m.capacity = (int)max_seq;
+        m.eps = eps();
+        m.scale = 1.0f / std::sqrt(static_cast<float>(d));
+        m.embd = tok_embd.ptr;
+        m.embd_stride = tok_embd.stride;
+        m.embd_type = tok_embd.type;
+        m.out_w = out_w.ptr;
+        m.out_type = out_w.type;
+        m.out_norm = out_norm;
+        m.rope = rope;
+        m.ints = ints;
+        m.h = h;
+        m.q = q;
+        m.k = k;
+        m.v = v;
+        m.att = att;
+        m.act = act;
+        m.logits = logits;
+        fused_layers.assign(layers.size(), cl_qwen2_layer{});
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            const Layer& L = layers[l];
+            cl_qwen2_layer& f = fused_layers[l];
+            f.q = L.q.ptr;
+            f.k = L.k.ptr;
+            f.v = L.v.ptr;
+            f.o = L.o.ptr;
+            f.gate = L.gate.ptr;
+            f.up = L.up.ptr;
+            f.down = L.down.ptr;
+            f.q_bias = L.q_b;
+            f.k_bias = L.k_b;
+            f.v_bias = L.v_b;
+            f.attn_norm = L.attn_norm;
+            f.ffn_norm = L.ffn_norm;
+            f.k_cache = L.k_cache;
+            f.v_cache = L.v_cache;
+            f.q_type = L.q.type;
+            f.k_type = L.k.type;
+            f.v_type = L.v.type;
+            f.o_type = L.o.type;
+            f.gate_type = L.gate.type;
+            f.down_type = L.down.type;
+        }
+    }
+
+    // Resident 16-bit copies of every layer matrix for the prefill GEMMs, each
+    // element the CPU decoder's FP32 value rounded once (cl_dequant16); the
+    // activations are rounded into x16 per product.  Matrices whose inner
+    // size the 16-bit GEMM does not take keep the native-block path.
+    static bool gemm16_ok(std::size_t kdim) { return kdim > 0 && kdim % 64 == 0; }
+
+    void setup_wide16() {
+        const std::size_t kmax = std::max<std::size_t>(std::max<std::size_t>(H, F_l), std::max<std::size_t>(o_kl, 1));
+        std::size_t bytes = 0;
+        auto plan = [&](std::size_t rows, std::size_t cols) {
+            const std::size_t b = (rows * cols * 2 + 255) / 256 * 256;
+            bytes += b;
+            return b;
+        };
+        for (Layer& L : layers) {
+            if (gemm16_ok(H)) plan((std::size_t)L.q.rows + L.k.rows + L.v.rows, H);
+            if (o_kl > 0 && gemm16_ok(o_kl)) plan(H, o_kl);
+            if (F_l > 0 && gemm16_ok(H)) plan(2 * F_l, H);
+            if (F_l > 0 && gemm16_ok(F_l)) plan(H, F_l);
+        }
+        w16_mem = DeviceBuffer(bytes + (prefill_chunk * kmax * 2 + 255) / 256 * 256 + 256);
+        char* base = static_cast<char*>(w16_mem.get());
+        const int fmt = fmt16();
+        auto dq = [&](const DevMat& m, char* dst) {
+            CUDALLM_CL(cl_dequant16(m.type, m.ptr, m.stride, m.rows, m.cols, dst, fmt, stream));
+        };
+        for (Layer& L : layers) {
+            if (gemm16_ok(H)) {
+                L.qkv16 = base;
+                dq(L.q, base);
+                dq(L.k, base + (std::size_t)L.q.rows * H * 2);
+                dq(L.v, base + ((std::size_t)L.q.rows + L.k.rows) * H * 2);
+                base += (((std::size_t)L.q.rows + L.k.rows + L.v.rows) * H * 2 + 255) / 256 * 256;
+            }
+            if (o_kl > 0 && gemm16_ok(o_kl)) {
+                L.o16 = base;
+                dq(L.o, base);
+                base += (H * o_kl * 2 + 255) / 256 * 256;
+            }
+            if (F_l > 0 && gemm16_ok(H)) {
+                L.gu16 = base;
+                dq(L.gate, base);
+                dq(L.up, base + F_l * H * 2);
+                base += (2 * F_l * H * 2 + 255) / 256 * 256;
+            }
+            if (F_l > 0 && gemm16_ok(F_l)) {
+                L.down16 = base;
+                dq(L.down, base);
+                base += (H * F_l * 2 + 255) / 256 * 256;
+            }
+        }
+        x16 = base;
+        // K-split partials of the 16-bit GEMM (a product runs unsplit when they do not fit)
+        g16_ws_mem = DeviceBuffer((std::size_t)64 << 20);
+    }
+
+    // Y column ranges = X[m, kdim] W16^T on the 16-bit path.
+    void gemm16(const void* w16, int n, int kdim, const float* x, int m, const cl_gemm_out* outs, int nout) {
+        CUDALLM_CL(cl_convert16(x, (long long)m * kdim, x16, fmt16(), stream));
+        CUDALLM_CL(cl_gemm16_run(w16, n, kdim, x16, m, outs, nout, fmt16(), g16_ws_mem.get(), g16_ws_mem.size(),
+                                 stream));
+    }
+
+    // Selects the one-launch decode step when it supports this model.
+    void setup_fused() {
+        if (par.world != 1 || fused_ws == nullptr) return;
+        std::string mode;
+        if (const char* e = std::getenv("CUDALLM_DECODE")) mode = e;
+        if (mode != "" && mode != "fused" && mode != "graph")
+            throw std::invalid_argument("CUDALLM_DECODE must be fused or graph");
+        if (mode == "graph") return;
+        fill_fused_desc();
+        const int rc = cl_qwen2_decode_supported(&fused_desc, fused_layers.data());
+        if (rc != CL_OK) {
+            if (mode == "fused") throw std::runtime_error(std::string("fused decode: ") + cl_status_string(rc));
+            return;
+        }
+        CUDALLM_CUDA(cudaMemcpyAsync(fused_layers_dev, fused_layers.data(),
+                                     fused_layers.size() * sizeof(cl_qwen2_layer), cudaMemcpyHostToDevice, stream));
+        CUDALLM_CL(cl_qwen2_decode_init(fused_ws, fused_ws_bytes, stream));
+        fused = true;
     }
 
     void init(const std::string& path, std::size_t max_sequence, int dev, const ParallelConfig& parallel) {
@@ -338,6 +500,8 @@ struct CudaLLM::Impl {
         CUDALLM_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
         CUDALLM_CUDA(cudaEventCreate(&ev0));
         CUDALLM_CUDA(cudaEventCreate(&ev1));
+        CUDALLM_CUDA(cudaEventCreate(&kev0));
+        CUDALLM_CUDA(cudaEventCreate(&kev1));
 
         GgufFile file(path);
         config = read_qwen2_config(file);
@@ -360,8 +524,12 @@ struct CudaLLM::Impl {
                 gemm_path = GemmPath::F16;
             else if (val == "simt")
                 gemm_path = GemmPath::Simt;
-            else if (val != "tf32x3" && !val.empty())
-                throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be tf32x3, f16 or simt");
+            else if (val == "tf32x3")
+                gemm_path = GemmPath::Auto;
+            else if (val == "bf16")
+                gemm_path = GemmPath::Bf16;
+            else if (val != "fp16" && !val.empty())
+                throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be fp16, bf16, tf32x3, f16 or simt");
         }
         std::size_t o_block = 1;
         for (std::size_t l = 0; l < config.layer_count; ++l) {
@@ -413,6 +581,8 @@ struct CudaLLM::Impl {
         CUDALLM_CUDA(cudaMemcpyAsync(const_cast<float*>(rope), table.data(), table.size() * sizeof(float),
                                      cudaMemcpyHostToDevice, stream));
         host_io = PinnedBuffer(sizeof(int32_t) * (4 + prefill_chunk));
+        if (wide16()) setup_wide16();
+        setup_fused();
         CUDALLM_CUDA(cudaStreamSynchronize(stream));
     }
 
@@ -479,6 +649,16 @@ struct CudaLLM::Impl {
     // One decode step: host_in[0] -> token; host_in[1] <- greedy token.
     void record_decode() {
         cudaStream_t s = stream;
+        if (fused) {
+            CUDALLM_CUDA(cudaMemcpyAsync(ints, host_in(), sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            CUDALLM_CUDA(cudaEventRecord(kev0, s));
+            CUDALLM_CL(cl_qwen2_decode_step(&fused_desc, fused_layers.data(), fused_ws, fused_ws_bytes, s));
+            CUDALLM_CUDA(cudaEventRecord(kev1, s));
+            CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+            CUDALLM_CUDA(cudaMemcpyAsync(host_in() + 2, cl_qwen2_decode_status(fused_ws), sizeof(int32_t),
+                                         cudaMemcpyDeviceToHost, s));
+            return;
+        }
         const int W = par.world;
         const float scale = 1.0f / std::sqrt(static_cast<float>(d));
         int32_t* tok_in = ints + 0;
@@ -542,8 +722,16 @@ struct CudaLLM::Impl {
         CUDALLM_CUDA(e);
     }
 
-    enum class GemmPath { Auto, F16, Simt };
-    GemmPath gemm_path = GemmPath::Auto;
+    // Prefill GEMM: the 16-bit tensor-core path over resident 16-bit weight
+    // copies (Fp16, the default; Bf16), the split-TF32 tcgen05 path over the
+    // native blocks (Auto: FP32-grade), its one-pass FP16 form, or the FP32
+    // CUDA-core kernel.
+    enum class GemmPath { Auto, F16, Simt, Fp16, Bf16 };
+    GemmPath gemm_path = GemmPath::Fp16;
+    DeviceBuffer w16_mem, g16_ws_mem;
+    void* x16 = nullptr;  // [prefill_chunk][max(H, F_l, o_kl)] 16-bit activations
+    bool wide16() const { return gemm_path == GemmPath::Fp16 || gemm_path == GemmPath::Bf16; }
+    int fmt16() const { return gemm_path == GemmPath::Bf16 ? CL_GEMM_BF16 : CL_GEMM_F16; }
 
     // Y[m, W.rows] = X[m, kdim] W^T (+ bias) (+ residual) on the selected path.
     void gemm(const DevMat& Wm, int n, int kdim, const float* x, int m, const float* bias, const float* res, float* y) {
@@ -559,7 +747,9 @@ struct CudaLLM::Impl {
         case GemmPath::Simt:
             CUDALLM_CL(cl_gemm_simt(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, stream));
             return;
-        case GemmPath::Auto: break;
+        case GemmPath::Auto:
+        case GemmPath::Fp16:  // matrices the 16-bit GEMM does not take
+        case GemmPath::Bf16: break;
         }
         CUDALLM_CL(cl_gemm(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, stream));
     }
@@ -573,9 +763,16 @@ struct CudaLLM::Impl {
         const std::size_t qd_l = hq_l * d;
         for (Layer& L : layers) {
             CUDALLM_CL(cl_rmsnorm(X, L.attn_norm, m, (int)H, eps(), Xn, nullptr, s));
-            gemm(L.q, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q);
-            gemm(L.k, L.k.rows, (int)H, Xn, m, L.k_b, nullptr, K);
-            gemm(L.v, L.v.rows, (int)H, Xn, m, L.v_b, nullptr, Vv);
+            if (L.qkv16) {
+                const cl_gemm_out outs[3] = {{Q, L.q_b, nullptr, 0, L.q.rows, L.q.rows},
+                                             {K, L.k_b, nullptr, L.q.rows, L.k.rows, L.k.rows},
+                                             {Vv, L.v_b, nullptr, L.q.rows + L.k.rows, L.v.rows, L.v.rows}};
+                gemm16(L.qkv16, L.q.rows + L.k.rows + L.v.rows, (int)H, Xn, m, outs, 3);
+            } else {
+                gemm(L.q, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q);
+                gemm(L.k, L.k.rows, (int)H, Xn, m, L.k_b, nullptr, K);
+                gemm(L.v, L.v.rows, (int)H, Xn, m, L.v_b, nullptr, Vv);
+            }
             CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
                                   pos0, L.k_cache, L.v_cache, s));
             CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
@@ -595,10 +792,14 @@ struct CudaLLM::Impl {
                 }
                 o_in = Xn;
             }
-            if (o_kl > 0)
+            if (o_kl > 0 && L.o16) {
+                const cl_gemm_out o{out, nullptr, res, 0, (int)H, (int)H};
+                gemm16(L.o16, (int)H, (int)o_kl, o_in, m, &o, 1);
+            } else if (o_kl > 0) {
                 gemm(L.o, (int)H, (int)o_kl, o_in, m, nullptr, res, out);
-            else
+            } else {
                 CUDALLM_CUDA(cudaMemsetAsync(out, 0, (std::size_t)m * H * sizeof(float), s));
+            }
             if (W > 1) all_reduce(P, X, (std::size_t)m * H);
             CUDALLM_CL(cl_rmsnorm(X, L.ffn_norm, m, (int)H, eps(), Xn, nullptr, s));
             if (F_l == 0) {
@@ -606,10 +807,21 @@ struct CudaLLM::Impl {
                 if (W > 1) all_reduce(P, X, (std::size_t)m * H);
                 continue;
             }
-            gemm(L.gate, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G);
-            gemm(L.up, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U);
+            if (L.gu16) {
+                const cl_gemm_out gu[2] = {{G, nullptr, nullptr, 0, (int)F_l, (int)F_l},
+                                           {U, nullptr, nullptr, (int)F_l, (int)F_l, (int)F_l}};
+                gemm16(L.gu16, 2 * (int)F_l, (int)H, Xn, m, gu, 2);
+            } else {
+                gemm(L.gate, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G);
+                gemm(L.up, (int)F_l, (int)H, Xn, m, nullptr, nullptr, U);
+            }
             CUDALLM_CL(cl_swiglu(G, U, G, (long long)m * F_l, s));
-            gemm(L.down, (int)H, (int)F_l, G, m, nullptr, res, out);
+            if (L.down16) {
+                const cl_gemm_out dn{out, nullptr, res, 0, (int)H, (int)H};
+                gemm16(L.down16, (int)H, (int)F_l, G, m, &dn, 1);
+            } else {
+                gemm(L.down, (int)H, (int)F_l, G, m, nullptr, res, out);
+            }
             if (W > 1) all_reduce(P, X, (std::size_t)m * H);
         }
     }
@@ -703,14 +915,36 @@ struct CudaLLM::Impl {
             throw std::out_of_range("CUDA decode token id is outside the vocabulary");
         if (position >= max_seq) throw std::length_error("CUDA decode exceeds sequence capacity");
         CUDALLM_CUDA(cudaSetDevice(device));
-        if (decode_exec == nullptr) build_decode_graph();
+        if (decode_exec == nullptr && !fused_eager) {
+            if (fused) {
+                try {
+                    build_decode_graph();
+                } catch (const std::runtime_error&) {
+                    fused_eager = true;  // launched directly, one step at a time
+                    cudaGetLastError();
+                }
+            } else {
+                build_decode_graph();
+            }
+        }
         host_in()[0] = token;
         const TraceRange trace("decode.gpu_resident");
         begin_timing();
-        CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
+        if (fused_eager)
+            record_decode();
+        else
+            CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
         end_timing("decode", 1);
+        last_kernel_ms = 0.0f;
+        if (fused) CUDALLM_CUDA(cudaEventElapsedTime(&last_kernel_ms, kev0, kev1));
         if (peer_allreduce && host_in()[2] != 0)
             throw std::runtime_error("peer all-reduce: a rank did not reach the decode step within the wait limit");
+        if (fused && host_in()[2] != 0) {
+            const int phase = host_in()[2];
+            CUDALLM_CL(cl_qwen2_decode_init(fused_ws, fused_ws_bytes, stream));
+            CUDALLM_CUDA(cudaStreamSynchronize(stream));
+            throw std::runtime_error("fused decode: a grid barrier wait ran out in phase " + std::to_string(phase - 1));
+        }
         position += 1;
         have_logits = true;
         return host_in()[1];
@@ -771,7 +1005,7 @@ const std::string& CudaLLM::device_name() const {
 MemoryStats CudaLLM::memory_stats() const noexcept {
     if (!impl_) return {};
     MemoryStats m;
-    m.weight_bytes = impl_->weight_mem.size();
+    m.weight_bytes = impl_->weight_mem.size() + impl_->w16_mem.size();
     m.kv_cache_bytes = impl_->kv_bytes;
     m.recurrent_state_bytes = 0;
     m.intermediate_bytes = impl_->act_bytes;
@@ -805,5 +1039,6 @@ void CudaLLM::last_logits(float* out, std::size_t n) const {
 }
 
 float CudaLLM::last_call_ms() const noexcept { return impl_ ? impl_->last_ms : 0.0f; }
+float CudaLLM::last_kernel_ms() const noexcept { return impl_ ? impl_->last_kernel_ms : 0.0f; }
 
 }  // namespace cudallm

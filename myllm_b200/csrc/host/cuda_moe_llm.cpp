@@ -727,5 +727,6 @@ void CudaMoeLLM::last_logits(float* out, std::size_t n) const {
 }
 
 float CudaMoeLLM::last_call_ms() const noexcept { return impl_ ? impl_->last_ms : 0.0f; }
+float CudaMoeLLM::last_kernel_ms() const noexcept { return 0.0f; }
 
 }  // namespace cudallm

@@ -1,0 +1,1035 @@
+// One batch-1 decode step of a qwen2 model in one persistent launch.
+//
+// Reference: the decode graph of cpu_decode_layer x n_layers + final norm +
+// LM head + greedy token (cpu_llm.cpp:843-914, 1051-1070) and Metal
+// encode_decode_layer (metal_llm.mm:2758-2904).  Same products and the same
+// expressions as the per-operator kernels of this library (the K-quant GEMV
+// of gemv_mma.cu with its exact integer dots, RMSNorm summed in double,
+// attention as in attn.cu), arranged for the B200 instead of as one launch
+// per operator:
+//
+// * One CTA per SM (cooperative launch, so all CTAs are resident), 16 warps.
+//   The step is a fixed sequence of phases: per layer QKV, attention, o_proj,
+//   gate/up, down; then the LM head.  Phases are separated by grid barriers
+//   (an arrival counter; every wait bounded by a 2 s clock and an abort flag).
+// * A GEMV phase is a list of units: 16 output rows x one super-block
+//   (Q4_K) or one half super-block (Q6_K); for gate/up, 8 gate + 8 up rows
+//   (one m16 MMA computes both, so the SwiGLU pair meets in one lane).  The
+//   units of a phase are split into equal contiguous ranges, one per warp of
+//   the grid (stream-K), so every SM streams the same bytes of every matrix.
+// * Each warp owns a 3-slot shared-memory ring that it fills itself with
+//   cp.async (no hand-off between warps).  The ring runs ahead through the
+//   warp's units of the following phases: weights never depend on the
+//   activations, so while the grid waits at a barrier, or encodes the next
+//   input vector, the next matrix is already in flight.
+// * At a phase start every CTA reads the input vector (RMS-normalised where
+//   the layer says so) and encodes it into the XQ4 limbs in shared memory,
+//   exactly as gemv_mma.cu does.
+// * A tile (16 rows) whose units span several warps is summed through a
+//   global partial buffer: each warp stores its partial and takes a ticket;
+//   the last one adds the partials in warp order (deterministic) and writes
+//   the rows (bias, residual, SwiGLU, argmax candidates).
+// * Attention: CTA (KV head, key split) rotates its query heads, appends the
+//   new key / value at the current position, runs an online softmax over its
+//   keys in 64-key tiles and leaves (m, l, o) partials; the last split of a
+//   KV head (ticket) merges them.  During attention the other warps' rings
+//   keep prefetching o_proj.
+// * Head: logits for every row, and per row a (value, index) candidate; the
+//   last CTA to finish merges the CTAs' candidates (lowest index on ties),
+//   writes the token, advances the position and re-arms the control block.
+#include "common.cuh"
+#include "dequant.cuh"
+#include "gemv_mma.cuh"
+#include "launch.cuh"
+
+#include <algorithm>
+
+namespace cl {
+namespace dfz {
+
+using gmma::Q4Lane;
+
+constexpr int kW = 16;                  // warps per CTA
+constexpr int kThreads = kW * 32;
+constexpr int kSlots = 3;               // ring depth per warp
+constexpr int kRS = 160;                // shared row stride of a unit (row stride % 64 == 32: conflict-free)
+constexpr int kSlotBytes = 16 * kRS;
+constexpr int kRingBytes = kW * kSlots * kSlotBytes;
+constexpr int kXBlocksPerWarp = 5;      // x blocks one warp encodes: k <= 16 * 5 * 256
+constexpr int kMaxK = kW * kXBlocksPerWarp * 256;
+constexpr int kSplitsMax = 16;          // key splits per KV head
+constexpr int kGMax = 8;                // query heads per KV head
+constexpr int kD = 128;                 // head dim
+constexpr int kKT = 64;                 // keys per attention tile
+constexpr int kQLD = kD + 4;            // padded q / K rows (bank-conflict-free score loop)
+constexpr int kMaxKvHeads = 32;
+constexpr unsigned long long kWaitNs = 2000ull * 1000 * 1000;
+
+// Control block at the head of the workspace; zero between steps.
+struct Ctl {
+    unsigned int bar;    // grid-barrier arrivals of this step
+    unsigned int done;   // CTAs that finished the head phase
+    int error;           // 0, or 1 + the phase whose barrier wait ran out
+    int abort;
+    unsigned int attn_ticket[kMaxKvHeads];
+    unsigned int pad[28];
+};
+static_assert(sizeof(Ctl) == 256, "control block is 256 bytes");
+
+struct Seg {
+    const uint8_t* w;
+    const uint8_t* w_up;  // gate/up: the up rows (same type and stride as w)
+    const float* bias;
+    float* y;
+    long long stride;
+    long long u0;         // first unit of the segment in its phase
+    int type, nsub, tile0, tiles;
+};
+
+struct Phase {
+    Seg seg[3];
+    long long U;          // units in the phase
+    const float* x;       // input vector; null in layer 0's QKV (the embedding row)
+    const float* gamma;   // RMSNorm weight, or null
+    int nseg, nb, K, sw, head, residual, attn, pad;
+};
+
+struct Params {
+    const cl_qwen2_layer* layers;
+    int n_layers, H, F, V, hq, hkv, cap, max_tiles;
+    float eps, scale;
+    const uint8_t* embd;
+    long long embd_stride;
+    int embd_type, out_type;
+    const uint8_t* out_w;
+    const float* out_norm;
+    const float* rope;
+    int* ints;
+    float *h, *q, *k, *v, *att, *act, *logits;
+    Ctl* ctl;
+    unsigned int* tickets;  // [max_tiles]
+    float2* records;        // [grid] head candidates (value, index as float bits)
+    float* partials;        // [grid * kW][2][16]
+    float* attn_part;       // [hkv][kSplitsMax][G][kD + 2]
+    int region_bytes;
+};
+
+CL_DEVINL long long row_stride(int type, int nb) {
+    return ((long long)nb * (type == CL_TYPE_Q4_K ? 144 : 210) + 15) & ~15ll;
+}
+
+CL_DEVINL void set_seg(Seg& s, const void* w, const void* w_up, int type, int rows, int nb, const float* bias,
+                       float* y, long long& u, int& tile) {
+    s.w = static_cast<const uint8_t*>(w);
+    s.w_up = static_cast<const uint8_t*>(w_up);
+    s.bias = bias;
+    s.y = y;
+    s.type = type;
+    s.stride = row_stride(type, nb);
+    s.nsub = type == CL_TYPE_Q4_K ? nb : 2 * nb;
+    s.tiles = w_up ? rows / 8 : rows / 16;
+    s.u0 = u;
+    s.tile0 = tile;
+    u += (long long)s.tiles * s.nsub;
+    tile += s.tiles;
+}
+
+// Phase p: 5 per layer (QKV, attention, o_proj, gate/up, down), then the head.
+CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
+    long long u = 0;
+    int tile = 0;
+    ph.x = nullptr;
+    ph.gamma = nullptr;
+    ph.nseg = 1;
+    ph.sw = ph.head = ph.residual = ph.attn = 0;
+    ph.U = 0;
+    const int d = kD;
+    if (p >= 5 * P.n_layers) {
+        ph.nb = P.H / 256;
+        ph.K = P.H;
+        ph.x = P.h;
+        ph.gamma = P.out_norm;
+        ph.head = 1;
+        set_seg(ph.seg[0], P.out_w, nullptr, P.out_type, P.V, ph.nb, nullptr, P.logits, u, tile);
+        ph.U = u;
+        return;
+    }
+    const cl_qwen2_layer& L = P.layers[p / 5];
+    switch (p % 5) {
+    case 0:
+        ph.nb = P.H / 256;
+        ph.K = P.H;
+        ph.x = p == 0 ? nullptr : P.h;
+        ph.gamma = L.attn_norm;
+        ph.nseg = 3;
+        set_seg(ph.seg[0], L.q, nullptr, L.q_type, P.hq * d, ph.nb, L.q_bias, P.q, u, tile);
+        set_seg(ph.seg[1], L.k, nullptr, L.k_type, P.hkv * d, ph.nb, L.k_bias, P.k, u, tile);
+        set_seg(ph.seg[2], L.v, nullptr, L.v_type, P.hkv * d, ph.nb, L.v_bias, P.v, u, tile);
+        break;
+    case 1:
+        ph.attn = 1;
+        ph.nb = 0;
+        ph.K = 0;
+        break;
+    case 2:
+        ph.nb = P.H / 256;
+        ph.K = P.H;
+        ph.x = P.att;
+        ph.residual = 1;
+        set_seg(ph.seg[0], L.o, nullptr, L.o_type, P.H, ph.nb, nullptr, P.h, u, tile);
+        break;
+    case 3:
+        ph.nb = P.H / 256;
+        ph.K = P.H;
+        ph.x = P.h;
+        ph.gamma = L.ffn_norm;
+        ph.sw = 1;
+        set_seg(ph.seg[0], L.gate, L.up, L.gate_type, P.F, ph.nb, nullptr, P.act, u, tile);
+        break;
+    default:
+        ph.nb = P.F / 256;
+        ph.K = P.F;
+        ph.x = P.act;
+        ph.residual = 1;
+        set_seg(ph.seg[0], L.down, nullptr, L.down_type, P.H, ph.nb, nullptr, P.h, u, tile);
+        break;
+    }
+    ph.U = u;
+}
+
+struct Unit {
+    int s, tile_l, j;
+};
+
+CL_DEVINL Unit unit_at(const Phase& ph, long long u) {
+    int s = 0;
+    if (ph.nseg > 1 && u >= ph.seg[1].u0) s = 1;
+    if (ph.nseg > 2 && u >= ph.seg[2].u0) s = 2;
+    const long long local = u - ph.seg[s].u0;
+    const int ns = ph.seg[s].nsub;
+    return Unit{s, (int)(local / ns), (int)(local % ns)};
+}
+
+// Range [begin(w), begin(w + 1)) of the grid's warp w over U units.
+CL_DEVINL long long range_begin(long long U, int w, int GW) { return U * w / GW; }
+// The warp whose range holds unit u.
+CL_DEVINL int warp_of(long long U, long long u, int GW) { return (int)(((u + 1) * GW - 1) / U); }
+
+CL_DEVINL const uint8_t* unit_row(const Seg& sg, int tile_l, int r) {
+    if (sg.w_up) return (r < 8 ? sg.w + (long long)(tile_l * 8 + r) * sg.stride
+                               : sg.w_up + (long long)(tile_l * 8 + r - 8) * sg.stride);
+    return sg.w + (long long)(tile_l * 16 + r) * sg.stride;
+}
+
+CL_DEVINL void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+CL_DEVINL void cp8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+CL_DEVINL void cp4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+CL_DEVINL void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CL_DEVINL void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+CL_DEVINL void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// The lane's copies of unit u into a ring slot.  Q4_K: 16 rows x 144 bytes
+// (9 x 16 B each).  Q6_K half hh of super-block sb, per row: ql[64hh..+64]
+// at 0, qh[32hh..+32] at 64, sc[8hh..+8] at 96, and the 4-byte word holding
+// the block's f16 d at 104.
+CL_DEVINL void issue_unit(const Phase& ph, long long u, uint8_t* slot, int lane) {
+    const Unit un = unit_at(ph, u);
+    const Seg& sg = ph.seg[un.s];
+    if (sg.type == CL_TYPE_Q4_K) {
+        const long long off = (long long)un.j * 144;
+        for (int c = lane; c < 144; c += 32) {
+            const int r = c / 9, piece = c - 9 * r;
+            cp16(slot + r * kRS + 16 * piece, unit_row(sg, un.tile_l, r) + off + 16 * piece);
+        }
+    } else {
+        const int sb = un.j >> 1, hh = un.j & 1, r = lane >> 1;
+        const uint8_t* row = unit_row(sg, un.tile_l, r);
+        const uint8_t* blk = row + (long long)sb * 208;
+        uint8_t* dst = slot + r * kRS;
+        if ((lane & 1) == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) cp16(dst + 16 * i, blk + 64 * hh + 16 * i);
+        } else {
+            cp16(dst + 64, blk + 128 + 32 * hh);
+            cp16(dst + 80, blk + 128 + 32 * hh + 16);
+            cp8(dst + 96, blk + 192 + 8 * hh);
+            cp4(dst + 104, row + (((long long)ph.nb * 208 + 2 * sb) & ~3ll));
+        }
+    }
+}
+
+// Q6_K value bytes v in [0, 63] -> v - 32 as signed bytes, four at a time
+// (v | 0x80 never borrows when 0x20 is taken away; xor 0x80 restores).
+CL_DEVINL uint32_t q6_signed(uint32_t v) { return ((v | 0x80808080u) - 0x20202020u) ^ 0x80808080u; }
+
+// Half hh of one Q6_K super-block for 16 rows (the layout of issue_unit),
+// on s8 x s8 MMAs (q - 32 in the weights).  p0 / p1: the lane's B bases in
+// the XQ4 block (the zero block for the other column half).
+CL_DEVINL void q6k_half(const uint8_t* bg, const uint8_t* b8, const uint8_t* p0, const uint8_t* p1, int hh,
+                        int sb, float xs, int t, int h, const Q4Lane& L6, float& yg, float& y8) {
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const uint32_t qg = *reinterpret_cast<const uint32_t*>(bg + 64 + 16 * s + 4 * t);
+        const uint32_t q8 = *reinterpret_cast<const uint32_t*>(b8 + 64 + 16 * s + 4 * t);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t lg = *reinterpret_cast<const uint32_t*>(bg + 32 * j + 16 * s + 4 * t);
+            const uint32_t l8 = *reinterpret_cast<const uint32_t*>(b8 + 32 * j + 16 * s + 4 * t);
+            const uint32_t hag = (j ? (qg << 2) : (qg << 4)) & 0x30303030u;
+            const uint32_t ha8 = (j ? (q8 << 2) : (q8 << 4)) & 0x30303030u;
+            const uint32_t hbg = (j ? (qg >> 2) : qg) & 0x30303030u;
+            const uint32_t hb8 = (j ? (q8 >> 2) : q8) & 0x30303030u;
+            const int boff = 512 * hh + 128 * j + 16 * s;
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(p0 + boff);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(p1 + boff);
+            int c[4];
+            gmma::mma_s8s8_z(c, q6_signed((lg & 0x0f0f0f0fu) | hag), q6_signed((l8 & 0x0f0f0f0fu) | ha8),
+                             q6_signed(((lg >> 4) & 0x0f0f0f0fu) | hbg), q6_signed(((l8 >> 4) & 0x0f0f0f0fu) | hb8),
+                             b0, b1);
+            const int sci = 96 + s + 2 * j + 4 * h;
+            const int sg = (int)*reinterpret_cast<const int8_t*>(bg + sci);
+            const int s8 = (int)*reinterpret_cast<const int8_t*>(b8 + sci);
+            a0 += c[0] * sg;
+            a1 += c[1] * sg;
+            a2 += c[2] * s8;
+            a3 += c[3] * s8;
+        }
+    }
+    const int dsh = 16 * (sb & 1);
+    const float dg = half_bits_to_float(*reinterpret_cast<const uint32_t*>(bg + 104) >> dsh);
+    const float d8 = half_bits_to_float(*reinterpret_cast<const uint32_t*>(b8 + 104) >> dsh);
+    const float vg = fmaf((float)a0, L6.lw0, (float)a1 * L6.lw1) * xs;
+    const float v8 = fmaf((float)a2, L6.lw0, (float)a3 * L6.lw1) * xs;
+    yg = fmaf(dg, vg, yg);
+    y8 = fmaf(d8, v8, y8);
+}
+
+CL_DEVINL unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+CL_DEVINL unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct Best {
+    float v;
+    int i;
+    CL_DEVINL void consider(float y, int o) {
+        if (y > v || (y == v && o < i)) {
+            v = y;
+            i = o;
+        }
+    }
+};
+
+CL_DEVINL bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
+
+// Rows of a finished tile: lanes with t == 0 hold rows g (vg) and g + 8 (v8).
+CL_DEVINL void tile_out(const Phase& ph, const Seg& sg, int tile_l, int g, float vg, float v8, Best& best) {
+    if (ph.sw) {
+        // Branch-stable SiLU(gate) * up (cpu_llm.cpp:188-202), as gemv_mma.cu.
+        const int o = tile_l * 8 + g;
+        const float sig = vg >= 0.0f ? 1.0f / (1.0f + expf(-vg)) : expf(vg) / (1.0f + expf(vg));
+        sg.y[o] = __fmul_rn(__fmul_rn(vg, sig), v8);
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int o = tile_l * 16 + g + 8 * i;
+        float y = i ? v8 : vg;
+        if (sg.bias) y += sg.bias[o];
+        if (ph.residual) y = __ldcg(sg.y + o) + y;
+        sg.y[o] = y;
+        if (ph.head) best.consider(y, o);
+    }
+}
+
+struct Smem {
+    uint8_t* ring;
+    uint8_t* region;
+    const uint8_t* zero;
+    Phase* cph;    // the phase being computed (CTA-wide)
+    Phase* wph;    // [kW] the phase each warp is issuing from
+    double* dred;  // [kW]
+    float2* bests; // [kW]
+    int* flags;    // [0] barrier ok, [1] last-of-split / last CTA
+};
+
+// ---- encode the phase's input into XQ4 limbs (all warps) -------------------
+CL_DEVINL void encode_input(const Params& P, const Phase& ph, const Smem& S, int tok, int warp, int lane) {
+    const int nb = ph.nb;
+    uint8_t* xq = S.region;
+    float* xs = reinterpret_cast<float*>(S.region + nb * 1024);
+    float* xsum = reinterpret_cast<float*>(S.region + nb * 1024 + ((nb * 4 + 15) & ~15));
+    float xv[kXBlocksPerWarp][8];
+    const bool embed = ph.x == nullptr;
+    const uint8_t* erow = P.embd + (long long)tok * P.embd_stride;
+#pragma unroll
+    for (int i = 0; i < kXBlocksPerWarp; ++i) {
+        const int b = warp + i * kW;
+        if (b < nb) {
+            const int c0 = b * 256 + lane * 8;
+            if (embed) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[i][e] = dequant_at(P.embd_type, erow, P.H, c0 + e);
+                if (blockIdx.x == 0) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) P.h[c0 + e] = xv[i][e];
+                }
+            } else {
+                const float4 u0 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0));
+                const float4 u1 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0 + 4));
+                xv[i][0] = u0.x; xv[i][1] = u0.y; xv[i][2] = u0.z; xv[i][3] = u0.w;
+                xv[i][4] = u1.x; xv[i][5] = u1.y; xv[i][6] = u1.z; xv[i][7] = u1.w;
+            }
+        }
+    }
+    if (ph.gamma) {
+        // cpu_llm.cpp:156-165: sum of squares in double, the same order in
+        // every CTA, inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < kXBlocksPerWarp; ++i)
+            if (warp + i * kW < nb) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += (double)xv[i][e] * (double)xv[i][e];
+            }
+        ss = warp_sum_d(ss);
+        if (lane == 0) S.dred[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < kW; ++w) tot += S.dred[w];
+        const float inv = 1.0f / sqrtf((float)(tot / (double)ph.K) + P.eps);
+#pragma unroll
+        for (int i = 0; i < kXBlocksPerWarp; ++i) {
+            const int b = warp + i * kW;
+            if (b < nb) {
+                const float4 q0 = *reinterpret_cast<const float4*>(ph.gamma + b * 256 + lane * 8);
+                const float4 q1 = *reinterpret_cast<const float4*>(ph.gamma + b * 256 + lane * 8 + 4);
+                const float gm[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[i][e] = __fmul_rn(xv[i][e], __fmul_rn(inv, gm[e]));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kXBlocksPerWarp; ++i) {
+        const int b = warp + i * kW;
+        if (b < nb) gmma::encode_block<true, false>(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8, nullptr);
+    }
+    __syncthreads();
+}
+
+// ---- attention of one layer (CTA = KV head x key split) -------------------
+CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, const Smem& S) {
+    const int G = P.hq / P.hkv, kvd = P.hkv * kD, len = pos + 1, tid = threadIdx.x;
+    int ns = min(kSplitsMax, max(1, (len + kKT - 1) / kKT));
+    ns = max(1, min(ns, (int)gridDim.x / P.hkv));
+    if ((int)blockIdx.x >= P.hkv * ns) return;
+    const int g = blockIdx.x / ns, sp = blockIdx.x - g * ns;
+    const int per = (len + ns - 1) / ns, k0 = sp * per;
+    const int nk_all = max(0, min(per, len - k0));
+    float* qs = reinterpret_cast<float*>(S.region);  // [G][kQLD]
+    float* ks = qs + kGMax * kQLD;                   // [kKT][kQLD]
+    float* vs = ks + kKT * kQLD;                     // [kKT][kD]
+    float* ps = vs + kKT * kD;                       // [G][kKT]
+    float* run = ps + kGMax * kKT;                   // [G][2]
+    float* fac = run + 2 * kGMax;                    // [G]
+    const float* cs = P.rope + (size_t)pos * kD;     // [d/2][cos, sin]
+    const int half = kD / 2;
+
+    for (int i = tid; i < G * (kD / 4); i += kThreads) {
+        const int hh = i / (kD / 4), c = i - hh * (kD / 4);
+        *reinterpret_cast<float4*>(qs + hh * kQLD + 4 * c) =
+            __ldcg(reinterpret_cast<const float4*>(P.q + (size_t)(g * G + hh) * kD + 4 * c));
+    }
+    if (tid < G) {
+        run[2 * tid] = -INFINITY;
+        run[2 * tid + 1] = 0.0f;
+    }
+    __syncthreads();
+    // NeoX RoPE of the query heads (the expressions of attn.cu / rope_kv_kernel)
+    for (int i = tid; i < G * half; i += kThreads) {
+        const int hh = i / half, pp = i - hh * half;
+        float* qh = qs + hh * kQLD;
+        const float c = cs[2 * pp], sn = cs[2 * pp + 1];
+        const float a = qh[pp], b = qh[pp + half];
+        qh[pp] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+        qh[pp + half] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+    }
+    const int dim = tid & (kD - 1), pt = tid / kD;  // 4 parts of the PV sums
+    float acc[kGMax];
+#pragma unroll
+    for (int hh = 0; hh < kGMax; ++hh) acc[hh] = 0.0f;
+    for (int t0 = 0; t0 < nk_all; t0 += kKT) {
+        const int nk = min(kKT, nk_all - t0);
+        const size_t base = (size_t)(k0 + t0) * kvd + (size_t)g * kD;
+        for (int i = tid; i < nk * (kD / 4); i += kThreads) {
+            const int r = i / (kD / 4), c = i - r * (kD / 4);
+            cp16(ks + r * kQLD + 4 * c, L.k_cache + base + (size_t)r * kvd + 4 * c);
+            cp16(vs + r * kD + 4 * c, L.v_cache + base + (size_t)r * kvd + 4 * c);
+        }
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        const int r = pos - (k0 + t0);
+        if (r >= 0 && r < nk) {
+            // the current position: rotate the new key, append K and V, use them here
+            const float* kn = P.k + (size_t)g * kD;
+            const float* vn = P.v + (size_t)g * kD;
+            float* kw = L.k_cache + (size_t)pos * kvd + (size_t)g * kD;
+            float* vw = L.v_cache + (size_t)pos * kvd + (size_t)g * kD;
+            for (int pp = tid; pp < half; pp += kThreads) {
+                const float c = cs[2 * pp], sn = cs[2 * pp + 1];
+                const float a = __ldcg(kn + pp), b = __ldcg(kn + pp + half);
+                const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+                const float rb = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+                kw[pp] = ra;
+                kw[pp + half] = rb;
+                ks[r * kQLD + pp] = ra;
+                ks[r * kQLD + pp + half] = rb;
+            }
+            for (int c = tid; c < kD; c += kThreads) {
+                const float vv = __ldcg(vn + c);
+                vw[c] = vv;
+                vs[r * kD + c] = vv;
+            }
+        }
+        __syncthreads();
+        // scores: thread per (key, head)
+        for (int pidx = tid; pidx < nk * G; pidx += kThreads) {
+            const int tk = pidx / G, hh = pidx - tk * G;
+            const float4* kr = reinterpret_cast<const float4*>(ks + tk * kQLD);
+            const float4* qr = reinterpret_cast<const float4*>(qs + hh * kQLD);
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 8
+            for (int c = 0; c < kD / 4; ++c) {
+                const float4 kv = kr[c], qv = qr[c];
+                a0 += kv.x * qv.x;
+                a1 += kv.y * qv.y;
+                a2 += kv.z * qv.z;
+                a3 += kv.w * qv.w;
+            }
+            ps[hh * kKT + tk] = ((a0 + a1) + (a2 + a3)) * P.scale;
+        }
+        __syncthreads();
+        {
+            const int warp = tid >> 5, lane = tid & 31;
+            if (warp < G) {
+                float* ph = ps + warp * kKT;
+                const float s0 = lane < nk ? ph[lane] : -INFINITY;
+                const float s1 = lane + 32 < nk ? ph[lane + 32] : -INFINITY;
+                const float mo = run[2 * warp], mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+                const float e0 = lane < nk ? expf(s0 - mn) : 0.0f;
+                const float e1 = lane + 32 < nk ? expf(s1 - mn) : 0.0f;
+                if (lane < nk) ph[lane] = e0;
+                if (lane + 32 < nk) ph[lane + 32] = e1;
+                const float l = warp_sum(e0 + e1);
+                if (lane == 0) {
+                    const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                    fac[warp] = f;
+                    run[2 * warp] = mn;
+                    run[2 * warp + 1] = run[2 * warp + 1] * f + l;
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int hh = 0; hh < kGMax; ++hh)
+            if (hh < G) acc[hh] *= fac[hh];
+        for (int tk = pt; tk < nk; tk += kThreads / kD) {
+            const float vv = vs[tk * kD + dim];
+#pragma unroll
+            for (int hh = 0; hh < kGMax; ++hh)
+                if (hh < G) acc[hh] += ps[hh * kKT + tk] * vv;
+        }
+        __syncthreads();  // tile buffers are refilled next
+    }
+    // this split's (m, l, o) per head; the K tile buffer holds the PV parts
+    float* pv = ks;
+    if (pt > 0) {
+#pragma unroll
+        for (int hh = 0; hh < kGMax; ++hh)
+            if (hh < G) pv[((pt - 1) * G + hh) * kD + dim] = acc[hh];
+    }
+    __syncthreads();
+    const int rec = kD + 2;
+    float* part = P.attn_part + (size_t)g * kSplitsMax * G * rec;
+    if (pt == 0) {
+#pragma unroll
+        for (int hh = 0; hh < kGMax; ++hh) {
+            if (hh < G) {
+                float o = acc[hh];
+                for (int q2 = 1; q2 < kThreads / kD; ++q2) o += pv[((q2 - 1) * G + hh) * kD + dim];
+                float* pr = part + ((size_t)sp * G + hh) * rec;
+                __stcg(pr + 2 + dim, o);
+                if (dim == 0) {
+                    __stcg(pr, run[2 * hh]);
+                    __stcg(pr + 1, run[2 * hh + 1]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned int old = atomicAdd(&P.ctl->attn_ticket[g], 1u);
+        S.flags[1] = old == (unsigned int)(ns - 1);
+    }
+    __syncthreads();
+    if (!S.flags[1]) return;
+    __threadfence();
+    // merge the splits (attn_decode_combine's weights: exp(m_s - m) / l)
+    float* wsm = ps;  // [G][kSplitsMax]
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        if (warp < G) {
+            const float ms = lane < ns ? __ldcg(part + ((size_t)lane * G + warp) * rec) : -INFINITY;
+            const float ls = lane < ns ? __ldcg(part + ((size_t)lane * G + warp) * rec + 1) : 0.0f;
+            const float m = warp_max(ms);
+            const float e = ls > 0.0f ? expf(ms - m) : 0.0f;
+            const float l = warp_sum(ls * e);
+            if (lane < kSplitsMax) wsm[warp * kSplitsMax + lane] = lane < ns ? e / l : 0.0f;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * kD; i += kThreads) {
+        const int hh = i / kD, dd = i - hh * kD;
+        float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int s2 = 0; s2 < ns; ++s2)
+            o4[s2 & 3] += __ldcg(part + ((size_t)s2 * G + hh) * rec + 2 + dd) * wsm[hh * kSplitsMax + s2];
+        P.att[(size_t)(g * G + hh) * kD + dd] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+    }
+    if (tid == 0) P.ctl->attn_ticket[g] = 0u;
+}
+
+// A finished tile's rows, direct or through the partial buffer.
+CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, long long b, long long e, int gw,
+                          int GW, float yg, float y8, float ym, int lane, Best& best) {
+    const int g = lane >> 2, t = lane & 3;
+    if (t & 1) y8 += ym;
+    else yg += ym;
+    yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+    yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+    y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+    y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+    const Seg& sg = ph.seg[s];
+    const long long uf = sg.u0 + (long long)tile_l * sg.nsub, ul = uf + sg.nsub - 1;
+    if (uf >= b && ul < e) {
+        if (t == 0) tile_out(ph, sg, tile_l, g, yg, y8, best);
+        return;
+    }
+    float* mine = P.partials + ((size_t)gw * 2 + (b >= uf ? 0 : 1)) * 16;
+    if (t == 0) {
+        __stcg(mine + g, yg);
+        __stcg(mine + 8 + g, y8);
+    }
+    __syncwarp();
+    const int wf = warp_of(ph.U, uf, GW), wl = warp_of(ph.U, ul, GW);
+    int last = 0;
+    if (lane == 0) {
+        int count = 0;
+        for (int k = wf; k <= wl; ++k) count += range_begin(ph.U, k + 1, GW) > range_begin(ph.U, k, GW);
+        __threadfence();
+        const unsigned int old = atomicAdd(&P.tickets[sg.tile0 + tile_l], 1u);
+        last = old == (unsigned int)(count - 1);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    if (t == 0) {
+        float vg = 0.0f, v8 = 0.0f;
+        for (int k = wf; k <= wl; ++k) {
+            const long long bk = range_begin(ph.U, k, GW);
+            if (range_begin(ph.U, k + 1, GW) == bk) continue;  // a warp without units
+            const float* pk = P.partials + ((size_t)k * 2 + (bk >= uf ? 0 : 1)) * 16;
+            vg += __ldcg(pk + g);
+            v8 += __ldcg(pk + 8 + g);
+        }
+        tile_out(ph, sg, tile_l, g, vg, v8, best);
+    }
+    if (lane == 0) P.tickets[sg.tile0 + tile_l] = 0u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_constant__ Params P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    Smem S;
+    S.ring = smem;
+    S.region = smem + kRingBytes;
+    uint8_t* zero = S.region + P.region_bytes;
+    S.zero = zero;
+    S.cph = reinterpret_cast<Phase*>(zero + 1024);
+    S.wph = S.cph + 1;
+    S.dred = reinterpret_cast<double*>(S.wph + kW);
+    S.bests = reinterpret_cast<float2*>(S.dred + kW);
+    S.flags = reinterpret_cast<int*>(S.bests + kW);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3, h = t >> 1;
+    const int GW = gridDim.x * kW, gw = blockIdx.x * kW + warp;
+    if (tid < 64) reinterpret_cast<uint4*>(zero)[tid] = make_uint4(0u, 0u, 0u, 0u);
+    const int tok = __ldcg(P.ints);
+    const int pos = __ldcg(P.ints + 1);
+    const int nph = 5 * P.n_layers + 1;
+
+    // ---- the warp's ring: issue iterator (lane-uniform) ----
+    uint8_t* ring = S.ring + (size_t)warp * kSlots * kSlotBytes;
+    Phase& wph = S.wph[warp];
+    int ip = -1;
+    long long iu = 0, ie = 0;
+    int n_issued = 0;
+    auto issue_next = [&]() {
+        while (iu >= ie) {
+            ++ip;
+            if (ip >= nph) {
+                ip = nph;
+                return;
+            }
+            if (ip < 5 * P.n_layers && ip % 5 == 1) continue;  // attention: no weight units
+            if (lane == 0) make_phase(P, ip, wph);
+            __syncwarp();
+            iu = range_begin(wph.U, gw, GW);
+            ie = range_begin(wph.U, gw + 1, GW);
+            __syncwarp();
+        }
+        issue_unit(wph, iu, ring + (size_t)(n_issued % kSlots) * kSlotBytes, lane);
+        ++iu;
+    };
+    for (int i = 0; i < kSlots; ++i) {
+        if (ip < nph) issue_next();
+        cp_commit();
+        ++n_issued;
+    }
+
+    Q4Lane L;
+    L.sh = 12u * (uint32_t)h;
+    L.lw0 = ((t & 1) ? (1.0f / 16384.0f) : 1.0f) * (h ? (1.0f / 16.0f) : 1.0f);
+    L.lw1 = L.lw0 * (1.0f / 128.0f);
+    L.pp = t & 1;
+    Q4Lane L6 = L;
+    L6.lw0 = (t & 1) ? (1.0f / 16384.0f) : 1.0f;
+    L6.lw1 = L6.lw0 * (1.0f / 128.0f);
+
+    Best best{-INFINITY, 0x7fffffff};
+    int n_done = 0;
+    __syncthreads();
+
+    for (int p = 0; p < nph; ++p) {
+        if (tid == 0) make_phase(P, p, *S.cph);
+        __syncthreads();
+        const Phase& ph = *S.cph;
+        if (ph.attn) {
+            attention(P, P.layers[p / 5], pos, S);
+        } else {
+            encode_input(P, ph, S, tok, warp, lane);
+            const uint8_t* xq = S.region;
+            const int nb = ph.nb;
+            const float* xs = reinterpret_cast<const float*>(S.region + nb * 1024);
+            const float* xsum = reinterpret_cast<const float*>(S.region + nb * 1024 + ((nb * 4 + 15) & ~15));
+            const long long b = range_begin(ph.U, gw, GW), e = range_begin(ph.U, gw + 1, GW);
+            int cur_s = -1, cur_tl = -1;
+            float yg = 0.0f, y8 = 0.0f, ym = 0.0f;
+            for (long long u = b; u < e; ++u) {
+                const Unit un = unit_at(ph, u);
+                if (un.s != cur_s || un.tile_l != cur_tl) {
+                    if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best);
+                    cur_s = un.s;
+                    cur_tl = un.tile_l;
+                    yg = y8 = ym = 0.0f;
+                }
+                cp_wait<kSlots - 1>();
+                __syncwarp();
+                const uint8_t* slot = ring + (size_t)(n_done % kSlots) * kSlotBytes;
+                const uint8_t* bg = slot + g * kRS;
+                const uint8_t* b8 = bg + 8 * kRS;
+                if (ph.seg[un.s].type == CL_TYPE_Q4_K) {
+                    const int sb = un.j;
+                    const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 8 * t : S.zero;
+                    const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 128 + (g - 4) * 32 + 8 * t : S.zero;
+                    uint2 bx0[4], bx1[4];
+#pragma unroll
+                    for (int gi = 0; gi < 4; ++gi) {
+                        bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
+                        bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
+                    }
+                    const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
+                    gmma::q4k_sb(bg, b8, bx0, bx1, xsum4, xs[sb], t, L, yg, y8, ym);
+                } else {
+                    const int sb = un.j >> 1, hh = un.j & 1;
+                    const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 4 * t : S.zero;
+                    const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 256 + (g - 4) * 32 + 4 * t : S.zero;
+                    q6k_half(bg, b8, p0, p1, hh, sb, xs[sb], t, h, L6, yg, y8);
+                }
+                __syncwarp();
+                ++n_done;
+                if (ip < nph) issue_next();
+                cp_commit();
+                ++n_issued;
+            }
+            if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best);
+        }
+        if (p + 1 < nph) {
+            // ---- grid barrier ----
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(&P.ctl->bar, 1u);
+                const unsigned int target = (unsigned int)(p + 1) * gridDim.x;
+                const unsigned long long t0 = global_ns();
+                int ok = 1;
+                while (ld_acquire(&P.ctl->bar) < target) {
+                    if (*reinterpret_cast<volatile int*>(&P.ctl->abort)) {
+                        ok = 0;
+                        break;
+                    }
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicCAS(&P.ctl->error, 0, p + 1);
+                        atomicExch(&P.ctl->abort, 1);
+                        ok = 0;
+                        break;
+                    }
+                }
+                __threadfence();
+                S.flags[0] = ok;
+            }
+            __syncthreads();
+            if (!S.flags[0]) {
+                cp_wait_all();
+                return;
+            }
+        }
+    }
+
+    // ---- head: the CTAs' candidates, merged by the last CTA ----
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+        if (better(ov, oi, best.v, best.i)) {
+            best.v = ov;
+            best.i = oi;
+        }
+    }
+    if (lane == 0) S.bests[warp] = make_float2(best.v, __int_as_float(best.i));
+    cp_wait_all();
+    __syncthreads();
+    if (tid == 0) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int w = 0; w < kW; ++w) {
+            const float v = S.bests[w].x;
+            const int i = __float_as_int(S.bests[w].y);
+            if (better(v, i, bv, bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+        __stcg(&P.records[blockIdx.x], make_float2(bv, __int_as_float(bi)));
+        __threadfence();
+        const unsigned int old = atomicAdd(&P.ctl->done, 1u);
+        if (old == gridDim.x - 1) {
+            __threadfence();
+            bv = -INFINITY;
+            bi = 0x7fffffff;
+            for (int c = 0; c < (int)gridDim.x; ++c) {
+                const float2 r = __ldcg(&P.records[c]);
+                const int i = __float_as_int(r.y);
+                if (better(r.x, i, bv, bi)) {
+                    bv = r.x;
+                    bi = i;
+                }
+            }
+            P.ints[3] = bi;
+            P.ints[1] = pos + 1;  // position and live length advance together (as cl_counter_add)
+            P.ints[2] = pos + 2;
+            P.ctl->bar = 0u;
+            P.ctl->done = 0u;
+            __threadfence();
+        }
+    }
+}
+
+size_t region_bytes(int hidden, int ffn) {
+    const int nb = std::max(hidden, ffn) / 256;
+    const size_t xq = (size_t)nb * 1024 + (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)nb * 32;
+    const size_t attn = sizeof(float) * ((size_t)kGMax * kQLD + (size_t)kKT * kQLD + (size_t)kKT * kD +
+                                         (size_t)kGMax * kKT + 3 * kGMax);
+    return (std::max(xq, attn) + 127) & ~(size_t)127;
+}
+
+size_t smem_bytes(int hidden, int ffn) {
+    return kRingBytes + region_bytes(hidden, ffn) + 1024 + (1 + kW) * sizeof(Phase) + kW * sizeof(double) +
+           kW * sizeof(float2) + 16;
+}
+
+int max_tiles(const cl_qwen2_decode* m) {
+    const int d = m->head_dim;
+    return std::max({m->vocab / 16, m->ffn / 8, (m->q_heads + 2 * m->kv_heads) * d / 16, m->hidden / 16});
+}
+
+struct Layout {
+    size_t tickets, records, partials, attn, total;
+};
+
+Layout layout(const cl_qwen2_decode* m, int grid) {
+    Layout l{};
+    size_t off = sizeof(Ctl);
+    l.tickets = off;
+    off += ((size_t)max_tiles(m) * 4 + 255) & ~(size_t)255;
+    l.records = off;
+    off += ((size_t)grid * 8 + 255) & ~(size_t)255;
+    l.partials = off;
+    off += (size_t)grid * kW * 2 * 16 * 4;
+    l.attn = off;
+    off += (size_t)m->kv_heads * kSplitsMax * (m->q_heads / m->kv_heads) * (kD + 2) * 4;
+    l.total = (off + 255) & ~(size_t)255;
+    return l;
+}
+
+bool k_type_ok(int t) { return t == CL_TYPE_Q4_K || t == CL_TYPE_Q6_K; }
+
+}  // namespace dfz
+}  // namespace cl
+
+using namespace cl;
+using namespace cl::dfz;
+
+extern "C" {
+
+CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_layer* hl) {
+    if (m == nullptr || hl == nullptr || m->layers == nullptr || m->n_layers <= 0) return CL_ERR_INVALID;
+    if (m->hidden <= 0 || m->ffn <= 0 || m->hidden % 256 || m->ffn % 256 || m->hidden > kMaxK || m->ffn > kMaxK ||
+        m->head_dim != kD || m->q_heads <= 0 || m->kv_heads <= 0 || m->kv_heads > kMaxKvHeads ||
+        m->q_heads % m->kv_heads || m->q_heads / m->kv_heads > kGMax || m->q_heads * kD != m->hidden ||
+        m->vocab <= 0 || m->vocab % 16 || m->ffn % 8 || m->capacity <= 0)
+        return CL_ERR_UNSUPPORTED;
+    if (!k_type_ok(m->out_type) || m->embd == nullptr || m->out_w == nullptr || m->out_norm == nullptr ||
+        m->rope == nullptr || m->ints == nullptr || !m->h || !m->q || !m->k || !m->v || !m->att || !m->act ||
+        !m->logits)
+        return CL_ERR_UNSUPPORTED;
+    if (m->embd_type != CL_TYPE_F32 && m->embd_type != CL_TYPE_F16 && m->embd_type != CL_TYPE_Q4_K &&
+        m->embd_type != CL_TYPE_Q5_K && m->embd_type != CL_TYPE_Q6_K && m->embd_type != CL_TYPE_Q8_0 &&
+        m->embd_type != CL_TYPE_Q5_0)
+        return CL_ERR_UNSUPPORTED;
+    // 16-byte alignment of every vector read with float4 / cp.async
+    const uintptr_t vec = reinterpret_cast<uintptr_t>(m->h) | reinterpret_cast<uintptr_t>(m->q) |
+                          reinterpret_cast<uintptr_t>(m->k) | reinterpret_cast<uintptr_t>(m->v) |
+                          reinterpret_cast<uintptr_t>(m->att) | reinterpret_cast<uintptr_t>(m->act) |
+                          reinterpret_cast<uintptr_t>(m->out_norm) | reinterpret_cast<uintptr_t>(m->out_w);
+    if (vec & 15u) return CL_ERR_INVALID;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const cl_qwen2_layer& L = hl[l];
+        if (!k_type_ok(L.q_type) || !k_type_ok(L.k_type) || !k_type_ok(L.v_type) || !k_type_ok(L.o_type) ||
+            !k_type_ok(L.gate_type) || !k_type_ok(L.down_type))
+            return CL_ERR_UNSUPPORTED;
+        if (!L.q || !L.k || !L.v || !L.o || !L.gate || !L.up || !L.down || !L.attn_norm || !L.ffn_norm ||
+            !L.k_cache || !L.v_cache)
+            return CL_ERR_INVALID;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(L.q) | reinterpret_cast<uintptr_t>(L.k) |
+                            reinterpret_cast<uintptr_t>(L.v) | reinterpret_cast<uintptr_t>(L.o) |
+                            reinterpret_cast<uintptr_t>(L.gate) | reinterpret_cast<uintptr_t>(L.up) |
+                            reinterpret_cast<uintptr_t>(L.down) | reinterpret_cast<uintptr_t>(L.attn_norm) |
+                            reinterpret_cast<uintptr_t>(L.ffn_norm) | reinterpret_cast<uintptr_t>(L.k_cache) |
+                            reinterpret_cast<uintptr_t>(L.v_cache);
+        if (a & 15u) return CL_ERR_INVALID;
+    }
+    return CL_OK;
+}
+
+CL_API size_t cl_qwen2_decode_workspace_bytes(const cl_qwen2_decode* m) {
+    if (m == nullptr || m->kv_heads <= 0 || m->q_heads <= 0 || m->q_heads % m->kv_heads) return 0;
+    int grid = 0;
+    if (device_sm_count(&grid) != cudaSuccess || grid <= 0) return 0;
+    return layout(m, grid).total;
+}
+
+CL_API int cl_qwen2_decode_init(void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (workspace == nullptr || workspace_bytes < sizeof(Ctl) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return CL_ERR_INVALID;
+    // the control block and the tile tickets must start at zero; the rest is
+    // written before it is read in every step
+    return cudaMemsetAsync(workspace, 0, workspace_bytes, stream) == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+}
+
+CL_API const int* cl_qwen2_decode_status(const void* workspace) {
+    if (workspace == nullptr) return nullptr;
+    return &static_cast<const Ctl*>(workspace)->error;
+}
+
+CL_API int cl_qwen2_decode_step(const cl_qwen2_decode* m, const cl_qwen2_layer* host_layers, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+    const int rc = cl_qwen2_decode_supported(m, host_layers);
+    if (rc != CL_OK) return rc;
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return CL_ERR_INVALID;
+    int grid = 0;
+    if (device_sm_count(&grid) != cudaSuccess) return CL_ERR_CUDA;
+    const Layout lay = layout(m, grid);
+    if (workspace_bytes < lay.total) return CL_ERR_WORKSPACE;
+    const size_t smem = smem_bytes(m->hidden, m->ffn);
+    static SmemLimit limit;
+    if (limit.ensure(decode_fused_kernel, (int)smem) != cudaSuccess) return CL_ERR_UNSUPPORTED;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fused_kernel, kThreads, smem) != cudaSuccess ||
+        occ < 1)
+        return CL_ERR_UNSUPPORTED;
+    char* ws = static_cast<char*>(workspace);
+    Params p{};
+    p.layers = m->layers;
+    p.n_layers = m->n_layers;
+    p.H = m->hidden;
+    p.F = m->ffn;
+    p.V = m->vocab;
+    p.hq = m->q_heads;
+    p.hkv = m->kv_heads;
+    p.cap = m->capacity;
+    p.max_tiles = max_tiles(m);
+    p.eps = m->eps;
+    p.scale = m->scale;
+    p.embd = static_cast<const uint8_t*>(m->embd);
+    p.embd_stride = m->embd_stride;
+    p.embd_type = m->embd_type;
+    p.out_type = m->out_type;
+    p.out_w = static_cast<const uint8_t*>(m->out_w);
+    p.out_norm = m->out_norm;
+    p.rope = m->rope;
+    p.ints = m->ints;
+    p.h = m->h;
+    p.q = m->q;
+    p.k = m->k;
+    p.v = m->v;
+    p.att = m->att;
+    p.act = m->act;
+    p.logits = m->logits;
+    p.ctl = reinterpret_cast<Ctl*>(ws);
+    p.tickets = reinterpret_cast<unsigned int*>(ws + lay.tickets);
+    p.records = reinterpret_cast<float2*>(ws + lay.records);
+    p.partials = reinterpret_cast<float*>(ws + lay.partials);
+    p.attn_part = reinterpret_cast<float*>(ws + lay.attn);
+    p.region_bytes = (int)region_bytes(m->hidden, m->ffn);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_fused_kernel, p) == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+}
+
+}  // extern "C"

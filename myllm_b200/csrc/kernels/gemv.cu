@@ -505,6 +505,7 @@ int launch_gemv(const cl_gemv_segment* segs, int nseg, int k, const float* x, co
 
 namespace cl {
 int gemm_tc_device_error(int* code, bool clear);  // gemm_tc.cu
+int gemm16_device_error(int* code, bool clear);   // gemm16.cu
 }  // namespace cl
 
 extern "C" {
@@ -530,13 +531,14 @@ CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long l
 
 CL_API int cl_device_error(int* code, int clear) {
     if (code == nullptr) return CL_ERR_INVALID;
-    int gemv = 0, gemm = 0, mma = 0;
+    int gemv = 0, gemm = 0, mma = 0, g16 = 0;
     if (cudaMemcpyFromSymbol(&gemv, cl::g_gemv_error, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;
     if (cl::gemv_mma_device_error(&mma, clear != 0) != CL_OK) return CL_ERR_CUDA;
     if (cl::gemm_tc_device_error(&gemm, clear != 0) != CL_OK) return CL_ERR_CUDA;
+    if (cl::gemm16_device_error(&g16, clear != 0) != CL_OK) return CL_ERR_CUDA;
     // GEMV codes are 1-5 (4-5: tensor-core GEMV); tensor-core GEMM codes are
-    // reported as 16 + code.
-    *code = gemv != 0 ? gemv : (mma != 0 ? mma : (gemm != 0 ? 16 + gemm : 0));
+    // reported as 16 + code, the 16-bit GEMM's as 32 + code.
+    *code = gemv != 0 ? gemv : (mma != 0 ? mma : (gemm != 0 ? 16 + gemm : (g16 != 0 ? 32 + g16 : 0)));
     if (clear) {
         const int zero = 0;
         if (cudaMemcpyToSymbol(cl::g_gemv_error, &zero, sizeof(int)) != cudaSuccess) return CL_ERR_CUDA;

@@ -93,7 +93,45 @@ def device_error(clear: bool = True) -> int:
     return code.value
 
 
-GEMM_TF32X3, GEMM_F16 = 0, 1
+GEMM_TF32X3, GEMM_F16, GEMM_BF16 = 0, 1, 2
+
+
+def dequant16(gtype: int, w: torch.Tensor, n: int, k: int, fmt: int = GEMM_F16) -> torch.Tensor:
+    """Device-layout rows -> row-major [n, k] FP16 / BF16 (cl_dequant16)."""
+    out = torch.empty((n, k), dtype=torch.bfloat16 if fmt == GEMM_BF16 else torch.float16, device=w.device)
+    check(_native.lib().cl_dequant16(gtype, _p(w), w.stride(0), n, k, _p(out), fmt, _stream()), "cl_dequant16")
+    return out
+
+
+def convert16(x: torch.Tensor, fmt: int = GEMM_F16) -> torch.Tensor:
+    out = torch.empty(x.shape, dtype=torch.bfloat16 if fmt == GEMM_BF16 else torch.float16, device=x.device)
+    check(_native.lib().cl_convert16(_p(x), x.numel(), _p(out), fmt, _stream()), "cl_convert16")
+    return out
+
+
+def gemm16_run(w16: torch.Tensor, x16: torch.Tensor, outs, fmt: int = GEMM_F16, split: bool = True) -> None:
+    """cl_gemm16_run over column ranges: outs = [(y, bias, residual, col0, cols)]
+    with y row-major [m, cols]."""
+    n, k = w16.shape
+    m = x16.shape[0]
+    arr = (_native.GemmOut * len(outs))()
+    for i, (y, bias, res, col0, cols) in enumerate(outs):
+        arr[i] = _native.GemmOut(y.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                 res.data_ptr() if res is not None else None, col0, cols, y.stride(0))
+    lib = _native.lib()
+    wsb = int(lib.cl_gemm16_workspace_bytes(m, n, k)) if split else 0
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x16.device) if wsb else None
+    check(lib.cl_gemm16_run(_p(w16), n, k, _p(x16), m, arr, len(outs), fmt, _p(ws), wsb, _stream()),
+          "cl_gemm16_run")
+
+
+def gemm16(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None,
+           fmt: int = GEMM_F16, split: bool = True) -> torch.Tensor:
+    """Y = X W^T (+bias) (+residual) on the 16-bit tensor-core path."""
+    m = x.shape[0]
+    y = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    gemm16_run(dequant16(gtype, w, n, k, fmt), convert16(x, fmt), [(y, bias, residual, 0, n)], fmt, split)
+    return y
 
 
 def gemm(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, bias=None, residual=None, path="auto",

@@ -240,3 +240,8 @@ class CudaLLM:
 
     def last_call_ms(self) -> float:
         return float(_native.lib().cudallm_last_call_ms(self._h))
+
+    def last_kernel_ms(self) -> float:
+        """Device time of the last decode's one-launch step kernel alone (0
+        when the decode ran as the per-operator graph)."""
+        return float(_native.lib().cudallm_last_kernel_ms(self._h))

@@ -254,11 +254,24 @@ CONFIGS: Dict[str, Qwen2Spec] = {
     "qwen2.5-7b": Qwen2Spec("qwen2.5-7b", hidden=3584, layers=28, heads=28, kv_heads=4,
                             ffn=18944, vocab=152064, seed=0x7B, types=qwen2_q4km_types,
                             embed_type=Q4_K, output_type=Q6_K),
+    # The 7B's widths and formats with 4 layers (1.4 GB): a profiling case that
+    # fits a full ncu capture while its weights still exceed the L2.
+    "qwen2.5-7b-4l": Qwen2Spec("qwen2.5-7b-4l", hidden=3584, layers=4, heads=28, kv_heads=4,
+                               ffn=18944, vocab=152064, seed=0x7B4, types=qwen2_q4km_types,
+                               embed_type=Q4_K, output_type=Q6_K),
     # Qwen2.5-14B architecture.
     "qwen2.5-14b": Qwen2Spec("qwen2.5-14b", hidden=5120, layers=48, heads=40, kv_heads=8,
                              ffn=13824, vocab=152064, seed=0x14B, types=qwen2_q4km_types,
                              embed_type=Q4_K, output_type=Q6_K),
 }
+
+
+def q4km_small_spec(seed: int = 0x128, layers: int = 3) -> Qwen2Spec:
+    """A small model with the 7B's structure: Q4_K_M layout, head_dim 128,
+    7 query heads per KV head (hidden 1792 = 14 x 128, 2 KV heads), ffn 4864."""
+    return Qwen2Spec(f"q4km-d128-s{seed}", hidden=1792, layers=layers, heads=14, kv_heads=2,
+                     ffn=4864, vocab=8192, context=2048, seed=seed, types=qwen2_q4km_types,
+                     embed_type=Q4_K, output_type=Q6_K)
 
 
 def tiny_mixed_types(layer: int, tensor: str) -> int:

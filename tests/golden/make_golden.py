@@ -22,6 +22,11 @@ Fixtures:
                      summary as qwen2_05b.  The reference holds ~35 GB of FP32
                      weights, so the harness and the CPULLM cross-check run
                      one after the other (--only-7b makes just this one).
+  q4km_d128.npz      a small model with the 7B's structure (Q4_K_M layout,
+                     head_dim 128, 7 query heads per KV head; 3 layers):
+                     prompts of 8 and 1100 tokens (the long one spans 16
+                     attention key splits of two 64-key tiles each), prefill
+                     + 4 greedy decodes, full logits (--only-small).
   qwen2_7b_long.npz  BASELINE config 2 at its full length: the bench's
                      512-token prompt, prefill + 128 greedy decodes, the same
                      summary (--only-7b-long).  The harness's fixture is
@@ -134,6 +139,22 @@ def qwen2_7b_long(tmp: str, prompt_len: int = 512, steps: int = 128) -> None:
                         **summ)
 
 
+def q4km_small(tmp: str) -> None:
+    spec = sg.q4km_small_spec()
+    path = os.path.join(tmp, "q4km_d128.gguf")
+    sha = sg.write_qwen2(spec, path)
+    out = {"sha256": np.array(sha)}
+    for n in (8, 1100):
+        prompt = sg.prompt_ids(spec.seed, n, spec.vocab)
+        ref, toks, logits = run_reference(path, prompt, 4)
+        ref.close()
+        out[f"prompt{n}"] = prompt
+        out[f"tokens{n}"] = toks
+        out[f"logits{n}"] = logits.astype(np.float32)
+        out[f"margin{n}"] = summary(logits)["margin"]
+    np.savez_compressed(os.path.join(HERE, "q4km_d128.npz"), **out)
+
+
 def tiny(seed: int, tmp: str) -> None:
     spec = sg.tiny_spec(seed=seed)
     path = os.path.join(tmp, f"tiny{seed}.gguf")
@@ -191,9 +212,14 @@ def main():
     ap.add_argument("--skip-05b", action="store_true")
     ap.add_argument("--only-7b", action="store_true")
     ap.add_argument("--only-7b-long", action="store_true")
+    ap.add_argument("--only-small", action="store_true")
     args = ap.parse_args()
     if not oracle.ref_available():
         oracle.build()
+    if args.only_small:
+        with tempfile.TemporaryDirectory() as tmp:
+            q4km_small(tmp)
+        return
     if args.only_7b_long:
         with tempfile.TemporaryDirectory(dir=os.environ.get("MYLLM_GOLDEN_TMP")) as tmp:
             qwen2_7b_long(tmp)

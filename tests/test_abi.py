@@ -118,6 +118,69 @@ def _is_ptr(a):
     return a in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(a, type) and issubclass(a, ctypes._Pointer))
 
 
+# Entry points whose pointer arguments are host structs describing device
+# memory (checked by test_fused_decode_description_checks instead).
+HOST_STRUCT_ENTRIES = ("cl_qwen2_decode_supported", "cl_qwen2_decode_step")
+
+
+def _fused_desc(n_layers=2, hidden=3584, ffn=18944, heads=28, kv=4, d=128, vocab=152064, types=None):
+    """A cl_qwen2_decode / cl_qwen2_layer pair of the 7B shape with made-up,
+    aligned device addresses (the checks never dereference them)."""
+    import ctypes
+    addr = iter(range(1 << 24, 1 << 40, 1 << 20))
+    layers = (_native.Qwen2Layer * n_layers)()
+    for l in range(n_layers):
+        L = layers[l]
+        for f in ("q", "k", "v", "o", "gate", "up", "down", "q_bias", "k_bias", "v_bias", "attn_norm", "ffn_norm",
+                  "k_cache", "v_cache"):
+            setattr(L, f, next(addr))
+        t = types or {}
+        L.q_type = t.get("q", sg.Q4_K)
+        L.k_type = t.get("k", sg.Q4_K)
+        L.v_type = t.get("v", sg.Q6_K)
+        L.o_type = t.get("o", sg.Q4_K)
+        L.gate_type = t.get("gate", sg.Q4_K)
+        L.down_type = t.get("down", sg.Q6_K if l % 2 == 0 else sg.Q4_K)
+    m = _native.Qwen2Decode()
+    m.layers = next(addr)
+    m.n_layers, m.hidden, m.ffn, m.vocab = n_layers, hidden, ffn, vocab
+    m.q_heads, m.kv_heads, m.head_dim, m.capacity = heads, kv, d, 4096
+    m.eps, m.scale = 1e-6, d ** -0.5
+    for f in ("embd", "out_w", "out_norm", "rope", "ints", "h", "q", "k", "v", "att", "act", "logits"):
+        setattr(m, f, next(addr))
+    m.embd_stride, m.embd_type, m.out_type = 2016, sg.Q4_K, sg.Q6_K
+    return m, layers, ctypes.byref(m), layers
+
+
+def test_fused_decode_description_checks():
+    """cl_qwen2_decode_supported / _step on host descriptions, without a GPU:
+    the 7B and 14B shapes qualify; other head widths, 32-column formats, more
+    than 8 query heads per KV head, missing or misaligned pointers do not;
+    the step checks its workspace before launching."""
+    import ctypes
+    lib = _native.lib()
+    m, layers, pm, pl = _fused_desc()
+    assert lib.cl_qwen2_decode_supported(pm, pl) == 0
+    m14, l14, pm14, pl14 = _fused_desc(hidden=5120, ffn=13824, heads=40, kv=8)
+    assert lib.cl_qwen2_decode_supported(pm14, pl14) == 0
+    assert lib.cl_qwen2_decode_supported(None, pl) == 1
+    assert lib.cl_qwen2_decode_supported(pm, None) == 1
+    for kw in (dict(d=64, hidden=1792), dict(heads=36, kv=4, hidden=36 * 128), dict(ffn=4864 + 128),
+               dict(types={"q": sg.Q5_0}), dict(types={"down": sg.Q8_0}), dict(vocab=152064 + 8)):
+        _, _, p2, l2 = _fused_desc(**kw)
+        assert lib.cl_qwen2_decode_supported(p2, l2) == 2, kw
+    layers[1].up = None
+    assert lib.cl_qwen2_decode_supported(pm, pl) == 1
+    layers[1].up = (1 << 30) + 8  # misaligned
+    assert lib.cl_qwen2_decode_supported(pm, pl) == 1
+    layers[1].up = 1 << 30
+    assert lib.cl_qwen2_decode_step(pm, pl, None, 1 << 20, None) == 1  # no workspace
+    assert lib.cl_qwen2_decode_step(pm, pl, (1 << 30) + 16, 1 << 20, None) == 1  # misaligned workspace
+    assert lib.cl_qwen2_decode_status(None) is None
+    assert lib.cl_qwen2_decode_status(1 << 30) == (1 << 30) + 8  # after the barrier and done counters
+    assert lib.cl_qwen2_decode_init(None, 256, None) == 1
+
+
 def test_null_pointers_are_rejected_before_any_launch():
     """Every kernel entry point returns an error status for a NULL required
     pointer instead of launching: on a GPU such a launch would read or write
@@ -131,8 +194,8 @@ def test_null_pointers_are_rejected_before_any_launch():
     fake = 1 << 20
     unchecked = []
     for name, (rt, args) in sorted(_native.SIGNATURES.items()):
-        if not name.startswith("cl_") or rt is not ctypes.c_int or name in ("cl_device_error",
-                                                                             "cl_attn_decode_noalloc"):
+        if not name.startswith("cl_") or rt is not ctypes.c_int or name in HOST_STRUCT_ENTRIES + (
+                "cl_device_error", "cl_attn_decode_noalloc"):
             continue
         base = [(ctypes.cast(fake, a) if isinstance(a, type) and issubclass(a, ctypes._Pointer) else fake)
                 if _is_ptr(a) else (1.0 if a is ctypes.c_float else 64) for a in args]

@@ -68,6 +68,9 @@ class _FakeLLM:
     def last_call_ms(self):
         return 2.0
 
+    def last_kernel_ms(self):
+        return 0.0  # the per-operator graph
+
     def last_logits(self):
         import numpy as np
         return np.linspace(-1.0, 1.0, 64, dtype=np.float32)

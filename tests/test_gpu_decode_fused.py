@@ -1,0 +1,112 @@
+"""The one-launch decode step (cl_qwen2_decode_step) against the reference.
+
+CudaLLM runs a one-GPU qwen2 decode step as a single persistent launch when
+every layer matrix is Q4_K / Q6_K and the heads are 128 wide (the 7B and
+14B shapes); CUDALLM_DECODE=graph selects the per-operator graph instead,
+and CUDALLM_DECODE=fused insists on the fused step (construction fails if
+the model does not qualify, so these tests cannot pass on a silent
+fallback).  Both must give the reference CPULLM's greedy tokens at every
+step and logits within 1e-4 (max-abs relative), on a small model with the
+7B's structure (head_dim 128, 7 query heads per KV head): a short prompt
+(one attention split) and a 1100-token prompt (16 key splits of two 64-key
+tiles each, the KV append landing in the last split's second tile).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from myllm_b200 import CudaLLM
+from myllm_b200 import synth_gguf as sg
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / np.abs(b).max())
+
+
+@pytest.fixture(scope="module")
+def small(model_dir, cuda):
+    d = np.load(os.path.join(GOLDEN, "q4km_d128.npz"))
+    path = os.path.join(model_dir, "q4km_d128.gguf")
+    if not os.path.exists(path) or os.path.getsize(path) == 0:
+        assert sg.write_qwen2(sg.q4km_small_spec(), path) == str(d["sha256"])
+    return path, d
+
+
+def run(path, prompt, steps, monkeypatch, mode, max_sequence=2048, prefill="tf32x3"):
+    monkeypatch.setenv("CUDALLM_DECODE", mode)
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
+    llm = CudaLLM(path, max_sequence=max_sequence)
+    toks = [llm.prefill(prompt)]
+    logits = [llm.last_logits()]
+    for _ in range(steps):
+        toks.append(llm.decode(toks[-1]))
+        logits.append(llm.last_logits())
+    llm.close()
+    return toks, logits
+
+
+@pytest.mark.parametrize("mode", ["fused", "graph"])
+@pytest.mark.parametrize("n", [8, 1100])
+def test_small_model_matches_reference(small, monkeypatch, mode, n):
+    path, d = small
+    toks, logits = run(path, d[f"prompt{n}"], 4, monkeypatch, mode)
+    assert toks == list(d[f"tokens{n}"])
+    for i, ref in enumerate(d[f"logits{n}"]):
+        assert rel(logits[i], ref) <= 1e-4, (i, rel(logits[i], ref))
+
+
+@pytest.mark.parametrize("n", [8, 1100])
+def test_small_model_default_paths(small, monkeypatch, n):
+    """The defaults together (FP16 prefill GEMM, fused decode step): the
+    reference's tokens, logits within the north-star 1e-2."""
+    path, d = small
+    toks, logits = run(path, d[f"prompt{n}"], 4, monkeypatch, "fused", prefill="fp16")
+    assert toks == list(d[f"tokens{n}"])
+    for i, ref in enumerate(d[f"logits{n}"]):
+        assert rel(logits[i], ref) <= 1e-2, (i, rel(logits[i], ref))
+
+
+def test_fused_step_is_deterministic(small, monkeypatch):
+    """Partial sums are added in warp order, never in arrival order: two
+    runs give bit-identical logits."""
+    path, d = small
+    a = run(path, d["prompt8"], 3, monkeypatch, "fused")
+    b = run(path, d["prompt8"], 3, monkeypatch, "fused")
+    assert a[0] == b[0]
+    for x, y in zip(a[1], b[1]):
+        assert np.array_equal(x, y)
+
+
+def test_fused_step_across_reset(small, monkeypatch):
+    """The control block is re-armed by every step: a second conversation on
+    the same model (reset, new prefill) decodes the same tokens."""
+    path, d = small
+    monkeypatch.setenv("CUDALLM_DECODE", "fused")
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", "tf32x3")
+    llm = CudaLLM(path, max_sequence=2048)
+    for _ in range(2):
+        llm.reset()
+        toks = [llm.prefill(d["prompt8"])]
+        for _ in range(4):
+            toks.append(llm.decode(toks[-1]))
+        assert toks == list(d["tokens8"])
+    llm.close()
+
+
+def test_fused_refuses_models_it_does_not_support(model_dir, cuda, monkeypatch):
+    """A model with 64-wide heads and 32-column formats (the tiny model) is
+    refused when the fused step is insisted on, and decoded by the graph
+    otherwise."""
+    path = os.path.join(model_dir, "tiny_s7.gguf")
+    sg.write_qwen2(sg.tiny_spec(seed=7), path)
+    monkeypatch.setenv("CUDALLM_DECODE", "fused")
+    with pytest.raises(Exception, match="fused decode"):
+        CudaLLM(path, max_sequence=64)
+    monkeypatch.delenv("CUDALLM_DECODE")
+    llm = CudaLLM(path, max_sequence=64)
+    llm.close()

@@ -1,8 +1,11 @@
 """End-to-end parity of CudaLLM with the reference CPULLM path.
 
 Tokens must be identical at every step; logits must satisfy
-max|g - r| / max|r| <= 1e-2 (the tolerance of the north-star spec).  The
-observed error is far smaller (~1e-5), which the tighter 1e-4 check pins.
+max|g - r| / max|r| <= 1e-2 (the tolerance of the north-star spec).  With
+the FP32-grade prefill GEMM (CUDALLM_PREFILL_GEMM=tf32x3) the observed error
+is ~1e-5, which the tighter 1e-4 check pins; the default prefill rounds the
+GEMM operands once to FP16 (11-bit significands) and is held to the spec's
+1e-2 with identical tokens.
 """
 import os
 
@@ -21,6 +24,11 @@ def rel(a, b):
     return float(np.abs(a - b).max() / np.abs(b).max())
 
 
+# Logit tolerance per prefill GEMM path: FP32-grade paths 1e-4, the 16-bit
+# paths the north-star 1e-2.
+PREFILL_TOL = {"tf32x3": 1e-4, "simt": 1e-4, "fp16": 1e-2, "bf16": 1e-2, "f16": 1e-2}
+
+
 @pytest.fixture(scope="module")
 def tiny_models(model_dir, cuda):
     paths = {}
@@ -33,9 +41,11 @@ def tiny_models(model_dir, cuda):
     return paths
 
 
+@pytest.mark.parametrize("prefill", ["tf32x3", "fp16"])
 @pytest.mark.parametrize("seed", [7, 11])
 @pytest.mark.parametrize("n", [8, 40])
-def test_tiny_parity(tiny_models, seed, n):
+def test_tiny_parity(tiny_models, monkeypatch, seed, n, prefill):
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     path, d = tiny_models[seed]
     llm = CudaLLM(path, max_sequence=64)
     toks = [llm.prefill(d[f"prompt{n}"])]
@@ -46,14 +56,15 @@ def test_tiny_parity(tiny_models, seed, n):
     assert toks == list(d[f"tokens{n}"])
     for got, ref in zip(logits, d[f"logits{n}"]):
         assert rel(got, ref) <= 1e-2
-        assert rel(got, ref) <= 1e-4
+        assert rel(got, ref) <= PREFILL_TOL[prefill]
     llm.close()
 
 
-@pytest.mark.parametrize("path_name", ["simt", "f16"])
+@pytest.mark.parametrize("path_name", ["simt", "f16", "bf16"])
 def test_prefill_gemm_paths(tiny_models, monkeypatch, path_name):
     """The other prefill GEMM paths: the FP32 CUDA-core kernel keeps the
-    1e-4 bar; the single-pass FP16 tensor-core path keeps the spec's 1e-2."""
+    1e-4 bar; the single-pass FP16 tensor-core path over native blocks and
+    the BF16 resident-weight path keep the spec's 1e-2."""
     path, d = tiny_models[11]
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", path_name)
     llm = CudaLLM(path, max_sequence=64)
@@ -137,8 +148,10 @@ def test_bad_model_files(tmp_path, cuda):
         CudaLLM(str(full), max_sequence=10**6)
 
 
-def test_qwen2_05b_parity(model_dir, cuda):
+@pytest.mark.parametrize("prefill", ["tf32x3", "fp16"])
+def test_qwen2_05b_parity(model_dir, cuda, monkeypatch, prefill):
     """BASELINE config 0 against the reference's tokens and logits."""
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     d = np.load(os.path.join(GOLDEN, "qwen2_05b.npz"))
     spec = sg.CONFIGS["qwen2.5-0.5b"]
     path = os.path.join(model_dir, "qwen2.5-0.5b.gguf")
@@ -156,14 +169,18 @@ def test_qwen2_05b_parity(model_dir, cuda):
         err_top = np.abs(lg[d["top_idx"][i]] - d["top_val"][i]).max()
         err_s = np.abs(lg[::16] - d["stride16"][i]).max()
         assert max(err_top, err_s) / d["maxabs"][i] <= 1e-2
-        assert max(err_top, err_s) / d["maxabs"][i] <= 1e-4
-        assert abs(np.abs(lg).max() - d["maxabs"][i]) / d["maxabs"][i] <= 1e-4
+        assert max(err_top, err_s) / d["maxabs"][i] <= PREFILL_TOL[prefill]
+        assert abs(np.abs(lg).max() - d["maxabs"][i]) / d["maxabs"][i] <= PREFILL_TOL[prefill]
     llm.close()
 
 
-def test_qwen2_7b_parity(model_dir, cuda):
+@pytest.mark.parametrize("mode,prefill", [("fused", "tf32x3"), ("graph", "tf32x3"), ("fused", "fp16")])
+def test_qwen2_7b_parity(model_dir, cuda, monkeypatch, mode, prefill):
     """BASELINE config 2 (the bench workload's model, Qwen2.5-7B shape with the
-    Q4_K_M layout) against the reference CPULLM's tokens and logits."""
+    Q4_K_M layout) against the reference CPULLM's tokens and logits, through
+    the one-launch decode step and through the per-operator graph."""
+    monkeypatch.setenv("CUDALLM_DECODE", mode)
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     d = np.load(os.path.join(GOLDEN, "qwen2_7b.npz"))
     spec = sg.CONFIGS["qwen2.5-7b"]
     path = os.path.join(model_dir, "qwen2.5-7b.gguf")
@@ -182,8 +199,39 @@ def test_qwen2_7b_parity(model_dir, cuda):
         err_s = np.abs(lg[::16] - d["stride16"][i]).max()
         # the north-star bar (1e-2) and the FP32-grade level observed at 0.5B
         assert max(err_top, err_s) / d["maxabs"][i] <= 1e-2
-        assert max(err_top, err_s) / d["maxabs"][i] <= 1e-4
+        assert max(err_top, err_s) / d["maxabs"][i] <= PREFILL_TOL[prefill]
     llm.close()
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(GOLDEN, "qwen2_7b_long.npz")),
+                    reason="the full-length 7B golden has not been generated")
+@pytest.mark.parametrize("prefill", ["fp16", "tf32x3"])
+def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, prefill):
+    """The bench workload end to end: the 512-token prompt
+    bench.py prefills, then 128 greedy decodes against a 4096-slot cache, on
+    the default decode path (and the default, FP16, prefill GEMM: what
+    bench.py times).  Every token identical to CPULLM's; logits (the
+    reference's top 64 and every 16th) within the path's bar."""
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
+    d = np.load(os.path.join(GOLDEN, "qwen2_7b_long.npz"))
+    assert int(d["cpullm_checked"]) == 1, "fixture not cross-checked against CPULLM itself"
+    spec = sg.CONFIGS["qwen2.5-7b"]
+    path = os.path.join(model_dir, "qwen2.5-7b.gguf")
+    if not os.path.exists(path) or os.path.getsize(path) == 0:
+        assert sg.write_qwen2(spec, path) == str(d["sha256"])
+    assert np.array_equal(d["prompt"], sg.prompt_ids(spec.seed, 512, spec.vocab))
+    llm = CudaLLM(path, max_sequence=4096)
+    toks = [llm.prefill(d["prompt"])]
+    errs = []
+    for i in range(len(d["tokens"])):
+        lg = llm.last_logits()
+        err = max(np.abs(lg[d["top_idx"][i]] - d["top_val"][i]).max(), np.abs(lg[::16] - d["stride16"][i]).max())
+        errs.append(err / d["maxabs"][i])
+        if i + 1 < len(d["tokens"]):
+            toks.append(llm.decode(toks[-1]))
+    llm.close()
+    assert toks == list(d["tokens"])
+    assert max(errs) <= PREFILL_TOL[prefill], (int(np.argmax(errs)), max(errs))
 
 
 def test_profile_csv(tiny_models, tmp_path):

@@ -20,7 +20,8 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("n", [8, 40])
-def test_tensor_parallel_two_gpus_matches_reference(model_dir, cuda, n):
+def test_tensor_parallel_two_gpus_matches_reference(model_dir, cuda, monkeypatch, n):
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", "tf32x3")  # FP32-grade prefill: the 1e-4 bar
     d = np.load(os.path.join(GOLDEN, "tiny_s7.npz"))
     path = os.path.join(model_dir, "tiny_s7.gguf")
     assert sg.write_qwen2(sg.tiny_spec(seed=7), path) == str(d["sha256"])
@@ -37,6 +38,7 @@ def test_tensor_parallel_peer_allreduce(model_dir, cuda, monkeypatch):
     mapped by CUDA IPC, rank-order sum) instead of NCCL: the same tokens and
     logits as the reference, and bit-identical logits on both ranks."""
     monkeypatch.setenv("CUDALLM_ALLREDUCE", "p2p")  # inherited by the spawned ranks
+    monkeypatch.setenv("CUDALLM_PREFILL_GEMM", "tf32x3")
     d = np.load(os.path.join(GOLDEN, "tiny_s7.npz"))
     path = os.path.join(model_dir, "tiny_s7.gguf")
     assert sg.write_qwen2(sg.tiny_spec(seed=7), path) == str(d["sha256"])
