@@ -218,6 +218,12 @@ CL_API int cl_attn_decode_noalloc(const float* q, const float* k_cache, const fl
  * cpu_llm.cpp:816-827).  q, out: [rows][q_heads*head_dim]. */
 CL_API int cl_attn_prefill(const float* q, const float* k_cache, const float* v_cache, int pos0, int rows,
                            int q_heads, int kv_heads, int head_dim, float* out, cudaStream_t stream);
+/* The same causal prefill attention on the tensor cores: q, k, v and the
+ * probabilities rounded to FP16 for mma.sync, FP32 accumulation and
+ * softmax (the fast prefill path).  head_dim 128 (else CL_ERR_UNSUPPORTED);
+ * q, caches and out 16-byte aligned. */
+CL_API int cl_attn_prefill_tc(const float* q, const float* k_cache, const float* v_cache, int pos0, int rows,
+                              int q_heads, int kv_heads, int head_dim, float* out, cudaStream_t stream);
 
 /* ---- greedy token (metal_argmax_partial/finalize_f32, metal_llm.metal:
  * 1544-1644; CPU greedy_token cpu_llm.cpp:34-48) -------------------------
@@ -255,10 +261,12 @@ CL_API int cl_counter_add(int* counters, int n, int delta, cudaStream_t stream);
  *
  * Supported: every layer matrix Q4_K or Q6_K (gate and up one type), hidden,
  * ffn % 256 == 0, output rows % 16 == 0, head_dim 128 with RoPE over the
- * whole head, q_heads / kv_heads <= 8, kv_heads <= 32, ffn and hidden <=
- * 20480; else CL_ERR_UNSUPPORTED (use the per-operator path).
+ * whole head, q_heads / kv_heads <= 8, kv_heads <= 32, hidden <= 6144,
+ * ffn <= 20480; else CL_ERR_UNSUPPORTED (use the per-operator path).
  * `layers` is a device array of n_layers entries; `host_layers` the same
- * table in host memory (checked here).  Weights are in the device layout
+ * table in host memory (checked here).  Every layer matrix and out_w is in
+ * the tiled decode layout of cl_decode_pack (gate: the pack of gate and up
+ * together; `up` is not read); embd stays in the device layout
  * (cl_repack_rows).  The workspace (cl_qwen2_decode_workspace_bytes, for
  * the current device) must be zeroed once by cl_qwen2_decode_init; every
  * step leaves it re-armed.  If a grid barrier wait runs out (2 s) the step
@@ -284,8 +292,20 @@ typedef struct cl_qwen2_decode {
     const float* rope;            /* [capacity][head_dim / 2][cos, sin] */
     int* ints;                    /* [0] token in, [1] position, [3] token out */
     float *h, *q, *k, *v, *att, *act, *logits; /* [hidden], [q_heads*d], [kv*d] x2, [q_heads*d], [ffn], [vocab] */
+    long long* trace;             /* optional (NULL): [grid][5 n_layers + 1][3] %globaltimer stamps per CTA and
+                                     phase: start, input encoded, work done */
 } cl_qwen2_decode;
 
+/* The tiled decode layout of one matrix: its device-layout rows
+ * (cl_repack_rows) regrouped so that each unit the step streams is one
+ * contiguous block: Q4_K 16 rows x two super-blocks (2 x 144 bytes; an odd
+ * last one padded with a zero super-block), Q6_K 16 rows x one super-block
+ * as two 112-byte halves (ql, qh, sc of the half, f16 d, zero pad).  With
+ * w_up (pair != 0 for the size query) the gate and up rows are interleaved
+ * 8 by 8.  rows % 16 == 0 (pair: % 8), k % 256 == 0. */
+CL_API size_t cl_decode_pack_bytes(int type, int rows, int k, int pair);
+CL_API int cl_decode_pack(int type, const void* w, long long stride, int rows, int k, const void* w_up, void* out,
+                          cudaStream_t stream);
 CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_layer* host_layers);
 CL_API size_t cl_qwen2_decode_workspace_bytes(const cl_qwen2_decode* m);
 CL_API int cl_qwen2_decode_init(void* workspace, size_t workspace_bytes, cudaStream_t stream);

@@ -59,6 +59,7 @@ SIGNATURES = {
     "cl_attn_decode_noalloc_limit_bytes": (c_size, []),
     "cl_attn_decode_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp]),
     "cl_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "cl_attn_prefill_tc": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     "cl_argmax_workspace_bytes": (c_size, [c_int]),
     "cl_argmax": (c_int, [c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
     "cl_argmax_ex": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_size, c_vp]),
@@ -85,6 +86,8 @@ SIGNATURES = {
     "cl_convert16": (c_int, [c_vp, c_ll, c_vp, c_int, c_vp]),
     "cl_gemm16_workspace_bytes": (c_size, [c_int, c_int, c_int]),
     "cl_gemm16_run": (c_int, [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_int, c_int, c_vp, c_size, c_vp]),
+    "cl_decode_pack_bytes": (c_size, [c_int, c_int, c_int, c_int]),
+    "cl_decode_pack": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
     "cl_qwen2_decode_supported": (c_int, [c_vp, c_vp]),
     "cl_qwen2_decode_workspace_bytes": (c_size, [c_vp]),
     "cl_qwen2_decode_init": (c_int, [c_vp, c_size, c_vp]),
@@ -136,7 +139,7 @@ class Qwen2Decode(ctypes.Structure):
                                       "capacity")] +
                 [("eps", c_float), ("scale", c_float), ("embd", c_vp), ("embd_stride", c_ll), ("embd_type", c_int),
                  ("out_type", c_int), ("out_w", c_vp), ("out_norm", c_vp), ("rope", c_vp), ("ints", c_vp)] +
-                [(n, c_vp) for n in ("h", "q", "k", "v", "att", "act", "logits")])
+                [(n, c_vp) for n in ("h", "q", "k", "v", "att", "act", "logits", "trace")])
 
 
 def lib():

@@ -212,12 +212,16 @@ struct CudaLLM::Impl {
     // the model's shapes and types allow it; CUDALLM_DECODE=graph selects the
     // per-operator graph instead.
     bool fused = false;
-    bool fused_eager = false;  // the step is launched directly when graph capture refuses it
     cl_qwen2_decode fused_desc{};
     std::vector<cl_qwen2_layer> fused_layers;
     cl_qwen2_layer* fused_layers_dev = nullptr;
     void* fused_ws = nullptr;
     std::size_t fused_ws_bytes = 0;
+    // CUDALLM_DECODE_TRACE=<file>: every fused step's per-CTA, per-phase
+    // timestamps (int64 [grid][phases][3]) overwrite <file> after the step
+    DeviceBuffer trace_mem;
+    std::string trace_path;
+    DeviceBuffer pack_mem;  // every layer matrix and the LM head in the tiled decode layout
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEvent_t kev0 = nullptr, kev1 = nullptr;  // around the fused step kernel
     float last_ms = 0.0f, last_kernel_ms = 0.0f;
@@ -482,6 +486,45 @@ struct CudaLLM::Impl {
         if (rc != CL_OK) {
             if (mode == "fused") throw std::runtime_error(std::string("fused decode: ") + cl_status_string(rc));
             return;
+        }
+        // the step streams each matrix from its tiled copy (cl_decode_pack)
+        {
+            auto bytes = [](const DevMat& m, bool pair) {
+                return (cl_decode_pack_bytes(m.type, m.rows, m.cols, pair ? 1 : 0) + 255) / 256 * 256;
+            };
+            std::size_t total = bytes(out_w, false);
+            for (const Layer& L : layers)
+                total += bytes(L.q, false) + bytes(L.k, false) + bytes(L.v, false) + bytes(L.o, false) +
+                         bytes(L.gate, true) + bytes(L.down, false);
+            pack_mem = DeviceBuffer(total + 256);
+            char* base = static_cast<char*>(pack_mem.get());
+            auto pack = [&](const DevMat& m, const DevMat* up) -> const void* {
+                char* dst = base;
+                CUDALLM_CL(cl_decode_pack(m.type, m.ptr, m.stride, m.rows, m.cols, up ? up->ptr : nullptr, dst, stream));
+                base += bytes(m, up != nullptr);
+                return dst;
+            };
+            fused_desc.out_w = pack(out_w, nullptr);
+            for (std::size_t l = 0; l < layers.size(); ++l) {
+                const Layer& L = layers[l];
+                cl_qwen2_layer& f = fused_layers[l];
+                f.q = pack(L.q, nullptr);
+                f.k = pack(L.k, nullptr);
+                f.v = pack(L.v, nullptr);
+                f.o = pack(L.o, nullptr);
+                f.gate = pack(L.gate, &L.up);
+                f.up = nullptr;
+                f.down = pack(L.down, nullptr);
+            }
+            CUDALLM_CL(cl_qwen2_decode_supported(&fused_desc, fused_layers.data()));
+        }
+        if (const char* e = std::getenv("CUDALLM_DECODE_TRACE")) {
+            int sms = 0;
+            CUDALLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+            trace_path = e;
+            trace_mem = DeviceBuffer((std::size_t)sms * (5 * layers.size() + 1) * 3 * sizeof(long long));
+            CUDALLM_CUDA(cudaMemsetAsync(trace_mem.get(), 0, trace_mem.size(), stream));
+            fused_desc.trace = static_cast<long long*>(trace_mem.get());
         }
         CUDALLM_CUDA(cudaMemcpyAsync(fused_layers_dev, fused_layers.data(),
                                      fused_layers.size() * sizeof(cl_qwen2_layer), cudaMemcpyHostToDevice, stream));
@@ -775,7 +818,10 @@ struct CudaLLM::Impl {
             }
             CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
                                   pos0, L.k_cache, L.v_cache, s));
-            CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
+            // the 16-bit prefill path takes the FP16 tensor-core attention where it applies
+            if (!(wide16() && d == 128 &&
+                  cl_attn_prefill_tc(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s) == CL_OK))
+                CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
             const float* o_in = A;
             if (gather_attn) {
                 // rank-major gather [W][m][qd_l] -> rows [m][hq*d], then the
@@ -915,28 +961,26 @@ struct CudaLLM::Impl {
             throw std::out_of_range("CUDA decode token id is outside the vocabulary");
         if (position >= max_seq) throw std::length_error("CUDA decode exceeds sequence capacity");
         CUDALLM_CUDA(cudaSetDevice(device));
-        if (decode_exec == nullptr && !fused_eager) {
-            if (fused) {
-                try {
-                    build_decode_graph();
-                } catch (const std::runtime_error&) {
-                    fused_eager = true;  // launched directly, one step at a time
-                    cudaGetLastError();
-                }
-            } else {
-                build_decode_graph();
-            }
-        }
+        // The fused step is three stream operations (token copy, the step
+        // kernel between two timing events, token copy back), launched
+        // directly; the per-operator path is one captured graph.
+        if (decode_exec == nullptr && !fused) build_decode_graph();
         host_in()[0] = token;
         const TraceRange trace("decode.gpu_resident");
         begin_timing();
-        if (fused_eager)
+        if (fused)
             record_decode();
         else
             CUDALLM_CUDA(cudaGraphLaunch(decode_exec, stream));
         end_timing("decode", 1);
         last_kernel_ms = 0.0f;
         if (fused) CUDALLM_CUDA(cudaEventElapsedTime(&last_kernel_ms, kev0, kev1));
+        if (fused && !trace_path.empty()) {
+            std::vector<long long> t(trace_mem.size() / sizeof(long long));
+            CUDALLM_CUDA(cudaMemcpy(t.data(), trace_mem.get(), trace_mem.size(), cudaMemcpyDeviceToHost));
+            std::ofstream f(trace_path, std::ios::binary | std::ios::trunc);
+            f.write(reinterpret_cast<const char*>(t.data()), (std::streamsize)(t.size() * sizeof(long long)));
+        }
         if (peer_allreduce && host_in()[2] != 0)
             throw std::runtime_error("peer all-reduce: a rank did not reach the decode step within the wait limit");
         if (fused && host_in()[2] != 0) {
@@ -1005,7 +1049,7 @@ const std::string& CudaLLM::device_name() const {
 MemoryStats CudaLLM::memory_stats() const noexcept {
     if (!impl_) return {};
     MemoryStats m;
-    m.weight_bytes = impl_->weight_mem.size() + impl_->w16_mem.size();
+    m.weight_bytes = impl_->weight_mem.size() + impl_->w16_mem.size() + impl_->pack_mem.size();
     m.kv_cache_bytes = impl_->kv_bytes;
     m.recurrent_state_bytes = 0;
     m.intermediate_bytes = impl_->act_bytes;

@@ -11,6 +11,7 @@ int g_pdl_enabled = 1;
 // One thread per GGML block: native row bytes -> device layout (gemv.cu header).
 __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                               int rows, int k, long long src_rb, long long dst_rb) {
+    grid_wait();  // launched with programmatic dependent launch: the previous kernel's writes first
     const int bsize = (type == CL_TYPE_Q8_0 || type == CL_TYPE_Q5_0) ? 32 : 256;
     const int nb = k / bsize;
     const long long total = (long long)rows * nb;
@@ -67,6 +68,7 @@ __global__ void repack_kernel(int type, const uint8_t* __restrict__ src, uint8_t
 
 __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
                                  long long src_rb, long long dst_rb) {
+    grid_wait();
     const long long total = (long long)rows * dst_rb;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
          t += (long long)gridDim.x * blockDim.x) {
@@ -192,14 +194,16 @@ CL_API int cl_repack_rows(int type, const void* native, void* packed, int rows, 
     const long long srb = cl_native_row_bytes(type, k), drb = cl_row_stride(type, k);
     if (srb < 0 || rows < 0 || native == nullptr || packed == nullptr) return CL_ERR_INVALID;
     if (rows == 0) return CL_OK;
-    if (type == CL_TYPE_F32 || type == CL_TYPE_F16) {
-        copy_rows_kernel<<<1184, 256, 0, stream>>>(static_cast<const uint8_t*>(native),
-                                                   static_cast<uint8_t*>(packed), rows, srb, drb);
-    } else {
-        repack_kernel<<<1184, 256, 0, stream>>>(type, static_cast<const uint8_t*>(native),
-                                                static_cast<uint8_t*>(packed), rows, k, srb, drb);
-    }
-    return cudaGetLastError() == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+    // the launch's own status (a stale error of an earlier runtime call must
+    // not be reported as this launch's)
+    cudaError_t e;
+    if (type == CL_TYPE_F32 || type == CL_TYPE_F16)
+        e = launch_pdl(copy_rows_kernel, dim3(1184), dim3(256), 0, stream, static_cast<const uint8_t*>(native),
+                       static_cast<uint8_t*>(packed), rows, srb, drb);
+    else
+        e = launch_pdl(repack_kernel, dim3(1184), dim3(256), 0, stream, type, static_cast<const uint8_t*>(native),
+                       static_cast<uint8_t*>(packed), rows, k, srb, drb);
+    return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
 }
 
 CL_API size_t cl_xq_bytes(int k) { return k > 0 && k % 32 == 0 ? xq_total_bytes(k) : 0; }

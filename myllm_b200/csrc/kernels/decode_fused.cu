@@ -8,7 +8,7 @@
 // attention as in attn.cu), arranged for the B200 instead of as one launch
 // per operator:
 //
-// * One CTA per SM (cooperative launch, so all CTAs are resident), 16 warps.
+// * One CTA per SM (cooperative launch, so all CTAs are resident), 12 warps.
 //   The step is a fixed sequence of phases: per layer QKV, attention, o_proj,
 //   gate/up, down; then the LM head.  Phases are separated by grid barriers
 //   (an arrival counter; every wait bounded by a 2 s clock and an abort flag).
@@ -17,7 +17,7 @@
 //   (one m16 MMA computes both, so the SwiGLU pair meets in one lane).  The
 //   units of a phase are split into equal contiguous ranges, one per warp of
 //   the grid (stream-K), so every SM streams the same bytes of every matrix.
-// * Each warp owns a 3-slot shared-memory ring that it fills itself with
+// * Each warp owns a 4-slot shared-memory ring that it fills itself with
 //   cp.async (no hand-off between warps).  The ring runs ahead through the
 //   warp's units of the following phases: weights never depend on the
 //   activations, so while the grid waits at a barrier, or encodes the next
@@ -49,14 +49,20 @@ namespace dfz {
 
 using gmma::Q4Lane;
 
-constexpr int kW = 16;                  // warps per CTA
+constexpr int kW = 8;                   // warps per CTA
 constexpr int kThreads = kW * 32;
 constexpr int kSlots = 3;               // ring depth per warp
-constexpr int kRS = 160;                // shared row stride of a unit (row stride % 64 == 32: conflict-free)
-constexpr int kSlotBytes = 16 * kRS;
+// Shared row strides of a unit in a ring slot, each chosen so the MMA
+// fragment reads are bank-conflict free: Q4_K 2 x 144 B rows read as 8-byte
+// words (stride % 64 == 32), Q6_K 2 x 112 B rows read as 4-byte words
+// (stride / 4 = 60: rows 0-7 start 4 banks apart).
+constexpr int kRS4 = 288;
+constexpr int kRS6 = 240;
+constexpr int kSlotBytes = 16 * kRS4;
 constexpr int kRingBytes = kW * kSlots * kSlotBytes;
-constexpr int kXBlocksPerWarp = 5;      // x blocks one warp encodes: k <= 16 * 5 * 256
+constexpr int kXBlocksPerWarp = 10;     // x blocks one warp encodes: k <= 8 * 10 * 256
 constexpr int kMaxK = kW * kXBlocksPerWarp * 256;
+constexpr int kNormBlocks = 3;          // RMS-normalised inputs: k <= 8 * 3 * 256
 constexpr int kSplitsMax = 16;          // key splits per KV head
 constexpr int kGMax = 8;                // query heads per KV head
 constexpr int kD = 128;                 // head dim
@@ -77,13 +83,11 @@ struct Ctl {
 static_assert(sizeof(Ctl) == 256, "control block is 256 bytes");
 
 struct Seg {
-    const uint8_t* w;
-    const uint8_t* w_up;  // gate/up: the up rows (same type and stride as w)
+    const uint8_t* w;     // the matrix in the tiled decode layout (cl_decode_pack)
     const float* bias;
     float* y;
-    long long stride;
     long long u0;         // first unit of the segment in its phase
-    int type, nsub, tile0, tiles;
+    int type, nsub, tile0, tiles, sw;
 };
 
 struct Phase {
@@ -111,23 +115,24 @@ struct Params {
     float2* records;        // [grid] head candidates (value, index as float bits)
     float* partials;        // [grid * kW][2][16]
     float* attn_part;       // [hkv][kSplitsMax][G][kD + 2]
+    long long* trace;       // optional [grid][phases][3] timestamps
     int region_bytes;
 };
 
-CL_DEVINL long long row_stride(int type, int nb) {
-    return ((long long)nb * (type == CL_TYPE_Q4_K ? 144 : 210) + 15) & ~15ll;
-}
+// Bytes of one unit (16 rows) in the tiled decode layout: Q4_K two
+// super-blocks (2 x 144 B per row), Q6_K one super-block as two 112-byte
+// halves per row.
+__host__ __device__ constexpr int unit_bytes(int type) { return type == CL_TYPE_Q4_K ? 16 * 288 : 16 * 224; }
 
-CL_DEVINL void set_seg(Seg& s, const void* w, const void* w_up, int type, int rows, int nb, const float* bias,
-                       float* y, long long& u, int& tile) {
+CL_DEVINL void set_seg(Seg& s, const void* w, bool sw, int type, int rows, int nb, const float* bias, float* y,
+                       long long& u, int& tile) {
     s.w = static_cast<const uint8_t*>(w);
-    s.w_up = static_cast<const uint8_t*>(w_up);
+    s.sw = sw;
     s.bias = bias;
     s.y = y;
     s.type = type;
-    s.stride = row_stride(type, nb);
-    s.nsub = type == CL_TYPE_Q4_K ? nb : 2 * nb;
-    s.tiles = w_up ? rows / 8 : rows / 16;
+    s.nsub = type == CL_TYPE_Q4_K ? (nb + 1) / 2 : nb;
+    s.tiles = sw ? rows / 8 : rows / 16;
     s.u0 = u;
     s.tile0 = tile;
     u += (long long)s.tiles * s.nsub;
@@ -150,7 +155,7 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         ph.x = P.h;
         ph.gamma = P.out_norm;
         ph.head = 1;
-        set_seg(ph.seg[0], P.out_w, nullptr, P.out_type, P.V, ph.nb, nullptr, P.logits, u, tile);
+        set_seg(ph.seg[0], P.out_w, false, P.out_type, P.V, ph.nb, nullptr, P.logits, u, tile);
         ph.U = u;
         return;
     }
@@ -162,9 +167,9 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         ph.x = p == 0 ? nullptr : P.h;
         ph.gamma = L.attn_norm;
         ph.nseg = 3;
-        set_seg(ph.seg[0], L.q, nullptr, L.q_type, P.hq * d, ph.nb, L.q_bias, P.q, u, tile);
-        set_seg(ph.seg[1], L.k, nullptr, L.k_type, P.hkv * d, ph.nb, L.k_bias, P.k, u, tile);
-        set_seg(ph.seg[2], L.v, nullptr, L.v_type, P.hkv * d, ph.nb, L.v_bias, P.v, u, tile);
+        set_seg(ph.seg[0], L.q, false, L.q_type, P.hq * d, ph.nb, L.q_bias, P.q, u, tile);
+        set_seg(ph.seg[1], L.k, false, L.k_type, P.hkv * d, ph.nb, L.k_bias, P.k, u, tile);
+        set_seg(ph.seg[2], L.v, false, L.v_type, P.hkv * d, ph.nb, L.v_bias, P.v, u, tile);
         break;
     case 1:
         ph.attn = 1;
@@ -176,7 +181,7 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         ph.K = P.H;
         ph.x = P.att;
         ph.residual = 1;
-        set_seg(ph.seg[0], L.o, nullptr, L.o_type, P.H, ph.nb, nullptr, P.h, u, tile);
+        set_seg(ph.seg[0], L.o, false, L.o_type, P.H, ph.nb, nullptr, P.h, u, tile);
         break;
     case 3:
         ph.nb = P.H / 256;
@@ -184,30 +189,43 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         ph.x = P.h;
         ph.gamma = L.ffn_norm;
         ph.sw = 1;
-        set_seg(ph.seg[0], L.gate, L.up, L.gate_type, P.F, ph.nb, nullptr, P.act, u, tile);
+        set_seg(ph.seg[0], L.gate, true, L.gate_type, P.F, ph.nb, nullptr, P.act, u, tile);
         break;
     default:
         ph.nb = P.F / 256;
         ph.K = P.F;
         ph.x = P.act;
         ph.residual = 1;
-        set_seg(ph.seg[0], L.down, nullptr, L.down_type, P.H, ph.nb, nullptr, P.h, u, tile);
+        set_seg(ph.seg[0], L.down, false, L.down_type, P.H, ph.nb, nullptr, P.h, u, tile);
         break;
     }
     ph.U = u;
 }
 
-struct Unit {
-    int s, tile_l, j;
+// A warp's position in its range of a phase: unit j of tile `tile` of
+// segment s, `left` units to go.  Advanced without divisions.
+struct Cursor {
+    int s, tile, j, left;
 };
 
-CL_DEVINL Unit unit_at(const Phase& ph, long long u) {
+CL_DEVINL Cursor cursor_at(const Phase& ph, long long u, long long e) {
     int s = 0;
     if (ph.nseg > 1 && u >= ph.seg[1].u0) s = 1;
     if (ph.nseg > 2 && u >= ph.seg[2].u0) s = 2;
-    const long long local = u - ph.seg[s].u0;
+    const int local = (int)(u - ph.seg[s].u0);
     const int ns = ph.seg[s].nsub;
-    return Unit{s, (int)(local / ns), (int)(local % ns)};
+    return Cursor{s, local / ns, local % ns, (int)(e - u)};
+}
+
+CL_DEVINL void cursor_next(const Phase& ph, Cursor& c) {
+    --c.left;
+    if (++c.j == ph.seg[c.s].nsub) {
+        c.j = 0;
+        if (++c.tile == ph.seg[c.s].tiles) {
+            c.tile = 0;
+            ++c.s;
+        }
+    }
 }
 
 // Range [begin(w), begin(w + 1)) of the grid's warp w over U units.
@@ -215,10 +233,10 @@ CL_DEVINL long long range_begin(long long U, int w, int GW) { return U * w / GW;
 // The warp whose range holds unit u.
 CL_DEVINL int warp_of(long long U, long long u, int GW) { return (int)(((u + 1) * GW - 1) / U); }
 
-CL_DEVINL const uint8_t* unit_row(const Seg& sg, int tile_l, int r) {
-    if (sg.w_up) return (r < 8 ? sg.w + (long long)(tile_l * 8 + r) * sg.stride
-                               : sg.w_up + (long long)(tile_l * 8 + r - 8) * sg.stride);
-    return sg.w + (long long)(tile_l * 16 + r) * sg.stride;
+// First byte of a unit: units are stored tile by tile, each 16 rows x the
+// unit's bytes per row, contiguous.
+CL_DEVINL const uint8_t* unit_src(const Seg& sg, int tile, int j) {
+    return sg.w + ((long long)tile * sg.nsub + j) * unit_bytes(sg.type);
 }
 
 CL_DEVINL void cp16(void* dst, const void* src) {
@@ -230,38 +248,61 @@ CL_DEVINL void cp8(void* dst, const void* src) {
 CL_DEVINL void cp4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// Weights are read once per step: evict-first keeps the KV cache, the
+// activations and the partials resident in L2 meanwhile.
+CL_DEVINL void cp16_stream(void* dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "l"(policy)
+                 : "memory");
+}
+CL_DEVINL uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 CL_DEVINL void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 CL_DEVINL void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 CL_DEVINL void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// The lane's copies of unit u into a ring slot.  Q4_K: 16 rows x 144 bytes
-// (9 x 16 B each).  Q6_K half hh of super-block sb, per row: ql[64hh..+64]
-// at 0, qh[32hh..+32] at 64, sc[8hh..+8] at 96, and the 4-byte word holding
-// the block's f16 d at 104.
-CL_DEVINL void issue_unit(const Phase& ph, long long u, uint8_t* slot, int lane) {
-    const Unit un = unit_at(ph, u);
-    const Seg& sg = ph.seg[un.s];
-    if (sg.type == CL_TYPE_Q4_K) {
-        const long long off = (long long)un.j * 144;
-        for (int c = lane; c < 144; c += 32) {
-            const int r = c / 9, piece = c - 9 * r;
-            cp16(slot + r * kRS + 16 * piece, unit_row(sg, un.tile_l, r) + off + 16 * piece);
-        }
-    } else {
-        const int sb = un.j >> 1, hh = un.j & 1, r = lane >> 1;
-        const uint8_t* row = unit_row(sg, un.tile_l, r);
-        const uint8_t* blk = row + (long long)sb * 208;
-        uint8_t* dst = slot + r * kRS;
-        if ((lane & 1) == 0) {
+// The lane's share of a unit's 16-byte pieces: a unit is 16 rows of 18
+// (Q4_K: 288 B) or 14 (Q6_K: 224 B) pieces, contiguous in global memory;
+// piece c goes to row c / P, offset 16 (c % P) of the slot's padded rows.
+// Pieces lane + 32 i, fixed per lane (Q4_K: 9 each, Q6_K: 7 each).
+struct LanePlan {
+    int dst4[9];
+    int dst6[7];
+};
+
+CL_DEVINL LanePlan lane_plan(int lane) {
+    LanePlan pl;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) cp16(dst + 16 * i, blk + 64 * hh + 16 * i);
-        } else {
-            cp16(dst + 64, blk + 128 + 32 * hh);
-            cp16(dst + 80, blk + 128 + 32 * hh + 16);
-            cp8(dst + 96, blk + 192 + 8 * hh);
-            cp4(dst + 104, row + (((long long)ph.nb * 208 + 2 * sb) & ~3ll));
-        }
+    for (int i = 0; i < 9; ++i) {
+        const int c = lane + 32 * i;
+        pl.dst4[i] = (c / 18) * kRS4 + 16 * (c % 18);
+    }
+#pragma unroll
+    for (int i = 0; i < 7; ++i) {
+        const int c = lane + 32 * i;
+        pl.dst6[i] = (c / 14) * kRS6 + 16 * (c % 14);
+    }
+    return pl;
+}
+
+// The lane's copies of the cursor's unit into a ring slot.  Row layout in
+// the slot: Q4_K (stride kRS4) super-blocks 2j and 2j + 1, 144 bytes each;
+// Q6_K (stride kRS6) the two halves of super-block j, 112 bytes each: ql of
+// the half at 0, qh at 64, sc at 96, the block's f16 d at 104.
+CL_DEVINL void issue_unit(const Phase& ph, const Cursor& cu, uint8_t* slot, int lane, const LanePlan& pl,
+                          uint64_t policy) {
+    const Seg& sg = ph.seg[cu.s];
+    const uint8_t* src = unit_src(sg, cu.tile, cu.j) + 16 * lane;
+    if (sg.type == CL_TYPE_Q4_K) {
+#pragma unroll
+        for (int i = 0; i < 9; ++i) cp16_stream(slot + pl.dst4[i], src + 512 * i, policy);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 7; ++i) cp16_stream(slot + pl.dst6[i], src + 512 * i, policy);
     }
 }
 
@@ -303,9 +344,8 @@ CL_DEVINL void q6k_half(const uint8_t* bg, const uint8_t* b8, const uint8_t* p0,
             a3 += c[3] * s8;
         }
     }
-    const int dsh = 16 * (sb & 1);
-    const float dg = half_bits_to_float(*reinterpret_cast<const uint32_t*>(bg + 104) >> dsh);
-    const float d8 = half_bits_to_float(*reinterpret_cast<const uint32_t*>(b8 + 104) >> dsh);
+    const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bg + 104));
+    const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b8 + 104));
     const float vg = fmaf((float)a0, L6.lw0, (float)a1 * L6.lw1) * xs;
     const float v8 = fmaf((float)a2, L6.lw0, (float)a3 * L6.lw1) * xs;
     yg = fmaf(dg, vg, yg);
@@ -374,35 +414,41 @@ CL_DEVINL void encode_input(const Params& P, const Phase& ph, const Smem& S, int
     uint8_t* xq = S.region;
     float* xs = reinterpret_cast<float*>(S.region + nb * 1024);
     float* xsum = reinterpret_cast<float*>(S.region + nb * 1024 + ((nb * 4 + 15) & ~15));
-    float xv[kXBlocksPerWarp][8];
-    const bool embed = ph.x == nullptr;
-    const uint8_t* erow = P.embd + (long long)tok * P.embd_stride;
+    if (ph.gamma) {
+        // RMS-normalised input (k = hidden <= kW * kNormBlocks * 256): x and
+        // gamma loads all in flight together, then cpu_llm.cpp:156-165's
+        // arithmetic: sum of squares in double, the same order in every CTA,
+        // inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).
+        float xv[kNormBlocks][8], gv[kNormBlocks][8];
+        const bool embed = ph.x == nullptr;
+        const uint8_t* erow = P.embd + (long long)tok * P.embd_stride;
 #pragma unroll
-    for (int i = 0; i < kXBlocksPerWarp; ++i) {
-        const int b = warp + i * kW;
-        if (b < nb) {
-            const int c0 = b * 256 + lane * 8;
-            if (embed) {
+        for (int i = 0; i < kNormBlocks; ++i) {
+            const int b = warp + i * kW;
+            if (b < nb) {
+                const int c0 = b * 256 + lane * 8;
+                const float4 q0 = *reinterpret_cast<const float4*>(ph.gamma + c0);
+                const float4 q1 = *reinterpret_cast<const float4*>(ph.gamma + c0 + 4);
+                gv[i][0] = q0.x; gv[i][1] = q0.y; gv[i][2] = q0.z; gv[i][3] = q0.w;
+                gv[i][4] = q1.x; gv[i][5] = q1.y; gv[i][6] = q1.z; gv[i][7] = q1.w;
+                if (embed) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) xv[i][e] = dequant_at(P.embd_type, erow, P.H, c0 + e);
-                if (blockIdx.x == 0) {
+                    for (int e = 0; e < 8; ++e) xv[i][e] = dequant_at(P.embd_type, erow, P.H, c0 + e);
+                    if (blockIdx.x == 0) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) P.h[c0 + e] = xv[i][e];
+                        for (int e = 0; e < 8; ++e) P.h[c0 + e] = xv[i][e];
+                    }
+                } else {
+                    const float4 u0 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0));
+                    const float4 u1 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0 + 4));
+                    xv[i][0] = u0.x; xv[i][1] = u0.y; xv[i][2] = u0.z; xv[i][3] = u0.w;
+                    xv[i][4] = u1.x; xv[i][5] = u1.y; xv[i][6] = u1.z; xv[i][7] = u1.w;
                 }
-            } else {
-                const float4 u0 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0));
-                const float4 u1 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0 + 4));
-                xv[i][0] = u0.x; xv[i][1] = u0.y; xv[i][2] = u0.z; xv[i][3] = u0.w;
-                xv[i][4] = u1.x; xv[i][5] = u1.y; xv[i][6] = u1.z; xv[i][7] = u1.w;
             }
         }
-    }
-    if (ph.gamma) {
-        // cpu_llm.cpp:156-165: sum of squares in double, the same order in
-        // every CTA, inv = 1/sqrt(mean + eps) in float, x * (inv * gamma).
         double ss = 0.0;
 #pragma unroll
-        for (int i = 0; i < kXBlocksPerWarp; ++i)
+        for (int i = 0; i < kNormBlocks; ++i)
             if (warp + i * kW < nb) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) ss += (double)xv[i][e] * (double)xv[i][e];
@@ -414,21 +460,33 @@ CL_DEVINL void encode_input(const Params& P, const Phase& ph, const Smem& S, int
         for (int w = 0; w < kW; ++w) tot += S.dred[w];
         const float inv = 1.0f / sqrtf((float)(tot / (double)ph.K) + P.eps);
 #pragma unroll
+        for (int i = 0; i < kNormBlocks; ++i) {
+            const int b = warp + i * kW;
+            if (b < nb) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[i][e] = __fmul_rn(xv[i][e], __fmul_rn(inv, gv[i][e]));
+                gmma::encode_block<true, false>(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8, nullptr);
+            }
+        }
+    } else {
+        float xv[kXBlocksPerWarp][8];
+#pragma unroll
         for (int i = 0; i < kXBlocksPerWarp; ++i) {
             const int b = warp + i * kW;
             if (b < nb) {
-                const float4 q0 = *reinterpret_cast<const float4*>(ph.gamma + b * 256 + lane * 8);
-                const float4 q1 = *reinterpret_cast<const float4*>(ph.gamma + b * 256 + lane * 8 + 4);
-                const float gm[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) xv[i][e] = __fmul_rn(xv[i][e], __fmul_rn(inv, gm[e]));
+                const int c0 = b * 256 + lane * 8;
+                const float4 u0 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0));
+                const float4 u1 = __ldcg(reinterpret_cast<const float4*>(ph.x + c0 + 4));
+                xv[i][0] = u0.x; xv[i][1] = u0.y; xv[i][2] = u0.z; xv[i][3] = u0.w;
+                xv[i][4] = u1.x; xv[i][5] = u1.y; xv[i][6] = u1.z; xv[i][7] = u1.w;
             }
         }
-    }
 #pragma unroll
-    for (int i = 0; i < kXBlocksPerWarp; ++i) {
-        const int b = warp + i * kW;
-        if (b < nb) gmma::encode_block<true, false>(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8, nullptr);
+        for (int i = 0; i < kXBlocksPerWarp; ++i) {
+            const int b = warp + i * kW;
+            if (b < nb)
+                gmma::encode_block<true, false>(xv[i], lane, xq + (size_t)b * 1024, xs + b, xsum + b * 8, nullptr);
+        }
     }
     __syncthreads();
 }
@@ -671,8 +729,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     S.region = smem + kRingBytes;
     uint8_t* zero = S.region + P.region_bytes;
     S.zero = zero;
-    S.cph = reinterpret_cast<Phase*>(zero + 1024);
-    S.wph = S.cph + 1;
+    S.cph = reinterpret_cast<Phase*>(zero + 1024);  // [2]: this phase and the next
+    S.wph = S.cph + 2;
     S.dred = reinterpret_cast<double*>(S.wph + kW);
     S.bests = reinterpret_cast<float2*>(S.dred + kW);
     S.flags = reinterpret_cast<int*>(S.bests + kW);
@@ -688,11 +746,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     // ---- the warp's ring: issue iterator (lane-uniform) ----
     uint8_t* ring = S.ring + (size_t)warp * kSlots * kSlotBytes;
     Phase& wph = S.wph[warp];
+    const LanePlan plan = lane_plan(lane);
+    const uint64_t policy = evict_first_policy();
     int ip = -1;
-    long long iu = 0, ie = 0;
+    Cursor ic{0, 0, 0, 0};
     int n_issued = 0;
     auto issue_next = [&]() {
-        while (iu >= ie) {
+        while (ic.left == 0) {
             ++ip;
             if (ip >= nph) {
                 ip = nph;
@@ -701,12 +761,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
             if (ip < 5 * P.n_layers && ip % 5 == 1) continue;  // attention: no weight units
             if (lane == 0) make_phase(P, ip, wph);
             __syncwarp();
-            iu = range_begin(wph.U, gw, GW);
-            ie = range_begin(wph.U, gw + 1, GW);
+            const long long b0 = range_begin(wph.U, gw, GW), e0 = range_begin(wph.U, gw + 1, GW);
+            ic = b0 < e0 ? cursor_at(wph, b0, e0) : Cursor{0, 0, 0, 0};
             __syncwarp();
         }
-        issue_unit(wph, iu, ring + (size_t)(n_issued % kSlots) * kSlotBytes, lane);
-        ++iu;
+        issue_unit(wph, ic, ring + (size_t)(n_issued % kSlots) * kSlotBytes, lane, plan, policy);
+        cursor_next(wph, ic);
     };
     for (int i = 0; i < kSlots; ++i) {
         if (ip < nph) issue_next();
@@ -727,14 +787,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     int n_done = 0;
     __syncthreads();
 
+    long long* trace = P.trace ? P.trace + (size_t)blockIdx.x * nph * 3 : nullptr;
+    if (tid == 0) make_phase(P, 0, S.cph[0]);
     for (int p = 0; p < nph; ++p) {
-        if (tid == 0) make_phase(P, p, *S.cph);
+        if (trace && tid == 0) trace[3 * p] = (long long)global_ns();
         __syncthreads();
-        const Phase& ph = *S.cph;
+        const Phase& ph = S.cph[p & 1];
         if (ph.attn) {
             attention(P, P.layers[p / 5], pos, S);
+            if (trace && tid == 0) trace[3 * p + 1] = (long long)global_ns();
         } else {
             encode_input(P, ph, S, tok, warp, lane);
+            if (trace && tid == 0) trace[3 * p + 1] = (long long)global_ns();
             const uint8_t* xq = S.region;
             const int nb = ph.nb;
             const float* xs = reinterpret_cast<const float*>(S.region + nb * 1024);
@@ -742,36 +806,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
             const long long b = range_begin(ph.U, gw, GW), e = range_begin(ph.U, gw + 1, GW);
             int cur_s = -1, cur_tl = -1;
             float yg = 0.0f, y8 = 0.0f, ym = 0.0f;
-            for (long long u = b; u < e; ++u) {
-                const Unit un = unit_at(ph, u);
-                if (un.s != cur_s || un.tile_l != cur_tl) {
+            Cursor cc = b < e ? cursor_at(ph, b, e) : Cursor{0, 0, 0, 0};
+            for (; cc.left > 0; cursor_next(ph, cc)) {
+                const Cursor un = cc;
+                if (un.s != cur_s || un.tile != cur_tl) {
                     if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best);
                     cur_s = un.s;
-                    cur_tl = un.tile_l;
+                    cur_tl = un.tile;
                     yg = y8 = ym = 0.0f;
                 }
                 cp_wait<kSlots - 1>();
                 __syncwarp();
                 const uint8_t* slot = ring + (size_t)(n_done % kSlots) * kSlotBytes;
-                const uint8_t* bg = slot + g * kRS;
-                const uint8_t* b8 = bg + 8 * kRS;
                 if (ph.seg[un.s].type == CL_TYPE_Q4_K) {
-                    const int sb = un.j;
-                    const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 8 * t : S.zero;
-                    const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 128 + (g - 4) * 32 + 8 * t : S.zero;
-                    uint2 bx0[4], bx1[4];
+                    // super-blocks 2j and 2j + 1: two independent dot chains
+                    const uint8_t* bg = slot + g * kRS4;
+                    const uint8_t* b8 = bg + 8 * kRS4;
 #pragma unroll
-                    for (int gi = 0; gi < 4; ++gi) {
-                        bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
-                        bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
+                    for (int q = 0; q < 2; ++q) {
+                        const int sb = 2 * un.j + q;
+                        if (sb >= nb) break;  // the zero padding of an odd super-block count
+                        const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 8 * t : S.zero;
+                        const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 128 + (g - 4) * 32 + 8 * t : S.zero;
+                        uint2 bx0[4], bx1[4];
+#pragma unroll
+                        for (int gi = 0; gi < 4; ++gi) {
+                            bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
+                            bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
+                        }
+                        const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
+                        gmma::q4k_sb(bg + 144 * q, b8 + 144 * q, bx0, bx1, xsum4, xs[sb], t, L, yg, y8, ym);
                     }
-                    const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
-                    gmma::q4k_sb(bg, b8, bx0, bx1, xsum4, xs[sb], t, L, yg, y8, ym);
                 } else {
-                    const int sb = un.j >> 1, hh = un.j & 1;
+                    const int sb = un.j;
+                    const uint8_t* bg = slot + g * kRS6;
+                    const uint8_t* b8 = bg + 8 * kRS6;
                     const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 4 * t : S.zero;
                     const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 256 + (g - 4) * 32 + 4 * t : S.zero;
-                    q6k_half(bg, b8, p0, p1, hh, sb, xs[sb], t, h, L6, yg, y8);
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh)
+                        q6k_half(bg + 112 * hh, b8 + 112 * hh, p0, p1, hh, sb, xs[sb], t, h, L6, yg, y8);
                 }
                 __syncwarp();
                 ++n_done;
@@ -784,7 +858,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
         if (p + 1 < nph) {
             // ---- grid barrier ----
             __syncthreads();
+            if (trace && tid == 0) trace[3 * p + 2] = (long long)global_ns();
             if (tid == 0) {
+                // the next phase's descriptor needs no activation: built before the wait
+                make_phase(P, p + 1, S.cph[(p + 1) & 1]);
                 __threadfence();
                 atomicAdd(&P.ctl->bar, 1u);
                 const unsigned int target = (unsigned int)(p + 1) * gridDim.x;
@@ -813,6 +890,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
         }
     }
 
+    if (trace && tid == 0) trace[3 * (nph - 1) + 2] = (long long)global_ns();
     // ---- head: the CTAs' candidates, merged by the last CTA ----
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -862,6 +940,53 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     }
 }
 
+// ---- the tiled decode layout -------------------------------------------------
+// Matrix [rows][k] (device layout, cl_repack_rows) -> units stored tile by
+// tile: tile t = rows 16t .. 16t + 15 (with w_up: gate rows 8t .. 8t + 7, then
+// up rows 8t .. 8t + 7), unit j of the tile = 16 rows x (Q4_K: super-blocks
+// 2j and 2j + 1, 2 x 144 B, the second zero when the row has an odd count;
+// Q6_K: super-block j as two 112-byte halves, each ql 64, qh 32, sc 8, f16 d,
+// 6 zero bytes).  One thread per 16-byte piece.
+__global__ void decode_pack_kernel(int type, const uint8_t* __restrict__ w, const uint8_t* __restrict__ w_up,
+                                   long long stride, int rows, int k, uint8_t* __restrict__ out) {
+    grid_wait();
+    const int nb = k / 256;
+    const bool q4 = type == CL_TYPE_Q4_K;
+    const int nsub = q4 ? (nb + 1) / 2 : nb, pieces = q4 ? 18 : 14;
+    const int tiles = w_up ? rows / 8 : rows / 16;
+    const long long total = (long long)tiles * nsub * 16 * pieces;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int pc = (int)(i % pieces);
+        const long long ur = i / pieces;  // (tile, unit, row)
+        const int r = (int)(ur % 16);
+        const long long tu = ur / 16;
+        const int j = (int)(tu % nsub);
+        const int t = (int)(tu / nsub);
+        const uint8_t* row = w_up ? (r < 8 ? w + (long long)(8 * t + r) * stride : w_up + (long long)(8 * t + r - 8) * stride)
+                                  : w + (long long)(16 * t + r) * stride;
+        uint4 v;
+        if (q4) {
+            v = 2 * j + pc / 9 < nb ? *reinterpret_cast<const uint4*>(row + 288LL * j + 16 * pc)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            const int sb = j, hh = pc / 7;
+            pc -= 7 * hh;
+            const uint8_t* blk = row + 208LL * sb;
+            if (pc < 4) {
+                v = *reinterpret_cast<const uint4*>(blk + 64 * hh + 16 * pc);
+            } else if (pc < 6) {
+                v = *reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16 * (pc - 4));
+            } else {
+                const uint2 sc = *reinterpret_cast<const uint2*>(blk + 192 + 8 * hh);
+                const uint8_t* dp = row + 208LL * nb + 2 * sb;
+                v = make_uint4(sc.x, sc.y, (uint32_t)dp[0] | ((uint32_t)dp[1] << 8), 0u);
+            }
+        }
+        reinterpret_cast<uint4*>(out)[i] = v;
+    }
+}
+
 size_t region_bytes(int hidden, int ffn) {
     const int nb = std::max(hidden, ffn) / 256;
     const size_t xq = (size_t)nb * 1024 + (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)nb * 32;
@@ -871,7 +996,7 @@ size_t region_bytes(int hidden, int ffn) {
 }
 
 size_t smem_bytes(int hidden, int ffn) {
-    return kRingBytes + region_bytes(hidden, ffn) + 1024 + (1 + kW) * sizeof(Phase) + kW * sizeof(double) +
+    return kRingBytes + region_bytes(hidden, ffn) + 1024 + (2 + kW) * sizeof(Phase) + kW * sizeof(double) +
            kW * sizeof(float2) + 16;
 }
 
@@ -909,9 +1034,32 @@ using namespace cl::dfz;
 
 extern "C" {
 
+CL_API size_t cl_decode_pack_bytes(int type, int rows, int k, int pair) {
+    if ((type != CL_TYPE_Q4_K && type != CL_TYPE_Q6_K) || rows <= 0 || k <= 0 || k % 256 || rows % (pair ? 8 : 16))
+        return 0;
+    const size_t nsub = type == CL_TYPE_Q4_K ? ((size_t)k / 256 + 1) / 2 : (size_t)k / 256;
+    const size_t tiles = pair ? (size_t)rows / 8 : (size_t)rows / 16;
+    return tiles * nsub * (size_t)unit_bytes(type);
+}
+
+CL_API int cl_decode_pack(int type, const void* w, long long stride, int rows, int k, const void* w_up, void* out,
+                          cudaStream_t stream) {
+    if (cl_decode_pack_bytes(type, rows, k, w_up != nullptr) == 0 || w == nullptr || out == nullptr ||
+        stride < cl_row_stride(type, k))
+        return CL_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(w_up) | reinterpret_cast<uintptr_t>(out)) % 16 ||
+        stride % 16)
+        return CL_ERR_INVALID;
+    return launch_pdl(decode_pack_kernel, dim3(148 * 8), dim3(256), 0, stream, type, static_cast<const uint8_t*>(w),
+                      static_cast<const uint8_t*>(w_up), stride, rows, k, static_cast<uint8_t*>(out)) == cudaSuccess
+               ? CL_OK
+               : CL_ERR_CUDA;
+}
+
 CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_layer* hl) {
     if (m == nullptr || hl == nullptr || m->layers == nullptr || m->n_layers <= 0) return CL_ERR_INVALID;
-    if (m->hidden <= 0 || m->ffn <= 0 || m->hidden % 256 || m->ffn % 256 || m->hidden > kMaxK || m->ffn > kMaxK ||
+    if (m->hidden <= 0 || m->ffn <= 0 || m->hidden % 256 || m->ffn % 256 || m->hidden > kW * kNormBlocks * 256 ||
+        m->ffn > kMaxK ||
         m->head_dim != kD || m->q_heads <= 0 || m->kv_heads <= 0 || m->kv_heads > kMaxKvHeads ||
         m->q_heads % m->kv_heads || m->q_heads / m->kv_heads > kGMax || m->q_heads * kD != m->hidden ||
         m->vocab <= 0 || m->vocab % 16 || m->ffn % 8 || m->capacity <= 0)
@@ -935,12 +1083,12 @@ CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_la
         if (!k_type_ok(L.q_type) || !k_type_ok(L.k_type) || !k_type_ok(L.v_type) || !k_type_ok(L.o_type) ||
             !k_type_ok(L.gate_type) || !k_type_ok(L.down_type))
             return CL_ERR_UNSUPPORTED;
-        if (!L.q || !L.k || !L.v || !L.o || !L.gate || !L.up || !L.down || !L.attn_norm || !L.ffn_norm ||
-            !L.k_cache || !L.v_cache)
+        if (!L.q || !L.k || !L.v || !L.o || !L.gate || !L.down || !L.attn_norm || !L.ffn_norm || !L.k_cache ||
+            !L.v_cache)
             return CL_ERR_INVALID;
         const uintptr_t a = reinterpret_cast<uintptr_t>(L.q) | reinterpret_cast<uintptr_t>(L.k) |
                             reinterpret_cast<uintptr_t>(L.v) | reinterpret_cast<uintptr_t>(L.o) |
-                            reinterpret_cast<uintptr_t>(L.gate) | reinterpret_cast<uintptr_t>(L.up) |
+                            reinterpret_cast<uintptr_t>(L.gate) |
                             reinterpret_cast<uintptr_t>(L.down) | reinterpret_cast<uintptr_t>(L.attn_norm) |
                             reinterpret_cast<uintptr_t>(L.ffn_norm) | reinterpret_cast<uintptr_t>(L.k_cache) |
                             reinterpret_cast<uintptr_t>(L.v_cache);
@@ -1018,6 +1166,7 @@ CL_API int cl_qwen2_decode_step(const cl_qwen2_decode* m, const cl_qwen2_layer* 
     p.records = reinterpret_cast<float2*>(ws + lay.records);
     p.partials = reinterpret_cast<float*>(ws + lay.partials);
     p.attn_part = reinterpret_cast<float*>(ws + lay.attn);
+    p.trace = m->trace;
     p.region_bytes = (int)region_bytes(m->hidden, m->ffn);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);

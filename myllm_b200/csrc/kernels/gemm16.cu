@@ -323,6 +323,7 @@ template <int T>
 __global__ void dequant16_kernel(const uint8_t* __restrict__ w, long long stride, int n, int k, uint16_t* out,
                                  int bf16) {
     grid_launch_dependents();
+    grid_wait();  // `out` may still be read by the previous kernel
     const int nc = k / 32;
     const long long total = (long long)n * nc;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;

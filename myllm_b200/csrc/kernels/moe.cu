@@ -20,6 +20,8 @@
 #include "gemv_common.cuh"
 #include "launch.cuh"
 
+#include <cooperative_groups.h>
+
 namespace cl {
 namespace moe {
 
@@ -349,6 +351,86 @@ __global__ void __launch_bounds__(2 * kMaxGdnDim) gdn_step_kernel(
     }
 }
 
+// The same step with each head's columns split across a thread-block
+// cluster: CTA r of the cluster owns columns 32 r .. 32 r + 31 (the delta
+// rule is independent per column: pred, delta, the state update and o all
+// read one column of S), 8 warps split the rows.  The per-head RMSNorm
+// needs the sum of o^2 over all columns: each CTA leaves its 32-column sum
+// in shared memory and every CTA adds the cluster's sums in rank order
+// through distributed shared memory.  d / 32 CTAs per head (4 at d = 128),
+// so a 32-head layer runs on 128 SMs instead of 32.
+constexpr int kGdnCols = 32, kGdnRowGroups = 8;
+
+__global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_kernel(
+    const float* __restrict__ act, const float* __restrict__ decay, const float* __restrict__ beta,
+    const float* __restrict__ z, const float* __restrict__ gamma, float* __restrict__ state, int key_heads,
+    int value_heads, int d, float eps, float* __restrict__ out) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    grid_launch_dependents();
+    grid_wait();
+    __shared__ float qs[kMaxGdnDim], ks[kMaxGdnDim], part[kGdnRowGroups][kGdnCols];
+    __shared__ float ssq;
+    const int nparts = d / kGdnCols;
+    const int h = blockIdx.x / nparts, cpart = (int)cluster.block_rank(), kh = h % key_heads;
+    const int t = threadIdx.x, cl = t % kGdnCols, rg = t / kGdnCols;
+    const int col = cpart * kGdnCols + cl, rows = d / kGdnRowGroups;
+    for (int i = t; i < d; i += blockDim.x) {
+        qs[i] = act[kh * d + i];
+        ks[i] = act[key_heads * d + kh * d + i];
+    }
+    __syncthreads();
+    float* S = state + (size_t)h * d * d;
+    const float dec = decay[h], bt = beta[h];
+    float s[kMaxGdnDim / kGdnRowGroups];
+    float pred = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
+        if (i < rows) {
+            const int row = rg * rows + i;
+            s[i] = S[(size_t)row * d + col] * dec;
+            pred += s[i] * ks[row];
+        }
+    }
+    part[rg][cl] = pred;
+    __syncthreads();
+    pred = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kGdnRowGroups; ++r) pred += part[r][cl];
+    const float delta = bt * (act[2 * key_heads * d + h * d + col] - pred);
+    const float qscale = rsqrtf((float)d);
+    float o = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
+        if (i < rows) {
+            const int row = rg * rows + i;
+            s[i] += ks[row] * delta;
+            S[(size_t)row * d + col] = s[i];
+            o += s[i] * qs[row] * qscale;
+        }
+    }
+    __syncthreads();
+    part[rg][cl] = o;
+    __syncthreads();
+    o = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kGdnRowGroups; ++r) o += part[r][cl];
+    if (t < kGdnCols) {
+        const float w = warp_sum(o * o);
+        if (t == 0) ssq = w;
+    }
+    cluster.sync();  // every CTA's ssq is written
+    float ss = 0.0f;
+    for (int r = 0; r < nparts; ++r) ss += *cluster.map_shared_rank(&ssq, r);
+    cluster.sync();  // no CTA leaves while another still reads its ssq
+    // per-head RMSNorm (metal_rmsnorm_f32) over the d outputs, then the gate
+    const float inv = rsqrtf(ss / (float)d + eps);
+    if (rg == 0) {
+        const float zz = z[h * d + col];
+        out[h * d + col] = o * inv * gamma[col] * (zz * sigmoid_stable(zz));
+    }
+}
+
 // ---- gated attention: split, per-head norms, partial RoPE, KV append -------
 // Blocks [0, hq): query heads (query and gate halves of the packed head);
 // blocks [hq, hq + hkv): KV heads.  blockDim = head_dim.
@@ -495,6 +577,25 @@ CL_API int cl_gdn_step(const float* act, const float* decay, const float* beta, 
         state == nullptr || out == nullptr || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads ||
         head_dim <= 0 || head_dim % 32 || head_dim > kMaxGdnDim)
         return CL_ERR_INVALID;
+    const int nparts = head_dim / kGdnCols;
+    if (nparts >= 1 && nparts <= 8) {
+        // cluster of nparts CTAs per head (programmatic dependent launch as elsewhere)
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(value_heads * nparts);
+        cfg.blockDim = dim3(kGdnCols * kGdnRowGroups);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = nparts;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = cl::g_pdl_enabled ? 2 : 1;
+        return status(cudaLaunchKernelEx(&cfg, gdn_step_cluster_kernel, act, decay, beta, z, gamma, state, key_heads,
+                                         value_heads, head_dim, eps, out));
+    }
     return status(launch_pdl(gdn_step_kernel, dim3(value_heads), dim3(2 * head_dim), 0, stream, act, decay, beta, z,
                              gamma, state, key_heads, value_heads, head_dim, eps, out));
 }

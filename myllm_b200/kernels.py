@@ -199,10 +199,11 @@ def attn_decode_rope(q, k_new, v_new, cos_sin, pos: int, rot: int, k_cache, v_ca
     return out
 
 
-def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d):
+def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d, tensor_cores: bool = False):
+    """Causal prefill attention: FP32 CUDA cores, or the FP16 tensor-core kernel."""
     out = torch.empty((rows, hq * d), dtype=torch.float32, device=q.device)
-    check(_native.lib().cl_attn_prefill(_p(q), _p(k_cache), _p(v_cache), pos0, rows, hq, hkv, d, _p(out),
-                                        _stream()), "cl_attn_prefill")
+    fn = _native.lib().cl_attn_prefill_tc if tensor_cores else _native.lib().cl_attn_prefill
+    check(fn(_p(q), _p(k_cache), _p(v_cache), pos0, rows, hq, hkv, d, _p(out), _stream()), "cl_attn_prefill")
     return out
 
 

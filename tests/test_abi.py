@@ -169,16 +169,34 @@ def test_fused_decode_description_checks():
                dict(types={"q": sg.Q5_0}), dict(types={"down": sg.Q8_0}), dict(vocab=152064 + 8)):
         _, _, p2, l2 = _fused_desc(**kw)
         assert lib.cl_qwen2_decode_supported(p2, l2) == 2, kw
-    layers[1].up = None
+    layers[1].up = None  # the tiled gate pack holds the up rows: `up` is not read
+    assert lib.cl_qwen2_decode_supported(pm, pl) == 0
+    layers[1].gate = None
     assert lib.cl_qwen2_decode_supported(pm, pl) == 1
-    layers[1].up = (1 << 30) + 8  # misaligned
+    layers[1].gate = (1 << 30) + 8  # misaligned
     assert lib.cl_qwen2_decode_supported(pm, pl) == 1
-    layers[1].up = 1 << 30
+    layers[1].gate = 1 << 30
     assert lib.cl_qwen2_decode_step(pm, pl, None, 1 << 20, None) == 1  # no workspace
     assert lib.cl_qwen2_decode_step(pm, pl, (1 << 30) + 16, 1 << 20, None) == 1  # misaligned workspace
     assert lib.cl_qwen2_decode_status(None) is None
     assert lib.cl_qwen2_decode_status(1 << 30) == (1 << 30) + 8  # after the barrier and done counters
     assert lib.cl_qwen2_decode_init(None, 256, None) == 1
+
+
+def test_decode_pack_sizes():
+    """The tiled decode layout: Q4_K units of 16 x 144 bytes, Q6_K half
+    super-block units of 16 x 112 bytes; shapes off the 16-row (8 for a
+    gate/up pair) or 256-column grid are refused."""
+    lib = _native.lib()
+    assert lib.cl_decode_pack_bytes(sg.Q4_K, 18944, 3584, 0) == 18944 // 16 * 14 * 16 * 144
+    assert lib.cl_decode_pack_bytes(sg.Q4_K, 18944, 3584, 1) == 18944 // 8 * 14 * 16 * 144
+    assert lib.cl_decode_pack_bytes(sg.Q6_K, 152064, 3584, 0) == 152064 // 16 * 28 * 16 * 112
+    assert lib.cl_decode_pack_bytes(sg.Q5_0, 896, 896, 0) == 0
+    assert lib.cl_decode_pack_bytes(sg.Q4_K, 100, 3584, 0) == 0
+    assert lib.cl_decode_pack_bytes(sg.Q4_K, 3584, 1000, 0) == 0
+    assert lib.cl_decode_pack_bytes(sg.Q4_K, 16, 768, 0) == 16 * 4 * 144  # an odd count padded to two units
+    assert lib.cl_decode_pack_bytes(sg.Q6_K, 16, 768, 0) == 16 * 3 * 210 + 16 * 3 * 14
+    assert lib.cl_decode_pack(sg.Q4_K, None, 2016, 16, 3584, None, 1 << 20, None) == 1
 
 
 def test_null_pointers_are_rejected_before_any_launch():
