@@ -292,8 +292,8 @@ typedef struct cl_qwen2_decode {
     const float* rope;            /* [capacity][head_dim / 2][cos, sin] */
     int* ints;                    /* [0] token in, [1] position, [3] token out */
     float *h, *q, *k, *v, *att, *act, *logits; /* [hidden], [q_heads*d], [kv*d] x2, [q_heads*d], [ffn], [vocab] */
-    long long* trace;             /* optional (NULL): [grid][5 n_layers + 1][3] %globaltimer stamps per CTA and
-                                     phase: start, input encoded, work done */
+    long long* trace;             /* optional (NULL): [grid][5 n_layers + 1][16] %globaltimer stamps per CTA
+                                     and phase: start, input ready, work done, then points inside the phase */
 } cl_qwen2_decode;
 
 /* The tiled decode layout of one matrix: its device-layout rows

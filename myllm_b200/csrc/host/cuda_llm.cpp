@@ -522,7 +522,7 @@ struct CudaLLM::Impl {
             int sms = 0;
             CUDALLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
             trace_path = e;
-            trace_mem = DeviceBuffer((std::size_t)sms * (5 * layers.size() + 1) * 3 * sizeof(long long));
+            trace_mem = DeviceBuffer((std::size_t)sms * (5 * layers.size() + 1) * 16 * sizeof(long long));
             CUDALLM_CUDA(cudaMemsetAsync(trace_mem.get(), 0, trace_mem.size(), stream));
             fused_desc.trace = static_cast<long long*>(trace_mem.get());
         }

@@ -70,6 +70,10 @@ constexpr int kKT = 64;                 // keys per attention tile
 constexpr int kQLD = kD + 4;            // padded q / K rows (bank-conflict-free score loop)
 constexpr int kMaxKvHeads = 32;
 constexpr unsigned long long kWaitNs = 2000ull * 1000 * 1000;
+// Optional trace, per CTA and phase: [0] start, [1] input ready, [2] work
+// done, [3 .. 3 + kW) each warp's last unit computed, [11 ..) points inside
+// attention (K/V landed, scores and PV done, partials published, combined).
+constexpr int kTraceSlots = 16;
 
 // Control block at the head of the workspace; zero between steps.
 struct Ctl {
@@ -95,7 +99,11 @@ struct Phase {
     long long U;          // units in the phase
     const float* x;       // input vector; null in layer 0's QKV (the embedding row)
     const float* gamma;   // RMSNorm weight, or null
-    int nseg, nb, K, sw, head, residual, attn, pad;
+    const float* gamma_out;  // the next GEMV's RMSNorm weight over this phase's output, or null
+    int nseg, nb, K, sw, head, residual, attn;
+    int in_buf;           // encoded input buffer (0 / 1), or -1: encode here (layer 0's embedding)
+    int out_buf;          // buffer this phase's output is encoded into, or -1
+    int out_target;       // tile (or head) completions per 256-row output block
 };
 
 struct Params {
@@ -116,8 +124,34 @@ struct Params {
     float* partials;        // [grid * kW][2][16]
     float* attn_part;       // [hkv][kSplitsMax][G][kD + 2]
     long long* trace;       // optional [grid][phases][3] timestamps
+    uint8_t* enc[2];        // encoded vectors: [nb_max] limbs (1 KB) | xs | xsum [8] | ssq (double)
+    unsigned int* enc_cnt;  // [2][nb_max] block completions
+    int nb_max;
     int region_bytes;
 };
+
+// Planes of an encoded-vector buffer of nb_max blocks.
+struct EncView {
+    uint8_t* xq;
+    float* xs;
+    float* xsum;
+    double* ssq;
+};
+
+__host__ __device__ inline size_t enc_bytes(int nb_max) {
+    return (size_t)nb_max * 1024 + (((size_t)nb_max * 4 + 15) & ~(size_t)15) + (size_t)nb_max * 32 +
+           (size_t)nb_max * 8;
+}
+
+CL_DEVINL EncView enc_view(const Params& P, int buf) {
+    uint8_t* b = P.enc[buf];
+    EncView v;
+    v.xq = b;
+    v.xs = reinterpret_cast<float*>(b + (size_t)P.nb_max * 1024);
+    v.xsum = reinterpret_cast<float*>(b + (size_t)P.nb_max * 1024 + (((size_t)P.nb_max * 4 + 15) & ~(size_t)15));
+    v.ssq = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(v.xsum) + (size_t)P.nb_max * 32);
+    return v;
+}
 
 // Bytes of one unit (16 rows) in the tiled decode layout: Q4_K two
 // super-blocks (2 x 144 B per row), Q6_K one super-block as two 112-byte
@@ -145,9 +179,15 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
     int tile = 0;
     ph.x = nullptr;
     ph.gamma = nullptr;
+    ph.gamma_out = nullptr;
     ph.nseg = 1;
     ph.sw = ph.head = ph.residual = ph.attn = 0;
     ph.U = 0;
+    // The encoded input of every GEMV phase but the first was written by the
+    // phase before it (buffers alternate by phase parity).
+    ph.in_buf = p == 0 ? -1 : (p - 1) & 1;
+    ph.out_buf = -1;
+    ph.out_target = 0;
     const int d = kD;
     if (p >= 5 * P.n_layers) {
         ph.nb = P.H / 256;
@@ -171,31 +211,41 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         set_seg(ph.seg[1], L.k, false, L.k_type, P.hkv * d, ph.nb, L.k_bias, P.k, u, tile);
         set_seg(ph.seg[2], L.v, false, L.v_type, P.hkv * d, ph.nb, L.v_bias, P.v, u, tile);
         break;
-    case 1:
+    case 1:  // attention output, encoded per block of two 128-wide heads
         ph.attn = 1;
         ph.nb = 0;
         ph.K = 0;
+        ph.out_buf = p & 1;
+        ph.out_target = 256 / kD;
         break;
-    case 2:
+    case 2:  // o_proj: h, encoded with ffn_norm for gate / up
         ph.nb = P.H / 256;
         ph.K = P.H;
         ph.x = P.att;
         ph.residual = 1;
+        ph.gamma_out = L.ffn_norm;
+        ph.out_buf = p & 1;
+        ph.out_target = 256 / 16;
         set_seg(ph.seg[0], L.o, false, L.o_type, P.H, ph.nb, nullptr, P.h, u, tile);
         break;
-    case 3:
+    case 3:  // gate / up: act, 8-row tiles
         ph.nb = P.H / 256;
         ph.K = P.H;
         ph.x = P.h;
         ph.gamma = L.ffn_norm;
         ph.sw = 1;
+        ph.out_buf = p & 1;
+        ph.out_target = 256 / 8;
         set_seg(ph.seg[0], L.gate, true, L.gate_type, P.F, ph.nb, nullptr, P.act, u, tile);
         break;
-    default:
+    default:  // down: h, encoded with the next layer's attn_norm (or output_norm)
         ph.nb = P.F / 256;
         ph.K = P.F;
         ph.x = P.act;
         ph.residual = 1;
+        ph.gamma_out = p / 5 + 1 < P.n_layers ? P.layers[p / 5 + 1].attn_norm : P.out_norm;
+        ph.out_buf = p & 1;
+        ph.out_target = 256 / 16;
         set_seg(ph.seg[0], L.down, false, L.down_type, P.H, ph.nb, nullptr, P.h, u, tile);
         break;
     }
@@ -358,6 +408,18 @@ CL_DEVINL unsigned long long global_ns() {
     return t;
 }
 
+// One-step publication: the add is a release of this thread's earlier
+// writes (and, through the preceding warp / CTA barrier, of the other
+// threads'), the returned count an acquire of the other adders' writes.
+CL_DEVINL unsigned int atom_add_acq_rel(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+CL_DEVINL void red_add_release(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 CL_DEVINL unsigned int ld_acquire(const unsigned int* p) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -378,7 +440,27 @@ struct Best {
 CL_DEVINL bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
 
 // Rows of a finished tile: lanes with t == 0 hold rows g (vg) and g + 8 (v8).
-CL_DEVINL void tile_out(const Phase& ph, const Seg& sg, int tile_l, int g, float vg, float v8, Best& best) {
+// Bias and residual of the lane's two rows of a tile, loaded when the warp
+// starts the tile so that no load waits at its end.
+struct RowPre {
+    float b[2], r[2];
+};
+
+CL_DEVINL RowPre row_pre(const Phase& ph, const Seg& sg, int tile_l, int g, int t) {
+    RowPre pr{{0.0f, 0.0f}, {0.0f, 0.0f}};
+    if (t == 0 && !ph.sw) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int o = tile_l * 16 + g + 8 * i;
+            if (sg.bias) pr.b[i] = sg.bias[o];
+            if (ph.residual) pr.r[i] = __ldcg(sg.y + o);
+        }
+    }
+    return pr;
+}
+
+CL_DEVINL void tile_out(const Phase& ph, const Seg& sg, int tile_l, int g, float vg, float v8, Best& best,
+                        const RowPre& pr) {
     if (ph.sw) {
         // Branch-stable SiLU(gate) * up (cpu_llm.cpp:188-202), as gemv_mma.cu.
         const int o = tile_l * 8 + g;
@@ -390,8 +472,8 @@ CL_DEVINL void tile_out(const Phase& ph, const Seg& sg, int tile_l, int g, float
     for (int i = 0; i < 2; ++i) {
         const int o = tile_l * 16 + g + 8 * i;
         float y = i ? v8 : vg;
-        if (sg.bias) y += sg.bias[o];
-        if (ph.residual) y = __ldcg(sg.y + o) + y;
+        if (sg.bias) y += pr.b[i];
+        if (ph.residual) y = pr.r[i] + y;
         sg.y[o] = y;
         if (ph.head) best.consider(y, o);
     }
@@ -406,6 +488,7 @@ struct Smem {
     double* dred;  // [kW]
     float2* bests; // [kW]
     int* flags;    // [0] barrier ok, [1] last-of-split / last CTA
+    uint64_t* xbar;  // completion of the encoded-input bulk copies
 };
 
 // ---- encode the phase's input into XQ4 limbs (all warps) -------------------
@@ -491,8 +574,89 @@ CL_DEVINL void encode_input(const Params& P, const Phase& ph, const Smem& S, int
     __syncthreads();
 }
 
+// ---- inputs encoded by the phase that produces them -------------------------
+// Block b (256 elements) of the finished vector y, by one warp, into buffer
+// `buf`: the XQ4 limbs of y (or, for the next RMSNorm, of y * gamma; the
+// consumer multiplies the block scales by 1/rms) and the block's sum of y^2
+// in double.
+CL_DEVINL void encode_out_block(const Params& P, const float* y, const float* gamma, int buf, int b, int lane) {
+    const EncView ev = enc_view(P, buf);
+    const int c0 = b * 256 + lane * 8;
+    const float4 u0 = __ldcg(reinterpret_cast<const float4*>(y + c0));
+    const float4 u1 = __ldcg(reinterpret_cast<const float4*>(y + c0 + 4));
+    float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    if (gamma) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += (double)v[e] * (double)v[e];
+        ss = warp_sum_d(ss);
+        if (lane == 0) ev.ssq[b] = ss;
+        const float4 g0 = *reinterpret_cast<const float4*>(gamma + c0);
+        const float4 g1 = *reinterpret_cast<const float4*>(gamma + c0 + 4);
+        const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], gm[e]);
+    }
+    gmma::encode_block<true, false>(v, lane, ev.xq + (size_t)b * 1024, ev.xs + b, ev.xsum + b * 8, nullptr);
+}
+
+// `add` completions of output block b (full warp, after its rows are
+// written): the completion that finishes the block encodes it.
+CL_DEVINL void block_done(const Params& P, const Phase& ph, const float* y, int b, int add, int lane) {
+    __syncwarp();  // the warp's rows, published by lane 0's release add
+    int last = 0;
+    if (lane == 0) {
+        unsigned int* c = P.enc_cnt + (size_t)ph.out_buf * P.nb_max + b;
+        last = atom_add_acq_rel(c, (unsigned int)add) + (unsigned int)add == (unsigned int)ph.out_target;
+        if (last) *c = 0u;  // re-armed: the buffer's next use is two phases later
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    encode_out_block(P, y, ph.gamma_out, ph.out_buf, b, lane);
+}
+
+// The phase's encoded input into shared memory: the limbs, scales and unit
+// sums by bulk copies completing on the CTA's input barrier; for a
+// normalised input the scales and sums are multiplied by 1/rms, summed from
+// the blocks' sums of squares in block order (the same in every CTA;
+// cpu_llm.cpp:156-165: the mean in double, inv = 1/sqrt(mean + eps) in float).
+CL_DEVINL bool load_input(const Params& P, const Phase& ph, const Smem& S, uint32_t parity) {
+    const int nb = ph.nb, tid = threadIdx.x;
+    const EncView ev = enc_view(P, ph.in_buf);
+    uint8_t* xq = S.region;
+    const int xs_bytes = (nb * 4 + 15) & ~15;
+    float* xs = reinterpret_cast<float*>(S.region + nb * 1024);
+    float* xsum = reinterpret_cast<float*>(S.region + nb * 1024 + xs_bytes);
+    if (tid == 0) {
+        mbar_arrive_expect_tx(S.xbar, (uint32_t)(nb * 1024 + xs_bytes + nb * 32));
+        bulk_g2s(xq, ev.xq, (uint32_t)(nb * 1024), S.xbar);
+        bulk_g2s(xs, ev.xs, (uint32_t)xs_bytes, S.xbar);
+        bulk_g2s(xsum, ev.xsum, (uint32_t)(nb * 32), S.xbar);
+    }
+    float inv = 1.0f;
+    if (ph.gamma) {
+        // every warp: lane b holds block b's sum (nb <= 32), one butterfly:
+        // the same order, hence the same bits, in every warp of every CTA
+        const int lane = tid & 31;
+        double tot = lane < nb ? __ldcg(ev.ssq + lane) : 0.0;
+        tot = warp_sum_d(tot);
+        inv = 1.0f / sqrtf((float)(tot / (double)ph.K) + P.eps);
+    }
+    const bool ok = __syncthreads_and(mbar_wait(S.xbar, parity));
+    if (ok && ph.gamma) {
+        for (int i = tid; i < nb; i += kThreads) xs[i] *= inv;
+        for (int i = tid; i < nb * 8; i += kThreads) xsum[i] *= inv;
+    }
+    __syncthreads();
+    return ok;
+}
+
 // ---- attention of one layer (CTA = KV head x key split) -------------------
-CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, const Smem& S) {
+CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer& L, int pos, const Smem& S,
+                         long long* tr) {
+    auto stamp = [&](int slot) {
+        if (tr && threadIdx.x == 0) tr[slot] = (long long)global_ns();
+    };
     const int G = P.hq / P.hkv, kvd = P.hkv * kD, len = pos + 1, tid = threadIdx.x;
     int ns = min(kSplitsMax, max(1, (len + kKT - 1) / kKT));
     ns = max(1, min(ns, (int)gridDim.x / P.hkv));
@@ -506,14 +670,53 @@ CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, cons
     float* ps = vs + kKT * kD;                       // [G][kKT]
     float* run = ps + kGMax * kKT;                   // [G][2]
     float* fac = run + 2 * kGMax;                    // [G]
-    const float* cs = P.rope + (size_t)pos * kD;     // [d/2][cos, sin]
+    float* csm = fac + kGMax;                        // [d/2][cos, sin] of the position
+    const float* cs = P.rope + (size_t)pos * kD;
     const int half = kD / 2;
-
-    for (int i = tid; i < G * (kD / 4); i += kThreads) {
-        const int hh = i / (kD / 4), c = i - hh * (kD / 4);
-        *reinterpret_cast<float4*>(qs + hh * kQLD + 4 * c) =
-            __ldcg(reinterpret_cast<const float4*>(P.q + (size_t)(g * G + hh) * kD + 4 * c));
+    auto load_tile = [&](int t0) {
+        const int nk = min(kKT, nk_all - t0);
+        const size_t base = (size_t)(k0 + t0) * kvd + (size_t)g * kD;
+        for (int i = tid; i < nk * (kD / 4); i += kThreads) {
+            const int r = i / (kD / 4), c = i - r * (kD / 4);
+            cp16(ks + r * kQLD + 4 * c, L.k_cache + base + (size_t)r * kvd + 4 * c);
+            cp16(vs + r * kD + 4 * c, L.v_cache + base + (size_t)r * kvd + 4 * c);
+        }
+        cp_commit();
+    };
+    // Every independent load in flight at once: the first key tile, the
+    // query heads, the position's rotation row and, in the split holding
+    // the position, the new key and value.
+    if (nk_all > 0) load_tile(0);
+    constexpr int kQv = (kGMax * kD / 4 + kThreads - 1) / kThreads;
+    float4 qv[kQv];
+#pragma unroll
+    for (int j = 0; j < kQv; ++j) {
+        const int i = tid + j * kThreads;
+        if (i < G * (kD / 4)) {
+            const int hh = i / (kD / 4), c = i - hh * (kD / 4);
+            qv[j] = __ldcg(reinterpret_cast<const float4*>(P.q + (size_t)(g * G + hh) * kD + 4 * c));
+        }
     }
+    const float4 csv = tid < kD / 4 ? *reinterpret_cast<const float4*>(cs + 4 * tid) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int rpos = pos - k0;  // the new key's row in this split, if 0 <= rpos < nk_all
+    const bool holds = rpos >= 0 && rpos < nk_all;
+    float ka = 0.0f, kb = 0.0f, vn = 0.0f;
+    if (holds) {
+        if (tid < half) {
+            ka = __ldcg(P.k + (size_t)g * kD + tid);
+            kb = __ldcg(P.k + (size_t)g * kD + tid + half);
+        }
+        if (tid < kD) vn = __ldcg(P.v + (size_t)g * kD + tid);
+    }
+#pragma unroll
+    for (int j = 0; j < kQv; ++j) {
+        const int i = tid + j * kThreads;
+        if (i < G * (kD / 4)) {
+            const int hh = i / (kD / 4), c = i - hh * (kD / 4);
+            *reinterpret_cast<float4*>(qs + hh * kQLD + 4 * c) = qv[j];
+        }
+    }
+    if (tid < kD / 4) *reinterpret_cast<float4*>(csm + 4 * tid) = csv;
     if (tid < G) {
         run[2 * tid] = -INFINITY;
         run[2 * tid + 1] = 0.0f;
@@ -523,47 +726,38 @@ CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, cons
     for (int i = tid; i < G * half; i += kThreads) {
         const int hh = i / half, pp = i - hh * half;
         float* qh = qs + hh * kQLD;
-        const float c = cs[2 * pp], sn = cs[2 * pp + 1];
+        const float c = csm[2 * pp], sn = csm[2 * pp + 1];
         const float a = qh[pp], b = qh[pp + half];
         qh[pp] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
         qh[pp + half] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
     }
-    const int dim = tid & (kD - 1), pt = tid / kD;  // 4 parts of the PV sums
+    const int dim = tid & (kD - 1), pt = tid / kD;  // parts of the PV sums
     float acc[kGMax];
 #pragma unroll
     for (int hh = 0; hh < kGMax; ++hh) acc[hh] = 0.0f;
     for (int t0 = 0; t0 < nk_all; t0 += kKT) {
         const int nk = min(kKT, nk_all - t0);
-        const size_t base = (size_t)(k0 + t0) * kvd + (size_t)g * kD;
-        for (int i = tid; i < nk * (kD / 4); i += kThreads) {
-            const int r = i / (kD / 4), c = i - r * (kD / 4);
-            cp16(ks + r * kQLD + 4 * c, L.k_cache + base + (size_t)r * kvd + 4 * c);
-            cp16(vs + r * kD + 4 * c, L.v_cache + base + (size_t)r * kvd + 4 * c);
-        }
-        cp_commit();
+        if (t0 > 0) load_tile(t0);
         cp_wait<0>();
         __syncthreads();
-        const int r = pos - (k0 + t0);
-        if (r >= 0 && r < nk) {
+        if (t0 == 0) stamp(11);
+        const int r = rpos - t0;
+        if (holds && r >= 0 && r < nk) {
             // the current position: rotate the new key, append K and V, use them here
-            const float* kn = P.k + (size_t)g * kD;
-            const float* vn = P.v + (size_t)g * kD;
             float* kw = L.k_cache + (size_t)pos * kvd + (size_t)g * kD;
             float* vw = L.v_cache + (size_t)pos * kvd + (size_t)g * kD;
-            for (int pp = tid; pp < half; pp += kThreads) {
-                const float c = cs[2 * pp], sn = cs[2 * pp + 1];
-                const float a = __ldcg(kn + pp), b = __ldcg(kn + pp + half);
-                const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
-                const float rb = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
-                kw[pp] = ra;
-                kw[pp + half] = rb;
-                ks[r * kQLD + pp] = ra;
-                ks[r * kQLD + pp + half] = rb;
+            if (tid < half) {
+                const float c = csm[2 * tid], sn = csm[2 * tid + 1];
+                const float ra = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, sn));
+                const float rb = __fadd_rn(__fmul_rn(ka, sn), __fmul_rn(kb, c));
+                kw[tid] = ra;
+                kw[tid + half] = rb;
+                ks[r * kQLD + tid] = ra;
+                ks[r * kQLD + tid + half] = rb;
             }
-            for (int c = tid; c < kD; c += kThreads) {
-                const float vv = __ldcg(vn + c);
-                vw[c] = vv;
-                vs[r * kD + c] = vv;
+            if (tid < kD) {
+                vw[tid] = vn;
+                vs[r * kD + tid] = vn;
             }
         }
         __syncthreads();
@@ -616,6 +810,7 @@ CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, cons
         }
         __syncthreads();  // tile buffers are refilled next
     }
+    stamp(12);
     // this split's (m, l, o) per head; the K tile buffer holds the PV parts
     float* pv = ks;
     if (pt > 0) {
@@ -648,6 +843,7 @@ CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, cons
         S.flags[1] = old == (unsigned int)(ns - 1);
     }
     __syncthreads();
+    stamp(13);
     if (!S.flags[1]) return;
     __threadfence();
     // merge the splits (attn_decode_combine's weights: exp(m_s - m) / l)
@@ -672,11 +868,41 @@ CL_DEVINL void attention(const Params& P, const cl_qwen2_layer& L, int pos, cons
         P.att[(size_t)(g * G + hh) * kD + dd] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
     }
     if (tid == 0) P.ctl->attn_ticket[g] = 0u;
+    stamp(14);
+    // the o_proj input blocks this KV head's query heads complete (two
+    // 128-wide heads per block)
+    __syncthreads();
+    if (aph.out_buf >= 0) {
+        const int h0 = g * G, h1 = h0 + G;
+        const int b = h0 / 2 + (tid >> 5);  // warp i: the i-th block these heads touch
+        if (b <= (h1 - 1) / 2) block_done(P, aph, P.att, b, min(h1, 2 * b + 2) - max(h0, 2 * b), tid & 31);
+    }
+}
+
+// Tile completions of output blocks a warp has not yet counted: its tiles
+// are consecutive, so it counts them per block and adds them to the block's
+// counter when it moves to another block or ends its range (one atomic per
+// block touched instead of one per tile).
+struct Pending {
+    int block, count;
+};
+
+CL_DEVINL void pending_flush(const Params& P, const Phase& ph, const float* y, Pending& pd, int lane) {
+    if (pd.count > 0) block_done(P, ph, y, pd.block, pd.count, lane);
+    pd.count = 0;
+}
+
+CL_DEVINL void pending_add(const Params& P, const Phase& ph, const float* y, int block, Pending& pd, int lane) {
+    if (ph.out_buf < 0) return;
+    if (pd.count > 0 && pd.block != block) pending_flush(P, ph, y, pd, lane);
+    pd.block = block;
+    ++pd.count;
 }
 
 // A finished tile's rows, direct or through the partial buffer.
 CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, long long b, long long e, int gw,
-                          int GW, float yg, float y8, float ym, int lane, Best& best) {
+                          int GW, float yg, float y8, float ym, int lane, Best& best, Pending& pd,
+                          const RowPre& pre) {
     const int g = lane >> 2, t = lane & 3;
     if (t & 1) y8 += ym;
     else yg += ym;
@@ -686,8 +912,10 @@ CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, l
     y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
     const Seg& sg = ph.seg[s];
     const long long uf = sg.u0 + (long long)tile_l * sg.nsub, ul = uf + sg.nsub - 1;
+    const int out_block = (tile_l * (sg.sw ? 8 : 16)) / 256;
     if (uf >= b && ul < e) {
-        if (t == 0) tile_out(ph, sg, tile_l, g, yg, y8, best);
+        if (t == 0) tile_out(ph, sg, tile_l, g, yg, y8, best, pre);
+        pending_add(P, ph, sg.y, out_block, pd, lane);
         return;
     }
     float* mine = P.partials + ((size_t)gw * 2 + (b >= uf ? 0 : 1)) * 16;
@@ -696,30 +924,50 @@ CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, l
         __stcg(mine + 8 + g, y8);
     }
     __syncwarp();
+    // The warps covering the tile, in order.  With at least one unit per
+    // warp (U >= GW) they are wf .. wl, each with a non-empty range; the
+    // first one's partial is in its slot 1 unless its range starts exactly
+    // at the tile, every later one's in slot 0.  With fewer units than warps
+    // every warp holds at most one unit: the tile's units lie in distinct
+    // warps, each partial in slot 0.
+    const bool sparse = ph.U < GW;
     const int wf = warp_of(ph.U, uf, GW), wl = warp_of(ph.U, ul, GW);
+    const int count = sparse ? sg.nsub : wl - wf + 1;
     int last = 0;
     if (lane == 0) {
-        int count = 0;
-        for (int k = wf; k <= wl; ++k) count += range_begin(ph.U, k + 1, GW) > range_begin(ph.U, k, GW);
-        __threadfence();
-        const unsigned int old = atomicAdd(&P.tickets[sg.tile0 + tile_l], 1u);
+        const unsigned int old = atom_add_acq_rel(&P.tickets[sg.tile0 + tile_l], 1u);
         last = old == (unsigned int)(count - 1);
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) return;
-    __threadfence();
     if (t == 0) {
         float vg = 0.0f, v8 = 0.0f;
-        for (int k = wf; k <= wl; ++k) {
-            const long long bk = range_begin(ph.U, k, GW);
-            if (range_begin(ph.U, k + 1, GW) == bk) continue;  // a warp without units
-            const float* pk = P.partials + ((size_t)k * 2 + (bk >= uf ? 0 : 1)) * 16;
-            vg += __ldcg(pk + g);
-            v8 += __ldcg(pk + 8 + g);
+        const int first_slot = (!sparse && range_begin(ph.U, wf, GW) < uf) ? 1 : 0;
+        // 16 partials in flight at a time, added in warp order
+        for (int i0 = 0; i0 < count; i0 += 16) {
+            float pg[16], p8[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                pg[i] = p8[i] = 0.0f;
+                if (i0 + i < count) {
+                    const int k = sparse ? warp_of(ph.U, uf + i0 + i, GW) : wf + i0 + i;
+                    const float* pk = P.partials + ((size_t)k * 2 + (i0 + i == 0 ? first_slot : 0)) * 16;
+                    pg[i] = __ldcg(pk + g);
+                    p8[i] = __ldcg(pk + 8 + g);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i0 + i < count) {
+                    vg += pg[i];
+                    v8 += p8[i];
+                }
+            }
         }
-        tile_out(ph, sg, tile_l, g, vg, v8, best);
+        tile_out(ph, sg, tile_l, g, vg, v8, best, pre);
     }
     if (lane == 0) P.tickets[sg.tile0 + tile_l] = 0u;
+    pending_add(P, ph, sg.y, out_block, pd, lane);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_constant__ Params P) {
@@ -734,11 +982,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     S.dred = reinterpret_cast<double*>(S.wph + kW);
     S.bests = reinterpret_cast<float2*>(S.dred + kW);
     S.flags = reinterpret_cast<int*>(S.bests + kW);
+    S.xbar = reinterpret_cast<uint64_t*>(S.flags + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3, h = t >> 1;
     const int GW = gridDim.x * kW, gw = blockIdx.x * kW + warp;
     if (tid < 64) reinterpret_cast<uint4*>(zero)[tid] = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) {
+        mbar_init(S.xbar, 1);
+        mbar_fence_init();
+    }
+    uint32_t xloads = 0;  // uses of the input barrier (its phase parity)
     const int tok = __ldcg(P.ints);
     const int pos = __ldcg(P.ints + 1);
     const int nph = 5 * P.n_layers + 1;
@@ -787,32 +1041,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     int n_done = 0;
     __syncthreads();
 
-    long long* trace = P.trace ? P.trace + (size_t)blockIdx.x * nph * 3 : nullptr;
+    long long* trace = P.trace ? P.trace + (size_t)blockIdx.x * nph * kTraceSlots : nullptr;
     if (tid == 0) make_phase(P, 0, S.cph[0]);
     for (int p = 0; p < nph; ++p) {
-        if (trace && tid == 0) trace[3 * p] = (long long)global_ns();
+        if (trace && tid == 0) trace[kTraceSlots * p] = (long long)global_ns();
         __syncthreads();
         const Phase& ph = S.cph[p & 1];
         if (ph.attn) {
-            attention(P, P.layers[p / 5], pos, S);
-            if (trace && tid == 0) trace[3 * p + 1] = (long long)global_ns();
+            attention(P, ph, P.layers[p / 5], pos, S, trace ? trace + kTraceSlots * p : nullptr);
+            if (trace && tid == 0) trace[kTraceSlots * p + 1] = (long long)global_ns();
         } else {
-            encode_input(P, ph, S, tok, warp, lane);
-            if (trace && tid == 0) trace[3 * p + 1] = (long long)global_ns();
+            if (ph.in_buf >= 0) {
+                if (!load_input(P, ph, S, xloads++ & 1u)) {
+                    if (tid == 0) {
+                        atomicCAS(&P.ctl->error, 0, p + 1);
+                        atomicExch(&P.ctl->abort, 1);
+                    }
+                    cp_wait_all();
+                    return;
+                }
+            } else {
+                encode_input(P, ph, S, tok, warp, lane);
+            }
+            if (trace && tid == 0) trace[kTraceSlots * p + 1] = (long long)global_ns();
             const uint8_t* xq = S.region;
             const int nb = ph.nb;
             const float* xs = reinterpret_cast<const float*>(S.region + nb * 1024);
             const float* xsum = reinterpret_cast<const float*>(S.region + nb * 1024 + ((nb * 4 + 15) & ~15));
             const long long b = range_begin(ph.U, gw, GW), e = range_begin(ph.U, gw + 1, GW);
             int cur_s = -1, cur_tl = -1;
+            Pending pend{0, 0};
+            RowPre pre{{0.0f, 0.0f}, {0.0f, 0.0f}};
             float yg = 0.0f, y8 = 0.0f, ym = 0.0f;
             Cursor cc = b < e ? cursor_at(ph, b, e) : Cursor{0, 0, 0, 0};
             for (; cc.left > 0; cursor_next(ph, cc)) {
                 const Cursor un = cc;
                 if (un.s != cur_s || un.tile != cur_tl) {
-                    if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best);
+                    if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best, pend, pre);
                     cur_s = un.s;
                     cur_tl = un.tile;
+                    pre = row_pre(ph, ph.seg[cur_s], cur_tl, g, t);
                     yg = y8 = ym = 0.0f;
                 }
                 cp_wait<kSlots - 1>();
@@ -824,18 +1092,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
                     const uint8_t* b8 = bg + 8 * kRS4;
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
+                        // the zero super-block padding an odd count: all its bytes
+                        // (d, dmin included) are zero, read against zeros
                         const int sb = 2 * un.j + q;
-                        if (sb >= nb) break;  // the zero padding of an odd super-block count
-                        const uint8_t* p0 = g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 8 * t : S.zero;
-                        const uint8_t* p1 = g >= 4 ? xq + (size_t)sb * 1024 + 128 + (g - 4) * 32 + 8 * t : S.zero;
+                        const bool live = sb < nb;
+                        const uint8_t* p0 = live && g < 4 ? xq + (size_t)sb * 1024 + g * 32 + 8 * t : S.zero;
+                        const uint8_t* p1 = live && g >= 4 ? xq + (size_t)sb * 1024 + 128 + (g - 4) * 32 + 8 * t
+                                                           : S.zero;
                         uint2 bx0[4], bx1[4];
 #pragma unroll
                         for (int gi = 0; gi < 4; ++gi) {
                             bx0[gi] = *reinterpret_cast<const uint2*>(p0 + 256 * gi);
                             bx1[gi] = *reinterpret_cast<const uint2*>(p1 + 256 * gi);
                         }
-                        const float4 xsum4 = *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4);
-                        gmma::q4k_sb(bg + 144 * q, b8 + 144 * q, bx0, bx1, xsum4, xs[sb], t, L, yg, y8, ym);
+                        const float4 xsum4 = live ? *reinterpret_cast<const float4*>(xsum + sb * 8 + h * 4)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                        gmma::q4k_sb(bg + 144 * q, b8 + 144 * q, bx0, bx1, xsum4, live ? xs[sb] : 0.0f, t, L, yg,
+                                     y8, ym);
                     }
                 } else {
                     const int sb = un.j;
@@ -853,17 +1126,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
                 cp_commit();
                 ++n_issued;
             }
-            if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best);
+            if (trace && lane == 0) trace[kTraceSlots * p + 3 + warp] = (long long)global_ns();
+            if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best, pend, pre);
+            pending_flush(P, ph, ph.seg[0].y, pend, lane);
         }
         if (p + 1 < nph) {
             // ---- grid barrier ----
             __syncthreads();
-            if (trace && tid == 0) trace[3 * p + 2] = (long long)global_ns();
+            if (trace && tid == 0) trace[kTraceSlots * p + 2] = (long long)global_ns();
             if (tid == 0) {
-                // the next phase's descriptor needs no activation: built before the wait
+                red_add_release(&P.ctl->bar, 1u);
+                // the next phase's descriptor needs no activation: built while the grid arrives
                 make_phase(P, p + 1, S.cph[(p + 1) & 1]);
-                __threadfence();
-                atomicAdd(&P.ctl->bar, 1u);
                 const unsigned int target = (unsigned int)(p + 1) * gridDim.x;
                 const unsigned long long t0 = global_ns();
                 int ok = 1;
@@ -879,7 +1153,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
                         break;
                     }
                 }
-                __threadfence();
                 S.flags[0] = ok;
             }
             __syncthreads();
@@ -890,7 +1163,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
         }
     }
 
-    if (trace && tid == 0) trace[3 * (nph - 1) + 2] = (long long)global_ns();
+    if (trace && tid == 0) trace[kTraceSlots * (nph - 1) + 2] = (long long)global_ns();
     // ---- head: the CTAs' candidates, merged by the last CTA ----
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -991,13 +1264,13 @@ size_t region_bytes(int hidden, int ffn) {
     const int nb = std::max(hidden, ffn) / 256;
     const size_t xq = (size_t)nb * 1024 + (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)nb * 32;
     const size_t attn = sizeof(float) * ((size_t)kGMax * kQLD + (size_t)kKT * kQLD + (size_t)kKT * kD +
-                                         (size_t)kGMax * kKT + 3 * kGMax);
+                                         (size_t)kGMax * kKT + 3 * kGMax + kD);
     return (std::max(xq, attn) + 127) & ~(size_t)127;
 }
 
 size_t smem_bytes(int hidden, int ffn) {
     return kRingBytes + region_bytes(hidden, ffn) + 1024 + (2 + kW) * sizeof(Phase) + kW * sizeof(double) +
-           kW * sizeof(float2) + 16;
+           kW * sizeof(float2) + 16 + 16;
 }
 
 int max_tiles(const cl_qwen2_decode* m) {
@@ -1006,7 +1279,7 @@ int max_tiles(const cl_qwen2_decode* m) {
 }
 
 struct Layout {
-    size_t tickets, records, partials, attn, total;
+    size_t tickets, records, partials, attn, enc0, enc1, enc_cnt, total;
 };
 
 Layout layout(const cl_qwen2_decode* m, int grid) {
@@ -1020,6 +1293,14 @@ Layout layout(const cl_qwen2_decode* m, int grid) {
     off += (size_t)grid * kW * 2 * 16 * 4;
     l.attn = off;
     off += (size_t)m->kv_heads * kSplitsMax * (m->q_heads / m->kv_heads) * (kD + 2) * 4;
+    const int nbm = std::max(m->hidden, m->ffn) / 256;
+    off = (off + 255) & ~(size_t)255;
+    l.enc0 = off;
+    off += (enc_bytes(nbm) + 255) & ~(size_t)255;
+    l.enc1 = off;
+    off += (enc_bytes(nbm) + 255) & ~(size_t)255;
+    l.enc_cnt = off;
+    off += (size_t)2 * nbm * 4;
     l.total = (off + 255) & ~(size_t)255;
     return l;
 }
@@ -1167,6 +1448,10 @@ CL_API int cl_qwen2_decode_step(const cl_qwen2_decode* m, const cl_qwen2_layer* 
     p.partials = reinterpret_cast<float*>(ws + lay.partials);
     p.attn_part = reinterpret_cast<float*>(ws + lay.attn);
     p.trace = m->trace;
+    p.enc[0] = reinterpret_cast<uint8_t*>(ws + lay.enc0);
+    p.enc[1] = reinterpret_cast<uint8_t*>(ws + lay.enc1);
+    p.enc_cnt = reinterpret_cast<unsigned int*>(ws + lay.enc_cnt);
+    p.nb_max = std::max(m->hidden, m->ffn) / 256;
     p.region_bytes = (int)region_bytes(m->hidden, m->ffn);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
