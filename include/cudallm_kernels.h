@@ -293,7 +293,11 @@ typedef struct cl_qwen2_decode {
     int* ints;                    /* [0] token in, [1] position, [3] token out */
     float *h, *q, *k, *v, *att, *act, *logits; /* [hidden], [q_heads*d], [kv*d] x2, [q_heads*d], [ffn], [vocab] */
     long long* trace;             /* optional (NULL): [grid][5 n_layers + 1][16] %globaltimer stamps per CTA
-                                     and phase: start, input ready, work done, then points inside the phase */
+                                     and phase: start, input ready, work done, then points inside the phase
+                                     (projection phases: warp 0's cycles waiting, computing, issuing,
+                                     flushing, and its unit count) */
+    int attn_splits;              /* key splits per KV head in attention, 0..32; 0 = automatic (one per 16
+                                     keys, at most 32 and at most SMs / kv_heads) */
 } cl_qwen2_decode;
 
 /* The tiled decode layout of one matrix: its device-layout rows

@@ -139,7 +139,8 @@ class Qwen2Decode(ctypes.Structure):
                                       "capacity")] +
                 [("eps", c_float), ("scale", c_float), ("embd", c_vp), ("embd_stride", c_ll), ("embd_type", c_int),
                  ("out_type", c_int), ("out_w", c_vp), ("out_norm", c_vp), ("rope", c_vp), ("ints", c_vp)] +
-                [(n, c_vp) for n in ("h", "q", "k", "v", "att", "act", "logits", "trace")])
+                [(n, c_vp) for n in ("h", "q", "k", "v", "att", "act", "logits", "trace")] +
+                [("attn_splits", c_int)])
 
 
 def lib():

@@ -518,6 +518,11 @@ struct CudaLLM::Impl {
             }
             CUDALLM_CL(cl_qwen2_decode_supported(&fused_desc, fused_layers.data()));
         }
+        if (const char* e = std::getenv("CUDALLM_DECODE_SPLITS")) {
+            // attention key splits per KV head (tests use few, to cover multi-tile splits)
+            fused_desc.attn_splits = std::atoi(e);
+            CUDALLM_CL(cl_qwen2_decode_supported(&fused_desc, fused_layers.data()));
+        }
         if (const char* e = std::getenv("CUDALLM_DECODE_TRACE")) {
             int sms = 0;
             CUDALLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));

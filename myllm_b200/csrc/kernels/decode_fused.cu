@@ -63,16 +63,22 @@ constexpr int kRingBytes = kW * kSlots * kSlotBytes;
 constexpr int kXBlocksPerWarp = 10;     // x blocks one warp encodes: k <= 8 * 10 * 256
 constexpr int kMaxK = kW * kXBlocksPerWarp * 256;
 constexpr int kNormBlocks = 3;          // RMS-normalised inputs: k <= 8 * 3 * 256
-constexpr int kSplitsMax = 16;          // key splits per KV head
+constexpr int kSplitsMax = 32;          // key splits per KV head (one warp merges their weights)
+constexpr int kSplitKeys = 16;          // automatic splits: at least this many keys each
 constexpr int kGMax = 8;                // query heads per KV head
 constexpr int kD = 128;                 // head dim
 constexpr int kKT = 64;                 // keys per attention tile
 constexpr int kQLD = kD + 4;            // padded q / K rows (bank-conflict-free score loop)
+constexpr int kRec = kD + 4;            // a split's record per query head: m, l, 2 pad, o[kD]
+constexpr int kRedUnits = 64;           // tile mode: a CTA's units (16 partial rows each in shared memory)
 constexpr int kMaxKvHeads = 32;
 constexpr unsigned long long kWaitNs = 2000ull * 1000 * 1000;
 // Optional trace, per CTA and phase: [0] start, [1] input ready, [2] work
-// done, [3 .. 3 + kW) each warp's last unit computed, [11 ..) points inside
-// attention (K/V landed, scores and PV done, partials published, combined).
+// done, [3 .. 3 + kW) each warp's last unit computed; in attention phases
+// [11 .. 15) points inside attention (K/V landed, scores and PV done,
+// partials published, combined); in projection phases [11 .. 15) warp 0's
+// SM cycles waiting for its ring, computing, issuing loads and flushing
+// tiles in its unit loop, and [15] its unit count.
 constexpr int kTraceSlots = 16;
 
 // Control block at the head of the workspace; zero between steps.
@@ -101,6 +107,9 @@ struct Phase {
     const float* gamma;   // RMSNorm weight, or null
     const float* gamma_out;  // the next GEMV's RMSNorm weight over this phase's output, or null
     int nseg, nb, K, sw, head, residual, attn;
+    int ctile;            // whole tiles per CTA (tile c, c + grid, ...; the CTA's warps take its
+                          // units in turn and add them up in shared memory), else warp ranges
+    int ntiles;
     int in_buf;           // encoded input buffer (0 / 1), or -1: encode here (layer 0's embedding)
     int out_buf;          // buffer this phase's output is encoded into, or -1
     int out_target;       // tile (or head) completions per 256-row output block
@@ -122,12 +131,15 @@ struct Params {
     unsigned int* tickets;  // [max_tiles]
     float2* records;        // [grid] head candidates (value, index as float bits)
     float* partials;        // [grid * kW][2][16]
-    float* attn_part;       // [hkv][kSplitsMax][G][kD + 2]
+    float* attn_part;       // [hkv][kSplitsMax][G][kRec]
     long long* trace;       // optional [grid][phases][3] timestamps
     uint8_t* enc[2];        // encoded vectors: [nb_max] limbs (1 KB) | xs | xsum [8] | ssq (double)
     unsigned int* enc_cnt;  // [2][nb_max] block completions
     int nb_max;
     int region_bytes;
+    int attn_off;           // attention's part of the region: after the QKV input, so that the
+                            // first key tile can land while the QKV phase still reads its input
+    int splits;             // key splits per KV head requested (0: automatic)
 };
 
 // Planes of an encoded-vector buffer of nb_max blocks.
@@ -181,7 +193,7 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
     ph.gamma = nullptr;
     ph.gamma_out = nullptr;
     ph.nseg = 1;
-    ph.sw = ph.head = ph.residual = ph.attn = 0;
+    ph.sw = ph.head = ph.residual = ph.attn = ph.ctile = 0;
     ph.U = 0;
     // The encoded input of every GEMV phase but the first was written by the
     // phase before it (buffers alternate by phase parity).
@@ -210,6 +222,7 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         set_seg(ph.seg[0], L.q, false, L.q_type, P.hq * d, ph.nb, L.q_bias, P.q, u, tile);
         set_seg(ph.seg[1], L.k, false, L.k_type, P.hkv * d, ph.nb, L.k_bias, P.k, u, tile);
         set_seg(ph.seg[2], L.v, false, L.v_type, P.hkv * d, ph.nb, L.v_bias, P.v, u, tile);
+        ph.ctile = 1;
         break;
     case 1:  // attention output, encoded per block of two 128-wide heads
         ph.attn = 1;
@@ -227,6 +240,7 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         ph.out_buf = p & 1;
         ph.out_target = 256 / 16;
         set_seg(ph.seg[0], L.o, false, L.o_type, P.H, ph.nb, nullptr, P.h, u, tile);
+        ph.ctile = 1;
         break;
     case 3:  // gate / up: act, 8-row tiles
         ph.nb = P.H / 256;
@@ -250,6 +264,14 @@ CL_DEVINL void make_phase(const Params& P, int p, Phase& ph) {
         break;
     }
     ph.U = u;
+    ph.ntiles = tile;
+    if (ph.ctile) {
+        // tile mode while a CTA's units fit the shared partial sums
+        int nsub_max = 0;
+        for (int i = 0; i < ph.nseg; ++i) nsub_max = max(nsub_max, ph.seg[i].nsub);
+        const int per_cta = (tile + (int)gridDim.x - 1) / (int)gridDim.x;
+        ph.ctile = per_cta * nsub_max <= kRedUnits;
+    }
 }
 
 // A warp's position in its range of a phase: unit j of tile `tile` of
@@ -275,6 +297,46 @@ CL_DEVINL void cursor_next(const Phase& ph, Cursor& c) {
             c.tile = 0;
             ++c.s;
         }
+    }
+}
+
+// Tile mode: global tile index -> (segment, tile in segment); false past the end.
+CL_DEVINL bool tile_locate(const Phase& ph, int tg, int& s, int& tile) {
+    if (tg >= ph.ntiles) return false;
+    s = 0;
+    if (ph.nseg > 1 && tg >= ph.seg[1].tile0) s = 1;
+    if (ph.nseg > 2 && tg >= ph.seg[2].tile0) s = 2;
+    tile = tg - ph.seg[s].tile0;
+    return true;
+}
+
+// Tile mode: the CTA's units in order (its tiles c, c + grid, ..., each
+// tile's units in turn), position `pos` onward in steps of kW; `left` the
+// positions of this warp still to go.
+CL_DEVINL Cursor cursor_ctile(const Phase& ph, int pos) {
+    int s = 0, tile = 0, total = 0;
+    for (int tg = blockIdx.x; tile_locate(ph, tg, s, tile); tg += gridDim.x) total += ph.seg[s].nsub;
+    Cursor c{0, 0, 0, pos < total ? (total - pos + kW - 1) / kW : 0};
+    if (c.left == 0) return c;
+    int tg = blockIdx.x;
+    tile_locate(ph, tg, c.s, c.tile);
+    c.j = pos;
+    while (c.j >= ph.seg[c.s].nsub) {
+        c.j -= ph.seg[c.s].nsub;
+        tg += gridDim.x;
+        tile_locate(ph, tg, c.s, c.tile);
+    }
+    return c;
+}
+
+CL_DEVINL void cursor_ctile_next(const Phase& ph, Cursor& c) {
+    if (--c.left == 0) return;
+    c.j += kW;
+    int tg = ph.seg[c.s].tile0 + c.tile;
+    while (c.j >= ph.seg[c.s].nsub) {
+        c.j -= ph.seg[c.s].nsub;
+        tg += gridDim.x;
+        tile_locate(ph, tg, c.s, c.tile);
     }
 }
 
@@ -315,10 +377,14 @@ template <int N>
 CL_DEVINL void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 CL_DEVINL void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+CL_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // The lane's share of a unit's 16-byte pieces: a unit is 16 rows of 18
 // (Q4_K: 288 B) or 14 (Q6_K: 224 B) pieces, contiguous in global memory;
 // piece c goes to row c / P, offset 16 (c % P) of the slot's padded rows.
-// Pieces lane + 32 i, fixed per lane (Q4_K: 9 each, Q6_K: 7 each).
+// Pieces lane + 32 i, fixed per lane (Q4_K: 9 each, Q6_K: 7 each).  (Per
+// lane cp.async measured faster here than one bulk copy per unit, and much
+// faster than one per 224-byte Q6_K row.)
 struct LanePlan {
     int dst4[9];
     int dst6[7];
@@ -483,13 +549,21 @@ struct Smem {
     uint8_t* ring;
     uint8_t* region;
     const uint8_t* zero;
-    Phase* cph;    // the phase being computed (CTA-wide)
+    float* red;    // [kRedUnits][16] tile mode: each unit's 16 row sums
+    Phase* pc;     // [kPhaseCache] descriptors of the coming phases: phase q in slot q % kPhaseCache
     Phase* wph;    // [kW] the phase each warp is issuing from
     double* dred;  // [kW]
     float2* bests; // [kW]
-    int* flags;    // [0] barrier ok, [1] last-of-split / last CTA
+    int* flags;    // [0] barrier ok, [1] last-of-split / last CTA, [4 ..) the phase in each cache slot
     uint64_t* xbar;  // completion of the encoded-input bulk copies
 };
+
+// Phase descriptors are built from the layer table in global memory (a few
+// dependent loads); thread 0 builds them kPhaseCache - 1 phases ahead, while
+// the grid waits at a barrier, so that no warp builds one in its unit loop.
+constexpr int kPhaseCache = 4;
+constexpr int kPhaseWords = (int)(sizeof(Phase) / 8);
+static_assert(sizeof(Phase) % 8 == 0 && kPhaseWords <= 32, "a phase descriptor is copied by one warp, 8 B a lane");
 
 // ---- encode the phase's input into XQ4 limbs (all warps) -------------------
 CL_DEVINL void encode_input(const Params& P, const Phase& ph, const Smem& S, int tok, int warp, int lane) {
@@ -628,6 +702,7 @@ CL_DEVINL bool load_input(const Params& P, const Phase& ph, const Smem& S, uint3
     float* xs = reinterpret_cast<float*>(S.region + nb * 1024);
     float* xsum = reinterpret_cast<float*>(S.region + nb * 1024 + xs_bytes);
     if (tid == 0) {
+        fence_proxy_async_smem();  // the region's last readers passed the CTA barrier before this phase
         mbar_arrive_expect_tx(S.xbar, (uint32_t)(nb * 1024 + xs_bytes + nb * 32));
         bulk_g2s(xq, ev.xq, (uint32_t)(nb * 1024), S.xbar);
         bulk_g2s(xs, ev.xs, (uint32_t)xs_bytes, S.xbar);
@@ -652,41 +727,72 @@ CL_DEVINL bool load_input(const Params& P, const Phase& ph, const Smem& S, uint3
 }
 
 // ---- attention of one layer (CTA = KV head x key split) -------------------
-CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer& L, int pos, const Smem& S,
-                         long long* tr) {
+// Splits per KV head: as requested, else one per kSplitKeys keys, at most
+// kSplitsMax and at most the CTAs per KV head; split sp of KV head g holds
+// keys k0 .. k0 + nk - 1 (nk may be 0 for a requested count).
+struct AttnSplit {
+    int g, sp, ns, k0, nk;
+};
+
+CL_DEVINL bool attn_split(const Params& P, int len, AttnSplit& a) {
+    int ns = P.splits > 0 ? P.splits : (len + kSplitKeys - 1) / kSplitKeys;
+    ns = max(1, min(min(ns, kSplitsMax), (int)gridDim.x / P.hkv));
+    if ((int)blockIdx.x >= P.hkv * ns) return false;
+    a.ns = ns;
+    a.g = blockIdx.x / ns;
+    a.sp = blockIdx.x - a.g * ns;
+    const int per = (len + ns - 1) / ns;
+    a.k0 = a.sp * per;
+    a.nk = max(0, min(per, len - a.k0));
+    return true;
+}
+
+// Attention's shared memory: after the QKV phase's input in the region.
+struct AttnSmem {
+    float *qs, *ks, *vs, *ps, *run, *fac, *csm;
+};
+
+CL_DEVINL AttnSmem attn_smem(const Params& P, const Smem& S) {
+    AttnSmem a;
+    a.qs = reinterpret_cast<float*>(S.region + P.attn_off);  // [G][kQLD]
+    a.ks = a.qs + kGMax * kQLD;                              // [kKT][kQLD]
+    a.vs = a.ks + kKT * kQLD;                                // [kKT][kD]
+    a.ps = a.vs + kKT * kD;                                  // [G][kKT]
+    a.run = a.ps + kGMax * kKT;                              // [G][2]
+    a.fac = a.run + 2 * kGMax;                               // [G]
+    a.csm = a.fac + kGMax;                                   // [d/2][cos, sin] of the position
+    return a;
+}
+
+// Rows r0, r0 + step, ... of the key tile at t0 of a split into shared
+// memory (K rows padded to kQLD), one 16-byte piece per lane and row.  The
+// row of the current position holds a stale key until attention writes it.
+CL_DEVINL void attn_load_rows(const Params& P, const cl_qwen2_layer& L, const AttnSplit& a, const AttnSmem& A,
+                              int t0, int r0, int step, int lane) {
+    const int kvd = P.hkv * kD, nk = min(kKT, a.nk - t0);
+    const size_t base = (size_t)(a.k0 + t0) * kvd + (size_t)a.g * kD;
+    for (int r = r0; r < nk; r += step) {
+        cp16(A.ks + r * kQLD + 4 * lane, L.k_cache + base + (size_t)r * kvd + 4 * lane);
+        cp16(A.vs + r * kD + 4 * lane, L.v_cache + base + (size_t)r * kvd + 4 * lane);
+    }
+}
+
+CL_DEVINL void attention(const Params& P, const Phase& aph, int layer, int pos, const Smem& S, long long* tr) {
+    const cl_qwen2_layer& L = P.layers[layer];
     auto stamp = [&](int slot) {
         if (tr && threadIdx.x == 0) tr[slot] = (long long)global_ns();
     };
-    const int G = P.hq / P.hkv, kvd = P.hkv * kD, len = pos + 1, tid = threadIdx.x;
-    int ns = min(kSplitsMax, max(1, (len + kKT - 1) / kKT));
-    ns = max(1, min(ns, (int)gridDim.x / P.hkv));
-    if ((int)blockIdx.x >= P.hkv * ns) return;
-    const int g = blockIdx.x / ns, sp = blockIdx.x - g * ns;
-    const int per = (len + ns - 1) / ns, k0 = sp * per;
-    const int nk_all = max(0, min(per, len - k0));
-    float* qs = reinterpret_cast<float*>(S.region);  // [G][kQLD]
-    float* ks = qs + kGMax * kQLD;                   // [kKT][kQLD]
-    float* vs = ks + kKT * kQLD;                     // [kKT][kD]
-    float* ps = vs + kKT * kD;                       // [G][kKT]
-    float* run = ps + kGMax * kKT;                   // [G][2]
-    float* fac = run + 2 * kGMax;                    // [G]
-    float* csm = fac + kGMax;                        // [d/2][cos, sin] of the position
+    const int G = P.hq / P.hkv, kvd = P.hkv * kD, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    AttnSplit sa;
+    if (!attn_split(P, pos + 1, sa)) return;
+    const int g = sa.g, sp = sa.sp, ns = sa.ns, k0 = sa.k0, nk_all = sa.nk;
+    const AttnSmem A = attn_smem(P, S);
+    float *qs = A.qs, *ks = A.ks, *vs = A.vs, *ps = A.ps, *run = A.run, *fac = A.fac, *csm = A.csm;
     const float* cs = P.rope + (size_t)pos * kD;
     const int half = kD / 2;
-    auto load_tile = [&](int t0) {
-        const int nk = min(kKT, nk_all - t0);
-        const size_t base = (size_t)(k0 + t0) * kvd + (size_t)g * kD;
-        for (int i = tid; i < nk * (kD / 4); i += kThreads) {
-            const int r = i / (kD / 4), c = i - r * (kD / 4);
-            cp16(ks + r * kQLD + 4 * c, L.k_cache + base + (size_t)r * kvd + 4 * c);
-            cp16(vs + r * kD + 4 * c, L.v_cache + base + (size_t)r * kvd + 4 * c);
-        }
-        cp_commit();
-    };
-    // Every independent load in flight at once: the first key tile, the
-    // query heads, the position's rotation row and, in the split holding
-    // the position, the new key and value.
-    if (nk_all > 0) load_tile(0);
+    // The first key tile is in flight since the QKV phase (attn_prefetch);
+    // the query heads, the position's rotation row and, in the split holding
+    // the position, the new key and value are loaded now, all at once.
     constexpr int kQv = (kGMax * kD / 4 + kThreads - 1) / kThreads;
     float4 qv[kQv];
 #pragma unroll
@@ -737,7 +843,10 @@ CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer
     for (int hh = 0; hh < kGMax; ++hh) acc[hh] = 0.0f;
     for (int t0 = 0; t0 < nk_all; t0 += kKT) {
         const int nk = min(kKT, nk_all - t0);
-        if (t0 > 0) load_tile(t0);
+        if (t0 > 0) {
+            attn_load_rows(P, L, sa, A, t0, warp, kW, lane);
+            cp_commit();
+        }
         cp_wait<0>();
         __syncthreads();
         if (t0 == 0) stamp(11);
@@ -778,24 +887,21 @@ CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer
             ps[hh * kKT + tk] = ((a0 + a1) + (a2 + a3)) * P.scale;
         }
         __syncthreads();
-        {
-            const int warp = tid >> 5, lane = tid & 31;
-            if (warp < G) {
-                float* ph = ps + warp * kKT;
-                const float s0 = lane < nk ? ph[lane] : -INFINITY;
-                const float s1 = lane + 32 < nk ? ph[lane + 32] : -INFINITY;
-                const float mo = run[2 * warp], mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
-                const float e0 = lane < nk ? expf(s0 - mn) : 0.0f;
-                const float e1 = lane + 32 < nk ? expf(s1 - mn) : 0.0f;
-                if (lane < nk) ph[lane] = e0;
-                if (lane + 32 < nk) ph[lane + 32] = e1;
-                const float l = warp_sum(e0 + e1);
-                if (lane == 0) {
-                    const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
-                    fac[warp] = f;
-                    run[2 * warp] = mn;
-                    run[2 * warp + 1] = run[2 * warp + 1] * f + l;
-                }
+        if (warp < G) {
+            float* ph = ps + warp * kKT;
+            const float s0 = lane < nk ? ph[lane] : -INFINITY;
+            const float s1 = lane + 32 < nk ? ph[lane + 32] : -INFINITY;
+            const float mo = run[2 * warp], mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
+            const float e0 = lane < nk ? expf(s0 - mn) : 0.0f;
+            const float e1 = lane + 32 < nk ? expf(s1 - mn) : 0.0f;
+            if (lane < nk) ph[lane] = e0;
+            if (lane + 32 < nk) ph[lane + 32] = e1;
+            const float l = warp_sum(e0 + e1);
+            if (lane == 0) {
+                const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                fac[warp] = f;
+                run[2 * warp] = mn;
+                run[2 * warp + 1] = run[2 * warp + 1] * f + l;
             }
         }
         __syncthreads();
@@ -810,6 +916,7 @@ CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer
         }
         __syncthreads();  // tile buffers are refilled next
     }
+    if (nk_all == 0) cp_wait<0>();  // an empty split: its (empty) prefetch group
     stamp(12);
     // this split's (m, l, o) per head; the K tile buffer holds the PV parts
     float* pv = ks;
@@ -819,16 +926,15 @@ CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer
             if (hh < G) pv[((pt - 1) * G + hh) * kD + dim] = acc[hh];
     }
     __syncthreads();
-    const int rec = kD + 2;
-    float* part = P.attn_part + (size_t)g * kSplitsMax * G * rec;
+    float* part = P.attn_part + (size_t)g * kSplitsMax * G * kRec;
     if (pt == 0) {
 #pragma unroll
         for (int hh = 0; hh < kGMax; ++hh) {
             if (hh < G) {
                 float o = acc[hh];
                 for (int q2 = 1; q2 < kThreads / kD; ++q2) o += pv[((q2 - 1) * G + hh) * kD + dim];
-                float* pr = part + ((size_t)sp * G + hh) * rec;
-                __stcg(pr + 2 + dim, o);
+                float* pr = part + ((size_t)sp * G + hh) * kRec;
+                __stcg(pr + 4 + dim, o);
                 if (dim == 0) {
                     __stcg(pr, run[2 * hh]);
                     __stcg(pr + 1, run[2 * hh + 1]);
@@ -839,44 +945,72 @@ CL_DEVINL void attention(const Params& P, const Phase& aph, const cl_qwen2_layer
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const unsigned int old = atomicAdd(&P.ctl->attn_ticket[g], 1u);
-        S.flags[1] = old == (unsigned int)(ns - 1);
+        atomicAdd(&P.ctl->attn_ticket[g], 1u);
+    }
+    stamp(13);
+    // Splits 0 .. G - 1 merge one query head each (split sp: heads sp, sp + ns,
+    // ... when there are fewer splits than heads) once every split of the KV
+    // head has published; the tickets count on through the step's layers.
+    if (sp >= G) return;
+    if (tid == 0) {
+        const unsigned int target = (unsigned int)((layer + 1) * ns);
+        const unsigned long long t0 = global_ns();
+        int ok = 1;
+        while (ld_acquire(&P.ctl->attn_ticket[g]) < target) {
+            if (*reinterpret_cast<volatile int*>(&P.ctl->abort) || global_ns() - t0 > kWaitNs) {
+                atomicCAS(&P.ctl->error, 0, 5 * layer + 2);
+                atomicExch(&P.ctl->abort, 1);
+                ok = 0;
+                break;
+            }
+        }
+        S.flags[1] = ok;
     }
     __syncthreads();
-    stamp(13);
-    if (!S.flags[1]) return;
-    __threadfence();
-    // merge the splits (attn_decode_combine's weights: exp(m_s - m) / l)
-    float* wsm = ps;  // [G][kSplitsMax]
-    {
-        const int warp = tid >> 5, lane = tid & 31;
-        if (warp < G) {
-            const float ms = lane < ns ? __ldcg(part + ((size_t)lane * G + warp) * rec) : -INFINITY;
-            const float ls = lane < ns ? __ldcg(part + ((size_t)lane * G + warp) * rec + 1) : 0.0f;
+    if (!S.flags[1]) return;  // the grid barrier ends the step
+    // (attn_decode_combine's weights: exp(m_s - m) / l); thread: one dim, half the splits
+    constexpr int kHalf = kSplitsMax / 2;
+    float* wsm = ps;                                   // [kSplitsMax]
+    float* osm = ps + kSplitsMax;                      // [kD] the second half's sums
+    const int dd = tid & (kD - 1), part2 = tid / kD;   // part2 in {0, 1}
+    for (int hh = sp; hh < G; hh += ns) {
+        float ov[kHalf];
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) {
+            const int s2 = part2 * kHalf + i;
+            ov[i] = s2 < ns ? __ldcg(part + ((size_t)s2 * G + hh) * kRec + 4 + dd) : 0.0f;
+        }
+        if (warp == 0) {
+            const float ms = lane < ns ? __ldcg(part + ((size_t)lane * G + hh) * kRec) : -INFINITY;
+            const float ls = lane < ns ? __ldcg(part + ((size_t)lane * G + hh) * kRec + 1) : 0.0f;
             const float m = warp_max(ms);
             const float e = ls > 0.0f ? expf(ms - m) : 0.0f;
             const float l = warp_sum(ls * e);
-            if (lane < kSplitsMax) wsm[warp * kSplitsMax + lane] = lane < ns ? e / l : 0.0f;
+            wsm[lane] = lane < ns ? e / l : 0.0f;
         }
+        __syncthreads();
+        float o = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) o += ov[i] * wsm[part2 * kHalf + i];
+        if (part2 == 1) osm[dd] = o;
+        __syncthreads();
+        if (part2 == 0) P.att[(size_t)(g * G + hh) * kD + dd] = o + osm[dd];
+        __syncthreads();
+        // the o_proj input block of the head (two 128-wide heads per block)
+        if (aph.out_buf >= 0 && warp == 0) block_done(P, aph, P.att, (g * G + hh) / 2, 1, lane);
     }
-    __syncthreads();
-    for (int i = tid; i < G * kD; i += kThreads) {
-        const int hh = i / kD, dd = i - hh * kD;
-        float o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int s2 = 0; s2 < ns; ++s2)
-            o4[s2 & 3] += __ldcg(part + ((size_t)s2 * G + hh) * rec + 2 + dd) * wsm[hh * kSplitsMax + s2];
-        P.att[(size_t)(g * G + hh) * kD + dd] = (o4[0] + o4[1]) + (o4[2] + o4[3]);
-    }
-    if (tid == 0) P.ctl->attn_ticket[g] = 0u;
     stamp(14);
-    // the o_proj input blocks this KV head's query heads complete (two
-    // 128-wide heads per block)
-    __syncthreads();
-    if (aph.out_buf >= 0) {
-        const int h0 = g * G, h1 = h0 + G;
-        const int b = h0 / 2 + (tid >> 5);  // warp i: the i-th block these heads touch
-        if (b <= (h1 - 1) / 2) block_done(P, aph, P.att, b, min(h1, 2 * b + 2) - max(h0, 2 * b), tid & 31);
-    }
+}
+
+// The first key tile of the CTA's split of layer l's attention, issued by
+// each warp as it finishes its QKV units (rows warp, warp + kW, ...): the
+// cached keys do not depend on the QKV products, and the region past the
+// QKV input is free.  One commit group per warp, waited for by attention.
+CL_DEVINL void attn_prefetch(const Params& P, const cl_qwen2_layer& L, int pos, const Smem& S, int warp,
+                             int lane) {
+    AttnSplit sa;
+    if (attn_split(P, pos + 1, sa) && sa.nk > 0) attn_load_rows(P, L, sa, attn_smem(P, S), 0, warp, kW, lane);
+    cp_commit();
 }
 
 // Tile completions of output blocks a warp has not yet counted: its tiles
@@ -899,17 +1033,55 @@ CL_DEVINL void pending_add(const Params& P, const Phase& ph, const float* y, int
     ++pd.count;
 }
 
-// A finished tile's rows, direct or through the partial buffer.
-CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, long long b, long long e, int gw,
-                          int GW, float yg, float y8, float ym, int lane, Best& best, Pending& pd,
-                          const RowPre& pre) {
-    const int g = lane >> 2, t = lane & 3;
+// A warp's sums over a unit or tile -> lanes with t == 0: rows g (yg) and g + 8 (y8).
+CL_DEVINL void quad_rows(float& yg, float& y8, float ym, int t) {
     if (t & 1) y8 += ym;
     else yg += ym;
     yg += __shfl_xor_sync(0xffffffffu, yg, 1);
     yg += __shfl_xor_sync(0xffffffffu, yg, 2);
     y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
     y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+}
+
+// Tile mode, after the CTA's units: warp w finishes the CTA's tiles w, w +
+// kW, ...: each row the sum of its units in order, then bias and residual
+// (as tile_out), then the output block's completion.
+CL_DEVINL void finish_ctile(const Params& P, const Phase& ph, const Smem& S, int warp, int lane) {
+    // the warp's first tile: bias and residual loads in flight across the CTA barrier
+    int s0 = 0, tl0 = 0;
+    const bool has0 = tile_locate(ph, blockIdx.x + warp * gridDim.x, s0, tl0);
+    float cb = 0.0f, cr = 0.0f;
+    if (has0 && lane < 16) {
+        const Seg& sg = ph.seg[s0];
+        if (sg.bias) cb = sg.bias[tl0 * 16 + lane];
+        if (ph.residual) cr = __ldcg(sg.y + tl0 * 16 + lane);
+    }
+    __syncthreads();
+    int pos0 = 0, k = 0, s = 0, tl = 0;
+    for (int tg = blockIdx.x; tile_locate(ph, tg, s, tl); tg += gridDim.x, ++k) {
+        const Seg& sg = ph.seg[s];
+        if (k % kW == warp) {
+            if (lane < 16) {
+                float v = 0.0f;
+                for (int j = 0; j < sg.nsub; ++j) v += S.red[(pos0 + j) * 16 + lane];
+                const int o = tl * 16 + lane;
+                const bool first = k == warp;
+                if (sg.bias) v += first ? cb : sg.bias[o];
+                if (ph.residual) v = (first ? cr : __ldcg(sg.y + o)) + v;
+                sg.y[o] = v;
+            }
+            if (ph.out_buf >= 0) block_done(P, ph, sg.y, (tl * 16) / 256, 1, lane);
+        }
+        pos0 += sg.nsub;
+    }
+}
+
+// A finished tile's rows, direct or through the partial buffer.
+CL_DEVINL void flush_tile(const Params& P, const Phase& ph, int s, int tile_l, long long b, long long e, int gw,
+                          int GW, float yg, float y8, float ym, int lane, Best& best, Pending& pd,
+                          const RowPre& pre) {
+    const int g = lane >> 2, t = lane & 3;
+    quad_rows(yg, y8, ym, t);
     const Seg& sg = ph.seg[s];
     const long long uf = sg.u0 + (long long)tile_l * sg.nsub, ul = uf + sg.nsub - 1;
     const int out_block = (tile_l * (sg.sw ? 8 : 16)) / 256;
@@ -977,12 +1149,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     S.region = smem + kRingBytes;
     uint8_t* zero = S.region + P.region_bytes;
     S.zero = zero;
-    S.cph = reinterpret_cast<Phase*>(zero + 1024);  // [2]: this phase and the next
-    S.wph = S.cph + 2;
+    S.red = reinterpret_cast<float*>(zero + 1024);
+    S.pc = reinterpret_cast<Phase*>(S.red + kRedUnits * 16);
+    S.wph = S.pc + kPhaseCache;
     S.dred = reinterpret_cast<double*>(S.wph + kW);
     S.bests = reinterpret_cast<float2*>(S.dred + kW);
     S.flags = reinterpret_cast<int*>(S.bests + kW);
-    S.xbar = reinterpret_cast<uint64_t*>(S.flags + 4);
+    S.xbar = reinterpret_cast<uint64_t*>(S.flags + 4 + kPhaseCache);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3, h = t >> 1;
@@ -996,6 +1169,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     const int tok = __ldcg(P.ints);
     const int pos = __ldcg(P.ints + 1);
     const int nph = 5 * P.n_layers + 1;
+    if (lane == 0 && warp < kPhaseCache) {  // phases 0 .. kPhaseCache - 1, one per warp
+        S.flags[4 + warp] = -1;
+        if (warp < nph) {
+            make_phase(P, warp, S.pc[warp]);
+            S.flags[4 + warp] = warp;
+        }
+    }
+    __syncthreads();
 
     // ---- the warp's ring: issue iterator (lane-uniform) ----
     uint8_t* ring = S.ring + (size_t)warp * kSlots * kSlotBytes;
@@ -1004,7 +1185,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     const uint64_t policy = evict_first_policy();
     int ip = -1;
     Cursor ic{0, 0, 0, 0};
-    int n_issued = 0;
+    int n_issued = 0;  // commit groups: one per unit, empty once the step's units are all issued
     auto issue_next = [&]() {
         while (ic.left == 0) {
             ++ip;
@@ -1013,20 +1194,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
                 return;
             }
             if (ip < 5 * P.n_layers && ip % 5 == 1) continue;  // attention: no weight units
-            if (lane == 0) make_phase(P, ip, wph);
+            const int slot = ip % kPhaseCache;
+            if (S.flags[4 + slot] == ip) {
+                if (lane < kPhaseWords)
+                    reinterpret_cast<long long*>(&wph)[lane] = reinterpret_cast<const long long*>(S.pc + slot)[lane];
+            } else if (lane == 0) {
+                make_phase(P, ip, wph);  // further ahead than the cache (few units per warp)
+            }
             __syncwarp();
-            const long long b0 = range_begin(wph.U, gw, GW), e0 = range_begin(wph.U, gw + 1, GW);
-            ic = b0 < e0 ? cursor_at(wph, b0, e0) : Cursor{0, 0, 0, 0};
+            if (wph.ctile) {
+                ic = cursor_ctile(wph, warp);
+            } else {
+                const long long b0 = range_begin(wph.U, gw, GW), e0 = range_begin(wph.U, gw + 1, GW);
+                ic = b0 < e0 ? cursor_at(wph, b0, e0) : Cursor{0, 0, 0, 0};
+            }
             __syncwarp();
         }
         issue_unit(wph, ic, ring + (size_t)(n_issued % kSlots) * kSlotBytes, lane, plan, policy);
-        cursor_next(wph, ic);
+        if (wph.ctile) cursor_ctile_next(wph, ic);
+        else cursor_next(wph, ic);
     };
     for (int i = 0; i < kSlots; ++i) {
         if (ip < nph) issue_next();
         cp_commit();
         ++n_issued;
     }
+    int n_done = 0;
 
     Q4Lane L;
     L.sh = 12u * (uint32_t)h;
@@ -1038,17 +1231,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
     L6.lw1 = L6.lw0 * (1.0f / 128.0f);
 
     Best best{-INFINITY, 0x7fffffff};
-    int n_done = 0;
     __syncthreads();
 
     long long* trace = P.trace ? P.trace + (size_t)blockIdx.x * nph * kTraceSlots : nullptr;
-    if (tid == 0) make_phase(P, 0, S.cph[0]);
+    // (the cache is filled before the warps' first issues read it)
     for (int p = 0; p < nph; ++p) {
         if (trace && tid == 0) trace[kTraceSlots * p] = (long long)global_ns();
         __syncthreads();
-        const Phase& ph = S.cph[p & 1];
+        const Phase& ph = S.pc[p % kPhaseCache];
         if (ph.attn) {
-            attention(P, ph, P.layers[p / 5], pos, S, trace ? trace + kTraceSlots * p : nullptr);
+            attention(P, ph, p / 5, pos, S, trace ? trace + kTraceSlots * p : nullptr);
             if (trace && tid == 0) trace[kTraceSlots * p + 1] = (long long)global_ns();
         } else {
             if (ph.in_buf >= 0) {
@@ -1073,18 +1265,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
             Pending pend{0, 0};
             RowPre pre{{0.0f, 0.0f}, {0.0f, 0.0f}};
             float yg = 0.0f, y8 = 0.0f, ym = 0.0f;
-            Cursor cc = b < e ? cursor_at(ph, b, e) : Cursor{0, 0, 0, 0};
-            for (; cc.left > 0; cursor_next(ph, cc)) {
+            Cursor cc = ph.ctile ? cursor_ctile(ph, warp) : b < e ? cursor_at(ph, b, e) : Cursor{0, 0, 0, 0};
+            int upos = warp;  // tile mode: the unit's position in the CTA's list
+            // traced: SM cycles spent waiting for the ring, computing units,
+            // issuing loads and flushing tiles, and the units computed
+            unsigned int cyc[4] = {0u, 0u, 0u, 0u};
+            int n_units = 0;
+            for (; cc.left > 0; ph.ctile ? cursor_ctile_next(ph, cc) : cursor_next(ph, cc)) {
                 const Cursor un = cc;
-                if (un.s != cur_s || un.tile != cur_tl) {
+                if (!ph.ctile && (un.s != cur_s || un.tile != cur_tl)) {
+                    const unsigned int cf = trace ? (unsigned int)clock() : 0u;
                     if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best, pend, pre);
+                    if (trace) cyc[3] += (unsigned int)clock() - cf;
                     cur_s = un.s;
                     cur_tl = un.tile;
                     pre = row_pre(ph, ph.seg[cur_s], cur_tl, g, t);
                     yg = y8 = ym = 0.0f;
                 }
+                const unsigned int c0 = trace ? (unsigned int)clock() : 0u;
                 cp_wait<kSlots - 1>();
                 __syncwarp();
+                const unsigned int c1 = trace ? (unsigned int)clock() : 0u;
+                if (trace) {
+                    cyc[0] += c1 - c0;
+                    ++n_units;
+                }
                 const uint8_t* slot = ring + (size_t)(n_done % kSlots) * kSlotBytes;
                 if (ph.seg[un.s].type == CL_TYPE_Q4_K) {
                     // super-blocks 2j and 2j + 1: two independent dot chains
@@ -1120,15 +1325,41 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
                     for (int hh = 0; hh < 2; ++hh)
                         q6k_half(bg + 112 * hh, b8 + 112 * hh, p0, p1, hh, sb, xs[sb], t, h, L6, yg, y8);
                 }
+                if (ph.ctile) {
+                    // the unit's 16 row sums into the CTA's list
+                    quad_rows(yg, y8, ym, t);
+                    if (t == 0) {
+                        S.red[upos * 16 + g] = yg;
+                        S.red[upos * 16 + 8 + g] = y8;
+                    }
+                    upos += kW;
+                    yg = y8 = ym = 0.0f;
+                }
                 __syncwarp();
+                const unsigned int c2 = trace ? (unsigned int)clock() : 0u;
                 ++n_done;
                 if (ip < nph) issue_next();
                 cp_commit();
                 ++n_issued;
+                if (trace) {
+                    cyc[1] += c2 - c1;
+                    cyc[2] += (unsigned int)clock() - c2;
+                }
             }
-            if (trace && lane == 0) trace[kTraceSlots * p + 3 + warp] = (long long)global_ns();
-            if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best, pend, pre);
-            pending_flush(P, ph, ph.seg[0].y, pend, lane);
+            if (trace && lane == 0) {
+                trace[kTraceSlots * p + 3 + warp] = (long long)global_ns();
+                if (warp == 0) {
+                    for (int i = 0; i < 4; ++i) trace[kTraceSlots * p + 11 + i] = cyc[i];  // (attention: 11-14)
+                    trace[kTraceSlots * p + 15] = n_units;
+                }
+            }
+            if (p % 5 == 0 && p < 5 * P.n_layers) attn_prefetch(P, P.layers[p / 5], pos, S, warp, lane);
+            if (ph.ctile) {
+                finish_ctile(P, ph, S, warp, lane);
+            } else {
+                if (cur_s >= 0) flush_tile(P, ph, cur_s, cur_tl, b, e, gw, GW, yg, y8, ym, lane, best, pend, pre);
+                pending_flush(P, ph, ph.seg[0].y, pend, lane);
+            }
         }
         if (p + 1 < nph) {
             // ---- grid barrier ----
@@ -1136,8 +1367,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
             if (trace && tid == 0) trace[kTraceSlots * p + 2] = (long long)global_ns();
             if (tid == 0) {
                 red_add_release(&P.ctl->bar, 1u);
-                // the next phase's descriptor needs no activation: built while the grid arrives
-                make_phase(P, p + 1, S.cph[(p + 1) & 1]);
+                // phase p's slot: the descriptor of phase p + kPhaseCache, built while the
+                // grid arrives (every warp of the CTA is past phase p)
+                if (p + kPhaseCache < nph) {
+                    make_phase(P, p + kPhaseCache, S.pc[p % kPhaseCache]);
+                    S.flags[4 + p % kPhaseCache] = p + kPhaseCache;
+                }
                 const unsigned int target = (unsigned int)(p + 1) * gridDim.x;
                 const unsigned long long t0 = global_ns();
                 int ok = 1;
@@ -1208,6 +1443,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_fused_kernel(const __grid_
             P.ints[2] = pos + 2;
             P.ctl->bar = 0u;
             P.ctl->done = 0u;
+            for (int i = 0; i < kMaxKvHeads; ++i) P.ctl->attn_ticket[i] = 0u;
             __threadfence();
         }
     }
@@ -1260,17 +1496,21 @@ __global__ void decode_pack_kernel(int type, const uint8_t* __restrict__ w, cons
     }
 }
 
+size_t xq_bytes(int nb) { return (size_t)nb * 1024 + (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)nb * 32; }
+
+size_t attn_off(int hidden) { return (xq_bytes(hidden / 256) + 127) & ~(size_t)127; }
+
 size_t region_bytes(int hidden, int ffn) {
-    const int nb = std::max(hidden, ffn) / 256;
-    const size_t xq = (size_t)nb * 1024 + (((size_t)nb * 4 + 15) & ~(size_t)15) + (size_t)nb * 32;
+    const size_t xq = xq_bytes(std::max(hidden, ffn) / 256);
     const size_t attn = sizeof(float) * ((size_t)kGMax * kQLD + (size_t)kKT * kQLD + (size_t)kKT * kD +
                                          (size_t)kGMax * kKT + 3 * kGMax + kD);
-    return (std::max(xq, attn) + 127) & ~(size_t)127;
+    return (std::max(xq, attn_off(hidden) + attn) + 127) & ~(size_t)127;
 }
 
 size_t smem_bytes(int hidden, int ffn) {
-    return kRingBytes + region_bytes(hidden, ffn) + 1024 + (2 + kW) * sizeof(Phase) + kW * sizeof(double) +
-           kW * sizeof(float2) + 16 + 16;
+    return kRingBytes + region_bytes(hidden, ffn) + 1024 + kRedUnits * 16 * sizeof(float) +
+           (2 + kW) * sizeof(Phase) + kW * sizeof(double) +
+           kW * sizeof(float2) + 16 + 4 * kPhaseCache + 16 + 3 * sizeof(Phase);
 }
 
 int max_tiles(const cl_qwen2_decode* m) {
@@ -1292,7 +1532,7 @@ Layout layout(const cl_qwen2_decode* m, int grid) {
     l.partials = off;
     off += (size_t)grid * kW * 2 * 16 * 4;
     l.attn = off;
-    off += (size_t)m->kv_heads * kSplitsMax * (m->q_heads / m->kv_heads) * (kD + 2) * 4;
+    off += (size_t)m->kv_heads * kSplitsMax * (m->q_heads / m->kv_heads) * kRec * 4;
     const int nbm = std::max(m->hidden, m->ffn) / 256;
     off = (off + 255) & ~(size_t)255;
     l.enc0 = off;
@@ -1343,7 +1583,8 @@ CL_API int cl_qwen2_decode_supported(const cl_qwen2_decode* m, const cl_qwen2_la
         m->ffn > kMaxK ||
         m->head_dim != kD || m->q_heads <= 0 || m->kv_heads <= 0 || m->kv_heads > kMaxKvHeads ||
         m->q_heads % m->kv_heads || m->q_heads / m->kv_heads > kGMax || m->q_heads * kD != m->hidden ||
-        m->vocab <= 0 || m->vocab % 16 || m->ffn % 8 || m->capacity <= 0)
+        m->vocab <= 0 || m->vocab % 16 || m->ffn % 8 || m->capacity <= 0 || m->attn_splits < 0 ||
+        m->attn_splits > kSplitsMax)
         return CL_ERR_UNSUPPORTED;
     if (!k_type_ok(m->out_type) || m->embd == nullptr || m->out_w == nullptr || m->out_norm == nullptr ||
         m->rope == nullptr || m->ints == nullptr || !m->h || !m->q || !m->k || !m->v || !m->att || !m->act ||
@@ -1453,6 +1694,8 @@ CL_API int cl_qwen2_decode_step(const cl_qwen2_decode* m, const cl_qwen2_layer* 
     p.enc_cnt = reinterpret_cast<unsigned int*>(ws + lay.enc_cnt);
     p.nb_max = std::max(m->hidden, m->ffn) / 256;
     p.region_bytes = (int)region_bytes(m->hidden, m->ffn);
+    p.attn_off = (int)attn_off(m->hidden);
+    p.splits = m->attn_splits;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

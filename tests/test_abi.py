@@ -169,6 +169,9 @@ def test_fused_decode_description_checks():
                dict(types={"q": sg.Q5_0}), dict(types={"down": sg.Q8_0}), dict(vocab=152064 + 8)):
         _, _, p2, l2 = _fused_desc(**kw)
         assert lib.cl_qwen2_decode_supported(p2, l2) == 2, kw
+    for splits, rc in ((32, 0), (33, 2), (-1, 2), (0, 0)):  # attention key splits: 0 (automatic) .. 32
+        m.attn_splits = splits
+        assert lib.cl_qwen2_decode_supported(pm, pl) == rc, splits
     layers[1].up = None  # the tiled gate pack holds the up rows: `up` is not read
     assert lib.cl_qwen2_decode_supported(pm, pl) == 0
     layers[1].gate = None

@@ -8,8 +8,10 @@ the model does not qualify, so these tests cannot pass on a silent
 fallback).  Both must give the reference CPULLM's greedy tokens at every
 step and logits within 1e-4 (max-abs relative), on a small model with the
 7B's structure (head_dim 128, 7 query heads per KV head): a short prompt
-(one attention split) and a 1100-token prompt (16 key splits of two 64-key
-tiles each, the KV append landing in the last split's second tile).
+(one attention split) and a 1100-token prompt (32 key splits of 35 keys),
+and the long prompt again with 4 splits forced (CUDALLM_DECODE_SPLITS): 276
+keys per split in five 64-key tiles, the KV append landing in the last
+split's last tile.
 """
 import os
 
@@ -37,8 +39,10 @@ def small(model_dir, cuda):
     return path, d
 
 
-def run(path, prompt, steps, monkeypatch, mode, max_sequence=2048, prefill="tf32x3"):
+def run(path, prompt, steps, monkeypatch, mode, max_sequence=2048, prefill="tf32x3", splits=None):
     monkeypatch.setenv("CUDALLM_DECODE", mode)
+    if splits is not None:
+        monkeypatch.setenv("CUDALLM_DECODE_SPLITS", str(splits))
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     llm = CudaLLM(path, max_sequence=max_sequence)
     toks = [llm.prefill(prompt)]
@@ -57,6 +61,17 @@ def test_small_model_matches_reference(small, monkeypatch, mode, n):
     toks, logits = run(path, d[f"prompt{n}"], 4, monkeypatch, mode)
     assert toks == list(d[f"tokens{n}"])
     for i, ref in enumerate(d[f"logits{n}"]):
+        assert rel(logits[i], ref) <= 1e-4, (i, rel(logits[i], ref))
+
+
+def test_small_model_multi_tile_splits(small, monkeypatch):
+    """Four key splits over 1100+ keys: every split runs five key tiles
+    (the first from the prefetch during the QKV phase, the rest loaded in
+    attention)."""
+    path, d = small
+    toks, logits = run(path, d["prompt1100"], 4, monkeypatch, "fused", splits=4)
+    assert toks == list(d["tokens1100"])
+    for i, ref in enumerate(d["logits1100"]):
         assert rel(logits[i], ref) <= 1e-4, (i, rel(logits[i], ref))
 
 
