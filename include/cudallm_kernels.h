@@ -113,7 +113,8 @@ CL_API int cl_gemm(int type, const void* w, long long stride, int n, int k, cons
 enum {
     CL_GEMM_TF32X3 = 0, /* operands split hi + lo TF32, 3 MMAs: FP32-grade (k % 32 == 0) */
     CL_GEMM_F16 = 1,    /* operands rounded to FP16, 1 MMA: 11-bit significands (k % 64 == 0) */
-    CL_GEMM_BF16 = 2    /* operands rounded to BF16 (cl_gemm16 path only): 8-bit significands */
+    CL_GEMM_BF16 = 2,   /* operands rounded to BF16 (cl_gemm16 path only): 8-bit significands */
+    CL_GEMM_F16X3 = 3   /* operands split hi + lo FP16, 3 MMAs: FP32-grade (cl_gemm16 path only) */
 };
 /* The tcgen05 path with an explicit precision; CL_ERR_UNSUPPORTED for shapes
  * it does not take. */
@@ -124,11 +125,21 @@ CL_API int cl_gemm_simt(int type, const void* w, long long stride, int n, int k,
                         const float* bias, const float* residual, float* y, cudaStream_t stream);
 
 /* The 16-bit tensor-core prefill path (same product as metal_gemm_*_f32 /
- * gemmtb, operands rounded once to FP16 or BF16, FP32 accumulation):
+ * gemmtb, operands rounded once to FP16 or BF16, or split into FP16 hi + lo
+ * parts; FP32 accumulation):
  *   cl_dequant16  W rows (device layout) -> row-major [n][k] 16-bit, each
  *                 element the CPU decoder's FP32 value rounded once
  *                 (format CL_GEMM_F16 or CL_GEMM_BF16; k % 32 == 0);
  *   cl_convert16  count FP32 values -> 16-bit (count % 4 == 0);
+ * and for the split form (CL_GEMM_F16X3), each operand scaled by the power
+ * of two that puts its largest magnitude in [2^13, 2^14):
+ *   cl_amax_dequant  *amax = max |element| of the dequantized W rows;
+ *   cl_amax          *amax = max |x[i]| (count % 4 == 0);
+ *   cl_dequant16_split  W rows -> [n][2k] FP16 rows [hi(k) | lo(k)] of the
+ *                 scaled values (hi = FP16(v), lo = FP16(v - hi));
+ *   cl_split16    X[rows][k] FP32 -> rows [hi(k) | lo(k)] likewise;
+ * the outputs of a split product name both maxima (xmax, wmax) and are
+ * multiplied by the exact inverse powers of two;
  *   cl_gemm16_run Y = X16[m][k] W16[n][k]^T on tcgen05 (k % 64 == 0; TMA
  *                 tensor loads, 128 x 256 or 128 x 128 tiles, optional K
  *                 split summed in split order).  The n output columns are
@@ -141,11 +152,18 @@ typedef struct cl_gemm_out {
     float* y;              /* [m][ld], columns col0 .. col0 + cols - 1 of the product */
     const float* bias;     /* [cols] or NULL */
     const float* residual; /* [m][ld] or NULL (may alias y) */
+    const float *xmax, *wmax; /* split form: device maxima X and these W rows were scaled by; else NULL */
     int col0, cols, ld;
 } cl_gemm_out;
 CL_API int cl_dequant16(int type, const void* w, long long stride, int n, int k, void* out, int format,
                         cudaStream_t stream);
 CL_API int cl_convert16(const float* x, long long count, void* out, int format, cudaStream_t stream);
+CL_API int cl_amax_dequant(int type, const void* w, long long stride, int n, int k, float* amax,
+                           cudaStream_t stream);
+CL_API int cl_amax(const float* x, long long count, float* amax, cudaStream_t stream);
+CL_API int cl_dequant16_split(int type, const void* w, long long stride, int n, int k, const float* amax, void* out,
+                              cudaStream_t stream);
+CL_API int cl_split16(const float* x, int rows, int k, const float* amax, void* out, cudaStream_t stream);
 CL_API size_t cl_gemm16_workspace_bytes(int m, int n, int k);
 CL_API int cl_gemm16_run(const void* w16, int n, int k, const void* x16, int m, const cl_gemm_out* outs, int nout,
                          int format, void* workspace, size_t workspace_bytes, cudaStream_t stream);

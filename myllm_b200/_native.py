@@ -84,6 +84,10 @@ SIGNATURES = {
     "cl_peer_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
     "cl_dequant16": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
     "cl_convert16": (c_int, [c_vp, c_ll, c_vp, c_int, c_vp]),
+    "cl_split16": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_amax": (c_int, [c_vp, c_ll, c_vp, c_vp]),
+    "cl_amax_dequant": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp]),
+    "cl_dequant16_split": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
     "cl_gemm16_workspace_bytes": (c_size, [c_int, c_int, c_int]),
     "cl_gemm16_run": (c_int, [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_int, c_int, c_vp, c_size, c_vp]),
     "cl_decode_pack_bytes": (c_size, [c_int, c_int, c_int, c_int]),
@@ -121,7 +125,8 @@ SIGNATURES = {
 
 class GemmOut(ctypes.Structure):
     """cl_gemm_out of cudallm_kernels.h: one column range of a cl_gemm16_run product."""
-    _fields_ = [("y", c_vp), ("bias", c_vp), ("residual", c_vp), ("col0", c_int), ("cols", c_int), ("ld", c_int)]
+    _fields_ = [("y", c_vp), ("bias", c_vp), ("residual", c_vp), ("xmax", c_vp), ("wmax", c_vp), ("col0", c_int),
+                ("cols", c_int), ("ld", c_int)]
 
 
 class Qwen2Layer(ctypes.Structure):

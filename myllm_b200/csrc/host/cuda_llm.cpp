@@ -105,6 +105,8 @@ struct Layer {
     float* v_cache = nullptr;
     // 16-bit prefill copies (row-major [rows][cols]): Q|K|V rows, o, gate|up rows, down
     void *qkv16 = nullptr, *o16 = nullptr, *gu16 = nullptr, *down16 = nullptr;
+    // split form: device maxima of q, k, v, o, gate, up, down (the scales of their 16-bit copies)
+    float* wmax = nullptr;
 };
 
 // Contiguous, block-aligned share [begin, end) of `n` units for one rank.
@@ -418,9 +420,10 @@ struct CudaLLM::Impl {
 
     void setup_wide16() {
         const std::size_t kmax = std::max<std::size_t>(std::max<std::size_t>(H, F_l), std::max<std::size_t>(o_kl, 1));
+        const std::size_t eb = split16() ? 4 : 2;  // bytes per element: the split form keeps hi and lo
         std::size_t bytes = 0;
         auto plan = [&](std::size_t rows, std::size_t cols) {
-            const std::size_t b = (rows * cols * 2 + 255) / 256 * 256;
+            const std::size_t b = (rows * cols * eb + 255) / 256 * 256;
             bytes += b;
             return b;
         };
@@ -430,35 +433,50 @@ struct CudaLLM::Impl {
             if (F_l > 0 && gemm16_ok(H)) plan(2 * F_l, H);
             if (F_l > 0 && gemm16_ok(F_l)) plan(H, F_l);
         }
-        w16_mem = DeviceBuffer(bytes + (prefill_chunk * kmax * 2 + 255) / 256 * 256 + 256);
+        w16_mem = DeviceBuffer(bytes + (prefill_chunk * kmax * eb + 255) / 256 * 256 + 256);
+        amax_mem = DeviceBuffer((layers.size() * 7 + 1) * sizeof(float));
+        xmax = static_cast<float*>(amax_mem.get()) + layers.size() * 7;
         char* base = static_cast<char*>(w16_mem.get());
         const int fmt = fmt16();
+        float* wm = nullptr;
         auto dq = [&](const DevMat& m, char* dst) {
-            CUDALLM_CL(cl_dequant16(m.type, m.ptr, m.stride, m.rows, m.cols, dst, fmt, stream));
+            if (split16()) {
+                CUDALLM_CL(cl_amax_dequant(m.type, m.ptr, m.stride, m.rows, m.cols, wm, stream));
+                CUDALLM_CL(cl_dequant16_split(m.type, m.ptr, m.stride, m.rows, m.cols, wm, dst, stream));
+            } else {
+                CUDALLM_CL(cl_dequant16(m.type, m.ptr, m.stride, m.rows, m.cols, dst, fmt, stream));
+            }
+            ++wm;
         };
-        for (Layer& L : layers) {
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            Layer& L = layers[l];
+            L.wmax = static_cast<float*>(amax_mem.get()) + 7 * l;
+            wm = L.wmax;
             if (gemm16_ok(H)) {
                 L.qkv16 = base;
                 dq(L.q, base);
-                dq(L.k, base + (std::size_t)L.q.rows * H * 2);
-                dq(L.v, base + ((std::size_t)L.q.rows + L.k.rows) * H * 2);
-                base += (((std::size_t)L.q.rows + L.k.rows + L.v.rows) * H * 2 + 255) / 256 * 256;
+                dq(L.k, base + (std::size_t)L.q.rows * H * eb);
+                dq(L.v, base + ((std::size_t)L.q.rows + L.k.rows) * H * eb);
+                base += (((std::size_t)L.q.rows + L.k.rows + L.v.rows) * H * eb + 255) / 256 * 256;
             }
+            wm = L.wmax + 3;
             if (o_kl > 0 && gemm16_ok(o_kl)) {
                 L.o16 = base;
                 dq(L.o, base);
-                base += (H * o_kl * 2 + 255) / 256 * 256;
+                base += (H * o_kl * eb + 255) / 256 * 256;
             }
+            wm = L.wmax + 4;
             if (F_l > 0 && gemm16_ok(H)) {
                 L.gu16 = base;
                 dq(L.gate, base);
-                dq(L.up, base + F_l * H * 2);
-                base += (2 * F_l * H * 2 + 255) / 256 * 256;
+                dq(L.up, base + F_l * H * eb);
+                base += (2 * F_l * H * eb + 255) / 256 * 256;
             }
+            wm = L.wmax + 6;
             if (F_l > 0 && gemm16_ok(F_l)) {
                 L.down16 = base;
                 dq(L.down, base);
-                base += (H * F_l * 2 + 255) / 256 * 256;
+                base += (H * F_l * eb + 255) / 256 * 256;
             }
         }
         x16 = base;
@@ -466,9 +484,31 @@ struct CudaLLM::Impl {
         g16_ws_mem = DeviceBuffer((std::size_t)64 << 20);
     }
 
+    // One output column range of a 16-bit product (the split form names the scales).
+    cl_gemm_out out16(float* y, const float* bias, const float* res, int col0, int cols, int ld,
+                      const float* wm) const {
+        cl_gemm_out o{};
+        o.y = y;
+        o.bias = bias;
+        o.residual = res;
+        o.col0 = col0;
+        o.cols = cols;
+        o.ld = ld;
+        if (split16()) {
+            o.xmax = xmax;
+            o.wmax = wm;
+        }
+        return o;
+    }
+
     // Y column ranges = X[m, kdim] W16^T on the 16-bit path.
     void gemm16(const void* w16, int n, int kdim, const float* x, int m, const cl_gemm_out* outs, int nout) {
-        CUDALLM_CL(cl_convert16(x, (long long)m * kdim, x16, fmt16(), stream));
+        if (split16()) {
+            CUDALLM_CL(cl_amax(x, (long long)m * kdim, xmax, stream));
+            CUDALLM_CL(cl_split16(x, m, kdim, xmax, x16, stream));
+        } else {
+            CUDALLM_CL(cl_convert16(x, (long long)m * kdim, x16, fmt16(), stream));
+        }
         CUDALLM_CL(cl_gemm16_run(w16, n, kdim, x16, m, outs, nout, fmt16(), g16_ws_mem.get(), g16_ws_mem.size(),
                                  stream));
     }
@@ -563,12 +603,16 @@ struct CudaLLM::Impl {
             const long val = std::strtol(e, nullptr, 10);
             if (val > 0) prefill_chunk = std::min<std::size_t>(max_seq, (std::size_t)val);
         }
-        // Prefill GEMM precision: "tf32x3" (default, FP32-grade, as the
-        // reference's FP32 GEMM), "f16" (one FP16 tensor-core pass) or "simt"
-        // (FP32 CUDA cores).
+        // Prefill GEMM: "fp16x3" (default: resident split FP16 copies, three
+        // tcgen05 MMAs per step, FP32-grade like the reference's FP32 GEMM),
+        // "fp16" / "bf16" (one 16-bit pass), "tf32x3" (split TF32 over the
+        // native blocks, FP32-grade), "f16" (one FP16 pass over the native
+        // blocks) or "simt" (FP32 CUDA cores).
         if (const char* e = std::getenv("CUDALLM_PREFILL_GEMM")) {
             const std::string val(e);
-            if (val == "f16")
+            if (val == "fp16")
+                gemm_path = GemmPath::Fp16;
+            else if (val == "f16")
                 gemm_path = GemmPath::F16;
             else if (val == "simt")
                 gemm_path = GemmPath::Simt;
@@ -576,8 +620,8 @@ struct CudaLLM::Impl {
                 gemm_path = GemmPath::Auto;
             else if (val == "bf16")
                 gemm_path = GemmPath::Bf16;
-            else if (val != "fp16" && !val.empty())
-                throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be fp16, bf16, tf32x3, f16 or simt");
+            else if (val != "fp16x3" && !val.empty())
+                throw std::invalid_argument("CUDALLM_PREFILL_GEMM must be fp16x3, fp16, bf16, tf32x3, f16 or simt");
         }
         std::size_t o_block = 1;
         for (std::size_t l = 0; l < config.layer_count; ++l) {
@@ -771,15 +815,21 @@ struct CudaLLM::Impl {
     }
 
     // Prefill GEMM: the 16-bit tensor-core path over resident 16-bit weight
-    // copies (Fp16, the default; Bf16), the split-TF32 tcgen05 path over the
-    // native blocks (Auto: FP32-grade), its one-pass FP16 form, or the FP32
-    // CUDA-core kernel.
-    enum class GemmPath { Auto, F16, Simt, Fp16, Bf16 };
-    GemmPath gemm_path = GemmPath::Fp16;
-    DeviceBuffer w16_mem, g16_ws_mem;
+    // copies (Fp16x3, the default: split hi + lo, FP32-grade; Fp16; Bf16),
+    // the split-TF32 tcgen05 path over the native blocks (Auto: FP32-grade),
+    // its one-pass FP16 form, or the FP32 CUDA-core kernel.
+    enum class GemmPath { Auto, F16, Simt, Fp16, Bf16, Fp16x3 };
+    GemmPath gemm_path = GemmPath::Fp16x3;
+    DeviceBuffer w16_mem, g16_ws_mem, amax_mem;
+    float* xmax = nullptr;  // split form: the device maximum of the current product's X
     void* x16 = nullptr;  // [prefill_chunk][max(H, F_l, o_kl)] 16-bit activations
-    bool wide16() const { return gemm_path == GemmPath::Fp16 || gemm_path == GemmPath::Bf16; }
-    int fmt16() const { return gemm_path == GemmPath::Bf16 ? CL_GEMM_BF16 : CL_GEMM_F16; }
+    bool wide16() const {
+        return gemm_path == GemmPath::Fp16 || gemm_path == GemmPath::Bf16 || gemm_path == GemmPath::Fp16x3;
+    }
+    bool split16() const { return gemm_path == GemmPath::Fp16x3; }
+    int fmt16() const {
+        return gemm_path == GemmPath::Bf16 ? CL_GEMM_BF16 : split16() ? CL_GEMM_F16X3 : CL_GEMM_F16;
+    }
 
     // Y[m, W.rows] = X[m, kdim] W^T (+ bias) (+ residual) on the selected path.
     void gemm(const DevMat& Wm, int n, int kdim, const float* x, int m, const float* bias, const float* res, float* y) {
@@ -797,7 +847,8 @@ struct CudaLLM::Impl {
             return;
         case GemmPath::Auto:
         case GemmPath::Fp16:  // matrices the 16-bit GEMM does not take
-        case GemmPath::Bf16: break;
+        case GemmPath::Bf16:
+        case GemmPath::Fp16x3: break;
         }
         CUDALLM_CL(cl_gemm(Wm.type, Wm.ptr, Wm.stride, n, kdim, x, m, bias, res, y, stream));
     }
@@ -812,9 +863,10 @@ struct CudaLLM::Impl {
         for (Layer& L : layers) {
             CUDALLM_CL(cl_rmsnorm(X, L.attn_norm, m, (int)H, eps(), Xn, nullptr, s));
             if (L.qkv16) {
-                const cl_gemm_out outs[3] = {{Q, L.q_b, nullptr, 0, L.q.rows, L.q.rows},
-                                             {K, L.k_b, nullptr, L.q.rows, L.k.rows, L.k.rows},
-                                             {Vv, L.v_b, nullptr, L.q.rows + L.k.rows, L.v.rows, L.v.rows}};
+                const cl_gemm_out outs[3] = {out16(Q, L.q_b, nullptr, 0, L.q.rows, L.q.rows, L.wmax),
+                                             out16(K, L.k_b, nullptr, L.q.rows, L.k.rows, L.k.rows, L.wmax + 1),
+                                             out16(Vv, L.v_b, nullptr, L.q.rows + L.k.rows, L.v.rows, L.v.rows,
+                                                   L.wmax + 2)};
                 gemm16(L.qkv16, L.q.rows + L.k.rows + L.v.rows, (int)H, Xn, m, outs, 3);
             } else {
                 gemm(L.q, L.q.rows, (int)H, Xn, m, L.q_b, nullptr, Q);
@@ -823,8 +875,9 @@ struct CudaLLM::Impl {
             }
             CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
                                   pos0, L.k_cache, L.v_cache, s));
-            // the 16-bit prefill path takes the FP16 tensor-core attention where it applies
-            if (!(wide16() && d == 128 &&
+            // the one-pass 16-bit prefill paths take the FP16 tensor-core attention where it
+            // applies; the FP32-grade paths keep the FP32 kernel
+            if (!(wide16() && !split16() && d == 128 &&
                   cl_attn_prefill_tc(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s) == CL_OK))
                 CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
             const float* o_in = A;
@@ -844,7 +897,7 @@ struct CudaLLM::Impl {
                 o_in = Xn;
             }
             if (o_kl > 0 && L.o16) {
-                const cl_gemm_out o{out, nullptr, res, 0, (int)H, (int)H};
+                const cl_gemm_out o = out16(out, nullptr, res, 0, (int)H, (int)H, L.wmax + 3);
                 gemm16(L.o16, (int)H, (int)o_kl, o_in, m, &o, 1);
             } else if (o_kl > 0) {
                 gemm(L.o, (int)H, (int)o_kl, o_in, m, nullptr, res, out);
@@ -859,8 +912,8 @@ struct CudaLLM::Impl {
                 continue;
             }
             if (L.gu16) {
-                const cl_gemm_out gu[2] = {{G, nullptr, nullptr, 0, (int)F_l, (int)F_l},
-                                           {U, nullptr, nullptr, (int)F_l, (int)F_l, (int)F_l}};
+                const cl_gemm_out gu[2] = {out16(G, nullptr, nullptr, 0, (int)F_l, (int)F_l, L.wmax + 4),
+                                           out16(U, nullptr, nullptr, (int)F_l, (int)F_l, (int)F_l, L.wmax + 5)};
                 gemm16(L.gu16, 2 * (int)F_l, (int)H, Xn, m, gu, 2);
             } else {
                 gemm(L.gate, (int)F_l, (int)H, Xn, m, nullptr, nullptr, G);
@@ -868,7 +921,7 @@ struct CudaLLM::Impl {
             }
             CUDALLM_CL(cl_swiglu(G, U, G, (long long)m * F_l, s));
             if (L.down16) {
-                const cl_gemm_out dn{out, nullptr, res, 0, (int)H, (int)H};
+                const cl_gemm_out dn = out16(out, nullptr, res, 0, (int)H, (int)H, L.wmax + 6);
                 gemm16(L.down16, (int)H, (int)F_l, G, m, &dn, 1);
             } else {
                 gemm(L.down, (int)H, (int)F_l, G, m, nullptr, res, out);

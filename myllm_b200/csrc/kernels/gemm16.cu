@@ -22,6 +22,16 @@
 //      row tiles fastest, so CTAs that run together share the weight tile
 //      in L2.  With a K split, units store FP32 partials and
 //      cl_gemm16 adds them (in split order) with the bias / residual.
+// Split form (CL_GEMM_F16X3): each operand is first multiplied by a power
+// of two that puts its largest magnitude in [2^13, 2^14) (from a device-side
+// absolute maximum, so that the low parts stay clear of FP16's subnormal
+// range); each row then holds the FP16 rounding of its k scaled values (hi)
+// followed by the FP16 rounding of what hi leaves (lo), so hi + lo carries
+// ~22 significant bits.  Every K step issues three MMAs, Xhi Whi + Xhi Wlo +
+// Xlo Whi, into the same FP32 accumulator (the Xlo Wlo term is below FP32
+// rounding), and the epilogue multiplies by the exact inverse powers of two:
+// an FP32-grade product on the 16-bit tensor cores, as CL_GEMM_TF32X3 is on
+// the TF32 ones.
 // Outputs may be split by column ranges into up to three destinations (a
 // fused Q/K/V or gate/up product writes each matrix to its own buffer).
 // Every mbarrier wait is bounded; TMEM is always released.
@@ -50,8 +60,23 @@ struct OutSeg {
     float* y;
     const float* bias;
     const float* res;
+    const float *xmax, *wmax;  // split form: the absolute maxima the operands were scaled by
     int n0, n1, ld;
 };
+
+// The power of two that puts |a| <= amax into [2^13, 2^14) at amax (1 for 0).
+__host__ __device__ inline int split_exp(float amax) {
+    if (!(amax > 0.0f) || !(amax < 3.0e38f)) return 0;
+    int e = 0;
+    frexpf(amax, &e);  // amax = f 2^e, f in [0.5, 1)
+    return max(-100, min(100, 14 - e));
+}
+
+// Output multiplier of a segment: 2^-(x exponent + w exponent), exact.
+CL_DEVINL float seg_unscale(const OutSeg& sg) {
+    if (sg.xmax == nullptr || sg.wmax == nullptr) return 1.0f;
+    return ldexpf(1.0f, -(split_exp(__ldg(sg.xmax)) + split_exp(__ldg(sg.wmax))));
+}
 
 struct Args {
     int m, n, k, splits, kb_per_split, mt, nt, units;
@@ -60,11 +85,12 @@ struct Args {
     float* partial;  // splits > 1: [splits][m][n] FP32
 };
 
-template <int BN>
+template <int BN, bool SPLIT>
 struct Cfg {
     static constexpr int kBTile = BN * 128;
-    static constexpr int kStage = kATile + kBTile;
-    static constexpr int NS = BN == 256 ? 4 : 6;
+    // stage: X hi, W hi (then X lo, W lo in the split form)
+    static constexpr int kStage = (SPLIT ? 2 : 1) * (kATile + kBTile);
+    static constexpr int NS = SPLIT ? (BN == 256 ? 2 : 3) : (BN == 256 ? 4 : 6);
     static constexpr int kTmemCols = 2 * BN;
     static constexpr size_t kSmem = 1024 + (size_t)NS * kStage + 4 * 32 * kStageLd * 4 + 256;
 };
@@ -133,11 +159,12 @@ CL_DEVINL void unit_of(const Args& a, int u, int& mt, int& nt, int& s) {
     s = r / a.nt;
 }
 
-template <int BN>
+template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+              const __grid_constant__ CUtensorMap map_xl, const __grid_constant__ CUtensorMap map_wl,
               const __grid_constant__ Args a, int bf16) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* stage_out = reinterpret_cast<float*>(ring + C::NS * C::kStage);  // [4][32][33]
@@ -182,6 +209,10 @@ gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+            if (SPLIT) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_xl)) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_wl)) : "memory");
+            }
         }
         int it = 0;
         for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
@@ -200,6 +231,10 @@ gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__
                         uint8_t* st = ring + (size_t)s * C::kStage;
                         tma_load_2d(st, &map_x, kb * BK, mt * BM, &full[s]);
                         tma_load_2d(st + kATile, &map_w, kb * BK, nt * BN, &full[s]);
+                        if (SPLIT) {
+                            tma_load_2d(st + kATile + C::kBTile, &map_xl, kb * BK, mt * BM, &full[s]);
+                            tma_load_2d(st + 2 * kATile + C::kBTile, &map_wl, kb * BK, nt * BN, &full[s]);
+                        }
                     } else {
                         atomicExch(&g_g16_error, 1);
                         *abort_flag = 1;
@@ -233,9 +268,15 @@ gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__
                     fence_after_sync();
                     const uint32_t st = smem_u32(ring + (size_t)s * C::kStage);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)  // 4 k-steps of 16 elements (32 bytes) per 128-byte row
-                        mma_f16(td, smem_desc(st + 32u * kk), smem_desc(st + kATile + 32u * kk), idesc,
-                                (kb > kb0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; ++kk) {  // 4 k-steps of 16 elements (32 bytes) per 128-byte row
+                        const uint64_t ah = smem_desc(st + 32u * kk), wh = smem_desc(st + kATile + 32u * kk);
+                        mma_f16(td, ah, wh, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                        if (SPLIT) {
+                            const uint32_t lo = st + (uint32_t)(kATile + C::kBTile);
+                            mma_f16(td, ah, smem_desc(lo + kATile + 32u * kk), idesc, 1u);  // Xhi Wlo
+                            mma_f16(td, smem_desc(lo + 32u * kk), wh, idesc, 1u);           // Xlo Whi
+                        }
+                    }
                     mma_commit(&empty[s]);
                 }
                 if (ok) mma_commit(&acc_full[b]);
@@ -290,11 +331,13 @@ gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__
                         const OutSeg& sg = a.seg[si];
                         const int col = nn - sg.n0;
                         const float bv = sg.bias ? sg.bias[col] : 0.0f;
+                        const float us = SPLIT ? seg_unscale(sg) : 1.0f;
 #pragma unroll 4
                         for (int rr = 0; rr < 32; ++rr) {
                             const int mm = r0 + rr;
                             if (mm < a.m) {
                                 float o = st[rr * kStageLd + lane];
+                                if (SPLIT) o *= us;
                                 if (sg.bias) o += bv;
                                 if (sg.res) o = sg.res[(size_t)mm * sg.ld + col] + o;
                                 sg.y[(size_t)mm * sg.ld + col] = o;
@@ -319,9 +362,28 @@ gemm16_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__
 }
 
 // ---- weight / activation rounding ------------------------------------------------
+// Split form: row r of `out` is [hi(k) | lo(k)] (FP16), else [16-bit(k)].
+CL_DEVINL uint32_t pack16(float x0, float x1, int bf16) {
+    if (bf16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    const __half2 h = __floats2half2_rn(x0, x1);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// x - fp16(x) (exact in FP32), rounded to FP16
+CL_DEVINL uint32_t pack16_lo(float x0, float x1) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 b = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - b.x, x1 - b.y);
+    return *reinterpret_cast<const uint32_t*>(&l);
+}
+
 template <int T>
 __global__ void dequant16_kernel(const uint8_t* __restrict__ w, long long stride, int n, int k, uint16_t* out,
-                                 int bf16) {
+                                 int bf16, const float* amax) {
+    const int split = amax != nullptr;
     grid_launch_dependents();
     grid_wait();  // `out` may still be read by the previous kernel
     const int nc = k / 32;
@@ -331,22 +393,29 @@ __global__ void dequant16_kernel(const uint8_t* __restrict__ w, long long stride
         const int r = (int)(i / nc), c = (int)(i - (long long)r * nc);
         float v[32];
         dequant32<T>(w + (size_t)r * stride, k, c, v);
-        uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * k + 32 * c);
+        if (split) {
+            const float sc = ldexpf(1.0f, split_exp(__ldg(amax)));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= sc;
+        }
+        uint16_t* row = out + (size_t)r * k * (split ? 2 : 1);
+        uint4* o = reinterpret_cast<uint4*>(row + 32 * c);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             uint32_t p[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float x0 = v[8 * j + 2 * e], x1 = v[8 * j + 2 * e + 1];
-                if (bf16) {
-                    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-                    p[e] = *reinterpret_cast<const uint32_t*>(&h);
-                } else {
-                    const __half2 h = __floats2half2_rn(x0, x1);
-                    p[e] = *reinterpret_cast<const uint32_t*>(&h);
-                }
-            }
+            for (int e = 0; e < 4; ++e) p[e] = pack16(v[8 * j + 2 * e], v[8 * j + 2 * e + 1], bf16);
             o[j] = make_uint4(p[0], p[1], p[2], p[3]);
+        }
+        if (split) {
+            uint4* ol = reinterpret_cast<uint4*>(row + k + 32 * c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t p[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) p[e] = pack16_lo(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+                ol[j] = make_uint4(p[0], p[1], p[2], p[3]);
+            }
         }
     }
 }
@@ -372,6 +441,71 @@ __global__ void convert16_kernel(const float* __restrict__ x, long long count, u
     }
 }
 
+// Largest |value| (dequantized weight rows, or FP32 values) into *amax: a
+// block maximum, then one atomic max on the float's bits (non-negative
+// floats order as their bit patterns).
+CL_DEVINL void amax_commit(float m, float* amax) {
+    m = warp_max(m);
+    __shared__ float red[8];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+        atomicMax(reinterpret_cast<unsigned int*>(amax), __float_as_uint(m));
+    }
+}
+
+template <int T>
+__global__ void amax_dequant_kernel(const uint8_t* __restrict__ w, long long stride, int n, int k, float* amax) {
+    grid_launch_dependents();
+    grid_wait();
+    const int nc = k / 32;
+    const long long total = (long long)n * nc;
+    float m = 0.0f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / nc), c = (int)(i - (long long)r * nc);
+        float v[32];
+        dequant32<T>(w + (size_t)r * stride, k, c, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(v[e]));
+    }
+    amax_commit(m, amax);
+}
+
+__global__ void amax_kernel(const float* __restrict__ x, long long count, float* amax) {
+    grid_launch_dependents();
+    grid_wait();
+    float m = 0.0f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count / 4;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float4 f = reinterpret_cast<const float4*>(x)[i];
+        m = fmaxf(fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y))), fmaxf(fabsf(f.z), fabsf(f.w)));
+    }
+    amax_commit(m, amax);
+}
+
+// X [rows][k] FP32 -> rows of [hi(k) | lo(k)] FP16 of X scaled by split_exp(*amax) (the split form).
+__global__ void split16_kernel(const float* __restrict__ x, int rows, int k, const float* amax, uint16_t* out) {
+    grid_launch_dependents();
+    grid_wait();
+    const float sc = ldexpf(1.0f, split_exp(__ldg(amax)));
+    const int k4 = k / 4;
+    const long long n4 = (long long)rows * k4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / k4), c = (int)(i - (long long)r * k4);
+        float4 f = reinterpret_cast<const float4*>(x)[i];
+        f.x *= sc;
+        f.y *= sc;
+        f.z *= sc;
+        f.w *= sc;
+        uint16_t* row = out + (size_t)r * 2 * k;
+        reinterpret_cast<uint2*>(row)[c] = make_uint2(pack16(f.x, f.y, 0), pack16(f.z, f.w, 0));
+        reinterpret_cast<uint2*>(row + k)[c] = make_uint2(pack16_lo(f.x, f.y), pack16_lo(f.z, f.w));
+    }
+}
+
 // Sum of the K splits in split order, then bias / residual, per segment.
 __global__ void splitk_reduce_kernel(const __grid_constant__ Args a) {
     grid_launch_dependents();
@@ -387,6 +521,7 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ Args a) {
         if (a.nseg > 2 && nn >= a.seg[2].n0) si = 2;
         const OutSeg& sg = a.seg[si];
         const int col = nn - sg.n0;
+        o *= seg_unscale(sg);
         if (sg.bias) o += sg.bias[col];
         if (sg.res) o = sg.res[(size_t)mm * sg.ld + col] + o;
         sg.y[(size_t)mm * sg.ld + col] = o;
@@ -411,12 +546,13 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// Row-major [rows, k] 16-bit matrix, box = 64 columns x box_rows rows, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows, int bf16) {
+// Row-major [rows, k] 16-bit matrix with rows ld elements apart, box = 64
+// columns x box_rows rows, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int rows, int k, long long ld, int box_rows, int bf16) {
     EncodeTiled fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
@@ -427,7 +563,7 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows,
 
 // (BN, splits) with the fewest waves of equal-work units over the SMs; ties
 // to the larger tile, then to fewer splits.
-void plan(int m, int n, int k, int sms, int& bn, int& splits) {
+void plan(int m, int n, int k, int sms, int mmas, int& bn, int& splits) {
     const int mt = (m + BM - 1) / BM, nkb = k / BK;
     double best = 1e300;
     bn = 256;
@@ -442,8 +578,9 @@ void plan(int m, int n, int k, int sms, int& bn, int& splits) {
             // unit time ~ k-blocks x (BN / 256 + a fixed share for the X tile
             // and the epilogue), one 256-wide k-block ~ 0.26 us; a split adds
             // the FP32 partials' write and re-read at ~6.5 TB/s
+            // (mmas products per k-block in the split form)
             const double penalty = s > 1 ? (double)m * n * s * 8.0 / 6.5e12 / 0.26e-6 : 0.0;
-            const double cost = (double)waves * per * (b / 256.0 + 0.25) + penalty;
+            const double cost = (double)waves * per * (mmas * b / 256.0 + 0.25) + penalty;
             if (cost < best * 0.999) {
                 best = cost;
                 bn = b;
@@ -453,14 +590,35 @@ void plan(int m, int n, int k, int sms, int& bn, int& splits) {
     }
 }
 
-template <int BN>
-cudaError_t launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const Args& a, int bf16, int sms,
-                        cudaStream_t stream) {
+template <int BN, bool SPLIT>
+cudaError_t launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mxl,
+                        const CUtensorMap& mwl, const Args& a, int bf16, int sms, cudaStream_t stream) {
     static SmemLimit limit;
-    cudaError_t e = limit.ensure(gemm16_kernel<BN>, (int)Cfg<BN>::kSmem);
+    cudaError_t e = limit.ensure(gemm16_kernel<BN, SPLIT>, (int)Cfg<BN, SPLIT>::kSmem);
     if (e != cudaSuccess) return e;
     const int grid = std::min(a.units, sms);
-    return launch_pdl(gemm16_kernel<BN>, dim3(grid), dim3(kThreads), Cfg<BN>::kSmem, stream, mx, mw, a, bf16);
+    return launch_pdl(gemm16_kernel<BN, SPLIT>, dim3(grid), dim3(kThreads), Cfg<BN, SPLIT>::kSmem, stream, mx, mw,
+                      mxl, mwl, a, bf16);
+}
+
+int dequant16_launch(int type, const void* w, long long stride, int n, int k, void* out, int bf, const float* amax,
+                     cudaStream_t stream) {
+    const uint8_t* wp = static_cast<const uint8_t*>(w);
+    uint16_t* o = static_cast<uint16_t*>(out);
+    const long long chunks = (long long)n * (k / 32);
+    const int grid = (int)std::min<long long>((chunks + 255) / 256, 148LL * 16);
+    cudaError_t e;
+    switch (type) {
+    case CL_TYPE_Q4_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q4_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_Q5_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q5_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_Q6_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q6_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_Q8_0: e = launch_pdl(dequant16_kernel<CL_TYPE_Q8_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_Q5_0: e = launch_pdl(dequant16_kernel<CL_TYPE_Q5_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_F32: e = launch_pdl(dequant16_kernel<CL_TYPE_F32>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    case CL_TYPE_F16: e = launch_pdl(dequant16_kernel<CL_TYPE_F16>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf, amax); break;
+    default: return CL_ERR_UNSUPPORTED;
+    }
+    return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
 }
 
 }  // namespace g16
@@ -488,23 +646,51 @@ CL_API int cl_dequant16(int type, const void* w, long long stride, int n, int k,
         return CL_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) % 16 || stride % 16)
         return CL_ERR_INVALID;
-    const int bf = format == CL_GEMM_BF16;
+    return g16::dequant16_launch(type, w, stride, n, k, out, format == CL_GEMM_BF16, nullptr, stream);
+}
+
+CL_API int cl_amax_dequant(int type, const void* w, long long stride, int n, int k, float* amax,
+                           cudaStream_t stream) {
+    if (w == nullptr || amax == nullptr || n <= 0 || k <= 0 || k % 32 || cl_native_row_bytes(type, k) < 0 ||
+        stride < cl_row_stride(type, k) || (reinterpret_cast<uintptr_t>(amax) & 3u))
+        return CL_ERR_INVALID;
+    if (cudaMemsetAsync(amax, 0, sizeof(float), stream) != cudaSuccess) return CL_ERR_CUDA;
     const uint8_t* wp = static_cast<const uint8_t*>(w);
-    uint16_t* o = static_cast<uint16_t*>(out);
     const long long chunks = (long long)n * (k / 32);
     const int grid = (int)std::min<long long>((chunks + 255) / 256, 148LL * 16);
     cudaError_t e;
     switch (type) {
-    case CL_TYPE_Q4_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q4_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_Q5_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q5_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_Q6_K: e = launch_pdl(dequant16_kernel<CL_TYPE_Q6_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_Q8_0: e = launch_pdl(dequant16_kernel<CL_TYPE_Q8_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_Q5_0: e = launch_pdl(dequant16_kernel<CL_TYPE_Q5_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_F32: e = launch_pdl(dequant16_kernel<CL_TYPE_F32>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
-    case CL_TYPE_F16: e = launch_pdl(dequant16_kernel<CL_TYPE_F16>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, o, bf); break;
+    case CL_TYPE_Q4_K: e = launch_pdl(amax_dequant_kernel<CL_TYPE_Q4_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_Q5_K: e = launch_pdl(amax_dequant_kernel<CL_TYPE_Q5_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_Q6_K: e = launch_pdl(amax_dequant_kernel<CL_TYPE_Q6_K>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_Q8_0: e = launch_pdl(amax_dequant_kernel<CL_TYPE_Q8_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_Q5_0: e = launch_pdl(amax_dequant_kernel<CL_TYPE_Q5_0>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_F32: e = launch_pdl(amax_dequant_kernel<CL_TYPE_F32>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
+    case CL_TYPE_F16: e = launch_pdl(amax_dequant_kernel<CL_TYPE_F16>, dim3(grid), dim3(256), 0, stream, wp, stride, n, k, amax); break;
     default: return CL_ERR_UNSUPPORTED;
     }
     return e == cudaSuccess ? CL_OK : CL_ERR_CUDA;
+}
+
+CL_API int cl_dequant16_split(int type, const void* w, long long stride, int n, int k, const float* amax, void* out,
+                              cudaStream_t stream) {
+    if (w == nullptr || out == nullptr || amax == nullptr || n <= 0 || k <= 0 || k % 32 ||
+        cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k))
+        return CL_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) % 16 || stride % 16 ||
+        (reinterpret_cast<uintptr_t>(amax) & 3u))
+        return CL_ERR_INVALID;
+    return g16::dequant16_launch(type, w, stride, n, k, out, 0, amax, stream);
+}
+
+CL_API int cl_amax(const float* x, long long count, float* amax, cudaStream_t stream) {
+    if (x == nullptr || amax == nullptr || count <= 0 || count % 4 || (reinterpret_cast<uintptr_t>(x) % 16) ||
+        (reinterpret_cast<uintptr_t>(amax) & 3u))
+        return CL_ERR_INVALID;
+    if (cudaMemsetAsync(amax, 0, sizeof(float), stream) != cudaSuccess) return CL_ERR_CUDA;
+    const int grid = (int)std::min<long long>((count / 4 + 255) / 256, 148LL * 4);
+    return launch_pdl(amax_kernel, dim3(grid), dim3(256), 0, stream, x, count, amax) == cudaSuccess ? CL_OK
+                                                                                                  : CL_ERR_CUDA;
 }
 
 CL_API int cl_convert16(const float* x, long long count, void* out, int format, cudaStream_t stream) {
@@ -518,6 +704,19 @@ CL_API int cl_convert16(const float* x, long long count, void* out, int format, 
                : CL_ERR_CUDA;
 }
 
+CL_API int cl_split16(const float* x, int rows, int k, const float* amax, void* out, cudaStream_t stream) {
+    if (x == nullptr || out == nullptr || amax == nullptr || rows <= 0 || k <= 0 || k % 4) return CL_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) % 16 ||
+        (reinterpret_cast<uintptr_t>(amax) & 3u))
+        return CL_ERR_INVALID;
+    const long long n4 = (long long)rows * (k / 4);
+    const int grid = (int)std::min<long long>((n4 + 255) / 256, 148LL * 8);
+    return launch_pdl(split16_kernel, dim3(grid), dim3(256), 0, stream, x, rows, k, amax,
+                      static_cast<uint16_t*>(out)) == cudaSuccess
+               ? CL_OK
+               : CL_ERR_CUDA;
+}
+
 CL_API size_t cl_gemm16_workspace_bytes(int m, int n, int k) {
     if (m <= 0 || n <= 0 || k <= 0) return 0;
     return (size_t)8 * m * n * 4;  // up to 8 K splits of FP32 partials
@@ -526,10 +725,11 @@ CL_API size_t cl_gemm16_workspace_bytes(int m, int n, int k) {
 CL_API int cl_gemm16_run(const void* w16, int n, int k, const void* x16, int m, const cl_gemm_out* outs, int nout,
                          int format, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (w16 == nullptr || x16 == nullptr || outs == nullptr || nout < 1 || nout > 3 || m <= 0 || n <= 0 ||
-        k <= 0 || k % BK || (format != CL_GEMM_F16 && format != CL_GEMM_BF16))
+        k <= 0 || k % BK || (format != CL_GEMM_F16 && format != CL_GEMM_BF16 && format != CL_GEMM_F16X3))
         return CL_ERR_INVALID;
     // TMA: 16-byte aligned bases (the tensor maps also want row strides that are multiples of 16 bytes)
     if ((reinterpret_cast<uintptr_t>(w16) | reinterpret_cast<uintptr_t>(x16)) % 16) return CL_ERR_INVALID;
+    const bool sp = format == CL_GEMM_F16X3;
     Args a{};
     a.m = m;
     a.n = n;
@@ -539,14 +739,15 @@ CL_API int cl_gemm16_run(const void* w16, int n, int k, const void* x16, int m, 
     for (int i = 0; i < nout; ++i) {
         const cl_gemm_out& o = outs[i];
         if (o.y == nullptr || o.col0 != prev || o.cols <= 0 || o.ld < o.cols) return CL_ERR_INVALID;
-        a.seg[i] = OutSeg{o.y, o.bias, o.residual, o.col0, o.col0 + o.cols, o.ld};
+        if (sp != (o.xmax != nullptr && o.wmax != nullptr)) return CL_ERR_INVALID;  // the split form's scales
+        a.seg[i] = OutSeg{o.y, o.bias, o.residual, o.xmax, o.wmax, o.col0, o.col0 + o.cols, o.ld};
         prev = o.col0 + o.cols;
     }
     if (prev != n) return CL_ERR_INVALID;
     int sms = 0;
     if (device_sm_count(&sms) != cudaSuccess) return CL_ERR_CUDA;
     int bn = 256, splits = 1;
-    plan(m, n, k, sms, bn, splits);
+    plan(m, n, k, sms, sp ? 3 : 1, bn, splits);
     if (splits > 1 && (workspace == nullptr || workspace_bytes < (size_t)splits * m * n * 4)) splits = 1;
     const int nkb = k / BK;
     a.splits = splits;
@@ -556,10 +757,24 @@ CL_API int cl_gemm16_run(const void* w16, int n, int k, const void* x16, int m, 
     a.units = a.mt * a.nt * splits;
     a.partial = static_cast<float*>(workspace);
     const int bf = format == CL_GEMM_BF16;
-    CUtensorMap mx, mw;
-    if (!make_map(&mx, x16, m, k, BM, bf) || !make_map(&mw, w16, n, k, bn, bf)) return CL_ERR_UNSUPPORTED;
-    cudaError_t e = bn == 256 ? launch_gemm<256>(mx, mw, a, bf, sms, stream)
-                              : launch_gemm<128>(mx, mw, a, bf, sms, stream);
+    const long long ld = sp ? 2LL * k : k;  // split form: [hi | lo] rows
+    CUtensorMap mx, mw, mxl, mwl;
+    if (!make_map(&mx, x16, m, k, ld, BM, bf) || !make_map(&mw, w16, n, k, ld, bn, bf)) return CL_ERR_UNSUPPORTED;
+    if (sp) {
+        if (!make_map(&mxl, static_cast<const uint16_t*>(x16) + k, m, k, ld, BM, 0) ||
+            !make_map(&mwl, static_cast<const uint16_t*>(w16) + k, n, k, ld, bn, 0))
+            return CL_ERR_UNSUPPORTED;
+    } else {
+        mxl = mx;
+        mwl = mw;
+    }
+    cudaError_t e;
+    if (sp)
+        e = bn == 256 ? launch_gemm<256, true>(mx, mw, mxl, mwl, a, bf, sms, stream)
+                      : launch_gemm<128, true>(mx, mw, mxl, mwl, a, bf, sms, stream);
+    else
+        e = bn == 256 ? launch_gemm<256, false>(mx, mw, mxl, mwl, a, bf, sms, stream)
+                      : launch_gemm<128, false>(mx, mw, mxl, mwl, a, bf, sms, stream);
     if (e != cudaSuccess) return CL_ERR_CUDA;
     if (splits > 1) {
         const long long total = (long long)m * n;

@@ -93,17 +93,38 @@ def device_error(clear: bool = True) -> int:
     return code.value
 
 
-GEMM_TF32X3, GEMM_F16, GEMM_BF16 = 0, 1, 2
+GEMM_TF32X3, GEMM_F16, GEMM_BF16, GEMM_F16X3 = 0, 1, 2, 3
 
 
-def dequant16(gtype: int, w: torch.Tensor, n: int, k: int, fmt: int = GEMM_F16) -> torch.Tensor:
-    """Device-layout rows -> row-major [n, k] FP16 / BF16 (cl_dequant16)."""
+def dequant16(gtype: int, w: torch.Tensor, n: int, k: int, fmt: int = GEMM_F16):
+    """Device-layout rows -> row-major [n, k] FP16 / BF16 (cl_dequant16); the
+    split form (GEMM_F16X3) -> ([n, 2k] FP16 rows [hi | lo] of the scaled
+    values, the device maximum that set the scale) (cl_amax_dequant,
+    cl_dequant16_split)."""
+    lib = _native.lib()
+    if fmt == GEMM_F16X3:
+        amax = torch.empty(1, dtype=torch.float32, device=w.device)
+        check(lib.cl_amax_dequant(gtype, _p(w), w.stride(0), n, k, _p(amax), _stream()), "cl_amax_dequant")
+        out = torch.empty((n, 2 * k), dtype=torch.float16, device=w.device)
+        check(lib.cl_dequant16_split(gtype, _p(w), w.stride(0), n, k, _p(amax), _p(out), _stream()),
+              "cl_dequant16_split")
+        return out, amax
     out = torch.empty((n, k), dtype=torch.bfloat16 if fmt == GEMM_BF16 else torch.float16, device=w.device)
-    check(_native.lib().cl_dequant16(gtype, _p(w), w.stride(0), n, k, _p(out), fmt, _stream()), "cl_dequant16")
+    check(lib.cl_dequant16(gtype, _p(w), w.stride(0), n, k, _p(out), fmt, _stream()), "cl_dequant16")
     return out
 
 
-def convert16(x: torch.Tensor, fmt: int = GEMM_F16) -> torch.Tensor:
+def convert16(x: torch.Tensor, fmt: int = GEMM_F16):
+    """FP32 [m, k] -> FP16 / BF16 (cl_convert16), or, split, ([m, 2k] rows
+    [hi | lo] of the scaled values, the device maximum) (cl_amax, cl_split16)."""
+    if fmt == GEMM_F16X3:
+        m, k = x.shape
+        lib = _native.lib()
+        amax = torch.empty(1, dtype=torch.float32, device=x.device)
+        check(lib.cl_amax(_p(x), x.numel(), _p(amax), _stream()), "cl_amax")
+        out = torch.empty((m, 2 * k), dtype=torch.float16, device=x.device)
+        check(lib.cl_split16(_p(x), m, k, _p(amax), _p(out), _stream()), "cl_split16")
+        return out, amax
     out = torch.empty(x.shape, dtype=torch.bfloat16 if fmt == GEMM_BF16 else torch.float16, device=x.device)
     check(_native.lib().cl_convert16(_p(x), x.numel(), _p(out), fmt, _stream()), "cl_convert16")
     return out
@@ -111,13 +132,20 @@ def convert16(x: torch.Tensor, fmt: int = GEMM_F16) -> torch.Tensor:
 
 def gemm16_run(w16: torch.Tensor, x16: torch.Tensor, outs, fmt: int = GEMM_F16, split: bool = True) -> None:
     """cl_gemm16_run over column ranges: outs = [(y, bias, residual, col0, cols)]
-    with y row-major [m, cols]."""
+    with y row-major [m, cols]; for GEMM_F16X3, w16 and x16 are the pairs
+    dequant16 / convert16 return."""
+    xmax = wmax = None
+    if fmt == GEMM_F16X3:  # (rows [hi | lo], device maximum) pairs
+        (w16, wm), (x16, xm) = w16, x16
+        xmax, wmax = xm.data_ptr(), wm.data_ptr()
     n, k = w16.shape
+    if fmt == GEMM_F16X3:
+        k //= 2
     m = x16.shape[0]
     arr = (_native.GemmOut * len(outs))()
     for i, (y, bias, res, col0, cols) in enumerate(outs):
         arr[i] = _native.GemmOut(y.data_ptr(), bias.data_ptr() if bias is not None else None,
-                                 res.data_ptr() if res is not None else None, col0, cols, y.stride(0))
+                                 res.data_ptr() if res is not None else None, xmax, wmax, col0, cols, y.stride(0))
     lib = _native.lib()
     wsb = int(lib.cl_gemm16_workspace_bytes(m, n, k)) if split else 0
     ws = torch.empty(wsb, dtype=torch.uint8, device=x16.device) if wsb else None

@@ -26,7 +26,12 @@ def rel(a, b):
 
 # Logit tolerance per prefill GEMM path: FP32-grade paths 1e-4, the 16-bit
 # paths the north-star 1e-2.
-PREFILL_TOL = {"tf32x3": 1e-4, "simt": 1e-4, "fp16": 1e-2, "bf16": 1e-2, "f16": 1e-2}
+# Logit bars (max-abs relative).  The FP32-grade paths: split TF32 and the
+# FP32 CUDA cores at 1e-4; split FP16 (three tcgen05 MMAs per step) at 5e-4,
+# its accumulation over long K in the tensor cores' FP32 adders putting the
+# 7B's logits at ~1.5e-4 of the CPU's (tokens identical); the one-pass 16-bit
+# paths at the north-star 1e-2.
+PREFILL_TOL = {"fp16x3": 5e-4, "tf32x3": 1e-4, "simt": 1e-4, "fp16": 1e-2, "bf16": 1e-2, "f16": 1e-2}
 
 
 @pytest.fixture(scope="module")
@@ -41,7 +46,7 @@ def tiny_models(model_dir, cuda):
     return paths
 
 
-@pytest.mark.parametrize("prefill", ["tf32x3", "fp16"])
+@pytest.mark.parametrize("prefill", ["fp16x3", "tf32x3", "fp16"])
 @pytest.mark.parametrize("seed", [7, 11])
 @pytest.mark.parametrize("n", [8, 40])
 def test_tiny_parity(tiny_models, monkeypatch, seed, n, prefill):
@@ -148,7 +153,7 @@ def test_bad_model_files(tmp_path, cuda):
         CudaLLM(str(full), max_sequence=10**6)
 
 
-@pytest.mark.parametrize("prefill", ["tf32x3", "fp16"])
+@pytest.mark.parametrize("prefill", ["fp16x3", "tf32x3", "fp16"])
 def test_qwen2_05b_parity(model_dir, cuda, monkeypatch, prefill):
     """BASELINE config 0 against the reference's tokens and logits."""
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
@@ -174,7 +179,8 @@ def test_qwen2_05b_parity(model_dir, cuda, monkeypatch, prefill):
     llm.close()
 
 
-@pytest.mark.parametrize("mode,prefill", [("fused", "tf32x3"), ("graph", "tf32x3"), ("fused", "fp16")])
+@pytest.mark.parametrize("mode,prefill", [("fused", "fp16x3"), ("graph", "fp16x3"), ("fused", "tf32x3"),
+                                          ("fused", "fp16")])
 def test_qwen2_7b_parity(model_dir, cuda, monkeypatch, mode, prefill):
     """BASELINE config 2 (the bench workload's model, Qwen2.5-7B shape with the
     Q4_K_M layout) against the reference CPULLM's tokens and logits, through
@@ -205,13 +211,16 @@ def test_qwen2_7b_parity(model_dir, cuda, monkeypatch, mode, prefill):
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(GOLDEN, "qwen2_7b_long.npz")),
                     reason="the full-length 7B golden has not been generated")
-@pytest.mark.parametrize("prefill", ["fp16", "tf32x3"])
+@pytest.mark.parametrize("prefill", ["fp16x3", "tf32x3"])
 def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, prefill):
     """The bench workload end to end: the 512-token prompt
     bench.py prefills, then 128 greedy decodes against a 4096-slot cache, on
-    the default decode path (and the default, FP16, prefill GEMM: what
-    bench.py times).  Every token identical to CPULLM's; logits (the
-    reference's top 64 and every 16th) within the path's bar."""
+    the default decode path (and the default prefill GEMM, split FP16 on the
+    tensor cores: what bench.py times; and split TF32).  Every token
+    identical to CPULLM's; logits (the reference's top 64 and every 16th)
+    within the path's bar.  (The one-pass FP16 prefill is not held to this:
+    at decode 76 the reference's two best logits are 0.2 % of the largest
+    apart, within that path's rounding.)"""
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     d = np.load(os.path.join(GOLDEN, "qwen2_7b_long.npz"))
     assert int(d["cpullm_checked"]) == 1, "fixture not cross-checked against CPULLM itself"
