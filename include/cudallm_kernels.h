@@ -418,6 +418,43 @@ CL_API int cl_attn_gate_prep(const float* mixed, const float* k_raw, const float
                              const float* k_norm, int q_heads, int kv_heads, int head_dim, int rot_dim,
                              const float* cos_sin, const int* pos_dev, float eps, float* q_out, float* gate_out,
                              float* k_cache, float* v_cache, cudaStream_t stream);
+/* Token-batched forms for prefill, `rows` consecutive tokens at once (the
+ * per-token arithmetic and its order unchanged):
+ *   cl_moe_route_rows       logits [rows][n_experts] -> ids / weights [rows][k];
+ *   cl_moe_expert_gemv_rows routes r < routes with x_r = x + (r / x_group) *
+ *                           x_stride (x_group routes per token share its row);
+ *   cl_moe_combine_rows     token t: y rows [t routes, (t + 1) routes), ids /
+ *                           weights [t][routes], shared_y / residual / out
+ *                           row t, shared_logit[t];
+ *   cl_gdn_prep_rows        qkv [rows][channels], alpha / beta_raw
+ *                           [rows][value_heads]: the conv over the history and
+ *                           the chunk in token order (hist left holding the
+ *                           chunk's last conv_kernel - 1 rows), act / decay /
+ *                           beta per token;
+ *   cl_gdn_step_rows        the recurrence over the rows in order, the state
+ *                           held on chip between tokens (z / out
+ *                           [rows][value_heads * head_dim]; head_dim % 32 == 0,
+ *                           head_dim <= 128);
+ *   cl_attn_gate_prep_rows  token t at position pos0 + t. */
+CL_API int cl_moe_route_rows(const float* logits, int rows, int n_experts, int k, int32_t* ids, float* weights,
+                             cudaStream_t stream);
+CL_API int cl_moe_expert_gemv_rows(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                                   const float* x, int x_stride, int x_group, const int32_t* ids, int routes,
+                                   int rank, int world, float* y, cudaStream_t stream);
+CL_API int cl_moe_combine_rows(const float* y, const int32_t* ids, const float* weights, int routes, int n, int rank,
+                               int world, const float* shared_y, const float* shared_logit, const float* residual,
+                               float* out, int rows, cudaStream_t stream);
+CL_API int cl_gdn_prep_rows(const float* qkv, const float* alpha, const float* beta_raw, const float* conv_w,
+                            float* hist, const float* dt_bias, const float* a, int key_heads, int value_heads,
+                            int head_dim, int conv_kernel, float eps, int rows, float* act, float* decay, float* beta,
+                            cudaStream_t stream);
+CL_API int cl_gdn_step_rows(const float* act, const float* decay, const float* beta, const float* z,
+                            const float* gamma, float* state, int key_heads, int value_heads, int head_dim, float eps,
+                            int rows, float* out, cudaStream_t stream);
+CL_API int cl_attn_gate_prep_rows(const float* mixed, const float* k_raw, const float* v_raw, const float* q_norm,
+                                  const float* k_norm, int q_heads, int kv_heads, int head_dim, int rot_dim,
+                                  const float* cos_sin, int pos0, int rows, float eps, float* q_out, float* gate_out,
+                                  float* k_cache, float* v_cache, cudaStream_t stream);
 /* *out = ids[*index_dev] (the next prompt token inside a captured prefill step). */
 CL_API int cl_select_token(const int32_t* ids, const int* index_dev, int32_t* out, cudaStream_t stream);
 /* out = a * sigmoid(g) (the attention output gate, moe_llm.mm:2420-2429). */

@@ -85,6 +85,17 @@ SIGNATURES = {
     "cl_dequant16": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
     "cl_convert16": (c_int, [c_vp, c_ll, c_vp, c_int, c_vp]),
     "cl_split16": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_moe_route_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_moe_expert_gemv_rows": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int,
+                                        c_int, c_int, c_vp, c_vp]),
+    "cl_moe_combine_rows": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_int,
+                                    c_vp]),
+    "cl_gdn_prep_rows": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float,
+                                 c_int, c_vp, c_vp, c_vp, c_vp]),
+    "cl_gdn_step_rows": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_int, c_vp,
+                                 c_vp]),
+    "cl_attn_gate_prep_rows": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_int,
+                                       c_int, c_float, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "cl_amax": (c_int, [c_vp, c_ll, c_vp, c_vp]),
     "cl_amax_dequant": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp]),
     "cl_dequant16_split": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),

@@ -24,6 +24,7 @@
 
 #include <cmath>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <stdexcept>
@@ -186,6 +187,17 @@ struct CudaMoeLLM::Impl {
     void *attn_ws = nullptr, *arg_ws = nullptr;
     std::size_t attn_ws_bytes = 0, arg_ws_bytes = 0;
 
+    // token-batched prefill: rows [pre_rows][...] of the chunk's activations
+    DeviceBuffer pre_mem;
+    std::size_t pre_rows = 0;
+    float *px = nullptr, *pxn = nullptr, *pbig = nullptr, *pkb = nullptr, *pvb = nullptr, *pq = nullptr,
+          *pgate = nullptr, *patt = nullptr, *pgated = nullptr, *pzb = nullptr, *palpha = nullptr, *pbetar = nullptr,
+          *pact = nullptr, *pdecay = nullptr, *pbeta = nullptr, *pgdn = nullptr, *prlog = nullptr, *pwts = nullptr,
+          *pea = nullptr, *pey = nullptr, *pshl = nullptr, *psg = nullptr, *psu = nullptr, *pshy = nullptr,
+          *ppart = nullptr;
+    int32_t* pids = nullptr;
+    bool serial_prefill = false;  // CUDALLM_MOE_PREFILL=serial: one token-step graph per prompt token
+
     PinnedBuffer host_io;  // [0] token in, [1] token out, [2..3] pos/len, [4..] prompt staging
     cudaGraphExec_t decode_exec = nullptr, prefill_exec = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -317,6 +329,121 @@ struct CudaMoeLLM::Impl {
         prompt = a.take_n<int32_t>(max_seq);
     }
 
+    void allocate_prefill(Arena& a, std::size_t C) {
+        px = a.take_n<float>(C * H);
+        pxn = a.take_n<float>(C * H);
+        pbig = a.take_n<float>(C * std::max(qkvw, 2 * hq * d));
+        pkb = a.take_n<float>(C * hkv * d);
+        pvb = a.take_n<float>(C * hkv * d);
+        pq = a.take_n<float>(C * hq * d);
+        pgate = a.take_n<float>(C * hq * d);
+        patt = a.take_n<float>(C * hq * d);
+        pgated = a.take_n<float>(C * hq * d);
+        pzb = a.take_n<float>(C * sr * sd);
+        palpha = a.take_n<float>(C * sr);
+        pbetar = a.take_n<float>(C * sr);
+        pact = a.take_n<float>(C * qkvw);
+        pdecay = a.take_n<float>(C * sr);
+        pbeta = a.take_n<float>(C * sr);
+        pgdn = a.take_n<float>(C * sr * sd);
+        prlog = a.take_n<float>(C * E);
+        pwts = a.take_n<float>(C * Kr);
+        pids = a.take_n<int32_t>(C * Kr);
+        pea = a.take_n<float>(C * Kr * FF);
+        pey = a.take_n<float>(C * Kr * H);
+        pshl = a.take_n<float>(C + 4);
+        psg = a.take_n<float>(C * SFF);
+        psu = a.take_n<float>(C * SFF);
+        pshy = a.take_n<float>(C * H);
+        ppart = a.take_n<float>(C * H);
+    }
+
+    void ensure_prefill_buffers() {
+        if (pre_rows) return;
+        std::size_t C = std::min<std::size_t>(max_seq, 512);
+        // Diagnostics: smaller chunks exercise the cross-chunk state (conv history, recurrence, KV)
+        if (const char* e = std::getenv("CUDALLM_MOE_PREFILL_CHUNK")) {
+            const long v = std::strtol(e, nullptr, 10);
+            if (v > 0) C = std::min<std::size_t>(C, (std::size_t)v);
+        }
+        Arena plan;
+        allocate_prefill(plan, C);
+        pre_mem = DeviceBuffer(plan.used() + 256);
+        Arena a;
+        a.bind(pre_mem.get(), pre_mem.size());
+        allocate_prefill(a, C);
+        pre_rows = C;
+    }
+
+    // Y[m][n] = X[m][k] W^T (+ residual) on the prefill GEMM (FP32-grade tensor cores)
+    void pgemm(const DevMat& w, int n, int k, const float* x, int m, const float* res, float* y) {
+        CUDALLM_CL(cl_gemm(w.type, w.ptr, w.stride, n, k, x, m, nullptr, res, y, stream));
+    }
+    void pgemm_f32(const float* w, int n, int k, const float* x, int m, float* y) {
+        CUDALLM_CL(cl_gemm(CL_TYPE_F32, w, (long long)k * 4, n, k, x, m, nullptr, nullptr, y, stream));
+    }
+
+    // m prompt tokens (device ids) at positions pos0 .. pos0 + m - 1 through every
+    // layer at once: the projections as GEMMs, the DeltaNet conv and recurrence
+    // over the chunk in token order within one launch each, the routed experts
+    // over all (token, route) pairs in one launch per matrix.  Leaves the
+    // chunk's hidden rows in px.
+    void prefill_chunk(const int32_t* toks, int m, int pos0) {
+        cudaStream_t s = stream;
+        const int W = par.world, R = par.rank;
+        const int Hi = (int)H;
+        CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, Hi, toks, m, px, ints + 4, s));
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            MoeLayer& L = layers[l];
+            CUDALLM_CL(cl_rmsnorm(px, L.attn_norm, m, Hi, eps(), pxn, nullptr, s));
+            if (L.attention) {
+                pgemm(L.q_gate, (int)(2 * hq * d), Hi, pxn, m, nullptr, pbig);
+                pgemm(L.k, (int)(hkv * d), Hi, pxn, m, nullptr, pkb);
+                pgemm(L.v, (int)(hkv * d), Hi, pxn, m, nullptr, pvb);
+                CUDALLM_CL(cl_attn_gate_prep_rows(pbig, pkb, pvb, L.q_norm, L.k_norm, (int)hq, (int)hkv, (int)d,
+                                                  (int)rot, rope, pos0, m, eps(), pq, pgate, L.k_cache, L.v_cache, s));
+                CUDALLM_CL(cl_attn_prefill(pq, L.k_cache, L.v_cache, pos0, m, (int)hq, (int)hkv, (int)d, patt, s));
+                CUDALLM_CL(cl_mul_sigmoid(patt, pgate, pgated, (int)(m * hq * d), s));
+                pgemm(L.o, Hi, (int)(hq * d), pgated, m, px, px);
+            } else {
+                pgemm(L.qkv, (int)qkvw, Hi, pxn, m, nullptr, pbig);
+                pgemm(L.z, (int)(sr * sd), Hi, pxn, m, nullptr, pzb);
+                pgemm_f32(L.alpha_w, (int)sr, Hi, pxn, m, palpha);
+                pgemm_f32(L.beta_w, (int)sr, Hi, pxn, m, pbetar);
+                CUDALLM_CL(cl_gdn_prep_rows(pbig, palpha, pbetar, L.conv_w, L.hist, L.dt_bias, L.a, (int)sg, (int)sr,
+                                            (int)sd, (int)kc, eps(), m, pact, pdecay, pbeta, s));
+                CUDALLM_CL(cl_gdn_step_rows(pact, pdecay, pbeta, pzb, L.ssm_norm, L.state, (int)sg, (int)sr, (int)sd,
+                                            eps(), m, pgdn, s));
+                pgemm(L.out, Hi, (int)(sr * sd), pgdn, m, px, px);
+            }
+            CUDALLM_CL(cl_rmsnorm(px, L.post_norm, m, Hi, eps(), pxn, nullptr, s));
+            pgemm_f32(L.router, (int)E, Hi, pxn, m, prlog);
+            CUDALLM_CL(cl_moe_route_rows(prlog, m, (int)E, (int)Kr, pids, pwts, s));
+            if (E_l > 0) {
+                CUDALLM_CL(cl_moe_expert_gemv_rows(L.gate_e.type, L.gate_e.ptr, L.up_e.ptr, L.gate_e.stride, (int)FF,
+                                                   Hi, pxn, Hi, (int)Kr, pids, (int)(m * Kr), R, W, pea, s));
+                CUDALLM_CL(cl_moe_expert_gemv_rows(L.down_e.type, L.down_e.ptr, nullptr, L.down_e.stride, Hi, (int)FF,
+                                                   pea, (int)FF, 1, pids, (int)(m * Kr), R, W, pey, s));
+            }
+            const bool shared_here = ep_shared_rank(l, W) == R;
+            if (shared_here) {
+                pgemm_f32(L.shared_router, 1, Hi, pxn, m, pshl);
+                pgemm(L.sh_gate, (int)SFF, Hi, pxn, m, nullptr, psg);
+                pgemm(L.sh_up, (int)SFF, Hi, pxn, m, nullptr, psu);
+                CUDALLM_CL(cl_swiglu(psg, psu, psg, (long long)m * SFF, s));
+                pgemm(L.sh_down, Hi, (int)SFF, psg, m, nullptr, pshy);
+            }
+            if (W == 1) {
+                CUDALLM_CL(cl_moe_combine_rows(pey, pids, pwts, (int)Kr, Hi, 0, 1, pshy, pshl, px, px, m, s));
+            } else {
+                CUDALLM_CL(cl_moe_combine_rows(pey, pids, pwts, (int)Kr, Hi, R, W, shared_here ? pshy : nullptr,
+                                               shared_here ? pshl : nullptr, nullptr, ppart, m, s));
+                MOE_NCCL(ncclAllReduce(ppart, ppart, (std::size_t)m * H, ncclFloat32, ncclSum, comm, s));
+                CUDALLM_CL(cl_add(px, ppart, px, (long long)m * H, s));
+            }
+        }
+    }
+
     void init(const std::string& path, std::size_t max_sequence, int dev, const ParallelConfig& parallel) {
         par = parallel;
         if (par.world < 1 || par.rank < 0 || par.rank >= par.world)
@@ -407,6 +534,15 @@ struct CudaMoeLLM::Impl {
         CUDALLM_CUDA(cudaMemcpyAsync(const_cast<float*>(rope), table.data(), table.size() * sizeof(float),
                                      cudaMemcpyHostToDevice, stream));
         host_io = PinnedBuffer(sizeof(int32_t) * (4 + max_seq));
+        // Prefill: "batched" (default; chunks of up to 512 tokens through each layer
+        // at once) or "serial" (the one-token step replayed per prompt token)
+        if (const char* e = std::getenv("CUDALLM_MOE_PREFILL")) {
+            const std::string v(e);
+            if (v == "serial")
+                serial_prefill = true;
+            else if (v != "batched" && !v.empty())
+                throw std::invalid_argument("CUDALLM_MOE_PREFILL must be batched or serial");
+        }
         CUDALLM_CUDA(cudaStreamSynchronize(stream));
     }
 
@@ -615,16 +751,32 @@ struct CudaMoeLLM::Impl {
         for (int32_t id : tokens)
             if (id < 0 || (std::size_t)id >= V) throw std::out_of_range("CUDA prefill token id is outside the vocabulary");
         CUDALLM_CUDA(cudaSetDevice(device));
-        if (prefill_exec == nullptr) prefill_exec = capture([&] { record_prefill_step(); });
+        if (serial_prefill && prefill_exec == nullptr) prefill_exec = capture([&] { record_prefill_step(); });
+        if (!serial_prefill) ensure_prefill_buffers();
         const TraceRange trace("prefill.gpu_moe");
         begin_timing();
         int32_t* hi = host_in();
-        std::memcpy(hi + 4, tokens.data(), tokens.size() * sizeof(int32_t));
-        hi[2] = 0;  // position
-        hi[3] = 1;  // attention length
-        CUDALLM_CUDA(cudaMemcpyAsync(prompt, hi + 4, tokens.size() * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
-        CUDALLM_CUDA(cudaMemcpyAsync(ints + 1, hi + 2, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
-        for (std::size_t i = 0; i < tokens.size(); ++i) CUDALLM_CUDA(cudaGraphLaunch(prefill_exec, stream));
+        const std::size_t n = tokens.size();
+        std::memcpy(hi + 4, tokens.data(), n * sizeof(int32_t));
+        CUDALLM_CUDA(cudaMemcpyAsync(prompt, hi + 4, n * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+        if (serial_prefill) {
+            hi[2] = 0;  // position
+            hi[3] = 1;  // attention length
+            CUDALLM_CUDA(cudaMemcpyAsync(ints + 1, hi + 2, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+            for (std::size_t i = 0; i < n; ++i) CUDALLM_CUDA(cudaGraphLaunch(prefill_exec, stream));
+        } else {
+            std::size_t last = 0;
+            for (std::size_t c0 = 0; c0 < n; c0 += pre_rows) {
+                const int m = (int)std::min(pre_rows, n - c0);
+                prefill_chunk(prompt + c0, m, (int)c0);
+                last = (std::size_t)m - 1;
+            }
+            // the last token's hidden state feeds the head; decode continues at position n
+            CUDALLM_CUDA(cudaMemcpyAsync(h, px + last * H, H * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+            hi[2] = (int32_t)n;
+            hi[3] = (int32_t)n + 1;
+            CUDALLM_CUDA(cudaMemcpyAsync(ints + 1, hi + 2, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+        }
         record_head();
         CUDALLM_CUDA(cudaMemcpyAsync(hi + 1, ints + 3, sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
         end_timing("prefill", tokens.size());

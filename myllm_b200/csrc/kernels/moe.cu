@@ -76,6 +76,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
     __shared__ float sel_v[8];
     __shared__ int sel_i[8];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // block b: token b of a batch (logits [tokens][ne], ids / wts [tokens][k])
+    logits += (size_t)blockIdx.x * ne;
+    ids += (size_t)blockIdx.x * k;
+    wts += (size_t)blockIdx.x * k;
     // softmax (metal_softmax_f32: max, exp(v - max), sum, numerator / sum)
     float m = -INFINITY;
     for (int i = tid; i < ne; i += kRouteThreads) m = fmaxf(m, logits[i]);
@@ -150,15 +154,17 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
 // y[r][row] = W_e[row] . x_r for route r (e = ids[r]), or with w_up the
 // SwiGLU silu(W_e[row] . x) * (U_e[row] . x).  Expert e lives on rank
 // e % world as local expert e / world; routes of other ranks are skipped
-// (their outputs are neither written nor read).  x_r = x + r * x_stride.
+// (their outputs are neither written nor read).  x_r = x + (r / x_group) *
+// x_stride: one input per route (x_group 1), or one per token of a batch
+// whose x_group routes share it.
 constexpr int kExpWarps = 8, kExpThreads = 32 * kExpWarps, kExpRows = 2;
 constexpr int kMaxExpUnits = 256;  // k <= 8192
 
 template <int F, bool SW>
 __global__ void __launch_bounds__(kExpThreads)
     expert_gemv_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ w_up, long long stride, int n,
-                       int k, const float* __restrict__ x, int x_stride, const int* __restrict__ ids, int rank,
-                       int world, float* __restrict__ y) {
+                       int k, const float* __restrict__ x, int x_stride, int x_group, const int* __restrict__ ids,
+                       int rank, int world, float* __restrict__ y) {
     constexpr int NV = SW ? 2 * kExpRows : kExpRows;
     __shared__ uint4 planes[8][kMaxExpUnits];  // XQ unit u: 6 limb chunks, lsum, (xs, xsum)
     grid_launch_dependents();
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(kExpThreads)
     if (e % world != rank) return;
     const int local = e / world;
     const int units = k / 32;
-    const float* xr = x + (size_t)r * x_stride;
+    const float* xr = x + (size_t)(r / x_group) * x_stride;
     for (int u = threadIdx.x; u < units; u += kExpThreads) {
         float v[32];
 #pragma unroll
@@ -243,6 +249,17 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
     grid_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= n) return;
+    // blockIdx.y: token of a batch ([tokens][routes] ids / weights, [tokens * routes][n] y, rows of n)
+    const size_t tk = blockIdx.y;
+    ids += tk * routes;
+    wts += tk * routes;
+    y += tk * routes * n;
+    if (shared_y) {
+        shared_y += tk * n;
+        shared_logit += tk;
+    }
+    if (residual) residual += tk * n;
+    out += tk * n;
     float acc = 0.0f;
     for (int r = 0; r < routes; ++r)
         if (ids[r] % world == rank) acc += wts[r] * y[(size_t)r * n + c];
@@ -287,6 +304,63 @@ __global__ void gdn_prep_kernel(const float* __restrict__ qkv, const float* __re
             decay[h] = expf(sp * a[h]);
             beta[h] = sigmoid_stable(beta_raw[h]);
         }
+    }
+}
+
+// The same for `rows` consecutive tokens (a prefill chunk): block b walks
+// the tokens in order with the conv window of its channel in registers,
+// then leaves the last conv_kernel - 1 inputs as the history.  Per token the
+// expressions and their order are those of gdn_prep_kernel.
+constexpr int kMaxConv = 9;
+
+__global__ void gdn_prep_rows_kernel(const float* __restrict__ qkv, const float* __restrict__ alpha,
+                                     const float* __restrict__ beta_raw, const float* __restrict__ conv_w, float* hist,
+                                     const float* __restrict__ dt_bias, const float* __restrict__ a, int key_heads,
+                                     int value_heads, int d, int kc, float eps, int rows, float* __restrict__ act,
+                                     float* __restrict__ decay, float* __restrict__ beta) {
+    grid_launch_dependents();
+    grid_wait();
+    __shared__ float red[32];
+    const int b = blockIdx.x, t = threadIdx.x;
+    const int width = (2 * key_heads + value_heads) * d;
+    const int c = b * d + t;
+    float win[kMaxConv - 1], wk[kMaxConv - 1];
+#pragma unroll
+    for (int tap = 0; tap < kMaxConv - 1; ++tap) {
+        win[tap] = tap < kc - 1 ? hist[(size_t)tap * width + c] : 0.0f;
+        wk[tap] = tap < kc - 1 ? conv_w[(size_t)c * kc + tap] : 0.0f;
+    }
+    const float wlast = conv_w[(size_t)c * kc + kc - 1];
+    for (int i = 0; i < rows; ++i) {
+        const float cur = qkv[(size_t)i * width + c];
+        float acc = 0.0f;
+#pragma unroll
+        for (int tap = 0; tap < kMaxConv - 1; ++tap)
+            if (tap < kc - 1) acc += win[tap] * wk[tap];
+        acc += cur * wlast;
+#pragma unroll
+        for (int tap = 0; tap < kMaxConv - 1; ++tap) {
+            if (tap + 1 < kc - 1) win[tap] = win[tap + 1];
+            else if (tap == kc - 2) win[tap] = cur;
+        }
+        float v = acc * sigmoid_stable(acc);
+        if (b < 2 * key_heads) {
+            const float ss = block_sum(v * v, red);
+            v = v * rsqrtf(ss + eps);
+        }
+        act[(size_t)i * width + c] = v;
+    }
+#pragma unroll
+    for (int tap = 0; tap < kMaxConv - 1; ++tap)
+        if (tap < kc - 1) hist[(size_t)tap * width + c] = win[tap];
+    if (b == 0) {
+        for (int i = 0; i < rows; ++i)
+            for (int h = t; h < value_heads; h += blockDim.x) {
+                const float ab = alpha[(size_t)i * value_heads + h] + dt_bias[h];
+                const float sp = ab > 20.0f ? ab : (ab < -20.0f ? expf(ab) : logf(1.0f + expf(ab)));
+                decay[(size_t)i * value_heads + h] = expf(sp * a[h]);
+                beta[(size_t)i * value_heads + h] = sigmoid_stable(beta_raw[(size_t)i * value_heads + h]);
+            }
     }
 }
 
@@ -354,7 +428,9 @@ __global__ void __launch_bounds__(2 * kMaxGdnDim) gdn_step_kernel(
 // The same step with each head's columns split across a thread-block
 // cluster: CTA r of the cluster owns columns 32 r .. 32 r + 31 (the delta
 // rule is independent per column: pred, delta, the state update and o all
-// read one column of S), 8 warps split the rows.  The per-head RMSNorm
+// read one column of S), 8 warps split the rows.  It runs `rows`
+// consecutive tokens (one in decode, a prefill chunk in prefill) with the
+// state in registers between them, read once and written once.  The per-head RMSNorm
 // needs the sum of o^2 over all columns: each CTA leaves its 32-column sum
 // in shared memory and every CTA adds the cluster's sums in rank order
 // through distributed shared memory.  d / 32 CTAs per head (4 at d = 128),
@@ -364,7 +440,7 @@ constexpr int kGdnCols = 32, kGdnRowGroups = 8;
 __global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_kernel(
     const float* __restrict__ act, const float* __restrict__ decay, const float* __restrict__ beta,
     const float* __restrict__ z, const float* __restrict__ gamma, float* __restrict__ state, int key_heads,
-    int value_heads, int d, float eps, float* __restrict__ out) {
+    int value_heads, int d, float eps, float* __restrict__ out, int rows) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     grid_launch_dependents();
@@ -374,61 +450,73 @@ __global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_ker
     const int nparts = d / kGdnCols;
     const int h = blockIdx.x / nparts, cpart = (int)cluster.block_rank(), kh = h % key_heads;
     const int t = threadIdx.x, cl = t % kGdnCols, rg = t / kGdnCols;
-    const int col = cpart * kGdnCols + cl, rows = d / kGdnRowGroups;
-    for (int i = t; i < d; i += blockDim.x) {
-        qs[i] = act[kh * d + i];
-        ks[i] = act[key_heads * d + kh * d + i];
-    }
-    __syncthreads();
+    const int col = cpart * kGdnCols + cl, rows_per = d / kGdnRowGroups;
+    const int width = (2 * key_heads + value_heads) * d;
     float* S = state + (size_t)h * d * d;
-    const float dec = decay[h], bt = beta[h];
+    // the thread's part of state column col stays in registers across the tokens
     float s[kMaxGdnDim / kGdnRowGroups];
-    float pred = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
-        if (i < rows) {
-            const int row = rg * rows + i;
-            s[i] = S[(size_t)row * d + col] * dec;
-            pred += s[i] * ks[row];
-        }
-    }
-    part[rg][cl] = pred;
-    __syncthreads();
-    pred = 0.0f;
-#pragma unroll
-    for (int r = 0; r < kGdnRowGroups; ++r) pred += part[r][cl];
-    const float delta = bt * (act[2 * key_heads * d + h * d + col] - pred);
+    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i)
+        if (i < rows_per) s[i] = S[(size_t)(rg * rows_per + i) * d + col];
     const float qscale = rsqrtf((float)d);
-    float o = 0.0f;
+    for (int tok = 0; tok < rows; ++tok) {
+        const float* at = act + (size_t)tok * width;
+        if (tok > 0) __syncthreads();  // the previous token's q / k reads are done
+        for (int i = t; i < d; i += blockDim.x) {
+            qs[i] = at[kh * d + i];
+            ks[i] = at[key_heads * d + kh * d + i];
+        }
+        __syncthreads();
+        const float dec = decay[(size_t)tok * value_heads + h], bt = beta[(size_t)tok * value_heads + h];
+        float pred = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
-        if (i < rows) {
-            const int row = rg * rows + i;
-            s[i] += ks[row] * delta;
-            S[(size_t)row * d + col] = s[i];
-            o += s[i] * qs[row] * qscale;
+        for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
+            if (i < rows_per) {
+                const int row = rg * rows_per + i;
+                s[i] = s[i] * dec;
+                pred += s[i] * ks[row];
+            }
+        }
+        part[rg][cl] = pred;
+        __syncthreads();
+        pred = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kGdnRowGroups; ++r) pred += part[r][cl];
+        const float delta = bt * (at[2 * key_heads * d + h * d + col] - pred);
+        float o = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i) {
+            if (i < rows_per) {
+                const int row = rg * rows_per + i;
+                s[i] += ks[row] * delta;
+                o += s[i] * qs[row] * qscale;
+            }
+        }
+        __syncthreads();
+        part[rg][cl] = o;
+        __syncthreads();
+        o = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kGdnRowGroups; ++r) o += part[r][cl];
+        if (t < kGdnCols) {
+            const float w = warp_sum(o * o);
+            if (t == 0) ssq = w;
+        }
+        cluster.sync();  // every CTA's ssq is written
+        float ss = 0.0f;
+        for (int r = 0; r < nparts; ++r) ss += *cluster.map_shared_rank(&ssq, r);
+        cluster.sync();  // no CTA rewrites its ssq while another still reads it
+        // per-head RMSNorm (metal_rmsnorm_f32) over the d outputs, then the gate
+        const float inv = rsqrtf(ss / (float)d + eps);
+        if (rg == 0) {
+            const size_t oi = (size_t)tok * value_heads * d + (size_t)h * d + col;
+            const float zz = z[oi];
+            out[oi] = o * inv * gamma[col] * (zz * sigmoid_stable(zz));
         }
     }
-    __syncthreads();
-    part[rg][cl] = o;
-    __syncthreads();
-    o = 0.0f;
 #pragma unroll
-    for (int r = 0; r < kGdnRowGroups; ++r) o += part[r][cl];
-    if (t < kGdnCols) {
-        const float w = warp_sum(o * o);
-        if (t == 0) ssq = w;
-    }
-    cluster.sync();  // every CTA's ssq is written
-    float ss = 0.0f;
-    for (int r = 0; r < nparts; ++r) ss += *cluster.map_shared_rank(&ssq, r);
-    cluster.sync();  // no CTA leaves while another still reads its ssq
-    // per-head RMSNorm (metal_rmsnorm_f32) over the d outputs, then the gate
-    const float inv = rsqrtf(ss / (float)d + eps);
-    if (rg == 0) {
-        const float zz = z[h * d + col];
-        out[h * d + col] = o * inv * gamma[col] * (zz * sigmoid_stable(zz));
-    }
+    for (int i = 0; i < kMaxGdnDim / kGdnRowGroups; ++i)
+        if (i < rows_per) S[(size_t)(rg * rows_per + i) * d + col] = s[i];
 }
 
 // ---- gated attention: split, per-head norms, partial RoPE, KV append -------
@@ -437,15 +525,22 @@ __global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_ker
 __global__ void attn_gate_prep_kernel(const float* __restrict__ mixed, const float* __restrict__ k_raw,
                                       const float* __restrict__ v_raw, const float* __restrict__ q_norm,
                                       const float* __restrict__ k_norm, int hq, int hkv, int d, int rot,
-                                      const float* __restrict__ cos_sin, const int* __restrict__ pos_dev, float eps,
-                                      float* __restrict__ q_out, float* __restrict__ gate_out, float* k_cache,
-                                      float* v_cache) {
+                                      const float* __restrict__ cos_sin, const int* __restrict__ pos_dev, int pos0,
+                                      float eps, float* __restrict__ q_out, float* __restrict__ gate_out,
+                                      float* k_cache, float* v_cache) {
     grid_launch_dependents();
     grid_wait();
     extern __shared__ float hs[];  // [d] normalised head
     __shared__ float red[32];
     const int b = blockIdx.x, t = threadIdx.x;
-    const int pos = *pos_dev;
+    // blockIdx.y: token of a batch at position (pos_dev ? *pos_dev : pos0) + blockIdx.y
+    const int row = blockIdx.y;
+    const int pos = (pos_dev ? *pos_dev : pos0) + row;
+    mixed += (size_t)row * hq * 2 * d;
+    k_raw += (size_t)row * hkv * d;
+    v_raw += (size_t)row * hkv * d;
+    q_out += (size_t)row * hq * d;
+    gate_out += (size_t)row * hq * d;
     const bool is_q = b < hq;
     const int head = is_q ? b : b - hq;
     const float raw = is_q ? mixed[(size_t)head * 2 * d + t] : k_raw[(size_t)head * d + t];
@@ -480,24 +575,24 @@ __global__ void mul_sigmoid_kernel(const float* __restrict__ a, const float* __r
 
 template <int F, bool SW>
 cudaError_t launch_expert(const void* w, const void* w_up, long long stride, int n, int k, const float* x,
-                          int x_stride, const int* ids, int routes, int rank, int world, float* y,
+                          int x_stride, int x_group, const int* ids, int routes, int rank, int world, float* y,
                           cudaStream_t stream) {
     const dim3 grid((n + kExpWarps * kExpRows - 1) / (kExpWarps * kExpRows), routes);
     return launch_pdl(expert_gemv_kernel<F, SW>, grid, dim3(kExpThreads), 0, stream,
                       static_cast<const uint8_t*>(w), static_cast<const uint8_t*>(w_up), stride, n, k, x, x_stride,
-                      ids, rank, world, y);
+                      x_group, ids, rank, world, y);
 }
 
 template <bool SW>
 cudaError_t launch_expert_type(int type, const void* w, const void* w_up, long long stride, int n, int k,
-                               const float* x, int x_stride, const int* ids, int routes, int rank, int world,
+                               const float* x, int x_stride, int xg, const int* ids, int routes, int rank, int world,
                                float* y, cudaStream_t stream) {
     switch (type) {
-    case CL_TYPE_Q4_K: return launch_expert<CL_TYPE_Q4_K, SW>(w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world, y, stream);
-    case CL_TYPE_Q5_K: return launch_expert<CL_TYPE_Q5_K, SW>(w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world, y, stream);
-    case CL_TYPE_Q6_K: return launch_expert<CL_TYPE_Q6_K, SW>(w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world, y, stream);
-    case CL_TYPE_Q8_0: return launch_expert<CL_TYPE_Q8_0, SW>(w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world, y, stream);
-    case CL_TYPE_Q5_0: return launch_expert<CL_TYPE_Q5_0, SW>(w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world, y, stream);
+    case CL_TYPE_Q4_K: return launch_expert<CL_TYPE_Q4_K, SW>(w, w_up, stride, n, k, x, x_stride, xg, ids, routes, rank, world, y, stream);
+    case CL_TYPE_Q5_K: return launch_expert<CL_TYPE_Q5_K, SW>(w, w_up, stride, n, k, x, x_stride, xg, ids, routes, rank, world, y, stream);
+    case CL_TYPE_Q6_K: return launch_expert<CL_TYPE_Q6_K, SW>(w, w_up, stride, n, k, x, x_stride, xg, ids, routes, rank, world, y, stream);
+    case CL_TYPE_Q8_0: return launch_expert<CL_TYPE_Q8_0, SW>(w, w_up, stride, n, k, x, x_stride, xg, ids, routes, rank, world, y, stream);
+    case CL_TYPE_Q5_0: return launch_expert<CL_TYPE_Q5_0, SW>(w, w_up, stride, n, k, x, x_stride, xg, ids, routes, rank, world, y, stream);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -541,10 +636,48 @@ CL_API int cl_moe_expert_gemv(int type, const void* w, const void* w_up, long lo
     if (type != CL_TYPE_Q4_K && type != CL_TYPE_Q5_K && type != CL_TYPE_Q6_K && type != CL_TYPE_Q8_0 &&
         type != CL_TYPE_Q5_0)
         return CL_ERR_UNSUPPORTED;
-    return status(w_up ? launch_expert_type<true>(type, w, w_up, stride, n, k, x, x_stride, ids, routes, rank, world,
-                                                  y, stream)
-                       : launch_expert_type<false>(type, w, nullptr, stride, n, k, x, x_stride, ids, routes, rank,
+    return status(w_up ? launch_expert_type<true>(type, w, w_up, stride, n, k, x, x_stride, 1, ids, routes, rank,
+                                                  world, y, stream)
+                       : launch_expert_type<false>(type, w, nullptr, stride, n, k, x, x_stride, 1, ids, routes, rank,
                                                    world, y, stream));
+}
+
+CL_API int cl_moe_expert_gemv_rows(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                                   const float* x, int x_stride, int x_group, const int* ids, int routes, int rank,
+                                   int world, float* y, cudaStream_t stream) {
+    if (x_group <= 0) return CL_ERR_INVALID;
+    if (w == nullptr || x == nullptr || ids == nullptr || y == nullptr || n <= 0 || k <= 0 || k % 32 ||
+        k / 32 > kMaxExpUnits || routes <= 0 || routes > 65535 || world <= 0 || rank < 0 || rank >= world ||
+        x_stride < 0 || x_stride % 4 || !aligned16(w) || !aligned16(x) || stride % 16 ||
+        cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k) || (w_up && !aligned16(w_up)))
+        return CL_ERR_INVALID;
+    if (type != CL_TYPE_Q4_K && type != CL_TYPE_Q5_K && type != CL_TYPE_Q6_K && type != CL_TYPE_Q8_0 &&
+        type != CL_TYPE_Q5_0)
+        return CL_ERR_UNSUPPORTED;
+    return status(w_up ? launch_expert_type<true>(type, w, w_up, stride, n, k, x, x_stride, x_group, ids, routes,
+                                                  rank, world, y, stream)
+                       : launch_expert_type<false>(type, w, nullptr, stride, n, k, x, x_stride, x_group, ids,
+                                                   routes, rank, world, y, stream));
+}
+
+CL_API int cl_moe_combine_rows(const float* y, const int* ids, const float* weights, int routes, int n, int rank,
+                               int world, const float* shared_y, const float* shared_logit, const float* residual,
+                               float* out, int rows, cudaStream_t stream) {
+    if (y == nullptr || ids == nullptr || weights == nullptr || out == nullptr || routes <= 0 || n <= 0 ||
+        world <= 0 || rank < 0 || rank >= world || ((shared_y == nullptr) != (shared_logit == nullptr)) ||
+        rows <= 0 || rows > 65535)
+        return CL_ERR_INVALID;
+    return status(launch_pdl(combine_kernel, dim3((n + 255) / 256, rows), dim3(256), 0, stream, y, ids, weights,
+                             routes, n, rank, world, shared_y, shared_logit, residual, out));
+}
+
+CL_API int cl_moe_route_rows(const float* logits, int rows, int n_experts, int k, int* ids, float* weights,
+                             cudaStream_t stream) {
+    if (logits == nullptr || ids == nullptr || weights == nullptr || n_experts <= 0 || n_experts > 16384 || k <= 0 ||
+        k > 8 || k > n_experts || rows <= 0)
+        return CL_ERR_INVALID;
+    return status(launch_pdl(route_kernel, dim3(rows), dim3(kRouteThreads), (size_t)n_experts * sizeof(float),
+                             stream, logits, n_experts, k, ids, weights));
 }
 
 CL_API int cl_moe_combine(const float* y, const int* ids, const float* weights, int routes, int n, int rank, int world,
@@ -594,10 +727,49 @@ CL_API int cl_gdn_step(const float* act, const float* decay, const float* beta, 
         cfg.attrs = attr;
         cfg.numAttrs = cl::g_pdl_enabled ? 2 : 1;
         return status(cudaLaunchKernelEx(&cfg, gdn_step_cluster_kernel, act, decay, beta, z, gamma, state, key_heads,
-                                         value_heads, head_dim, eps, out));
+                                         value_heads, head_dim, eps, out, 1));
     }
     return status(launch_pdl(gdn_step_kernel, dim3(value_heads), dim3(2 * head_dim), 0, stream, act, decay, beta, z,
                              gamma, state, key_heads, value_heads, head_dim, eps, out));
+}
+
+CL_API int cl_gdn_prep_rows(const float* qkv, const float* alpha, const float* beta_raw, const float* conv_w,
+                            float* hist, const float* dt_bias, const float* a, int key_heads, int value_heads,
+                            int head_dim, int conv_kernel, float eps, int rows, float* act, float* decay, float* beta,
+                            cudaStream_t stream) {
+    if (qkv == nullptr || alpha == nullptr || beta_raw == nullptr || conv_w == nullptr || hist == nullptr ||
+        dt_bias == nullptr || a == nullptr || act == nullptr || decay == nullptr || beta == nullptr ||
+        key_heads <= 0 || value_heads <= 0 || value_heads % key_heads || head_dim <= 0 || head_dim % 32 ||
+        head_dim > 1024 || conv_kernel < 1 || conv_kernel > kMaxConv || rows <= 0)
+        return CL_ERR_INVALID;
+    return status(launch_pdl(gdn_prep_rows_kernel, dim3(2 * key_heads + value_heads), dim3(head_dim), 0, stream, qkv,
+                             alpha, beta_raw, conv_w, hist, dt_bias, a, key_heads, value_heads, head_dim, conv_kernel,
+                             eps, rows, act, decay, beta));
+}
+
+CL_API int cl_gdn_step_rows(const float* act, const float* decay, const float* beta, const float* z,
+                            const float* gamma, float* state, int key_heads, int value_heads, int head_dim, float eps,
+                            int rows, float* out, cudaStream_t stream) {
+    if (act == nullptr || decay == nullptr || beta == nullptr || z == nullptr || gamma == nullptr ||
+        state == nullptr || out == nullptr || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads ||
+        head_dim <= 0 || head_dim % 32 || head_dim > kMaxGdnDim || rows <= 0)
+        return CL_ERR_INVALID;
+    const int nparts = head_dim / kGdnCols;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(value_heads * nparts);
+    cfg.blockDim = dim3(kGdnCols * kGdnRowGroups);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = nparts;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cl::g_pdl_enabled ? 2 : 1;
+    return status(cudaLaunchKernelEx(&cfg, gdn_step_cluster_kernel, act, decay, beta, z, gamma, state, key_heads,
+                                     value_heads, head_dim, eps, out, rows));
 }
 
 CL_API int cl_attn_gate_prep(const float* mixed, const float* k_raw, const float* v_raw, const float* q_norm,
@@ -611,7 +783,23 @@ CL_API int cl_attn_gate_prep(const float* mixed, const float* k_raw, const float
         return CL_ERR_INVALID;
     return status(launch_pdl(attn_gate_prep_kernel, dim3(q_heads + kv_heads), dim3(head_dim),
                              (size_t)head_dim * sizeof(float), stream, mixed, k_raw, v_raw, q_norm, k_norm, q_heads,
-                             kv_heads, head_dim, rot_dim, cos_sin, pos_dev, eps, q_out, gate_out, k_cache, v_cache));
+                             kv_heads, head_dim, rot_dim, cos_sin, pos_dev, 0, eps, q_out, gate_out, k_cache,
+                             v_cache));
+}
+
+CL_API int cl_attn_gate_prep_rows(const float* mixed, const float* k_raw, const float* v_raw, const float* q_norm,
+                                  const float* k_norm, int q_heads, int kv_heads, int head_dim, int rot_dim,
+                                  const float* cos_sin, int pos0, int rows, float eps, float* q_out, float* gate_out,
+                                  float* k_cache, float* v_cache, cudaStream_t stream) {
+    if (mixed == nullptr || k_raw == nullptr || v_raw == nullptr || q_norm == nullptr || k_norm == nullptr ||
+        cos_sin == nullptr || q_out == nullptr || gate_out == nullptr || k_cache == nullptr || v_cache == nullptr ||
+        q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 32 || head_dim > 1024 || rot_dim < 0 ||
+        rot_dim > head_dim || rot_dim % 2 || pos0 < 0 || rows <= 0 || rows > 65535)
+        return CL_ERR_INVALID;
+    return status(launch_pdl(attn_gate_prep_kernel, dim3(q_heads + kv_heads, rows), dim3(head_dim),
+                             (size_t)head_dim * sizeof(float), stream, mixed, k_raw, v_raw, q_norm, k_norm, q_heads,
+                             kv_heads, head_dim, rot_dim, cos_sin, nullptr, pos0, eps, q_out, gate_out, k_cache,
+                             v_cache));
 }
 
 CL_API int cl_mul_sigmoid(const float* a, const float* g, float* out, int n, cudaStream_t stream) {

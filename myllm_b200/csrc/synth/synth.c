@@ -313,6 +313,16 @@ int synth_fill(uint8_t* dst, int type, long long rows, long long cols,
     return failed ? -1 : 0;
 }
 
+/* Threads of the parallel loops below for the calling thread (a launcher
+ * such as torch.distributed.run sets OMP_NUM_THREADS=1 for its ranks; the
+ * values written do not depend on the thread count). */
+void synth_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#endif
+    (void)n;
+}
+
 /* Pack caller-provided FP32 rows as `type`. */
 int synth_quantize(const float* src, uint8_t* dst, int type, long long rows, long long cols) {
     const long long rb = synth_row_bytes(type, cols);

@@ -66,6 +66,9 @@ def lib():
                                         ctypes.c_longlong]
         l.synth_mix64.argtypes = [ctypes.c_ulonglong]
         l.synth_mix64.restype = ctypes.c_ulonglong
+        l.synth_set_threads.argtypes = [ctypes.c_int]
+        # every core the process may run on, whatever OMP_NUM_THREADS says
+        l.synth_set_threads(len(os.sched_getaffinity(0)))
         _lib = l
     return _lib
 
@@ -102,7 +105,7 @@ def quantize(x: np.ndarray, gtype: int) -> np.ndarray:
 
 def fill(gtype: int, rows: int, cols: int, key: int, mean: float, std: float) -> np.ndarray:
     out = np.empty((rows, row_bytes(gtype, cols)), dtype=np.uint8)
-    if lib().synth_fill(out.ctypes.data, gtype, rows, cols, key, mean, std, 0) != 0:
+    if lib().synth_fill(out.ctypes.data, gtype, rows, cols, key, mean, std, len(os.sched_getaffinity(0))) != 0:
         raise ValueError("synth_fill failed")
     return out
 

@@ -1,11 +1,10 @@
 """The one-launch decode step (cl_qwen2_decode_step) against the reference.
 
-CudaLLM runs a one-GPU qwen2 decode step as a single persistent launch when
-every layer matrix is Q4_K / Q6_K and the heads are 128 wide (the 7B and
-14B shapes); CUDALLM_DECODE=graph selects the per-operator graph instead,
-and CUDALLM_DECODE=fused insists on the fused step (construction fails if
-the model does not qualify, so these tests cannot pass on a silent
-fallback).  Both must give the reference CPULLM's greedy tokens at every
+With CUDALLM_DECODE=fused, CudaLLM runs a one-GPU qwen2 decode step as a
+single persistent launch (every layer matrix Q4_K / Q6_K, 128-wide heads:
+the 7B and 14B shapes; construction fails if the model does not qualify,
+so these tests cannot pass on a silent fallback); the default is the
+per-operator graph (CUDALLM_DECODE=graph).  Both must give the reference CPULLM's greedy tokens at every
 step and logits within 1e-4 (max-abs relative), on a small model with the
 7B's structure (head_dim 128, 7 query heads per KV head): a short prompt
 (one attention split) and a 1100-token prompt (32 key splits of 35 keys),
@@ -77,8 +76,8 @@ def test_small_model_multi_tile_splits(small, monkeypatch):
 
 @pytest.mark.parametrize("n", [8, 1100])
 def test_small_model_default_paths(small, monkeypatch, n):
-    """The defaults together (split FP16 prefill GEMM, fused decode step):
-    the reference's tokens, logits within 1e-4."""
+    """The default prefill (split FP16 GEMM) with the fused decode step: the
+    reference's tokens, logits within 1e-4."""
     path, d = small
     monkeypatch.delenv("CUDALLM_PREFILL_GEMM", raising=False)
     monkeypatch.setenv("CUDALLM_DECODE", "fused")

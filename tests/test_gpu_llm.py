@@ -211,17 +211,19 @@ def test_qwen2_7b_parity(model_dir, cuda, monkeypatch, mode, prefill):
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(GOLDEN, "qwen2_7b_long.npz")),
                     reason="the full-length 7B golden has not been generated")
-@pytest.mark.parametrize("prefill", ["fp16x3", "tf32x3"])
-def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, prefill):
+@pytest.mark.parametrize("decode,prefill", [("graph", "fp16x3"), ("fused", "fp16x3"), ("graph", "tf32x3")])
+def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, decode, prefill):
     """The bench workload end to end: the 512-token prompt
     bench.py prefills, then 128 greedy decodes against a 4096-slot cache, on
-    the default decode path (and the default prefill GEMM, split FP16 on the
-    tensor cores: what bench.py times; and split TF32).  Every token
+    the default decode path (the per-operator graph) and the one-launch
+    step, with the default prefill GEMM (split FP16 on the tensor cores: what
+    bench.py times) and split TF32.  Every token
     identical to CPULLM's; logits (the reference's top 64 and every 16th)
     within the path's bar.  (The one-pass FP16 prefill is not held to this:
     at decode 76 the reference's two best logits are 0.2 % of the largest
     apart, within that path's rounding.)"""
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
+    monkeypatch.setenv("CUDALLM_DECODE", decode)
     d = np.load(os.path.join(GOLDEN, "qwen2_7b_long.npz"))
     assert int(d["cpullm_checked"]) == 1, "fixture not cross-checked against CPULLM itself"
     spec = sg.CONFIGS["qwen2.5-7b"]

@@ -4,7 +4,13 @@ models.  The reference has no CPU qwen35moe path; the oracle restates its
 formulas (moe_llm.mm, metal_llm.metal) in float64.
 
 Tokens must be identical at every step; logits within 1e-2 max-abs relative
-(the north-star tolerance); the observed error is pinned tighter.
+(the north-star tolerance); the observed error is pinned tighter.  Prefill
+runs token-batched by default (each layer over the whole prompt chunk: the
+projections as GEMMs, the DeltaNet conv and recurrence in one launch each,
+the routed experts over all (token, route) pairs); CUDALLM_MOE_PREFILL=serial
+replays the one-token step per prompt token, and CUDALLM_MOE_PREFILL_CHUNK
+splits the prompt into chunks that hand the conv history, recurrent state
+and KV cache on to each other.
 """
 import os
 
@@ -33,8 +39,13 @@ def tiny_moe(model_dir, cuda):
     return out
 
 
+@pytest.mark.parametrize("prefill", ["batched", "serial", "chunk5"])
 @pytest.mark.parametrize("seed", [5, 9])
-def test_moe_parity_with_fp64_oracle(tiny_moe, seed):
+def test_moe_parity_with_fp64_oracle(tiny_moe, seed, prefill, monkeypatch):
+    if prefill == "chunk5":
+        monkeypatch.setenv("CUDALLM_MOE_PREFILL_CHUNK", "5")  # 12 tokens: chunks of 5, 5, 2
+    else:
+        monkeypatch.setenv("CUDALLM_MOE_PREFILL", prefill)
     spec, path = tiny_moe[seed]
     prompt = sg.prompt_ids(spec.seed, 12, spec.vocab)
     ref = MoeFP64(path, max_sequence=64)
