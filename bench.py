@@ -149,13 +149,24 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary."""
+def profile_traffic(kernel: str, shape=None, algorithmic=None):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summaries
+    (profiles/traffic.json: the shape each was captured at, its DRAM bytes and
+    algorithmic bytes).  At another shape of the same kernel the measured
+    traffic / algorithmic ratio is applied to this launch's algorithmic bytes
+    (the kernel streams each weight byte once, so traffic grows in
+    proportion).  Returns (bytes or None, where the number comes from)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
-        return None
+        return None, "no ncu capture committed"
     with open(p) as f:
-        return json.load(f).get(kernel)
+        e = json.load(f).get(kernel)
+    if not isinstance(e, dict):
+        return None, f"no ncu capture of {kernel}"
+    if shape is None or shape == e["shape"] or not algorithmic:
+        return e["traffic"], f"measured at {e['shape']} ({e['source']})"
+    ratio = e["traffic"] / e["algorithmic"]
+    return ratio * algorithmic, f"scaled: {ratio:.3f} x the algorithmic bytes, as measured at {e['shape']}"
 
 
 # ---------------------------------------------------------------------------
@@ -699,7 +710,9 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         launches_per_step = 1  # the whole step is one cooperative launch
     roofline = {"bound": "hbm", "achieved": kern["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": kern["gbs"] / peak if kern["gbs"] else None,
-                "traffic": profile_traffic("gemv_head" if moe else "gemv_gateup"),
+                **dict(zip(("traffic", "traffic_source"),
+                           profile_traffic("gemv_head" if moe else "gemv_gateup", kern.get("shape"),
+                                           kern.get("bytes_per_launch")))),
                 "kernel": kern["kernel"], "shape": kern["shape"],
                 "bytes_per_launch": kern["bytes_per_launch"], "avg_launch_us": kern["avg_launch_us"],
                 "peak_kind": f"{peak_kind} hbm_gbs (STREAM copy)",
@@ -710,7 +723,7 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         k_us = fused_ms / args.steps * 1e3
         ach = tok_bytes / (k_us * 1e-6) / 1e9
         roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                    "traffic": profile_traffic(f"decode_fused_{name}"),
+                    **dict(zip(("traffic", "traffic_source"), profile_traffic(f"decode_fused_{name}"))),
                     "kernel": "decode_fused_kernel (one decode step: every layer, LM head and argmax in one "
                               "cooperative launch)",
                     "shape": f"{name}, position {mid}", "bytes_per_launch": tok_bytes, "avg_launch_us": k_us,

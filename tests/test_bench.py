@@ -461,3 +461,16 @@ def test_a_failing_report_does_not_lose_the_line(monkeypatch, capsys):
     assert REQUIRED <= set(line) and line["value"] > 0
     assert line["roofline"]["error"] == "RuntimeError: planted" and line["roofline"]["frac"] is None
     assert line["kernel_sweep"]["error"] == "RuntimeError: planted" and "moe_kernels" in line["kernel_sweep"]
+
+
+def test_traffic_is_measured_or_scaled_per_shape():
+    """roofline.traffic: the ncu capture's bytes at the shape it was taken
+    at; at another shape of the same kernel its traffic / algorithmic ratio
+    times that launch's algorithmic bytes, saying so; None without one."""
+    import bench
+    t, src = bench.profile_traffic("gemv_gateup", "2x[18944,3584] Q4_K", 76490752)
+    assert t == 77935872 and src.startswith("measured")
+    algo14 = 2 * 13824 * 5120 * 144 // 256
+    t2, src2 = bench.profile_traffic("gemv_gateup", "2x[13824,5120] Q4_K", algo14)
+    assert abs(t2 / algo14 - 77935872 / 76490752) < 1e-12 and src2.startswith("scaled")
+    assert bench.profile_traffic("gemv_head")[0] is None
