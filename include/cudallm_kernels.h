@@ -95,6 +95,39 @@ CL_API int cl_gemv_multi(const cl_gemv_segment* segs, int nseg, int k, const flo
  * metal_llm.metal:895) fused.  gate and up share type and stride. */
 CL_API int cl_gemv_swiglu(int type, const void* w_gate, const void* w_up, long long stride, int n, int k,
                           const float* x, const float* norm_gamma, float eps, float* y, cudaStream_t stream);
+
+/* ---- decode GEMV over fragment-packed K-quant weights (the same products
+ * as metal_gevm_q4_k_f32 / metal_gevm_q6_k_f32, metal_llm.metal:708-781,
+ * and the CPU gevmt, cpu_llm.cpp:512-547) ------------------------------
+ * cl_gemv_pack regroups a Q4_K or Q6_K matrix in the device layout
+ * (cl_repack_rows) into units of 16 rows x one super-block, each lane's
+ * tensor-core operand bytes contiguous (k % 256 == 0; rows past the last
+ * 16-row tile are zero).  With w_up (pair != 0 in the size query) a unit
+ * holds 8 gate rows then the same 8 up rows. */
+CL_API size_t cl_gemv_pack_bytes(int type, int rows, int k, int pair);
+CL_API int cl_gemv_pack(int type, const void* w, long long stride, int rows, int k, const void* w_up, void* out,
+                        cudaStream_t stream);
+typedef struct cl_gemv_packed_segment {
+    int type;     /* CL_TYPE_Q4_K or CL_TYPE_Q6_K */
+    const void* w; /* cl_gemv_pack output (16-byte aligned) */
+    int n;        /* output rows (SwiGLU: gate rows) */
+    const float* bias;
+    const float* residual;
+    float* y;
+} cl_gemv_packed_segment;
+/* Workspace of cl_gemv_packed for launches of at most max_tiles 16-row
+ * tiles (SwiGLU: 8-row pairs) on the current device.  Zero it once before
+ * first use; every launch leaves it re-armed. */
+CL_API size_t cl_gemv_packed_workspace_bytes(int max_tiles);
+/* y = W x (+ bias) (+ residual) for 1-4 packed matrices sharing x, with x
+ * RMS-normalised first when norm_gamma != NULL (cpu_llm.cpp:143-166); with
+ * swiglu != 0 one pair-packed matrix and y = SiLU(gate.x') * (up.x')
+ * (cpu_llm.cpp:188-202).  k <= 20480.  Deterministic (partial sums are
+ * added in a fixed order).  Launches that share a workspace must not
+ * overlap on the GPU. */
+CL_API int cl_gemv_packed(const cl_gemv_packed_segment* segs, int nseg, int k, const float* x,
+                          const float* norm_gamma, float eps, int swiglu, void* workspace, size_t workspace_bytes,
+                          cudaStream_t stream);
 /* Device error word of the pipelined kernels: non-zero when a bounded wait
  * gave up (never expected): 1-3 from the GEMV, 16 + 1..3 from the
  * tensor-core GEMM, 32 + 1..3 from the 16-bit GEMM.  Synchronous;

@@ -29,6 +29,11 @@ class GemvSegment(ctypes.Structure):
                 ("residual", c_vp), ("y", c_vp)]
 
 
+class GemvPackedSegment(ctypes.Structure):
+    """cl_gemv_packed_segment (include/cudallm_kernels.h)."""
+    _fields_ = [("type", c_int), ("w", c_vp), ("n", c_int), ("bias", c_vp), ("residual", c_vp), ("y", c_vp)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "cl_status_string": (c_char_p, [c_int]),
@@ -41,6 +46,11 @@ SIGNATURES = {
     "cl_gemv": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "cl_gemv_multi": (c_int, [ctypes.POINTER(GemvSegment), c_int, c_int, c_vp, c_vp, c_float, c_vp]),
     "cl_gemv_swiglu": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    "cl_gemv_pack_bytes": (c_size, [c_int, c_int, c_int, c_int]),
+    "cl_gemv_pack": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_gemv_packed_workspace_bytes": (c_size, [c_int]),
+    "cl_gemv_packed": (c_int, [ctypes.POINTER(GemvPackedSegment), c_int, c_int, c_vp, c_vp, c_float, c_int, c_vp,
+                               c_size, c_vp]),
     "cl_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "cl_gemm": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
     "cl_gemm_simt": (c_int, [c_int, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),

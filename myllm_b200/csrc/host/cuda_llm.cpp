@@ -224,6 +224,19 @@ struct CudaLLM::Impl {
     DeviceBuffer trace_mem;
     std::string trace_path;
     DeviceBuffer pack_mem;  // every layer matrix and the LM head in the tiled decode layout
+    // Decode GEMVs over fragment-packed copies (cl_gemv_packed), which stream
+    // a large matrix faster than the shared-memory ring kernels but carry a
+    // larger fixed cost per launch (measured on B200: the 7B LM head 87 vs
+    // 111 us; a 7B layer's QKV, o_proj, gate/up and down all slower).  So by
+    // default only the LM head is packed; CUDALLM_DECODE_GEMV=packed packs
+    // every decode matrix, =ring none.  Q4_K / Q6_K on the 256-column grid.
+    struct PackedLayer {
+        const void *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *down = nullptr;
+    };
+    bool packed_layers = false;
+    std::vector<PackedLayer> pk_layers;
+    const void* pk_head = nullptr;
+    DeviceBuffer pk_mem, pk_ws;  // packed matrices, GEMV workspace
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEvent_t kev0 = nullptr, kev1 = nullptr;  // around the fused step kernel
     float last_ms = 0.0f, last_kernel_ms = 0.0f;
@@ -513,6 +526,72 @@ struct CudaLLM::Impl {
                                  stream));
     }
 
+    // Pack the decode matrices for cl_gemv_packed (see `packed_layers`).
+    void setup_packed() {
+        std::string mode = "head";
+        if (const char* e = std::getenv("CUDALLM_DECODE_GEMV")) mode = e;
+        if (mode != "head" && mode != "packed" && mode != "ring")
+            throw std::invalid_argument("CUDALLM_DECODE_GEMV must be head, packed or ring");
+        if (mode == "ring" || fused) return;
+        auto ok = [](const DevMat& m, std::size_t kdim) {
+            return (m.type == kQ4_K || m.type == kQ6_K) && kdim % 256 == 0 && kdim <= 21504 && m.ptr != nullptr;
+        };
+        const bool layers_too = mode == "packed";
+        bool all = ok(out_w, H);
+        if (layers_too) {
+            all = all && o_kl > 0 && F_l > 0;
+            for (const Layer& L : layers)
+                all = all && ok(L.q, H) && ok(L.k, H) && ok(L.v, H) && ok(L.o, o_kl) && ok(L.gate, H) &&
+                      L.up.type == L.gate.type && ok(L.down, F_l);
+        }
+        if (!all) {
+            if (layers_too)
+                throw std::runtime_error("CUDALLM_DECODE_GEMV=packed: a decode matrix is not Q4_K / Q6_K on the "
+                                         "256-column grid");
+            return;  // the head stays on the ring kernels
+        }
+        auto bytes = [](const DevMat& m, std::size_t kdim, bool pair) {
+            return (cl_gemv_pack_bytes(m.type, m.rows, (int)kdim, pair ? 1 : 0) + 255) / 256 * 256;
+        };
+        std::size_t total = bytes(out_w, H, false);
+        if (layers_too)
+            for (const Layer& L : layers)
+                total += bytes(L.q, H, false) + bytes(L.k, H, false) + bytes(L.v, H, false) +
+                         bytes(L.o, o_kl, false) + bytes(L.gate, H, true) + bytes(L.down, F_l, false);
+        pk_mem = DeviceBuffer(total + 256);
+        char* base = static_cast<char*>(pk_mem.get());
+        auto pack = [&](const DevMat& m, std::size_t kdim, const DevMat* up) -> const void* {
+            char* dst = base;
+            CUDALLM_CL(cl_gemv_pack(m.type, m.ptr, m.stride, m.rows, (int)kdim, up ? up->ptr : nullptr, dst, stream));
+            base += bytes(m, kdim, up != nullptr);
+            return dst;
+        };
+        pk_head = pack(out_w, H, nullptr);
+        std::size_t tiles = (V_l + 15) / 16;
+        if (layers_too) {
+            pk_layers.resize(layers.size());
+            for (std::size_t l = 0; l < layers.size(); ++l) {
+                const Layer& L = layers[l];
+                PackedLayer& P = pk_layers[l];
+                P.q = pack(L.q, H, nullptr);
+                P.k = pack(L.k, H, nullptr);
+                P.v = pack(L.v, H, nullptr);
+                P.o = pack(L.o, o_kl, nullptr);
+                P.gate = pack(L.gate, H, &L.up);
+                P.down = pack(L.down, F_l, nullptr);
+            }
+            // the widest launch: the LM head, QKV, gate/up pairs or o / down
+            tiles = std::max<std::size_t>(tiles, (F_l + 7) / 8);
+            tiles = std::max<std::size_t>(tiles, (hq_l * d + 15) / 16 + 2 * ((hkv_l * d + 15) / 16));
+            tiles = std::max<std::size_t>(tiles, (H + 15) / 16);
+            packed_layers = true;
+        }
+        const std::size_t wsb = cl_gemv_packed_workspace_bytes((int)tiles);
+        if (wsb == 0) throw std::runtime_error("cl_gemv_packed_workspace_bytes failed");
+        pk_ws = DeviceBuffer(wsb);
+        CUDALLM_CUDA(cudaMemsetAsync(pk_ws.get(), 0, pk_ws.size(), stream));
+    }
+
     // Decode path: "graph" (default: the per-operator kernels in one CUDA
     // graph per step, measured faster on the 7B) or "fused" (the one-launch
     // step, cl_qwen2_decode_step; construction fails if the model does not
@@ -678,6 +757,7 @@ struct CudaLLM::Impl {
         host_io = PinnedBuffer(sizeof(int32_t) * (4 + prefill_chunk));
         if (wide16()) setup_wide16();
         setup_fused();
+        setup_packed();
         CUDALLM_CUDA(cudaStreamSynchronize(stream));
     }
 
@@ -725,11 +805,22 @@ struct CudaLLM::Impl {
         peer_allreduce = true;
     }
 
+    // A packed decode GEMV (x RMS-normalised by gamma when given).
+    void gemv_packed(const cl_gemv_packed_segment* segs, int nseg, std::size_t kdim, const float* x,
+                     const float* gamma, int swiglu) {
+        CUDALLM_CL(cl_gemv_packed(segs, nseg, (int)kdim, x, gamma, eps(), swiglu, pk_ws.get(), pk_ws.size(), stream));
+    }
+
     // Final RMSNorm + LM head + greedy token for the hidden row `hrow`.
     void record_head(const float* hrow, int32_t* token_out) {
         cudaStream_t s = stream;
-        const cl_gemv_segment seg{out_w.type, out_w.ptr, out_w.stride, (int)V_l, nullptr, nullptr, logits};
-        CUDALLM_CL(cl_gemv_multi(&seg, 1, (int)H, hrow, out_norm, eps(), s));
+        if (pk_head) {
+            const cl_gemv_packed_segment seg{out_w.type, pk_head, (int)V_l, nullptr, nullptr, logits};
+            gemv_packed(&seg, 1, H, hrow, out_norm, 0);
+        } else {
+            const cl_gemv_segment seg{out_w.type, out_w.ptr, out_w.stride, (int)V_l, nullptr, nullptr, logits};
+            CUDALLM_CL(cl_gemv_multi(&seg, 1, (int)H, hrow, out_norm, eps(), s));
+        }
         if (par.world == 1) {
             CUDALLM_CL(cl_argmax(logits, (int)V_l, token_out, arg_ws, arg_ws_bytes, s));
         } else {
@@ -762,13 +853,24 @@ struct CudaLLM::Impl {
         CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, (int)H, tok_in, 1, h, ints + 4, s));
         float* out = W > 1 ? part : h;
         const float* res = par.rank == 0 ? h : nullptr;
-        for (Layer& L : layers) {
-            const cl_gemv_segment segs[3] = {
-                {L.q.type, L.q.ptr, L.q.stride, L.q.rows, L.q_b, nullptr, q},
-                {L.k.type, L.k.ptr, L.k.stride, L.k.rows, L.k_b, nullptr, k},
-                {L.v.type, L.v.ptr, L.v.stride, L.v.rows, L.v_b, nullptr, v},
-            };
-            CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, h, L.attn_norm, eps(), s));
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            Layer& L = layers[l];
+            const PackedLayer* PL = packed_layers ? &pk_layers[l] : nullptr;
+            if (PL) {
+                const cl_gemv_packed_segment segs[3] = {
+                    {L.q.type, PL->q, L.q.rows, L.q_b, nullptr, q},
+                    {L.k.type, PL->k, L.k.rows, L.k_b, nullptr, k},
+                    {L.v.type, PL->v, L.v.rows, L.v_b, nullptr, v},
+                };
+                gemv_packed(segs, 3, H, h, L.attn_norm, 0);
+            } else {
+                const cl_gemv_segment segs[3] = {
+                    {L.q.type, L.q.ptr, L.q.stride, L.q.rows, L.q_b, nullptr, q},
+                    {L.k.type, L.k.ptr, L.k.stride, L.k.rows, L.k_b, nullptr, k},
+                    {L.v.type, L.v.ptr, L.v.stride, L.v.rows, L.v_b, nullptr, v},
+                };
+                CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, h, L.attn_norm, eps(), s));
+            }
             // RoPE of q/k at *pos, the KV append and attention over keys 0..*pos in one launch pair
             CUDALLM_CL(cl_attn_decode_rope(q, k, v, rope, pos, (int)config.rotary_dimension, L.k_cache, L.v_cache,
                                            (int)max_seq, (int)hq_l, (int)hkv_l, (int)d, scale, att, nullptr, attn_ws,
@@ -778,7 +880,10 @@ struct CudaLLM::Impl {
                 CUDALLM_NCCL(ncclAllGather(att, att_full, hq_l * d, ncclFloat32, comm, s));
                 o_in = att_full + o_k0;
             }
-            if (o_kl > 0)
+            if (PL) {
+                const cl_gemv_packed_segment seg{L.o.type, PL->o, (int)H, nullptr, res, out};
+                gemv_packed(&seg, 1, o_kl, o_in, nullptr, 0);
+            } else if (o_kl > 0)
                 CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)o_kl, o_in, nullptr, res, out, s));
             else
                 CUDALLM_CUDA(cudaMemsetAsync(out, 0, H * sizeof(float), s));
@@ -788,9 +893,17 @@ struct CudaLLM::Impl {
                 if (W > 1) decode_all_reduce(part, h);
                 continue;
             }
-            CUDALLM_CL(cl_gemv_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, h, L.ffn_norm,
-                                      eps(), act, s));
-            CUDALLM_CL(cl_gemv(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, act, nullptr, res, out, s));
+            if (PL) {
+                const cl_gemv_packed_segment gu{L.gate.type, PL->gate, (int)F_l, nullptr, nullptr, act};
+                gemv_packed(&gu, 1, H, h, L.ffn_norm, 1);
+                const cl_gemv_packed_segment dn{L.down.type, PL->down, (int)H, nullptr, res, out};
+                gemv_packed(&dn, 1, F_l, act, nullptr, 0);
+            } else {
+                CUDALLM_CL(cl_gemv_swiglu(L.gate.type, L.gate.ptr, L.up.ptr, L.gate.stride, (int)F_l, (int)H, h,
+                                          L.ffn_norm, eps(), act, s));
+                CUDALLM_CL(cl_gemv(L.down.type, L.down.ptr, L.down.stride, (int)H, (int)F_l, act, nullptr, res, out,
+                                   s));
+            }
             if (W > 1) decode_all_reduce(part, h);
         }
         record_head(h, ints + 3);

@@ -87,6 +87,38 @@ def gemv_swiglu(gtype: int, w_gate: torch.Tensor, w_up: torch.Tensor, n: int, k:
     return out
 
 
+def gemv_pack(gtype: int, w: torch.Tensor, n: int, k: int, w_up: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Device-layout rows (repack) -> the fragment-packed layout of cl_gemv_packed
+    (with w_up: gate/up pair units for the SwiGLU form)."""
+    nbytes = _native.lib().cl_gemv_pack_bytes(gtype, n, k, 0 if w_up is None else 1)
+    if nbytes == 0:
+        raise ValueError("cl_gemv_pack: unsupported type or shape")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+    check(_native.lib().cl_gemv_pack(gtype, _p(w), w.stride(0), n, k, _p(w_up), _p(out), _stream()), "cl_gemv_pack")
+    return out
+
+
+def gemv_packed_workspace(max_tiles: int, device="cuda") -> torch.Tensor:
+    """A zeroed workspace for cl_gemv_packed launches of up to max_tiles tiles."""
+    return torch.zeros(_native.lib().cl_gemv_packed_workspace_bytes(max_tiles), dtype=torch.uint8, device=device)
+
+
+def gemv_packed(segments: Sequence[tuple], k: int, x: torch.Tensor, gamma=None, eps: float = 1e-6,
+                swiglu: bool = False, ws: Optional[torch.Tensor] = None) -> None:
+    """segments: (gtype, packed w, n, bias, residual, out) tuples sharing x (RMS-normalised by
+    gamma if given); swiglu: one pair-packed (gate, up) matrix, out = SiLU(gate.x) * (up.x)."""
+    arr = (_native.GemvPackedSegment * len(segments))()
+    tiles = 0
+    for i, (gtype, w, n, bias, res, out) in enumerate(segments):
+        arr[i] = _native.GemvPackedSegment(gtype, w.data_ptr(), n, 0 if bias is None else bias.data_ptr(),
+                                           0 if res is None else res.data_ptr(), out.data_ptr())
+        tiles += (n + 7) // 8 if swiglu else (n + 15) // 16
+    if ws is None:
+        ws = gemv_packed_workspace(tiles, x.device)
+    check(_native.lib().cl_gemv_packed(arr, len(segments), k, _p(x), _p(gamma), eps, 1 if swiglu else 0, _p(ws),
+                                       ws.numel(), _stream()), "cl_gemv_packed")
+
+
 def device_error(clear: bool = True) -> int:
     code = ctypes.c_int(0)
     check(_native.lib().cl_device_error(ctypes.byref(code), 1 if clear else 0), "cl_device_error")

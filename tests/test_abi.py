@@ -202,6 +202,54 @@ def test_decode_pack_sizes():
     assert lib.cl_decode_pack(sg.Q4_K, None, 2016, 16, 3584, None, 1 << 20, None) == 1
 
 
+def test_gemv_pack_sizes_and_checks():
+    """The fragment-packed GEMV layout: units of 16 rows x one super-block
+    (Q4_K 2304 bytes, Q6_K 3360), ragged row counts padded to a whole tile
+    (8 rows per tile for a gate/up pair); other formats and k % 256 != 0
+    are refused; cl_gemv_packed checks its segments and alignments before
+    it looks at the device."""
+    import ctypes
+    lib = _native.lib()
+    assert lib.cl_gemv_pack_bytes(sg.Q4_K, 18944, 3584, 0) == 1184 * 14 * 2304
+    assert lib.cl_gemv_pack_bytes(sg.Q4_K, 18944, 3584, 1) == 2368 * 14 * 2304
+    assert lib.cl_gemv_pack_bytes(sg.Q6_K, 152064, 3584, 0) == 9504 * 14 * 3360
+    assert lib.cl_gemv_pack_bytes(sg.Q4_K, 17, 256, 0) == 2 * 2304
+    assert lib.cl_gemv_pack_bytes(sg.Q6_K, 17, 256, 1) == 3 * 3360
+    assert lib.cl_gemv_pack_bytes(sg.Q5_0, 896, 896, 0) == 0
+    assert lib.cl_gemv_pack_bytes(sg.Q4_K, 3584, 1000, 0) == 0
+    F, M = 1 << 20, (1 << 20) + 4
+    st = lib.cl_row_stride(sg.Q4_K, 256)
+    assert lib.cl_gemv_pack(sg.Q4_K, F, st, 16, 256, None, M, None) == 1  # misaligned output
+    assert lib.cl_gemv_pack(sg.Q4_K, F, st - 16, 16, 256, None, F, None) == 1  # stride too short
+
+    def seg(w=F, gtype=sg.Q4_K, n=16, bias=None):
+        return _native.GemvPackedSegment(gtype, w, n, bias, None, F)
+
+    one = (_native.GemvPackedSegment * 1)(seg())
+    two = (_native.GemvPackedSegment * 2)(seg(), seg())
+    assert lib.cl_gemv_packed(one, 1, 256, M, None, 1e-6, 0, F, 1 << 20, None) == 1  # misaligned x
+    assert lib.cl_gemv_packed(one, 1, 256, F, None, 1e-6, 0, M, 1 << 20, None) == 1  # misaligned workspace
+    assert lib.cl_gemv_packed((_native.GemvPackedSegment * 1)(seg(w=M)), 1, 256, F, None, 1e-6, 0, F, 1 << 20,
+                              None) == 1  # misaligned weights
+    assert lib.cl_gemv_packed((_native.GemvPackedSegment * 1)(seg(gtype=sg.Q8_0)), 1, 256, F, None, 1e-6, 0, F,
+                              1 << 20, None) == 1  # not a K-quant
+    assert lib.cl_gemv_packed(two, 2, 256, F, None, 1e-6, 1, F, 1 << 20, None) == 1  # SwiGLU takes one pair
+    assert lib.cl_gemv_packed((_native.GemvPackedSegment * 1)(seg(bias=F)), 1, 256, F, None, 1e-6, 1, F, 1 << 20,
+                              None) == 1  # no bias on the SwiGLU form
+    assert lib.cl_gemv_packed(one, 1, 300, F, None, 1e-6, 0, F, 1 << 20, None) == 1  # k % 256
+    assert lib.cl_gemv_packed(one, 1, 256 * 85, F, None, 1e-6, 0, F, 1 << 20, None) == 2  # k beyond 21504
+    assert lib.cl_gemv_packed(ctypes.cast(None, ctypes.POINTER(_native.GemvPackedSegment)), 1, 256, F, None, 1e-6,
+                              0, F, 1 << 20, None) == 1
+    # valid arguments reach the device query (CL_ERR_CUDA without a GPU)
+    if not _gpu_present():
+        assert lib.cl_gemv_packed(one, 1, 256, F, None, 1e-6, 0, F, 1 << 20, None) == 3
+
+
+def _gpu_present():
+    import torch
+    return torch.cuda.is_available()
+
+
 def test_null_pointers_are_rejected_before_any_launch():
     """Every kernel entry point returns an error status for a NULL required
     pointer instead of launching: on a GPU such a launch would read or write

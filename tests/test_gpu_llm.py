@@ -211,12 +211,15 @@ def test_qwen2_7b_parity(model_dir, cuda, monkeypatch, mode, prefill):
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(GOLDEN, "qwen2_7b_long.npz")),
                     reason="the full-length 7B golden has not been generated")
-@pytest.mark.parametrize("decode,prefill", [("graph", "fp16x3"), ("fused", "fp16x3"), ("graph", "tf32x3")])
-def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, decode, prefill):
+@pytest.mark.parametrize("decode,prefill,gemv", [("graph", "fp16x3", "head"), ("fused", "fp16x3", "head"),
+                                                 ("graph", "tf32x3", "head"), ("graph", "fp16x3", "packed"),
+                                                 ("graph", "fp16x3", "ring")])
+def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, decode, prefill, gemv):
     """The bench workload end to end: the 512-token prompt
     bench.py prefills, then 128 greedy decodes against a 4096-slot cache, on
-    the default decode path (the per-operator graph) and the one-launch
-    step, with the default prefill GEMM (split FP16 on the tensor cores: what
+    the default decode path (the per-operator graph, LM head on the packed
+    GEMV) and the one-launch step, with every decode GEMV packed or none, with
+    the default prefill GEMM (split FP16 on the tensor cores: what
     bench.py times) and split TF32.  Every token
     identical to CPULLM's; logits (the reference's top 64 and every 16th)
     within the path's bar.  (The one-pass FP16 prefill is not held to this:
@@ -224,6 +227,7 @@ def test_qwen2_7b_bench_workload_parity(model_dir, cuda, monkeypatch, decode, pr
     apart, within that path's rounding.)"""
     monkeypatch.setenv("CUDALLM_PREFILL_GEMM", prefill)
     monkeypatch.setenv("CUDALLM_DECODE", decode)
+    monkeypatch.setenv("CUDALLM_DECODE_GEMV", gemv)
     d = np.load(os.path.join(GOLDEN, "qwen2_7b_long.npz"))
     assert int(d["cpullm_checked"]) == 1, "fixture not cross-checked against CPULLM itself"
     spec = sg.CONFIGS["qwen2.5-7b"]
