@@ -257,18 +257,17 @@ def moe_launches_per_step(spec, world: int, rank: int) -> int:
     t = sg.moe_a3b_types
     n = 1                                                       # embed
     for l in range(spec.layers):
-        n += 1                                                  # attn_norm
         if spec.is_attention(l):
-            # q/gate + k + v GEMV, gate prep, attention split + combine, gate, o_proj
+            # q/gate + k + v GEMV (input norm fused), gate prep, attention split + combine, gate, o_proj
             n += gemv_launches([t(l, "attn_q"), t(l, "attn_k"), t(l, "attn_v")]) + 1 + 2 + 1 + 1
         else:
-            # qkv + z GEMV, alpha, beta, prep, recurrence step, out GEMV
-            n += gemv_launches([t(l, "attn_qkv"), t(l, "attn_gate")]) + 2 + 1 + 1 + 1
-        n += 1 + 1 + 1                                          # post norm, router, top-k
+            # attn_norm, qkv + z GEMV, alpha | beta, prep, recurrence step, out GEMV
+            n += 1 + gemv_launches([t(l, "attn_qkv"), t(l, "attn_gate")]) + 1 + 1 + 1 + 1
+        n += 1 + 1 + 1                                          # post norm, router | shared gate, top-k
         if any(e % world == rank for e in range(spec.experts)):
             n += 2                                              # routed gate/up, down
         if l % world == rank:
-            n += 3                                              # shared router, gate/up, down
+            n += 2                                              # shared gate/up, down
         n += 1 if world == 1 else 2                             # combine (+ residual add)
     return n + 3                                                # head GEMV, argmax, counter
 
@@ -387,9 +386,18 @@ def kernel_sweep(peak_gbs: float, seed: int):
             x = torch.randn(k, device="cuda")
             y = torch.empty(n, device="cuda")
             us = graph_time_us(lambda i: K.gemv(gtype, ws[i % copies], n, k, x, out=y), 40)
-            gemv.append({"type": sg.TYPE_NAMES[gtype], "n": n, "k": k, "us": round(us, 2),
-                         "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak_gbs, 3),
-                         "l2_resident": copies * nbytes < 126e6})
+            entry = {"type": sg.TYPE_NAMES[gtype], "n": n, "k": k, "us": round(us, 2),
+                     "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak_gbs, 3),
+                     "l2_resident": copies * nbytes < 126e6}
+            if gtype in (sg.Q4_K, sg.Q6_K):
+                # the same product on the fragment-packed GEMV (cl_gemv_packed)
+                pks = [K.gemv_pack(gtype, wi, n, k) for wi in ws]
+                pws = K.gemv_packed_workspace((n + 15) // 16)
+                us = graph_time_us(lambda i: K.gemv_packed([(gtype, pks[i % copies], n, None, None, y)], k, x, ws=pws),
+                                   40)
+                entry.update(packed_us=round(us, 2), packed_gbs=round(nbytes / us / 1e3, 1))
+                del pks
+            gemv.append(entry)
             del ws
             # prefill GEMM on the same weights at the config's batch sizes
             for m in (128, 512, 2048):
@@ -404,8 +412,31 @@ def kernel_sweep(peak_gbs: float, seed: int):
                     entry["error"] = f"{type(e).__name__}: {e}"
                 gemm.append(entry)
             del w
-    return {"gemv": gemv, "gemm": gemm,
-            "note": "GEMV frac of the measured HBM copy peak; GEMM (cl_gemm, the path prefill uses: split-TF32 "
+    # the 7B LM head (the largest decode matrix), where the decode graph uses the packed GEMV
+    head = None
+    try:
+        V, H = 152064, 3584
+        wn = sg.fill(sg.Q6_K, V, H, sg.stream_key(seed, "sweep_head"), 0.0, 0.02)
+        w = K.repack(sg.Q6_K, wn, H)
+        pk = K.gemv_pack(sg.Q6_K, w, V, H)
+        ws2, pk2 = [w, w.clone()], [pk, pk.clone()]
+        x = torch.randn(H, device="cuda")
+        gm = torch.ones(H, device="cuda")
+        y = torch.empty(V, device="cuda")
+        pws = K.gemv_packed_workspace((V + 15) // 16)
+        nbytes = V * sg.row_bytes(sg.Q6_K, H) + 8 * H + 4 * V
+        ring = graph_time_us(lambda i: K.gemv_multi([(sg.Q6_K, ws2[i % 2], V, None, None, y)], H, x, gm, 1e-6), 20)
+        pkd = graph_time_us(lambda i: K.gemv_packed([(sg.Q6_K, pk2[i % 2], V, None, None, y)], H, x, gm, 1e-6,
+                                                    ws=pws), 20)
+        head = {"shape": f"[{V},{H}] Q6_K + RMSNorm", "ring_us": round(ring, 2),
+                "ring_gbs": round(nbytes / ring / 1e3, 1), "packed_us": round(pkd, 2),
+                "packed_gbs": round(nbytes / pkd / 1e3, 1)}
+        del ws2, pk2, w, pk
+    except Exception as e:
+        head = {"error": f"{type(e).__name__}: {e}"}
+    return {"gemv": gemv, "gemm": gemm, "lm_head_7b": head,
+            "note": "GEMV frac of the measured HBM copy peak (packed_*: the fragment-packed GEMV on the same "
+                    "weights); GEMM (cl_gemm, the path prefill uses: split-TF32 "
                     "tcgen05 where the shape allows, else FP32 CUDA cores) TFLOP/s of useful work (2 M N K); "
                     "split-TF32 issues three tensor-core products per useful one"}
 

@@ -154,6 +154,15 @@ std::string gguf_architecture(const std::string& gguf_path) {
 }
 
 struct CudaMoeLLM::Impl {
+    // F32 GEMVs of a decode step that share their input, stacked so that each
+    // pair is one launch: per DeltaNet layer the alpha and beta rows, per layer
+    // the router and the shared expert's gate row.
+    DeviceBuffer stack_mem;
+    std::vector<const float*> stack_ab, stack_rs;
+    // The LM head on the fragment-packed GEMV (cl_gemv_packed) where it is
+    // Q4_K / Q6_K on the 256-column grid: it streams the 248k-row head faster
+    // than the ring GEMV; CUDALLM_DECODE_GEMV=ring keeps the ring kernel.
+    DeviceBuffer head_pk, head_ws;
     ModelConfig config;
     ParallelConfig par;
     int device = 0;
@@ -294,13 +303,50 @@ struct CudaMoeLLM::Impl {
         rope = a.take_n<float>(max_seq * (rot / 2) * 2);
     }
 
+    void stack_f32() {
+        std::size_t total = 0;
+        for (const MoeLayer& L : layers) total += (L.attention ? 0 : 2 * sr * H) + (E + 1) * H;
+        stack_mem = DeviceBuffer(total * sizeof(float) + 256);
+        float* p = static_cast<float*>(stack_mem.get());
+        stack_ab.assign(layers.size(), nullptr);
+        stack_rs.assign(layers.size(), nullptr);
+        auto put = [&](const float* src, std::size_t n) {
+            CUDALLM_CUDA(cudaMemcpyAsync(p, src, n * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+            p += n;
+        };
+        for (std::size_t l = 0; l < layers.size(); ++l) {
+            const MoeLayer& L = layers[l];
+            if (!L.attention) {
+                stack_ab[l] = p;
+                put(L.alpha_w, sr * H);
+                put(L.beta_w, sr * H);
+            }
+            stack_rs[l] = p;
+            put(L.router, E * H);
+            put(L.shared_router, H);
+        }
+    }
+
+    void pack_head() {
+        std::string mode = "head";
+        if (const char* e = std::getenv("CUDALLM_DECODE_GEMV")) mode = e;
+        if (mode == "ring") return;
+        if ((out_w.type != CL_TYPE_Q4_K && out_w.type != CL_TYPE_Q6_K) || H % 256 != 0 || H > 21504) return;
+        head_pk = DeviceBuffer(cl_gemv_pack_bytes(out_w.type, (int)V, (int)H, 0));
+        CUDALLM_CL(cl_gemv_pack(out_w.type, out_w.ptr, out_w.stride, (int)V, (int)H, nullptr, head_pk.get(), stream));
+        const std::size_t wsb = cl_gemv_packed_workspace_bytes((int)((V + 15) / 16));
+        if (wsb == 0) throw std::runtime_error("cl_gemv_packed_workspace_bytes failed");
+        head_ws = DeviceBuffer(wsb);
+        CUDALLM_CUDA(cudaMemsetAsync(head_ws.get(), 0, head_ws.size(), stream));
+    }
+
     void allocate_activations(Arena& a) {
         h = a.take_n<float>(H);
         xn = a.take_n<float>(H);
         big = a.take_n<float>(std::max(qkvw, 2 * hq * d));
         zb = a.take_n<float>(sr * sd);
-        alpha = a.take_n<float>(sr);
-        beta_raw = a.take_n<float>(sr);
+        alpha = a.take_n<float>(2 * sr);  // alpha | beta_raw: one stacked GEMV writes both
+        beta_raw = alpha + sr;
         act = a.take_n<float>(qkvw);
         decay = a.take_n<float>(sr);
         beta = a.take_n<float>(sr);
@@ -311,12 +357,12 @@ struct CudaMoeLLM::Impl {
         vb = a.take_n<float>(hkv * d);
         att = a.take_n<float>(hq * d);
         gated = a.take_n<float>(hq * d);
-        rlog = a.take_n<float>(E);
+        rlog = a.take_n<float>(E + 4);  // router logits | the shared expert's gate logit
+        sh_logit = rlog + E;
         wts = a.take_n<float>(Kr);
         ids = a.take_n<int32_t>(Kr);
         ea = a.take_n<float>(Kr * FF);
         ey = a.take_n<float>(Kr * H);
-        sh_logit = a.take_n<float>(4);
         sh_act = a.take_n<float>(SFF);
         sh_y = a.take_n<float>(H);
         moe_part = a.take_n<float>(H);
@@ -530,6 +576,9 @@ struct CudaMoeLLM::Impl {
         act_bytes = ap.used();
         CUDALLM_CUDA(cudaMemsetAsync(act_mem.get(), 0, act_mem.size(), stream));
 
+        stack_f32();
+        pack_head();
+
         const std::vector<float> table = rope_table_f64(max_seq, rot, (double)config.rope_theta);
         CUDALLM_CUDA(cudaMemcpyAsync(const_cast<float*>(rope), table.data(), table.size() * sizeof(float),
                                      cudaMemcpyHostToDevice, stream));
@@ -556,14 +605,14 @@ struct CudaMoeLLM::Impl {
         CUDALLM_CL(cl_embed(tok_embd.type, tok_embd.ptr, tok_embd.stride, (int)V, (int)H, tok, 1, h, ints + 4, s));
         for (std::size_t l = 0; l < layers.size(); ++l) {
             MoeLayer& L = layers[l];
-            CUDALLM_CL(cl_rmsnorm(h, L.attn_norm, 1, (int)H, eps(), xn, nullptr, s));
             if (L.attention) {
+                // the input RMSNorm fused into the projections (x is read by them alone)
                 const cl_gemv_segment segs[3] = {
                     {L.q_gate.type, L.q_gate.ptr, L.q_gate.stride, L.q_gate.rows, nullptr, nullptr, big},
                     {L.k.type, L.k.ptr, L.k.stride, L.k.rows, nullptr, nullptr, kb},
                     {L.v.type, L.v.ptr, L.v.stride, L.v.rows, nullptr, nullptr, vb},
                 };
-                CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, xn, nullptr, 0.0f, s));
+                CUDALLM_CL(cl_gemv_multi(segs, 3, (int)H, h, L.attn_norm, eps(), s));
                 CUDALLM_CL(cl_attn_gate_prep(big, kb, vb, L.q_norm, L.k_norm, (int)hq, (int)hkv, (int)d, (int)rot, rope,
                                              pos, eps(), q, gate, L.k_cache, L.v_cache, s));
                 CUDALLM_CL(cl_attn_decode(q, L.k_cache, L.v_cache, len, (int)max_seq, (int)hq, (int)hkv, (int)d, scale,
@@ -571,13 +620,13 @@ struct CudaMoeLLM::Impl {
                 CUDALLM_CL(cl_mul_sigmoid(att, gate, gated, (int)(hq * d), s));
                 CUDALLM_CL(cl_gemv(L.o.type, L.o.ptr, L.o.stride, (int)H, (int)(hq * d), gated, nullptr, h, h, s));
             } else {
+                CUDALLM_CL(cl_rmsnorm(h, L.attn_norm, 1, (int)H, eps(), xn, nullptr, s));
                 const cl_gemv_segment segs[2] = {
                     {L.qkv.type, L.qkv.ptr, L.qkv.stride, L.qkv.rows, nullptr, nullptr, big},
                     {L.z.type, L.z.ptr, L.z.stride, L.z.rows, nullptr, nullptr, zb},
                 };
                 CUDALLM_CL(cl_gemv_multi(segs, 2, (int)H, xn, nullptr, 0.0f, s));
-                CUDALLM_CL(cl_gemv_f32(L.alpha_w, (int)sr, (int)H, xn, alpha, s));
-                CUDALLM_CL(cl_gemv_f32(L.beta_w, (int)sr, (int)H, xn, beta_raw, s));
+                CUDALLM_CL(cl_gemv_f32(stack_ab[l], (int)(2 * sr), (int)H, xn, alpha, s));  // alpha | beta_raw
                 CUDALLM_CL(cl_gdn_prep(big, alpha, beta_raw, L.conv_w, L.hist, L.dt_bias, L.a, (int)sg, (int)sr, (int)sd,
                                        (int)kc, eps(), act, decay, beta, s));
                 CUDALLM_CL(cl_gdn_step(act, decay, beta, zb, L.ssm_norm, L.state, (int)sg, (int)sr, (int)sd, eps(),
@@ -586,7 +635,7 @@ struct CudaMoeLLM::Impl {
             }
             // MoE: route on device, local experts, shared expert, combine
             CUDALLM_CL(cl_rmsnorm(h, L.post_norm, 1, (int)H, eps(), xn, nullptr, s));
-            CUDALLM_CL(cl_gemv_f32(L.router, (int)E, (int)H, xn, rlog, s));
+            CUDALLM_CL(cl_gemv_f32(stack_rs[l], (int)(E + 1), (int)H, xn, rlog, s));  // router | shared gate
             CUDALLM_CL(cl_moe_route(rlog, (int)E, (int)Kr, ids, wts, s));
             if (E_l > 0) {
                 CUDALLM_CL(cl_moe_expert_gemv(L.gate_e.type, L.gate_e.ptr, L.up_e.ptr, L.gate_e.stride, (int)FF, (int)H,
@@ -596,7 +645,6 @@ struct CudaMoeLLM::Impl {
             }
             const bool shared_here = ep_shared_rank(l, W) == R;
             if (shared_here) {
-                CUDALLM_CL(cl_gemv_f32(L.shared_router, 1, (int)H, xn, sh_logit, s));
                 CUDALLM_CL(cl_gemv_swiglu(L.sh_gate.type, L.sh_gate.ptr, L.sh_up.ptr, L.sh_gate.stride, (int)SFF,
                                           (int)H, xn, nullptr, 0.0f, sh_act, s));
                 CUDALLM_CL(cl_gemv(L.sh_down.type, L.sh_down.ptr, L.sh_down.stride, (int)H, (int)SFF, sh_act, nullptr,
@@ -614,8 +662,13 @@ struct CudaMoeLLM::Impl {
     }
 
     void record_head() {
-        const cl_gemv_segment seg{out_w.type, out_w.ptr, out_w.stride, (int)V, nullptr, nullptr, logits};
-        CUDALLM_CL(cl_gemv_multi(&seg, 1, (int)H, h, out_norm, eps(), stream));
+        if (head_pk.get()) {
+            const cl_gemv_packed_segment seg{out_w.type, head_pk.get(), (int)V, nullptr, nullptr, logits};
+            CUDALLM_CL(cl_gemv_packed(&seg, 1, (int)H, h, out_norm, eps(), 0, head_ws.get(), head_ws.size(), stream));
+        } else {
+            const cl_gemv_segment seg{out_w.type, out_w.ptr, out_w.stride, (int)V, nullptr, nullptr, logits};
+            CUDALLM_CL(cl_gemv_multi(&seg, 1, (int)H, h, out_norm, eps(), stream));
+        }
         CUDALLM_CL(cl_argmax(logits, (int)V, ints + 3, arg_ws, arg_ws_bytes, stream));
     }
 
