@@ -275,6 +275,14 @@ CL_API int cl_attn_prefill(const float* q, const float* k_cache, const float* v_
  * q, caches and out 16-byte aligned. */
 CL_API int cl_attn_prefill_tc(const float* q, const float* k_cache, const float* v_cache, int pos0, int rows,
                               int q_heads, int kv_heads, int head_dim, float* out, cudaStream_t stream);
+/* The same attention FP32-grade on the tensor cores: q, k, v and the
+ * probabilities each carried as an FP16 pair (hi + lo, 22 significant
+ * bits; probabilities scaled by 2^12 first), every product as three
+ * FP16 MMAs (hi.hi + hi.lo + lo.hi) with FP32 accumulation and softmax.
+ * head_dim 128 (else CL_ERR_UNSUPPORTED); q, caches and out 16-byte
+ * aligned.  The FP32-grade prefill paths use it. */
+CL_API int cl_attn_prefill_tc3(const float* q, const float* k_cache, const float* v_cache, int pos0, int rows,
+                               int q_heads, int kv_heads, int head_dim, float* out, cudaStream_t stream);
 
 /* ---- greedy token (metal_argmax_partial/finalize_f32, metal_llm.metal:
  * 1544-1644; CPU greedy_token cpu_llm.cpp:34-48) -------------------------

@@ -70,6 +70,7 @@ SIGNATURES = {
     "cl_attn_decode_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp]),
     "cl_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     "cl_attn_prefill_tc": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "cl_attn_prefill_tc3": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     "cl_argmax_workspace_bytes": (c_size, [c_int]),
     "cl_argmax": (c_int, [c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
     "cl_argmax_ex": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_size, c_vp]),

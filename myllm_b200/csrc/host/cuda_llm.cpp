@@ -690,6 +690,13 @@ struct CudaLLM::Impl {
         // "fp16" / "bf16" (one 16-bit pass), "tf32x3" (split TF32 over the
         // native blocks, FP32-grade), "f16" (one FP16 pass over the native
         // blocks) or "simt" (FP32 CUDA cores).
+        if (const char* e = std::getenv("CUDALLM_PREFILL_ATTN")) {
+            const std::string v(e);
+            if (v == "fp32") prefill_attn = PrefillAttn::Fp32;
+            else if (v == "fp16") prefill_attn = PrefillAttn::Tc;
+            else if (v == "fp16x3") prefill_attn = PrefillAttn::Tc3;
+            else if (!v.empty()) throw std::invalid_argument("CUDALLM_PREFILL_ATTN must be fp32, fp16 or fp16x3");
+        }
         if (const char* e = std::getenv("CUDALLM_PREFILL_GEMM")) {
             const std::string val(e);
             if (val == "fp16")
@@ -935,6 +942,10 @@ struct CudaLLM::Impl {
     // the split-TF32 tcgen05 path over the native blocks (Auto: FP32-grade),
     // its one-pass FP16 form, or the FP32 CUDA-core kernel.
     enum class GemmPath { Auto, F16, Simt, Fp16, Bf16, Fp16x3 };
+    // Prefill attention: Auto (by the GEMM path's grade), or forced with
+    // CUDALLM_PREFILL_ATTN=fp32 | fp16 | fp16x3.
+    enum class PrefillAttn { Auto, Fp32, Tc, Tc3 };
+    PrefillAttn prefill_attn = PrefillAttn::Auto;
     GemmPath gemm_path = GemmPath::Fp16x3;
     DeviceBuffer w16_mem, g16_ws_mem, amax_mem;
     float* xmax = nullptr;  // split form: the device maximum of the current product's X
@@ -991,10 +1002,14 @@ struct CudaLLM::Impl {
             }
             CUDALLM_CL(cl_rope_kv(Q, K, Vv, m, (int)hq_l, (int)hkv_l, (int)d, (int)config.rotary_dimension, rope, nullptr,
                                   pos0, L.k_cache, L.v_cache, s));
-            // the one-pass 16-bit prefill paths take the FP16 tensor-core attention where it
-            // applies; the FP32-grade paths keep the FP32 kernel
-            if (!(wide16() && !split16() && d == 128 &&
-                  cl_attn_prefill_tc(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s) == CL_OK))
+            // the one-pass 16-bit prefill paths take the FP16 tensor-core attention, the
+            // FP32-grade paths its split-FP16 form (head_dim 128); else the FP32 kernel
+            const PrefillAttn pa = prefill_attn == PrefillAttn::Auto
+                                       ? (wide16() && !split16() ? PrefillAttn::Tc : PrefillAttn::Tc3)
+                                       : prefill_attn;
+            if (!(d == 128 && pa != PrefillAttn::Fp32 &&
+                  (pa == PrefillAttn::Tc ? cl_attn_prefill_tc : cl_attn_prefill_tc3)(
+                      Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s) == CL_OK))
                 CUDALLM_CL(cl_attn_prefill(Q, L.k_cache, L.v_cache, pos0, m, (int)hq_l, (int)hkv_l, (int)d, A, s));
             const float* o_in = A;
             if (gather_attn) {

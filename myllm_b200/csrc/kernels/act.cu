@@ -78,7 +78,7 @@ __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __res
 }
 
 // ---- XQ quantization --------------------------------------------------------
-__global__ void quantize_xq_kernel(const float* __restrict__ x, int k, void* xq) {
+__global__ void quantize_xq_kernel(const float* x, int k, void* xq) {
     grid_launch_dependents();
     grid_wait();
     const int blk = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -90,8 +90,8 @@ __global__ void quantize_xq_kernel(const float* __restrict__ x, int k, void* xq)
 constexpr int kNormThreads = 512;
 
 __global__ void __launch_bounds__(kNormThreads)
-rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma, int k, float eps,
-               float* __restrict__ y, void* xq, long long xq_stride) {
+rmsnorm_kernel(const float* x, const float* __restrict__ gamma, int k, float eps,
+               float* y, void* xq, long long xq_stride) {
     grid_launch_dependents();
     grid_wait();
     const int row = blockIdx.x;
@@ -132,7 +132,7 @@ rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma, int
 
 // ---- embedding ---------------------------------------------------------------
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, long long stride, int vocab, int k,
-                             const int32_t* __restrict__ ids, int count, float* __restrict__ out,
+                             const int32_t* ids, int count, float* out,
                              int* error_flag) {
     grid_launch_dependents();
     grid_wait();

@@ -95,9 +95,9 @@ struct AttnRope {
 };
 
 __global__ void __launch_bounds__(kDecThreads)
-attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                  const int* __restrict__ len_dev, int cap, int hq, int hkv, int d, float scale,
-                  float* __restrict__ part, const AttnRope rope) {
+attn_decode_split(const float* q, const float* kc, const float* vc,
+                  const int* len_dev, int cap, int hq, int hkv, int d, float scale,
+                  float* part, const AttnRope rope) {
     grid_launch_dependents();
     grid_wait();
     const int g = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
@@ -291,7 +291,7 @@ attn_decode_split(const float* __restrict__ q, const float* __restrict__ kc, con
 // The split weights exp(m_s - m) / l come from one warp; the partial loads
 // are independent and unrolled, so they are all in flight together.
 __global__ void __launch_bounds__(kMaxHeadDim)
-attn_decode_combine(const float* __restrict__ part, int nsplit, int d, float* __restrict__ out, void* xq,
+attn_decode_combine(const float* part, int nsplit, int d, float* out, void* xq,
                     int xq_k) {
     grid_launch_dependents();
     grid_wait();
@@ -322,8 +322,8 @@ constexpr int kKT = 32;   // keys per tile
 constexpr int kPreThreads = 256;
 
 __global__ void __launch_bounds__(kPreThreads)
-attn_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                    int pos0, int rows, int hq, int hkv, int d, float* __restrict__ out) {
+attn_prefill_kernel(const float* q, const float* kc, const float* vc,
+                    int pos0, int rows, int hq, int hkv, int d, float* out) {
     grid_launch_dependents();
     grid_wait();
     extern __shared__ __align__(16) float sm[];

@@ -14,9 +14,19 @@ namespace cl {
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  Every kernel launched by this library
 // carries the programmatic-stream-serialization attribute, so the next kernel
-// in the stream may start while this one drains.  Rule kept by every kernel:
-// before grid_wait() a kernel reads only immutable data (weights, tables)
-// and writes nothing.
+// in the stream may start while this one drains.  Rules kept by every kernel:
+// * before grid_wait() a kernel reads only immutable data (weights, tables)
+//   and writes nothing;
+// * data an earlier kernel wrote (activations, caches, maxima, ids) is never
+//   read on the non-coherent path (ld.global.nc, __ldg, or a const
+//   __restrict__ pointer the compiler may read that way): the kernel may
+//   have started before that data was written, and a line of a buffer that
+//   every layer reuses can still sit in the SM's read-only cache from an
+//   earlier kernel.  Measured on B200: the split tensor-core prefill
+//   attention read Q and the KV cache through const __restrict__ pointers
+//   and gave a wrong prefill, different each run, with programmatic
+//   dependent launch on; coherent loads made it exact.  Weights keep
+//   __restrict__ and the non-coherent loads.
 // ---------------------------------------------------------------------------
 CL_DEVINL void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 CL_DEVINL void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

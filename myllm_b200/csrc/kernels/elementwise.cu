@@ -7,10 +7,10 @@ namespace cl {
 // One thread per element pair.  Head slot s < q_heads: query head (rotated in
 // place); next kv_heads slots: key heads (rotated into the cache); last
 // kv_heads slots: value heads (copied into the cache).
-__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+__global__ void rope_kv_kernel(float* q, const float* k, const float* v,
                                int rows, int hq, int hkv, int d, int rot, const float* __restrict__ cs,
-                               const int* pos_dev, int pos_host, float* __restrict__ kc,
-                               float* __restrict__ vc) {
+                               const int* pos_dev, int pos_host, float* kc,
+                               float* vc) {
     grid_launch_dependents();
     grid_wait();
     const int half = rot / 2, pairs = d / 2, slots = hq + 2 * hkv;
@@ -62,7 +62,7 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
     }
 }
 
-__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o,
+__global__ void swiglu_kernel(const float* g, const float* u, float* o,
                               long long n) {
     grid_launch_dependents();
     grid_wait();
@@ -74,7 +74,7 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
     }
 }
 
-__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o,
+__global__ void add_kernel(const float* a, const float* b, float* o,
                            long long n) {
     grid_launch_dependents();
     grid_wait();
@@ -132,7 +132,7 @@ __host__ __device__ inline int argmax_ctas(int n) {
 }
 
 __global__ void __launch_bounds__(kArgThreads)
-argmax_kernel(const float* __restrict__ x, int n, int index_offset, int32_t* token, float* value,
+argmax_kernel(const float* x, int n, int index_offset, int32_t* token, float* value,
               unsigned int* counter, float2* partial) {
     grid_launch_dependents();
     grid_wait();
@@ -174,7 +174,7 @@ argmax_kernel(const float* __restrict__ x, int n, int index_offset, int32_t* tok
 }
 
 // records[i] = (value, index bits); lowest index wins ties.
-__global__ void argmax_merge_kernel(const float2* __restrict__ rec, int n, int32_t* token) {
+__global__ void argmax_merge_kernel(const float2* rec, int n, int32_t* token) {
     grid_launch_dependents();
     grid_wait();
     if (threadIdx.x != 0) return;

@@ -75,7 +75,7 @@ __host__ __device__ inline int split_exp(float amax) {
 // Output multiplier of a segment: 2^-(x exponent + w exponent), exact.
 CL_DEVINL float seg_unscale(const OutSeg& sg) {
     if (sg.xmax == nullptr || sg.wmax == nullptr) return 1.0f;
-    return ldexpf(1.0f, -(split_exp(__ldg(sg.xmax)) + split_exp(__ldg(sg.wmax))));
+    return ldexpf(1.0f, -(split_exp(__ldcg(sg.xmax)) + split_exp(__ldg(sg.wmax))));  // xmax: the previous kernel's
 }
 
 struct Args {
@@ -420,7 +420,7 @@ __global__ void dequant16_kernel(const uint8_t* __restrict__ w, long long stride
     }
 }
 
-__global__ void convert16_kernel(const float* __restrict__ x, long long count, uint16_t* out, int bf16) {
+__global__ void convert16_kernel(const float* x, long long count, uint16_t* out, int bf16) {
     grid_launch_dependents();
     grid_wait();
     const long long n4 = count / 4;
@@ -473,7 +473,7 @@ __global__ void amax_dequant_kernel(const uint8_t* __restrict__ w, long long str
     amax_commit(m, amax);
 }
 
-__global__ void amax_kernel(const float* __restrict__ x, long long count, float* amax) {
+__global__ void amax_kernel(const float* x, long long count, float* amax) {
     grid_launch_dependents();
     grid_wait();
     float m = 0.0f;
@@ -486,10 +486,10 @@ __global__ void amax_kernel(const float* __restrict__ x, long long count, float*
 }
 
 // X [rows][k] FP32 -> rows of [hi(k) | lo(k)] FP16 of X scaled by split_exp(*amax) (the split form).
-__global__ void split16_kernel(const float* __restrict__ x, int rows, int k, const float* amax, uint16_t* out) {
+__global__ void split16_kernel(const float* x, int rows, int k, const float* amax, uint16_t* out) {
     grid_launch_dependents();
     grid_wait();
-    const float sc = ldexpf(1.0f, split_exp(__ldg(amax)));
+    const float sc = ldexpf(1.0f, split_exp(__ldcg(amax)));  // written by the previous kernel: read from L2
     const int k4 = k / 4;
     const long long n4 = (long long)rows * k4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;

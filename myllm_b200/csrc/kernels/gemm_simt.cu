@@ -16,7 +16,7 @@ constexpr int kBM = 64, kBN = 64, kBK = 32, kSimtThreads = 256;
 
 __global__ void __launch_bounds__(kSimtThreads)
 gemm_simt_kernel(int type, const uint8_t* __restrict__ w, long long stride, int n, int k,
-                 const float* __restrict__ x, int m, const float* __restrict__ bias,
+                 const float* x, int m, const float* __restrict__ bias,
                  const float* res, float* y) {
     grid_launch_dependents();
     grid_wait();

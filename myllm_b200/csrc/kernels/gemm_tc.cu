@@ -178,7 +178,7 @@ CL_DEVINL void load_x32(const float* x, int k, int mm, int c, float (&v)[32]) {
 // ---------------------------------------------------------------------------
 template <int T, bool X3>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_tc_kernel(const uint8_t* __restrict__ w, long long stride, int n, int k, const float* __restrict__ x, int m,
+gemm_tc_kernel(const uint8_t* __restrict__ w, long long stride, int n, int k, const float* x, int m,
                const float* __restrict__ bias, const float* res, float* y) {
     using P = Mode<X3>;
     extern __shared__ uint8_t smem_raw[];

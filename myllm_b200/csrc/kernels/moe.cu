@@ -42,8 +42,8 @@ CL_DEVINL float block_sum(float v, float* red) {
 }
 
 // ---- FP32 GEMV (router, DeltaNet alpha/beta, shared-expert gate) -------------
-__global__ void gemv_f32_kernel(const float* __restrict__ w, int n, int k, const float* __restrict__ x,
-                                float* __restrict__ y) {
+__global__ void gemv_f32_kernel(const float* __restrict__ w, int n, int k, const float* x,
+                                float* y) {
     grid_launch_dependents();
     grid_wait();
     const int row = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
@@ -65,8 +65,8 @@ __global__ void gemv_f32_kernel(const float* __restrict__ w, int n, int k, const
 // ---- router: softmax over the logits, top-k, renormalisation -----------------
 constexpr int kRouteThreads = 256;
 
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __restrict__ logits, int ne, int k,
-                                                              int* __restrict__ ids, float* __restrict__ wts) {
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* logits, int ne, int k,
+                                                              int* ids, float* wts) {
     grid_launch_dependents();
     grid_wait();
     extern __shared__ float prob[];  // [ne]
@@ -163,8 +163,8 @@ constexpr int kMaxExpUnits = 256;  // k <= 8192
 template <int F, bool SW>
 __global__ void __launch_bounds__(kExpThreads)
     expert_gemv_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ w_up, long long stride, int n,
-                       int k, const float* __restrict__ x, int x_stride, int x_group, const int* __restrict__ ids,
-                       int rank, int world, float* __restrict__ y) {
+                       int k, const float* x, int x_stride, int x_group, const int* ids,
+                       int rank, int world, float* y) {
     constexpr int NV = SW ? 2 * kExpRows : kExpRows;
     __shared__ uint4 planes[8][kMaxExpUnits];  // XQ unit u: 6 limb chunks, lsum, (xs, xsum)
     grid_launch_dependents();
@@ -242,9 +242,9 @@ __global__ void __launch_bounds__(kExpThreads)
 }
 
 // ---- expert combine: out = residual + (sum_r w_r y_r + sigmoid(g) * shared) ----
-__global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ ids, const float* __restrict__ wts,
-                               int routes, int n, int rank, int world, const float* __restrict__ shared_y,
-                               const float* __restrict__ shared_logit, const float* residual, float* out) {
+__global__ void combine_kernel(const float* y, const int* ids, const float* wts,
+                               int routes, int n, int rank, int world, const float* shared_y,
+                               const float* shared_logit, const float* residual, float* out) {
     grid_launch_dependents();
     grid_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -271,11 +271,11 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
 // Block b of D threads owns qkv channels [b D, b D + D): blocks < 2 G are the
 // q and k heads (L2-normalised), the rest the value heads.  Block 0 also
 // turns alpha / beta into decay / beta.
-__global__ void gdn_prep_kernel(const float* __restrict__ qkv, const float* __restrict__ alpha,
-                                const float* __restrict__ beta_raw, const float* __restrict__ conv_w, float* hist,
+__global__ void gdn_prep_kernel(const float* qkv, const float* alpha,
+                                const float* beta_raw, const float* __restrict__ conv_w, float* hist,
                                 const float* __restrict__ dt_bias, const float* __restrict__ a, int key_heads,
-                                int value_heads, int d, int kc, float eps, float* __restrict__ act,
-                                float* __restrict__ decay, float* __restrict__ beta) {
+                                int value_heads, int d, int kc, float eps, float* act,
+                                float* decay, float* beta) {
     grid_launch_dependents();
     grid_wait();
     __shared__ float red[32];
@@ -313,11 +313,11 @@ __global__ void gdn_prep_kernel(const float* __restrict__ qkv, const float* __re
 // expressions and their order are those of gdn_prep_kernel.
 constexpr int kMaxConv = 9;
 
-__global__ void gdn_prep_rows_kernel(const float* __restrict__ qkv, const float* __restrict__ alpha,
-                                     const float* __restrict__ beta_raw, const float* __restrict__ conv_w, float* hist,
+__global__ void gdn_prep_rows_kernel(const float* qkv, const float* alpha,
+                                     const float* beta_raw, const float* __restrict__ conv_w, float* hist,
                                      const float* __restrict__ dt_bias, const float* __restrict__ a, int key_heads,
-                                     int value_heads, int d, int kc, float eps, int rows, float* __restrict__ act,
-                                     float* __restrict__ decay, float* __restrict__ beta) {
+                                     int value_heads, int d, int kc, float eps, int rows, float* act,
+                                     float* decay, float* beta) {
     grid_launch_dependents();
     grid_wait();
     __shared__ float red[32];
@@ -371,9 +371,9 @@ __global__ void gdn_prep_rows_kernel(const float* __restrict__ qkv, const float*
 constexpr int kMaxGdnDim = 128;
 
 __global__ void __launch_bounds__(2 * kMaxGdnDim) gdn_step_kernel(
-    const float* __restrict__ act, const float* __restrict__ decay, const float* __restrict__ beta,
-    const float* __restrict__ z, const float* __restrict__ gamma, float* __restrict__ state, int key_heads,
-    int value_heads, int d, float eps, float* __restrict__ out) {
+    const float* act, const float* decay, const float* beta,
+    const float* z, const float* __restrict__ gamma, float* state, int key_heads,
+    int value_heads, int d, float eps, float* out) {
     grid_launch_dependents();
     grid_wait();
     __shared__ float qs[kMaxGdnDim], ks[kMaxGdnDim], part[2][kMaxGdnDim];
@@ -438,9 +438,9 @@ __global__ void __launch_bounds__(2 * kMaxGdnDim) gdn_step_kernel(
 constexpr int kGdnCols = 32, kGdnRowGroups = 8;
 
 __global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_kernel(
-    const float* __restrict__ act, const float* __restrict__ decay, const float* __restrict__ beta,
-    const float* __restrict__ z, const float* __restrict__ gamma, float* __restrict__ state, int key_heads,
-    int value_heads, int d, float eps, float* __restrict__ out, int rows) {
+    const float* act, const float* decay, const float* beta,
+    const float* z, const float* __restrict__ gamma, float* state, int key_heads,
+    int value_heads, int d, float eps, float* out, int rows) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     grid_launch_dependents();
@@ -522,10 +522,10 @@ __global__ void __launch_bounds__(kGdnCols * kGdnRowGroups) gdn_step_cluster_ker
 // ---- gated attention: split, per-head norms, partial RoPE, KV append -------
 // Blocks [0, hq): query heads (query and gate halves of the packed head);
 // blocks [hq, hq + hkv): KV heads.  blockDim = head_dim.
-__global__ void attn_gate_prep_kernel(const float* __restrict__ mixed, const float* __restrict__ k_raw,
-                                      const float* __restrict__ v_raw, const float* __restrict__ q_norm,
+__global__ void attn_gate_prep_kernel(const float* mixed, const float* k_raw,
+                                      const float* v_raw, const float* __restrict__ q_norm,
                                       const float* __restrict__ k_norm, int hq, int hkv, int d, int rot,
-                                      const float* __restrict__ cos_sin, const int* __restrict__ pos_dev, int pos0,
+                                      const float* __restrict__ cos_sin, const int* pos_dev, int pos0,
                                       float eps, float* __restrict__ q_out, float* __restrict__ gate_out,
                                       float* k_cache, float* v_cache) {
     grid_launch_dependents();
@@ -565,7 +565,7 @@ __global__ void attn_gate_prep_kernel(const float* __restrict__ mixed, const flo
     }
 }
 
-__global__ void mul_sigmoid_kernel(const float* __restrict__ a, const float* __restrict__ g, float* __restrict__ out,
+__global__ void mul_sigmoid_kernel(const float* a, const float* g, float* out,
                                    int n) {
     grid_launch_dependents();
     grid_wait();
@@ -811,8 +811,8 @@ CL_API int cl_mul_sigmoid(const float* a, const float* g, float* out, int n, cud
 
 namespace cl {
 namespace moe {
-__global__ void select_token_kernel(const int32_t* __restrict__ ids, const int* __restrict__ index,
-                                    int32_t* __restrict__ out) {
+__global__ void select_token_kernel(const int32_t* ids, const int* index,
+                                    int32_t* out) {
     grid_launch_dependents();
     grid_wait();
     out[0] = ids[*index];

@@ -75,7 +75,7 @@ CL_DEVINL unsigned long long global_ns() {
 }
 
 __global__ void __launch_bounds__(kThreads)
-    peer_allreduce_kernel(const float* __restrict__ in, float* __restrict__ out, int n, int rank, int world,
+    peer_allreduce_kernel(const float* in, float* out, int n, int rank, int world,
                           size_t slot, unsigned long long wait_limit_ns, const __grid_constant__ PeerBuffers peers) {
     const int b = blockIdx.x;
     PeerHeader* mine = reinterpret_cast<PeerHeader*>(peers.buf[rank]);

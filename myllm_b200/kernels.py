@@ -259,10 +259,13 @@ def attn_decode_rope(q, k_new, v_new, cos_sin, pos: int, rot: int, k_cache, v_ca
     return out
 
 
-def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d, tensor_cores: bool = False):
-    """Causal prefill attention: FP32 CUDA cores, or the FP16 tensor-core kernel."""
+def attn_prefill(q, k_cache, v_cache, pos0: int, rows: int, hq, hkv, d, tensor_cores=False):
+    """Causal prefill attention: FP32 CUDA cores, the FP16 tensor-core kernel
+    (tensor_cores=True), or its split-FP16 FP32-grade form (tensor_cores="split")."""
     out = torch.empty((rows, hq * d), dtype=torch.float32, device=q.device)
-    fn = _native.lib().cl_attn_prefill_tc if tensor_cores else _native.lib().cl_attn_prefill
+    lib = _native.lib()
+    fn = lib.cl_attn_prefill_tc3 if tensor_cores == "split" else lib.cl_attn_prefill_tc if tensor_cores \
+        else lib.cl_attn_prefill
     check(fn(_p(q), _p(k_cache), _p(v_cache), pos0, rows, hq, hkv, d, _p(out), _stream()), "cl_attn_prefill")
     return out
 

@@ -299,17 +299,21 @@ def causal_attention_ref(q, kc, vc, hq, hkv, d, pos0, rows):
     return out
 
 
-@pytest.mark.parametrize("tc", [False, True])
+@pytest.mark.parametrize("tc", [False, True, "split"])
 @pytest.mark.parametrize("hq,hkv,d,pos0,rows", [
     (28, 4, 128, 0, 512),    # BASELINE config 2 (7B shape): the bench's 512-token prompt
     (40, 8, 128, 0, 1024),   # BASELINE config 3 (14B shape): the 1024-token prompt
     (28, 4, 128, 512, 256),  # a later chunk of a chunked prefill
     (14, 2, 128, 37, 100),   # ragged: a chunk starting mid-tile, rows not a multiple of 64
+    (28, 4, 128, 0, 8),      # a short prompt: fewer rows than one warp's 16
+    (28, 4, 128, 0, 1),      # one row
+    (28, 4, 128, 5, 3),      # a short chunk after earlier rows
 ])
 def test_attention_prefill_long(cuda, hq, hkv, d, pos0, rows, tc):
     """Causal prefill attention at the prompt lengths the benchmarks prefill:
-    the FP32 kernel at 1e-5, the FP16 tensor-core kernel at 5e-3 (operands
-    and probabilities rounded to 11-bit significands) of each row's scale."""
+    the FP32 kernel and the split-FP16 tensor-core kernel at 1e-5, the FP16
+    tensor-core kernel at 5e-3 (operands and probabilities rounded to 11-bit
+    significands) of each row's scale."""
     cap = pos0 + rows
     q = xvec(hq * d, rows, seed=93)
     kc = xvec(hkv * d, cap, seed=94)
@@ -318,7 +322,7 @@ def test_attention_prefill_long(cuda, hq, hkv, d, pos0, rows, tc):
                          pos0, rows, hq, hkv, d, tensor_cores=tc).cpu().numpy()
     ref = causal_attention_ref(q, kc, vc, hq, hkv, d, pos0, rows)
     err = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
-    assert err.max() <= (5e-3 if tc else 1e-5), (int(err.argmax()), float(err.max()))
+    assert err.max() <= (5e-3 if tc is True else 1e-5), (int(err.argmax()), float(err.max()))
 
 
 def test_argmax_lowest_index_on_ties(cuda):
