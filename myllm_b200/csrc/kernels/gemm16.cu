@@ -394,7 +394,8 @@ __global__ void dequant16_kernel(const uint8_t* __restrict__ w, long long stride
         float v[32];
         dequant32<T>(w + (size_t)r * stride, k, c, v);
         if (split) {
-            const float sc = ldexpf(1.0f, split_exp(__ldg(amax)));
+            // the maximum comes from the previous kernel (amax_dequant_kernel): read it from L2
+            const float sc = ldexpf(1.0f, split_exp(__ldcg(amax)));
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] *= sc;
         }
