@@ -482,6 +482,32 @@ CL_API int cl_moe_route_rows(const float* logits, int rows, int n_experts, int k
 CL_API int cl_moe_expert_gemv_rows(int type, const void* w, const void* w_up, long long stride, int n, int k,
                                    const float* x, int x_stride, int x_group, const int32_t* ids, int routes,
                                    int rank, int world, float* y, cudaStream_t stream);
+/* Grouped form of cl_moe_expert_gemv_rows for prefill: the routes of a
+ * prompt chunk evaluated expert by expert (the reference's per-expert
+ * evaluation of a prompt's (token, expert) pairs, moe_llm.mm:2692-2843 and
+ * 3087-3108), so an expert's rows are read from HBM once per launch rather
+ * than once per route, and each input row is encoded once.
+ *   cl_moe_group_routes      buckets this rank's routes (ids[r] % world ==
+ *                            rank) by local expert ids[r] / world:
+ *                            offsets [n_local + 1] (offsets[e] .. offsets[e+1]
+ *                            index `list`), list [routes] (route indices; the
+ *                            order within an expert is unspecified).
+ *                            1 <= n_local <= 4095.  Once per layer: the gate/up
+ *                            and the down product share it;
+ *   cl_moe_expert_gemv_grouped  y rows of this rank's routes, each equal to
+ *                            what cl_moe_expert_gemv_rows writes for the same
+ *                            arguments (same unit dots in the same order);
+ *                            offsets / list / n_local from cl_moe_group_routes
+ *                            over the same ids; planes = scratch of
+ *                            cl_moe_xq_planes_bytes(ceil(routes / x_group), k)
+ *                            bytes (the XQ encoding of each input row). */
+CL_API size_t cl_moe_xq_planes_bytes(int inputs, int k);
+CL_API int cl_moe_group_routes(const int32_t* ids, int routes, int n_local, int rank, int world, int32_t* offsets,
+                               int32_t* list, cudaStream_t stream);
+CL_API int cl_moe_expert_gemv_grouped(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                                      const float* x, int x_stride, int x_group, const int32_t* ids, int routes,
+                                      int rank, int world, const int32_t* offsets, const int32_t* list, int n_local,
+                                      void* planes, size_t planes_bytes, float* y, cudaStream_t stream);
 CL_API int cl_moe_combine_rows(const float* y, const int32_t* ids, const float* weights, int routes, int n, int rank,
                                int world, const float* shared_y, const float* shared_logit, const float* residual,
                                float* out, int rows, cudaStream_t stream);

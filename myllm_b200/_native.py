@@ -99,6 +99,10 @@ SIGNATURES = {
     "cl_moe_route_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     "cl_moe_expert_gemv_rows": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int,
                                         c_int, c_int, c_vp, c_vp]),
+    "cl_moe_xq_planes_bytes": (c_size, [c_int, c_int]),
+    "cl_moe_group_routes": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
+    "cl_moe_expert_gemv_grouped": (c_int, [c_int, c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int,
+                                           c_int, c_int, c_vp, c_vp, c_int, c_vp, c_size, c_vp, c_vp]),
     "cl_moe_combine_rows": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_int,
                                     c_vp]),
     "cl_gdn_prep_rows": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float,

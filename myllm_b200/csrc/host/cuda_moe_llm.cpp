@@ -205,7 +205,11 @@ struct CudaMoeLLM::Impl {
           *pea = nullptr, *pey = nullptr, *pshl = nullptr, *psg = nullptr, *psu = nullptr, *pshy = nullptr,
           *ppart = nullptr;
     int32_t* pids = nullptr;
-    bool serial_prefill = false;  // CUDALLM_MOE_PREFILL=serial: one token-step graph per prompt token
+    int32_t *pgoff = nullptr, *plist = nullptr;  // routes bucketed by local expert (grouped expert GEMV)
+    void* pplanes = nullptr;                     // XQ encodings of the expert GEMVs' input rows
+    std::size_t pplanes_bytes = 0;
+    bool serial_prefill = false;
+    bool grouped_experts = true;  // CUDALLM_MOE_EXPERTS=grouped|routes: prefill expert GEMV form  // CUDALLM_MOE_PREFILL=serial: one token-step graph per prompt token
 
     PinnedBuffer host_io;  // [0] token in, [1] token out, [2..3] pos/len, [4..] prompt staging
     cudaGraphExec_t decode_exec = nullptr, prefill_exec = nullptr;
@@ -402,6 +406,10 @@ struct CudaMoeLLM::Impl {
         psu = a.take_n<float>(C * SFF);
         pshy = a.take_n<float>(C * H);
         ppart = a.take_n<float>(C * H);
+        pgoff = a.take_n<int32_t>(E_l + 1);
+        plist = a.take_n<int32_t>(C * Kr);
+        pplanes_bytes = std::max(cl_moe_xq_planes_bytes((int)C, (int)H), cl_moe_xq_planes_bytes((int)(C * Kr), (int)FF));
+        pplanes = a.take(pplanes_bytes);
     }
 
     void ensure_prefill_buffers() {
@@ -465,7 +473,16 @@ struct CudaMoeLLM::Impl {
             CUDALLM_CL(cl_rmsnorm(px, L.post_norm, m, Hi, eps(), pxn, nullptr, s));
             pgemm_f32(L.router, (int)E, Hi, pxn, m, prlog);
             CUDALLM_CL(cl_moe_route_rows(prlog, m, (int)E, (int)Kr, pids, pwts, s));
-            if (E_l > 0) {
+            if (E_l > 0 && grouped_experts) {
+                const int routes = (int)(m * Kr), nl = (int)E_l;
+                CUDALLM_CL(cl_moe_group_routes(pids, routes, nl, R, W, pgoff, plist, s));
+                CUDALLM_CL(cl_moe_expert_gemv_grouped(L.gate_e.type, L.gate_e.ptr, L.up_e.ptr, L.gate_e.stride,
+                                                      (int)FF, Hi, pxn, Hi, (int)Kr, pids, routes, R, W, pgoff, plist,
+                                                      nl, pplanes, pplanes_bytes, pea, s));
+                CUDALLM_CL(cl_moe_expert_gemv_grouped(L.down_e.type, L.down_e.ptr, nullptr, L.down_e.stride, Hi,
+                                                      (int)FF, pea, (int)FF, 1, pids, routes, R, W, pgoff, plist, nl,
+                                                      pplanes, pplanes_bytes, pey, s));
+            } else if (E_l > 0) {
                 CUDALLM_CL(cl_moe_expert_gemv_rows(L.gate_e.type, L.gate_e.ptr, L.up_e.ptr, L.gate_e.stride, (int)FF,
                                                    Hi, pxn, Hi, (int)Kr, pids, (int)(m * Kr), R, W, pea, s));
                 CUDALLM_CL(cl_moe_expert_gemv_rows(L.down_e.type, L.down_e.ptr, nullptr, L.down_e.stride, Hi, (int)FF,
@@ -592,6 +609,17 @@ struct CudaMoeLLM::Impl {
             else if (v != "batched" && !v.empty())
                 throw std::invalid_argument("CUDALLM_MOE_PREFILL must be batched or serial");
         }
+        // Batched prefill's routed experts: "grouped" (default; routes bucketed by
+        // expert, each expert's rows read once per layer) or "routes" (one pass
+        // of the expert's rows per route); both give the same rows
+        if (const char* e = std::getenv("CUDALLM_MOE_EXPERTS")) {
+            const std::string v(e);
+            if (v == "routes")
+                grouped_experts = false;
+            else if (v != "grouped" && !v.empty())
+                throw std::invalid_argument("CUDALLM_MOE_EXPERTS must be grouped or routes");
+        }
+        if (E_l >= 4096) grouped_experts = false;  // beyond cl_moe_group_routes' bucket table
         CUDALLM_CUDA(cudaStreamSynchronize(stream));
     }
 

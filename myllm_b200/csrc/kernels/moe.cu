@@ -241,6 +241,179 @@ __global__ void __launch_bounds__(kExpThreads)
     if ((lane & (G - 1)) == 0 && idx < kExpRows && idx < rows) y[(size_t)r * n + row0 + idx] = v;
 }
 
+// ---- grouped expert GEMV (prefill) --------------------------------------------
+// The per-route kernel above encodes a route's input in every CTA of the
+// route and reads an expert's rows once per route that picked it.  A prompt
+// chunk of m tokens makes m * top_k routes over at most n_experts experts, so
+// prefill groups them by expert (the reference evaluates a prompt's
+// (token, expert) pairs expert by expert: moe_llm.mm:2692-2843, 3087-3108):
+//   1. route_group_kernel buckets this rank's routes by local expert
+//      (offsets [n_local + 1], route list; once per layer, shared by the
+//      gate/up and the down product);
+//   2. xq_planes_kernel encodes every input row once into the XQ unit planes
+//      that expert_gemv_kernel builds in shared memory ([input][unit][8]);
+//   3. expert_grouped_kernel: CTA (row block, local expert) walks the
+//      expert's routes kGroupChunk at a time.  Per route and row it forms the
+//      same unit dots in the same order as expert_gemv_kernel, so each output
+//      equals that kernel's, while the expert's rows are read from HBM once
+//      and come from L1 for the routes after the first.
+constexpr int kGroupThreads = 1024, kMaxGroupExperts = 4096, kGroupChunk = 4;
+
+__global__ void __launch_bounds__(kGroupThreads)
+    route_group_kernel(const int* ids, int routes, int n_local, int rank, int world, int* offsets, int* list) {
+    __shared__ int cnt[kMaxGroupExperts];
+    __shared__ int warp_tot[kGroupThreads / 32];
+    grid_launch_dependents();
+    grid_wait();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < kMaxGroupExperts; e += kGroupThreads) cnt[e] = 0;
+    __syncthreads();
+    for (int r = tid; r < routes; r += kGroupThreads) {
+        const int e = ids[r];
+        if (e >= 0 && e % world == rank && e / world < n_local) atomicAdd(&cnt[e / world], 1);
+    }
+    __syncthreads();
+    // exclusive scan: thread t owns experts [4t, 4t + 4)
+    constexpr int kPer = kMaxGroupExperts / kGroupThreads;
+    int own[kPer], run = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        own[i] = run;
+        run += cnt[kPer * tid + i];
+    }
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += warp_tot[w];
+    base += incl - run;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int e = kPer * tid + i;
+        cnt[e] = base + own[i];  // from here on: the next free slot of expert e
+        if (e <= n_local) offsets[e] = base + own[i];
+    }
+    __syncthreads();
+    for (int r = tid; r < routes; r += kGroupThreads) {
+        const int e = ids[r];
+        if (e >= 0 && e % world == rank && e / world < n_local) list[atomicAdd(&cnt[e / world], 1)] = r;
+    }
+}
+
+// Plane p of unit u of input row i at planes[(i * units + u) * 8 + p]: limbs
+// (chunk c, limb l) at 3c + l, the chunk sums at 6, (xs, xsum) at 7.
+// skip_remote (one input per route): rows of other ranks' routes are skipped.
+__global__ void xq_planes_kernel(const float* x, int x_stride, int inputs, int units, const int* ids, int rank,
+                                 int world, int skip_remote, uint4* planes) {
+    grid_launch_dependents();
+    grid_wait();
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)inputs * units) return;
+    const int i = (int)(t / units), u = (int)(t - (long long)i * units);
+    if (skip_remote && ids[i] % world != rank) return;
+    const float* xr = x + (size_t)i * x_stride + 32 * u;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 f = reinterpret_cast<const float4*>(xr)[q];
+        v[4 * q] = f.x;
+        v[4 * q + 1] = f.y;
+        v[4 * q + 2] = f.z;
+        v[4 * q + 3] = f.w;
+    }
+    XUnit xu;
+    encode_unit(v, xu);
+    uint4* p = planes + (size_t)t * 8;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+            const int4 q = xu.l[c][l];
+            p[3 * c + l] = make_uint4((uint32_t)q.x, (uint32_t)q.y, (uint32_t)q.z, (uint32_t)q.w);
+        }
+    p[6] = make_uint4((uint32_t)xu.s[0].x, (uint32_t)xu.s[0].y, (uint32_t)xu.s[1].x, (uint32_t)xu.s[1].y);
+    p[7] = make_uint4(__float_as_uint(xu.xs), __float_as_uint(xu.xsum), 0u, 0u);
+}
+
+template <int F, bool SW>
+__global__ void __launch_bounds__(kExpThreads)
+    expert_grouped_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ w_up, long long stride, int n,
+                          int k, const uint4* planes, int x_group, const int* offsets, const int* list, float* y) {
+    constexpr int NV = SW ? 2 * kExpRows : kExpRows;
+    grid_launch_dependents();
+    grid_wait();
+    const int local = blockIdx.y;
+    const int beg = offsets[local], end = offsets[local + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * kExpWarps + warp) * kExpRows;
+    if (beg >= end || row0 >= n) return;
+    const int rows = min(kExpRows, n - row0);
+    const int units = k / 32;
+    const int nb = (F == CL_TYPE_Q8_0 || F == CL_TYPE_Q5_0) ? units : units / 8;
+    const uint8_t* rp[NV];
+#pragma unroll
+    for (int j = 0; j < kExpRows; ++j) {
+        const size_t off = ((size_t)local * n + row0 + min(j, rows - 1)) * (size_t)stride;
+        rp[j] = w + off;
+        if (SW) rp[kExpRows + j] = w_up + off;
+    }
+    constexpr int G = 32 / NV;
+    const int idx = red_index<NV>(lane);
+    for (int c0 = beg; c0 < end; c0 += kGroupChunk) {
+        const int nr = min(kGroupChunk, end - c0);
+        int r[kGroupChunk];
+        const uint4* xp[kGroupChunk];
+#pragma unroll
+        for (int q = 0; q < kGroupChunk; ++q) {
+            r[q] = list[c0 + min(q, nr - 1)];
+            xp[q] = planes + (size_t)(r[q] / x_group) * units * 8;
+        }
+        float acc[kGroupChunk][NV];
+#pragma unroll
+        for (int q = 0; q < kGroupChunk; ++q)
+#pragma unroll
+            for (int j = 0; j < NV; ++j) acc[q][j] = 0.0f;
+        for (int u = lane; u < units; u += 32) {
+#pragma unroll
+            for (int q = 0; q < kGroupChunk; ++q) {
+                if (q >= nr) break;
+                const uint4* p = xp[q] + (size_t)u * 8;
+                XUnit xu;
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int l = 0; l < 3; ++l) {
+                        const uint4 t = p[3 * c + l];
+                        xu.l[c][l] = make_int4((int)t.x, (int)t.y, (int)t.z, (int)t.w);
+                    }
+                const uint4 s4 = p[6], f4 = p[7];
+                xu.s[0] = make_int2((int)s4.x, (int)s4.y);
+                xu.s[1] = make_int2((int)s4.z, (int)s4.w);
+                xu.xs = __uint_as_float(f4.x);
+                xu.xsum = __uint_as_float(f4.y);
+#pragma unroll
+                for (int j = 0; j < NV; ++j) acc[q][j] += Fmt<F>::template dot<GlobalLd>(rp[j], u, nb, xu);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kGroupChunk; ++q) {
+            if (q >= nr) break;
+            float v = warp_sum_many<NV>(acc[q], lane);
+            if (SW) {
+                const float up = __shfl_down_sync(0xffffffffu, v, (kExpRows * G) & 31);
+                v = v * sigmoid_stable(v) * up;
+            }
+            if ((lane & (G - 1)) == 0 && idx < kExpRows && idx < rows) y[(size_t)r[q] * n + row0 + idx] = v;
+        }
+    }
+}
+
 // ---- expert combine: out = residual + (sum_r w_r y_r + sigmoid(g) * shared) ----
 __global__ void combine_kernel(const float* y, const int* ids, const float* wts,
                                int routes, int n, int rank, int world, const float* shared_y,
@@ -597,6 +770,30 @@ cudaError_t launch_expert_type(int type, const void* w, const void* w_up, long l
     }
 }
 
+template <int F, bool SW>
+cudaError_t launch_grouped(const void* w, const void* w_up, long long stride, int n, int k, const uint4* planes,
+                           int x_group, const int* offsets, const int* list, int n_local, float* y,
+                           cudaStream_t stream) {
+    const dim3 grid((n + kExpWarps * kExpRows - 1) / (kExpWarps * kExpRows), n_local);
+    return launch_pdl(expert_grouped_kernel<F, SW>, grid, dim3(kExpThreads), 0, stream,
+                      static_cast<const uint8_t*>(w), static_cast<const uint8_t*>(w_up), stride, n, k, planes,
+                      x_group, offsets, list, y);
+}
+
+template <bool SW>
+cudaError_t launch_grouped_type(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                                const uint4* planes, int xg, const int* offsets, const int* list, int n_local,
+                                float* y, cudaStream_t stream) {
+    switch (type) {
+    case CL_TYPE_Q4_K: return launch_grouped<CL_TYPE_Q4_K, SW>(w, w_up, stride, n, k, planes, xg, offsets, list, n_local, y, stream);
+    case CL_TYPE_Q5_K: return launch_grouped<CL_TYPE_Q5_K, SW>(w, w_up, stride, n, k, planes, xg, offsets, list, n_local, y, stream);
+    case CL_TYPE_Q6_K: return launch_grouped<CL_TYPE_Q6_K, SW>(w, w_up, stride, n, k, planes, xg, offsets, list, n_local, y, stream);
+    case CL_TYPE_Q8_0: return launch_grouped<CL_TYPE_Q8_0, SW>(w, w_up, stride, n, k, planes, xg, offsets, list, n_local, y, stream);
+    case CL_TYPE_Q5_0: return launch_grouped<CL_TYPE_Q5_0, SW>(w, w_up, stride, n, k, planes, xg, offsets, list, n_local, y, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 int status(cudaError_t e) { return e == cudaSuccess ? CL_OK : CL_ERR_CUDA; }
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
@@ -658,6 +855,49 @@ CL_API int cl_moe_expert_gemv_rows(int type, const void* w, const void* w_up, lo
                                                   rank, world, y, stream)
                        : launch_expert_type<false>(type, w, nullptr, stride, n, k, x, x_stride, x_group, ids,
                                                    routes, rank, world, y, stream));
+}
+
+CL_API size_t cl_moe_xq_planes_bytes(int inputs, int k) {
+    if (inputs <= 0 || k <= 0 || k % 32) return 0;
+    return (size_t)inputs * (size_t)(k / 32) * 8 * sizeof(uint4);
+}
+
+CL_API int cl_moe_group_routes(const int* ids, int routes, int n_local, int rank, int world, int* offsets, int* list,
+                               cudaStream_t stream) {
+    if (ids == nullptr || offsets == nullptr || list == nullptr || routes <= 0 || routes > (1 << 24) ||
+        n_local <= 0 || n_local >= kMaxGroupExperts || world <= 0 || rank < 0 || rank >= world)
+        return CL_ERR_INVALID;
+    return status(launch_pdl(route_group_kernel, dim3(1), dim3(kGroupThreads), 0, stream, ids, routes, n_local, rank,
+                             world, offsets, list));
+}
+
+CL_API int cl_moe_expert_gemv_grouped(int type, const void* w, const void* w_up, long long stride, int n, int k,
+                                      const float* x, int x_stride, int x_group, const int* ids, int routes,
+                                      int rank, int world, const int* offsets, const int* list, int n_local,
+                                      void* planes, size_t planes_bytes, float* y, cudaStream_t stream) {
+    if (w == nullptr || x == nullptr || ids == nullptr || offsets == nullptr || list == nullptr ||
+        planes == nullptr || y == nullptr || n <= 0 || k <= 0 || k % 32 || x_group <= 0 || routes <= 0 ||
+        routes > (1 << 24) || n_local <= 0 || n_local >= kMaxGroupExperts || world <= 0 || rank < 0 ||
+        rank >= world || x_stride < 0 || x_stride % 4 || !aligned16(w) || !aligned16(x) || !aligned16(planes) ||
+        stride % 16 || cl_native_row_bytes(type, k) < 0 || stride < cl_row_stride(type, k) ||
+        (w_up && !aligned16(w_up)))
+        return CL_ERR_INVALID;
+    if (type != CL_TYPE_Q4_K && type != CL_TYPE_Q5_K && type != CL_TYPE_Q6_K && type != CL_TYPE_Q8_0 &&
+        type != CL_TYPE_Q5_0)
+        return CL_ERR_UNSUPPORTED;
+    const int inputs = (routes + x_group - 1) / x_group, units = k / 32;
+    if (planes_bytes < cl_moe_xq_planes_bytes(inputs, k)) return CL_ERR_INVALID;
+    uint4* pl = static_cast<uint4*>(planes);
+    const long long work = (long long)inputs * units;
+    const int threads = 256;
+    cudaError_t e = launch_pdl(xq_planes_kernel, dim3((unsigned)((work + threads - 1) / threads)), dim3(threads), 0,
+                               stream, x, x_stride, inputs, units, ids, rank, world,
+                               (x_group == 1 && world > 1) ? 1 : 0, pl);
+    if (e != cudaSuccess) return status(e);
+    return status(w_up ? launch_grouped_type<true>(type, w, w_up, stride, n, k, pl, x_group, offsets, list, n_local,
+                                                   y, stream)
+                       : launch_grouped_type<false>(type, w, nullptr, stride, n, k, pl, x_group, offsets, list,
+                                                    n_local, y, stream));
 }
 
 CL_API int cl_moe_combine_rows(const float* y, const int* ids, const float* weights, int routes, int n, int rank,

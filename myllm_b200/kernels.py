@@ -314,6 +314,46 @@ def moe_expert_gemv(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor
     return y
 
 
+def moe_expert_gemv_rows(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, ids: torch.Tensor,
+                         x_stride: int, x_group: int, w_up=None, rank: int = 0, world: int = 1, out=None):
+    """Prefill form: route r reads input row r // x_group (rows x_stride apart)."""
+    routes = ids.numel()
+    y = out if out is not None else torch.zeros((routes, n), dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_moe_expert_gemv_rows(gtype, _p(w), _p(w_up), w.stride(0), n, k, _p(x), x_stride, x_group,
+                                                _p(ids), routes, rank, world, _p(y), _stream()),
+          "cl_moe_expert_gemv_rows")
+    return y
+
+
+def moe_group_routes(ids: torch.Tensor, n_local: int, rank: int = 0, world: int = 1):
+    """(offsets [n_local + 1], list [routes]) of this rank's routes by local expert."""
+    routes = ids.numel()
+    offsets = torch.empty(n_local + 1, dtype=torch.int32, device=ids.device)
+    lst = torch.empty(routes, dtype=torch.int32, device=ids.device)
+    check(_native.lib().cl_moe_group_routes(_p(ids), routes, n_local, rank, world, _p(offsets), _p(lst), _stream()),
+          "cl_moe_group_routes")
+    return offsets, lst
+
+
+def moe_expert_gemv_grouped(gtype: int, w: torch.Tensor, n: int, k: int, x: torch.Tensor, ids: torch.Tensor,
+                            x_stride: int, x_group: int, n_local: int, w_up=None, rank: int = 0, world: int = 1,
+                            groups=None, planes=None, out=None):
+    """The grouped prefill expert GEMV; `groups` = moe_group_routes(...) over
+    the same ids (made here when None), `planes` its scratch (made when None)."""
+    routes = ids.numel()
+    if groups is None:
+        groups = moe_group_routes(ids, n_local, rank, world)
+    nbytes = int(_native.lib().cl_moe_xq_planes_bytes((routes + x_group - 1) // x_group, k))
+    if planes is None:
+        planes = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device)
+    y = out if out is not None else torch.zeros((routes, n), dtype=torch.float32, device=x.device)
+    check(_native.lib().cl_moe_expert_gemv_grouped(gtype, _p(w), _p(w_up), w.stride(0), n, k, _p(x), x_stride,
+                                                   x_group, _p(ids), routes, rank, world, _p(groups[0]),
+                                                   _p(groups[1]), n_local, _p(planes), planes.numel(), _p(y),
+                                                   _stream()), "cl_moe_expert_gemv_grouped")
+    return y
+
+
 def moe_combine(y: torch.Tensor, ids, wts, shared_y=None, shared_logit=None, residual=None, rank=0, world=1):
     routes, n = y.shape
     out = torch.empty(n, dtype=torch.float32, device=y.device)

@@ -202,6 +202,34 @@ def test_decode_pack_sizes():
     assert lib.cl_decode_pack(sg.Q4_K, None, 2016, 16, 3584, None, 1 << 20, None) == 1
 
 
+def test_grouped_expert_sizes_and_checks():
+    """The grouped prefill expert GEMV: XQ planes of 128 bytes per 32 input
+    columns per input row; at most 4095 local experts; the planes scratch
+    must hold every input row (ceil(routes / x_group) of them); the checks
+    come before any launch."""
+    lib = _native.lib()
+    assert lib.cl_moe_xq_planes_bytes(64, 2048) == 64 * 64 * 128
+    assert lib.cl_moe_xq_planes_bytes(512, 512) == 512 * 16 * 128
+    assert lib.cl_moe_xq_planes_bytes(0, 2048) == 0 and lib.cl_moe_xq_planes_bytes(4, 100) == 0
+    F = 1 << 20
+    assert lib.cl_moe_group_routes(F, 8, 4096, 0, 1, F, F, None) == 1   # too many local experts
+    assert lib.cl_moe_group_routes(F, 8, 256, 2, 2, F, F, None) == 1    # rank outside the world
+    assert lib.cl_moe_group_routes(F, 0, 256, 0, 1, F, F, None) == 1    # no routes
+    assert lib.cl_moe_group_routes(F, 8, 256, 0, 1, F, F, None) == 3    # reaches the launch (no GPU here)
+    st = lib.cl_row_stride(sg.Q4_K, 256)
+
+    def grouped(routes=8, x_group=4, n_local=4, planes_bytes=2 * 8 * 128, gtype=sg.Q4_K, x_stride=256):
+        return lib.cl_moe_expert_gemv_grouped(gtype, F, None, st, 16, 256, F, x_stride, x_group, F, routes, 0, 1, F,
+                                              F, n_local, F, planes_bytes, F, None)
+
+    assert grouped() == 3
+    assert grouped(planes_bytes=2 * 8 * 128 - 16) == 1                  # planes too small for 2 input rows
+    assert grouped(routes=9, planes_bytes=2 * 8 * 128) == 1            # 9 routes over groups of 4: 3 rows
+    assert grouped(routes=9, planes_bytes=3 * 8 * 128) == 3
+    assert grouped(x_group=0) == 1 and grouped(n_local=0) == 1 and grouped(x_stride=6) == 1
+    assert grouped(gtype=sg.F32) != 3
+
+
 def test_gemv_pack_sizes_and_checks():
     """The fragment-packed GEMV layout: units of 16 rows x one super-block
     (Q4_K 2304 bytes, Q6_K 3360), ragged row counts padded to a whole tile
@@ -304,6 +332,9 @@ def test_misaligned_pointers_are_rejected_where_kernels_use_wide_loads():
                                 ("q", "kc", "vc")),
         "cl_moe_expert_gemv": (lambda w=F, x=F: lib.cl_moe_expert_gemv(q4, w, F, st, 16, 256, x, 0, F, 2, 0, 1, F,
                                                                        None), ("w", "x")),
+        "cl_moe_expert_gemv_grouped": (lambda w=F, x=F, planes=2 * F: lib.cl_moe_expert_gemv_grouped(
+            q4, w, None, st, 16, 256, x, 256, 1, F, 2, 0, 1, F, F, 4, planes, 4096, F, None),
+                                       ("w", "x", "planes")),
         "cl_gemv_f32": (lambda w=F, x=F: lib.cl_gemv_f32(w, 16, 256, x, F, None), ("w", "x")),
         "cl_peer_allreduce": (lambda inp=F, out=2 * F: lib.cl_peer_allreduce(
             inp, out, 256, 256, 0, 1, (ctypes.c_void_p * 1)(4 * F), None), ("inp", "out")),
