@@ -518,6 +518,46 @@ def moe_kernel_times(peak_gbs: float, seed: int):
         timed("expert_down", lambda i: K.check(lib.cl_moe_expert_gemv(
             q4, p(down), None, down.stride(0), H, FF, p(act), FF, p(sets[i % len(sets)]), Kr, 0, 1, p(ey), st()),
             "experts"), 32, dn_bytes)
+        # prefill: one layer's routed experts (gate/up + SwiGLU, down) for a
+        # chunk of T tokens, per route (cl_moe_expert_gemv_rows) and grouped by
+        # expert (cl_moe_group_routes + cl_moe_expert_gemv_grouped); the two
+        # forms' rows compared bit for bit
+        pre = {}
+        for T in (64, 512):
+            rng = torch.Generator().manual_seed(seed + T)
+            pids = torch.stack([torch.randperm(E, generator=rng)[:Kr] for _ in range(T)]).reshape(-1).to(
+                dtype=torch.int32, device=xn.device)
+            px = torch.randn(T, H, device="cuda")
+            rt = T * Kr
+            a_r, y_r = torch.empty(rt, FF, device="cuda"), torch.empty(rt, H, device="cuda")
+            a_g, y_g = torch.empty(rt, FF, device="cuda"), torch.empty(rt, H, device="cuda")
+            offs = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+            lst = torch.empty(rt, dtype=torch.int32, device="cuda")
+            nbp = max(int(lib.cl_moe_xq_planes_bytes(T, H)), int(lib.cl_moe_xq_planes_bytes(rt, FF)))
+            planes = torch.empty(nbp, dtype=torch.uint8, device="cuda")
+
+            def per_route(i, px=px, pids=pids, rt=rt, a_r=a_r, y_r=y_r):
+                K.check(lib.cl_moe_expert_gemv_rows(q4, p(gate), p(up), gate.stride(0), FF, H, p(px), H, Kr,
+                                                    p(pids), rt, 0, 1, p(a_r), st()), "experts_rows")
+                K.check(lib.cl_moe_expert_gemv_rows(q4, p(down), None, down.stride(0), H, FF, p(a_r), FF, 1,
+                                                    p(pids), rt, 0, 1, p(y_r), st()), "experts_rows")
+
+            def grouped(i, px=px, pids=pids, rt=rt, a_g=a_g, y_g=y_g, offs=offs, lst=lst, planes=planes, nbp=nbp):
+                K.check(lib.cl_moe_group_routes(p(pids), rt, E, 0, 1, p(offs), p(lst), st()), "group_routes")
+                K.check(lib.cl_moe_expert_gemv_grouped(q4, p(gate), p(up), gate.stride(0), FF, H, p(px), H, Kr,
+                                                       p(pids), rt, 0, 1, p(offs), p(lst), E, p(planes), nbp,
+                                                       p(a_g), st()), "experts_grouped")
+                K.check(lib.cl_moe_expert_gemv_grouped(q4, p(down), None, down.stride(0), H, FF, p(a_g), FF, 1,
+                                                       p(pids), rt, 0, 1, p(offs), p(lst), E, p(planes), nbp,
+                                                       p(y_g), st()), "experts_grouped")
+            try:
+                t_r, t_g = graph_time_us(per_route, 4), graph_time_us(grouped, 4)
+                pre[str(T)] = {"routes_us": round(t_r, 1), "grouped_us": round(t_g, 1),
+                               "speedup": round(t_r / t_g, 2),
+                               "bit_identical": bool(torch.equal(a_r, a_g) and torch.equal(y_r, y_g))}
+            except Exception as e:
+                pre[str(T)] = {"error": f"{type(e).__name__}: {e}"}
+        out["prefill_experts"] = pre
         del gate, up, down
     except Exception as e:
         out["experts"] = {"error": f"{type(e).__name__}: {e}"}

@@ -254,9 +254,13 @@ def test_moe_kernel_timing_code_runs(monkeypatch):
     calls = _dry_run(monkeypatch)
     out = bench.moe_kernel_times(6545.0, 1)
     assert set(out) == {"router_gemv_f32", "route_topk", "expert_gate_up_swiglu", "expert_down", "gdn_prep",
-                        "gdn_step", "attn_gate_prep", "attn_decode_512_keys"}
+                        "gdn_step", "attn_gate_prep", "attn_decode_512_keys", "prefill_experts"}
     assert all("error" not in v for v in out.values()), out
     assert calls["cl_moe_expert_gemv"] > 0 and calls["cl_gdn_step"] > 0 and calls["cl_attn_decode"] > 0
+    # MoE prefill experts, per route and grouped, at 64- and 512-token chunks
+    assert set(out["prefill_experts"]) == {"64", "512"}
+    assert all("error" not in v for v in out["prefill_experts"].values()), out["prefill_experts"]
+    assert calls["cl_moe_expert_gemv_rows"] > 0 and calls["cl_moe_expert_gemv_grouped"] > 0
 
 
 class _Event:
