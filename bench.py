@@ -149,6 +149,31 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peaks():
+    """(sustained, burst) dense bf16 TFLOP/s of one GPU and where they come
+    from: the measured cuBLAS GEMM, else the earlier pool measurement."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops_sustained" in d and "bf16_tflops" in d:
+            return float(d["bf16_tflops_sustained"]), float(d["bf16_tflops"]), "measured"
+    return 1400.0, 1590.0, "fallback"
+
+
+def prefill_flops(spec, tokens: int) -> int:
+    """Useful FLOPs of a qwen2 prefill of `tokens` tokens from position 0
+    (2 per multiply-add): every layer's q/k/v/o and gate/up/down products
+    over all rows, causal attention (row i scores and mixes keys 0..i), and
+    the LM head on the last row only (prefill returns the next token)."""
+    H, F, T = spec.hidden, spec.ffn, tokens
+    d = H // spec.heads
+    kvd = spec.kv_heads * d
+    per_row = 2 * (H * H + 2 * kvd * H + H * H + 2 * F * H + H * F)
+    attn = 2 * 2 * spec.heads * d * (T * (T + 1) // 2)
+    return spec.layers * (T * per_row + attn) + 2 * spec.vocab * H
+
+
 def profile_traffic(kernel: str, shape=None, algorithmic=None):
     """Per-launch DRAM bytes of `kernel` from the committed ncu summaries
     (profiles/traffic.json: the shape each was captured at, its DRAM bytes and
@@ -212,6 +237,22 @@ def decode_bytes_per_token(spec, position: int) -> int:
     out_t = spec.output_type if spec.output_type is not None else spec.embed_type
     total += spec.vocab * sg.row_bytes(out_t, H) + sg.row_bytes(spec.embed_type, H) + 4 * H
     return total
+
+
+def prefill_roofline(spec, tokens: int, prefill_ms: float, world: int, moe: bool):
+    """The prefill as a tensor-bound job: useful TFLOP/s per GPU against the
+    measured dense bf16 GEMM peak (sustained; the burst fraction beside it)."""
+    if moe:
+        return {"unavailable": "qwen35moe prefill: the routed experts and the DeltaNet scan are not GEMM-shaped "
+                               "work; no tensor roofline is stated for them"}
+    sus, burst, kind = measured_tensor_peaks()
+    flops = prefill_flops(spec, tokens)
+    ach = flops / world / (prefill_ms * 1e-3) / 1e12 if prefill_ms > 0 else 0.0
+    return {"bound": "tensor", "achieved": ach, "peak": sus, "unit": "TFLOP/s", "frac": ach / sus,
+            "burst_peak": burst, "burst_frac": ach / burst, "flops": flops,
+            "peak_kind": f"{kind} bf16_tflops_sustained (cuBLAS bf16 GEMM, seconds-long loop), per GPU",
+            "note": "useful FLOPs (2 per multiply-add: layer GEMMs, causal attention, last-row LM head); the "
+                    "default FP32-grade path (split FP16) issues three tensor-core products per useful one"}
 
 
 def moe_decode_bytes(spec, position: int):
@@ -816,7 +857,8 @@ def make_line(name, spec, args, world, rank, *, dev_ms, e2e_ms, prefill_ms, pref
         "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "prefill": {"value": args.prompt / (prefill_ms / 1e3), "unit": "tokens/s", "tokens": args.prompt,
-                    "e2e_tokens_per_s": args.prompt / (prefill_e2e_ms / 1e3)},
+                    "e2e_tokens_per_s": args.prompt / (prefill_e2e_ms / 1e3),
+                    "roofline": prefill_roofline(spec, args.prompt, prefill_ms, world, moe)},
         "decode_hbm": {"bytes_per_token_per_gpu": tok_bytes, "achieved_gbs": tok_bytes / (ms_step * 1e-3) / 1e9,
                        "peak_gbs": peak, "frac": tok_bytes / (ms_step * 1e-3) / 1e9 / peak,
                        "peak_kind": peak_kind},

@@ -107,6 +107,18 @@ def test_scaling_base_failure_is_reported_not_raised(monkeypatch):
     assert out["unavailable"] == "RuntimeError: no device"
 
 
+def test_prefill_flops_of_the_qwen2_shapes():
+    """7B at 512 tokens: 28 layers of q/k/v/o and gate/up/down products over
+    512 rows (k and v are 512 wide: 4 KV heads of 128), causal attention over
+    28 heads of 128, and the last row's LM head: ~6.74 TFLOP."""
+    spec = sg.CONFIGS["qwen2.5-7b"]
+    H, F, L = 3584, 18944, 28
+    gemm = L * 512 * 2 * (2 * H * H + 2 * 512 * H + 3 * F * H)
+    attn = L * 2 * 2 * 28 * 128 * (512 * 513 // 2)
+    assert bench.prefill_flops(spec, 512) == gemm + attn + 2 * 152064 * H
+    assert 6.7e12 < bench.prefill_flops(spec, 512) < 6.8e12
+
+
 def test_moe_bytes_per_token():
     spec = sg.MOE_CONFIGS["qwen3.6-35b-a3b"]
     rep, exp = bench.moe_decode_bytes(spec, 0)
@@ -192,6 +204,14 @@ def test_json_line_contract(name, world):
     assert line["e2e"]["value"] == pytest.approx(128 / 0.26)
     assert set(line["roofline"]) >= {"bound", "achieved", "peak", "unit", "frac", "traffic"}
     assert line["roofline"]["frac"] == pytest.approx(5000 / 6545)
+    pr = line["prefill"]["roofline"]
+    if "a3b" in name:
+        assert "unavailable" in pr
+    else:  # useful FLOPs per GPU over the measured bf16 GEMM peak
+        sus, burst, _ = bench.measured_tensor_peaks()
+        ach = bench.prefill_flops(spec, 512) / world / 0.1 / 1e12
+        assert pr["bound"] == "tensor" and pr["unit"] == "TFLOP/s"
+        assert pr["achieved"] == pytest.approx(ach) and pr["frac"] == pytest.approx(ach / sus)
     assert "workload" in line["config"] and name in line["config"]["workload"]
     assert line["config"]["parallelism"] == ("single GPU" if world == 1 else
                                              ("ep" if "a3b" in name else "tp") + str(world))
