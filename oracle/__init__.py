@@ -13,6 +13,10 @@ Two checkers live here:
   sources into ``oracle/_ref/libref_cpu.so`` by ``oracle/Makefile``, driven
   through ``ref_harness.cpp`` so the logits are visible.  Present only when
   the reference sources were available at build time.
+* ``metal_ref``: the reference's Metal compute kernels for qwen35moe
+  (``metal_llm.metal``) compiled as C++ into ``oracle/_ref/libref_metal.so``
+  by the same target and run on the host in the reference's dispatch order,
+  the check of the qwen35moe FP64 restatement (``moe_fp64.py``).
 """
 from __future__ import annotations
 

@@ -3,9 +3,12 @@
 The reference has no CPU implementation of qwen35moe (Metal only), so parity
 for the MoE model rests on this host re-implementation of its formulas, run
 in float64 over the reference-exact FP32 weight values (``oracle.dequant``).
-Parity is therefore pinned to this restatement, not to reference outputs:
-parity unpinned (no reference test, golden vector or output exists for this
-path to check the restatement against).
+The reference ships no test or golden vector for this path; instead the
+per-step functions below (``deltanet_token``, ``route_probs``,
+``routed_experts``, ``attention_token``) are checked against the reference's
+own Metal kernels compiled as C++ and run on the host in the reference's
+dispatch order (``oracle/metal_ref.py``, tests/test_oracle_moe_pinned.py).
+The layer loop that chains them is restated from moe_llm.mm, not executed.
 
 Followed step by step (reference files):
 
@@ -56,6 +59,98 @@ def _silu(v):
 
 def _softplus(v):
     return np.where(v > 20.0, v, np.where(v < -20.0, np.exp(np.minimum(v, 0.0)), np.log1p(np.exp(np.minimum(v, 20.0)))))
+
+
+# ---- one mixer / router / expert step after its projections (float64) ----
+# The class below calls these; tests/test_oracle_moe_pinned.py checks them
+# against the reference's own kernels run in the reference's order
+# (oracle/metal_ref.py).
+
+def rope_neox(v, pos, rot, theta):
+    """NeoX RoPE of one head's first `rot` dims at position `pos`
+    (metal_llm.metal:928-967: pair i with i + rot/2, angle pos * theta^(-2i/rot))."""
+    half = rot // 2
+    p = np.arange(half, dtype=np.float64)
+    ang = pos * theta ** (-2.0 * p / rot)
+    c, s = np.cos(ang), np.sin(ang)
+    a, b = v[:half].copy(), v[half:rot].copy()
+    out = v.copy()
+    out[:half] = a * c - b * s
+    out[half:rot] = a * s + b * c
+    return out
+
+
+def attention_token(mixed, k, v, q_norm, k_norm, pos, k_hist, v_hist, hq, hkv, hd, rot, theta, eps):
+    """Gated attention of one token between its projections
+    (moe_llm.mm:2256-2428): split [query, gate] per head, RMSNorm and RoPE of
+    q and k per head, append k / v to the history lists, softmax over the
+    keys so far, the value mix, times sigmoid(gate)."""
+    mixed = mixed.reshape(hq, 2, hd)
+    q, gate = mixed[:, 0, :], mixed[:, 1, :].reshape(-1)
+    k = k.reshape(hkv, hd)
+    v = v.reshape(hkv, hd)
+    q = np.stack([rope_neox(_rmsnorm(q[h], q_norm, eps), pos, rot, theta) for h in range(hq)])
+    k = np.stack([rope_neox(_rmsnorm(k[h], k_norm, eps), pos, rot, theta) for h in range(hkv)])
+    k_hist.append(k)
+    v_hist.append(v)
+    K = np.stack(k_hist)  # [T, hkv, hd]
+    Vv = np.stack(v_hist)
+    grp = hq // hkv
+    out = np.empty((hq, hd))
+    for h in range(hq):
+        g = h // grp
+        s = K[:, g, :] @ q[h] / np.sqrt(hd)
+        e = np.exp(s - s.max())
+        out[h] = (e / e.sum()) @ Vv[:, g, :]
+    return out.reshape(-1) * _sigmoid(gate)
+
+
+def deltanet_token(qkv, z, beta_raw, alpha, dt_bias, a, conv_w, hist, S, norm, sg, sd, sr, eps):
+    """One token of the Gated DeltaNet mixer after its projections
+    (moe_llm.mm:2470-2635).  conv_w [channels, kernel], hist [kernel - 1,
+    channels], S [value heads, d, d] (row = key dim) updated in place.
+    Returns (gated output [value heads * d], the new history)."""
+    kw = sg * sd
+    beta = _sigmoid(beta_raw)
+    decay = np.exp(_softplus(alpha + dt_bias) * a)
+    cat = np.concatenate([hist, qkv[None, :]], axis=0)  # [kernel, channels]
+    conv = np.einsum("tc,ct->c", cat, conv_w)
+    act = _silu(conv)
+    q = act[:kw].reshape(sg, sd)
+    k = act[kw:2 * kw].reshape(sg, sd)
+    v = act[2 * kw:].reshape(sr, sd)
+    q = q / np.sqrt((q * q).sum(axis=1, keepdims=True) + eps)
+    k = k / np.sqrt((k * k).sum(axis=1, keepdims=True) + eps)
+    o = np.empty((sr, sd))
+    for h in range(sr):
+        kh = h % sg
+        S[h] *= decay[h]
+        pred = S[h].T @ k[kh]
+        delta = beta[h] * (v[h] - pred)
+        S[h] += np.outer(k[kh], delta)
+        o[h] = _rmsnorm(S[h].T @ q[kh] / np.sqrt(sd), norm, eps)
+    return o.reshape(-1) * _silu(z), cat[1:].copy()
+
+
+def route_probs(logits, k):
+    """Softmax of the router logits, the top k by strict '>' with the lower
+    expert id first on ties, renormalised (moe_llm.mm:2642-2690)."""
+    e = np.exp(logits - logits.max())
+    prob = e / e.sum()
+    order = sorted(range(len(prob)), key=lambda i: (-prob[i], i))[:k]
+    sel = prob[order]
+    return np.array(order), sel / sel.sum()
+
+
+def routed_experts(x, ids, wts, expert_rows):
+    """sum_r w_r down_e(silu(gate_e x) * up_e x) (moe_llm.mm:2692-2843);
+    expert_rows(kind, e) gives expert e's float64 rows, kind in gate / up / down."""
+    acc = np.zeros(len(x))
+    for e, wt in zip(ids, wts):
+        g = expert_rows("gate", e) @ x
+        u = expert_rows("up", e) @ x
+        acc += wt * (expert_rows("down", e) @ (_silu(g) * u))
+    return acc
 
 
 class MoeFP64:
@@ -128,89 +223,33 @@ class MoeFP64:
 
     # ---- blocks ----
     def _rope(self, v, pos):
-        half = self.rot // 2
-        p = np.arange(half, dtype=np.float64)
-        ang = pos * self.theta ** (-2.0 * p / self.rot)
-        c, s = np.cos(ang), np.sin(ang)
-        a, b = v[:half].copy(), v[half:self.rot].copy()
-        out = v.copy()
-        out[:half] = a * c - b * s
-        out[half:self.rot] = a * s + b * c
-        return out
+        return rope_neox(v, pos, self.rot, self.theta)
 
     def _attention(self, l, x):
         p = f"blk.{l}."
-        hd, hq, hkv = self.hd, self.hq, self.hkv
-        mixed = (self.w(p + "attn_q.weight") @ x).reshape(hq, 2, hd)
-        q, gate = mixed[:, 0, :], mixed[:, 1, :].reshape(-1)
-        k = (self.w(p + "attn_k.weight") @ x).reshape(hkv, hd)
-        v = (self.w(p + "attn_v.weight") @ x).reshape(hkv, hd)
-        qn, kn = self.vec(p + "attn_q_norm.weight"), self.vec(p + "attn_k_norm.weight")
-        q = np.stack([self._rope(_rmsnorm(q[h], qn, self.eps), self.pos) for h in range(hq)])
-        k = np.stack([self._rope(_rmsnorm(k[h], kn, self.eps), self.pos) for h in range(hkv)])
-        self.kc[l].append(k)
-        self.vc[l].append(v)
-        K = np.stack(self.kc[l])  # [T, hkv, hd]
-        Vv = np.stack(self.vc[l])
-        grp = hq // hkv
-        out = np.empty((hq, hd))
-        for h in range(hq):
-            g = h // grp
-            s = K[:, g, :] @ q[h] / np.sqrt(hd)
-            e = np.exp(s - s.max())
-            out[h] = (e / e.sum()) @ Vv[:, g, :]
-        gated = out.reshape(-1) * _sigmoid(gate)
+        gated = attention_token(self.w(p + "attn_q.weight") @ x, self.w(p + "attn_k.weight") @ x,
+                                self.w(p + "attn_v.weight") @ x, self.vec(p + "attn_q_norm.weight"),
+                                self.vec(p + "attn_k_norm.weight"), self.pos, self.kc[l], self.vc[l], self.hq,
+                                self.hkv, self.hd, self.rot, self.theta, self.eps)
         return self.w(p + "attn_output.weight") @ gated
 
     def _deltanet(self, l, x):
         p = f"blk.{l}."
-        sd, sg, sr = self.sd, self.sg, self.sr
-        kw = sg * sd
-        qkv = self.w(p + "attn_qkv.weight") @ x
-        z = self.w(p + "attn_gate.weight") @ x
-        beta = _sigmoid(self.w(p + "ssm_beta.weight") @ x)
-        alpha = self.w(p + "ssm_alpha.weight") @ x
-        decay = np.exp(_softplus(alpha + self.vec(p + "ssm_dt.bias")) * self.vec(p + "ssm_a"))
-        cw = self.w(p + "ssm_conv1d.weight")  # [channels, kernel]
-        cat = np.concatenate([self.hist[l], qkv[None, :]], axis=0)  # [kernel, channels]
-        conv = np.einsum("tc,ct->c", cat, cw)
-        self.hist[l] = cat[1:].copy()
-        act = _silu(conv)
-        q = act[:kw].reshape(sg, sd)
-        k = act[kw:2 * kw].reshape(sg, sd)
-        v = act[2 * kw:].reshape(sr, sd)
-        q = q / np.sqrt((q * q).sum(axis=1, keepdims=True) + self.eps)
-        k = k / np.sqrt((k * k).sum(axis=1, keepdims=True) + self.eps)
-        S = self.S[l]
-        o = np.empty((sr, sd))
-        norm = self.vec(p + "ssm_norm.weight")
-        for h in range(sr):
-            kh = h % sg
-            S[h] *= decay[h]
-            pred = S[h].T @ k[kh]
-            delta = beta[h] * (v[h] - pred)
-            S[h] += np.outer(k[kh], delta)
-            o[h] = _rmsnorm(S[h].T @ q[kh] / np.sqrt(sd), norm, self.eps)
-        gated = o.reshape(-1) * _silu(z)
+        gated, self.hist[l] = deltanet_token(
+            self.w(p + "attn_qkv.weight") @ x, self.w(p + "attn_gate.weight") @ x,
+            self.w(p + "ssm_beta.weight") @ x, self.w(p + "ssm_alpha.weight") @ x, self.vec(p + "ssm_dt.bias"),
+            self.vec(p + "ssm_a"), self.w(p + "ssm_conv1d.weight"), self.hist[l], self.S[l],
+            self.vec(p + "ssm_norm.weight"), self.sg, self.sd, self.sr, self.eps)
         return self.w(p + "ssm_out.weight") @ gated
 
     def route(self, l, x) -> Tuple[np.ndarray, np.ndarray]:
         """(expert ids, renormalised weights) for the normalised input x."""
-        logits = self.w(f"blk.{l}.ffn_gate_inp.weight") @ x
-        e = np.exp(logits - logits.max())
-        prob = e / e.sum()
-        order = sorted(range(self.E), key=lambda i: (-prob[i], i))[: self.K]
-        sel = prob[order]
-        return np.array(order), sel / sel.sum()
+        return route_probs(self.w(f"blk.{l}.ffn_gate_inp.weight") @ x, self.K)
 
     def _moe(self, l, x):
         p = f"blk.{l}."
         ids, wts = self.route(l, x)
-        acc = np.zeros(self.H)
-        for e, wt in zip(ids, wts):
-            g = self.expert(p + "ffn_gate_exps.weight", e) @ x
-            u = self.expert(p + "ffn_up_exps.weight", e) @ x
-            acc += wt * (self.expert(p + "ffn_down_exps.weight", e) @ (_silu(g) * u))
+        acc = routed_experts(x, ids, wts, lambda kind, e: self.expert(p + f"ffn_{kind}_exps.weight", e))
         sgate = _sigmoid(self.vec(p + "ffn_gate_inp_shexp.weight") @ x)
         sa = _silu(self.w(p + "ffn_gate_shexp.weight") @ x) * (self.w(p + "ffn_up_shexp.weight") @ x)
         return acc + (self.w(p + "ffn_down_shexp.weight") @ sa) * sgate
