@@ -257,4 +257,76 @@ void mref_av(const float* scores, const float* vc, float* out, uint q_rows, uint
     flat((unsigned long long)q_rows * q_heads * head_dim, [&](uint i) { metal_kv_cache_av_f32(scores, vc, out, p, i); });
 }
 
+// encode_product for one row (moe_llm.mm:1978-2030): one thread per output;
+// type 0 = F32 (metal_gevm_f32, row-major weight), else a GGML block type
+int mref_gevm(int type, const void* w, const float* x, float* out, uint n, uint k, uint row_bytes) {
+    if (type == 0) {
+        MetalGemvParams p{};
+        p.output_size = n;
+        p.input_size = k;
+        p.matrix_stride = row_bytes / 4;
+        p.matrix_transposed = 1;
+        p.has_bias = 0;
+        p.scale = 1.0f;
+        flat(n, [&](uint i) { metal_gevm_f32(static_cast<const float*>(w), x, nullptr, out, p, i); });
+        return 0;
+    }
+    MetalQuantizedProductParams p{};
+    p.m = 1;
+    p.n = n;
+    p.k = k;
+    p.activation_stride = k;
+    p.weight_row_bytes = row_bytes;
+    p.has_bias = 0;
+    p.scale = 1.0f;
+    const uchar* q = static_cast<const uchar*>(w);
+    switch (type) {
+        case 6: flat(n, [&](uint i) { metal_gevm_q5_0_f32(q, x, nullptr, out, p, i); }); return 0;
+        case 8: flat(n, [&](uint i) { metal_gevm_q8_0_f32(q, x, nullptr, out, p, i); }); return 0;
+        case 12: flat(n, [&](uint i) { metal_gevm_q4_k_f32(q, x, nullptr, out, p, i); }); return 0;
+        case 13: flat(n, [&](uint i) { metal_gevm_q5_k_f32(q, x, nullptr, out, p, i); }); return 0;
+        case 14: flat(n, [&](uint i) { metal_gevm_q6_k_f32(q, x, nullptr, out, p, i); }); return 0;
+        default: return 1;
+    }
+}
+
+// encode_embedding (moe_llm.mm:1951-1976)
+int mref_embedding(int type, const int* ids, const void* w, float* out, uint n_rows, uint size, uint vocab,
+                   uint row_bytes) {
+    MetalEmbeddingParams p{};
+    p.sequence_length = n_rows;
+    p.embedding_size = size;
+    p.vocabulary_size = vocab;
+    p.weight_row_bytes = row_bytes;
+    const uchar* q = static_cast<const uchar*>(w);
+    const unsigned long long count = (unsigned long long)n_rows * size;
+    switch (type) {
+        case 0: flat(count, [&](uint i) { metal_embedding_f32(ids, static_cast<const float*>(w), out, p, i); }); return 0;
+        case 6: flat(count, [&](uint i) { metal_embedding_q5_0_f32(ids, q, out, p, i); }); return 0;
+        case 8: flat(count, [&](uint i) { metal_embedding_q8_0_f32(ids, q, out, p, i); }); return 0;
+        case 12: flat(count, [&](uint i) { metal_embedding_q4_k_f32(ids, q, out, p, i); }); return 0;
+        case 14: flat(count, [&](uint i) { metal_embedding_q6_k_f32(ids, q, out, p, i); }); return 0;
+        default: return 1;
+    }
+}
+
+// encode_row_scale (moe_llm.mm:2204-2236): row r times row_weights[r * stride + column]
+void mref_row_scale(const float* in, const float* row_weights, float* out, uint n_rows, uint cols, uint stride,
+                    uint column) {
+    MetalRowScaleParams p{};
+    p.rows = n_rows;
+    p.cols = cols;
+    p.weight_stride = stride;
+    p.weight_column = column;
+    flat((unsigned long long)n_rows * cols, [&](uint i) { metal_row_scale_selected_f32(in, row_weights, out, p, i); });
+}
+
+// encode_binary with the residual kernel: a + b
+void mref_residual(const float* a, const float* b, float* out, uint n) {
+    MetalElementwiseParams p{};
+    p.rows = 1;
+    p.cols = n;
+    flat(n, [&](uint i) { metal_residual_f32(a, b, out, p, i); });
+}
+
 }  // extern "C"

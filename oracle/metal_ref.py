@@ -14,15 +14,21 @@ Sequences restated here (each function cites its source):
 * ``deltanet``: moe_llm.mm:2436-2640 after the projections;
 * ``route``: moe_llm.mm:2642-2690 after the router product;
 * ``experts``: moe_llm.mm:2692-2843 (routed experts only);
-* ``attention``: moe_llm.mm:2238-2434 between the projections.
+* ``attention``: moe_llm.mm:2238-2434 between the projections;
+* ``MoeReference``: one whole token step (embedding, every layer's mixer,
+  router, routed and shared experts, residuals, final norm, LM head) with
+  every product, norm and activation a reference kernel, in the layer order
+  of the reference's forward (moe_llm.mm:2845-3039).
 """
 from __future__ import annotations
 
 import ctypes
 import os
-from typing import Tuple
+from typing import Dict, Tuple
 
 import numpy as np
+
+from .gguf_read import GgufReader
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "_ref", "libref_metal.so")
@@ -49,7 +55,12 @@ _SIGS = {
     "mref_kv_write": [_p, _p, _p, _p, _u, _u, _u, _u],
     "mref_qk": [_p, _p, _p, _u, _u, _u, _u, _u, _u, _u, _u, _f],
     "mref_av": [_p, _p, _p, _u, _u, _u, _u, _u, _u, _u, _u],
+    "mref_gevm": [_i, _p, _p, _p, _u, _u, _u],
+    "mref_embedding": [_i, _p, _p, _p, _u, _u, _u, _u],
+    "mref_row_scale": [_p, _p, _p, _u, _u, _u, _u],
+    "mref_residual": [_p, _p, _p, _u],
 }
+_INT_RESULT = {"mref_expert", "mref_gevm", "mref_embedding"}
 
 
 def available() -> bool:
@@ -63,7 +74,7 @@ def lib():
         for name, args in _SIGS.items():
             fn = getattr(l, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_int if name == "mref_expert" else None
+            fn.restype = ctypes.c_int if name in _INT_RESULT else None
         _lib = l
     return _lib
 
@@ -226,3 +237,140 @@ def attention(mixed, k, v, q_norm, k_norm, k_cache, v_cache, position: int, q_he
     out = _new(T, qw)
     L.mref_av(_ptr(probs), _ptr(vc), _ptr(out), T, klen, q_heads, kv_heads, kvw, klen, head_dim, qw)
     return _binary(0, out, _unary(0, gate)), kc, vc
+
+
+def _residual(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    out = np.empty_like(a)
+    lib().mref_residual(_ptr(a), _ptr(b), _ptr(out), a.size)
+    return out
+
+
+class MoeReference:
+    """A qwen35moe GGUF run token by token through the reference's kernels.
+
+    The layer order restates the reference's forward (moe_llm.mm:2845-3039):
+    h = embed(token); per layer h += mixer(rmsnorm(h)) with the mixer the
+    gated attention or the DeltaNet of its layer kind (moe_model.cpp:164-166),
+    then h += routed experts + sigmoid(shared router) * shared expert of
+    rmsnorm(h); logits = LM head(rmsnorm(h)).  Every product is the
+    reference's one-row product kernel for the tensor's type (rows == 1, as
+    in the reference's decode), every other step the kernel the reference
+    encodes for it.  State (DeltaNet state and history, KV caches) is FP32
+    as in the reference."""
+
+    def __init__(self, path: str, max_sequence: int = 64):
+        r = GgufReader(path)
+        m = r.metadata
+        a = "qwen35moe."
+        self.H = int(m[a + "embedding_length"])
+        self.L = int(m[a + "block_count"]) - int(m.get(a + "nextn_predict_layers", 0))
+        self.E = int(m[a + "expert_count"])
+        self.K = int(m[a + "expert_used_count"])
+        self.hq = int(m[a + "attention.head_count"])
+        self.hkv = int(m[a + "attention.head_count_kv"])
+        self.hd = int(m[a + "attention.key_length"])
+        self.rot = int(m[a + "rope.dimension_count"])
+        self.theta = float(m[a + "rope.freq_base"])
+        self.eps = float(m[a + "attention.layer_norm_rms_epsilon"])
+        self.interval = int(m[a + "full_attention_interval"])
+        self.ck = int(m[a + "ssm.conv_kernel"])
+        self.sd = int(m[a + "ssm.state_size"])
+        self.sg = int(m[a + "ssm.group_count"])
+        self.sr = int(m[a + "ssm.time_step_rank"])
+        self.si = int(m[a + "ssm.inner_size"])
+        self.V = int(m["tokenizer.ggml.tokens_count"])
+        self.max_sequence = max_sequence
+        self._r = r
+        self._t: Dict[str, tuple] = {}
+        self.reset()
+
+    def is_attention(self, l: int) -> bool:
+        return (l + 1) % self.interval == 0
+
+    def reset(self):
+        self.pos = 0
+        qkvw = 2 * self.sg * self.sd + self.si
+        kvw = self.hkv * self.hd
+        self.S = {l: _new(self.sr, self.sd, self.sd) for l in range(self.L) if not self.is_attention(l)}
+        self.hist = {l: _new(self.ck - 1, qkvw) for l in range(self.L) if not self.is_attention(l)}
+        self.kc = {l: _new(self.max_sequence, kvw) for l in range(self.L) if self.is_attention(l)}
+        self.vc = {l: _new(self.max_sequence, kvw) for l in range(self.L) if self.is_attention(l)}
+
+    def t(self, name: str):
+        """(type, rows, cols, native rows [rows, row bytes]) of a tensor."""
+        if name not in self._t:
+            self._t[name] = self._r.rows(name)
+        return self._t[name]
+
+    def f32(self, name: str) -> np.ndarray:
+        gtype, rows, cols, data = self.t(name)
+        assert gtype == 0, name
+        return np.ascontiguousarray(data).view(np.float32).reshape(rows, cols)
+
+    def vec(self, name: str) -> np.ndarray:
+        return self.f32(name).reshape(-1)
+
+    def product(self, name: str, x: np.ndarray) -> np.ndarray:
+        gtype, rows, cols, data = self.t(name)
+        x = _f32(x).reshape(-1)
+        assert x.size == cols, name
+        out = _new(rows)
+        w = np.ascontiguousarray(data)
+        if lib().mref_gevm(gtype, _ptr(w), _ptr(x), _ptr(out), rows, cols, w.shape[1]) != 0:
+            raise ValueError(f"no reference product kernel for type {gtype} ({name})")
+        return out
+
+    def _rms(self, x, name):
+        return rmsnorm_rows(x[None, :], self.vec(name), self.eps)[0]
+
+    def _attention(self, l, xn):
+        p = f"blk.{l}."
+        gated, self.kc[l], self.vc[l] = attention(
+            self.product(p + "attn_q.weight", xn)[None, :], self.product(p + "attn_k.weight", xn)[None, :],
+            self.product(p + "attn_v.weight", xn)[None, :], self.vec(p + "attn_q_norm.weight"),
+            self.vec(p + "attn_k_norm.weight"), self.kc[l], self.vc[l], self.pos, self.hq, self.hkv, self.hd,
+            self.rot, self.theta, self.eps)
+        return self.product(p + "attn_output.weight", gated[0])
+
+    def _deltanet(self, l, xn):
+        p = f"blk.{l}."
+        gated, self.hist[l], self.S[l] = deltanet(
+            self.product(p + "attn_qkv.weight", xn)[None, :], self.product(p + "attn_gate.weight", xn)[None, :],
+            self.product(p + "ssm_beta.weight", xn)[None, :], self.product(p + "ssm_alpha.weight", xn)[None, :],
+            self.vec(p + "ssm_dt.bias"), self.vec(p + "ssm_a"), self.f32(p + "ssm_conv1d.weight"), self.hist[l],
+            self.S[l], self.vec(p + "ssm_norm.weight"), self.sg, self.sd, self.sr, self.eps)
+        return self.product(p + "ssm_out.weight", gated[0])
+
+    def _moe(self, l, xn):
+        p = f"blk.{l}."
+        ids, wts = route(self.product(p + "ffn_gate_inp.weight", xn)[None, :], self.K)
+        gt, _, _, gate = self.t(p + "ffn_gate_exps.weight")
+        _, _, _, up = self.t(p + "ffn_up_exps.weight")
+        dt, _, ffn, down = self.t(p + "ffn_down_exps.weight")
+        routed = experts(xn[None, :], ids, wts, gt, gate, up, dt, down, ffn)[0]
+        sgate = _unary(0, self.product(p + "ffn_gate_inp_shexp.weight", xn))
+        act = _binary(1, self.product(p + "ffn_gate_shexp.weight", xn), self.product(p + "ffn_up_shexp.weight", xn))
+        down_sh = self.product(p + "ffn_down_shexp.weight", act)
+        scaled = np.empty_like(down_sh)
+        lib().mref_row_scale(_ptr(down_sh), _ptr(sgate), _ptr(scaled), 1, down_sh.size, 1, 0)
+        return _residual(routed, scaled)
+
+    def step(self, token: int) -> np.ndarray:
+        """Advance one token; returns the logits."""
+        if self.pos >= self.max_sequence:
+            raise IndexError("capacity")
+        gtype, rows, cols, data = self.t("token_embd.weight")
+        w = np.ascontiguousarray(data)
+        ids = np.array([token], dtype=np.int32)
+        x = _new(cols)
+        if lib().mref_embedding(gtype, _ptr(ids), _ptr(w), _ptr(x), 1, cols, rows, w.shape[1]) != 0:
+            raise ValueError(f"no reference embedding kernel for type {gtype}")
+        for l in range(self.L):
+            p = f"blk.{l}."
+            xn = self._rms(x, p + "attn_norm.weight")
+            mix = self._attention(l, xn) if self.is_attention(l) else self._deltanet(l, xn)
+            x = _residual(x, mix)
+            x = _residual(x, self._moe(l, self._rms(x, p + "post_attention_norm.weight")))
+        self.pos += 1
+        return self.product("output.weight", self._rms(x, "output_norm.weight"))

@@ -8,7 +8,10 @@ per-step functions below (``deltanet_token``, ``route_probs``,
 ``routed_experts``, ``attention_token``) are checked against the reference's
 own Metal kernels compiled as C++ and run on the host in the reference's
 dispatch order (``oracle/metal_ref.py``, tests/test_oracle_moe_pinned.py).
-The layer loop that chains them is restated from moe_llm.mm, not executed.
+Whole token steps are also checked against ``metal_ref.MoeReference``,
+which chains the reference kernels in the layer order of the reference's
+forward (moe_llm.mm:2845-3039, restated: that host code is Objective-C++ on
+Metal).
 
 Followed step by step (reference files):
 

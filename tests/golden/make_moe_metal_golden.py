@@ -8,6 +8,11 @@ stored: `cases()` rebuilds them from seeds with this project's deterministic
 synthetic generator (myllm_b200.synth_gguf), here and in
 tests/test_oracle_moe_pinned.py.
 
+It also runs whole token steps of two seeded tiny qwen35moe models through
+the reference kernels (oracle.metal_ref.MoeReference: a 6-token prompt, then
+4 greedy steps) and stores the tokens fed and the logits of every step in
+tests/golden/moe_metal_ref_model.npz.
+
     python tests/golden/make_moe_metal_golden.py      # needs the built library
 """
 import os
@@ -22,6 +27,9 @@ if ROOT not in sys.path:
 from myllm_b200 import synth_gguf as sg  # noqa: E402
 
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "moe_metal_ref.npz")
+OUT_MODEL = os.path.join(os.path.dirname(os.path.abspath(__file__)), "moe_metal_ref_model.npz")
+MODEL_SEEDS = (5, 11)
+PROMPT, DECODES = 6, 4
 EPS = 1e-6
 
 
@@ -121,7 +129,28 @@ def run_reference(c):
     return {"out": out, "k_cache": kc, "v_cache": vc}
 
 
+def tiny_model(seed, directory):
+    """(spec, path) of the seeded tiny qwen35moe model (the one the other
+    qwen35moe tests use), written under `directory` if it is not there."""
+    spec = sg.tiny_moe_spec(seed=seed)
+    return spec, sg.cached_moe(spec, directory)
+
+
+def run_reference_model(path, prompt, steps, max_sequence=32):
+    """Tokens fed and logits [steps, vocab] of the reference-kernel model:
+    the prompt, then greedy steps on its own argmax (lowest index on ties)."""
+    from oracle import metal_ref as M
+    ref = M.MoeReference(path, max_sequence)
+    fed, logits = [], []
+    for i in range(steps):
+        t = int(prompt[i]) if i < len(prompt) else int(np.argmax(logits[-1]))
+        fed.append(t)
+        logits.append(ref.step(t))
+    return np.array(fed, dtype=np.int32), np.stack(logits)
+
+
 def main():
+    import tempfile
     from oracle import metal_ref as M
     if not M.available():
         raise SystemExit("build oracle/_ref/libref_metal.so first (make -C oracle metal REF=<reference checkout>)")
@@ -131,6 +160,15 @@ def main():
             arrays[f"{c['name']}.{key}"] = val
     np.savez_compressed(OUT, **arrays)
     print(f"wrote {OUT}: {len(arrays)} arrays")
+    model = {}
+    with tempfile.TemporaryDirectory() as d:
+        for seed in MODEL_SEEDS:
+            spec, path = tiny_model(seed, d)
+            fed, logits = run_reference_model(path, sg.prompt_ids(spec.seed, PROMPT, spec.vocab), PROMPT + DECODES)
+            model[f"s{seed}.tokens"] = fed
+            model[f"s{seed}.logits"] = logits
+    np.savez_compressed(OUT_MODEL, **model)
+    print(f"wrote {OUT_MODEL}: {len(model)} arrays")
 
 
 if __name__ == "__main__":

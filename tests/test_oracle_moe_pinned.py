@@ -16,7 +16,12 @@ step by step against them, after the projections:
   three-way tie, renormalisation;
 * routed experts (moe_llm.mm:2692-2843) over native Q4_K / Q6_K rows;
 * gated attention (moe_llm.mm:2256-2428) at config 4's head size 256 and
-  rotary width 64, three tokens after five cached rows.
+  rotary width 64, three tokens after five cached rows;
+* whole token steps of two seeded tiny qwen35moe models (embedding, every
+  layer, routed and shared experts, LM head) with every product, norm and
+  activation a reference kernel, in the layer order of the reference's
+  forward (moe_llm.mm:2845-3039; oracle.metal_ref.MoeReference): a 6-token
+  prompt and 4 greedy steps, same tokens, logits within 2e-5.
 
 The reference kernels compute in FP32 and the restatement in float64: values
 agree within 2e-5 of the largest, expert ids and copied rows exactly.
@@ -28,6 +33,7 @@ import numpy as np
 import pytest
 
 import oracle
+from myllm_b200 import synth_gguf as sg
 from oracle import metal_ref as M
 from oracle import moe_fp64 as O
 
@@ -49,6 +55,16 @@ def rel(got, ref):
 @pytest.fixture(scope="module")
 def golden():
     return np.load(os.path.join(GOLDEN_DIR, "moe_metal_ref.npz"))
+
+
+@pytest.fixture(scope="module")
+def model_golden():
+    return np.load(os.path.join(GOLDEN_DIR, "moe_metal_ref_model.npz"))
+
+
+@pytest.fixture(scope="module")
+def model_dir(tmp_path_factory):
+    return str(tmp_path_factory.mktemp("moe_ref_models"))
 
 
 CASES = G.cases()
@@ -116,10 +132,30 @@ def test_gated_attention_matches_reference_kernels(c, golden):
     assert np.array_equal(golden[n + ".v_cache"][pos:], c["v"])
 
 
+@pytest.mark.parametrize("seed", G.MODEL_SEEDS)
+def test_whole_token_steps_match_reference_kernels(seed, model_golden, model_dir):
+    """The FP64 forward fed the reference run's tokens: every step's logits
+    within 2e-5 of the reference kernels' and the same greedy token."""
+    spec, path = G.tiny_model(seed, model_dir)
+    fed, ref_logits = model_golden[f"s{seed}.tokens"], model_golden[f"s{seed}.logits"]
+    np.testing.assert_array_equal(fed[:G.PROMPT], sg.prompt_ids(spec.seed, G.PROMPT, spec.vocab))
+    fp64 = O.MoeFP64(path, max_sequence=32)
+    for i, t in enumerate(fed):
+        logits = fp64.step(int(t))
+        assert rel(logits, ref_logits[i]) <= TOL, i
+        assert int(np.argmax(logits)) == int(np.argmax(ref_logits[i])), i
+
+
 @pytest.mark.skipif(not M.available(), reason="the reference kernels were not built here (oracle/Makefile metal)")
-def test_fixture_is_what_the_reference_kernels_compute(golden):
+def test_fixture_is_what_the_reference_kernels_compute(golden, model_golden, model_dir):
     """Where the reference sources were built, the reference kernels run now
     reproduce the committed outputs bit for bit."""
     for c in CASES:
         for key, val in G.run_reference(c).items():
             assert np.array_equal(val, golden[f"{c['name']}.{key}"]), (c["name"], key)
+    for seed in G.MODEL_SEEDS:
+        spec, path = G.tiny_model(seed, model_dir)
+        fed, logits = G.run_reference_model(path, sg.prompt_ids(spec.seed, G.PROMPT, spec.vocab),
+                                            G.PROMPT + G.DECODES)
+        assert np.array_equal(fed, model_golden[f"s{seed}.tokens"]) and np.array_equal(
+            logits, model_golden[f"s{seed}.logits"]), seed
