@@ -11,7 +11,11 @@ tests/test_oracle_moe_pinned.py.
 It also runs whole token steps of two seeded tiny qwen35moe models through
 the reference kernels (oracle.metal_ref.MoeReference: a 6-token prompt, then
 4 greedy steps) and stores the tokens fed and the logits of every step in
-tests/golden/moe_metal_ref_model.npz.
+tests/golden/moe_metal_ref_model.npz; and the same for the 4-layer model with
+every config-4 width (synth_gguf.a3b_width_spec, a 2 GB GGUF written to a
+temporary directory) over the prompt of tests/golden/moe_a3b_width.npz, then
+4 greedy steps, storing the model's SHA-256, the greedy tokens and the
+logits of the last prompt step and the 4 decodes (the FP64 fixture's layout).
 
     python tests/golden/make_moe_metal_golden.py      # needs the built library
 """
@@ -167,6 +171,16 @@ def main():
             fed, logits = run_reference_model(path, sg.prompt_ids(spec.seed, PROMPT, spec.vocab), PROMPT + DECODES)
             model[f"s{seed}.tokens"] = fed
             model[f"s{seed}.logits"] = logits
+    fp64 = np.load(os.path.join(os.path.dirname(OUT), "moe_a3b_width.npz"))
+    with tempfile.TemporaryDirectory(dir=os.environ.get("MYLLM_GOLDEN_TMP")) as d:
+        path = os.path.join(d, "a3b_width.gguf")
+        sha = sg.write_moe(sg.a3b_width_spec(), path)
+        prompt = fp64["prompt"]
+        fed, logits = run_reference_model(path, prompt, len(prompt) + 4, max_sequence=64)
+    tail = logits[len(prompt) - 1:]
+    model["a3b.sha256"] = np.array(sha)
+    model["a3b.tokens"] = np.argmax(tail, axis=1).astype(np.int64)
+    model["a3b.logits"] = tail
     np.savez_compressed(OUT_MODEL, **model)
     print(f"wrote {OUT_MODEL}: {len(model)} arrays")
 

@@ -21,7 +21,11 @@ step by step against them, after the projections:
   layer, routed and shared experts, LM head) with every product, norm and
   activation a reference kernel, in the layer order of the reference's
   forward (moe_llm.mm:2845-3039; oracle.metal_ref.MoeReference): a 6-token
-  prompt and 4 greedy steps, same tokens, logits within 2e-5.
+  prompt and 4 greedy steps, same tokens, logits within 2e-5;
+* the FP64 fixture the GPU test at config 4's layer widths uses
+  (moe_a3b_width.npz: 4 layers, 256 experts top-8, hidden 2048) against the
+  reference-kernel forward of the same model (stored beside the tiny models'
+  runs): the same greedy tokens, logits within 2e-5.
 
 The reference kernels compute in FP32 and the restatement in float64: values
 agree within 2e-5 of the largest, expert ids and copied rows exactly.
@@ -144,6 +148,16 @@ def test_whole_token_steps_match_reference_kernels(seed, model_golden, model_dir
         logits = fp64.step(int(t))
         assert rel(logits, ref_logits[i]) <= TOL, i
         assert int(np.argmax(logits)) == int(np.argmax(ref_logits[i])), i
+
+
+def test_config4_width_fixture_matches_reference_kernels(model_golden):
+    """The FP64 forward's fixture at config 4's widths and the reference
+    kernels' forward of the same GGUF (same SHA-256) agree."""
+    fp64 = np.load(os.path.join(GOLDEN_DIR, "moe_a3b_width.npz"))
+    assert str(fp64["sha256"]) == str(model_golden["a3b.sha256"])
+    np.testing.assert_array_equal(fp64["tokens"], model_golden["a3b.tokens"])
+    for i in range(len(fp64["tokens"])):
+        assert rel(fp64["logits"][i], model_golden["a3b.logits"][i]) <= TOL, i
 
 
 @pytest.mark.skipif(not M.available(), reason="the reference kernels were not built here (oracle/Makefile metal)")
