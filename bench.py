@@ -643,18 +643,19 @@ def moe_kernel_times(peak_gbs: float, seed: int):
 
 
 def run_cpu_baseline(path: str, spec=None, prompt: int = 4, decode: int = 2, warmup: int = 0,
-                     timeout: int = 900):
+                     timeout: int = 900, moe: bool = False):
     """The reference CPULLM sample in a child process (oracle.cpu_baseline),
     so that running out of host memory or time gives an `unavailable` record
-    instead of ending the bench."""
-    if spec is not None:
+    instead of ending the bench.  moe: the reference's qwen35moe kernels run
+    on the host instead (the file is mapped, not copied)."""
+    if spec is not None and not moe:
         need, avail = reference_host_bytes(spec), mem_available()
         if avail is not None and need > 0.9 * avail:
             return {"value": None, "unavailable": f"the reference CPULLM holds FP32 weights and the file image: "
                                                   f"~{need / 1e9:.0f} GB of host memory, {avail / 1e9:.0f} GB "
                                                   f"available here"}
     cmd = [sys.executable, "-m", "oracle.cpu_baseline", "--model", path, "--prompt", str(prompt),
-           "--decode", str(decode), "--warmup", str(warmup)]
+           "--decode", str(decode), "--warmup", str(warmup)] + (["--moe"] if moe else [])
     try:
         res = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=timeout)
     except subprocess.TimeoutExpired:
@@ -1009,11 +1010,9 @@ def bench_cuda(args):
             dist.destroy_process_group()
         return
     cpu = None
-    if moe:
-        cpu = {"value": None, "unavailable": "the reference has no CPU qwen35moe path (its parity oracle is the "
-                                             "FP64 restatement, not a timed baseline)"}
-    elif world == 1 and not args.no_cpu_baseline:
-        cpu = run_cpu_baseline(path, spec)
+    if world == 1 and not args.no_cpu_baseline:
+        # qwen35moe: the reference's own kernels on the host, 2 prompt tokens + 2 decodes
+        cpu = run_cpu_baseline(path, spec, prompt=2, moe=True) if moe else run_cpu_baseline(path, spec)
     base = scaling_base(raw_args, local) if world == 1 and not args.no_scaling_base and not args.model else None
     line = make_line(name, spec, args, world, rank, dev_ms=dev_ms, e2e_ms=e2e_ms, prefill_ms=prefill_ms,
                      prefill_e2e_ms=prefill_e2e_ms, kern=kern, peak=peak, peak_kind=peak_kind, sweep=sweep, cpu=cpu,
@@ -1032,14 +1031,12 @@ def bench_reference(args):
     name = model_name(args, world)
     args = for_model(args, name)
     from myllm_b200 import synth_gguf as sg
-    if name in sg.MOE_CONFIGS:
-        print(json.dumps({"impl": "reference", "unavailable": "the reference's qwen35moe path is Metal-only "
-                                                             "(no CPU implementation to run here)"}))
-        return
+    moe = name in sg.MOE_CONFIGS
     spec, path = ensure_model(name, 0, 1, None)
     steps = min(args.steps, 4)
     warm = min(args.warmup, 1)
-    res = run_cpu_baseline(path, spec, prompt=4, decode=steps, warmup=warm, timeout=1800)
+    # qwen35moe has no reference CPU path: its own Metal kernels compiled for the host stand in
+    res = run_cpu_baseline(path, spec, prompt=2 if moe else 4, decode=steps, warmup=warm, timeout=1800, moe=moe)
     if res.get("value") is None:
         print(json.dumps({"impl": "reference", "unavailable": res.get("unavailable", "reference CPU path failed")}))
         return
@@ -1055,13 +1052,14 @@ def bench_reference(args):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": vs_published(name, res["value"]),
-        "dtype": "fp32 (reference dequantizes to FP32 at load)",
+        "dtype": "fp32 (reference kernels decode the blocks per product)" if moe else
+                 "fp32 (reference dequantizes to FP32 at load)",
         "data": "synthetic (same seeded GGUF as the cuda arm)",
         "config": workload_config(name, spec, args, world),
-        "prefill": {"value": res["prefill_tokens_per_s"], "unit": "tokens/s", "tokens": 4},
+        "prefill": {"value": res["prefill_tokens_per_s"], "unit": "tokens/s", "tokens": 2 if moe else 4},
         "cpu_baseline": dict(res, sample=f"{res.get('sample', '')}; a bounded sample of the workload in `config` "
-                                         f"(prompt 4 + {steps} decode tokens), 1 host thread (CPULLM has no "
-                                         f"threading)"),
+                                         f"(prompt {2 if moe else 4} + {steps} decode tokens), 1 host thread "
+                                         f"({'the kernels run one thread at a time' if moe else 'CPULLM has no threading'})"),
         "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -7,6 +7,7 @@ the reference-exact FP32 values.
 """
 from __future__ import annotations
 
+import mmap
 import struct
 from typing import Dict, Tuple
 
@@ -19,8 +20,10 @@ _BLOCK = {0: (1, 4), 1: (1, 2), 6: (32, 22), 8: (32, 34), 12: (256, 144), 13: (2
 class GgufReader:
     def __init__(self, path: str):
         self.path = path
+        # mapped read-only: a full-size model is tens of GB, and a test or a
+        # CPU sample touches only the rows it uses
         with open(path, "rb") as f:
-            self._buf = f.read()
+            self._buf = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
         b = self._buf
         magic, version, n_tensors, n_kv = struct.unpack_from("<IIQQ", b, 0)
         if magic != 0x46554747 or version != 3:

@@ -407,17 +407,18 @@ def test_peer_allreduce_switch(monkeypatch, capsys):
 
 
 @pytest.mark.parametrize("gpus,model,expect", [(1, None, "qwen2.5-7b"), (2, None, "qwen2.5-14b"),
-                                               (1, "qwen3.6-35b-a3b", None)])
+                                               (1, "qwen3.6-35b-a3b", "qwen3.6-35b-a3b")])
 def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect):
     """`--impl reference`: the CPULLM sample (stubbed) on the cuda arm's
-    workload, with the contract keys; rank 0 only; the MoE model reports the
-    reference's missing CPU path."""
+    workload, with the contract keys; rank 0 only; the MoE model times the
+    reference's own kernels on the host (stubbed the same way)."""
     import json
     import sys
     seen = {}
 
     def sample(path, spec=None, **k):
         seen["spec"] = spec.name
+        seen["moe"] = k.get("moe", False)
         return {"value": 0.25, "unit": "tokens/s", "cores": 1, "kind": "reference", "sample": "stub",
                 "prefill_tokens_per_s": 1.0}
     monkeypatch.setattr(bench, "run_cpu_baseline", sample)
@@ -432,7 +433,7 @@ def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect)
     if expect is None:
         assert "unavailable" in line
         return
-    assert seen["spec"] == expect
+    assert seen["spec"] == expect and seen["moe"] == ("a3b" in expect)
     assert REQUIRED - {"clocks", "gpu_launches", "roofline"} <= set(line) and line["value"] == 0.25
     # the cuda arm's config, so that the driver pairs the two lines
     spec = bench.model_spec(expect)[0]
@@ -448,7 +449,8 @@ def test_reference_arm_prints_its_line(monkeypatch, capsys, gpus, model, expect)
 @pytest.mark.parametrize("gpus", [1, 2])
 def test_moe_mode_prints_a_complete_line(monkeypatch, capsys, gpus):
     """`--model qwen3.6-35b-a3b`: the expert-parallel workload's line (LM-head
-    roofline kernel, replicated + expert bytes, no timed CPU reference)."""
+    roofline kernel, replicated + expert bytes; at N = 1 the CPU sample of the
+    reference's own kernels on the host, none at N > 1)."""
     import json
     _fake_run(monkeypatch, ["--gpus", str(gpus), "--model", "qwen3.6-35b-a3b", "--prompt", "64", "--steps", "8",
                             "--warmup", "3", "--max-sequence", "1024"],
@@ -457,7 +459,8 @@ def test_moe_mode_prints_a_complete_line(monkeypatch, capsys, gpus):
     line = json.loads([l for l in capsys.readouterr().out.splitlines() if l.startswith("{")][0])
     assert REQUIRED <= set(line)
     assert line["config"]["parallelism"] == ("single GPU" if gpus == 1 else "ep2")
-    assert line["roofline"]["shape"].endswith("Q6_K") and line["cpu_baseline"]["value"] is None
+    assert line["roofline"]["shape"].endswith("Q6_K")
+    assert (line["cpu_baseline"] is None) == (gpus > 1)
     assert (line["collectives"] is None) == (gpus == 1) and line["kernel_sweep"] is None
 
 
@@ -504,3 +507,15 @@ def test_traffic_is_measured_or_scaled_per_shape():
     t2, src2 = bench.profile_traffic("gemv_gateup", "2x[13824,5120] Q4_K", algo14)
     assert abs(t2 / algo14 - 77935872 / 76490752) < 1e-12 and src2.startswith("scaled")
     assert bench.profile_traffic("gemv_head")[0] is None
+
+
+def test_moe_reference_sample_runs_the_reference_kernels(tmp_path):
+    """qwen35moe's CPU sample: the reference's own kernels on the host
+    (oracle/_ref/libref_metal.so) in a child process, on a tiny model."""
+    from oracle import metal_ref
+    if not metal_ref.available():
+        pytest.skip("the reference kernels were not built here")
+    path = sg.cached_moe(sg.tiny_moe_spec(seed=5), str(tmp_path))
+    out = bench.run_cpu_baseline(path, sg.tiny_moe_spec(seed=5), prompt=2, decode=1, timeout=300, moe=True)
+    assert out["value"] > 0 and out["kind"] == "reference" and out["cores"] == 1
+    assert "Metal kernels compiled for the host" in out["sample"]
